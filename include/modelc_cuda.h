@@ -1,0 +1,193 @@
+/*
+ * modelc_cuda.h -- C ABI of the B200 (sm_100a) speculative-decoding step for
+ * modelc (yingkitw/modelc).  Plain pointers and sizes only; no CUDA or torch
+ * types cross this boundary.  Every entry point cites the reference interface
+ * it replaces (paths inside the modelc repository).
+ *
+ * Ownership and threading (mirrors the reference's Runtime / KvCache split,
+ * serve/infer.rs:129 and generate.rs:18-24):
+ *   - mc_weights is immutable after mc_weights_load and may be shared by any
+ *     number of sessions and host threads (the reference's RwLock<Runtime>).
+ *   - mc_session owns one request's KV cache, draft state and stream; it is
+ *     not thread-safe: one host thread per session (one KvCache per request).
+ * All functions return MC_OK (0) or a negative mc_status; mc_last_error()
+ * returns the calling thread's last error message.  There is no CPU
+ * fallback: without a usable sm_100 device every entry point fails with
+ * MC_E_CUDA.
+ */
+#ifndef MODELC_CUDA_H
+#define MODELC_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define MC_API __attribute__((visibility("default")))
+#else
+#define MC_API
+#endif
+
+typedef int32_t mc_status;
+#define MC_OK 0
+#define MC_E_INVALID -1   /* bad argument / null pointer */
+#define MC_E_SHAPE -2     /* tensor shape mismatch (reference: transformer.rs:831 panic) */
+#define MC_E_DTYPE -3     /* unsupported tensor dtype for the B200 path */
+#define MC_E_OOM -4       /* device allocation failed */
+#define MC_E_CUDA -5      /* CUDA runtime error / no sm_100 device */
+#define MC_E_NCCL -6      /* collective failure (tensor-parallel builds) */
+#define MC_E_TIMEOUT -7   /* a bounded device wait expired */
+#define MC_E_CANCELLED -8 /* the cancel flag was raised (generate.rs:639) */
+#define MC_E_NO_HEAD -9   /* no lm_head and no tied embedding: the reference's None
+                             (transformer.rs:94-95) */
+#define MC_E_CAPACITY -10 /* context would exceed the session's KV capacity */
+
+/* Tensor dtypes accepted by mc_weights_load (model.rs:6-42 DataType subset). */
+#define MC_DTYPE_F32 0       /* f32; matrices must be exactly representable as
+                                int8 rows with power-of-two scales */
+#define MC_DTYPE_I8_TENSOR 1 /* int8 + one scale (compiler.rs:207-229 format;
+                                dequant q as f32 * scale, model.rs:182-185) */
+#define MC_DTYPE_I8_ROW 2    /* int8 + one f32 scale per output row */
+#define MC_DTYPE_Q4_0 3      /* ggml q4_0 blocks (parsers/gguf/dequant.rs:23-46) */
+
+#define MC_MEM_HOST 0
+#define MC_MEM_DEVICE 1
+
+/* Head-geometry modes.  REFERENCE reproduces the reference runtime exactly:
+ * n_heads = hidden/64 (metadata is dropped, transformer.rs:1007-1027 +
+ * arch.rs:128-137), MHA, RoPE base 10000 (transformer.rs:925), RMSNorm eps
+ * 1e-6 (transformer.rs:91, :775, :806).  GENERAL takes the fields below. */
+#define MC_MODE_REFERENCE 0
+#define MC_MODE_GENERAL 1
+
+typedef struct mc_model_cfg {
+  int32_t mode;
+  int32_t n_layers;
+  int32_t hidden;
+  int32_t n_heads;    /* GENERAL only */
+  int32_t n_kv_heads; /* GENERAL only */
+  int32_t head_dim;   /* GENERAL only */
+  int32_t ffn;
+  int32_t vocab;
+  float rope_theta;   /* GENERAL only */
+  float eps;          /* GENERAL only */
+} mc_model_cfg;
+
+/* One tensor, as the reference's TensorData {shape, dtype, data}
+ * (model.rs:14-18) plus its name.  Names follow the reference
+ * (model.layers.{i}.self_attn.q_proj.weight, model.embed_tokens.weight,
+ * lm_head.weight, model.norm.weight, ...). */
+typedef struct mc_tensor_desc {
+  const char* name;
+  int32_t dtype;
+  int32_t location;     /* MC_MEM_HOST or MC_MEM_DEVICE (data and scales) */
+  int32_t ndim;         /* 1 or 2 */
+  int64_t shape[2];     /* [out, in] for matrices (transformer.rs:825) */
+  const void* data;
+  const float* scales;  /* I8_ROW: shape[0] floats; I8_TENSOR: 1 float */
+} mc_tensor_desc;
+
+typedef struct mc_weights mc_weights;
+typedef struct mc_session mc_session;
+typedef struct mc_linear mc_linear;
+
+/* Speculative session configuration (GenerationConfig, generate.rs:65-167,
+ * restricted to the fields the speculative step reads). */
+typedef struct mc_spec_cfg {
+  int32_t gamma;        /* draft tokens per round (GenerationConfig::gamma) */
+  int32_t max_context;  /* KV capacity in tokens (prompt + generated + gamma) */
+  int32_t bonus;        /* 0: reference verify (gamma positions, no bonus
+                           token, generate.rs:695-726); 1: gamma+1 positions
+                           with the bonus token */
+  float temperature;    /* 0 = greedy (the only mode of this build) */
+  uint64_t seed;
+  volatile int32_t* cancel;  /* optional; checked between rounds (generate.rs:639) */
+} mc_spec_cfg;
+
+/* Load (quantize-free) weights to the device and repack them for the
+ * tensor-core GEMV.  Replaces Runtime::from_raw (runtime/serve.rs:121-132),
+ * which dequantizes every tensor to f32; here int8 rows stay int8 in HBM. */
+MC_API mc_status mc_weights_load(const mc_tensor_desc* tensors, size_t n,
+                          const mc_model_cfg* cfg, int32_t device,
+                          mc_weights** out);
+MC_API mc_status mc_weights_destroy(mc_weights* w);
+/* Bytes of packed weights resident on the device. */
+MC_API int64_t mc_weights_bytes(const mc_weights* w);
+
+/* A session = one request: target KV (and draft KV when draft != NULL).
+ * Replaces make_kv_cache (generate.rs:18-24) + the per-request state of
+ * speculative_generate (generate.rs:598-637). */
+MC_API mc_status mc_session_create(const mc_weights* target, const mc_weights* draft,
+                            const mc_spec_cfg* cfg, mc_session** out);
+MC_API mc_status mc_session_destroy(mc_session* s);
+
+/* Batched forward_llama_cached (transformer.rs:64-96): forwards n token ids
+ * (token_embedding, generate.rs:843-863) at positions kv_len..kv_len+n-1,
+ * appends their K/V and writes n x vocab logits to logits_out (host memory,
+ * may be NULL).  Equivalent to n sequential single-token calls. */
+MC_API mc_status mc_forward(mc_session* s, const uint32_t* ids, int32_t n,
+                     float* logits_out);
+/* The same forward through the draft model's weights and KV. */
+MC_API mc_status mc_draft_forward(mc_session* s, const uint32_t* ids, int32_t n,
+                           float* logits_out);
+/* KvCache::len (transformer.rs:633-638) and rollback from the end. */
+MC_API int32_t mc_kv_len(const mc_session* s);
+MC_API mc_status mc_kv_truncate(mc_session* s, int32_t len);
+
+/* DraftModel::draft (draft.rs:18-21) for the transformer draft: greedy
+ * decode of gamma tokens after context (KV of the common prefix reused). */
+MC_API mc_status mc_draft(mc_session* s, const uint32_t* context, int32_t n,
+                   int32_t gamma, uint32_t* out, int32_t* n_out);
+
+/* speculative_generate (generate.rs:598-767) with the draft model given at
+ * session creation: prime the prompt, then rounds of draft -> batched verify
+ * -> acceptance, all on the device, until >= max_tokens tokens exist (the
+ * reference may overshoot by up to gamma-1, generate.rs:638,751).
+ * out receives up to cap generated ids; accepted (may be NULL) receives the
+ * accepted-draft count of each round (up to accepted_cap). */
+MC_API mc_status mc_speculative_generate(mc_session* s, const uint32_t* prompt,
+                                  int32_t n_prompt, int32_t max_tokens,
+                                  uint32_t* out, int32_t cap, int32_t* n_out,
+                                  int32_t* accepted, int32_t accepted_cap,
+                                  int32_t* n_rounds);
+
+/* Device-resident variants for measurement: prompt already primed with
+ * mc_spec_prime; mc_spec_decode runs the round loop only. */
+MC_API mc_status mc_spec_prime(mc_session* s, const uint32_t* prompt, int32_t n_prompt);
+MC_API mc_status mc_spec_decode(mc_session* s, int32_t max_tokens, int32_t* n_generated);
+MC_API mc_status mc_spec_read(mc_session* s, uint32_t* out, int32_t cap, int32_t* n_out,
+                       int32_t* accepted, int32_t accepted_cap, int32_t* n_rounds);
+/* Restart decoding from the primed prompt: the prompt's KV is kept, the
+ * generated tokens and round log are dropped. */
+MC_API mc_status mc_spec_rewind(mc_session* s);
+/* Enqueue n verify forwards (gamma or gamma+1 positions at the current
+ * target length, no acceptance, no state change) on the session stream and
+ * return immediately: for timing the verify forward with stream events. */
+MC_API mc_status mc_spec_verify_launch(mc_session* s, int32_t n);
+/* The session's CUDA stream (a cudaStream_t) for stream-ordered timing. */
+MC_API void* mc_session_stream(mc_session* s);
+/* Kernel launches one speculative round enqueues (draft steps, verify,
+ * acceptance). */
+MC_API int32_t mc_session_round_launches(const mc_session* s);
+
+/* Standalone quantized projection y = x . dequant(W)^T (linear_with,
+ * transformer.rs:825-843) on device buffers: x is m x in (f32, row-major),
+ * y is m x out.  `stream` is a cudaStream_t passed as void* (NULL = legacy
+ * default stream). */
+MC_API mc_status mc_linear_create(const mc_tensor_desc* w, int32_t device,
+                           mc_linear** out);
+MC_API mc_status mc_linear_destroy(mc_linear* l);
+MC_API mc_status mc_linear_run(mc_linear* l, const float* x_dev, int32_t m,
+                        float* y_dev, void* stream);
+MC_API int64_t mc_linear_weight_bytes(const mc_linear* l);
+
+MC_API size_t mc_last_error(char* buf, size_t cap);
+MC_API const char* mc_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MODELC_CUDA_H */

@@ -1,0 +1,1254 @@
+// mc_api.cu -- host side of the C ABI (include/modelc_cuda.h): weight
+// loading and repacking, per-request sessions (paged KV, device-resident
+// speculative state), forward enqueue, and the CUDA-graph speculative round.
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "mc_internal.cuh"
+#include "modelc_cuda.h"
+
+using namespace mc;
+
+// ------------------------------------------------------------------ errors
+static thread_local std::string g_err;
+
+static mc_status set_err(mc_status st, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return st;
+}
+
+#define CK(call)                                                                    \
+  do {                                                                              \
+    cudaError_t e_ = (call);                                                        \
+    if (e_ != cudaSuccess)                                                          \
+      return set_err(e_ == cudaErrorMemoryAllocation ? MC_E_OOM : MC_E_CUDA,        \
+                     "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__,     \
+                     __LINE__);                                                     \
+  } while (0)
+
+#define CKS(expr)                  \
+  do {                             \
+    mc_status s_ = (expr);         \
+    if (s_ != MC_OK) return s_;    \
+  } while (0)
+
+extern "C" size_t mc_last_error(char* buf, size_t cap) {
+  if (buf && cap) {
+    size_t n = std::min(cap - 1, g_err.size());
+    memcpy(buf, g_err.data(), n);
+    buf[n] = 0;
+  }
+  return g_err.size();
+}
+
+extern "C" const char* mc_version(void) { return "modelc_b200 0.1 (sm_100a)"; }
+
+static mc_status check_device(int device) {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0)
+    return set_err(MC_E_CUDA, "no CUDA device available (%s)", cudaGetErrorString(e));
+  if (device < 0 || device >= n) return set_err(MC_E_INVALID, "device %d out of range", device);
+  cudaDeviceProp p;
+  CK(cudaGetDeviceProperties(&p, device));
+  if (p.major != 10)
+    return set_err(MC_E_CUDA, "device %d is sm_%d%d; this library is built for sm_100a", device,
+                   p.major, p.minor);
+  CK(cudaSetDevice(device));
+  return MC_OK;
+}
+
+// ------------------------------------------------------------------ memory
+struct Allocs {
+  std::vector<void*> ptrs;
+  size_t bytes = 0;
+  template <class T>
+  mc_status alloc(T** p, size_t n) {
+    void* q = nullptr;
+    size_t b = std::max<size_t>(n * sizeof(T), 16);
+    cudaError_t e = cudaMalloc(&q, b);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return set_err(MC_E_OOM, "cudaMalloc(%zu) failed: %s", b, cudaGetErrorString(e));
+    }
+    ptrs.push_back(q);
+    bytes += b;
+    *p = (T*)q;
+    return MC_OK;
+  }
+  void free_all() {
+    for (void* p : ptrs) cudaFree(p);
+    ptrs.clear();
+    bytes = 0;
+  }
+};
+
+static inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+// ------------------------------------------------------------------ packed matrices
+struct PMat {
+  int N = 0, K = 0;  // logical rows / cols
+  int n_stripes = 0, KB = 0;
+  int4* w = nullptr;
+  float* scale = nullptr;
+  long long algo_bytes = 0;  // int8 codes + f32 row scales actually used
+};
+
+// Source matrix staged on the device as int8 [rows][cols] + f32 scales.
+struct SrcI8 {
+  int rows = 0, cols = 0;
+  int8_t* q = nullptr;
+  float* s = nullptr;
+  std::vector<void*> tmp;
+  ~SrcI8() {
+    for (void* p : tmp) cudaFree(p);
+  }
+};
+
+// f32 rows accepted only when exactly representable as int8 codes times a
+// power-of-two row scale (e.g. the reference's integer-valued test fixtures).
+static bool f32_row_exact_i8(const float* x, int K, int8_t* q, float* scale) {
+  float amax = 0.0f;
+  for (int c = 0; c < K; ++c) {
+    if (!isfinite(x[c])) return false;
+    amax = fmaxf(amax, fabsf(x[c]));
+  }
+  if (amax == 0.0f) {
+    memset(q, 0, K);
+    *scale = 1.0f;
+    return true;
+  }
+  int p = -160;
+  while (ldexpf(127.0f, p) < amax) ++p;
+  const float s = ldexpf(1.0f, p);
+  for (int c = 0; c < K; ++c) {
+    const float v = ldexpf(x[c], -p);
+    if (v != rintf(v) || fabsf(v) > 127.0f) return false;
+    q[c] = (int8_t)v;
+  }
+  *scale = s;
+  return true;
+}
+
+static mc_status stage_matrix(const mc_tensor_desc* t, SrcI8* out) {
+  if (t->ndim != 2) return set_err(MC_E_SHAPE, "%s: expected a matrix", t->name);
+  const int rows = (int)t->shape[0], cols = (int)t->shape[1];
+  out->rows = rows;
+  out->cols = cols;
+  const size_t n = (size_t)rows * cols;
+  void* q = nullptr;
+  void* s = nullptr;
+  CK(cudaMalloc(&q, std::max<size_t>(n, 16)));
+  out->tmp.push_back(q);
+  CK(cudaMalloc(&s, std::max<size_t>((size_t)rows * 4, 16)));
+  out->tmp.push_back(s);
+  out->q = (int8_t*)q;
+  out->s = (float*)s;
+  const cudaMemcpyKind kind =
+      t->location == MC_MEM_DEVICE ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  switch (t->dtype) {
+    case MC_DTYPE_I8_ROW:
+      if (!t->scales) return set_err(MC_E_INVALID, "%s: I8_ROW needs scales", t->name);
+      CK(cudaMemcpy(q, t->data, n, kind));
+      CK(cudaMemcpy(s, t->scales, (size_t)rows * 4, kind));
+      break;
+    case MC_DTYPE_I8_TENSOR: {
+      if (!t->scales) return set_err(MC_E_INVALID, "%s: I8_TENSOR needs a scale", t->name);
+      float sc = 0.0f;
+      CK(cudaMemcpy(&sc, t->scales, 4, t->location == MC_MEM_DEVICE ? cudaMemcpyDeviceToHost
+                                                                    : cudaMemcpyHostToHost));
+      std::vector<float> sv(rows, sc);
+      CK(cudaMemcpy(q, t->data, n, kind));
+      CK(cudaMemcpy(s, sv.data(), (size_t)rows * 4, cudaMemcpyHostToDevice));
+      break;
+    }
+    case MC_DTYPE_F32: {
+      std::vector<float> host;
+      const float* src = (const float*)t->data;
+      if (t->location == MC_MEM_DEVICE) {
+        host.resize(n);
+        CK(cudaMemcpy(host.data(), t->data, n * 4, cudaMemcpyDeviceToHost));
+        src = host.data();
+      }
+      std::vector<int8_t> hq(n);
+      std::vector<float> hs(rows);
+      for (int r = 0; r < rows; ++r)
+        if (!f32_row_exact_i8(src + (size_t)r * cols, cols, hq.data() + (size_t)r * cols, &hs[r]))
+          return set_err(MC_E_DTYPE,
+                         "%s: f32 matrix row %d is not exactly representable as int8 "
+                         "codes with a power-of-two scale; quantize it (int8 rows) first",
+                         t->name, r);
+      CK(cudaMemcpy(q, hq.data(), n, cudaMemcpyHostToDevice));
+      CK(cudaMemcpy(s, hs.data(), (size_t)rows * 4, cudaMemcpyHostToDevice));
+      break;
+    }
+    default:
+      return set_err(MC_E_DTYPE, "%s: dtype %d is not supported by this build", t->name,
+                     t->dtype);
+  }
+  return MC_OK;
+}
+
+static mc_status stage_vector(const mc_tensor_desc* t, int n_expect, std::vector<float>* out) {
+  const int n = (int)(t->ndim == 1 ? t->shape[0] : t->shape[0] * t->shape[1]);
+  if (n != n_expect) return set_err(MC_E_SHAPE, "%s: %d elements, expected %d", t->name, n, n_expect);
+  out->resize(n);
+  const cudaMemcpyKind kind =
+      t->location == MC_MEM_DEVICE ? cudaMemcpyDeviceToHost : cudaMemcpyHostToHost;
+  if (t->dtype == MC_DTYPE_F32) {
+    CK(cudaMemcpy(out->data(), t->data, (size_t)n * 4, kind));
+  } else if (t->dtype == MC_DTYPE_I8_TENSOR || t->dtype == MC_DTYPE_I8_ROW) {
+    std::vector<int8_t> q(n);
+    float sc = 0.0f;
+    CK(cudaMemcpy(q.data(), t->data, n, kind));
+    CK(cudaMemcpy(&sc, t->scales, 4, kind));
+    for (int i = 0; i < n; ++i) (*out)[i] = (float)q[i] * sc;  // model.rs:182-185
+  } else {
+    return set_err(MC_E_DTYPE, "%s: unsupported vector dtype", t->name);
+  }
+  return MC_OK;
+}
+
+// Concatenate staged sources row-wise into one device int8 matrix.
+static mc_status concat_rows(const std::vector<const SrcI8*>& parts, SrcI8* out) {
+  int rows = 0;
+  const int cols = parts[0]->cols;
+  for (auto* p : parts) {
+    if (p->cols != cols) return set_err(MC_E_SHAPE, "fused projections disagree on input width");
+    rows += p->rows;
+  }
+  out->rows = rows;
+  out->cols = cols;
+  void* q = nullptr;
+  void* s = nullptr;
+  CK(cudaMalloc(&q, std::max<size_t>((size_t)rows * cols, 16)));
+  out->tmp.push_back(q);
+  CK(cudaMalloc(&s, std::max<size_t>((size_t)rows * 4, 16)));
+  out->tmp.push_back(s);
+  out->q = (int8_t*)q;
+  out->s = (float*)s;
+  size_t r0 = 0;
+  for (auto* p : parts) {
+    CK(cudaMemcpy((int8_t*)q + r0 * cols, p->q, (size_t)p->rows * cols, cudaMemcpyDeviceToDevice));
+    CK(cudaMemcpy((float*)s + r0, p->s, (size_t)p->rows * 4, cudaMemcpyDeviceToDevice));
+    r0 += p->rows;
+  }
+  return MC_OK;
+}
+
+// Pack src through row_map (size n_stripes*16) and col_map (size KB*32).
+static mc_status pack_matrix(const SrcI8& src, const std::vector<int>& row_map,
+                             const std::vector<int>& col_map, int n_real_rows, int n_real_cols,
+                             Allocs& al, PMat* out) {
+  out->n_stripes = (int)row_map.size() / 16;
+  out->KB = (int)col_map.size() / 32;
+  out->N = n_real_rows;
+  out->K = n_real_cols;
+  out->algo_bytes = (long long)n_real_rows * n_real_cols + 4ll * n_real_rows;
+  CKS(al.alloc(&out->w, (size_t)out->n_stripes * out->KB * 32));
+  CKS(al.alloc(&out->scale, (size_t)out->n_stripes * 16));
+  int* drm = nullptr;
+  int* dcm = nullptr;
+  CK(cudaMalloc(&drm, row_map.size() * 4));
+  CK(cudaMalloc(&dcm, col_map.size() * 4));
+  cudaMemcpy(drm, row_map.data(), row_map.size() * 4, cudaMemcpyHostToDevice);
+  cudaMemcpy(dcm, col_map.data(), col_map.size() * 4, cudaMemcpyHostToDevice);
+  cudaError_t e = launch_pack_int8(src.q, src.cols, src.s, drm, dcm, out->n_stripes, out->KB,
+                                   out->w, out->scale, 0);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaFree(drm);
+  cudaFree(dcm);
+  if (e != cudaSuccess) return set_err(MC_E_CUDA, "packing failed: %s", cudaGetErrorString(e));
+  return MC_OK;
+}
+
+static std::vector<int> identity_map(int n_real, int n_padded) {
+  std::vector<int> m(n_padded, -1);
+  for (int i = 0; i < n_real && i < n_padded; ++i) m[i] = i;
+  return m;
+}
+
+// ------------------------------------------------------------------ weights
+struct LayerW {
+  bool attn = false, mlp = false;
+  float* attn_norm = nullptr;
+  float* mlp_norm = nullptr;
+  PMat qkv, o, gu, down;
+  int sq = 0, sk = 0;
+};
+
+struct mc_weights {
+  int dev = 0;
+  int L = 0, d = 0, H = 0, Hkv = 0, hd = 0, half = 0, half_p = 0, hdp = 0, F = 0, V = 0;
+  float theta = 10000.0f, eps = 1e-6f;
+  std::vector<LayerW> layers;
+  float* final_norm = nullptr;
+  PMat head;
+  bool has_head = false;
+  int8_t* emb_q = nullptr;
+  float* emb_scale = nullptr;
+  Allocs al;
+  long long algo_bytes_per_forward = 0;  // streamed weight bytes of one forward
+};
+
+static const mc_tensor_desc* find_t(const mc_tensor_desc* ts, size_t n, const std::string& name) {
+  for (size_t i = 0; i < n; ++i)
+    if (ts[i].name && name == ts[i].name) return &ts[i];
+  return nullptr;
+}
+
+// Padded head layout: first-half dims at [0, half), second-half dims at
+// [half_p, half_p + half); a dim p of the padded head maps to a source
+// index inside the real head, or -1.
+static int padded_src(int p, int half, int half_p) {
+  if (p < half_p) return p < half ? p : -1;
+  const int j = p - half_p;
+  return j < half ? half + j : -1;
+}
+
+static mc_status load_model(const mc_tensor_desc* ts, size_t n, const mc_model_cfg* cfg,
+                            mc_weights* W) {
+  W->L = cfg->n_layers;
+  W->d = cfg->hidden;
+  W->F = cfg->ffn;
+  W->V = cfg->vocab;
+  if (W->L < 0 || W->d <= 0 || W->V <= 0) return set_err(MC_E_INVALID, "bad model config");
+  // q_proj rows define the query width (transformer.rs:944-946).
+  int q_rows = W->d;
+  if (W->L > 0) {
+    const mc_tensor_desc* q = find_t(ts, n, "model.layers.0.self_attn.q_proj.weight");
+    if (q && q->ndim == 2) q_rows = (int)q->shape[0];
+  }
+  if (cfg->mode == MC_MODE_REFERENCE) {
+    int nh = W->d / 64;
+    if (nh < 1) nh = 1;
+    W->H = nh;
+    W->Hkv = nh;
+    W->hd = q_rows / nh;
+    W->theta = 10000.0f;
+    W->eps = 1e-6f;
+  } else {
+    W->H = cfg->n_heads;
+    W->Hkv = cfg->n_kv_heads;
+    W->hd = cfg->head_dim;
+    W->theta = cfg->rope_theta;
+    W->eps = cfg->eps;
+  }
+  if (W->H <= 0 || W->Hkv <= 0 || W->hd <= 0 || W->H % W->Hkv)
+    return set_err(MC_E_SHAPE, "bad head geometry H=%d Hkv=%d hd=%d", W->H, W->Hkv, W->hd);
+  if (W->hd % 2) return set_err(MC_E_SHAPE, "odd head_dim %d is not supported", W->hd);
+  if (W->H / W->Hkv * kMaxTokens > 128)
+    return set_err(MC_E_SHAPE, "query group %d too large", W->H / W->Hkv);
+  W->half = W->hd / 2;
+  W->half_p = round_up(W->half, 8);
+  W->hdp = 2 * W->half_p;
+  const int H = W->H, Hkv = W->Hkv, hd = W->hd, half = W->half, half_p = W->half_p,
+            hdp = W->hdp, d = W->d, F = W->F;
+  Allocs& al = W->al;
+
+  // embedding (row-major int8 for the gather)
+  const mc_tensor_desc* te = find_t(ts, n, "model.embed_tokens.weight");
+  SrcI8 emb;
+  if (te) {
+    CKS(stage_matrix(te, &emb));
+    if (emb.rows != W->V || emb.cols != d)
+      return set_err(MC_E_SHAPE, "embed_tokens is %dx%d, expected %dx%d", emb.rows, emb.cols,
+                     W->V, d);
+    CKS(al.alloc(&W->emb_q, (size_t)W->V * d));
+    CKS(al.alloc(&W->emb_scale, (size_t)W->V));
+    CK(cudaMemcpy(W->emb_q, emb.q, (size_t)W->V * d, cudaMemcpyDeviceToDevice));
+    CK(cudaMemcpy(W->emb_scale, emb.s, (size_t)W->V * 4, cudaMemcpyDeviceToDevice));
+  } else {
+    // token_embedding returns zeros without an embedding (generate.rs:858-862)
+    CKS(al.alloc(&W->emb_q, (size_t)W->V * d));
+    CKS(al.alloc(&W->emb_scale, (size_t)W->V));
+    CK(cudaMemset(W->emb_q, 0, (size_t)W->V * d));
+    CK(cudaMemset(W->emb_scale, 0, (size_t)W->V * 4));
+  }
+
+  auto upload_vec = [&](const char* name, int len, float** dst) -> mc_status {
+    const mc_tensor_desc* t = find_t(ts, n, name);
+    if (!t) {
+      *dst = nullptr;
+      return MC_OK;
+    }
+    std::vector<float> v;
+    CKS(stage_vector(t, len, &v));
+    CKS(al.alloc(dst, (size_t)len));
+    CK(cudaMemcpy(*dst, v.data(), (size_t)len * 4, cudaMemcpyHostToDevice));
+    return MC_OK;
+  };
+
+  W->layers.resize(W->L);
+  long long bytes = 0;
+  for (int l = 0; l < W->L; ++l) {
+    LayerW& Lw = W->layers[l];
+    const std::string p = "model.layers." + std::to_string(l) + ".";
+    const mc_tensor_desc* tq = find_t(ts, n, p + "self_attn.q_proj.weight");
+    const mc_tensor_desc* tk = find_t(ts, n, p + "self_attn.k_proj.weight");
+    const mc_tensor_desc* tv = find_t(ts, n, p + "self_attn.v_proj.weight");
+    const mc_tensor_desc* to = find_t(ts, n, p + "self_attn.o_proj.weight");
+    Lw.attn = tq && tk && tv && to;  // llama_attention returns None otherwise (:769-772)
+    if (Lw.attn) {
+      CKS(upload_vec((p + "input_layernorm.weight").c_str(), d, &Lw.attn_norm));
+      SrcI8 sq, sk, sv, so;
+      CKS(stage_matrix(tq, &sq));
+      CKS(stage_matrix(tk, &sk));
+      CKS(stage_matrix(tv, &sv));
+      CKS(stage_matrix(to, &so));
+      if (sq.rows != H * hd || sk.rows != Hkv * hd || sv.rows != Hkv * hd || sq.cols != d ||
+          so.rows != d || so.cols != H * hd)
+        return set_err(MC_E_SHAPE, "layer %d attention shapes do not match H=%d Hkv=%d hd=%d d=%d",
+                       l, H, Hkv, hd, d);
+      SrcI8 cat;
+      CKS(concat_rows({&sq, &sk, &sv}, &cat));
+      const int per_head = half_p / 8;
+      Lw.sq = H * per_head;
+      Lw.sk = Hkv * per_head;
+      const int sv_n = Hkv * per_head;
+      std::vector<int> rm((size_t)(Lw.sq + Lw.sk + sv_n) * 16, -1);
+      for (int s = 0; s < Lw.sq + Lw.sk; ++s) {
+        const bool isq = s < Lw.sq;
+        const int s2 = isq ? s : s - Lw.sq;
+        const int hh = s2 / per_head, j = s2 % per_head;
+        const int base = isq ? hh * hd : H * hd + hh * hd;
+        for (int g = 0; g < 8; ++g) {
+          const int i = 8 * j + g;
+          rm[s * 16 + g] = i < half ? base + i : -1;
+          rm[s * 16 + g + 8] = i < half ? base + half + i : -1;
+        }
+      }
+      for (int s = 0; s < sv_n; ++s) {
+        const int hh = s / per_head, j = s % per_head;
+        for (int r = 0; r < 16; ++r) {
+          const int src = padded_src(16 * j + r, half, half_p);
+          rm[(Lw.sq + Lw.sk + s) * 16 + r] = src < 0 ? -1 : (H + Hkv) * hd + hh * hd + src;
+        }
+      }
+      CKS(pack_matrix(cat, rm, identity_map(d, round_up(d, 32)), (H + 2 * Hkv) * hd, d, al,
+                      &Lw.qkv));
+      Lw.qkv.algo_bytes = (long long)(H + 2 * Hkv) * hd * d + 4ll * (H + 2 * Hkv) * hd;
+      // O projection: columns follow the padded head layout of the attention output
+      std::vector<int> cm(round_up(H * hdp, 32), -1);
+      for (int hh = 0; hh < H; ++hh)
+        for (int pp = 0; pp < hdp; ++pp) {
+          const int src = padded_src(pp, half, half_p);
+          cm[hh * hdp + pp] = src < 0 ? -1 : hh * hd + src;
+        }
+      CKS(pack_matrix(so, identity_map(d, round_up(d, 16)), cm, d, H * hd, al, &Lw.o));
+      bytes += Lw.qkv.algo_bytes + Lw.o.algo_bytes;
+    }
+    const mc_tensor_desc* tg = find_t(ts, n, p + "mlp.gate_proj.weight");
+    const mc_tensor_desc* tu = find_t(ts, n, p + "mlp.up_proj.weight");
+    const mc_tensor_desc* td = find_t(ts, n, p + "mlp.down_proj.weight");
+    Lw.mlp = tg && tu && td;  // llama_mlp returns None otherwise (:801-803)
+    if (Lw.mlp) {
+      CKS(upload_vec((p + "post_attention_layernorm.weight").c_str(), d, &Lw.mlp_norm));
+      SrcI8 sg, su, sdn;
+      CKS(stage_matrix(tg, &sg));
+      CKS(stage_matrix(tu, &su));
+      CKS(stage_matrix(td, &sdn));
+      if (sg.rows != F || su.rows != F || sg.cols != d || su.cols != d || sdn.rows != d ||
+          sdn.cols != F)
+        return set_err(MC_E_SHAPE, "layer %d MLP shapes do not match d=%d ffn=%d", l, d, F);
+      SrcI8 cat;
+      CKS(concat_rows({&sg, &su}, &cat));
+      const int ns = (F + 7) / 8;
+      std::vector<int> rm((size_t)ns * 16, -1);
+      for (int s = 0; s < ns; ++s)
+        for (int g = 0; g < 8; ++g) {
+          const int i = 8 * s + g;
+          rm[s * 16 + g] = i < F ? i : -1;
+          rm[s * 16 + g + 8] = i < F ? F + i : -1;
+        }
+      CKS(pack_matrix(cat, rm, identity_map(d, round_up(d, 32)), 2 * F, d, al, &Lw.gu));
+      CKS(pack_matrix(sdn, identity_map(d, round_up(d, 16)), identity_map(F, round_up(F, 32)), d,
+                      F, al, &Lw.down));
+      bytes += Lw.gu.algo_bytes + Lw.down.algo_bytes;
+    }
+  }
+  CKS(upload_vec("model.norm.weight", d, &W->final_norm));
+  const mc_tensor_desc* th = find_t(ts, n, "lm_head.weight");
+  if (!th) th = te;  // tied head (transformer.rs:94-95)
+  if (th) {
+    SrcI8 sh;
+    CKS(stage_matrix(th, &sh));
+    if (sh.rows != W->V || sh.cols != d)
+      return set_err(MC_E_SHAPE, "lm_head is %dx%d, expected %dx%d", sh.rows, sh.cols, W->V, d);
+    CKS(pack_matrix(sh, identity_map(W->V, round_up(W->V, 16)), identity_map(d, round_up(d, 32)),
+                    W->V, d, al, &W->head));
+    W->has_head = true;
+    bytes += W->head.algo_bytes;
+  }
+  W->algo_bytes_per_forward = bytes;
+  return MC_OK;
+}
+
+extern "C" mc_status mc_weights_load(const mc_tensor_desc* tensors, size_t n,
+                                     const mc_model_cfg* cfg, int32_t device, mc_weights** out) {
+  if (!tensors || !cfg || !out) return set_err(MC_E_INVALID, "null argument");
+  *out = nullptr;
+  CKS(check_device(device));
+  mc_weights* W = new mc_weights();
+  W->dev = device;
+  mc_status st = load_model(tensors, n, cfg, W);
+  if (st != MC_OK) {
+    W->al.free_all();
+    delete W;
+    return st;
+  }
+  *out = W;
+  return MC_OK;
+}
+
+extern "C" mc_status mc_weights_destroy(mc_weights* w) {
+  if (!w) return MC_OK;
+  cudaSetDevice(w->dev);
+  w->al.free_all();
+  delete w;
+  return MC_OK;
+}
+
+extern "C" int64_t mc_weights_bytes(const mc_weights* w) {
+  return w ? (int64_t)w->algo_bytes_per_forward : 0;
+}
+
+// ------------------------------------------------------------------ sessions
+constexpr int kPage = 64;       // KV positions per page
+constexpr int kChunk = kMaxTokens;  // prefill tokens per forward launch
+
+struct KVSet {
+  float* k = nullptr;
+  float* v = nullptr;
+  size_t layer_stride = 0;  // floats per layer
+  int* page_table = nullptr;
+  int n_pages = 0;
+  float* rope_cos = nullptr;
+  float* rope_sin = nullptr;
+};
+
+struct mc_session {
+  const mc_weights* tw = nullptr;
+  const mc_weights* dw = nullptr;
+  mc_spec_cfg cfg{};
+  int cap = 0;
+  int dev = 0;
+  int nsm = 0;
+  cudaStream_t stream = nullptr;
+  Allocs al;
+  // shared scratch
+  float* h = nullptr;
+  uint8_t* xq = nullptr;
+  int* xexp = nullptr;
+  float* qb = nullptr;
+  float* attn = nullptr;
+  float* act = nullptr;
+  float* logits = nullptr;
+  int* ws = nullptr;
+  int* cnt = nullptr;
+  float* part_o = nullptr;
+  float* part_ml = nullptr;
+  int* acnt = nullptr;
+  KVSet tkv, dkv;
+  // device-resident speculative state
+  SpecState* st = nullptr;
+  uint32_t* ctx = nullptr;
+  int* acc_log = nullptr;
+  uint32_t* ids = nullptr;
+  int* pos = nullptr;  // [2]: target / draft length for the plain forward API
+  // host mirrors
+  int lt = 0, ld = 0;
+  int prompt_len = 0;
+  std::vector<uint32_t> draft_tokens;  // tokens in the draft KV (mc_draft)
+  uint32_t* h_ids = nullptr;           // pinned staging
+  cudaGraphExec_t round_exec = nullptr;
+  cudaGraphExec_t verify_exec = nullptr;
+  int round_launches = 0;
+  int bps[5][7] = {};
+};
+
+static int bps_of(mc_session* s, int epi, int nt) {
+  if (!s->bps[epi][nt]) s->bps[epi][nt] = std::max(1, gemv_blocks_per_sm(epi, nt));
+  return s->bps[epi][nt];
+}
+
+static mc_status alloc_kv(mc_session* s, const mc_weights* W, KVSet* kv) {
+  kv->n_pages = (s->cap + kPage - 1) / kPage;
+  kv->layer_stride = (size_t)kv->n_pages * W->Hkv * kPage * W->hdp;
+  const size_t total = kv->layer_stride * std::max(W->L, 1);
+  CKS(s->al.alloc(&kv->k, total));
+  CKS(s->al.alloc(&kv->v, total));
+  CK(cudaMemset(kv->k, 0, total * 4));
+  CK(cudaMemset(kv->v, 0, total * 4));
+  CKS(s->al.alloc(&kv->page_table, (size_t)kv->n_pages));
+  std::vector<int> pt(kv->n_pages);
+  for (int i = 0; i < kv->n_pages; ++i) pt[i] = i;
+  CK(cudaMemcpy(kv->page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice));
+  // RoPE factors computed on the host with libm exactly as transformer.rs:926-927:
+  // theta = pos * base^(-i/half) in f32, then sin/cos.
+  const int hp = W->half_p;
+  std::vector<float> c((size_t)s->cap * hp), sn((size_t)s->cap * hp);
+  for (int p = 0; p < s->cap; ++p)
+    for (int i = 0; i < hp; ++i) {
+      float cv = 1.0f, sv = 0.0f;
+      if (i < W->half) {
+        const float expo = -(float)i / (float)W->half;
+        const float theta = (float)p * powf(W->theta, expo);
+        cv = cosf(theta);
+        sv = sinf(theta);
+      }
+      c[(size_t)p * hp + i] = cv;
+      sn[(size_t)p * hp + i] = sv;
+    }
+  CKS(s->al.alloc(&kv->rope_cos, c.size()));
+  CKS(s->al.alloc(&kv->rope_sin, sn.size()));
+  CK(cudaMemcpy(kv->rope_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(kv->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+  return MC_OK;
+}
+
+static int max_kp(const mc_weights* W) {
+  int m = round_up(W->d, 32);
+  m = std::max(m, round_up(W->H * W->hdp, 32));
+  m = std::max(m, round_up(W->F, 32));
+  return m;
+}
+
+static int max_stripes(const mc_weights* W) {
+  int m = W->has_head ? W->head.n_stripes : 0;
+  for (const LayerW& L : W->layers) {
+    m = std::max(m, L.qkv.n_stripes);
+    m = std::max(m, L.o.n_stripes);
+    m = std::max(m, L.gu.n_stripes);
+    m = std::max(m, L.down.n_stripes);
+  }
+  return m;
+}
+
+static mc_status session_alloc(mc_session* s) {
+  const mc_weights* ws[2] = {s->tw, s->dw};
+  int d = 0, kp = 0, hq = 0, F = 0, V = 0, stripes = 0, hkv = 0;
+  size_t po = 0, pml = 0;  // attention partials per page
+  for (const mc_weights* W : ws) {
+    if (!W) continue;
+    d = std::max(d, W->d);
+    kp = std::max(kp, max_kp(W));
+    hq = std::max(hq, W->H * W->hdp);
+    F = std::max(F, W->F);
+    V = std::max(V, W->V);
+    stripes = std::max(stripes, max_stripes(W));
+    const size_t rows = (size_t)(W->H / W->Hkv) * kChunk;
+    po = std::max(po, (size_t)W->Hkv * rows * W->hdp);
+    pml = std::max(pml, (size_t)W->Hkv * rows * 2);
+    hkv = std::max(hkv, W->Hkv);
+  }
+  const int M = kChunk;
+  CKS(s->al.alloc(&s->h, (size_t)M * d));
+  CKS(s->al.alloc(&s->xq, (size_t)kp * 8 * 6));
+  CK(cudaMemset(s->xq, 0, (size_t)kp * 8 * 6));
+  CKS(s->al.alloc(&s->xexp, (size_t)M));
+  CKS(s->al.alloc(&s->qb, (size_t)M * hq));
+  CKS(s->al.alloc(&s->attn, (size_t)M * hq));
+  CK(cudaMemset(s->attn, 0, (size_t)M * hq * 4));
+  CKS(s->al.alloc(&s->act, (size_t)M * std::max(F, 1)));
+  CKS(s->al.alloc(&s->logits, (size_t)M * V));
+  CKS(s->al.alloc(&s->ws, (size_t)stripes * 32 * 24));
+  CK(cudaMemset(s->ws, 0, (size_t)stripes * 32 * 24 * 4));
+  CKS(s->al.alloc(&s->cnt, (size_t)stripes));
+  CK(cudaMemset(s->cnt, 0, (size_t)stripes * 4));
+  const int n_pages = (s->cap + kPage - 1) / kPage;
+  CKS(s->al.alloc(&s->part_o, po * n_pages));
+  CKS(s->al.alloc(&s->part_ml, pml * n_pages));
+  CKS(s->al.alloc(&s->acnt, (size_t)hkv));
+  CK(cudaMemset(s->acnt, 0, (size_t)hkv * 4));
+  CKS(alloc_kv(s, s->tw, &s->tkv));
+  if (s->dw) CKS(alloc_kv(s, s->dw, &s->dkv));
+  // kernel limits and occupancy are settled here, never inside a capture
+  size_t qsm = 0, asm_ = 0;
+  for (const mc_weights* W : ws) {
+    if (!W) continue;
+    qsm = std::max(qsm, (size_t)max_kp(W) * sizeof(float));
+    asm_ = std::max(asm_, attention_smem_bytes(W->H / W->Hkv, kChunk, W->hdp, kPage));
+  }
+  CK(prepare_kernels(qsm, asm_));
+  for (int epi = 0; epi < 5; ++epi)
+    for (int nt : {1, 2, 3, 6}) bps_of(s, epi, nt);
+  CKS(s->al.alloc(&s->st, 1));
+  CK(cudaMemset(s->st, 0, sizeof(SpecState)));
+  CKS(s->al.alloc(&s->ctx, (size_t)s->cap + 8));
+  CKS(s->al.alloc(&s->acc_log, (size_t)s->cap + 8));
+  CKS(s->al.alloc(&s->ids, (size_t)M));
+  CKS(s->al.alloc(&s->pos, 2));
+  CK(cudaMemset(s->pos, 0, 8));
+  CK(cudaMallocHost(&s->h_ids, (size_t)std::max(s->cap, M) * 4));
+  return MC_OK;
+}
+
+extern "C" mc_status mc_session_create(const mc_weights* target, const mc_weights* draft,
+                                       const mc_spec_cfg* cfg, mc_session** out) {
+  if (!target || !cfg || !out) return set_err(MC_E_INVALID, "null argument");
+  *out = nullptr;
+  if (draft && draft->dev != target->dev)
+    return set_err(MC_E_INVALID, "target and draft live on different devices");
+  if (cfg->gamma < 0 || cfg->gamma + 1 > kMaxTokens)
+    return set_err(MC_E_INVALID, "gamma %d outside [0, %d]", cfg->gamma, kMaxTokens - 1);
+  if (cfg->max_context <= 0) return set_err(MC_E_INVALID, "max_context must be positive");
+  if (cfg->temperature > 0.0f)
+    return set_err(MC_E_INVALID, "stochastic acceptance is not built yet; use temperature 0");
+  if (draft && (draft->V != target->V))
+    return set_err(MC_E_SHAPE, "draft vocab %d != target vocab %d", draft->V, target->V);
+  CK(cudaSetDevice(target->dev));
+  mc_session* s = new mc_session();
+  s->tw = target;
+  s->dw = draft;
+  s->cfg = *cfg;
+  s->dev = target->dev;
+  s->cap = round_up(cfg->max_context + kChunk + 2, kPage);
+  cudaDeviceGetAttribute(&s->nsm, cudaDevAttrMultiProcessorCount, s->dev);
+  mc_status st = MC_OK;
+  if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess)
+    st = set_err(MC_E_CUDA, "stream creation failed");
+  if (st == MC_OK) st = session_alloc(s);
+  if (st != MC_OK) {
+    if (s->h_ids) cudaFreeHost(s->h_ids);
+    if (s->stream) cudaStreamDestroy(s->stream);
+    s->al.free_all();
+    delete s;
+    return st;
+  }
+  *out = s;
+  return MC_OK;
+}
+
+extern "C" mc_status mc_session_destroy(mc_session* s) {
+  if (!s) return MC_OK;
+  cudaSetDevice(s->dev);
+  if (s->stream) cudaStreamSynchronize(s->stream);
+  if (s->round_exec) cudaGraphExecDestroy(s->round_exec);
+  if (s->verify_exec) cudaGraphExecDestroy(s->verify_exec);
+  if (s->h_ids) cudaFreeHost(s->h_ids);
+  if (s->stream) cudaStreamDestroy(s->stream);
+  s->al.free_all();
+  delete s;
+  return MC_OK;
+}
+
+// ------------------------------------------------------------------ forward
+static mc_status enq_quant(mc_session* s, const float* h, int ld, int d, int M, const float* w,
+                           float eps, int do_norm) {
+  QuantArgs q{};
+  q.h = h;
+  q.ld = ld;
+  q.d = d;
+  q.M = M;
+  q.w = w;
+  q.wlen = d;
+  q.eps = eps;
+  q.do_norm = do_norm;
+  q.xq = s->xq;
+  q.KB = (d + 31) / 32;
+  q.nt = nt_for_tokens(M);
+  q.xexp = s->xexp;
+  CK(launch_quant(q, s->stream, true));
+  return MC_OK;
+}
+
+static mc_status enq_gemv(mc_session* s, const PMat& W, int epi, int M, GemvArgs a) {
+  a.w = W.w;
+  a.scale = W.scale;
+  a.x = s->xq;
+  a.xexp = s->xexp;
+  a.KB = W.KB;
+  a.n_stripes = W.n_stripes;
+  a.M = M;
+  a.ws = s->ws;
+  a.cnt = s->cnt;
+  const int nt = nt_for_tokens(M);
+  const int grid = s->nsm * bps_of(s, epi, nt);
+  CK(launch_gemv(a, epi, nt, grid, s->stream, true));
+  return MC_OK;
+}
+
+// One batched forward of M tokens through W (forward_llama_cached,
+// transformer.rs:64-96, for M positions at once).
+static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv, int M,
+                             EmbedArgs ea, const int* pos_ptr, int pos_add,
+                             unsigned long long* keys, float* logits_dev) {
+  if (!W->has_head) return set_err(MC_E_NO_HEAD, "model has no lm_head and no embedding");
+  ea.emb_q = W->emb_q;
+  ea.emb_scale = W->emb_scale;
+  ea.d = W->d;
+  ea.vocab = W->V;
+  ea.M = M;
+  ea.h = s->h;
+  ea.zero_keys = keys;
+  ea.n_zero = keys ? M : 0;
+  CK(launch_embed(ea, s->stream, true));
+  const int d = W->d, F = W->F;
+  for (int l = 0; l < W->L; ++l) {
+    const LayerW& Lw = W->layers[l];
+    if (Lw.attn) {
+      CKS(enq_quant(s, s->h, d, d, M, Lw.attn_norm, W->eps, Lw.attn_norm ? 1 : 0));
+      GemvArgs a{};
+      a.q_out = s->qb;
+      a.kc = kv.k + (size_t)l * kv.layer_stride;
+      a.vc = kv.v + (size_t)l * kv.layer_stride;
+      a.page_table = kv.page_table;
+      a.pos_ptr = pos_ptr;
+      a.pos_add = pos_add;
+      a.rope_cos = kv.rope_cos;
+      a.rope_sin = kv.rope_sin;
+      a.half_p = W->half_p;
+      a.hdp = W->hdp;
+      a.H = W->H;
+      a.Hkv = W->Hkv;
+      a.page = kPage;
+      a.sq = Lw.sq;
+      a.sk = Lw.sk;
+      CKS(enq_gemv(s, Lw.qkv, EPI_QKV, M, a));
+      AttnArgs t{};
+      t.q = s->qb;
+      t.kc = a.kc;
+      t.vc = a.vc;
+      t.page_table = kv.page_table;
+      t.pos_ptr = pos_ptr;
+      t.pos_add = pos_add;
+      t.M = M;
+      t.H = W->H;
+      t.Hkv = W->Hkv;
+      t.hdp = W->hdp;
+      t.page = kPage;
+      t.inv_scale_den = sqrtf((float)W->hd);
+      t.max_chunks = kv.n_pages;
+      t.part_o = s->part_o;
+      t.part_ml = s->part_ml;
+      t.cnt = s->acnt;
+      t.out = s->attn;
+      CK(launch_attention(t, s->stream, true));
+      CKS(enq_quant(s, s->attn, W->H * W->hdp, W->H * W->hdp, M, nullptr, 0.0f, 0));
+      GemvArgs o{};
+      o.out = s->h;
+      o.ldo = d;
+      o.n_out = d;
+      CKS(enq_gemv(s, Lw.o, EPI_RESID, M, o));
+    }
+    if (Lw.mlp) {
+      CKS(enq_quant(s, s->h, d, d, M, Lw.mlp_norm, W->eps, Lw.mlp_norm ? 1 : 0));
+      GemvArgs g{};
+      g.out = s->act;
+      g.ldo = F;
+      g.n_out = F;
+      CKS(enq_gemv(s, Lw.gu, EPI_SWIGLU, M, g));
+      CKS(enq_quant(s, s->act, F, F, M, nullptr, 0.0f, 0));
+      GemvArgs dn{};
+      dn.out = s->h;
+      dn.ldo = d;
+      dn.n_out = d;
+      CKS(enq_gemv(s, Lw.down, EPI_RESID, M, dn));
+    }
+  }
+  CKS(enq_quant(s, s->h, d, d, M, W->final_norm, W->eps, W->final_norm ? 1 : 0));
+  GemvArgs hd{};
+  hd.out = logits_dev;
+  hd.ldo = W->V;
+  hd.n_out = W->V;
+  hd.keys = keys;
+  CKS(enq_gemv(s, W->head, EPI_LMHEAD, M, hd));
+  return MC_OK;
+}
+
+// Plain batched forward through the C ABI (target: which=0, draft: which=1).
+static mc_status forward_api(mc_session* s, int which, const uint32_t* ids, int n, float* logits) {
+  const mc_weights* W = which ? s->dw : s->tw;
+  if (!W) return set_err(MC_E_INVALID, "session has no draft model");
+  const KVSet& kv = which ? s->dkv : s->tkv;
+  int& len = which ? s->ld : s->lt;
+  if (n < 0 || (n > 0 && !ids)) return set_err(MC_E_INVALID, "bad ids");
+  if (len + n > s->cap - 1) return set_err(MC_E_CAPACITY, "KV capacity %d exceeded", s->cap);
+  CK(cudaSetDevice(s->dev));
+  for (int c0 = 0; c0 < n; c0 += kChunk) {
+    const int M = std::min(kChunk, n - c0);
+    memcpy(s->h_ids, ids + c0, (size_t)M * 4);
+    CK(cudaMemcpyAsync(s->ids, s->h_ids, (size_t)M * 4, cudaMemcpyHostToDevice, s->stream));
+    CK(launch_set_int(s->pos + which, len, s->stream));
+    EmbedArgs ea{};
+    ea.src = SRC_IDS;
+    ea.ids = s->ids;
+    CKS(enq_forward(s, W, kv, M, ea, s->pos + which, 0, s->st->tkeys, logits ? s->logits : nullptr));
+    if (logits)
+      CK(cudaMemcpyAsync(logits + (size_t)c0 * W->V, s->logits, (size_t)M * W->V * 4,
+                         cudaMemcpyDeviceToHost, s->stream));
+    CK(cudaStreamSynchronize(s->stream));
+    len += M;
+  }
+  if (which) s->draft_tokens.insert(s->draft_tokens.end(), ids, ids + n);
+  return MC_OK;
+}
+
+extern "C" mc_status mc_forward(mc_session* s, const uint32_t* ids, int32_t n, float* logits_out) {
+  if (!s) return set_err(MC_E_INVALID, "null session");
+  return forward_api(s, 0, ids, n, logits_out);
+}
+
+extern "C" mc_status mc_draft_forward(mc_session* s, const uint32_t* ids, int32_t n,
+                                      float* logits_out) {
+  if (!s) return set_err(MC_E_INVALID, "null session");
+  return forward_api(s, 1, ids, n, logits_out);
+}
+
+extern "C" int32_t mc_kv_len(const mc_session* s) { return s ? s->lt : 0; }
+
+extern "C" mc_status mc_kv_truncate(mc_session* s, int32_t len) {
+  if (!s || len < 0) return set_err(MC_E_INVALID, "bad arguments");
+  if (len < s->lt) s->lt = len;
+  return MC_OK;
+}
+
+// DraftModel::draft (draft.rs:18-21) for the transformer draft.
+extern "C" mc_status mc_draft(mc_session* s, const uint32_t* context, int32_t n, int32_t gamma,
+                              uint32_t* out, int32_t* n_out) {
+  if (!s || !out || !n_out || n < 0 || gamma < 0) return set_err(MC_E_INVALID, "bad arguments");
+  *n_out = 0;
+  if (!s->dw) return set_err(MC_E_INVALID, "session has no draft model");
+  if (n == 0 || gamma == 0) return MC_OK;
+  if (n + gamma > s->cap - 1) return set_err(MC_E_CAPACITY, "KV capacity %d exceeded", s->cap);
+  size_t p = 0;
+  while (p < s->draft_tokens.size() && p < (size_t)n && s->draft_tokens[p] == context[p]) ++p;
+  if (p > (size_t)n - 1) p = n - 1;
+  s->draft_tokens.resize(p);
+  s->ld = (int)p;
+  // forward the uncached context (chunks); keep only the last chunk's argmax
+  std::vector<uint32_t> rest(context + p, context + n);
+  CKS(forward_api(s, 1, rest.data(), (int)rest.size(), nullptr));
+  for (int j = 0; j < gamma; ++j) {
+    unsigned long long key = 0;
+    const int last = (int)((rest.size() - 1) % kChunk);
+    CK(cudaMemcpy(&key, &s->st->tkeys[last], 8, cudaMemcpyDeviceToHost));
+    out[j] = key_index(key);
+    if (j + 1 < gamma) {
+      rest.assign(1, out[j]);
+      CKS(forward_api(s, 1, &out[j], 1, nullptr));
+    }
+  }
+  *n_out = gamma;
+  return MC_OK;
+}
+
+// ------------------------------------------------------------------ speculative loop
+static int forward_launches(const mc_weights* W) {
+  int n = 1 + 2;  // embedding; final norm + LM head
+  for (const LayerW& L : W->layers) n += (L.attn ? 5 : 0) + (L.mlp ? 4 : 0);
+  return n;
+}
+
+static mc_status enq_verify(mc_session* s) {
+  const int vm = s->cfg.gamma + (s->cfg.bonus ? 1 : 0);
+  EmbedArgs ea{};
+  ea.src = SRC_VERIFY;
+  ea.ctx = s->ctx;
+  ea.off = &s->st->ctx_len;
+  ea.keys = s->st->dkeys;
+  return enq_forward(s, s->tw, s->tkv, vm, ea, &s->st->lt, 0, s->st->tkeys, nullptr);
+}
+
+static mc_status capture_verify(mc_session* s) {
+  if (s->verify_exec) return MC_OK;
+  CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+  mc_status rc = enq_verify(s);
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(s->stream, &graph);
+  if (rc != MC_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) return set_err(MC_E_CUDA, "capture failed: %s", cudaGetErrorString(e));
+  e = cudaGraphInstantiate(&s->verify_exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) return set_err(MC_E_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+  return MC_OK;
+}
+
+static mc_status capture_round(mc_session* s) {
+  if (s->round_exec) return MC_OK;
+  const int g = s->cfg.gamma;
+  const int bonus = s->cfg.bonus ? 1 : 0;
+  const int vm = g + bonus;
+  const int dsteps = g + bonus;
+  SpecState* st = s->st;
+  CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+  mc_status rc = MC_OK;
+  for (int j = 0; j < dsteps && rc == MC_OK; ++j) {
+    EmbedArgs ea{};
+    if (j == 0) {
+      ea.src = SRC_CTX_AT;
+      ea.ctx = s->ctx;
+      ea.off = &st->ld;
+    } else {
+      ea.src = SRC_KEYS;
+      ea.keys = &st->dkeys[j - 1];
+    }
+    rc = enq_forward(s, s->dw, s->dkv, 1, ea, &st->ld, j, &st->dkeys[j], nullptr);
+  }
+  if (rc == MC_OK) rc = enq_verify(s);
+  if (rc == MC_OK) {
+    cudaError_t e = launch_accept_greedy(st, s->ctx, s->acc_log, vm, s->stream, true);
+    if (e != cudaSuccess) rc = set_err(MC_E_CUDA, "accept launch: %s", cudaGetErrorString(e));
+  }
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(s->stream, &graph);
+  if (rc != MC_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) return set_err(MC_E_CUDA, "capture failed: %s", cudaGetErrorString(e));
+  e = cudaGraphInstantiate(&s->round_exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) return set_err(MC_E_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+  s->round_launches = dsteps * forward_launches(s->dw) + forward_launches(s->tw) + 1;
+  return MC_OK;
+}
+
+extern "C" mc_status mc_spec_prime(mc_session* s, const uint32_t* prompt, int32_t n_prompt) {
+  if (!s || (!prompt && n_prompt > 0) || n_prompt < 0) return set_err(MC_E_INVALID, "bad arguments");
+  if (!s->dw) return set_err(MC_E_INVALID, "speculative decoding needs a draft model");
+  if (s->cfg.gamma < 1) return set_err(MC_E_INVALID, "gamma must be >= 1");
+  if (n_prompt == 0) return set_err(MC_E_INVALID, "empty prompt (generate.rs:609-611 returns nothing)");
+  if (n_prompt + s->cfg.gamma + 2 > s->cap)
+    return set_err(MC_E_CAPACITY, "prompt of %d does not fit KV capacity %d", n_prompt, s->cap);
+  CK(cudaSetDevice(s->dev));
+  s->prompt_len = n_prompt;
+  s->draft_tokens.clear();
+  memcpy(s->h_ids, prompt, (size_t)n_prompt * 4);
+  CK(cudaMemcpyAsync(s->ctx, s->h_ids, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, s->stream));
+  // prime the target (generate.rs:629-636): every prompt token, logits discarded
+  for (int c0 = 0; c0 < n_prompt; c0 += kChunk) {
+    const int M = std::min(kChunk, n_prompt - c0);
+    CK(launch_set_int(s->pos, c0, s->stream));
+    EmbedArgs ea{};
+    ea.src = SRC_IDS;
+    ea.ids = s->ctx + c0;
+    CKS(enq_forward(s, s->tw, s->tkv, M, ea, s->pos, 0, s->st->tkeys, nullptr));
+  }
+  // prime the draft with all but the last prompt token (the first round
+  // forwards the last one)
+  for (int c0 = 0; c0 < n_prompt - 1; c0 += kChunk) {
+    const int M = std::min(kChunk, n_prompt - 1 - c0);
+    CK(launch_set_int(s->pos + 1, c0, s->stream));
+    EmbedArgs ea{};
+    ea.src = SRC_IDS;
+    ea.ids = s->ctx + c0;
+    CKS(enq_forward(s, s->dw, s->dkv, M, ea, s->pos + 1, 0, s->st->dkeys, nullptr));
+  }
+  SpecState h{};
+  h.ctx_len = n_prompt;
+  h.lt = n_prompt;
+  h.ld = n_prompt - 1;
+  h.generated = 0;
+  h.prompt_len = n_prompt;
+  h.gamma = s->cfg.gamma;
+  h.bonus = s->cfg.bonus ? 1 : 0;
+  h.rounds_cap = s->cap;
+  CK(cudaMemcpyAsync(s->st, &h, sizeof(h), cudaMemcpyHostToDevice, s->stream));
+  CK(cudaStreamSynchronize(s->stream));
+  s->lt = n_prompt;
+  s->ld = n_prompt - 1;
+  return MC_OK;
+}
+
+extern "C" mc_status mc_spec_decode(mc_session* s, int32_t max_tokens, int32_t* n_generated) {
+  if (!s || max_tokens < 0) return set_err(MC_E_INVALID, "bad arguments");
+  if (!s->prompt_len) return set_err(MC_E_INVALID, "call mc_spec_prime first");
+  CK(cudaSetDevice(s->dev));
+  CKS(capture_round(s));
+  const int max_emit = s->cfg.gamma + (s->cfg.bonus ? 1 : 0);
+  SpecState h{};
+  CK(cudaMemcpy(&h, s->st, sizeof(h), cudaMemcpyDeviceToHost));
+  // The reference checks the budget only at round start (generate.rs:638);
+  // launching ceil(remaining / max_emit) rounds per batch keeps every launched
+  // round one the reference would also run.
+  while (h.generated < max_tokens) {
+    if (s->cfg.cancel && *s->cfg.cancel) return set_err(MC_E_CANCELLED, "cancelled");
+    const int remaining = max_tokens - h.generated;
+    if (h.ctx_len + max_emit * ((remaining + max_emit - 1) / max_emit) + 2 > s->cap ||
+        h.ctx_len + remaining + max_emit + 2 > s->cap)
+      return set_err(MC_E_CAPACITY, "generation would exceed KV capacity %d", s->cap);
+    const int R = (remaining + max_emit - 1) / max_emit;
+    for (int r = 0; r < R; ++r) CK(cudaGraphLaunch(s->round_exec, s->stream));
+    CK(cudaMemcpyAsync(&h, s->st, sizeof(h), cudaMemcpyDeviceToHost, s->stream));
+    CK(cudaStreamSynchronize(s->stream));
+  }
+  s->lt = h.lt;
+  s->ld = h.ld;
+  if (n_generated) *n_generated = h.generated;
+  return MC_OK;
+}
+
+extern "C" mc_status mc_spec_read(mc_session* s, uint32_t* out, int32_t cap, int32_t* n_out,
+                                  int32_t* accepted, int32_t accepted_cap, int32_t* n_rounds) {
+  if (!s) return set_err(MC_E_INVALID, "null session");
+  CK(cudaSetDevice(s->dev));
+  SpecState h{};
+  CK(cudaMemcpy(&h, s->st, sizeof(h), cudaMemcpyDeviceToHost));
+  const int gen = h.ctx_len - h.prompt_len;
+  const int nc = std::max(0, std::min(gen, (int)cap));
+  if (out && nc) CK(cudaMemcpy(out, s->ctx + h.prompt_len, (size_t)nc * 4, cudaMemcpyDeviceToHost));
+  if (n_out) *n_out = nc;
+  if (accepted && accepted_cap > 0) {
+    const int na = std::min(h.n_rounds, (int)accepted_cap);
+    if (na) CK(cudaMemcpy(accepted, s->acc_log, (size_t)na * 4, cudaMemcpyDeviceToHost));
+  }
+  if (n_rounds) *n_rounds = h.n_rounds;
+  return MC_OK;
+}
+
+extern "C" mc_status mc_spec_rewind(mc_session* s) {
+  if (!s || !s->prompt_len) return set_err(MC_E_INVALID, "call mc_spec_prime first");
+  CK(cudaSetDevice(s->dev));
+  SpecState h{};
+  h.ctx_len = s->prompt_len;
+  h.lt = s->prompt_len;
+  h.ld = s->prompt_len - 1;
+  h.prompt_len = s->prompt_len;
+  h.gamma = s->cfg.gamma;
+  h.bonus = s->cfg.bonus ? 1 : 0;
+  h.rounds_cap = s->cap;
+  CK(cudaMemcpyAsync(s->st, &h, sizeof(h), cudaMemcpyHostToDevice, s->stream));
+  CK(cudaStreamSynchronize(s->stream));
+  s->lt = h.lt;
+  s->ld = h.ld;
+  return MC_OK;
+}
+
+extern "C" mc_status mc_spec_verify_launch(mc_session* s, int32_t n) {
+  if (!s || n < 0) return set_err(MC_E_INVALID, "bad arguments");
+  if (!s->prompt_len) return set_err(MC_E_INVALID, "call mc_spec_prime first");
+  CK(cudaSetDevice(s->dev));
+  CKS(capture_verify(s));
+  for (int i = 0; i < n; ++i) CK(cudaGraphLaunch(s->verify_exec, s->stream));
+  return MC_OK;
+}
+
+extern "C" void* mc_session_stream(mc_session* s) { return s ? (void*)s->stream : nullptr; }
+
+extern "C" int32_t mc_session_round_launches(const mc_session* s) {
+  if (!s || !s->dw) return 0;
+  const int dsteps = s->cfg.gamma + (s->cfg.bonus ? 1 : 0);
+  return dsteps * forward_launches(s->dw) + forward_launches(s->tw) + 1;
+}
+
+extern "C" mc_status mc_speculative_generate(mc_session* s, const uint32_t* prompt,
+                                             int32_t n_prompt, int32_t max_tokens, uint32_t* out,
+                                             int32_t cap, int32_t* n_out, int32_t* accepted,
+                                             int32_t accepted_cap, int32_t* n_rounds) {
+  if (n_out) *n_out = 0;
+  if (n_rounds) *n_rounds = 0;
+  if (s && n_prompt == 0) return MC_OK;  // generate.rs:609-611
+  CKS(mc_spec_prime(s, prompt, n_prompt));
+  CKS(mc_spec_decode(s, max_tokens, nullptr));
+  return mc_spec_read(s, out, cap, n_out, accepted, accepted_cap, n_rounds);
+}
+
+// ------------------------------------------------------------------ standalone linear
+struct mc_linear {
+  int dev = 0;
+  PMat m;
+  Allocs al;
+  uint8_t* xq = nullptr;
+  int* xexp = nullptr;
+  int* ws = nullptr;
+  int* cnt = nullptr;
+  int nsm = 0;
+  int bps[7] = {};
+};
+
+extern "C" mc_status mc_linear_create(const mc_tensor_desc* w, int32_t device, mc_linear** out) {
+  if (!w || !out) return set_err(MC_E_INVALID, "null argument");
+  *out = nullptr;
+  CKS(check_device(device));
+  mc_linear* L = new mc_linear();
+  L->dev = device;
+  SrcI8 src;
+  mc_status st = stage_matrix(w, &src);
+  if (st == MC_OK)
+    st = pack_matrix(src, identity_map(src.rows, round_up(src.rows, 16)),
+                     identity_map(src.cols, round_up(src.cols, 32)), src.rows, src.cols, L->al,
+                     &L->m);
+  const int kp = round_up(src.cols, 32);
+  if (st == MC_OK && prepare_kernels((size_t)kp * sizeof(float), 0) != cudaSuccess)
+    st = set_err(MC_E_CUDA, "kernel preparation failed");
+  if (st == MC_OK) st = L->al.alloc(&L->xq, (size_t)kp * 48);
+  if (st == MC_OK) st = L->al.alloc(&L->xexp, (size_t)kMaxTokens);
+  if (st == MC_OK) st = L->al.alloc(&L->ws, (size_t)L->m.n_stripes * 32 * 24);
+  if (st == MC_OK) st = L->al.alloc(&L->cnt, (size_t)L->m.n_stripes);
+  if (st == MC_OK && (cudaMemset(L->xq, 0, (size_t)kp * 48) != cudaSuccess ||
+                      cudaMemset(L->ws, 0, (size_t)L->m.n_stripes * 32 * 24 * 4) != cudaSuccess ||
+                      cudaMemset(L->cnt, 0, (size_t)L->m.n_stripes * 4) != cudaSuccess))
+    st = set_err(MC_E_CUDA, "memset failed");
+  cudaDeviceGetAttribute(&L->nsm, cudaDevAttrMultiProcessorCount, device);
+  if (st != MC_OK) {
+    L->al.free_all();
+    delete L;
+    return st;
+  }
+  *out = L;
+  return MC_OK;
+}
+
+extern "C" mc_status mc_linear_destroy(mc_linear* l) {
+  if (!l) return MC_OK;
+  cudaSetDevice(l->dev);
+  l->al.free_all();
+  delete l;
+  return MC_OK;
+}
+
+extern "C" int64_t mc_linear_weight_bytes(const mc_linear* l) { return l ? l->m.algo_bytes : 0; }
+
+extern "C" mc_status mc_linear_run(mc_linear* l, const float* x_dev, int32_t m, float* y_dev,
+                                   void* stream) {
+  if (!l || (!x_dev && m > 0) || (!y_dev && m > 0) || m < 0)
+    return set_err(MC_E_INVALID, "bad arguments");
+  CK(cudaSetDevice(l->dev));
+  cudaStream_t s = (cudaStream_t)stream;
+  for (int r0 = 0; r0 < m; r0 += kMaxTokens) {
+    const int M = std::min(kMaxTokens, m - r0);
+    QuantArgs q{};
+    q.h = x_dev + (size_t)r0 * l->m.K;
+    q.ld = l->m.K;
+    q.d = l->m.K;
+    q.M = M;
+    q.xq = l->xq;
+    q.KB = l->m.KB;
+    q.nt = nt_for_tokens(M);
+    q.xexp = l->xexp;
+    CK(launch_quant(q, s, true));
+    GemvArgs a{};
+    a.w = l->m.w;
+    a.scale = l->m.scale;
+    a.x = l->xq;
+    a.xexp = l->xexp;
+    a.KB = l->m.KB;
+    a.n_stripes = l->m.n_stripes;
+    a.M = M;
+    a.ws = l->ws;
+    a.cnt = l->cnt;
+    a.out = y_dev + (size_t)r0 * l->m.N;
+    a.ldo = l->m.N;
+    a.n_out = l->m.N;
+    const int nt = nt_for_tokens(M);
+    if (!l->bps[nt]) l->bps[nt] = std::max(1, gemv_blocks_per_sm(EPI_STORE, nt));
+    CK(launch_gemv(a, EPI_STORE, nt, l->nsm * l->bps[nt], s, true));
+  }
+  return MC_OK;
+}

@@ -1,0 +1,187 @@
+// mc_internal.cuh -- shared device helpers and kernel interfaces of the
+// modelc B200 speculative-decoding library (sm_100a only).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "modelc_b200 is built for sm_100a only"
+#endif
+
+namespace mc {
+
+// ---------------------------------------------------------------------------
+// Packed-weight geometry.
+//
+// A quantized [N, K] matrix (reference layout [out, in], transformer.rs:825)
+// is stored as 16-row "stripes" x 32-column "k-blocks".  One k-block of one
+// stripe is 512 bytes: 32 lanes x 16 bytes, each lane's 16 bytes being exactly
+// its A fragment of mma.m16n8k32.s8 (rows g and g+8, columns 4t..4t+3 and
+// 16+4t..16+4t+3, g = lane/4, t = lane%4).  Stripes are stored k-block-major,
+// so a warp streaming a contiguous range of (stripe, k-block) indices reads
+// contiguous, fully coalesced 512-byte runs.
+// ---------------------------------------------------------------------------
+constexpr int kStripeRows = 16;
+constexpr int kKBlock = 32;
+constexpr int kFragBytes = 512;
+
+// Activations are fixed-point: per token a power-of-two exponent e with
+// X = round(x * 2^e), |X| <= 2^20, held as three balanced base-128 int8
+// digits X = d0*2^14 + d1*2^7 + d2.  Column c = 3*token + digit of the B
+// operand; NT n8-tiles cover 8*NT columns.
+constexpr int kDigits = 3;
+constexpr int kMaxTokens = 16;  // tokens per GEMV launch (NT <= 6)
+constexpr int kExpNonFinite = -100000;  // exponent marking a non-finite row
+
+__host__ __device__ inline int nt_for_tokens(int m) {
+  int cols = kDigits * m;
+  int nt = (cols + 7) / 8;
+  if (nt == 4 || nt == 5) nt = 6;
+  return nt;  // 1, 2, 3 or 6
+}
+
+// Epilogue kinds of the quantized GEMV.
+enum Epi : int {
+  EPI_STORE = 0,   // out[m][row] = y
+  EPI_RESID = 1,   // out[m][row] += y           (O and down projections)
+  EPI_SWIGLU = 2,  // act[m][i] = silu(gate)*up  (gate/up rows interleaved)
+  EPI_QKV = 3,     // RoPE(q), RoPE(k) -> q buffer and paged KV, v -> KV
+  EPI_LMHEAD = 4,  // logits + first-index argmax keys
+};
+
+struct GemvArgs {
+  const int4* w;         // packed weights
+  const float* scale;    // [n_stripes*16] per packed row (0 on padding rows)
+  const uint8_t* x;      // packed activation digits [KB][32][8*NT]
+  const int* xexp;       // [M] exponents
+  int KB;                // k-blocks per stripe
+  int n_stripes;
+  int M;                 // tokens
+  int* ws;               // split-K partial sums [n_stripes][32][4*NT] (zeroed)
+  int* cnt;              // [n_stripes] k-block arrival counters (zeroed)
+  // epilogue
+  float* out;            // STORE/RESID/SWIGLU/LMHEAD destination
+  int ldo;               // row stride (elements) of out per token
+  int n_out;             // valid output rows (N) or SwiGLU width (F)
+  unsigned long long* keys;  // LMHEAD: per-token argmax keys
+  // QKV epilogue
+  float* q_out;          // [M][H][hdp]
+  float* kc;             // layer K pages [page][Hkv][P][hdp]
+  float* vc;
+  const int* page_table;
+  const int* pos_ptr;    // first position = *pos_ptr + pos_add
+  int pos_add;
+  const float* rope_cos; // [pos][half_p]
+  const float* rope_sin;
+  int half_p, hdp, H, Hkv, page;
+  int sq, sk;            // Q and K stripe counts
+};
+
+struct QuantArgs {
+  const float* h;        // [M][ld]
+  int ld;
+  int d;                 // logical length
+  int M;
+  const float* w;        // RMSNorm weight or nullptr
+  int wlen;
+  float eps;
+  int do_norm;
+  uint8_t* xq;           // packed digits
+  int KB;                // ceil(d/32) (padded k-blocks written)
+  int nt;
+  int* xexp;
+};
+
+struct AttnArgs {
+  const float* q;        // [M][H][hdp]
+  const float* kc;       // layer pages
+  const float* vc;
+  const int* page_table;
+  const int* pos_ptr;
+  int pos_add;
+  int M, H, Hkv, hdp, page;
+  float inv_scale_den;   // sqrt(head_dim) (divisor, transformer.rs:966)
+  int max_chunks;
+  float* part_o;         // [Hkv][max_chunks][G*M][hdp]
+  float* part_ml;        // [Hkv][max_chunks][G*M][2]
+  int* cnt;              // [Hkv]
+  float* out;            // [M][H][hdp]
+};
+
+enum EmbedSrc : int {
+  SRC_IDS = 0,     // ids[m]
+  SRC_CTX_AT = 1,  // ctx[*off + m]
+  SRC_KEYS = 2,    // argmax key keys[m]
+  SRC_VERIFY = 3,  // m == 0 ? ctx[*len - 1] : key keys[m-1]
+};
+
+struct EmbedArgs {
+  int src;
+  const uint32_t* ids;
+  const uint32_t* ctx;
+  const int* off;        // SRC_CTX_AT offset / SRC_VERIFY context length
+  const unsigned long long* keys;
+  uint32_t* ids_out;     // optional: resolved ids [M]
+  const int8_t* emb_q;   // [vocab][d] int8
+  const float* emb_scale;// [vocab]
+  int d, vocab, M;
+  float* h;              // [M][d]
+  unsigned long long* zero_keys;  // keys this forward will produce
+  int n_zero;
+};
+
+struct SpecState {
+  int ctx_len;
+  int lt;          // target KV length
+  int ld;          // draft KV length
+  int generated;
+  int prompt_len;
+  int max_tokens;
+  int gamma;
+  int n_rounds;
+  int bonus;
+  int rounds_cap;
+  int pad[6];
+  unsigned long long tkeys[kMaxTokens];
+  unsigned long long dkeys[kMaxTokens];
+};
+
+// Argmax keys: larger key = larger value, ties -> smaller index.
+__host__ __device__ inline unsigned long long argmax_key(float v, uint32_t idx) {
+  uint32_t b = 0;
+#ifdef __CUDA_ARCH__
+  b = __float_as_uint(v);
+#else
+  memcpy(&b, &v, 4);
+#endif
+  uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)o << 32) | (unsigned long long)(~idx);
+}
+__host__ __device__ inline uint32_t key_index(unsigned long long k) {
+  return k == 0ull ? 0u : ~(uint32_t)(k & 0xffffffffull);
+}
+
+// Kernel launchers (mc_kernels.cu).  All kernels are launched with
+// programmatic stream serialization allowed: each one issues its
+// data-independent loads (weights) before griddepcontrol.wait.
+cudaError_t launch_gemv(const GemvArgs& a, int epi, int nt, int grid,
+                        cudaStream_t s, bool pdl);
+int gemv_blocks_per_sm(int epi, int nt);
+cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl);
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
+cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t s, bool pdl);
+cudaError_t launch_accept_greedy(SpecState* st, uint32_t* ctx, int* acc_log,
+                                 int vm, cudaStream_t s, bool pdl);
+cudaError_t launch_set_int(int* p, int v, cudaStream_t s);
+size_t attention_smem_bytes(int G, int M, int hdp, int page);
+cudaError_t prepare_kernels(size_t quant_smem, size_t attn_smem);
+cudaError_t launch_pack_int8(const int8_t* src, long long src_ld,
+                             const float* src_scale, const int* row_map,
+                             const int* col_map, int n_stripes, int KB,
+                             int4* dst, float* dst_scale, cudaStream_t s);
+cudaError_t launch_pack_rows_q(const int8_t* src, long long n, int8_t* dst,
+                               cudaStream_t s);
+
+}  // namespace mc

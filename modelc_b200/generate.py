@@ -1,0 +1,173 @@
+"""Host API mirroring modelc's generation interface over the C ABI.
+
+Names follow the reference: ``GenerationConfig`` (generate.rs:65-167),
+``speculative_generate`` (generate.rs:598-767), ``forward_llama_cached``
+(transformer.rs:64-96, batched here), ``DraftModel.draft`` (draft.rs:18-21).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+from ._lib import check, lib
+from .model import Weights
+
+
+@dataclass
+class GenerationConfig:
+    """The speculative-path subset of generate.rs:65-167 (defaults :146-167)."""
+    max_tokens: int = 128
+    temperature: float = 0.0
+    gamma: int = 0
+    seed: int = 0
+    bonus: bool = False   # False: the reference verify (no bonus token)
+
+
+def _u32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.uint32))
+
+
+class Session:
+    """One request's device state: target KV, draft KV, speculative state.
+
+    Mirrors the reference's per-request ``Option<KvCache>`` (generate.rs:
+    617-627) plus the draft model's cache."""
+
+    def __init__(self, target: Weights, draft: Weights | None = None, gamma: int = 4,
+                 max_context: int = 2048, bonus: bool = False, temperature: float = 0.0,
+                 seed: int = 0):
+        self.target, self.draft = target, draft
+        self.gamma = gamma
+        self._cancel = C.c_int32(0)
+        cfg = _lib.SpecCfg(gamma, max_context, int(bonus), temperature, seed,
+                           C.pointer(self._cancel))
+        h = C.c_void_p()
+        check(lib().mc_session_create(target.handle, draft.handle if draft else None,
+                                      C.byref(cfg), C.byref(h)))
+        self.handle = h
+
+    # -- forward_llama_cached (batched) ------------------------------------
+    def forward(self, ids, logits: bool = True):
+        """Forward ids at the current KV length; returns [n, vocab] logits."""
+        ids = _u32(ids)
+        out = np.empty((len(ids), self.target.cfg.vocab), np.float32) if logits else None
+        check(lib().mc_forward(self.handle, ids.ctypes.data_as(C.POINTER(C.c_uint32)), len(ids),
+                               out.ctypes.data_as(C.POINTER(C.c_float)) if logits else None))
+        return out
+
+    def draft_forward(self, ids, logits: bool = True):
+        ids = _u32(ids)
+        out = np.empty((len(ids), self.draft.cfg.vocab), np.float32) if logits else None
+        check(lib().mc_draft_forward(self.handle, ids.ctypes.data_as(C.POINTER(C.c_uint32)),
+                                     len(ids),
+                                     out.ctypes.data_as(C.POINTER(C.c_float)) if logits else None))
+        return out
+
+    def kv_len(self) -> int:
+        return int(lib().mc_kv_len(self.handle))
+
+    def kv_truncate(self, n: int):
+        check(lib().mc_kv_truncate(self.handle, n))
+
+    # -- DraftModel::draft ---------------------------------------------------
+    def draft_tokens(self, context, gamma: int):
+        ctx = _u32(context)
+        out = np.zeros(max(gamma, 1), np.uint32)
+        n = C.c_int32()
+        check(lib().mc_draft(self.handle, ctx.ctypes.data_as(C.POINTER(C.c_uint32)), len(ctx),
+                             gamma, out.ctypes.data_as(C.POINTER(C.c_uint32)), C.byref(n)))
+        return out[: n.value].tolist()
+
+    # -- speculative_generate ------------------------------------------------
+    def speculative_generate(self, prompt, max_tokens: int):
+        """Returns (generated ids, accepted-draft count per round)."""
+        p = _u32(prompt)
+        cap = max_tokens + self.gamma + 2
+        out = np.zeros(cap, np.uint32)
+        acc = np.zeros(cap + 1, np.int32)
+        n_out, n_rounds = C.c_int32(), C.c_int32()
+        check(lib().mc_speculative_generate(
+            self.handle, p.ctypes.data_as(C.POINTER(C.c_uint32)), len(p), max_tokens,
+            out.ctypes.data_as(C.POINTER(C.c_uint32)), cap, C.byref(n_out),
+            acc.ctypes.data_as(C.POINTER(C.c_int32)), len(acc), C.byref(n_rounds)))
+        return out[: n_out.value].tolist(), acc[: min(n_rounds.value, len(acc))].tolist()
+
+    def prime(self, prompt):
+        p = _u32(prompt)
+        check(lib().mc_spec_prime(self.handle, p.ctypes.data_as(C.POINTER(C.c_uint32)), len(p)))
+
+    def decode(self, max_tokens: int) -> int:
+        n = C.c_int32()
+        check(lib().mc_spec_decode(self.handle, max_tokens, C.byref(n)))
+        return n.value
+
+    def read(self, cap: int = 1 << 16):
+        out = np.zeros(cap, np.uint32)
+        acc = np.zeros(cap, np.int32)
+        n_out, n_rounds = C.c_int32(), C.c_int32()
+        check(lib().mc_spec_read(self.handle, out.ctypes.data_as(C.POINTER(C.c_uint32)), cap,
+                                 C.byref(n_out), acc.ctypes.data_as(C.POINTER(C.c_int32)), cap,
+                                 C.byref(n_rounds)))
+        return out[: n_out.value].tolist(), acc[: min(n_rounds.value, cap)].tolist()
+
+    def rewind(self):
+        """Back to the primed prompt (its KV kept)."""
+        check(lib().mc_spec_rewind(self.handle))
+
+    def verify_launch(self, n: int):
+        """Enqueue n verify forwards on the session stream (timing only)."""
+        check(lib().mc_spec_verify_launch(self.handle, n))
+
+    @property
+    def stream_ptr(self) -> int:
+        return int(lib().mc_session_stream(self.handle) or 0)
+
+    @property
+    def round_launches(self) -> int:
+        return int(lib().mc_session_round_launches(self.handle))
+
+    def cancel(self):
+        self._cancel.value = 1
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().mc_session_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class LlamaDraftModel:
+    """A transformer drafter behind the reference's DraftModel trait
+    (draft.rs:18-21): ``draft(context, gamma) -> list of ids``."""
+
+    def __init__(self, target: Weights, draft: Weights, max_context: int = 2048):
+        self.session = Session(target, draft, gamma=1, max_context=max_context)
+
+    def draft(self, context, gamma: int):
+        return self.session.draft_tokens(context, gamma)
+
+
+def speculative_generate(target: Weights, draft: Weights, prompt, config: GenerationConfig,
+                         max_context: int | None = None):
+    """generate.rs:598-767 with a transformer draft; returns (ids, accepted)."""
+    if config.temperature > 0:
+        raise NotImplementedError("stochastic acceptance is not built yet")
+    cap = max_context or (len(prompt) + config.max_tokens + config.gamma + 8)
+    s = Session(target, draft, gamma=config.gamma, max_context=cap, bonus=config.bonus)
+    try:
+        return s.speculative_generate(prompt, config.max_tokens)
+    finally:
+        s.close()
+
+
+def forward_llama_cached(session: Session, ids):
+    """Batched transformer.rs:64-96: logits for each id, KV appended."""
+    return session.forward(ids)

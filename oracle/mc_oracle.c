@@ -1,0 +1,969 @@
+/*
+ * mc_oracle.c -- CPU restatement of modelc's speculative-decoding path.
+ *
+ * TEST INFRASTRUCTURE ONLY (the parity oracle).  See mc_oracle.h.
+ * Compiled with -O2 -fno-fast-math -ffp-contract=off so
+ * every f32 multiply and add is rounded separately, in the reference's order.
+ * All reference citations are paths inside the yingkitw/modelc repository.
+ */
+#include "mc_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#include <pthread.h>
+
+/* ======================= numeric helpers ======================= */
+
+/* transformer.rs:825-843 linear_with: y[r] = bias[r] + sum_c W[r,c]*x[c],
+ * c ascending, multiply then add (Rust does not contract to FMA). */
+void oracle_linear(const float* w, int rows, int cols, const float* bias,
+                   const float* x, float* out) {
+  for (int r = 0; r < rows; ++r) {
+    float acc = bias ? bias[r] : 0.0f;
+    const float* row = w + (size_t)r * cols;
+    for (int c = 0; c < cols; ++c) acc += row[c] * x[c];
+    out[r] = acc;
+  }
+}
+
+/* Bit-identical parallel variant of linear_with: output rows are split over
+ * pthreads and eight rows are interleaved per thread; every row keeps its own
+ * sequential c-ascending f32 sum, so each output equals oracle_linear's. */
+typedef struct {
+  const float* w;
+  const float* x;
+  float* out;
+  int cols, b0, b1, rows;
+} lin_job;
+
+static void* lin_worker(void* arg) {
+  lin_job* j = (lin_job*)arg;
+  int cols = j->cols;
+  const float* x = j->x;
+  for (int b = j->b0; b < j->b1; ++b) {
+    int r0 = b * 8;
+    int nr = j->rows - r0 < 8 ? j->rows - r0 : 8;
+    if (nr == 8) {
+      const float* p0 = j->w + (size_t)r0 * cols;
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f, a5 = 0.f,
+            a6 = 0.f, a7 = 0.f;
+      for (int c = 0; c < cols; ++c) {
+        float xc = x[c];
+        a0 += p0[c] * xc;
+        a1 += p0[(size_t)cols + c] * xc;
+        a2 += p0[(size_t)2 * cols + c] * xc;
+        a3 += p0[(size_t)3 * cols + c] * xc;
+        a4 += p0[(size_t)4 * cols + c] * xc;
+        a5 += p0[(size_t)5 * cols + c] * xc;
+        a6 += p0[(size_t)6 * cols + c] * xc;
+        a7 += p0[(size_t)7 * cols + c] * xc;
+      }
+      float* o = j->out + r0;
+      o[0] = a0; o[1] = a1; o[2] = a2; o[3] = a3;
+      o[4] = a4; o[5] = a5; o[6] = a6; o[7] = a7;
+    } else {
+      for (int r = r0; r < r0 + nr; ++r) {
+        float acc = 0.0f;
+        const float* row = j->w + (size_t)r * cols;
+        for (int c = 0; c < cols; ++c) acc += row[c] * x[c];
+        j->out[r] = acc;
+      }
+    }
+  }
+  return NULL;
+}
+
+void oracle_linear_par(const float* w, int rows, int cols, const float* x,
+                       float* out, int n_threads) {
+  int nblk = (rows + 7) / 8;
+  if (n_threads < 1) n_threads = 1;
+  if (n_threads > 256) n_threads = 256;
+  if (n_threads > nblk) n_threads = nblk > 0 ? nblk : 1;
+  pthread_t th[256];
+  lin_job jobs[256];
+  for (int t = 0; t < n_threads; ++t) {
+    jobs[t].w = w;
+    jobs[t].x = x;
+    jobs[t].out = out;
+    jobs[t].cols = cols;
+    jobs[t].rows = rows;
+    jobs[t].b0 = (int)((long long)nblk * t / n_threads);
+    jobs[t].b1 = (int)((long long)nblk * (t + 1) / n_threads);
+  }
+  for (int t = 1; t < n_threads; ++t) pthread_create(&th[t], NULL, lin_worker, &jobs[t]);
+  lin_worker(&jobs[0]);
+  for (int t = 1; t < n_threads; ++t) pthread_join(th[t], NULL);
+}
+
+/* transformer.rs:888-896 rms_norm: ms = sum(v*v)/n; rms = sqrt(ms+eps);
+ * out = v / rms * w  (w defaults to 1.0 past its length). */
+void oracle_rms_norm(const float* x, int n, const float* w, int wlen, float eps,
+                     float* out) {
+  float nf = (float)(n > 1 ? n : 1);
+  float ss = 0.0f;
+  for (int i = 0; i < n; ++i) ss += x[i] * x[i];
+  float ms = ss / nf;
+  float rms = sqrtf(ms + eps);
+  for (int i = 0; i < n; ++i) {
+    float wi = (w && i < wlen) ? w[i] : 1.0f;
+    out[i] = x[i] / rms * wi;
+  }
+}
+
+/* transformer.rs:907-909 silu: v / (1 + e^-v). */
+void oracle_silu(const float* x, int n, float* out) {
+  for (int i = 0; i < n; ++i) out[i] = x[i] / (1.0f + expf(-x[i]));
+}
+
+/* transformer.rs:911-916 add: elementwise, missing entries read as 0. */
+void oracle_add(const float* a, int na, const float* b, int nb, float* out) {
+  int n = na > nb ? na : nb;
+  for (int i = 0; i < n; ++i) {
+    float av = i < na ? a[i] : 0.0f;
+    float bv = i < nb ? b[i] : 0.0f;
+    out[i] = av + bv;
+  }
+}
+
+/* transformer.rs:921-938 rope: rotate-half pairs (i, i+half) of each head,
+ * theta = pos * base^(-i/half) in f32, sin/cos from libm. */
+void oracle_rope(const float* x, int n, int pos, int n_heads, float base,
+                 float* out) {
+  int nh = n_heads > 1 ? n_heads : 1;
+  int head_dim = n / nh;
+  if (head_dim < 1) head_dim = 1;
+  int half = head_dim / 2;
+  if (out != x) memcpy(out, x, sizeof(float) * (size_t)n);
+  for (int h = 0; h < n_heads; ++h) {
+    int off = h * head_dim;
+    for (int i = 0; i < half; ++i) {
+      float expo = -(float)i / (float)half;
+      float theta = (float)pos * powf(base, expo);
+      float s = sinf(theta), c = cosf(theta);
+      float x0 = x[off + i];
+      float x1 = x[off + i + half];
+      out[off + i] = x0 * c - x1 * s;
+      out[off + i + half] = x0 * s + x1 * c;
+    }
+  }
+}
+
+/* The per-(pos, i) cos/sin factors oracle_rope uses, laid out [pos][half]. */
+void oracle_rope_table(int max_pos, int head_dim, float base, float* cos_out,
+                       float* sin_out) {
+  int half = head_dim / 2;
+  for (int p = 0; p < max_pos; ++p)
+    for (int i = 0; i < half; ++i) {
+      float expo = -(float)i / (float)half;
+      float theta = (float)p * powf(base, expo);
+      cos_out[(size_t)p * half + i] = cosf(theta);
+      sin_out[(size_t)p * half + i] = sinf(theta);
+    }
+}
+
+/* transformer.rs:985-1000 softmax_inplace: max fold from -inf, exp(x-max),
+ * sequential sum, divide when the sum is positive. */
+void oracle_softmax_inplace(float* xs, int n) {
+  if (n <= 0) return;
+  float mx = -INFINITY;
+  for (int i = 0; i < n; ++i) mx = fmaxf(mx, xs[i]);
+  float sum = 0.0f;
+  for (int i = 0; i < n; ++i) {
+    xs[i] = expf(xs[i] - mx);
+    sum += xs[i];
+  }
+  if (sum > 0.0f)
+    for (int i = 0; i < n; ++i) xs[i] /= sum;
+}
+
+/* transformer.rs:944-982 attention_kv.  k_all/v_all hold seq_len positions of
+ * n_kv_heads*head_dim floats.  With n_kv_heads == n_heads this is exactly the
+ * reference (MHA); with fewer KV heads query head h reads KV head
+ * h / (n_heads/n_kv_heads) (grouped-query generalisation). */
+void oracle_attention_kv(const float* q, int q_len, const float* k_all,
+                         const float* v_all, int seq_len, int n_heads,
+                         int n_kv_heads, float* out) {
+  int nh = n_heads > 1 ? n_heads : 1;
+  int head_dim = q_len / nh;
+  if (head_dim < 1) head_dim = 1;
+  int group = n_heads / (n_kv_heads > 0 ? n_kv_heads : 1);
+  if (group < 1) group = 1;
+  int kv_stride = n_kv_heads * head_dim;
+  float* scores = (float*)malloc(sizeof(float) * (size_t)(seq_len > 0 ? seq_len : 1));
+  float scale = sqrtf((float)head_dim);
+  for (int h = 0; h < n_heads; ++h) {
+    const float* qh = q + (size_t)h * head_dim;
+    int kvh = h / group;
+    for (int t = 0; t < seq_len; ++t) {
+      const float* kh = k_all + (size_t)t * kv_stride + (size_t)kvh * head_dim;
+      float dot = 0.0f;
+      for (int i = 0; i < head_dim; ++i) dot += qh[i] * kh[i];
+      scores[t] = dot / scale;
+    }
+    oracle_softmax_inplace(scores, seq_len);
+    float* oh = out + (size_t)h * head_dim;
+    for (int i = 0; i < head_dim; ++i) oh[i] = 0.0f;
+    for (int t = 0; t < seq_len; ++t) {
+      const float* vh = v_all + (size_t)t * kv_stride + (size_t)kvh * head_dim;
+      float wgt = scores[t];
+      for (int i = 0; i < head_dim; ++i) oh[i] += wgt * vh[i];
+    }
+  }
+  free(scores);
+}
+
+/* ======================= sampling ======================= */
+
+/* generate.rs:1088-1098 argmax: first strict maximum, NaN never wins. */
+int oracle_argmax(const float* xs, int n) {
+  int best = 0;
+  float best_val = -INFINITY;
+  for (int i = 0; i < n; ++i)
+    if (xs[i] > best_val) {
+      best = i;
+      best_val = xs[i];
+    }
+  return best;
+}
+
+/* generate.rs:1100-1105 softmax (no zero-sum guard). */
+void oracle_softmax(const float* xs, int n, float* out) {
+  float mx = -INFINITY;
+  for (int i = 0; i < n; ++i) mx = fmaxf(mx, xs[i]);
+  float sum = 0.0f;
+  for (int i = 0; i < n; ++i) {
+    out[i] = expf(xs[i] - mx);
+    sum += out[i];
+  }
+  for (int i = 0; i < n; ++i) out[i] = out[i] / sum;
+}
+
+typedef struct {
+  float p;
+  int i;
+} prob_idx;
+
+static int cmp_prob_desc(const void* a, const void* b) {
+  const prob_idx* x = (const prob_idx*)a;
+  const prob_idx* y = (const prob_idx*)b;
+  if (x->p > y->p) return -1;
+  if (x->p < y->p) return 1;
+  return x->i - y->i; /* stable: equal probabilities keep index order */
+}
+
+/* generate.rs:1034-1063 apply_top_p. */
+void oracle_apply_top_p(float* probs, int n, float top_p) {
+  prob_idx* idx = (prob_idx*)malloc(sizeof(prob_idx) * (size_t)(n > 0 ? n : 1));
+  for (int i = 0; i < n; ++i) {
+    idx[i].p = probs[i];
+    idx[i].i = i;
+  }
+  qsort(idx, (size_t)n, sizeof(prob_idx), cmp_prob_desc);
+  float cum = 0.0f;
+  int keep = 0;
+  for (int j = 0; j < n; ++j) {
+    cum += idx[j].p;
+    keep += 1;
+    if (cum >= top_p) break;
+  }
+  char* kept = (char*)calloc((size_t)(n > 0 ? n : 1), 1);
+  for (int j = 0; j < keep; ++j) kept[idx[j].i] = 1;
+  for (int i = 0; i < n; ++i)
+    if (!kept[i]) probs[i] = 0.0f;
+  float sum = 0.0f;
+  for (int i = 0; i < n; ++i) sum += probs[i];
+  if (sum > 0.0f)
+    for (int i = 0; i < n; ++i) probs[i] /= sum;
+  free(kept);
+  free(idx);
+}
+
+/* generate.rs:1071-1086 apply_min_p. */
+void oracle_apply_min_p(float* probs, int n, float min_p) {
+  float mx = 0.0f;
+  for (int i = 0; i < n; ++i) mx = fmaxf(mx, probs[i]);
+  float threshold = mx * min_p;
+  for (int i = 0; i < n; ++i)
+    if (probs[i] < threshold) probs[i] = 0.0f;
+  float sum = 0.0f;
+  for (int i = 0; i < n; ++i) sum += probs[i];
+  if (sum > 0.0f)
+    for (int i = 0; i < n; ++i) probs[i] /= sum;
+}
+
+/* ChaCha block function (D. J. Bernstein, "ChaCha, a variant of Salsa20",
+ * 2008): 64-bit block counter in words 12-13, 64-bit nonce in words 14-15,
+ * `rounds` rounds (rand_chacha's ChaCha12Rng uses 12). */
+#define ROTL32(v, c) (((v) << (c)) | ((v) >> (32 - (c))))
+#define QR(a, b, c, d)              \
+  a += b; d ^= a; d = ROTL32(d, 16); \
+  c += d; b ^= c; b = ROTL32(b, 12); \
+  a += b; d ^= a; d = ROTL32(d, 8);  \
+  c += d; b ^= c; b = ROTL32(b, 7);
+
+void oracle_chacha_block(const uint32_t key[8], uint64_t counter,
+                         uint64_t nonce, int rounds, uint32_t out[16]) {
+  uint32_t s[16] = {0x61707865u, 0x3320646eu, 0x79622d32u, 0x6b206574u,
+                    key[0], key[1], key[2], key[3], key[4], key[5], key[6],
+                    key[7], (uint32_t)counter, (uint32_t)(counter >> 32),
+                    (uint32_t)nonce, (uint32_t)(nonce >> 32)};
+  uint32_t x[16];
+  memcpy(x, s, sizeof(x));
+  for (int r = 0; r < rounds; r += 2) {
+    QR(x[0], x[4], x[8], x[12]);
+    QR(x[1], x[5], x[9], x[13]);
+    QR(x[2], x[6], x[10], x[14]);
+    QR(x[3], x[7], x[11], x[15]);
+    QR(x[0], x[5], x[10], x[15]);
+    QR(x[1], x[6], x[11], x[12]);
+    QR(x[2], x[7], x[8], x[13]);
+    QR(x[3], x[4], x[9], x[14]);
+  }
+  for (int i = 0; i < 16; ++i) out[i] = x[i] + s[i];
+}
+
+/* rand_core 0.6.4 SeedableRng::seed_from_u64: a PCG32 stream (M. O'Neill,
+ * PCG, 2014: LCG multiplier 6364136223846793005, increment
+ * 11634580027462260723, XSH-RR output) fills the 32-byte seed little-endian. */
+static void seed_from_u64(uint64_t state, uint32_t key[8]) {
+  const uint64_t MUL = 6364136223846793005ull;
+  const uint64_t INC = 11634580027462260723ull;
+  for (int i = 0; i < 8; ++i) {
+    state = state * MUL + INC;
+    uint32_t xorshifted = (uint32_t)(((state >> 18) ^ state) >> 27);
+    uint32_t rot = (uint32_t)(state >> 59);
+    key[i] = (xorshifted >> rot) | (xorshifted << ((32 - rot) & 31));
+  }
+}
+
+/* rand 0.8.6: StdRng (= rand_chacha 0.3.1 ChaCha12Rng, key = seed, counter 0,
+ * stream 0) seeded by seed_from_u64, then Standard's f32: the top 24 bits of
+ * next_u32() times 2^-24.  Used by generate.rs:1107-1124 multinomial. */
+float oracle_rand_f32(uint64_t seed) {
+  uint32_t key[8], blk[16];
+  seed_from_u64(seed, key);
+  oracle_chacha_block(key, 0, 0, 12, blk);
+  return (float)(blk[0] >> 8) * (1.0f / 16777216.0f);
+}
+
+/* generate.rs:1107-1124 multinomial with a seed (seed + step). */
+uint32_t oracle_multinomial(const float* probs, int n, uint64_t step,
+                            uint64_t seed) {
+  float r = oracle_rand_f32(seed + step);
+  float cum = 0.0f;
+  for (int i = 0; i < n; ++i) {
+    cum += probs[i];
+    if (r < cum) return (uint32_t)i;
+  }
+  return n > 0 ? (uint32_t)(n - 1) : 0u;
+}
+
+/* generate.rs:948-969 sample (the penalty/constraint-free fast path of
+ * sample_constrained, generate.rs:982-1027). */
+uint32_t oracle_sample(const float* logits, int n, float temperature,
+                       float top_p, float min_p, uint64_t step, uint64_t seed) {
+  if (!logits || n <= 0) return 0;
+  if (temperature <= 0.0f) return (uint32_t)oracle_argmax(logits, n);
+  float* scaled = (float*)malloc(sizeof(float) * (size_t)n);
+  float* probs = (float*)malloc(sizeof(float) * (size_t)n);
+  for (int i = 0; i < n; ++i) scaled[i] = logits[i] / temperature;
+  oracle_softmax(scaled, n, probs);
+  if (top_p > 0.0f && top_p < 1.0f) oracle_apply_top_p(probs, n, top_p);
+  if (min_p > 0.0f && min_p < 1.0f) oracle_apply_min_p(probs, n, min_p);
+  uint32_t t = oracle_multinomial(probs, n, step, seed);
+  free(scaled);
+  free(probs);
+  return t;
+}
+
+/* ======================= weight materialisation ======================= */
+
+/* compiler.rs:207-229 int8 per-tensor quantiser: scale = max|x|/127,
+ * q = round(clamp(x/scale, -127, 127)).  A zero tensor is left unquantised;
+ * *scale = 0 reports that case. */
+void oracle_quantize_int8_tensor(const float* x, size_t n, int8_t* q,
+                                 float* scale) {
+  float max_abs = 0.0f;
+  for (size_t i = 0; i < n; ++i) max_abs = fmaxf(max_abs, fabsf(x[i]));
+  if (!(max_abs > 0.0f)) {
+    *scale = 0.0f;
+    memset(q, 0, n);
+    return;
+  }
+  float s = max_abs / 127.0f;
+  for (size_t i = 0; i < n; ++i) {
+    float v = x[i] / s;
+    v = v < -127.0f ? -127.0f : (v > 127.0f ? 127.0f : v);
+    q[i] = (int8_t)roundf(v);
+  }
+  *scale = s;
+}
+
+/* The same rule applied to each output row of an [out, in] matrix (the
+ * per-row int8 format the B200 kernels stream).  An all-zero row gets scale
+ * 1.0 and zero codes, as transformer.rs:195-197 does for KV rows. */
+void oracle_quantize_int8_rows(const float* x, int rows, int cols, int8_t* q,
+                               float* scales) {
+  for (int r = 0; r < rows; ++r) {
+    float s;
+    oracle_quantize_int8_tensor(x + (size_t)r * cols, (size_t)cols,
+                                q + (size_t)r * cols, &s);
+    scales[r] = s > 0.0f ? s : 1.0f;
+  }
+}
+
+/* model.rs:182-185 int8 dequantisation: (q as f32) * scale, per row. */
+void oracle_dequant_int8_rows(const int8_t* q, const float* scales, int rows,
+                              int cols, float* out) {
+  for (int r = 0; r < rows; ++r)
+    for (int c = 0; c < cols; ++c)
+      out[(size_t)r * cols + c] = (float)q[(size_t)r * cols + c] * scales[r];
+}
+
+void oracle_dequant_int8_tensor(const int8_t* q, float scale, size_t n,
+                                float* out) {
+  for (size_t i = 0; i < n; ++i) out[i] = (float)q[i] * scale;
+}
+
+float oracle_f16_to_f32(uint16_t h) {
+  _Float16 f;
+  memcpy(&f, &h, 2);
+  return (float)f;
+}
+
+uint16_t oracle_f32_to_f16(float f) {
+  _Float16 h = (_Float16)f;
+  uint16_t b;
+  memcpy(&b, &h, 2);
+  return b;
+}
+
+/* q4_0 block quantiser, restating the published ggml reference quantiser
+ * (quantize_row_q4_0_reference, ggml MIT): per 32-element block the value of
+ * largest magnitude m gives d = m / -8, codes = min(15, (int)(x/d + 8.5)),
+ * element j in the low nibble of byte j, element j+16 in the high nibble.
+ * Block = fp16 d (little-endian) + 16 code bytes = 18 bytes. */
+int oracle_quantize_q4_0(const float* x, size_t n, uint8_t* blocks) {
+  if (n % 32) return -1;
+  for (size_t b = 0; b < n / 32; ++b) {
+    const float* xb = x + b * 32;
+    float amax = 0.0f, mx = 0.0f;
+    for (int j = 0; j < 32; ++j)
+      if (amax < fabsf(xb[j])) {
+        amax = fabsf(xb[j]);
+        mx = xb[j];
+      }
+    float d = mx / -8.0f;
+    float id = d != 0.0f ? 1.0f / d : 0.0f;
+    uint16_t dh = oracle_f32_to_f16(d);
+    uint8_t* out = blocks + b * 18;
+    out[0] = (uint8_t)(dh & 0xff);
+    out[1] = (uint8_t)(dh >> 8);
+    for (int j = 0; j < 16; ++j) {
+      float x0 = xb[j] * id, x1 = xb[16 + j] * id;
+      int q0 = (int)(int8_t)(x0 + 8.5f), q1 = (int)(int8_t)(x1 + 8.5f);
+      if (q0 > 15) q0 = 15;
+      if (q1 > 15) q1 = 15;
+      out[2 + j] = (uint8_t)(q0 | (q1 << 4));
+    }
+  }
+  return 0;
+}
+
+/* parsers/gguf/dequant.rs:23-46 dequantize_q4_0: y[j] = (lo-8)*d,
+ * y[j+16] = (hi-8)*d with d the block's fp16 scale widened to f32. */
+int oracle_dequant_q4_0(const uint8_t* blocks, size_t n, float* out) {
+  if (n % 32) return -1;
+  for (size_t b = 0; b < n / 32; ++b) {
+    const uint8_t* blk = blocks + b * 18;
+    float d = oracle_f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+    for (int j = 0; j < 16; ++j) {
+      int x0 = (blk[2 + j] & 0x0F) - 8;
+      int x1 = (blk[2 + j] >> 4) - 8;
+      out[b * 32 + j] = (float)x0 * d;
+      out[b * 32 + j + 16] = (float)x1 * d;
+    }
+  }
+  return 0;
+}
+
+/* ======================= model + KV cache ======================= */
+
+/* Resolve the head geometry.  Reference mode follows arch.rs:128-137 (the
+ * runtime view drops metadata, transformer.rs:1007-1027, so heads = hidden/64)
+ * and the hard-coded constants at transformer.rs:91, :775, :806 and :925. */
+int oracle_model_resolve(oracle_model* m) {
+  if (m->mode == ORACLE_MODE_REFERENCE) {
+    int nh = m->hidden == 0 ? 1 : m->hidden / 64;
+    if (nh < 1) nh = 1;
+    m->n_heads = nh;
+    m->head_dim = m->hidden / nh;
+    if (m->head_dim < 1) m->head_dim = 1;
+    if (m->n_kv_heads != 0 && m->n_kv_heads != nh) return -1; /* MHA only */
+    m->n_kv_heads = nh;
+    m->rope_base = 10000.0f;
+    m->eps = 1e-6f;
+  }
+  if (m->n_heads <= 0 || m->n_kv_heads <= 0 || m->head_dim <= 0) return -1;
+  if (m->n_heads % m->n_kv_heads) return -1;
+  return 0;
+}
+
+oracle_kv* oracle_kv_new(int n_layers, int kv_dim, int cap) {
+  oracle_kv* kv = (oracle_kv*)calloc(1, sizeof(oracle_kv));
+  kv->n_layers = n_layers;
+  kv->kv_dim = kv_dim;
+  kv->cap = cap;
+  kv->len = 0;
+  size_t n = (size_t)n_layers * (size_t)cap * (size_t)kv_dim;
+  kv->k = (float*)calloc(n > 0 ? n : 1, sizeof(float));
+  kv->v = (float*)calloc(n > 0 ? n : 1, sizeof(float));
+  return kv;
+}
+
+void oracle_kv_free(oracle_kv* kv) {
+  if (!kv) return;
+  free(kv->k);
+  free(kv->v);
+  free(kv);
+}
+
+/* Dropping positions from the end (speculative rollback).  The reference has
+ * only front eviction (transformer.rs:424-583); its sequential verify never
+ * forwards a rejected draft, and truncation reproduces exactly that state. */
+void oracle_kv_truncate(oracle_kv* kv, int len) {
+  if (len < kv->len) kv->len = len < 0 ? 0 : len;
+}
+
+int oracle_kv_len(const oracle_kv* kv) { return kv ? kv->len : 0; }
+
+/* generate.rs:843-863 token_embedding: the id's row, zeros when out of range. */
+void oracle_token_embedding(const oracle_model* m, uint32_t id, float* out) {
+  if (m->embed && (size_t)id < (size_t)m->vocab) {
+    memcpy(out, m->embed + (size_t)id * m->hidden, sizeof(float) * (size_t)m->hidden);
+  } else {
+    memset(out, 0, sizeof(float) * (size_t)m->hidden);
+  }
+}
+
+static void lin(const oracle_model* m, const float* w, int rows, int cols,
+                const float* x, float* out) {
+  if (m->n_threads > 1)
+    oracle_linear_par(w, rows, cols, x, out, m->n_threads);
+  else
+    oracle_linear(w, rows, cols, NULL, x, out);
+}
+
+/* transformer.rs:64-96 forward_llama_cached with llama_step (:739-760),
+ * llama_attention (:762-798) and llama_mlp (:800-817).  Returns 1 when logits
+ * were produced, 0 when the model has no output head (the reference's None). */
+int oracle_forward(const oracle_model* m, const float* input, oracle_kv* kv,
+                   float* logits) {
+  int d = m->hidden, hd = m->head_dim;
+  int qd = m->n_heads * hd, kvd = m->n_kv_heads * hd, f = m->ffn;
+  float* h = (float*)malloc(sizeof(float) * (size_t)d);
+  float* normed = (float*)malloc(sizeof(float) * (size_t)d);
+  float* tmp = (float*)malloc(sizeof(float) * (size_t)d);
+  float* q = (float*)malloc(sizeof(float) * (size_t)qd);
+  float* k = (float*)malloc(sizeof(float) * (size_t)kvd);
+  float* v = (float*)malloc(sizeof(float) * (size_t)kvd);
+  float* attn = (float*)malloc(sizeof(float) * (size_t)qd);
+  float* g = (float*)malloc(sizeof(float) * (size_t)(f > 0 ? f : 1));
+  float* u = (float*)malloc(sizeof(float) * (size_t)(f > 0 ? f : 1));
+  memcpy(h, input, sizeof(float) * (size_t)d);
+  int pos = kv ? kv->len : 0;
+
+  for (int l = 0; l < m->n_layers; ++l) {
+    const oracle_layer* L = &m->layers[l];
+    if (L->wq && L->wk && L->wv && L->wo) {
+      if (L->attn_norm)
+        oracle_rms_norm(h, d, L->attn_norm, d, m->eps, normed);
+      else
+        memcpy(normed, h, sizeof(float) * (size_t)d);
+      lin(m, L->wq, qd, d, normed, q);
+      lin(m, L->wk, kvd, d, normed, k);
+      lin(m, L->wv, kvd, d, normed, v);
+      oracle_rope(q, qd, pos, m->n_heads, m->rope_base, q);
+      oracle_rope(k, kvd, pos, m->n_kv_heads, m->rope_base, k);
+      const float *k_all = k, *v_all = v;
+      int seq = 1;
+      if (kv && pos < kv->cap) {
+        float* kl = kv->k + ((size_t)l * kv->cap) * kvd;
+        float* vl = kv->v + ((size_t)l * kv->cap) * kvd;
+        memcpy(kl + (size_t)pos * kvd, k, sizeof(float) * (size_t)kvd);
+        memcpy(vl + (size_t)pos * kvd, v, sizeof(float) * (size_t)kvd);
+        k_all = kl;
+        v_all = vl;
+        seq = pos + 1;
+      }
+      oracle_attention_kv(q, qd, k_all, v_all, seq, m->n_heads, m->n_kv_heads,
+                          attn);
+      lin(m, L->wo, d, qd, attn, tmp);
+      oracle_add(h, d, tmp, d, h);
+    }
+    if (L->wg && L->wu && L->wd) {
+      if (L->mlp_norm)
+        oracle_rms_norm(h, d, L->mlp_norm, d, m->eps, normed);
+      else
+        memcpy(normed, h, sizeof(float) * (size_t)d);
+      lin(m, L->wg, f, d, normed, g);
+      lin(m, L->wu, f, d, normed, u);
+      oracle_silu(g, f, g);
+      for (int i = 0; i < f; ++i) g[i] = g[i] * u[i];
+      lin(m, L->wd, d, f, g, tmp);
+      oracle_add(h, d, tmp, d, h);
+    }
+  }
+  if (kv && pos < kv->cap) kv->len = pos + 1;
+
+  if (m->final_norm) oracle_rms_norm(h, d, m->final_norm, d, m->eps, h);
+  int have = 0;
+  const float* head = m->lm_head ? m->lm_head : m->embed;
+  if (head && logits) {
+    lin(m, head, m->vocab, d, h, logits);
+    have = 1;
+  } else if (head) {
+    have = 1;
+  }
+  free(h); free(normed); free(tmp); free(q); free(k); free(v); free(attn);
+  free(g); free(u);
+  return have;
+}
+
+/* Batched form of forward_llama_cached: n single-token forwards in order, one
+ * logits row per position (the per-position math is unchanged). */
+int oracle_forward_ids(const oracle_model* m, const uint32_t* ids, int n,
+                       oracle_kv* kv, float* logits) {
+  float* e = (float*)malloc(sizeof(float) * (size_t)m->hidden);
+  int have = 1;
+  for (int i = 0; i < n; ++i) {
+    oracle_token_embedding(m, ids[i], e);
+    have = oracle_forward(m, e, kv,
+                          logits ? logits + (size_t)i * m->vocab : NULL);
+  }
+  free(e);
+  return have;
+}
+
+/* ======================= drafters ======================= */
+
+struct oracle_llama_draft {
+  const oracle_model* m;
+  oracle_kv* kv;
+  uint32_t* cached; /* token at each KV position */
+  float* logits;
+  float* emb;
+};
+
+/* A transformer draft behind the DraftModel trait (draft.rs:18-21).  The
+ * reference ships no transformer drafter; this one is defined as: greedily
+ * decode `gamma` tokens after `ctx` with the draft model.  The KV of the
+ * longest common prefix with the previous call is reused, which gives the same
+ * result as a fresh forward over ctx because each position's math only reads
+ * earlier positions. */
+oracle_llama_draft* oracle_llama_draft_new(const oracle_model* m, int cap) {
+  oracle_llama_draft* d = (oracle_llama_draft*)calloc(1, sizeof(*d));
+  d->m = m;
+  d->kv = oracle_kv_new(m->n_layers, m->n_kv_heads * m->head_dim, cap);
+  d->cached = (uint32_t*)calloc((size_t)cap, sizeof(uint32_t));
+  d->logits = (float*)malloc(sizeof(float) * (size_t)m->vocab);
+  d->emb = (float*)malloc(sizeof(float) * (size_t)m->hidden);
+  return d;
+}
+
+void oracle_llama_draft_free(oracle_llama_draft* d) {
+  if (!d) return;
+  oracle_kv_free(d->kv);
+  free(d->cached);
+  free(d->logits);
+  free(d->emb);
+  free(d);
+}
+
+static void draft_step(oracle_llama_draft* d, uint32_t tok) {
+  int pos = d->kv->len;
+  oracle_token_embedding(d->m, tok, d->emb);
+  oracle_forward(d->m, d->emb, d->kv, d->logits);
+  if (pos < d->kv->cap) d->cached[pos] = tok;
+}
+
+int oracle_llama_draft_run(oracle_llama_draft* d, const uint32_t* ctx, int n,
+                       int gamma, uint32_t* out) {
+  if (n <= 0 || gamma <= 0) return 0;
+  if (n + gamma > d->kv->cap) return 0;
+  int p = 0;
+  while (p < d->kv->len && p < n && d->cached[p] == ctx[p]) ++p;
+  if (p > n - 1) p = n - 1;
+  oracle_kv_truncate(d->kv, p);
+  for (int i = p; i < n; ++i) draft_step(d, ctx[i]);
+  for (int j = 0; j < gamma; ++j) {
+    out[j] = (uint32_t)oracle_argmax(d->logits, d->m->vocab);
+    if (j + 1 < gamma) draft_step(d, out[j]);
+  }
+  return gamma;
+}
+
+/* draft.rs:91-147 MlpDraftModel::{forward, draft}: embed -> FC1+ReLU -> FC2
+ * -> argmax (temperature <= 0).  The reference samples with an unseeded
+ * thread_rng when temperature > 0; the restatement draws from seed 0. */
+int oracle_mlp_draft_run(const oracle_mlp_draft* d, const uint32_t* ctx, int n,
+                         int gamma, uint32_t* out) {
+  uint32_t cur = n > 0 ? ctx[n - 1] : 0u;
+  float* hid = (float*)malloc(sizeof(float) * (size_t)(d->draft_hidden > 0 ? d->draft_hidden : 1));
+  float* logits = (float*)malloc(sizeof(float) * (size_t)(d->vocab > 0 ? d->vocab : 1));
+  for (int s = 0; s < gamma; ++s) {
+    size_t idx = (size_t)cur * d->hidden;
+    if (idx + d->hidden <= (size_t)d->vocab * d->hidden) {
+      const float* e = d->embed + idx;
+      for (int i = 0; i < d->draft_hidden; ++i) {
+        float sum = d->b1[i];
+        const float* row = d->w1 + (size_t)i * d->hidden;
+        for (int j = 0; j < d->hidden; ++j) sum += row[j] * e[j];
+        hid[i] = fmaxf(sum, 0.0f);
+      }
+      for (int i = 0; i < d->vocab; ++i) {
+        float sum = d->b2[i];
+        const float* row = d->w2 + (size_t)i * d->draft_hidden;
+        for (int j = 0; j < d->draft_hidden; ++j) sum += row[j] * hid[j];
+        logits[i] = sum;
+      }
+    } else {
+      memset(logits, 0, sizeof(float) * (size_t)d->vocab);
+    }
+    uint32_t next = d->temperature <= 0.0f
+                        ? (uint32_t)oracle_argmax(logits, d->vocab)
+                        : oracle_sample(logits, d->vocab, d->temperature,
+                                        d->top_p, 0.0f, 0, 0);
+    out[s] = next;
+    cur = next;
+  }
+  free(hid);
+  free(logits);
+  return gamma;
+}
+
+/* generate.rs:771-841 n-gram drafter.  `tokens` holds the (key, next) pairs
+ * the index was built from, as a flat token sequence per window; here the
+ * index is rebuilt from the window list passed in (see ngram_* below). */
+typedef struct {
+  uint32_t* keys; /* n per entry */
+  uint32_t* next;
+  int len, cap, n;
+} ngram_index;
+
+static void ngram_push(ngram_index* ix, const uint32_t* key, uint32_t next) {
+  if (ix->len == ix->cap) {
+    ix->cap = ix->cap ? ix->cap * 2 : 64;
+    ix->keys = (uint32_t*)realloc(ix->keys, sizeof(uint32_t) * (size_t)ix->cap * ix->n);
+    ix->next = (uint32_t*)realloc(ix->next, sizeof(uint32_t) * (size_t)ix->cap);
+  }
+  memcpy(ix->keys + (size_t)ix->len * ix->n, key, sizeof(uint32_t) * (size_t)ix->n);
+  ix->next[ix->len++] = next;
+}
+
+/* generate.rs:771-784 build_ngram_index. */
+static void ngram_build(ngram_index* ix, const uint32_t* t, int len) {
+  if (len < ix->n + 1) return;
+  for (int s = 0; s + ix->n < len; ++s) ngram_push(ix, t + s, t[s + ix->n]);
+}
+
+/* generate.rs:787-801 update_ngram_index: adds only the window ending at the
+ * last token. */
+static void ngram_update(ngram_index* ix, const uint32_t* t, int len) {
+  if (len < ix->n + 1) return;
+  int s = len - (ix->n + 1);
+  ngram_push(ix, t + s, t[s + ix->n]);
+}
+
+/* generate.rs:804-841 draft_tokens + most_frequent.  The reference breaks
+ * count ties by HashMap iteration order (unspecified); the restatement takes
+ * the candidate seen first. */
+static int ngram_draft(const ngram_index* ix, const uint32_t* ctx, int n_ctx,
+                       int gamma, uint32_t* out) {
+  int n = ix->n, cnt = 0;
+  uint32_t* c = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)(n_ctx + gamma + 1));
+  memcpy(c, ctx, sizeof(uint32_t) * (size_t)n_ctx);
+  int clen = n_ctx;
+  uint32_t* cands = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)(ix->len + 1));
+  for (int g = 0; g < gamma; ++g) {
+    if (clen < n) break; /* a short key never equals an n-token key */
+    const uint32_t* key = c + clen - n;
+    int nc = 0;
+    for (int e = 0; e < ix->len; ++e)
+      if (!memcmp(ix->keys + (size_t)e * n, key, sizeof(uint32_t) * (size_t)n))
+        cands[nc++] = ix->next[e];
+    if (nc == 0) break;
+    uint32_t best = cands[0];
+    int best_count = 0;
+    for (int i = 0; i < nc; ++i) {
+      int seen_before = 0;
+      for (int j = 0; j < i; ++j)
+        if (cands[j] == cands[i]) { seen_before = 1; break; }
+      if (seen_before) continue;
+      int count = 0;
+      for (int j = i; j < nc; ++j) count += cands[j] == cands[i];
+      if (count > best_count) {
+        best_count = count;
+        best = cands[i];
+      }
+    }
+    out[cnt++] = best;
+    c[clen++] = best;
+  }
+  free(cands);
+  free(c);
+  return cnt;
+}
+
+int oracle_ngram_draft(const uint32_t* tokens, int n_tokens,
+                       const uint32_t* ctx, int n_ctx, int ngram, int gamma,
+                       uint32_t* out) {
+  ngram_index ix = {0};
+  ix.n = ngram;
+  ngram_build(&ix, tokens, n_tokens);
+  int r = ngram_draft(&ix, ctx, n_ctx, gamma, out);
+  free(ix.keys);
+  free(ix.next);
+  return r;
+}
+
+/* ======================= generation ======================= */
+
+static int is_cancelled(const oracle_gen_cfg* cfg) {
+  return cfg->cancel && *cfg->cancel;
+}
+
+/* generate.rs:399-525 generate_core (penalties, constraints, stop strings and
+ * context shifting are off at the default config and are not restated). */
+int oracle_generate_core(const oracle_model* m, const uint32_t* prompt,
+                         int n_prompt, const oracle_gen_cfg* cfg,
+                         uint32_t* out, int cap) {
+  if (n_prompt <= 0) return 0;
+  oracle_kv* kv = oracle_kv_new(m->n_layers, m->n_kv_heads * m->head_dim,
+                                n_prompt + cfg->max_tokens + 1);
+  float* logits = (float*)malloc(sizeof(float) * (size_t)m->vocab);
+  float* e = (float*)malloc(sizeof(float) * (size_t)m->hidden);
+  int have = 0;
+  for (int i = 0; i < n_prompt; ++i) {
+    oracle_token_embedding(m, prompt[i], e);
+    have = oracle_forward(m, e, kv, logits);
+  }
+  int generated = 0;
+  if (have) {
+    for (;;) {
+      if (generated >= cfg->max_tokens || is_cancelled(cfg)) break;
+      uint32_t next = oracle_sample(logits, m->vocab, cfg->temperature,
+                                    cfg->top_p, cfg->min_p,
+                                    (uint64_t)generated, cfg->seed);
+      if (generated < cap) out[generated] = next;
+      generated++;
+      if (cfg->tok_vocab > 0 && (int)next >= cfg->tok_vocab) break;
+      oracle_token_embedding(m, next, e);
+      if (!oracle_forward(m, e, kv, logits)) break;
+    }
+  }
+  oracle_kv_free(kv);
+  free(logits);
+  free(e);
+  return generated < cap ? generated : cap;
+}
+
+/* generate.rs:598-767 speculative_generate, restated in order: prime every
+ * prompt token (logits discarded), then per round draft `gamma` tokens and
+ * verify them one forward at a time starting from the last context token
+ * (which re-forwards the last prompt token once), accepting while the
+ * target's sample equals the draft and pushing the target's token at the
+ * first mismatch.  No bonus token unless cfg->bonus (then a fully accepted
+ * round forwards the last draft and pushes the target's next token, the
+ * k+1-position verify).  Returns the number of generated tokens; accepted[]
+ * receives each round's accepted-draft count. */
+int oracle_speculative_generate(const oracle_model* m, int draft_kind,
+                                void* drafter, const uint32_t* prompt,
+                                int n_prompt, const oracle_gen_cfg* cfg,
+                                uint32_t* out, int cap, int* accepted,
+                                int* n_rounds, int rounds_cap) {
+  if (n_rounds) *n_rounds = 0;
+  if (n_prompt <= 0) return 0;
+  int gamma = cfg->gamma;
+  int tcap = n_prompt + cfg->max_tokens + gamma + 2;
+  uint32_t* tok = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)tcap);
+  memcpy(tok, prompt, sizeof(uint32_t) * (size_t)n_prompt);
+  int len = n_prompt, prompt_len = n_prompt;
+  oracle_kv* kv = oracle_kv_new(m->n_layers, m->n_kv_heads * m->head_dim, tcap + 1);
+  float* logits = (float*)malloc(sizeof(float) * (size_t)m->vocab);
+  float* e = (float*)malloc(sizeof(float) * (size_t)m->hidden);
+  uint32_t* draft = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)(gamma + 1));
+  ngram_index ix = {0};
+  ix.n = 3;
+  ngram_build(&ix, tok, len);
+
+  for (int i = 0; i < n_prompt; ++i) {
+    oracle_token_embedding(m, prompt[i], e);
+    oracle_forward(m, e, kv, logits);
+  }
+  int rounds = 0;
+  while (len - prompt_len < cfg->max_tokens) {
+    if (is_cancelled(cfg)) break;
+    int nd = 0;
+    if (draft_kind == ORACLE_DRAFT_LLAMA)
+      nd = oracle_llama_draft_run((oracle_llama_draft*)drafter, tok, len, gamma, draft);
+    else if (draft_kind == ORACLE_DRAFT_MLP)
+      nd = oracle_mlp_draft_run((const oracle_mlp_draft*)drafter, tok, len, gamma, draft);
+    else if (draft_kind == ORACLE_DRAFT_NGRAM)
+      nd = ngram_draft(&ix, tok, len, gamma, draft);
+    if (nd == 0) {
+      uint32_t last = tok[len - 1];
+      oracle_token_embedding(m, last, e);
+      int have = oracle_forward(m, e, kv, logits);
+      uint32_t next = oracle_sample(have ? logits : NULL, m->vocab,
+                                    cfg->temperature, cfg->top_p, cfg->min_p,
+                                    (uint64_t)(len - prompt_len), cfg->seed);
+      tok[len++] = next;
+      ngram_update(&ix, tok, len);
+      if (cfg->tok_vocab > 0 && (int)next >= cfg->tok_vocab) break;
+      continue;
+    }
+    int acc = 0;
+    for (int j = 0; j < nd; ++j) {
+      uint32_t last = tok[len - 1];
+      oracle_token_embedding(m, last, e);
+      int have = oracle_forward(m, e, kv, logits);
+      uint32_t next = oracle_sample(have ? logits : NULL, m->vocab,
+                                    cfg->temperature, cfg->top_p, cfg->min_p,
+                                    (uint64_t)(len - prompt_len), cfg->seed);
+      if (next == draft[j]) {
+        tok[len++] = draft[j];
+        acc++;
+        if (cfg->tok_vocab > 0 && (int)draft[j] >= cfg->tok_vocab) break;
+      } else {
+        tok[len++] = next;
+        break;
+      }
+    }
+    if (cfg->bonus && acc == nd) {
+      uint32_t last = tok[len - 1];
+      oracle_token_embedding(m, last, e);
+      int have = oracle_forward(m, e, kv, logits);
+      uint64_t step = (uint64_t)(len - prompt_len);
+      uint32_t bonus = oracle_sample(have ? logits : NULL, m->vocab,
+                                     cfg->temperature, cfg->top_p, cfg->min_p,
+                                     step, cfg->seed);
+      tok[len++] = bonus;
+    }
+    if (accepted && rounds < rounds_cap) accepted[rounds] = acc;
+    rounds++;
+    ngram_update(&ix, tok, len);
+    if (len - prompt_len >= cfg->max_tokens) break;
+    if (acc < nd && cfg->tok_vocab > 0 && (int)tok[len - 1] >= cfg->tok_vocab)
+      break;
+  }
+  int gen = len - prompt_len;
+  int ncopy = gen < cap ? gen : cap;
+  memcpy(out, tok + prompt_len, sizeof(uint32_t) * (size_t)ncopy);
+  if (n_rounds) *n_rounds = rounds;
+  oracle_kv_free(kv);
+  free(logits); free(e); free(draft); free(tok);
+  free(ix.keys); free(ix.next);
+  return ncopy;
+}
