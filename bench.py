@@ -172,11 +172,11 @@ def cpu_tokens_per_s(t_layer, t_head, rounds, tokens, accepted):
 
 
 # ---------------------------------------------------------------------- GPU
-def build_models(device_index: int):
+def build_models(device_index: int, layers: int | None = None):
     import torch
     import modelc_b200 as mb
     dev = torch.device("cuda", device_index)
-    cfg = mb.LLAMA3_8B
+    cfg = mb.LLAMA3_8B if not layers else mb.LLAMA3_8B.with_layers(layers)
     dcfg = cfg.with_layers(2)
     tt = mb.synth_weights_torch(cfg, seed=0, device=dev)
     target = mb.Weights(tt, cfg, device=device_index)
@@ -323,6 +323,31 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
 
 
+def run_profile(args):
+    """Short run for ncu launch lists: prime the 1024-token prompt, then
+    3 verify forwards and 2 speculative rounds.  Launch counts before the
+    verify forwards are printed so a capture can skip exactly to them."""
+    import torch
+    import modelc_b200 as mb
+    torch.cuda.set_device(0)
+    cfg, target, draft, prompt = build_models(0, args.layers)
+    sess = mb.Session(target, draft, gamma=GAMMA,
+                      max_context=PROMPT_LEN + NEW_TOKENS + 2 * GAMMA + 8)
+    sess.prime(prompt)
+    torch.cuda.synchronize()
+    chunks_t = -(-PROMPT_LEN // 16)
+    chunks_d = -(-(PROMPT_LEN - 1) // 16)
+    per_t = (sess.round_launches - 1 - GAMMA * 21)
+    print(json.dumps({"prime_launches": chunks_t * (1 + per_t) + chunks_d * (1 + 21),
+                      "verify_launches": per_t, "round_launches": sess.round_launches}),
+          flush=True)
+    sess.verify_launch(3)
+    torch.cuda.synchronize()
+    sess.decode(2)
+    torch.cuda.synchronize()
+    sess.close()
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
@@ -359,10 +384,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--profile", action="store_true", help="short run for ncu launch lists")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="--profile only: target layers (fewer = smaller device footprint)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.profile:
+        run_profile(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

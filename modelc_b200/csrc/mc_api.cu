@@ -560,6 +560,7 @@ struct mc_session {
   float* part_o = nullptr;
   float* part_ml = nullptr;
   int* acnt = nullptr;
+  int* err = nullptr;  // device flag raised by an expired bounded wait
   KVSet tkv, dkv;
   // device-resident speculative state
   SpecState* st = nullptr;
@@ -670,6 +671,8 @@ static mc_status session_alloc(mc_session* s) {
   const int n_pages = (s->cap + kPage - 1) / kPage;
   CKS(s->al.alloc(&s->part_o, po * n_pages));
   CKS(s->al.alloc(&s->part_ml, pml * n_pages));
+  CKS(s->al.alloc(&s->err, 1));
+  CK(cudaMemset(s->err, 0, 4));
   CKS(s->al.alloc(&s->acnt, (size_t)hkv));
   CK(cudaMemset(s->acnt, 0, (size_t)hkv * 4));
   CKS(alloc_kv(s, s->tw, &s->tkv));
@@ -745,6 +748,14 @@ extern "C" mc_status mc_session_destroy(mc_session* s) {
 }
 
 // ------------------------------------------------------------------ forward
+// A raised device error flag means a bounded wait expired inside a kernel.
+static mc_status check_err(int* err) {
+  int v = 0;
+  CK(cudaMemcpy(&v, err, 4, cudaMemcpyDeviceToHost));
+  if (v) return set_err(MC_E_TIMEOUT, "a bounded device wait expired (pipeline stalled)");
+  return MC_OK;
+}
+
 static mc_status enq_quant(mc_session* s, const float* h, int ld, int d, int M, const float* w,
                            float eps, int do_norm) {
   QuantArgs q{};
@@ -764,7 +775,15 @@ static mc_status enq_quant(mc_session* s, const float* h, int ld, int d, int M, 
   return MC_OK;
 }
 
-static mc_status enq_gemv(mc_session* s, const PMat& W, int epi, int M, GemvArgs a) {
+constexpr long long kNextPrefetch = 24ll << 20;  // L2 bytes warmed for the next GEMV
+
+static mc_status enq_gemv(mc_session* s, const PMat& W, int epi, int M, GemvArgs a,
+                          const PMat* next = nullptr) {
+  if (next && next->w) {
+    a.next_w = next->w;
+    a.next_bytes = (long long)next->n_stripes * next->KB * kFragBytes;
+    a.next_pf_bytes = std::min(a.next_bytes, kNextPrefetch);
+  }
   a.w = W.w;
   a.scale = W.scale;
   a.x = s->xq;
@@ -774,8 +793,9 @@ static mc_status enq_gemv(mc_session* s, const PMat& W, int epi, int M, GemvArgs
   a.M = M;
   a.ws = s->ws;
   a.cnt = s->cnt;
+  a.err = s->err;
   const int nt = nt_for_tokens(M);
-  const int grid = s->nsm * bps_of(s, epi, nt);
+  const int grid = std::min(W.n_stripes, s->nsm * bps_of(s, epi, nt));
   CK(launch_gemv(a, epi, nt, grid, s->stream, true));
   return MC_OK;
 }
@@ -796,6 +816,15 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
   ea.n_zero = keys ? M : 0;
   CK(launch_embed(ea, s->stream, true));
   const int d = W->d, F = W->F;
+  // the GEMVs of this forward in launch order (each warms L2 for the next)
+  std::vector<const PMat*> seq;
+  for (const LayerW& Lw : W->layers) {
+    if (Lw.attn) { seq.push_back(&Lw.qkv); seq.push_back(&Lw.o); }
+    if (Lw.mlp) { seq.push_back(&Lw.gu); seq.push_back(&Lw.down); }
+  }
+  seq.push_back(&W->head);
+  size_t gi = 0;
+  auto nxt = [&]() -> const PMat* { ++gi; return gi < seq.size() ? seq[gi] : nullptr; };
   for (int l = 0; l < W->L; ++l) {
     const LayerW& Lw = W->layers[l];
     if (Lw.attn) {
@@ -816,7 +845,7 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       a.page = kPage;
       a.sq = Lw.sq;
       a.sk = Lw.sk;
-      CKS(enq_gemv(s, Lw.qkv, EPI_QKV, M, a));
+      CKS(enq_gemv(s, Lw.qkv, EPI_QKV, M, a, nxt()));
       AttnArgs t{};
       t.q = s->qb;
       t.kc = a.kc;
@@ -841,7 +870,7 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       o.out = s->h;
       o.ldo = d;
       o.n_out = d;
-      CKS(enq_gemv(s, Lw.o, EPI_RESID, M, o));
+      CKS(enq_gemv(s, Lw.o, EPI_RESID, M, o, nxt()));
     }
     if (Lw.mlp) {
       CKS(enq_quant(s, s->h, d, d, M, Lw.mlp_norm, W->eps, Lw.mlp_norm ? 1 : 0));
@@ -849,13 +878,13 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       g.out = s->act;
       g.ldo = F;
       g.n_out = F;
-      CKS(enq_gemv(s, Lw.gu, EPI_SWIGLU, M, g));
+      CKS(enq_gemv(s, Lw.gu, EPI_SWIGLU, M, g, nxt()));
       CKS(enq_quant(s, s->act, F, F, M, nullptr, 0.0f, 0));
       GemvArgs dn{};
       dn.out = s->h;
       dn.ldo = d;
       dn.n_out = d;
-      CKS(enq_gemv(s, Lw.down, EPI_RESID, M, dn));
+      CKS(enq_gemv(s, Lw.down, EPI_RESID, M, dn, nxt()));
     }
   }
   CKS(enq_quant(s, s->h, d, d, M, W->final_norm, W->eps, W->final_norm ? 1 : 0));
@@ -890,6 +919,7 @@ static mc_status forward_api(mc_session* s, int which, const uint32_t* ids, int 
       CK(cudaMemcpyAsync(logits + (size_t)c0 * W->V, s->logits, (size_t)M * W->V * 4,
                          cudaMemcpyDeviceToHost, s->stream));
     CK(cudaStreamSynchronize(s->stream));
+    CKS(check_err(s->err));
     len += M;
   }
   if (which) s->draft_tokens.insert(s->draft_tokens.end(), ids, ids + n);
@@ -1087,6 +1117,7 @@ extern "C" mc_status mc_spec_decode(mc_session* s, int32_t max_tokens, int32_t* 
     for (int r = 0; r < R; ++r) CK(cudaGraphLaunch(s->round_exec, s->stream));
     CK(cudaMemcpyAsync(&h, s->st, sizeof(h), cudaMemcpyDeviceToHost, s->stream));
     CK(cudaStreamSynchronize(s->stream));
+    CKS(check_err(s->err));
   }
   s->lt = h.lt;
   s->ld = h.ld;
@@ -1168,6 +1199,7 @@ struct mc_linear {
   int* xexp = nullptr;
   int* ws = nullptr;
   int* cnt = nullptr;
+  int* err = nullptr;
   int nsm = 0;
   int bps[7] = {};
 };
@@ -1185,17 +1217,21 @@ extern "C" mc_status mc_linear_create(const mc_tensor_desc* w, int32_t device, m
                      identity_map(src.cols, round_up(src.cols, 32)), src.rows, src.cols, L->al,
                      &L->m);
   const int kp = round_up(src.cols, 32);
-  if (st == MC_OK && prepare_kernels((size_t)kp * sizeof(float), 0) != cudaSuccess)
+  if (st == MC_OK && prepare_kernels(0, 0) != cudaSuccess)
     st = set_err(MC_E_CUDA, "kernel preparation failed");
   if (st == MC_OK) st = L->al.alloc(&L->xq, (size_t)kp * 48);
   if (st == MC_OK) st = L->al.alloc(&L->xexp, (size_t)kMaxTokens);
   if (st == MC_OK) st = L->al.alloc(&L->ws, (size_t)L->m.n_stripes * 32 * 24);
   if (st == MC_OK) st = L->al.alloc(&L->cnt, (size_t)L->m.n_stripes);
+  if (st == MC_OK) st = L->al.alloc(&L->err, 1);
+  if (st == MC_OK && cudaMemset(L->err, 0, 4) != cudaSuccess) st = set_err(MC_E_CUDA, "memset");
   if (st == MC_OK && (cudaMemset(L->xq, 0, (size_t)kp * 48) != cudaSuccess ||
                       cudaMemset(L->ws, 0, (size_t)L->m.n_stripes * 32 * 24 * 4) != cudaSuccess ||
                       cudaMemset(L->cnt, 0, (size_t)L->m.n_stripes * 4) != cudaSuccess))
     st = set_err(MC_E_CUDA, "memset failed");
   cudaDeviceGetAttribute(&L->nsm, cudaDevAttrMultiProcessorCount, device);
+  if (st == MC_OK)
+    for (int nt : {1, 2, 3, 6}) L->bps[nt] = std::max(1, gemv_blocks_per_sm(EPI_STORE, nt));
   if (st != MC_OK) {
     L->al.free_all();
     delete L;
@@ -1243,12 +1279,13 @@ extern "C" mc_status mc_linear_run(mc_linear* l, const float* x_dev, int32_t m, 
     a.M = M;
     a.ws = l->ws;
     a.cnt = l->cnt;
+    a.err = l->err;
     a.out = y_dev + (size_t)r0 * l->m.N;
     a.ldo = l->m.N;
     a.n_out = l->m.N;
     const int nt = nt_for_tokens(M);
     if (!l->bps[nt]) l->bps[nt] = std::max(1, gemv_blocks_per_sm(EPI_STORE, nt));
-    CK(launch_gemv(a, EPI_STORE, nt, l->nsm * l->bps[nt], s, true));
+    CK(launch_gemv(a, EPI_STORE, nt, std::min(l->m.n_stripes, l->nsm * l->bps[nt]), s, true));
   }
   return MC_OK;
 }

@@ -59,8 +59,12 @@ struct GemvArgs {
   int KB;                // k-blocks per stripe
   int n_stripes;
   int M;                 // tokens
-  int* ws;               // split-K partial sums [n_stripes][32][4*NT] (zeroed)
+  int* ws;               // split-K partial sums [n_stripes][16][8*NT] (zeroed)
   int* cnt;              // [n_stripes] k-block arrival counters (zeroed)
+  int* err;              // set to 1 when a bounded device wait expires
+  const void* next_w;    // weights of the next GEMV in the stream (L2 prefetch)
+  long long next_bytes;  // its packed size
+  long long next_pf_bytes;  // how much of it to prefetch
   // epilogue
   float* out;            // STORE/RESID/SWIGLU/LMHEAD destination
   int ldo;               // row stride (elements) of out per token
@@ -176,6 +180,7 @@ cudaError_t launch_accept_greedy(SpecState* st, uint32_t* ctx, int* acc_log,
                                  int vm, cudaStream_t s, bool pdl);
 cudaError_t launch_set_int(int* p, int v, cudaStream_t s);
 size_t attention_smem_bytes(int G, int M, int hdp, int page);
+size_t gemv_ws_ints_per_stripe(int nt);
 cudaError_t prepare_kernels(size_t quant_smem, size_t attn_smem);
 cudaError_t launch_pack_int8(const int8_t* src, long long src_ld,
                              const float* src_scale, const int* row_map,

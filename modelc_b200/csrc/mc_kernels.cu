@@ -18,23 +18,33 @@
 namespace mc {
 
 // ------------------------------------------------------------ PTX helpers
-__device__ __forceinline__ int4 ldg_stream(const int4* p) {
+// Weight stream: read once per forward, so it bypasses L1 and is marked
+// evict-first in L2 (it must not evict the next GEMV's prefetched lines).
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ int4 ldg_stream(const int4* p, uint64_t pol) {
   int4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.s32 {%0,%1,%2,%3}, [%4], %5;"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
+               : "l"(p), "l"(pol));
   return v;
 }
+// Activation digits are rewritten by the previous kernel while this grid may
+// already be resident (programmatic dependent launch), so they are read
+// through L2 (.cg), never through the non-coherent path.
 __device__ __forceinline__ uint4 ldg_u4(const void* p) {
   uint4 v;
-  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
   return v;
 }
 __device__ __forceinline__ uint2 ldg_u2(const void* p) {
   uint2 v;
-  asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];"
+  asm volatile("ld.global.cg.v2.u32 {%0,%1}, [%2];"
                : "=r"(v.x), "=r"(v.y)
                : "l"(p));
   return v;
@@ -113,6 +123,15 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 }
 
 // ------------------------------------------------------------ GEMV
+// Work split: each CTA owns a contiguous range of the linear (stripe,
+// k-block) index (stream-K, balanced to one k-block); its 8 warps own
+// contiguous eighths of it.  A warp streams its weights with 16-byte loads
+// (U k-blocks in flight), the first batch issued before griddepcontrol.wait.
+// A stripe finished inside one warp goes straight to the epilogue.  Stripes
+// shared by warps of one CTA are summed with shared-memory atomics and the
+// last contributing warp finishes them; only a CTA's first and last stripe
+// can be shared with other CTAs, and those go through the global split-K
+// workspace (int32 sums, so the reduction order never changes the result).
 template <int NT>
 struct GemvCfg {
   static constexpr int U = (NT <= 2) ? 8 : 4;  // k-blocks per load batch
@@ -121,28 +140,22 @@ struct GemvCfg {
 
 constexpr int kGemvWarps = 8;
 
+// Epilogue of a finished stripe from a row-major [16][ld] int tile.
 template <int NT, int EPI>
-__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe,
-                                              int (*sm)[8 * NT + 1], const int (&acc)[NT][4],
-                                              int lane, unsigned long long* kmax) {
-  const int g = lane >> 2, tq = lane & 3;
-#pragma unroll
-  for (int t = 0; t < NT; ++t) {
-    sm[g][t * 8 + 2 * tq] = acc[t][0];
-    sm[g][t * 8 + 2 * tq + 1] = acc[t][1];
-    sm[g + 8][t * 8 + 2 * tq] = acc[t][2];
-    sm[g + 8][t * 8 + 2 * tq + 1] = acc[t][3];
-  }
-  __syncwarp();
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, const int* tile,
+                                              int ld, int lane, unsigned long long* kmax,
+                                              const float* scale, const int* xexp) {
   const int M = a.M;
-  for (int it = 0; it * 32 < 8 * M; ++it) {
+#pragma unroll
+  for (int it = 0; it < (8 * kMaxTokens) / 32; ++it) {
     const int idx = it * 32 + lane;
+    if (it * 32 >= 8 * M) break;
     if (idx < 8 * M) {
       const int r = idx & 7, m = idx >> 3;
-      const int e = a.xexp[m];
+      const int e = xexp[m];
       const int prow = stripe * 16 + r;
-      const float y0 = combine_digits(sm[r], m, a.scale[prow], e);
-      const float y1 = combine_digits(sm[r + 8], m, a.scale[prow + 8], e);
+      const float y0 = combine_digits(tile + r * ld, m, scale[prow], e);
+      const float y1 = combine_digits(tile + (r + 8) * ld, m, scale[prow + 8], e);
       if constexpr (EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_LMHEAD) {
         float* o = a.out ? a.out + (size_t)m * a.ldo : nullptr;
         if (prow < a.n_out) {
@@ -203,64 +216,112 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe,
       }
     }
   }
-  __syncwarp();
 }
+
+// Work split (whole stripes, no cross-CTA reduction): CTA c owns stripes
+// [c*S/G, (c+1)*S/G).  With s stripes per CTA each stripe is cut into
+// F = ceil(8/s) k-ranges so that all 8 warps have units; unit u (stripe
+// u/F, k-range u%F) belongs to warp u%8.  A stripe cut into F > 1 units is
+// summed with shared-memory atomics and finished by its last warp.
+// Per-SM streaming capacity exceeds each SM's share of HBM bandwidth, so the
+// mild imbalance of whole-stripe ownership costs nothing.
+constexpr int kTileSlots = 8;      // stripes in flight per CTA when F > 1
+constexpr int kMaxCtaStripes = 64; // scales staged per CTA (before the wait)
 
 template <int NT, int EPI>
 __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   constexpr int U = GemvCfg<NT>::U;
   constexpr int COLS = GemvCfg<NT>::COLS;
-  __shared__ int sm_epi[kGemvWarps][16][COLS + 1];
+  extern __shared__ __align__(16) int gemv_smem[];
+  // per-warp fragment staging [warp][16][COLS+1], then shared stripe sums
+  int (*sm_epi)[16][COLS + 1] = reinterpret_cast<int (*)[16][COLS + 1]>(gemv_smem);
+  int (*sm_tile)[16 * COLS] =
+      reinterpret_cast<int (*)[16 * COLS]>(gemv_smem + kGemvWarps * 16 * (COLS + 1));
+  __shared__ int sm_cnt[kTileSlots];
+  __shared__ float sm_scale[kMaxCtaStripes * 16];
+  __shared__ int sm_exp[kMaxTokens];
   __shared__ unsigned long long sm_keys[kMaxTokens];
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const long long gw = (long long)blockIdx.x * kGemvWarps + warp;
-  const long long nw = (long long)gridDim.x * kGemvWarps;
-  const long long T = (long long)a.n_stripes * a.KB;
-  const long long r0 = T * gw / nw, r1 = T * (gw + 1) / nw;
+  const int s0 = (int)((long long)a.n_stripes * blockIdx.x / gridDim.x);
+  const int s1 = (int)((long long)a.n_stripes * (blockIdx.x + 1) / gridDim.x);
+  const int ns = s1 - s0;
+  const int F = ns >= kGemvWarps ? 1 : (kGemvWarps + max(ns, 1) - 1) / max(ns, 1);
+  const int n_units = ns * F;
 
-  if (EPI == EPI_LMHEAD && threadIdx.x < kMaxTokens) sm_keys[threadIdx.x] = 0ull;
+  if (threadIdx.x < kTileSlots) sm_cnt[threadIdx.x] = 0;
+  if (threadIdx.x < kMaxTokens) sm_keys[threadIdx.x] = 0ull;
+  if (F > 1)
+    for (int i = threadIdx.x; i < kTileSlots * 16 * COLS; i += blockDim.x) (&sm_tile[0][0])[i] = 0;
+  const bool scale_smem = ns <= kMaxCtaStripes;
+  if (scale_smem)
+    for (int i = threadIdx.x; i < ns * 16; i += blockDim.x) sm_scale[i] = a.scale[s0 * 16 + i];
 
-  // Weights never depend on the producer grid: start streaming them (and
-  // warm L2 with the next part of this warp's range) before the wait.
+  // Weights never depend on the producer grid: start streaming them (first
+  // batch of this warp's first unit) before the wait.
+  const uint64_t pol = policy_evict_first();
   int4 wv[U];
-  if (r0 < r1) {
-    const int s0 = (int)(r0 / a.KB);
-    const long long e0 = min(r1, (long long)(s0 + 1) * a.KB);
-    const int nb0 = (int)min((long long)U, e0 - r0);
+  auto unit_range = [&](int u, int& stripe, int& kb0, int& kb1) {
+    stripe = s0 + u / F;
+    const int part = u - (u / F) * F;
+    kb0 = (int)((long long)a.KB * part / F);
+    kb1 = (int)((long long)a.KB * (part + 1) / F);
+  };
+  if (warp < n_units) {
+    int st, k0, k1;
+    unit_range(warp, st, k0, k1);
+    const int4* wp = a.w + ((size_t)st * a.KB + k0) * 32 + lane;
 #pragma unroll
     for (int j = 0; j < U; ++j)
-      if (j < nb0) wv[j] = ldg_stream(a.w + (r0 + j) * 32 + lane);
-    if (lane == 0 && r1 - r0 > U) {
-      const long long pf = min(r1 - r0 - U, 64ll);
-      prefetch_l2_bulk(a.w + (r0 + U) * 32, (uint32_t)(pf * kFragBytes));
+      if (j < k1 - k0) wv[j] = ldg_stream(wp + (size_t)j * 32, pol);
+  }
+  // Warm L2 with the next GEMV's weights (split like this grid) so HBM keeps
+  // streaming through this grid's tail and the small kernels in between.
+  if (a.next_w && lane == 1 && a.next_bytes > 0) {
+    const long long nw = (long long)gridDim.x * kGemvWarps;
+    const long long gw = (long long)blockIdx.x * kGemvWarps + warp;
+    const long long chunk = (a.next_bytes / nw) & ~15ll;
+    if (chunk >= 16) {
+      const char* p = reinterpret_cast<const char*>(a.next_w) + chunk * gw;
+      long long left = min(chunk, a.next_pf_bytes / nw);
+      while (left >= 16) {
+        const uint32_t b = (uint32_t)min(left, 32768ll) & ~15u;
+        prefetch_l2_bulk(p, b);
+        p += b;
+        left -= b;
+      }
     }
   }
   grid_wait();
-  if (EPI == EPI_LMHEAD) __syncthreads();
+  if (threadIdx.x < a.M) sm_exp[threadIdx.x] = __ldcg(a.xexp + threadIdx.x);
+  __syncthreads();
 
-  unsigned long long kmax[(8 * kMaxTokens + 31) / 32];
+  unsigned long long kmax[(8 * kMaxTokens) / 32];
 #pragma unroll
-  for (int i = 0; i < (8 * kMaxTokens + 31) / 32; ++i) kmax[i] = 0ull;
+  for (int i = 0; i < (8 * kMaxTokens) / 32; ++i) kmax[i] = 0ull;
+  const float* scl = scale_smem ? sm_scale - s0 * 16 : a.scale;
 
   bool pre = true;
-  long long seg = r0;
-  while (seg < r1) {
-    const int stripe = (int)(seg / a.KB);
-    const int kb0 = (int)(seg - (long long)stripe * a.KB);
-    const int n = (int)(min(r1, (long long)(stripe + 1) * a.KB) - seg);
+  for (int u = warp; u < n_units; u += kGemvWarps) {
+    int stripe, k0, k1;
+    unit_range(u, stripe, k0, k1);
+    const int n = k1 - k0;
+    if (n <= 0) {  // empty k-range (K shorter than the split): contributes nothing
+      pre = false;
+      continue;
+    }
     int acc[NT][4];
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0;
-    const int4* wp = a.w + seg * 32 + lane;
-    const uint8_t* xp = a.x + ((size_t)kb0 * 32 + lane) * COLS;
+    const int4* wp = a.w + ((size_t)stripe * a.KB + k0) * 32 + lane;
+    const uint8_t* xp = a.x + ((size_t)k0 * 32 + lane) * COLS;
     for (int i = 0; i < n; i += U) {
       const int nb = min(U, n - i);
       if (!pre) {
 #pragma unroll
         for (int j = 0; j < U; ++j)
-          if (j < nb) wv[j] = ldg_stream(wp + (size_t)(i + j) * 32);
+          if (j < nb) wv[j] = ldg_stream(wp + (size_t)(i + j) * 32, pol);
       }
       pre = false;
       uint32_t xv[U][2 * NT];
@@ -274,39 +335,48 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
           for (int t = 0; t < NT; ++t) imma(acc[t], wv[j], xv[j][2 * t], xv[j][2 * t + 1]);
         }
     }
-    // flush this stripe segment
-    if (kb0 == 0 && n == a.KB) {
-      gemv_epilogue<NT, EPI>(a, stripe, sm_epi[warp], acc, lane, kmax);
+    const int g = lane >> 2, tq = lane & 3;
+    if (F == 1) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        sm_epi[warp][g][t * 8 + 2 * tq] = acc[t][0];
+        sm_epi[warp][g][t * 8 + 2 * tq + 1] = acc[t][1];
+        sm_epi[warp][g + 8][t * 8 + 2 * tq] = acc[t][2];
+        sm_epi[warp][g + 8][t * 8 + 2 * tq + 1] = acc[t][3];
+      }
+      __syncwarp();
+      gemv_epilogue<NT, EPI>(a, stripe, &sm_epi[warp][0][0], COLS + 1, lane, kmax, scl, sm_exp);
+      __syncwarp();
     } else {
-      int* wsp = a.ws + ((size_t)stripe * 32 + lane) * (4 * NT);
+      // F <= 8 and ns < 8, so a stripe's slot is its index in the CTA
+      const int slot = stripe - s0;
+      int* tile = sm_tile[slot];
 #pragma unroll
-      for (int t = 0; t < NT; ++t)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) red_add(wsp + t * 4 + q, acc[t][q]);
-      __threadfence();
+      for (int t = 0; t < NT; ++t) {
+        atomicAdd(tile + g * COLS + t * 8 + 2 * tq, acc[t][0]);
+        atomicAdd(tile + g * COLS + t * 8 + 2 * tq + 1, acc[t][1]);
+        atomicAdd(tile + (g + 8) * COLS + t * 8 + 2 * tq, acc[t][2]);
+        atomicAdd(tile + (g + 8) * COLS + t * 8 + 2 * tq + 1, acc[t][3]);
+      }
+      __syncwarp();
       int last = 0;
-      if (lane == 0) last = (atomicAdd(a.cnt + stripe, n) + n == a.KB);
+      if (lane == 0) {
+        __threadfence_block();
+        last = (atomicAdd(&sm_cnt[slot], n) + n == a.KB);
+      }
       last = __shfl_sync(0xffffffffu, last, 0);
       if (last) {
-        __threadfence();
-#pragma unroll
-        for (int t = 0; t < NT; ++t)
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            acc[t][q] = ld_cg(wsp + t * 4 + q);
-            wsp[t * 4 + q] = 0;
-          }
-        if (lane == 0) atomicExch(a.cnt + stripe, 0);
-        gemv_epilogue<NT, EPI>(a, stripe, sm_epi[warp], acc, lane, kmax);
+        __threadfence_block();
+        gemv_epilogue<NT, EPI>(a, stripe, tile, COLS, lane, kmax, scl, sm_exp);
       }
+      __syncwarp();
     }
-    seg += n;
   }
   grid_launch_dependents();
 
   if constexpr (EPI == EPI_LMHEAD) {
 #pragma unroll
-    for (int it = 0; it < (8 * kMaxTokens + 31) / 32; ++it) {
+    for (int it = 0; it < (8 * kMaxTokens) / 32; ++it) {
       unsigned long long k = kmax[it];
 #pragma unroll
       for (int o = 1; o < 8; o <<= 1) {
@@ -322,12 +392,17 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   }
 }
 
+template <int NT>
+static constexpr size_t gemv_dyn_smem() {
+  return ((size_t)kGemvWarps * 16 * (8 * NT + 1) + (size_t)kTileSlots * 16 * 8 * NT) * sizeof(int);
+}
+
 template <int NT, int EPI>
 static cudaError_t launch_gemv_t(const GemvArgs& a, int grid, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kGemvWarps * 32);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = gemv_dyn_smem<NT>();
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -359,18 +434,31 @@ cudaError_t launch_gemv(const GemvArgs& a, int epi, int nt, int grid, cudaStream
   return cudaErrorInvalidValue;
 }
 
-template <int NT>
-static int bps_nt(int epi) {
+template <int NT, int EPI>
+static int bps_t() {
+  const size_t sm = gemv_dyn_smem<NT>();
+  if (sm > 48 * 1024)
+    cudaFuncSetAttribute(k_gemv<NT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   int n = 0;
-  switch (epi) {
-    case EPI_STORE: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<NT, EPI_STORE>, kGemvWarps * 32, 0); break;
-    case EPI_RESID: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<NT, EPI_RESID>, kGemvWarps * 32, 0); break;
-    case EPI_SWIGLU: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<NT, EPI_SWIGLU>, kGemvWarps * 32, 0); break;
-    case EPI_QKV: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<NT, EPI_QKV>, kGemvWarps * 32, 0); break;
-    case EPI_LMHEAD: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<NT, EPI_LMHEAD>, kGemvWarps * 32, 0); break;
-  }
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<NT, EPI>, kGemvWarps * 32, sm);
   return n;
 }
+
+// Occupancy of a GEMV variant; also raises its dynamic shared-memory limit,
+// so it is called once per variant outside any stream capture.
+template <int NT>
+static int bps_nt(int epi) {
+  switch (epi) {
+    case EPI_STORE: return bps_t<NT, EPI_STORE>();
+    case EPI_RESID: return bps_t<NT, EPI_RESID>();
+    case EPI_SWIGLU: return bps_t<NT, EPI_SWIGLU>();
+    case EPI_QKV: return bps_t<NT, EPI_QKV>();
+    case EPI_LMHEAD: return bps_t<NT, EPI_LMHEAD>();
+  }
+  return 0;
+}
+
+size_t gemv_ws_ints_per_stripe(int nt) { return (size_t)16 * 8 * nt; }
 
 int gemv_blocks_per_sm(int epi, int nt) {
   switch (nt) {
@@ -383,154 +471,212 @@ int gemv_blocks_per_sm(int epi, int nt) {
 }
 
 // ------------------------------------------------------------ quantize
-// One block per token.  Optional RMSNorm (transformer.rs:888-896:
-// ms = sum(v*v)/n, rms = sqrt(ms + eps), out = v / rms * w), then the
-// fixed-point digit encoding of the GEMV's B operand.
-constexpr int kQuantThreads = 1024;
-static int g_quant_smem = 48 * 1024;  // current dynamic smem limits (per process;
-static int g_attn_smem = 48 * 1024;   // single-device use assumed per limit)
-
-__device__ __forceinline__ float block_sum(float v, float* red) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
-  if (l == 0) red[w] = v;
-  __syncthreads();
-  float t = 0.0f;
-  if (threadIdx.x < 32) {
-    t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-    if (threadIdx.x == 0) red[0] = t;
-  }
-  __syncthreads();
-  return red[0];
-}
-
-__device__ __forceinline__ uint32_t block_max_u(uint32_t v, uint32_t* red) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
-  if (l == 0) red[w] = v;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    uint32_t t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0u;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) t = max(t, __shfl_xor_sync(0xffffffffu, t, o));
-    if (threadIdx.x == 0) red[0] = t;
-  }
-  __syncthreads();
-  return red[0];
-}
+// Encodes the next GEMV's B operand.  Every CTA first recomputes, for all M
+// tokens, sum(h*h) and max|h*w| over the whole vector (vectorised L2 reads;
+// cheap next to a grid-wide reduction), then writes its own slice of the
+// packed digit words, one coalesced 4-byte word per thread.  RMSNorm follows
+// transformer.rs:888-896 (ms = sum(v*v)/n, rms = sqrt(ms + eps),
+// x = v / rms * w).  The exponent makes |x| * 2^e < 2^20 with a one-ulp
+// margin (digits tolerate |X| < 2^21).
+constexpr int kQuantThreads = 512;
+constexpr int kQuantMaxCtas = 64;
+static int g_attn_smem = 48 * 1024;  // attention dynamic smem limit set so far
 
 __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
-  extern __shared__ float sx[];
-  __shared__ float redf[32];
-  __shared__ uint32_t redu[32];
+  __shared__ float red_ss[kQuantThreads / 32][kMaxTokens];
+  __shared__ float red_hw[kQuantThreads / 32][kMaxTokens];
+  __shared__ float s_rms[kMaxTokens];
+  __shared__ int s_e[kMaxTokens];
+  __shared__ uint32_t s_bad;  // bit m: token m holds a non-finite value
+  extern __shared__ float s_x[];
   grid_launch_dependents();
+  if (threadIdx.x == 0) s_bad = 0u;
   grid_wait();
-  const int m = blockIdx.x;
-  const float* h = a.h + (size_t)m * a.ld;
-  const int d = a.d;
-  float rms = 1.0f;
-  if (a.do_norm) {
-    float ss = 0.0f;
+  const int M = a.M, d = a.d;
+  float ss[kMaxTokens], hw[kMaxTokens];
+#pragma unroll
+  for (int m = 0; m < kMaxTokens; ++m) { ss[m] = 0.0f; hw[m] = 0.0f; }
+  uint32_t bad = 0u;
+  const bool vec = ((a.ld & 3) == 0) && ((d & 3) == 0) &&
+                   ((reinterpret_cast<uintptr_t>(a.h) & 15) == 0);
+  // this CTA's k-blocks; their x values are kept in shared memory (s_x)
+  const int kbs = (a.KB + gridDim.x - 1) / gridDim.x;
+  const int kb0 = blockIdx.x * kbs, kb1 = min(a.KB, kb0 + kbs);
+  const int span = max(kb1 - kb0, 0) * 32;
+  const int lo = kb0 * 32, hi = kb0 * 32 + span;
+  if (vec) {
+#pragma unroll 4
+    for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
+      float4 wv = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+      if (a.do_norm && a.w) {
+        wv.x = i < a.wlen ? a.w[i] : 1.0f;
+        wv.y = i + 1 < a.wlen ? a.w[i + 1] : 1.0f;
+        wv.z = i + 2 < a.wlen ? a.w[i + 2] : 1.0f;
+        wv.w = i + 3 < a.wlen ? a.w[i + 3] : 1.0f;
+      }
+#pragma unroll
+      for (int m = 0; m < kMaxTokens; ++m)
+        if (m < M) {
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)m * a.ld + i));
+          if (i >= lo && i < hi) *reinterpret_cast<float4*>(s_x + m * span + (i - lo)) = v;
+          ss[m] = __fadd_rn(ss[m], __fmul_rn(v.x, v.x));
+          ss[m] = __fadd_rn(ss[m], __fmul_rn(v.y, v.y));
+          ss[m] = __fadd_rn(ss[m], __fmul_rn(v.z, v.z));
+          ss[m] = __fadd_rn(ss[m], __fmul_rn(v.w, v.w));
+          hw[m] = fmaxf(hw[m], fmaxf(fmaxf(fabsf(__fmul_rn(v.x, wv.x)), fabsf(__fmul_rn(v.y, wv.y))),
+                                     fmaxf(fabsf(__fmul_rn(v.z, wv.z)), fabsf(__fmul_rn(v.w, wv.w)))));
+          if (!(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w))) bad |= 1u << m;
+        }
+    }
+  } else {
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
-      float v = h[i];
-      ss = __fadd_rn(ss, __fmul_rn(v, v));
+      const float wi = (a.do_norm && a.w && i < a.wlen) ? a.w[i] : 1.0f;
+#pragma unroll
+      for (int m = 0; m < kMaxTokens; ++m)
+        if (m < M) {
+          const float v = __ldcg(a.h + (size_t)m * a.ld + i);
+          if (i >= lo && i < hi) s_x[m * span + (i - lo)] = v;
+          ss[m] = __fadd_rn(ss[m], __fmul_rn(v, v));
+          hw[m] = fmaxf(hw[m], fabsf(__fmul_rn(v, wi)));
+          if (!isfinite(v)) bad |= 1u << m;
+        }
     }
-    ss = block_sum(ss, redf);
-    float nf = (float)(d > 1 ? d : 1);
-    rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, nf), a.eps));
   }
-  uint32_t amax = 0u, bad = 0u;
-  for (int i = threadIdx.x; i < d; i += blockDim.x) {
-    float v = h[i];
-    if (a.do_norm) {
-      float wi = (a.w && i < a.wlen) ? a.w[i] : 1.0f;
-      v = __fmul_rn(__fdiv_rn(v, rms), wi);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int m = 0; m < kMaxTokens; ++m) {
+    if (m < M) {
+      float x = ss[m], y = hw[m];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        x += __shfl_xor_sync(0xffffffffu, x, o);
+        y = fmaxf(y, __shfl_xor_sync(0xffffffffu, y, o));
+      }
+      if (lane == 0) { red_ss[warp][m] = x; red_hw[warp][m] = y; }
     }
-    sx[i] = v;
-    uint32_t b = __float_as_uint(fabsf(v));
-    if (!isfinite(v)) bad = 1u;
-    amax = max(amax, b);
   }
-  amax = block_max_u(amax, redu);
-  bad = block_max_u(bad, redu);
-  int e = 0;
-  if (bad) {
-    e = kExpNonFinite;
-  } else if (amax != 0u) {
-    int E;
-    frexpf(__uint_as_float(amax), &E);
-    e = 20 - E;  // |x| * 2^e < 2^20
+  bad = __reduce_or_sync(0xffffffffu, bad);
+  if (lane == 0 && bad) atomicOr(&s_bad, bad);
+  __syncthreads();
+  if (threadIdx.x < M) {
+    const int m = threadIdx.x;
+    float x = 0.0f, y = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { x += red_ss[w][m]; y = fmaxf(y, red_hw[w][m]); }
+    float rms = 1.0f;
+    if (a.do_norm) rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(x, (float)(d > 1 ? d : 1)), a.eps));
+    const float amax = a.do_norm ? y / rms : y;
+    int e = 0;
+    if (((s_bad >> m) & 1u) || !isfinite(amax)) {
+      e = kExpNonFinite;
+    } else if (amax > 0.0f) {
+      int E;
+      frexpf(amax * 1.0000002f, &E);
+      e = 20 - E;
+    }
+    // x * 2^e = (h * w) * (2^e / rms): the power-of-two factor is exact; one
+    // reciprocal per token replaces the per-element division (<= 1 ulp).
+    float mul = 0.0f;
+    if (e != kExpNonFinite) {
+      const float inv = a.do_norm ? 1.0f / rms : 1.0f;
+      mul = ldexpf(inv, e);
+    }
+    s_rms[m] = mul;
+    s_e[m] = e;
+    if (blockIdx.x == 0) a.xexp[m] = e;
   }
-  if (threadIdx.x == 0) a.xexp[m] = e;
+  __syncthreads();
+  // Encode: one thread per (token, 4 consecutive k) group computes the 4
+  // fixed-point values once and writes its three digit words; leftover
+  // columns of the last n8 tile are written as zero words.
   const int nt = a.nt;
   const int cols = 8 * nt;
+  const int pad_cols = cols - 3 * M;
+  const int ngroups = (kb1 - kb0) * 8;  // 4-element groups in this CTA's slice
   uint32_t* xq = reinterpret_cast<uint32_t*>(a.xq);
-  const int ngroups = a.KB * 8;
-  for (int gi = threadIdx.x; gi < ngroups; gi += blockDim.x) {
-    const int k0 = gi * 4;
-    const int kb = k0 >> 5, kk = k0 & 31;
+  const int tasks = ngroups * (M + pad_cols);
+  for (int task = threadIdx.x; task < tasks; task += blockDim.x) {
+    const int grp = task % ngroups;
+    const int q = task / ngroups;  // token (q < M) or padding column (q >= M)
+    const int kb = kb0 + (grp >> 3);
+    const int kk = (grp & 7) * 4;
     const int reg = kk >> 4, t = (kk & 15) >> 2;
+    if (q >= M) {
+      const int c = 3 * M + (q - M);
+      const int tile = c >> 3, ln = (c & 7) * 4 + t;
+      xq[(((size_t)kb * 32 + ln) * nt + tile) * 2 + reg] = 0u;
+      continue;
+    }
+    const int m = q;
+    const int e = s_e[m];
     uint32_t w0 = 0, w1 = 0, w2 = 0;
+    if (e != kExpNonFinite) {
+      const float mul = s_rms[m];  // 2^e / rms (or 2^e), see above
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int k = k0 + j;
-      int X = 0;
-      if (k < d && e != kExpNonFinite) X = __float2int_rn(ldexpf(sx[k], e));
-      const int d2 = ((X + 64) & 127) - 64;
-      const int X1 = (X - d2) >> 7;
-      const int d1 = ((X1 + 64) & 127) - 64;
-      const int d0 = (X1 - d1) >> 7;
-      w0 |= (uint32_t)(d0 & 0xff) << (8 * j);
-      w1 |= (uint32_t)(d1 & 0xff) << (8 * j);
-      w2 |= (uint32_t)(d2 & 0xff) << (8 * j);
+      for (int j = 0; j < 4; ++j) {
+        const int k = kb * 32 + kk + j;
+        int X = 0;
+        if (k < d) {
+          float v = s_x[m * span + (k - kb0 * 32)];
+          if (a.do_norm) v = __fmul_rn(v, (a.w && k < a.wlen) ? a.w[k] : 1.0f);
+          X = __float2int_rn(__fmul_rn(v, mul));
+        }
+        const int d2 = ((X + 64) & 127) - 64;
+        const int X1 = (X - d2) >> 7;
+        const int d1 = ((X1 + 64) & 127) - 64;
+        const int d0 = (X1 - d1) >> 7;
+        w0 |= (uint32_t)(d0 & 0xff) << (8 * j);
+        w1 |= (uint32_t)(d1 & 0xff) << (8 * j);
+        w2 |= (uint32_t)(d2 & 0xff) << (8 * j);
+      }
     }
     const uint32_t wd[3] = {w0, w1, w2};
 #pragma unroll
-    for (int s = 0; s < 3; ++s) {
-      const int c = 3 * m + s;
-      const int tile = c >> 3, n = c & 7, ln = n * 4 + t;
-      xq[(((size_t)kb * 32 + ln) * cols + tile * 8 + reg * 4) >> 2] = wd[s];
-    }
-    if (m == a.M - 1) {
-      for (int c = 3 * a.M; c < cols; ++c) {
-        const int tile = c >> 3, n = c & 7, ln = n * 4 + t;
-        xq[(((size_t)kb * 32 + ln) * cols + tile * 8 + reg * 4) >> 2] = 0u;
-      }
+    for (int dg = 0; dg < 3; ++dg) {
+      const int c = 3 * m + dg;
+      const int tile = c >> 3, ln = (c & 7) * 4 + t;
+      xq[(((size_t)kb * 32 + ln) * nt + tile) * 2 + reg] = wd[dg];
     }
   }
 }
 
 cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl) {
+  if (a.M < 1 || a.M > kMaxTokens) return cudaErrorInvalidValue;
+  const int words = a.KB * 32 * 2 * a.nt;
+  int ctas = (words + kQuantThreads - 1) / kQuantThreads;
+  ctas = ctas < 1 ? 1 : (ctas > kQuantMaxCtas ? kQuantMaxCtas : ctas);
+  const int kbs_fit = (40 * 1024) / (a.M * 32 * (int)sizeof(float));  // staged slice <= 40 KB
+  if (kbs_fit < 1) return cudaErrorInvalidConfiguration;
+  const int need = (a.KB + kbs_fit - 1) / kbs_fit;
+  ctas = ctas < need ? need : ctas;
+  ctas = ctas > a.KB ? a.KB : ctas;
+  const int kbs = (a.KB + ctas - 1) / ctas;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.M);
+  cfg.gridDim = dim3(ctas);
   cfg.blockDim = dim3(kQuantThreads);
-  cfg.dynamicSmemBytes = (size_t)a.KB * 32 * sizeof(float);
+  cfg.dynamicSmemBytes = (size_t)a.M * kbs * 32 * sizeof(float);
+  if (cfg.dynamicSmemBytes > 48 * 1024) return cudaErrorInvalidConfiguration;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cfg.dynamicSmemBytes > (size_t)g_quant_smem) return cudaErrorInvalidConfiguration;
   return cudaLaunchKernelEx(&cfg, k_quant, a);
 }
 
 // ------------------------------------------------------------ attention
-// One CTA per (KV head, KV page).  Query rows are the G query heads sharing
-// the KV head times the M new tokens; token m sees positions <= pos0 + m.
-// Scores: dot / sqrt(head_dim) (transformer.rs:959-966); softmax with the
-// max subtracted (transformer.rs:985-1000), combined across pages by the
-// last-arriving CTA of the head.
+// One CTA per (KV head, KV page of 64 positions).  Query rows are the G
+// query heads sharing the KV head times the M new tokens; token m sees
+// positions <= pos0 + m.  Scores are dot / sqrt(head_dim) (transformer.rs:
+// 959-966); the softmax subtracts the row max (transformer.rs:985-1000).
+// Pages are combined by the last CTA of each KV head (flash-decoding split).
 constexpr int kAttnThreads = 256;
+constexpr int kAttnRowBlk = 8;  // query rows per thread in the score pass
 
 __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
   extern __shared__ float smem[];
+  __shared__ float s_m[128], s_l[128];
+  __shared__ int s_last;
   grid_launch_dependents();
   grid_wait();
   const int kvh = blockIdx.x, chunk = blockIdx.y;
@@ -543,51 +689,100 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
   if (chunk >= n_chunks) return;
   const int t0 = chunk * P;
   const int nt = min(P, L - t0);
-  const int ks = hdp + 1;  // padded K row stride (bank-conflict free)
+  const int ks = hdp + 4;  // K row stride: float4-aligned, conflict-free float4 reads
   float* sq = smem;                    // [R][hdp]
-  float* sk = sq + (size_t)R * hdp;    // [P][hdp+1]
+  float* sk = sq + (size_t)R * hdp;    // [P][hdp+4]
   float* sv = sk + (size_t)P * ks;     // [P][hdp]
   float* ss = sv + (size_t)P * hdp;    // [R][P]
-  __shared__ float s_m[128], s_l[128];
 
   const int pg = a.page_table[chunk];
-  const float* kbase = a.kc + ((size_t)pg * a.Hkv + kvh) * P * hdp;
-  const float* vbase = a.vc + ((size_t)pg * a.Hkv + kvh) * P * hdp;
-  for (int i = threadIdx.x; i < R * hdp; i += blockDim.x) {
-    const int row = i / hdp, c = i - row * hdp;
-    const int m = row / G, gi = row - m * G;
-    sq[i] = a.q[((size_t)m * a.H + kvh * G + gi) * hdp + c];
-  }
-  for (int i = threadIdx.x; i < nt * hdp; i += blockDim.x) {
-    const int t = i / hdp, c = i - t * hdp;
-    sk[t * ks + c] = kbase[i];
-    sv[i] = vbase[i];
+  const float4* kbase = reinterpret_cast<const float4*>(a.kc + ((size_t)pg * a.Hkv + kvh) * P * hdp);
+  const float4* vbase = reinterpret_cast<const float4*>(a.vc + ((size_t)pg * a.Hkv + kvh) * P * hdp);
+  const int h4 = hdp >> 2;
+  // issue every K/V/q load of this CTA before the first shared store
+  {
+    constexpr int kMaxLd = 8;  // P * hdp / 4 / threads for hdp <= 128
+    float4 kr[kMaxLd], vr[kMaxLd];
+    const int n4 = nt * h4;
+#pragma unroll
+    for (int u = 0; u < kMaxLd; ++u) {
+      const int i = threadIdx.x + u * kAttnThreads;
+      if (i < n4) { kr[u] = __ldcg(kbase + i); vr[u] = __ldcg(vbase + i); }
+    }
+    constexpr int kMaxQ = 16;  // R * hdp / 4 / threads for R * hdp <= 16384
+    float4 qr[kMaxQ];
+#pragma unroll
+    for (int u = 0; u < kMaxQ; ++u) {
+      const int i = threadIdx.x + u * kAttnThreads;
+      if (i < R * h4) {
+        const int row = i / h4, c4 = i - row * h4;
+        const int m = row / G, gi = row - m * G;
+        qr[u] = __ldcg(reinterpret_cast<const float4*>(a.q + ((size_t)m * a.H + kvh * G + gi) * hdp) + c4);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kMaxQ; ++u) {
+      const int i = threadIdx.x + u * kAttnThreads;
+      if (i < R * h4) reinterpret_cast<float4*>(sq)[i] = qr[u];
+    }
+#pragma unroll
+    for (int u = 0; u < kMaxLd; ++u) {
+      const int i = threadIdx.x + u * kAttnThreads;
+      if (i < n4) {
+        const int t = i / h4, c4 = i - t * h4;
+        *reinterpret_cast<float4*>(sk + (size_t)t * ks + 4 * c4) = kr[u];
+        reinterpret_cast<float4*>(sv)[i] = vr[u];
+      }
+    }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < R * nt; i += blockDim.x) {
-    const int row = i / nt, t = i - row * nt;
-    const int m = row / G;
-    float s = -INFINITY;
-    if (t0 + t <= pos0 + m) {
-      const float* qr = sq + (size_t)row * hdp;
-      const float* kr = sk + (size_t)t * ks;
-      float dot = 0.0f;
-      for (int c = 0; c < hdp; ++c) dot = __fmaf_rn(qr[c], kr[c], dot);
-      s = __fdiv_rn(dot, a.inv_scale_den);
+  // scores: thread -> position t, row group; rows r, r+rg, ... share each K load
+  {
+    const int t = threadIdx.x % P;
+    const int rg = blockDim.x / P;
+    for (int r0 = threadIdx.x / P; r0 < R; r0 += rg * kAttnRowBlk) {
+      float acc[kAttnRowBlk];
+#pragma unroll
+      for (int j = 0; j < kAttnRowBlk; ++j) acc[j] = 0.0f;
+      if (t < nt) {
+        const float* kr = sk + (size_t)t * ks;
+        for (int c = 0; c < hdp; c += 4) {
+          const float4 kv = *reinterpret_cast<const float4*>(kr + c);
+#pragma unroll
+          for (int j = 0; j < kAttnRowBlk; ++j) {
+            const int row = r0 + j * rg;
+            if (row < R) {
+              const float4 qv = *reinterpret_cast<const float4*>(sq + row * hdp + c);
+              acc[j] = __fmaf_rn(qv.x, kv.x, acc[j]);
+              acc[j] = __fmaf_rn(qv.y, kv.y, acc[j]);
+              acc[j] = __fmaf_rn(qv.z, kv.z, acc[j]);
+              acc[j] = __fmaf_rn(qv.w, kv.w, acc[j]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kAttnRowBlk; ++j) {
+        const int row = r0 + j * rg;
+        if (row < R) {
+          const int m = row / G;
+          ss[row * P + t] = (t < nt && t0 + t <= pos0 + m) ? __fdiv_rn(acc[j], a.inv_scale_den)
+                                                            : -INFINITY;
+        }
+      }
     }
-    ss[row * P + t] = s;
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int row = warp; row < R; row += blockDim.x >> 5) {
     float mx = -INFINITY;
-    for (int t = lane; t < nt; t += 32) mx = fmaxf(mx, ss[row * P + t]);
+    for (int t = lane; t < P; t += 32) mx = fmaxf(mx, ss[row * P + t]);
 #pragma unroll
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float sum = 0.0f;
-    for (int t = lane; t < nt; t += 32) {
-      const float s = ss[row * P + t];
-      const float p = (mx == -INFINITY) ? 0.0f : expf(s - mx);
+    for (int t = lane; t < P; t += 32) {
+      const float sc = ss[row * P + t];
+      const float p = (sc == -INFINITY) ? 0.0f : expf(sc - mx);
       ss[row * P + t] = p;
       sum += p;
     }
@@ -596,12 +791,30 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
     if (lane == 0) { s_m[row] = mx; s_l[row] = sum; }
   }
   __syncthreads();
+  // P.V: thread -> column c, row group; rows share each V load
   const size_t pbase = ((size_t)kvh * a.max_chunks + chunk) * R;
-  for (int i = threadIdx.x; i < R * hdp; i += blockDim.x) {
-    const int row = i / hdp, c = i - row * hdp;
-    float o = 0.0f;
-    for (int t = 0; t < nt; ++t) o = __fmaf_rn(ss[row * P + t], sv[t * hdp + c], o);
-    a.part_o[(pbase + row) * hdp + c] = o;
+  {
+    const int c = threadIdx.x % hdp;
+    const int rg = blockDim.x / hdp;
+    const int r_first = (threadIdx.x < rg * hdp) ? (int)(threadIdx.x / hdp) : R;
+    for (int r0 = r_first; r0 < R; r0 += rg * kAttnRowBlk) {
+      float acc[kAttnRowBlk];
+#pragma unroll
+      for (int j = 0; j < kAttnRowBlk; ++j) acc[j] = 0.0f;
+      for (int t = 0; t < nt; ++t) {
+        const float vv = sv[t * hdp + c];
+#pragma unroll
+        for (int j = 0; j < kAttnRowBlk; ++j) {
+          const int row = r0 + j * rg;
+          if (row < R) acc[j] = __fmaf_rn(ss[row * P + t], vv, acc[j]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kAttnRowBlk; ++j) {
+        const int row = r0 + j * rg;
+        if (row < R) a.part_o[(pbase + row) * hdp + c] = acc[j];
+      }
+    }
   }
   for (int row = threadIdx.x; row < R; row += blockDim.x) {
     a.part_ml[(pbase + row) * 2] = s_m[row];
@@ -609,46 +822,86 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
   }
   __threadfence();
   __syncthreads();
-  __shared__ int s_last;
   if (threadIdx.x == 0) s_last = (atomicAdd(a.cnt + kvh, 1) == n_chunks - 1);
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  // combine the pages of this KV head
+  // combine the pages of this KV head.  All (m_c, l_c) pairs are loaded in
+  // one round; page c contributes e^(m_c - M) * (sum_t e^(s_t - m_c) v_t) to
+  // the numerator and e^(m_c - M) * l_c to the denominator.
+  float* sml = sk;  // reuse the K tile area: [R][n_chunks][2]
+  for (int i = threadIdx.x; i < R * n_chunks; i += blockDim.x) {
+    const int row = i / n_chunks, c = i - row * n_chunks;
+    const float2 v = __ldcg(reinterpret_cast<const float2*>(a.part_ml) +
+                            (((size_t)kvh * a.max_chunks + c) * R + row));
+    sml[2 * i] = v.x;
+    sml[2 * i + 1] = v.y;
+  }
+  __syncthreads();
+  float* wgt = ss;  // [R][n_chunks]
   for (int row = threadIdx.x; row < R; row += blockDim.x) {
     float M_ = -INFINITY;
-    for (int c = 0; c < n_chunks; ++c)
-      M_ = fmaxf(M_, ld_cg_f(a.part_ml + (((size_t)kvh * a.max_chunks + c) * R + row) * 2));
+    for (int c = 0; c < n_chunks; ++c) M_ = fmaxf(M_, sml[2 * (row * n_chunks + c)]);
     float l = 0.0f;
     for (int c = 0; c < n_chunks; ++c) {
-      const size_t b = (((size_t)kvh * a.max_chunks + c) * R + row) * 2;
-      const float mc = ld_cg_f(a.part_ml + b);
-      if (mc != -INFINITY) l += ld_cg_f(a.part_ml + b + 1) * expf(mc - M_);
+      const float mc = sml[2 * (row * n_chunks + c)];
+      const float w = (mc == -INFINITY) ? 0.0f : expf(mc - M_);
+      wgt[row * n_chunks + c] = w;
+      l += w * sml[2 * (row * n_chunks + c) + 1];
     }
-    s_m[row] = M_;
     s_l[row] = l;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < R * hdp; i += blockDim.x) {
-    const int row = i / hdp, c = i - row * hdp;
-    float o = 0.0f;
-    for (int ch = 0; ch < n_chunks; ++ch) {
-      const size_t b = ((size_t)kvh * a.max_chunks + ch) * R + row;
-      const float mc = ld_cg_f(a.part_ml + b * 2);
-      if (mc != -INFINITY) o += ld_cg_f(a.part_o + b * hdp + c) * expf(mc - s_m[row]);
+  {
+    const int c = threadIdx.x % hdp;
+    const int rg = blockDim.x / hdp;
+    const int r_first = (threadIdx.x < rg * hdp) ? (int)(threadIdx.x / hdp) : R;
+    const size_t cstride = (size_t)R * hdp;
+    for (int r0 = r_first; r0 < R; r0 += rg * kAttnRowBlk) {
+      float acc[kAttnRowBlk];
+#pragma unroll
+      for (int j = 0; j < kAttnRowBlk; ++j) acc[j] = 0.0f;
+      const float* base = a.part_o + ((size_t)kvh * a.max_chunks * R) * hdp + c;
+#pragma unroll 4
+      for (int ch = 0; ch < n_chunks; ++ch) {
+        float v[kAttnRowBlk];
+#pragma unroll
+        for (int j = 0; j < kAttnRowBlk; ++j) {
+          const int row = r0 + j * rg;
+          v[j] = row < R ? __ldcg(base + ch * cstride + (size_t)row * hdp) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < kAttnRowBlk; ++j) {
+          const int row = r0 + j * rg;
+          if (row < R) acc[j] = __fmaf_rn(v[j], wgt[row * n_chunks + ch], acc[j]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kAttnRowBlk; ++j) {
+        const int row = r0 + j * rg;
+        if (row < R) {
+          const int m = row / G, gi = row - m * G;
+          a.out[((size_t)m * a.H + kvh * G + gi) * hdp + c] = __fdiv_rn(acc[j], s_l[row]);
+        }
+      }
     }
-    const int m = row / G, gi = row - m * G;
-    a.out[((size_t)m * a.H + kvh * G + gi) * hdp + c] = __fdiv_rn(o, s_l[row]);
   }
   if (threadIdx.x == 0) atomicExch(a.cnt + kvh, 0);
+}
+
+size_t attention_smem_bytes(int G, int M, int hdp, int page) {
+  const size_t R = (size_t)G * M;
+  return (R * hdp + (size_t)page * (hdp + 4) + (size_t)page * hdp + R * page) * sizeof(float);
 }
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
   const int G = a.H / a.Hkv;
   const int R = G * a.M;
-  size_t smem = ((size_t)R * a.hdp + (size_t)a.page * (a.hdp + 1) + (size_t)a.page * a.hdp +
-                 (size_t)R * a.page) * sizeof(float);
-  if (R > 128) return cudaErrorInvalidValue;
+  if (R > 128 || a.page != 64 || a.max_chunks > a.page || a.hdp > 128 || (a.hdp & 3) ||
+      (size_t)R * a.max_chunks * 2 > (size_t)a.page * (a.hdp + 4) || R * a.hdp > 16 * 4 * kAttnThreads)
+    return cudaErrorInvalidValue;
+  const size_t smem = attention_smem_bytes(G, a.M, a.hdp, a.page);
+  if (smem > (size_t)g_attn_smem) return cudaErrorInvalidConfiguration;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.Hkv, a.max_chunks);
   cfg.blockDim = dim3(kAttnThreads);
@@ -659,23 +912,13 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (smem > (size_t)g_attn_smem) return cudaErrorInvalidConfiguration;
   return cudaLaunchKernelEx(&cfg, k_attention, a);
 }
 
-size_t attention_smem_bytes(int G, int M, int hdp, int page) {
-  const size_t R = (size_t)G * M;
-  return (R * hdp + (size_t)page * (hdp + 1) + (size_t)page * hdp + R * page) * sizeof(float);
-}
-
-// Raise the dynamic shared-memory limits once, outside any stream capture.
+// Raise the dynamic shared-memory limit once, outside any stream capture.
 cudaError_t prepare_kernels(size_t quant_smem, size_t attn_smem) {
-  if (quant_smem > (size_t)g_quant_smem) {
-    cudaError_t e = cudaFuncSetAttribute(k_quant, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)quant_smem);
-    if (e != cudaSuccess) return e;
-    g_quant_smem = (int)quant_smem;
-  }
+  (void)quant_smem;
+
   if (attn_smem > (size_t)g_attn_smem) {
     cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)attn_smem);
