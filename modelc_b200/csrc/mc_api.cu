@@ -561,6 +561,11 @@ struct mc_session {
   float* part_ml = nullptr;
   int* acnt = nullptr;
   int* err = nullptr;  // device flag raised by an expired bounded wait
+  // activation statistics handed from each producer to the next encoder:
+  // two max|x*w| slots used alternately, and per-stripe sums of squares
+  unsigned* st_amax = nullptr;  // [2][kMaxTokens]
+  float* st_pss = nullptr;      // [kMaxTokens][max stripes]
+  int st_np_cap = 0;
   KVSet tkv, dkv;
   // device-resident speculative state
   SpecState* st = nullptr;
@@ -673,6 +678,10 @@ static mc_status session_alloc(mc_session* s) {
   CKS(s->al.alloc(&s->part_ml, pml * n_pages));
   CKS(s->al.alloc(&s->err, 1));
   CK(cudaMemset(s->err, 0, 4));
+  CKS(s->al.alloc(&s->st_amax, (size_t)2 * kMaxTokens));
+  CK(cudaMemset(s->st_amax, 0, (size_t)2 * kMaxTokens * 4));
+  s->st_np_cap = std::max(stripes, 1);
+  CKS(s->al.alloc(&s->st_pss, (size_t)kMaxTokens * s->st_np_cap));
   CKS(s->al.alloc(&s->acnt, (size_t)hkv));
   CK(cudaMemset(s->acnt, 0, (size_t)hkv * 4));
   CKS(alloc_kv(s, s->tw, &s->tkv));
@@ -756,9 +765,25 @@ static mc_status check_err(int* err) {
   return MC_OK;
 }
 
+// Statistics an encoder takes from its producer (see QuantArgs).
+struct StatIO {
+  const float* pss;
+  int np;
+  const unsigned* amax;
+  unsigned* amax_next;
+};
+
 static mc_status enq_quant(mc_session* s, const float* h, int ld, int d, int M, const float* w,
-                           float eps, int do_norm) {
+                           float eps, int do_norm, const StatIO* io = nullptr) {
   QuantArgs q{};
+  if (io) {
+    q.use_stats = 1;
+    q.pss = io->pss;
+    q.np = io->np;
+    q.np_stride = io->np;
+    q.amax = io->amax;
+    q.amax_next = io->amax_next;
+  }
   q.h = h;
   q.ld = ld;
   q.d = d;
@@ -814,7 +839,35 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
   ea.h = s->h;
   ea.zero_keys = keys;
   ea.n_zero = keys ? M : 0;
+  // Encoders in launch order with the RMSNorm weight each applies (nullptr:
+  // no norm).  Producer j (embedding, attention, or a GEMV epilogue) folds
+  // the statistics of its output into slot j % 2 for encoder j, which zeroes
+  // the other slot for producer j + 1.
+  std::vector<const float*> enc_w;
+  for (const LayerW& Lw : W->layers) {
+    if (Lw.attn) { enc_w.push_back(Lw.attn_norm); enc_w.push_back(nullptr); }
+    if (Lw.mlp) { enc_w.push_back(Lw.mlp_norm); enc_w.push_back(nullptr); }
+  }
+  enc_w.push_back(W->final_norm);
+  size_t ej = 0;  // next encoder
+  auto slot = [&](size_t j) { return s->st_amax + (j & 1) * kMaxTokens; };
+  auto io_for = [&](size_t j, int np) {
+    return StatIO{s->st_pss, np, slot(j), slot(j + 1)};
+  };
+  ea.st_pss = s->st_pss;
+  ea.st_np = 1;
+  ea.st_amax = slot(0);
+  ea.st_w = enc_w[0];
   CK(launch_embed(ea, s->stream, true));
+  int prod_np = 1;  // sum-of-squares partials written by the last h producer
+  // residual producers fill st_* for the encoder that follows them
+  auto resid_stats = [&](GemvArgs& g, const PMat& Wm) {
+    g.st_pss = s->st_pss;
+    g.st_np = Wm.n_stripes;
+    g.st_amax = slot(ej);
+    g.st_w = enc_w[ej];
+    prod_np = Wm.n_stripes;
+  };
   const int d = W->d, F = W->F;
   // the GEMVs of this forward in launch order (each warms L2 for the next)
   std::vector<const PMat*> seq;
@@ -828,7 +881,9 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
   for (int l = 0; l < W->L; ++l) {
     const LayerW& Lw = W->layers[l];
     if (Lw.attn) {
-      CKS(enq_quant(s, s->h, d, d, M, Lw.attn_norm, W->eps, Lw.attn_norm ? 1 : 0));
+      StatIO io = io_for(ej, prod_np);
+      CKS(enq_quant(s, s->h, d, d, M, Lw.attn_norm, W->eps, Lw.attn_norm ? 1 : 0, &io));
+      ++ej;
       GemvArgs a{};
       a.q_out = s->qb;
       a.kc = kv.k + (size_t)l * kv.layer_stride;
@@ -864,30 +919,41 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       t.part_ml = s->part_ml;
       t.cnt = s->acnt;
       t.out = s->attn;
+      t.st_amax = slot(ej);
       CK(launch_attention(t, s->stream, true));
-      CKS(enq_quant(s, s->attn, W->H * W->hdp, W->H * W->hdp, M, nullptr, 0.0f, 0));
+      io = io_for(ej, 0);
+      CKS(enq_quant(s, s->attn, W->H * W->hdp, W->H * W->hdp, M, nullptr, 0.0f, 0, &io));
+      ++ej;
       GemvArgs o{};
       o.out = s->h;
       o.ldo = d;
       o.n_out = d;
+      resid_stats(o, Lw.o);
       CKS(enq_gemv(s, Lw.o, EPI_RESID, M, o, nxt()));
     }
     if (Lw.mlp) {
-      CKS(enq_quant(s, s->h, d, d, M, Lw.mlp_norm, W->eps, Lw.mlp_norm ? 1 : 0));
+      StatIO io = io_for(ej, prod_np);
+      CKS(enq_quant(s, s->h, d, d, M, Lw.mlp_norm, W->eps, Lw.mlp_norm ? 1 : 0, &io));
+      ++ej;
       GemvArgs g{};
       g.out = s->act;
       g.ldo = F;
       g.n_out = F;
+      g.st_amax = slot(ej);
       CKS(enq_gemv(s, Lw.gu, EPI_SWIGLU, M, g, nxt()));
-      CKS(enq_quant(s, s->act, F, F, M, nullptr, 0.0f, 0));
+      io = io_for(ej, 0);
+      CKS(enq_quant(s, s->act, F, F, M, nullptr, 0.0f, 0, &io));
+      ++ej;
       GemvArgs dn{};
       dn.out = s->h;
       dn.ldo = d;
       dn.n_out = d;
+      resid_stats(dn, Lw.down);
       CKS(enq_gemv(s, Lw.down, EPI_RESID, M, dn, nxt()));
     }
   }
-  CKS(enq_quant(s, s->h, d, d, M, W->final_norm, W->eps, W->final_norm ? 1 : 0));
+  StatIO io = io_for(ej, prod_np);
+  CKS(enq_quant(s, s->h, d, d, M, W->final_norm, W->eps, W->final_norm ? 1 : 0, &io));
   GemvArgs hd{};
   hd.out = logits_dev;
   hd.ldo = W->V;

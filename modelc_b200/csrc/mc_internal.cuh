@@ -62,6 +62,14 @@ struct GemvArgs {
   int* ws;               // split-K partial sums [n_stripes][16][8*NT] (zeroed)
   int* cnt;              // [n_stripes] k-block arrival counters (zeroed)
   int* err;              // set to 1 when a bounded device wait expires
+  // Statistics for the next activation encoding, produced by the RESID and
+  // SWIGLU epilogues: per-stripe sum of squares st_pss[m * st_np + stripe]
+  // (RESID only) and max |value * st_w[row]| folded into st_amax[m] (float
+  // bits, atomicMax).  st_amax == nullptr disables both.
+  float* st_pss;
+  int st_np;
+  unsigned* st_amax;
+  const float* st_w;
   const void* next_w;    // weights of the next GEMV in the stream (L2 prefetch)
   long long next_bytes;  // its packed size
   long long next_pf_bytes;  // how much of it to prefetch
@@ -96,6 +104,14 @@ struct QuantArgs {
   int KB;                // ceil(d/32) (padded k-blocks written)
   int nt;
   int* xexp;
+  // Producer-side statistics (use_stats != 0): sum of squares as np partials
+  // pss[m * np_stride + j], and max |x * w| as float bits amax[m]; the kernel
+  // then zeroes amax_next[0..kMaxTokens) for the following producer.
+  int use_stats;
+  const float* pss;
+  int np, np_stride;
+  const unsigned* amax;
+  unsigned* amax_next;
 };
 
 struct AttnArgs {
@@ -112,6 +128,7 @@ struct AttnArgs {
   float* part_ml;        // [Hkv][max_chunks][G*M][2]
   int* cnt;              // [Hkv]
   float* out;            // [M][H][hdp]
+  unsigned* st_amax;     // max |out| per token (float bits, atomicMax) or nullptr
 };
 
 enum EmbedSrc : int {
@@ -134,6 +151,14 @@ struct EmbedArgs {
   float* h;              // [M][d]
   unsigned long long* zero_keys;  // keys this forward will produce
   int n_zero;
+  // statistics of h for the first encoding: st_pss[m * st_np] = sum(h*h),
+  // st_amax[m] = max |h * st_w| (plain stores); st_zero[0..n_st_zero) zeroed
+  float* st_pss;
+  int st_np;
+  unsigned* st_amax;
+  const float* st_w;
+  unsigned* st_zero;
+  int n_st_zero;
 };
 
 struct SpecState {

@@ -13,6 +13,8 @@
 //  k_accept    greedy acceptance (generate.rs:695-726).
 #include <math.h>
 
+#include <algorithm>
+
 #include "mc_internal.cuh"
 
 namespace mc {
@@ -122,6 +124,214 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
   return __fmul_rn(s, u);
 }
 
+// ------------------------------------------------------------ activation encoding
+// Per-token statistics of an activation row block, reduced with one fixed
+// tree of kStatLanes virtual lanes (partials per lane, xor-shuffles within a
+// virtual warp, then the 16 virtual warps summed in order), so every kernel
+// that encodes activations -- whatever its block size -- gets bit-identical
+// exponents and multipliers.  RMSNorm follows transformer.rs:888-896
+// (ms = sum(v*v)/n, rms = sqrt(ms + eps), x = v / rms * w).  The exponent
+// makes |x| * 2^e < 2^20 with a one-ulp margin (digits tolerate |X| < 2^21).
+constexpr int kStatLanes = 512;
+constexpr int kStatWarps = kStatLanes / 32;
+
+struct StatArgs {
+  const float* h;
+  int ld, d, M;
+  const float* w;
+  int wlen;
+  float eps;
+  int do_norm;
+};
+
+// Slice capture: if cap != nullptr, elements [lo, hi) of every token are also
+// stored to cap[m * (hi - lo) + (i - lo)].
+__device__ __forceinline__ void token_stats(const StatArgs& a, float (*red_ss)[kMaxTokens],
+                                            float (*red_hw)[kMaxTokens], uint32_t* s_bad,
+                                            float* s_mul, int* s_e, float* cap, int lo, int hi) {
+  const int M = a.M, d = a.d;
+  const bool vec = ((a.ld & 3) == 0) && ((d & 3) == 0) &&
+                   ((reinterpret_cast<uintptr_t>(a.h) & 15) == 0);
+  const int span = hi - lo;
+  if (threadIdx.x == 0) *s_bad = 0u;
+  __syncthreads();
+  uint32_t bad = 0u;
+  for (int v = threadIdx.x; v < kStatLanes; v += blockDim.x) {
+    float ss[kMaxTokens], hw[kMaxTokens];
+#pragma unroll
+    for (int m = 0; m < kMaxTokens; ++m) { ss[m] = 0.0f; hw[m] = 0.0f; }
+    if (vec) {
+#pragma unroll 4
+      for (int i = v * 4; i < d; i += kStatLanes * 4) {
+        float4 wv = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+        if (a.do_norm && a.w) {
+          wv.x = i < a.wlen ? a.w[i] : 1.0f;
+          wv.y = i + 1 < a.wlen ? a.w[i + 1] : 1.0f;
+          wv.z = i + 2 < a.wlen ? a.w[i + 2] : 1.0f;
+          wv.w = i + 3 < a.wlen ? a.w[i + 3] : 1.0f;
+        }
+#pragma unroll
+        for (int m = 0; m < kMaxTokens; ++m)
+          if (m < M) {
+            const float4 x = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)m * a.ld + i));
+            if (cap && i >= lo && i < hi) *reinterpret_cast<float4*>(cap + m * span + (i - lo)) = x;
+            ss[m] = __fadd_rn(ss[m], __fmul_rn(x.x, x.x));
+            ss[m] = __fadd_rn(ss[m], __fmul_rn(x.y, x.y));
+            ss[m] = __fadd_rn(ss[m], __fmul_rn(x.z, x.z));
+            ss[m] = __fadd_rn(ss[m], __fmul_rn(x.w, x.w));
+            hw[m] = fmaxf(hw[m], fmaxf(fmaxf(fabsf(__fmul_rn(x.x, wv.x)), fabsf(__fmul_rn(x.y, wv.y))),
+                                       fmaxf(fabsf(__fmul_rn(x.z, wv.z)), fabsf(__fmul_rn(x.w, wv.w)))));
+            if (!(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w))) bad |= 1u << m;
+          }
+      }
+    } else {
+      for (int i = v; i < d; i += kStatLanes) {
+        const float wi = (a.do_norm && a.w && i < a.wlen) ? a.w[i] : 1.0f;
+#pragma unroll
+        for (int m = 0; m < kMaxTokens; ++m)
+          if (m < M) {
+            const float x = __ldcg(a.h + (size_t)m * a.ld + i);
+            if (cap && i >= lo && i < hi) cap[m * span + (i - lo)] = x;
+            ss[m] = __fadd_rn(ss[m], __fmul_rn(x, x));
+            hw[m] = fmaxf(hw[m], fabsf(__fmul_rn(x, wi)));
+            if (!isfinite(x)) bad |= 1u << m;
+          }
+      }
+    }
+    const int vw = v >> 5;
+#pragma unroll
+    for (int m = 0; m < kMaxTokens; ++m) {
+      if (m < M) {
+        float x = ss[m], y = hw[m];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+          x += __shfl_xor_sync(0xffffffffu, x, o);
+          y = fmaxf(y, __shfl_xor_sync(0xffffffffu, y, o));
+        }
+        if ((v & 31) == 0) { red_ss[vw][m] = x; red_hw[vw][m] = y; }
+      }
+    }
+  }
+  bad = __reduce_or_sync(0xffffffffu, bad);
+  if ((threadIdx.x & 31) == 0 && bad) atomicOr(s_bad, bad);
+  __syncthreads();
+  if (threadIdx.x < M) {
+    const int m = threadIdx.x;
+    float x = 0.0f, y = 0.0f;
+    for (int w = 0; w < kStatWarps; ++w) { x += red_ss[w][m]; y = fmaxf(y, red_hw[w][m]); }
+    float rms = 1.0f;
+    if (a.do_norm) rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(x, (float)(d > 1 ? d : 1)), a.eps));
+    const float amax = a.do_norm ? y / rms : y;
+    int e = 0;
+    if (((*s_bad >> m) & 1u) || !isfinite(amax)) {
+      e = kExpNonFinite;
+    } else if (amax > 0.0f) {
+      int E;
+      frexpf(amax * 1.0000002f, &E);
+      e = 20 - E;
+    }
+    // x * 2^e = (h * w) * (2^e / rms): the power-of-two factor is exact; one
+    // reciprocal per token replaces the per-element division (<= 1 ulp).
+    float mul = 0.0f;
+    if (e != kExpNonFinite) mul = ldexpf(a.do_norm ? 1.0f / rms : 1.0f, e);
+    s_mul[m] = mul;
+    s_e[m] = e;
+  }
+  __syncthreads();
+}
+
+// Encodes k-blocks [kb0, kb1) of the digit operand: one task per (token,
+// 4 consecutive k) computes the 4 fixed-point values once and writes its
+// three digit words; leftover columns of the last n8 tile get zero words.
+// Tasks run in batches of kEncBatch per thread with all their loads issued
+// first.  src4(m, k) returns the raw activations k..k+3 (k % 4 == 0, zeros
+// past d); dst(word, value) stores a word.
+constexpr int kEncBatch = 8;
+
+template <class Src4, class Dst>
+__device__ __forceinline__ void encode_digits(const StatArgs& a, int nt, int kb0, int kb1,
+                                              const float* s_mul, const int* s_e, Src4 src4,
+                                              Dst dst) {
+  const int M = a.M, d = a.d;
+  const int pad_cols = 8 * nt - 3 * M;
+  const int ngroups = (kb1 - kb0) * 8;
+  const int tasks = ngroups * (M + pad_cols);
+  for (int t0 = threadIdx.x; t0 < tasks; t0 += blockDim.x * kEncBatch) {
+    float4 v[kEncBatch];
+#pragma unroll
+    for (int u = 0; u < kEncBatch; ++u) {
+      const int task = t0 + u * blockDim.x;
+      v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (task < tasks) {
+        const int grp = task % ngroups, q = task / ngroups;
+        if (q < M && s_e[q] != kExpNonFinite)
+          v[u] = src4(q, (kb0 + (grp >> 3)) * 32 + (grp & 7) * 4);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kEncBatch; ++u) {
+      const int task = t0 + u * blockDim.x;
+      if (task >= tasks) continue;
+      const int grp = task % ngroups;
+      const int q = task / ngroups;  // token (q < M) or padding column (q >= M)
+      const int kb = kb0 + (grp >> 3);
+      const int kk = (grp & 7) * 4;
+      const int reg = kk >> 4, t = (kk & 15) >> 2;
+      if (q >= M) {
+        const int c = 3 * M + (q - M);
+        const int tile = c >> 3, ln = (c & 7) * 4 + t;
+        dst((((size_t)kb * 32 + ln) * nt + tile) * 2 + reg, 0u);
+        continue;
+      }
+      const int m = q;
+      uint32_t w0 = 0, w1 = 0, w2 = 0;
+      if (s_e[m] != kExpNonFinite) {
+        const float mul = s_mul[m];
+        const float vv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int k = kb * 32 + kk + j;
+          int X = 0;
+          if (k < d) {
+            float x = vv[j];
+            if (a.do_norm) x = __fmul_rn(x, (a.w && k < a.wlen) ? a.w[k] : 1.0f);
+            X = __float2int_rn(__fmul_rn(x, mul));
+          }
+          const int d2 = ((X + 64) & 127) - 64;
+          const int X1 = (X - d2) >> 7;
+          const int d1 = ((X1 + 64) & 127) - 64;
+          const int d0 = (X1 - d1) >> 7;
+          w0 |= (uint32_t)(d0 & 0xff) << (8 * j);
+          w1 |= (uint32_t)(d1 & 0xff) << (8 * j);
+          w2 |= (uint32_t)(d2 & 0xff) << (8 * j);
+        }
+      }
+      const uint32_t wd[3] = {w0, w1, w2};
+#pragma unroll
+      for (int dg = 0; dg < 3; ++dg) {
+        const int c = 3 * m + dg;
+        const int tile = c >> 3, ln = (c & 7) * 4 + t;
+        dst((((size_t)kb * 32 + ln) * nt + tile) * 2 + reg, wd[dg]);
+      }
+    }
+  }
+}
+
+// Four consecutive activations of token m starting at k (k % 4 == 0), zero
+// past d; vectorised when the row is float4-aligned.  Read through L2: the
+// producing kernel may have finished after this grid was scheduled.
+__device__ __forceinline__ float4 load_act4(const float* h, int ld, int d, int m, int k) {
+  const float* p = h + (size_t)m * ld + k;
+  if (k + 3 < d && ((reinterpret_cast<uintptr_t>(p) & 15) == 0))
+    return __ldcg(reinterpret_cast<const float4*>(p));
+  float4 r;
+  r.x = k < d ? __ldcg(p) : 0.0f;
+  r.y = k + 1 < d ? __ldcg(p + 1) : 0.0f;
+  r.z = k + 2 < d ? __ldcg(p + 2) : 0.0f;
+  r.w = k + 3 < d ? __ldcg(p + 3) : 0.0f;
+  return r;
+}
+
 // ------------------------------------------------------------ GEMV
 // Work split: each CTA owns a contiguous range of the linear (stripe,
 // k-block) index (stream-K, balanced to one k-block); its 8 warps own
@@ -140,7 +350,10 @@ struct GemvCfg {
 
 constexpr int kGemvWarps = 8;
 
-// Epilogue of a finished stripe from a row-major [16][ld] int tile.
+// Epilogue of a finished stripe from a row-major [16][ld] int tile, run by
+// one warp.  Lane (it, lane) handles rows r and r+8 of token m, with
+// idx = it*32 + lane, r = idx & 7, m = idx >> 3; the 8 lanes of a token form
+// one shuffle group for the encoding statistics.
 template <int NT, int EPI>
 __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, const int* tile,
                                               int ld, int lane, unsigned long long* kmax,
@@ -148,19 +361,30 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
   const int M = a.M;
 #pragma unroll
   for (int it = 0; it < (8 * kMaxTokens) / 32; ++it) {
+    if (it * 32 >= 8 * M) break;  // warp-uniform
     const int idx = it * 32 + lane;
-    if (it * 32 >= 8 * M) break;
-    if (idx < 8 * M) {
-      const int r = idx & 7, m = idx >> 3;
+    const bool valid = idx < 8 * M;
+    const int r = idx & 7, m = valid ? (idx >> 3) : 0;
+    const int prow = stripe * 16 + r;
+    // statistics contribution of this lane: sum(h*h) and max|h*w| kept as
+    // float bits, whose unsigned order matches |x| and lets NaN/inf win
+    float st_sq = 0.0f;
+    uint32_t st_mx = 0u;
+    if (valid) {
       const int e = xexp[m];
-      const int prow = stripe * 16 + r;
       const float y0 = combine_digits(tile + r * ld, m, scale[prow], e);
       const float y1 = combine_digits(tile + (r + 8) * ld, m, scale[prow + 8], e);
       if constexpr (EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_LMHEAD) {
         float* o = a.out ? a.out + (size_t)m * a.ldo : nullptr;
         if (prow < a.n_out) {
-          if constexpr (EPI == EPI_RESID) o[prow] = __fadd_rn(o[prow], y0);
-          else if (o) o[prow] = y0;
+          if constexpr (EPI == EPI_RESID) {
+            const float h0 = __fadd_rn(o[prow], y0);
+            o[prow] = h0;
+            st_sq = __fmul_rn(h0, h0);
+            st_mx = __float_as_uint(fabsf(__fmul_rn(h0, a.st_w ? a.st_w[prow] : 1.0f)));
+          } else if (o) {
+            o[prow] = y0;
+          }
           if constexpr (EPI == EPI_LMHEAD) {
             if (!isnan(y0)) {
               unsigned long long k = argmax_key(y0, (uint32_t)prow);
@@ -169,8 +393,14 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
           }
         }
         if (prow + 8 < a.n_out) {
-          if constexpr (EPI == EPI_RESID) o[prow + 8] = __fadd_rn(o[prow + 8], y1);
-          else if (o) o[prow + 8] = y1;
+          if constexpr (EPI == EPI_RESID) {
+            const float h1 = __fadd_rn(o[prow + 8], y1);
+            o[prow + 8] = h1;
+            st_sq = __fadd_rn(st_sq, __fmul_rn(h1, h1));
+            st_mx = max(st_mx, __float_as_uint(fabsf(__fmul_rn(h1, a.st_w ? a.st_w[prow + 8] : 1.0f))));
+          } else if (o) {
+            o[prow + 8] = y1;
+          }
           if constexpr (EPI == EPI_LMHEAD) {
             if (!isnan(y1)) {
               unsigned long long k = argmax_key(y1, (uint32_t)(prow + 8));
@@ -180,7 +410,11 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
         }
       } else if constexpr (EPI == EPI_SWIGLU) {
         const int i = stripe * 8 + r;  // row r = gate_i, row r+8 = up_i
-        if (i < a.n_out) a.out[(size_t)m * a.ldo + i] = silu_mul(y0, y1);
+        if (i < a.n_out) {
+          const float act = silu_mul(y0, y1);
+          a.out[(size_t)m * a.ldo + i] = act;
+          st_mx = __float_as_uint(fabsf(act));
+        }
       } else if constexpr (EPI == EPI_QKV) {
         const int pos = *a.pos_ptr + a.pos_add + m;
         const int per_head = a.half_p >> 3;  // stripes per head (Q/K) = hdp/16
@@ -212,6 +446,20 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
           float* v = a.vc + (((size_t)pg * a.Hkv + hh) * a.page + slot) * a.hdp;
           v[j] = y0;
           v[j + 8] = y1;
+        }
+      }
+    }
+    if constexpr (EPI == EPI_RESID || EPI == EPI_SWIGLU) {
+      if (a.st_amax) {  // warp-uniform; every lane takes part in the shuffles
+#pragma unroll
+        for (int off = 1; off < 8; off <<= 1) {
+          if constexpr (EPI == EPI_RESID)
+            st_sq = __fadd_rn(st_sq, __shfl_xor_sync(0xffffffffu, st_sq, off, 8));
+          st_mx = max(st_mx, __shfl_xor_sync(0xffffffffu, st_mx, off, 8));
+        }
+        if (valid && r == 0) {
+          if constexpr (EPI == EPI_RESID) a.st_pss[(size_t)m * a.st_np + stripe] = st_sq;
+          atomicMax(a.st_amax + m, st_mx);
         }
       }
     }
@@ -483,160 +731,71 @@ constexpr int kQuantMaxCtas = 64;
 static int g_attn_smem = 48 * 1024;  // attention dynamic smem limit set so far
 
 __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
-  __shared__ float red_ss[kQuantThreads / 32][kMaxTokens];
-  __shared__ float red_hw[kQuantThreads / 32][kMaxTokens];
-  __shared__ float s_rms[kMaxTokens];
+  __shared__ float red_ss[kStatWarps][kMaxTokens];
+  __shared__ float red_hw[kStatWarps][kMaxTokens];
+  __shared__ float s_mul[kMaxTokens];
   __shared__ int s_e[kMaxTokens];
-  __shared__ uint32_t s_bad;  // bit m: token m holds a non-finite value
+  __shared__ uint32_t s_bad;
   extern __shared__ float s_x[];
   grid_launch_dependents();
-  if (threadIdx.x == 0) s_bad = 0u;
   grid_wait();
-  const int M = a.M, d = a.d;
-  float ss[kMaxTokens], hw[kMaxTokens];
-#pragma unroll
-  for (int m = 0; m < kMaxTokens; ++m) { ss[m] = 0.0f; hw[m] = 0.0f; }
-  uint32_t bad = 0u;
-  const bool vec = ((a.ld & 3) == 0) && ((d & 3) == 0) &&
-                   ((reinterpret_cast<uintptr_t>(a.h) & 15) == 0);
-  // this CTA's k-blocks; their x values are kept in shared memory (s_x)
+  const StatArgs sa{a.h, a.ld, a.d, a.M, a.w, a.wlen, a.eps, a.do_norm};
+  // this CTA's k-blocks
   const int kbs = (a.KB + gridDim.x - 1) / gridDim.x;
   const int kb0 = blockIdx.x * kbs, kb1 = min(a.KB, kb0 + kbs);
-  const int span = max(kb1 - kb0, 0) * 32;
-  const int lo = kb0 * 32, hi = kb0 * 32 + span;
-  if (vec) {
-#pragma unroll 4
-    for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
-      float4 wv = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
-      if (a.do_norm && a.w) {
-        wv.x = i < a.wlen ? a.w[i] : 1.0f;
-        wv.y = i + 1 < a.wlen ? a.w[i + 1] : 1.0f;
-        wv.z = i + 2 < a.wlen ? a.w[i + 2] : 1.0f;
-        wv.w = i + 3 < a.wlen ? a.w[i + 3] : 1.0f;
-      }
-#pragma unroll
-      for (int m = 0; m < kMaxTokens; ++m)
-        if (m < M) {
-          const float4 v = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)m * a.ld + i));
-          if (i >= lo && i < hi) *reinterpret_cast<float4*>(s_x + m * span + (i - lo)) = v;
-          ss[m] = __fadd_rn(ss[m], __fmul_rn(v.x, v.x));
-          ss[m] = __fadd_rn(ss[m], __fmul_rn(v.y, v.y));
-          ss[m] = __fadd_rn(ss[m], __fmul_rn(v.z, v.z));
-          ss[m] = __fadd_rn(ss[m], __fmul_rn(v.w, v.w));
-          hw[m] = fmaxf(hw[m], fmaxf(fmaxf(fabsf(__fmul_rn(v.x, wv.x)), fabsf(__fmul_rn(v.y, wv.y))),
-                                     fmaxf(fabsf(__fmul_rn(v.z, wv.z)), fabsf(__fmul_rn(v.w, wv.w)))));
-          if (!(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w))) bad |= 1u << m;
-        }
-    }
-  } else {
-    for (int i = threadIdx.x; i < d; i += blockDim.x) {
-      const float wi = (a.do_norm && a.w && i < a.wlen) ? a.w[i] : 1.0f;
-#pragma unroll
-      for (int m = 0; m < kMaxTokens; ++m)
-        if (m < M) {
-          const float v = __ldcg(a.h + (size_t)m * a.ld + i);
-          if (i >= lo && i < hi) s_x[m * span + (i - lo)] = v;
-          ss[m] = __fadd_rn(ss[m], __fmul_rn(v, v));
-          hw[m] = fmaxf(hw[m], fabsf(__fmul_rn(v, wi)));
-          if (!isfinite(v)) bad |= 1u << m;
-        }
-    }
-  }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-  for (int m = 0; m < kMaxTokens; ++m) {
-    if (m < M) {
-      float x = ss[m], y = hw[m];
-#pragma unroll
-      for (int o = 16; o; o >>= 1) {
-        x += __shfl_xor_sync(0xffffffffu, x, o);
-        y = fmaxf(y, __shfl_xor_sync(0xffffffffu, y, o));
-      }
-      if (lane == 0) { red_ss[warp][m] = x; red_hw[warp][m] = y; }
-    }
-  }
-  bad = __reduce_or_sync(0xffffffffu, bad);
-  if (lane == 0 && bad) atomicOr(&s_bad, bad);
-  __syncthreads();
-  if (threadIdx.x < M) {
-    const int m = threadIdx.x;
-    float x = 0.0f, y = 0.0f;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { x += red_ss[w][m]; y = fmaxf(y, red_hw[w][m]); }
-    float rms = 1.0f;
-    if (a.do_norm) rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(x, (float)(d > 1 ? d : 1)), a.eps));
-    const float amax = a.do_norm ? y / rms : y;
-    int e = 0;
-    if (((s_bad >> m) & 1u) || !isfinite(amax)) {
-      e = kExpNonFinite;
-    } else if (amax > 0.0f) {
-      int E;
-      frexpf(amax * 1.0000002f, &E);
-      e = 20 - E;
-    }
-    // x * 2^e = (h * w) * (2^e / rms): the power-of-two factor is exact; one
-    // reciprocal per token replaces the per-element division (<= 1 ulp).
-    float mul = 0.0f;
-    if (e != kExpNonFinite) {
-      const float inv = a.do_norm ? 1.0f / rms : 1.0f;
-      mul = ldexpf(inv, e);
-    }
-    s_rms[m] = mul;
-    s_e[m] = e;
-    if (blockIdx.x == 0) a.xexp[m] = e;
-  }
-  __syncthreads();
-  // Encode: one thread per (token, 4 consecutive k) group computes the 4
-  // fixed-point values once and writes its three digit words; leftover
-  // columns of the last n8 tile are written as zero words.
-  const int nt = a.nt;
-  const int cols = 8 * nt;
-  const int pad_cols = cols - 3 * M;
-  const int ngroups = (kb1 - kb0) * 8;  // 4-element groups in this CTA's slice
+  const int lo = kb0 * 32, hi = kb0 * 32 + max(kb1 - kb0, 0) * 32;
   uint32_t* xq = reinterpret_cast<uint32_t*>(a.xq);
-  const int tasks = ngroups * (M + pad_cols);
-  for (int task = threadIdx.x; task < tasks; task += blockDim.x) {
-    const int grp = task % ngroups;
-    const int q = task / ngroups;  // token (q < M) or padding column (q >= M)
-    const int kb = kb0 + (grp >> 3);
-    const int kk = (grp & 7) * 4;
-    const int reg = kk >> 4, t = (kk & 15) >> 2;
-    if (q >= M) {
-      const int c = 3 * M + (q - M);
-      const int tile = c >> 3, ln = (c & 7) * 4 + t;
-      xq[(((size_t)kb * 32 + ln) * nt + tile) * 2 + reg] = 0u;
-      continue;
-    }
-    const int m = q;
-    const int e = s_e[m];
-    uint32_t w0 = 0, w1 = 0, w2 = 0;
-    if (e != kExpNonFinite) {
-      const float mul = s_rms[m];  // 2^e / rms (or 2^e), see above
+  if (a.use_stats) {
+    // statistics from the producing kernel: one warp per token sums the
+    // partials in a fixed order (lane-strided, then an xor-shuffle tree)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int m = warp; m < a.M; m += blockDim.x >> 5) {
+      float ss = 0.0f;
+      if (a.do_norm)
+        for (int j = lane; j < a.np; j += 32) ss = __fadd_rn(ss, __ldcg(a.pss + (size_t)m * a.np_stride + j));
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int k = kb * 32 + kk + j;
-        int X = 0;
-        if (k < d) {
-          float v = s_x[m * span + (k - kb0 * 32)];
-          if (a.do_norm) v = __fmul_rn(v, (a.w && k < a.wlen) ? a.w[k] : 1.0f);
-          X = __float2int_rn(__fmul_rn(v, mul));
+      for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      if (lane == 0) {
+        const float mx = __uint_as_float(__ldcg(a.amax + m));
+        float rms = 1.0f;
+        if (a.do_norm) rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)(a.d > 1 ? a.d : 1)), a.eps));
+        const float amax = a.do_norm ? mx / rms : mx;
+        int e = 0;
+        if (!isfinite(amax)) {  // a NaN/inf element makes the bit-max non-finite
+          e = kExpNonFinite;
+        } else if (amax > 0.0f) {
+          int E;
+          frexpf(amax * 1.0000002f, &E);
+          e = 20 - E;
         }
-        const int d2 = ((X + 64) & 127) - 64;
-        const int X1 = (X - d2) >> 7;
-        const int d1 = ((X1 + 64) & 127) - 64;
-        const int d0 = (X1 - d1) >> 7;
-        w0 |= (uint32_t)(d0 & 0xff) << (8 * j);
-        w1 |= (uint32_t)(d1 & 0xff) << (8 * j);
-        w2 |= (uint32_t)(d2 & 0xff) << (8 * j);
+        s_mul[m] = (e != kExpNonFinite) ? ldexpf(a.do_norm ? 1.0f / rms : 1.0f, e) : 0.0f;
+        s_e[m] = e;
       }
     }
-    const uint32_t wd[3] = {w0, w1, w2};
-#pragma unroll
-    for (int dg = 0; dg < 3; ++dg) {
-      const int c = 3 * m + dg;
-      const int tile = c >> 3, ln = (c & 7) * 4 + t;
-      xq[(((size_t)kb * 32 + ln) * nt + tile) * 2 + reg] = wd[dg];
-    }
+    if (blockIdx.x == 0 && a.amax_next && threadIdx.x < kMaxTokens) a.amax_next[threadIdx.x] = 0u;
+    __syncthreads();
+    if (blockIdx.x == 0 && threadIdx.x < a.M) a.xexp[threadIdx.x] = s_e[threadIdx.x];
+    encode_digits(sa, a.nt, kb0, kb1, s_mul, s_e,
+                  [&](int m, int k) { return load_act4(a.h, a.ld, a.d, m, k); },
+                  [&](size_t wi, uint32_t v) { xq[wi] = v; });
+    return;
   }
+  // no producer statistics: reduce over the whole vector here, capturing
+  // this CTA's slice in shared memory
+  token_stats(sa, red_ss, red_hw, &s_bad, s_mul, s_e, s_x, lo, hi);
+  if (blockIdx.x == 0 && threadIdx.x < a.M) a.xexp[threadIdx.x] = s_e[threadIdx.x];
+  const int span = hi - lo;
+  encode_digits(sa, a.nt, kb0, kb1, s_mul, s_e,
+                [&](int m, int k) {
+                  const float* p = s_x + m * span + (k - lo);
+                  float4 r;
+                  r.x = k < a.d ? p[0] : 0.0f;
+                  r.y = k + 1 < a.d ? p[1] : 0.0f;
+                  r.z = k + 2 < a.d ? p[2] : 0.0f;
+                  r.w = k + 3 < a.d ? p[3] : 0.0f;
+                  return r;
+                },
+                [&](size_t wi, uint32_t v) { xq[wi] = v; });
 }
 
 cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl) {
@@ -653,7 +812,7 @@ cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ctas);
   cfg.blockDim = dim3(kQuantThreads);
-  cfg.dynamicSmemBytes = (size_t)a.M * kbs * 32 * sizeof(float);
+  cfg.dynamicSmemBytes = a.use_stats ? 0 : (size_t)a.M * kbs * 32 * sizeof(float);
   if (cfg.dynamicSmemBytes > 48 * 1024) return cudaErrorInvalidConfiguration;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -671,9 +830,11 @@ cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl) {
 // 959-966); the softmax subtracts the row max (transformer.rs:985-1000).
 // Pages are combined by the last CTA of each KV head (flash-decoding split).
 constexpr int kAttnThreads = 256;
-constexpr int kAttnRowBlk = 8;  // query rows per thread in the score pass
 
-__global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
+// RB: query rows per thread (all of them valid: R is a multiple of the
+// number of row groups in both passes, checked by the launcher).
+template <int RB>
+__global__ void __launch_bounds__(kAttnThreads, 2) k_attention(AttnArgs a) {
   extern __shared__ float smem[];
   __shared__ float s_m[128], s_l[128];
   __shared__ int s_last;
@@ -683,6 +844,9 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
   const int G = a.H / a.Hkv;
   const int R = G * a.M;
   const int hdp = a.hdp, P = a.page;
+  // rows padded with zero queries to a multiple of both passes' row groups
+  const int rgmax = max(kAttnThreads / P, kAttnThreads / hdp);
+  const int Rp = (R + rgmax - 1) / rgmax * rgmax;
   const int pos0 = *a.pos_ptr + a.pos_add;
   const int L = pos0 + a.M;
   const int n_chunks = (L + P - 1) / P;
@@ -690,10 +854,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
   const int t0 = chunk * P;
   const int nt = min(P, L - t0);
   const int ks = hdp + 4;  // K row stride: float4-aligned, conflict-free float4 reads
-  float* sq = smem;                    // [R][hdp]
-  float* sk = sq + (size_t)R * hdp;    // [P][hdp+4]
+  float* sq = smem;                    // [Rp][hdp]
+  float* sk = sq + (size_t)Rp * hdp;   // [P][hdp+4]
   float* sv = sk + (size_t)P * ks;     // [P][hdp]
-  float* ss = sv + (size_t)P * hdp;    // [R][P]
+  float* ss = sv + (size_t)P * hdp;    // [Rp][P]
 
   const int pg = a.page_table[chunk];
   const float4* kbase = reinterpret_cast<const float4*>(a.kc + ((size_t)pg * a.Hkv + kvh) * P * hdp);
@@ -709,21 +873,24 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
       const int i = threadIdx.x + u * kAttnThreads;
       if (i < n4) { kr[u] = __ldcg(kbase + i); vr[u] = __ldcg(vbase + i); }
     }
-    constexpr int kMaxQ = 16;  // R * hdp / 4 / threads for R * hdp <= 16384
-    float4 qr[kMaxQ];
+    // q: four loads in flight per batch (the K/V loads above are already out)
+    for (int i0 = threadIdx.x; i0 < Rp * h4; i0 += 4 * kAttnThreads) {
+      float4 qr[4];
 #pragma unroll
-    for (int u = 0; u < kMaxQ; ++u) {
-      const int i = threadIdx.x + u * kAttnThreads;
-      if (i < R * h4) {
-        const int row = i / h4, c4 = i - row * h4;
-        const int m = row / G, gi = row - m * G;
-        qr[u] = __ldcg(reinterpret_cast<const float4*>(a.q + ((size_t)m * a.H + kvh * G + gi) * hdp) + c4);
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * kAttnThreads;
+        qr[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (i < R * h4) {
+          const int row = i / h4, c4 = i - row * h4;
+          const int m = row / G, gi = row - m * G;
+          qr[u] = __ldcg(reinterpret_cast<const float4*>(a.q + ((size_t)m * a.H + kvh * G + gi) * hdp) + c4);
+        }
       }
-    }
 #pragma unroll
-    for (int u = 0; u < kMaxQ; ++u) {
-      const int i = threadIdx.x + u * kAttnThreads;
-      if (i < R * h4) reinterpret_cast<float4*>(sq)[i] = qr[u];
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u * kAttnThreads;
+        if (i < Rp * h4) reinterpret_cast<float4*>(sq)[i] = qr[u];
+      }
     }
 #pragma unroll
     for (int u = 0; u < kMaxLd; ++u) {
@@ -734,47 +901,47 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
         reinterpret_cast<float4*>(sv)[i] = vr[u];
       }
     }
+    // the P.V pass steps 4 positions at a time: zero V rows past the last
+    // position (their probabilities are 0, and 0 * stale data could be NaN)
+    const int ntr = (nt + 3) & ~3;
+    for (int i = nt * h4 + threadIdx.x; i < ntr * h4; i += blockDim.x)
+      reinterpret_cast<float4*>(sv)[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   }
   __syncthreads();
-  // scores: thread -> position t, row group; rows r, r+rg, ... share each K load
+  // scores: thread -> position t and rows rq, rq+RG, ... (RB of them)
   {
     const int t = threadIdx.x % P;
-    const int rg = blockDim.x / P;
-    for (int r0 = threadIdx.x / P; r0 < R; r0 += rg * kAttnRowBlk) {
-      float acc[kAttnRowBlk];
+    const int RG = kAttnThreads / P;  // row groups
+    for (int rq = threadIdx.x / P; rq < Rp; rq += RG * RB) {
+      float acc[RB];
 #pragma unroll
-      for (int j = 0; j < kAttnRowBlk; ++j) acc[j] = 0.0f;
+      for (int j = 0; j < RB; ++j) acc[j] = 0.0f;
       if (t < nt) {
         const float* kr = sk + (size_t)t * ks;
         for (int c = 0; c < hdp; c += 4) {
           const float4 kv = *reinterpret_cast<const float4*>(kr + c);
 #pragma unroll
-          for (int j = 0; j < kAttnRowBlk; ++j) {
-            const int row = r0 + j * rg;
-            if (row < R) {
-              const float4 qv = *reinterpret_cast<const float4*>(sq + row * hdp + c);
-              acc[j] = __fmaf_rn(qv.x, kv.x, acc[j]);
-              acc[j] = __fmaf_rn(qv.y, kv.y, acc[j]);
-              acc[j] = __fmaf_rn(qv.z, kv.z, acc[j]);
-              acc[j] = __fmaf_rn(qv.w, kv.w, acc[j]);
-            }
+          for (int j = 0; j < RB; ++j) {
+            const float4 qv = *reinterpret_cast<const float4*>(sq + (rq + j * RG) * hdp + c);
+            acc[j] = __fmaf_rn(qv.x, kv.x, acc[j]);
+            acc[j] = __fmaf_rn(qv.y, kv.y, acc[j]);
+            acc[j] = __fmaf_rn(qv.z, kv.z, acc[j]);
+            acc[j] = __fmaf_rn(qv.w, kv.w, acc[j]);
           }
         }
       }
 #pragma unroll
-      for (int j = 0; j < kAttnRowBlk; ++j) {
-        const int row = r0 + j * rg;
-        if (row < R) {
-          const int m = row / G;
-          ss[row * P + t] = (t < nt && t0 + t <= pos0 + m) ? __fdiv_rn(acc[j], a.inv_scale_den)
-                                                            : -INFINITY;
-        }
+      for (int j = 0; j < RB; ++j) {
+        const int row = rq + j * RG;
+        const int m = min(row, R - 1) / G;
+        ss[row * P + t] = (t < nt && t0 + t <= pos0 + m) ? __fdiv_rn(acc[j], a.inv_scale_den)
+                                                          : -INFINITY;
       }
     }
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int row = warp; row < R; row += blockDim.x >> 5) {
+  for (int row = warp; row < Rp; row += blockDim.x >> 5) {
     float mx = -INFINITY;
     for (int t = lane; t < P; t += 32) mx = fmaxf(mx, ss[row * P + t]);
 #pragma unroll
@@ -791,29 +958,30 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
     if (lane == 0) { s_m[row] = mx; s_l[row] = sum; }
   }
   __syncthreads();
-  // P.V: thread -> column c, row group; rows share each V load
+  // P.V: thread -> column c and rows rq, rq+RG, ... ; four positions per step
   const size_t pbase = ((size_t)kvh * a.max_chunks + chunk) * R;
   {
     const int c = threadIdx.x % hdp;
-    const int rg = blockDim.x / hdp;
-    const int r_first = (threadIdx.x < rg * hdp) ? (int)(threadIdx.x / hdp) : R;
-    for (int r0 = r_first; r0 < R; r0 += rg * kAttnRowBlk) {
-      float acc[kAttnRowBlk];
+    const int RG = kAttnThreads / hdp;
+    for (int rq = threadIdx.x / hdp; rq < Rp; rq += RG * RB) {
+      float acc[RB];
 #pragma unroll
-      for (int j = 0; j < kAttnRowBlk; ++j) acc[j] = 0.0f;
-      for (int t = 0; t < nt; ++t) {
-        const float vv = sv[t * hdp + c];
+      for (int j = 0; j < RB; ++j) acc[j] = 0.0f;
+      for (int t = 0; t < nt; t += 4) {  // nt < P only on the last page: p == 0 there
+        const float v0 = sv[(t + 0) * hdp + c], v1 = sv[(t + 1) * hdp + c];
+        const float v2 = sv[(t + 2) * hdp + c], v3 = sv[(t + 3) * hdp + c];
 #pragma unroll
-        for (int j = 0; j < kAttnRowBlk; ++j) {
-          const int row = r0 + j * rg;
-          if (row < R) acc[j] = __fmaf_rn(ss[row * P + t], vv, acc[j]);
+        for (int j = 0; j < RB; ++j) {
+          const float4 p = *reinterpret_cast<const float4*>(ss + (rq + j * RG) * P + t);
+          acc[j] = __fmaf_rn(p.x, v0, acc[j]);
+          acc[j] = __fmaf_rn(p.y, v1, acc[j]);
+          acc[j] = __fmaf_rn(p.z, v2, acc[j]);
+          acc[j] = __fmaf_rn(p.w, v3, acc[j]);
         }
       }
 #pragma unroll
-      for (int j = 0; j < kAttnRowBlk; ++j) {
-        const int row = r0 + j * rg;
-        if (row < R) a.part_o[(pbase + row) * hdp + c] = acc[j];
-      }
+      for (int j = 0; j < RB; ++j)
+        if (rq + j * RG < R) a.part_o[(pbase + rq + j * RG) * hdp + c] = acc[j];
     }
   }
   for (int row = threadIdx.x; row < R; row += blockDim.x) {
@@ -854,34 +1022,35 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
   __syncthreads();
   {
     const int c = threadIdx.x % hdp;
-    const int rg = blockDim.x / hdp;
-    const int r_first = (threadIdx.x < rg * hdp) ? (int)(threadIdx.x / hdp) : R;
+    const int RG = kAttnThreads / hdp;
     const size_t cstride = (size_t)R * hdp;
-    for (int r0 = r_first; r0 < R; r0 += rg * kAttnRowBlk) {
-      float acc[kAttnRowBlk];
+    for (int rq = threadIdx.x / hdp; rq < Rp; rq += RG * RB) {
+      float acc[RB];
 #pragma unroll
-      for (int j = 0; j < kAttnRowBlk; ++j) acc[j] = 0.0f;
+      for (int j = 0; j < RB; ++j) acc[j] = 0.0f;
       const float* base = a.part_o + ((size_t)kvh * a.max_chunks * R) * hdp + c;
 #pragma unroll 4
       for (int ch = 0; ch < n_chunks; ++ch) {
-        float v[kAttnRowBlk];
+        float v[RB];
 #pragma unroll
-        for (int j = 0; j < kAttnRowBlk; ++j) {
-          const int row = r0 + j * rg;
-          v[j] = row < R ? __ldcg(base + ch * cstride + (size_t)row * hdp) : 0.0f;
+        for (int j = 0; j < RB; ++j) {
+          const int row = min(rq + j * RG, R - 1);
+          v[j] = __ldcg(base + ch * cstride + (size_t)row * hdp);
         }
 #pragma unroll
-        for (int j = 0; j < kAttnRowBlk; ++j) {
-          const int row = r0 + j * rg;
-          if (row < R) acc[j] = __fmaf_rn(v[j], wgt[row * n_chunks + ch], acc[j]);
+        for (int j = 0; j < RB; ++j) {
+          const int row = min(rq + j * RG, R - 1);
+          acc[j] = __fmaf_rn(v[j], wgt[row * n_chunks + ch], acc[j]);
         }
       }
 #pragma unroll
-      for (int j = 0; j < kAttnRowBlk; ++j) {
-        const int row = r0 + j * rg;
+      for (int j = 0; j < RB; ++j) {
+        const int row = rq + j * RG;
         if (row < R) {
           const int m = row / G, gi = row - m * G;
-          a.out[((size_t)m * a.H + kvh * G + gi) * hdp + c] = __fdiv_rn(acc[j], s_l[row]);
+          const float o = __fdiv_rn(acc[j], s_l[row]);
+          a.out[((size_t)m * a.H + kvh * G + gi) * hdp + c] = o;
+          if (a.st_amax) atomicMax(a.st_amax + m, __float_as_uint(fabsf(o)));
         }
       }
     }
@@ -890,16 +1059,31 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(AttnArgs a) {
 }
 
 size_t attention_smem_bytes(int G, int M, int hdp, int page) {
-  const size_t R = (size_t)G * M;
+  const int rgmax = std::max(kAttnThreads / page, kAttnThreads / hdp);
+  const size_t R = (size_t)((G * M + rgmax - 1) / rgmax * rgmax);
   return (R * hdp + (size_t)page * (hdp + 4) + (size_t)page * hdp + R * page) * sizeof(float);
+}
+
+// Rows per thread for both passes: the score pass has threads/P row groups
+// and the P.V pass threads/hdp; RB must divide R / groups in both.
+static int attention_rb(int R, int hdp, int page) {
+  const int g1 = kAttnThreads / page, g2 = kAttnThreads / hdp;
+  for (int rb : {8, 4, 2, 1})
+    if (R % (g1 * rb) == 0 && R % (g2 * rb) == 0) return rb;
+  return 0;
 }
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
   const int G = a.H / a.Hkv;
   const int R = G * a.M;
-  if (R > 128 || a.page != 64 || a.max_chunks > a.page || a.hdp > 128 || (a.hdp & 3) ||
-      (size_t)R * a.max_chunks * 2 > (size_t)a.page * (a.hdp + 4) || R * a.hdp > 16 * 4 * kAttnThreads)
+  if (a.page != 64 || a.max_chunks > a.page || a.hdp > 128 || (a.hdp & 3) ||
+      (kAttnThreads % a.hdp) || (size_t)R * a.max_chunks * 2 > (size_t)a.page * (a.hdp + 4))
     return cudaErrorInvalidValue;
+  const int rgmax = std::max(kAttnThreads / a.page, kAttnThreads / a.hdp);
+  const int Rp = (R + rgmax - 1) / rgmax * rgmax;
+  if (Rp > 128) return cudaErrorInvalidValue;
+  const int rb = attention_rb(Rp, a.hdp, a.page);
+  if (rb == 0) return cudaErrorInvalidValue;
   const size_t smem = attention_smem_bytes(G, a.M, a.hdp, a.page);
   if (smem > (size_t)g_attn_smem) return cudaErrorInvalidConfiguration;
   cudaLaunchConfig_t cfg = {};
@@ -912,7 +1096,12 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_attention, a);
+  switch (rb) {
+    case 8: return cudaLaunchKernelEx(&cfg, k_attention<8>, a);
+    case 4: return cudaLaunchKernelEx(&cfg, k_attention<4>, a);
+    case 2: return cudaLaunchKernelEx(&cfg, k_attention<2>, a);
+    default: return cudaLaunchKernelEx(&cfg, k_attention<1>, a);
+  }
 }
 
 // Raise the dynamic shared-memory limit once, outside any stream capture.
@@ -920,9 +1109,11 @@ cudaError_t prepare_kernels(size_t quant_smem, size_t attn_smem) {
   (void)quant_smem;
 
   if (attn_smem > (size_t)g_attn_smem) {
-    cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)attn_smem);
-    if (e != cudaSuccess) return e;
+    for (auto f : {k_attention<8>, k_attention<4>, k_attention<2>, k_attention<1>}) {
+      cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)attn_smem);
+      if (e != cudaSuccess) return e;
+    }
     g_attn_smem = (int)attn_smem;
   }
   return cudaSuccess;
@@ -942,15 +1133,39 @@ __global__ void __launch_bounds__(256) k_embed(EmbedArgs a) {
   }
   if (a.ids_out && threadIdx.x == 0) a.ids_out[m] = id;
   float* h = a.h + (size_t)m * a.d;
-  if (id < (uint32_t)a.vocab) {
-    const int8_t* q = a.emb_q + (size_t)id * a.d;
-    const float sc = a.emb_scale[id];
-    for (int i = threadIdx.x; i < a.d; i += blockDim.x) h[i] = __fmul_rn((float)q[i], sc);
-  } else {
-    for (int i = threadIdx.x; i < a.d; i += blockDim.x) h[i] = 0.0f;
+  float ss = 0.0f;
+  uint32_t mx = 0u;  // max|h*w| as float bits (NaN/inf win)
+  const bool in = id < (uint32_t)a.vocab;
+  const int8_t* q = in ? a.emb_q + (size_t)id * a.d : nullptr;
+  const float sc = in ? a.emb_scale[id] : 0.0f;
+  for (int i = threadIdx.x; i < a.d; i += blockDim.x) {
+    const float v = in ? __fmul_rn((float)q[i], sc) : 0.0f;
+    h[i] = v;
+    ss = __fadd_rn(ss, __fmul_rn(v, v));
+    mx = max(mx, __float_as_uint(fabsf(__fmul_rn(v, a.st_w ? a.st_w[i] : 1.0f))));
   }
   if (m == 0)
     for (int i = threadIdx.x; i < a.n_zero; i += blockDim.x) a.zero_keys[i] = 0ull;
+  if (m == 0)
+    for (int i = threadIdx.x; i < a.n_st_zero; i += blockDim.x) a.st_zero[i] = 0u;
+  if (a.st_amax) {
+    __shared__ float rs[8];
+    __shared__ uint32_t rm[8];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    if ((threadIdx.x & 31) == 0) { rs[threadIdx.x >> 5] = ss; rm[threadIdx.x >> 5] = mx; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.0f;
+      uint32_t u = 0u;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { t = __fadd_rn(t, rs[w]); u = max(u, rm[w]); }
+      a.st_pss[(size_t)m * a.st_np] = t;
+      a.st_amax[m] = u;
+    }
+  }
 }
 
 cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t s, bool pdl) {
