@@ -184,6 +184,32 @@ MC_API mc_status mc_linear_run(mc_linear* l, const float* x_dev, int32_t m,
                         float* y_dev, void* stream);
 MC_API int64_t mc_linear_weight_bytes(const mc_linear* l);
 
+/* Allocation-free variant of mc_linear_run.  It has no counterpart in the
+ * reference, which has no device path at all.  Same arguments, kernels and
+ * results as mc_linear_run, but the activation scratch (the packed digit
+ * operand and the per-token exponents) lives in one fixed device array
+ * compiled into this library, 768 KiB + 256 B per device, instead of in
+ * buffers owned by the handle, and the call itself allocates no device or
+ * host memory.
+ *
+ * It exists for callers that may allocate at start-up (mc_linear_create
+ * packs the weights then) but not when they run a projection. One example
+ * is a serving process whose HBM is already divided between weights and KV
+ * pages under a hard budget, where a new allocation can fail or fragment
+ * the pool. Another is a latency-critical decode loop sharing the GPU with
+ * other streams, where cudaMalloc/cudaFree may synchronise the whole device
+ * and stall them.
+ *
+ * Limit: in_features <= 16384; a larger matrix returns MC_E_CAPACITY and
+ * launches nothing.  The first call on each device does the set-up (looks
+ * up the array's device address and clears it once), so make that first
+ * call before any stream capture.  All calls on one device share the array:
+ * calls that overlap in time (different streams or threads with no ordering
+ * between them) race on it and corrupt each other's results; issue them on
+ * one stream or synchronise between them. */
+MC_API mc_status mc_linear_run_static(mc_linear* l, const float* x_dev, int32_t m,
+                               float* y_dev, void* stream);
+
 MC_API size_t mc_last_error(char* buf, size_t cap);
 MC_API const char* mc_version(void);
 

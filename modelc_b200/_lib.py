@@ -26,7 +26,7 @@ EXPORTS = [
     "mc_draft", "mc_speculative_generate", "mc_spec_prime", "mc_spec_decode", "mc_spec_read",
     "mc_linear_create", "mc_linear_destroy", "mc_linear_run", "mc_linear_weight_bytes",
     "mc_last_error", "mc_version", "mc_spec_rewind", "mc_spec_verify_launch",
-    "mc_session_stream", "mc_session_round_launches",
+    "mc_session_stream", "mc_session_round_launches", "mc_linear_run_static",
 ]
 
 
@@ -89,6 +89,7 @@ def lib():
         "mc_linear_destroy": (i32, [vp]),
         "mc_linear_run": (i32, [vp, vp, i32, vp, vp]),
         "mc_linear_weight_bytes": (i64, [vp]),
+        "mc_linear_run_static": (i32, [vp, vp, i32, vp, vp]),
         "mc_last_error": (C.c_size_t, [C.c_char_p, C.c_size_t]),
         "mc_spec_rewind": (i32, [vp]),
         "mc_spec_verify_launch": (i32, [vp, i32]),

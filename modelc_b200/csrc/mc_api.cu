@@ -7,6 +7,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1352,6 +1353,90 @@ extern "C" mc_status mc_linear_run(mc_linear* l, const float* x_dev, int32_t m, 
     const int nt = nt_for_tokens(M);
     if (!l->bps[nt]) l->bps[nt] = std::max(1, gemv_blocks_per_sm(EPI_STORE, nt));
     CK(launch_gemv(a, EPI_STORE, nt, std::min(l->m.n_stripes, l->nsm * l->bps[nt]), s, true));
+  }
+  return MC_OK;
+}
+
+// ------------------------------------------------ allocation-free projection
+// mc_linear_run_static: the encoder + GEMV pair of mc_linear_run with its
+// activation scratch in one module-scope device array instead of buffers the
+// handle owns.  Layout: packed digit words (48 bytes per input column: up to
+// 6 n8 tiles x 8 columns, one byte each) then kMaxTokens int exponents.
+constexpr int kStaticMaxK = 16384;
+constexpr size_t kStaticXqBytes = (size_t)kStaticMaxK * 48;  // 768 KiB
+constexpr size_t kStaticBytes = kStaticXqBytes + 256;        // + exponents
+static_assert(kMaxTokens * sizeof(int) <= 256, "exponent slot too small");
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticBytes];
+
+constexpr int kStaticMaxDevices = 64;
+static std::mutex g_static_mu;
+static unsigned char* g_static_ptr[kStaticMaxDevices];
+
+// Set-up, once per device, with that device current: the array's device
+// address, and one clear of the whole array.  Afterwards nothing has to be
+// zero at the start of a call: every call's encoder rewrites all digit words
+// the GEMV reads (padding columns of the last n8 tile included) and the
+// exponents of its tokens.
+static mc_status static_scratch(int dev, unsigned char** out) {
+  if (dev < 0 || dev >= kStaticMaxDevices)
+    return set_err(MC_E_INVALID, "device %d outside [0, %d)", dev, kStaticMaxDevices);
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_ptr[dev]) {
+    unsigned char* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress((void**)&ptr, g_static_scratch);
+    if (e != cudaSuccess || !ptr)
+      return set_err(MC_E_CUDA, "static scratch address on device %d: %s", dev,
+                     cudaGetErrorString(e));
+    e = cudaMemset(ptr, 0, kStaticBytes);
+    if (e != cudaSuccess)
+      return set_err(MC_E_CUDA, "static scratch clear on device %d: %s", dev,
+                     cudaGetErrorString(e));
+    g_static_ptr[dev] = ptr;
+  }
+  *out = g_static_ptr[dev];
+  return MC_OK;
+}
+
+extern "C" mc_status mc_linear_run_static(mc_linear* l, const float* x_dev, int32_t m,
+                                          float* y_dev, void* stream) {
+  if (!l || (!x_dev && m > 0) || (!y_dev && m > 0) || m < 0)
+    return set_err(MC_E_INVALID, "bad arguments");
+  if (l->m.K > kStaticMaxK)
+    return set_err(MC_E_CAPACITY,
+                   "mc_linear_run_static: in_features %d exceeds the static scratch limit %d "
+                   "(use mc_linear_run)", l->m.K, kStaticMaxK);
+  CK(cudaSetDevice(l->dev));
+  unsigned char* scratch = nullptr;
+  CKS(static_scratch(l->dev, &scratch));
+  uint8_t* xq = scratch;
+  int* xexp = reinterpret_cast<int*>(scratch + kStaticXqBytes);
+  cudaStream_t s = (cudaStream_t)stream;
+  for (int r0 = 0; r0 < m; r0 += kMaxTokens) {
+    const int M = std::min(kMaxTokens, m - r0);
+    const int nt = nt_for_tokens(M);
+    QuantArgs q{};
+    q.h = x_dev + (size_t)r0 * l->m.K;
+    q.ld = l->m.K;
+    q.d = l->m.K;
+    q.M = M;
+    q.xq = xq;
+    q.KB = l->m.KB;
+    q.nt = nt;
+    q.xexp = xexp;
+    CK(launch_quant(q, s, true));
+    GemvArgs a{};
+    a.w = l->m.w;
+    a.scale = l->m.scale;
+    a.x = xq;
+    a.xexp = xexp;
+    a.KB = l->m.KB;
+    a.n_stripes = l->m.n_stripes;
+    a.M = M;
+    a.out = y_dev + (size_t)r0 * l->m.N;
+    a.ldo = l->m.N;
+    a.n_out = l->m.N;
+    const int bps = l->bps[nt] ? l->bps[nt] : 1;
+    CK(launch_gemv(a, EPI_STORE, nt, std::min(l->m.n_stripes, l->nsm * bps), s, true));
   }
   return MC_OK;
 }
