@@ -1019,41 +1019,71 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attention(AttnArgs a) {
     }
     s_l[row] = l;
   }
+  __shared__ uint32_t s_mx[kMaxTokens];  // max |out| per token, float bits
+  if (threadIdx.x < kMaxTokens) s_mx[threadIdx.x] = 0u;
   __syncthreads();
   {
-    const int c = threadIdx.x % hdp;
-    const int RG = kAttnThreads / hdp;
-    const size_t cstride = (size_t)R * hdp;
-    for (int rq = threadIdx.x / hdp; rq < Rp; rq += RG * RB) {
-      float acc[RB];
+    // thread -> 4 columns of one row; pages summed in order with eight
+    // float4 loads in flight.  Rp is a multiple of the rows a warp spans, so
+    // the row loop and the shuffles below are warp-uniform.
+    const int h4 = hdp >> 2;
+    const int RGc = kAttnThreads / h4;
+    const int c4 = threadIdx.x % h4;
+    const int seg = min(h4, 32);  // lanes of a warp that share a row
+    const float4* base =
+        reinterpret_cast<const float4*>(a.part_o) + (size_t)kvh * a.max_chunks * R * h4 + c4;
+    const size_t cs4 = (size_t)R * h4;
+    for (int row = threadIdx.x / h4; row < Rp; row += RGc) {
+      const bool live = row < R;
+      const int rr = live ? row : R - 1;
+      const float* wr = wgt + rr * n_chunks;
+      const float4* src = base + (size_t)rr * h4;
+      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      int ch = 0;
+      for (; ch + 8 <= n_chunks; ch += 8) {
+        float4 v[8];
 #pragma unroll
-      for (int j = 0; j < RB; ++j) acc[j] = 0.0f;
-      const float* base = a.part_o + ((size_t)kvh * a.max_chunks * R) * hdp + c;
-#pragma unroll 4
-      for (int ch = 0; ch < n_chunks; ++ch) {
-        float v[RB];
+        for (int u = 0; u < 8; ++u) v[u] = __ldcg(src + (size_t)(ch + u) * cs4);
 #pragma unroll
-        for (int j = 0; j < RB; ++j) {
-          const int row = min(rq + j * RG, R - 1);
-          v[j] = __ldcg(base + ch * cstride + (size_t)row * hdp);
-        }
-#pragma unroll
-        for (int j = 0; j < RB; ++j) {
-          const int row = min(rq + j * RG, R - 1);
-          acc[j] = __fmaf_rn(v[j], wgt[row * n_chunks + ch], acc[j]);
+        for (int u = 0; u < 8; ++u) {
+          const float w = wr[ch + u];
+          acc.x = __fmaf_rn(v[u].x, w, acc.x);
+          acc.y = __fmaf_rn(v[u].y, w, acc.y);
+          acc.z = __fmaf_rn(v[u].z, w, acc.z);
+          acc.w = __fmaf_rn(v[u].w, w, acc.w);
         }
       }
-#pragma unroll
-      for (int j = 0; j < RB; ++j) {
-        const int row = rq + j * RG;
-        if (row < R) {
-          const int m = row / G, gi = row - m * G;
-          const float o = __fdiv_rn(acc[j], s_l[row]);
-          a.out[((size_t)m * a.H + kvh * G + gi) * hdp + c] = o;
-          if (a.st_amax) atomicMax(a.st_amax + m, __float_as_uint(fabsf(o)));
-        }
+      for (; ch < n_chunks; ++ch) {
+        const float4 v = __ldcg(src + (size_t)ch * cs4);
+        const float w = wr[ch];
+        acc.x = __fmaf_rn(v.x, w, acc.x);
+        acc.y = __fmaf_rn(v.y, w, acc.y);
+        acc.z = __fmaf_rn(v.z, w, acc.z);
+        acc.w = __fmaf_rn(v.w, w, acc.w);
+      }
+      uint32_t bits = 0u;
+      if (live) {
+        const float l = s_l[row];
+        float4 o;
+        o.x = __fdiv_rn(acc.x, l);
+        o.y = __fdiv_rn(acc.y, l);
+        o.z = __fdiv_rn(acc.z, l);
+        o.w = __fdiv_rn(acc.w, l);
+        const int m = row / G, gi = row - m * G;
+        reinterpret_cast<float4*>(a.out + ((size_t)m * a.H + kvh * G + gi) * hdp)[c4] = o;
+        bits = max(max(__float_as_uint(fabsf(o.x)), __float_as_uint(fabsf(o.y))),
+                   max(__float_as_uint(fabsf(o.z)), __float_as_uint(fabsf(o.w))));
+      }
+      if (a.st_amax) {
+        for (int off = 1; off < seg; off <<= 1)
+          bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, off));
+        if (live && (threadIdx.x % seg) == 0) atomicMax(s_mx + row / G, bits);
       }
     }
+  }
+  if (a.st_amax) {
+    __syncthreads();
+    if (threadIdx.x < a.M) atomicMax(a.st_amax + threadIdx.x, s_mx[threadIdx.x]);
   }
   if (threadIdx.x == 0) atomicExch(a.cnt + kvh, 0);
 }
