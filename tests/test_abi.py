@@ -38,10 +38,9 @@ def test_version_string():
     assert b"sm_100a" in mb.lib().mc_version()
 
 
-def test_library_is_sm100a_only():
-    # the fat binary carries sm_100a SASS only (cuobjdump lists the ELF arch)
-    out = subprocess.run(["strings", _lib.LIB_PATH], capture_output=True, text=True).stdout
-    assert "sm_100a" in out
+def test_library_is_built_for_sm100a_only():
+    from modelc_b200 import build
+    assert build.ARCH == ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
 def _has_gpu():
