@@ -101,16 +101,21 @@ static inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
 struct PMat {
   int N = 0, K = 0;  // logical rows / cols
   int n_stripes = 0, KB = 0;
+  int fmt = WF_I8;
   int4* w = nullptr;
-  float* scale = nullptr;
-  long long algo_bytes = 0;  // int8 codes + f32 row scales actually used
+  float* scale = nullptr;      // WF_I8 row scales
+  uint32_t* qscale = nullptr;  // WF_Q4 block scales
+  long long algo_bytes = 0;  // codes + scales actually used
 };
 
-// Source matrix staged on the device as int8 [rows][cols] + f32 scales.
+// Source matrix staged on the device: int8 [rows][cols] + f32 row scales, or
+// q4_0 blocks [rows][cols/32][18] (fmt WF_Q4).
 struct SrcI8 {
   int rows = 0, cols = 0;
+  int fmt = WF_I8;
   int8_t* q = nullptr;
   float* s = nullptr;
+  uint8_t* q4 = nullptr;
   std::vector<void*> tmp;
   ~SrcI8() {
     for (void* p : tmp) cudaFree(p);
@@ -148,6 +153,21 @@ static mc_status stage_matrix(const mc_tensor_desc* t, SrcI8* out) {
   out->rows = rows;
   out->cols = cols;
   const size_t n = (size_t)rows * cols;
+  if (t->dtype == MC_DTYPE_Q4_0) {
+    // blocks run along each row (dequant.rs:33-44 is flat over elements, so a
+    // row that is not a whole number of blocks would share a block)
+    if (cols % 32)
+      return set_err(MC_E_SHAPE, "%s: q4_0 needs in_features %% 32 == 0 (got %d)", t->name, cols);
+    const size_t bytes = n / 32 * kQ4BlockBytes;
+    void* q4 = nullptr;
+    CK(cudaMalloc(&q4, std::max<size_t>(bytes, 16)));
+    out->tmp.push_back(q4);
+    out->q4 = (uint8_t*)q4;
+    out->fmt = WF_Q4;
+    CK(cudaMemcpy(q4, t->data, bytes,
+                  t->location == MC_MEM_DEVICE ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+    return MC_OK;
+  }
   void* q = nullptr;
   void* s = nullptr;
   CK(cudaMalloc(&q, std::max<size_t>(n, 16)));
@@ -227,10 +247,27 @@ static mc_status concat_rows(const std::vector<const SrcI8*>& parts, SrcI8* out)
   const int cols = parts[0]->cols;
   for (auto* p : parts) {
     if (p->cols != cols) return set_err(MC_E_SHAPE, "fused projections disagree on input width");
+    if (p->fmt != parts[0]->fmt)
+      return set_err(MC_E_DTYPE, "fused projections (q/k/v or gate/up) must share one dtype");
     rows += p->rows;
   }
   out->rows = rows;
   out->cols = cols;
+  if (parts[0]->fmt == WF_Q4) {
+    const size_t row_bytes = (size_t)cols / 32 * kQ4BlockBytes;
+    void* q4 = nullptr;
+    CK(cudaMalloc(&q4, std::max<size_t>((size_t)rows * row_bytes, 16)));
+    out->tmp.push_back(q4);
+    out->q4 = (uint8_t*)q4;
+    out->fmt = WF_Q4;
+    size_t r0 = 0;
+    for (auto* p : parts) {
+      CK(cudaMemcpy(out->q4 + r0 * row_bytes, p->q4, (size_t)p->rows * row_bytes,
+                    cudaMemcpyDeviceToDevice));
+      r0 += p->rows;
+    }
+    return MC_OK;
+  }
   void* q = nullptr;
   void* s = nullptr;
   CK(cudaMalloc(&q, std::max<size_t>((size_t)rows * cols, 16)));
@@ -257,6 +294,28 @@ static mc_status pack_matrix(const SrcI8& src, const std::vector<int>& row_map,
   out->N = n_real_rows;
   out->K = n_real_cols;
   out->algo_bytes = (long long)n_real_rows * n_real_cols + 4ll * n_real_rows;
+  if (src.fmt == WF_Q4) {
+    // q4_0 keeps its blocks: columns can only be taken in place
+    for (size_t c = 0; c < col_map.size(); ++c)
+      if (col_map[c] != (c < (size_t)src.cols ? (int)c : -1) || (int)col_map.size() != src.cols)
+        return set_err(MC_E_SHAPE,
+                       "q4_0 matrix %dx%d cannot be re-laid-out (head_dim must be a "
+                       "multiple of 16 for q4_0 attention weights)", src.rows, src.cols);
+    out->fmt = WF_Q4;
+    out->algo_bytes = (long long)n_real_rows * n_real_cols / 32 * kQ4BlockBytes;
+    const size_t units = (size_t)out->n_stripes * out->KB * 32;
+    CKS(al.alloc(&out->w, units / 2));  // 8 bytes per unit (int4 = 16 bytes)
+    CKS(al.alloc(&out->qscale, (size_t)out->n_stripes * out->KB * 8));
+    int* drm = nullptr;
+    CK(cudaMalloc(&drm, row_map.size() * 4));
+    cudaMemcpy(drm, row_map.data(), row_map.size() * 4, cudaMemcpyHostToDevice);
+    cudaError_t e = launch_pack_q4(src.q4, drm, out->n_stripes, out->KB,
+                                   reinterpret_cast<uint2*>(out->w), out->qscale, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaFree(drm);
+    if (e != cudaSuccess) return set_err(MC_E_CUDA, "q4_0 packing failed: %s", cudaGetErrorString(e));
+    return MC_OK;
+  }
   CKS(al.alloc(&out->w, (size_t)out->n_stripes * out->KB * 32));
   CKS(al.alloc(&out->scale, (size_t)out->n_stripes * 16));
   int* drm = nullptr;
@@ -299,6 +358,7 @@ struct mc_weights {
   bool has_head = false;
   int8_t* emb_q = nullptr;
   float* emb_scale = nullptr;
+  uint8_t* emb_q4 = nullptr;  // q4_0 embedding blocks (emb_q unused then)
   Allocs al;
   long long algo_bytes_per_forward = 0;  // streamed weight bytes of one forward
 };
@@ -361,7 +421,15 @@ static mc_status load_model(const mc_tensor_desc* ts, size_t n, const mc_model_c
   // embedding (row-major int8 for the gather)
   const mc_tensor_desc* te = find_t(ts, n, "model.embed_tokens.weight");
   SrcI8 emb;
-  if (te) {
+  if (te && te->dtype == MC_DTYPE_Q4_0) {
+    CKS(stage_matrix(te, &emb));
+    if (emb.rows != W->V || emb.cols != d)
+      return set_err(MC_E_SHAPE, "embed_tokens is %dx%d, expected %dx%d", emb.rows, emb.cols,
+                     W->V, d);
+    const size_t bytes = (size_t)W->V * (d / 32) * kQ4BlockBytes;
+    CKS(al.alloc(&W->emb_q4, bytes));
+    CK(cudaMemcpy(W->emb_q4, emb.q4, bytes, cudaMemcpyDeviceToDevice));
+  } else if (te) {
     CKS(stage_matrix(te, &emb));
     if (emb.rows != W->V || emb.cols != d)
       return set_err(MC_E_SHAPE, "embed_tokens is %dx%d, expected %dx%d", emb.rows, emb.cols,
@@ -439,7 +507,8 @@ static mc_status load_model(const mc_tensor_desc* ts, size_t n, const mc_model_c
       }
       CKS(pack_matrix(cat, rm, identity_map(d, round_up(d, 32)), (H + 2 * Hkv) * hd, d, al,
                       &Lw.qkv));
-      Lw.qkv.algo_bytes = (long long)(H + 2 * Hkv) * hd * d + 4ll * (H + 2 * Hkv) * hd;
+      if (Lw.qkv.fmt == WF_I8)  // padded head rows are not algorithmic bytes
+        Lw.qkv.algo_bytes = (long long)(H + 2 * Hkv) * hd * d + 4ll * (H + 2 * Hkv) * hd;
       // O projection: columns follow the padded head layout of the attention output
       std::vector<int> cm(round_up(H * hdp, 32), -1);
       for (int hh = 0; hh < H; ++hh)
@@ -582,12 +651,24 @@ struct mc_session {
   cudaGraphExec_t round_exec = nullptr;
   cudaGraphExec_t verify_exec = nullptr;
   int round_launches = 0;
-  int bps[5][7] = {};
+  int bps[2][5][7] = {};
 };
 
-static int bps_of(mc_session* s, int epi, int nt) {
-  if (!s->bps[epi][nt]) s->bps[epi][nt] = std::max(1, gemv_blocks_per_sm(epi, nt));
-  return s->bps[epi][nt];
+static int bps_of(mc_session* s, int epi, int nt, int wf) {
+  int& b = s->bps[wf][epi][nt];
+  if (!b) b = std::max(1, gemv_blocks_per_sm(epi, nt, wf));
+  return b;
+}
+
+// CTAs per GEMV launch.  q4_0 partial sums are f32 and the grid sets their
+// k-split, so a q4_0 grid must not depend on the token count: it uses the
+// smallest occupancy over all token tiles.
+template <class BpsFn>
+static int gemv_grid(const PMat& W, int nsm, int nt, BpsFn bps) {
+  int b = bps(nt);
+  if (W.fmt == WF_Q4)
+    for (int t : {1, 2, 3, 6}) b = std::min(b, bps(t));
+  return std::min(W.n_stripes, nsm * std::max(b, 1));
 }
 
 static mc_status alloc_kv(mc_session* s, const mc_weights* W, KVSet* kv) {
@@ -695,8 +776,9 @@ static mc_status session_alloc(mc_session* s) {
     asm_ = std::max(asm_, attention_smem_bytes(W->H / W->Hkv, kChunk, W->hdp, kPage));
   }
   CK(prepare_kernels(qsm, asm_));
-  for (int epi = 0; epi < 5; ++epi)
-    for (int nt : {1, 2, 3, 6}) bps_of(s, epi, nt);
+  for (int wf : {(int)WF_I8, (int)WF_Q4})
+    for (int epi = 0; epi < 5; ++epi)
+      for (int nt : {1, 2, 3, 6}) bps_of(s, epi, nt, wf);
   CKS(s->al.alloc(&s->st, 1));
   CK(cudaMemset(s->st, 0, sizeof(SpecState)));
   CKS(s->al.alloc(&s->ctx, (size_t)s->cap + 8));
@@ -807,11 +889,14 @@ static mc_status enq_gemv(mc_session* s, const PMat& W, int epi, int M, GemvArgs
                           const PMat* next = nullptr) {
   if (next && next->w) {
     a.next_w = next->w;
-    a.next_bytes = (long long)next->n_stripes * next->KB * kFragBytes;
+    // packed code bytes of the next matrix (q4_0: 256 per stripe k-block)
+    a.next_bytes = (long long)next->n_stripes * next->KB * (next->fmt == WF_Q4 ? kFragBytes / 2
+                                                                               : kFragBytes);
     a.next_pf_bytes = std::min(a.next_bytes, kNextPrefetch);
   }
   a.w = W.w;
   a.scale = W.scale;
+  a.qscale = W.qscale;
   a.x = s->xq;
   a.xexp = s->xexp;
   a.KB = W.KB;
@@ -821,8 +906,8 @@ static mc_status enq_gemv(mc_session* s, const PMat& W, int epi, int M, GemvArgs
   a.cnt = s->cnt;
   a.err = s->err;
   const int nt = nt_for_tokens(M);
-  const int grid = std::min(W.n_stripes, s->nsm * bps_of(s, epi, nt));
-  CK(launch_gemv(a, epi, nt, grid, s->stream, true));
+  const int grid = gemv_grid(W, s->nsm, nt, [&](int t) { return bps_of(s, epi, t, W.fmt); });
+  CK(launch_gemv(a, epi, nt, W.fmt, grid, s->stream, true));
   return MC_OK;
 }
 
@@ -834,6 +919,7 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
   if (!W->has_head) return set_err(MC_E_NO_HEAD, "model has no lm_head and no embedding");
   ea.emb_q = W->emb_q;
   ea.emb_scale = W->emb_scale;
+  ea.emb_q4 = W->emb_q4;
   ea.d = W->d;
   ea.vocab = W->V;
   ea.M = M;
@@ -1268,8 +1354,16 @@ struct mc_linear {
   int* cnt = nullptr;
   int* err = nullptr;
   int nsm = 0;
-  int bps[7] = {};
+  int bps[2][7] = {};
 };
+
+static int linear_grid(mc_linear* l, int nt) {
+  return gemv_grid(l->m, l->nsm, nt, [&](int t) {
+    int& b = l->bps[l->m.fmt][t];
+    if (!b) b = std::max(1, gemv_blocks_per_sm(EPI_STORE, t, l->m.fmt));
+    return b;
+  });
+}
 
 extern "C" mc_status mc_linear_create(const mc_tensor_desc* w, int32_t device, mc_linear** out) {
   if (!w || !out) return set_err(MC_E_INVALID, "null argument");
@@ -1298,7 +1392,8 @@ extern "C" mc_status mc_linear_create(const mc_tensor_desc* w, int32_t device, m
     st = set_err(MC_E_CUDA, "memset failed");
   cudaDeviceGetAttribute(&L->nsm, cudaDevAttrMultiProcessorCount, device);
   if (st == MC_OK)
-    for (int nt : {1, 2, 3, 6}) L->bps[nt] = std::max(1, gemv_blocks_per_sm(EPI_STORE, nt));
+    for (int nt : {1, 2, 3, 6})
+      L->bps[L->m.fmt][nt] = std::max(1, gemv_blocks_per_sm(EPI_STORE, nt, L->m.fmt));
   if (st != MC_OK) {
     L->al.free_all();
     delete L;
@@ -1339,6 +1434,7 @@ extern "C" mc_status mc_linear_run(mc_linear* l, const float* x_dev, int32_t m, 
     GemvArgs a{};
     a.w = l->m.w;
     a.scale = l->m.scale;
+    a.qscale = l->m.qscale;
     a.x = l->xq;
     a.xexp = l->xexp;
     a.KB = l->m.KB;
@@ -1351,8 +1447,7 @@ extern "C" mc_status mc_linear_run(mc_linear* l, const float* x_dev, int32_t m, 
     a.ldo = l->m.N;
     a.n_out = l->m.N;
     const int nt = nt_for_tokens(M);
-    if (!l->bps[nt]) l->bps[nt] = std::max(1, gemv_blocks_per_sm(EPI_STORE, nt));
-    CK(launch_gemv(a, EPI_STORE, nt, std::min(l->m.n_stripes, l->nsm * l->bps[nt]), s, true));
+    CK(launch_gemv(a, EPI_STORE, nt, l->m.fmt, linear_grid(l, nt), s, true));
   }
   return MC_OK;
 }
@@ -1427,6 +1522,7 @@ extern "C" mc_status mc_linear_run_static(mc_linear* l, const float* x_dev, int3
     GemvArgs a{};
     a.w = l->m.w;
     a.scale = l->m.scale;
+    a.qscale = l->m.qscale;
     a.x = xq;
     a.xexp = xexp;
     a.KB = l->m.KB;
@@ -1435,8 +1531,7 @@ extern "C" mc_status mc_linear_run_static(mc_linear* l, const float* x_dev, int3
     a.out = y_dev + (size_t)r0 * l->m.N;
     a.ldo = l->m.N;
     a.n_out = l->m.N;
-    const int bps = l->bps[nt] ? l->bps[nt] : 1;
-    CK(launch_gemv(a, EPI_STORE, nt, std::min(l->m.n_stripes, l->nsm * bps), s, true));
+    CK(launch_gemv(a, EPI_STORE, nt, l->m.fmt, linear_grid(l, nt), s, true));
   }
   return MC_OK;
 }

@@ -42,6 +42,19 @@ __host__ __device__ inline int nt_for_tokens(int m) {
   return nt;  // 1, 2, 3 or 6
 }
 
+// Packed weight formats.
+//   WF_I8: per (stripe, k-block) 512 bytes, one 16-byte A fragment per lane,
+//          plus one f32 scale per packed row.
+//   WF_Q4: ggml q4_0 (32-weight blocks along K with one fp16 scale,
+//          parsers/gguf/dequant.rs:23-46).  Per (stripe, k-block) 256 bytes,
+//          8 per lane: word 0 byte b holds the nibbles of A registers a0
+//          (low) and a1 (high) byte b, word 1 those of a2 and a3, so
+//          (w & 0x0F0F0F0F) and ((w >> 4) & 0x0F0F0F0F) are the unsigned
+//          codes.  Block scales: one u32 per (stripe, k-block, g) holding
+//          the fp16 scales of rows g (low half) and g + 8.
+enum WFmt : int { WF_I8 = 0, WF_Q4 = 1 };
+constexpr int kQ4BlockBytes = 18;  // fp16 scale + 16 bytes of nibbles
+
 // Epilogue kinds of the quantized GEMV.
 enum Epi : int {
   EPI_STORE = 0,   // out[m][row] = y
@@ -52,8 +65,9 @@ enum Epi : int {
 };
 
 struct GemvArgs {
-  const int4* w;         // packed weights
-  const float* scale;    // [n_stripes*16] per packed row (0 on padding rows)
+  const int4* w;         // packed weights (WF_Q4: 8 bytes per lane per k-block)
+  const float* scale;    // WF_I8: [n_stripes*16] per packed row (0 on padding rows)
+  const uint32_t* qscale;// WF_Q4: [n_stripes][KB][8] fp16 pairs (rows g, g+8)
   const uint8_t* x;      // packed activation digits [KB][32][8*NT]
   const int* xexp;       // [M] exponents
   int KB;                // k-blocks per stripe
@@ -147,6 +161,7 @@ struct EmbedArgs {
   uint32_t* ids_out;     // optional: resolved ids [M]
   const int8_t* emb_q;   // [vocab][d] int8
   const float* emb_scale;// [vocab]
+  const uint8_t* emb_q4; // or q4_0 blocks [vocab][d/32][18] (then emb_q unused)
   int d, vocab, M;
   float* h;              // [M][d]
   unsigned long long* zero_keys;  // keys this forward will produce
@@ -195,9 +210,9 @@ __host__ __device__ inline uint32_t key_index(unsigned long long k) {
 // Kernel launchers (mc_kernels.cu).  All kernels are launched with
 // programmatic stream serialization allowed: each one issues its
 // data-independent loads (weights) before griddepcontrol.wait.
-cudaError_t launch_gemv(const GemvArgs& a, int epi, int nt, int grid,
+cudaError_t launch_gemv(const GemvArgs& a, int epi, int nt, int wf, int grid,
                         cudaStream_t s, bool pdl);
-int gemv_blocks_per_sm(int epi, int nt);
+int gemv_blocks_per_sm(int epi, int nt, int wf);
 cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t s, bool pdl);
@@ -211,7 +226,9 @@ cudaError_t launch_pack_int8(const int8_t* src, long long src_ld,
                              const float* src_scale, const int* row_map,
                              const int* col_map, int n_stripes, int KB,
                              int4* dst, float* dst_scale, cudaStream_t s);
-cudaError_t launch_pack_rows_q(const int8_t* src, long long n, int8_t* dst,
-                               cudaStream_t s);
+// q4_0 source [rows][KB] blocks of 18 bytes -> WF_Q4 stripes through row_map
+// (size n_stripes*16, -1 = padding row: zero scale, codes 8).
+cudaError_t launch_pack_q4(const uint8_t* src, const int* row_map, int n_stripes, int KB,
+                           uint2* dst, uint32_t* dst_scale, cudaStream_t s);
 
 }  // namespace mc

@@ -11,9 +11,11 @@
 //              (attention_kv, transformer.rs:944-982).
 //  k_embed     token_embedding (generate.rs:843-863) from int8 rows.
 //  k_accept    greedy acceptance (generate.rs:695-726).
+#include <cuda_fp16.h>
 #include <math.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "mc_internal.cuh"
 
@@ -31,6 +33,20 @@ __device__ __forceinline__ int4 ldg_stream(const int4* p, uint64_t pol) {
   int4 v;
   asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.s32 {%0,%1,%2,%3}, [%4], %5;"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ uint2 ldg_stream2(const uint2* p, uint64_t pol) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.u32 {%0,%1}, [%2], %3;"
+               : "=r"(v.x), "=r"(v.y)
+               : "l"(p), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ uint32_t ldg_stream1(const uint32_t* p, uint64_t pol) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.u32 %0, [%1], %2;"
+               : "=r"(v)
                : "l"(p), "l"(pol));
   return v;
 }
@@ -115,6 +131,30 @@ __device__ __forceinline__ float combine_digits(const int* row, int m, float sca
   double v = (double)X * (double)scale;
   v *= __longlong_as_double((long long)(1023 - e) << 52);
   return __double2float_rn(v);
+}
+
+// q4_0 tiles hold per-digit sums already scaled by the block scales (f32).
+__device__ __forceinline__ float combine_digits(const float* row, int m, float, int e) {
+  if (e == kExpNonFinite) return __int_as_float(0x7fc00000);
+  double v = (double)row[3 * m] * 16384.0 + (double)row[3 * m + 1] * 128.0 +
+             (double)row[3 * m + 2];
+  v *= __longlong_as_double((long long)(1023 - e) << 52);
+  return __double2float_rn(v);
+}
+
+// Four unsigned 4-bit codes (one per byte, 0..15) -> signed bytes code - 8.
+// Bytes stay below 0x80 after the add, so no carry crosses a byte.
+__device__ __forceinline__ uint32_t q4_signed(uint32_t u) {
+  return (u + 0x78787878u) ^ 0x80808080u;
+}
+__device__ __forceinline__ int4 q4_fragment(uint2 w) {
+  return make_int4((int)q4_signed(w.x & 0x0F0F0F0Fu), (int)q4_signed((w.x >> 4) & 0x0F0F0F0Fu),
+                   (int)q4_signed(w.y & 0x0F0F0F0Fu), (int)q4_signed((w.y >> 4) & 0x0F0F0F0Fu));
+}
+// Exact int -> float for |c| < 2^22 on the full-rate integer and FP32 pipes:
+// c + 0x4B400000 is the bit pattern of 1.5 * 2^23 + c.
+__device__ __forceinline__ float small_int_to_float(int c) {
+  return __fsub_rn(__int_as_float(c + 0x4B400000), 12582912.0f);
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) {
@@ -354,8 +394,8 @@ constexpr int kGemvWarps = 8;
 // one warp.  Lane (it, lane) handles rows r and r+8 of token m, with
 // idx = it*32 + lane, r = idx & 7, m = idx >> 3; the 8 lanes of a token form
 // one shuffle group for the encoding statistics.
-template <int NT, int EPI>
-__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, const int* tile,
+template <int NT, int EPI, typename T>
+__device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, const T* tile,
                                               int ld, int lane, unsigned long long* kmax,
                                               const float* scale, const int* xexp) {
   const int M = a.M;
@@ -372,8 +412,10 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
     uint32_t st_mx = 0u;
     if (valid) {
       const int e = xexp[m];
-      const float y0 = combine_digits(tile + r * ld, m, scale[prow], e);
-      const float y1 = combine_digits(tile + (r + 8) * ld, m, scale[prow + 8], e);
+      // q4_0 tiles carry their block scales already; int8 tiles take the row scale
+      const float sc0 = scale ? scale[prow] : 1.0f, sc1 = scale ? scale[prow + 8] : 1.0f;
+      const float y0 = combine_digits(tile + r * ld, m, sc0, e);
+      const float y1 = combine_digits(tile + (r + 8) * ld, m, sc1, e);
       if constexpr (EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_LMHEAD) {
         float* o = a.out ? a.out + (size_t)m * a.ldo : nullptr;
         if (prow < a.n_out) {
@@ -476,15 +518,29 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
 constexpr int kTileSlots = 8;      // stripes in flight per CTA when F > 1
 constexpr int kMaxCtaStripes = 64; // scales staged per CTA (before the wait)
 
-template <int NT, int EPI>
+// Shared memory of a k-split: int8 sums arrive by integer atomics (exact, so
+// order-free) in one tile per stripe; q4_0 sums are f32, so every unit keeps
+// its own partial tile and the last warp adds them in k order (results do
+// not depend on arrival order).
+constexpr int kMaxSplitUnits = 16;  // units per CTA when F > 1 (ns * F <= 14)
+
+template <int NT, int WF>
+static constexpr size_t gemv_dyn_smem() {
+  return ((size_t)kGemvWarps * 16 * (8 * NT + 1) +
+          (size_t)(WF == WF_Q4 ? kMaxSplitUnits : kTileSlots) * 16 * 8 * NT) * 4;
+}
+
+template <int NT, int EPI, int WF>
 __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   constexpr int U = GemvCfg<NT>::U;
   constexpr int COLS = GemvCfg<NT>::COLS;
+  constexpr bool Q4 = WF == WF_Q4;
+  using Acc = typename std::conditional<Q4, float, int>::type;
   extern __shared__ __align__(16) int gemv_smem[];
-  // per-warp fragment staging [warp][16][COLS+1], then shared stripe sums
-  int (*sm_epi)[16][COLS + 1] = reinterpret_cast<int (*)[16][COLS + 1]>(gemv_smem);
-  int (*sm_tile)[16 * COLS] =
-      reinterpret_cast<int (*)[16 * COLS]>(gemv_smem + kGemvWarps * 16 * (COLS + 1));
+  // per-warp fragment staging [warp][16][COLS+1], then the k-split area
+  Acc (*sm_epi)[16][COLS + 1] = reinterpret_cast<Acc (*)[16][COLS + 1]>(gemv_smem);
+  Acc (*sm_tile)[16 * COLS] =
+      reinterpret_cast<Acc (*)[16 * COLS]>(gemv_smem + kGemvWarps * 16 * (COLS + 1));
   __shared__ int sm_cnt[kTileSlots];
   __shared__ float sm_scale[kMaxCtaStripes * 16];
   __shared__ int sm_exp[kMaxTokens];
@@ -500,29 +556,45 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
 
   if (threadIdx.x < kTileSlots) sm_cnt[threadIdx.x] = 0;
   if (threadIdx.x < kMaxTokens) sm_keys[threadIdx.x] = 0ull;
-  if (F > 1)
+  if (!Q4 && F > 1)
     for (int i = threadIdx.x; i < kTileSlots * 16 * COLS; i += blockDim.x) (&sm_tile[0][0])[i] = 0;
-  const bool scale_smem = ns <= kMaxCtaStripes;
+  const bool scale_smem = !Q4 && ns <= kMaxCtaStripes;
   if (scale_smem)
     for (int i = threadIdx.x; i < ns * 16; i += blockDim.x) sm_scale[i] = a.scale[s0 * 16 + i];
 
   // Weights never depend on the producer grid: start streaming them (first
   // batch of this warp's first unit) before the wait.
   const uint64_t pol = policy_evict_first();
-  int4 wv[U];
+  int4 wv[Q4 ? 1 : U];
+  uint2 wq[Q4 ? U : 1];
+  uint32_t wsc[Q4 ? U : 1];
   auto unit_range = [&](int u, int& stripe, int& kb0, int& kb1) {
     stripe = s0 + u / F;
     const int part = u - (u / F) * F;
     kb0 = (int)((long long)a.KB * part / F);
     kb1 = (int)((long long)a.KB * (part + 1) / F);
   };
+  auto load_batch = [&](int stripe, int kb, int nb) {
+    if constexpr (Q4) {
+      const uint2* wp = reinterpret_cast<const uint2*>(a.w) + ((size_t)stripe * a.KB + kb) * 32 + lane;
+      const uint32_t* sp = a.qscale + ((size_t)stripe * a.KB + kb) * 8 + (lane >> 2);
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (j < nb) {
+          wq[j] = ldg_stream2(wp + (size_t)j * 32, pol);
+          wsc[j] = ldg_stream1(sp + (size_t)j * 8, pol);
+        }
+    } else {
+      const int4* wp = a.w + ((size_t)stripe * a.KB + kb) * 32 + lane;
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (j < nb) wv[j] = ldg_stream(wp + (size_t)j * 32, pol);
+    }
+  };
   if (warp < n_units) {
     int st, k0, k1;
     unit_range(warp, st, k0, k1);
-    const int4* wp = a.w + ((size_t)st * a.KB + k0) * 32 + lane;
-#pragma unroll
-    for (int j = 0; j < U; ++j)
-      if (j < k1 - k0) wv[j] = ldg_stream(wp + (size_t)j * 32, pol);
+    load_batch(st, k0, min(U, k1 - k0));
   }
   // Warm L2 with the next GEMV's weights (split like this grid) so HBM keeps
   // streaming through this grid's tail and the small kernels in between.
@@ -548,7 +620,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   unsigned long long kmax[(8 * kMaxTokens) / 32];
 #pragma unroll
   for (int i = 0; i < (8 * kMaxTokens) / 32; ++i) kmax[i] = 0ull;
-  const float* scl = scale_smem ? sm_scale - s0 * 16 : a.scale;
+  const float* scl = Q4 ? nullptr : (scale_smem ? sm_scale - s0 * 16 : a.scale);
 
   bool pre = true;
   for (int u = warp; u < n_units; u += kGemvWarps) {
@@ -559,18 +631,13 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
       pre = false;
       continue;
     }
-    int acc[NT][4];
+    Acc acc[NT][4];
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0;
-    const int4* wp = a.w + ((size_t)stripe * a.KB + k0) * 32 + lane;
     const uint8_t* xp = a.x + ((size_t)k0 * 32 + lane) * COLS;
     for (int i = 0; i < n; i += U) {
       const int nb = min(U, n - i);
-      if (!pre) {
-#pragma unroll
-        for (int j = 0; j < U; ++j)
-          if (j < nb) wv[j] = ldg_stream(wp + (size_t)(i + j) * 32, pol);
-      }
+      if (!pre) load_batch(stripe, k0 + i, nb);
       pre = false;
       uint32_t xv[U][2 * NT];
 #pragma unroll
@@ -579,8 +646,24 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
 #pragma unroll
       for (int j = 0; j < U; ++j)
         if (j < nb) {
+          if constexpr (Q4) {
+            // one k-block per MMA: exact int32 sums, then its block scales
+            const int4 af = q4_fragment(wq[j]);
+            const float d0 = __half2float(__ushort_as_half((unsigned short)(wsc[j] & 0xffffu)));
+            const float d1 = __half2float(__ushort_as_half((unsigned short)(wsc[j] >> 16)));
 #pragma unroll
-          for (int t = 0; t < NT; ++t) imma(acc[t], wv[j], xv[j][2 * t], xv[j][2 * t + 1]);
+            for (int t = 0; t < NT; ++t) {
+              int c[4] = {0, 0, 0, 0};
+              imma(c, af, xv[j][2 * t], xv[j][2 * t + 1]);
+              acc[t][0] = __fmaf_rn(small_int_to_float(c[0]), d0, acc[t][0]);
+              acc[t][1] = __fmaf_rn(small_int_to_float(c[1]), d0, acc[t][1]);
+              acc[t][2] = __fmaf_rn(small_int_to_float(c[2]), d1, acc[t][2]);
+              acc[t][3] = __fmaf_rn(small_int_to_float(c[3]), d1, acc[t][3]);
+            }
+          } else {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) imma(acc[t], wv[j], xv[j][2 * t], xv[j][2 * t + 1]);
+          }
         }
     }
     const int g = lane >> 2, tq = lane & 3;
@@ -598,13 +681,24 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
     } else {
       // F <= 8 and ns < 8, so a stripe's slot is its index in the CTA
       const int slot = stripe - s0;
-      int* tile = sm_tile[slot];
+      if constexpr (Q4) {
+        Acc* part = sm_tile[u];
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        atomicAdd(tile + g * COLS + t * 8 + 2 * tq, acc[t][0]);
-        atomicAdd(tile + g * COLS + t * 8 + 2 * tq + 1, acc[t][1]);
-        atomicAdd(tile + (g + 8) * COLS + t * 8 + 2 * tq, acc[t][2]);
-        atomicAdd(tile + (g + 8) * COLS + t * 8 + 2 * tq + 1, acc[t][3]);
+        for (int t = 0; t < NT; ++t) {
+          part[g * COLS + t * 8 + 2 * tq] = acc[t][0];
+          part[g * COLS + t * 8 + 2 * tq + 1] = acc[t][1];
+          part[(g + 8) * COLS + t * 8 + 2 * tq] = acc[t][2];
+          part[(g + 8) * COLS + t * 8 + 2 * tq + 1] = acc[t][3];
+        }
+      } else {
+        Acc* tile = sm_tile[slot];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          atomicAdd(tile + g * COLS + t * 8 + 2 * tq, acc[t][0]);
+          atomicAdd(tile + g * COLS + t * 8 + 2 * tq + 1, acc[t][1]);
+          atomicAdd(tile + (g + 8) * COLS + t * 8 + 2 * tq, acc[t][2]);
+          atomicAdd(tile + (g + 8) * COLS + t * 8 + 2 * tq + 1, acc[t][3]);
+        }
       }
       __syncwarp();
       int last = 0;
@@ -615,7 +709,23 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
       last = __shfl_sync(0xffffffffu, last, 0);
       if (last) {
         __threadfence_block();
-        gemv_epilogue<NT, EPI>(a, stripe, tile, COLS, lane, kmax, scl, sm_exp);
+        if constexpr (Q4) {
+          // add the stripe's non-empty partial tiles in k order into this
+          // warp's staging (empty k-ranges wrote no tile)
+          const Acc* parts = sm_tile[slot * F];
+          for (int i = lane; i < 16 * COLS; i += 32) {
+            float v = 0.0f;
+            for (int p = 0; p < F; ++p)
+              if ((long long)a.KB * (p + 1) / F > (long long)a.KB * p / F)
+                v = __fadd_rn(v, parts[p * 16 * COLS + i]);
+            sm_epi[warp][i / COLS][i % COLS] = v;
+          }
+          __syncwarp();
+          gemv_epilogue<NT, EPI>(a, stripe, &sm_epi[warp][0][0], COLS + 1, lane, kmax, scl,
+                                 sm_exp);
+        } else {
+          gemv_epilogue<NT, EPI>(a, stripe, sm_tile[slot], COLS, lane, kmax, scl, sm_exp);
+        }
       }
       __syncwarp();
     }
@@ -640,83 +750,96 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   }
 }
 
-template <int NT>
-static constexpr size_t gemv_dyn_smem() {
-  return ((size_t)kGemvWarps * 16 * (8 * NT + 1) + (size_t)kTileSlots * 16 * 8 * NT) * sizeof(int);
-}
-
-template <int NT, int EPI>
+template <int NT, int EPI, int WF>
 static cudaError_t launch_gemv_t(const GemvArgs& a, int grid, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kGemvWarps * 32);
-  cfg.dynamicSmemBytes = gemv_dyn_smem<NT>();
+  cfg.dynamicSmemBytes = gemv_dyn_smem<NT, WF>();
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_gemv<NT, EPI>, a);
+  return cudaLaunchKernelEx(&cfg, k_gemv<NT, EPI, WF>, a);
 }
 
-template <int NT>
+template <int NT, int WF>
 static cudaError_t launch_gemv_nt(const GemvArgs& a, int epi, int grid, cudaStream_t s, bool pdl) {
   switch (epi) {
-    case EPI_STORE: return launch_gemv_t<NT, EPI_STORE>(a, grid, s, pdl);
-    case EPI_RESID: return launch_gemv_t<NT, EPI_RESID>(a, grid, s, pdl);
-    case EPI_SWIGLU: return launch_gemv_t<NT, EPI_SWIGLU>(a, grid, s, pdl);
-    case EPI_QKV: return launch_gemv_t<NT, EPI_QKV>(a, grid, s, pdl);
-    case EPI_LMHEAD: return launch_gemv_t<NT, EPI_LMHEAD>(a, grid, s, pdl);
+    case EPI_STORE: return launch_gemv_t<NT, EPI_STORE, WF>(a, grid, s, pdl);
+    case EPI_RESID: return launch_gemv_t<NT, EPI_RESID, WF>(a, grid, s, pdl);
+    case EPI_SWIGLU: return launch_gemv_t<NT, EPI_SWIGLU, WF>(a, grid, s, pdl);
+    case EPI_QKV: return launch_gemv_t<NT, EPI_QKV, WF>(a, grid, s, pdl);
+    case EPI_LMHEAD: return launch_gemv_t<NT, EPI_LMHEAD, WF>(a, grid, s, pdl);
   }
   return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_gemv(const GemvArgs& a, int epi, int nt, int grid, cudaStream_t s, bool pdl) {
+template <int WF>
+static cudaError_t launch_gemv_wf(const GemvArgs& a, int epi, int nt, int grid, cudaStream_t s,
+                                  bool pdl) {
   switch (nt) {
-    case 1: return launch_gemv_nt<1>(a, epi, grid, s, pdl);
-    case 2: return launch_gemv_nt<2>(a, epi, grid, s, pdl);
-    case 3: return launch_gemv_nt<3>(a, epi, grid, s, pdl);
-    case 6: return launch_gemv_nt<6>(a, epi, grid, s, pdl);
+    case 1: return launch_gemv_nt<1, WF>(a, epi, grid, s, pdl);
+    case 2: return launch_gemv_nt<2, WF>(a, epi, grid, s, pdl);
+    case 3: return launch_gemv_nt<3, WF>(a, epi, grid, s, pdl);
+    case 6: return launch_gemv_nt<6, WF>(a, epi, grid, s, pdl);
   }
   return cudaErrorInvalidValue;
 }
 
-template <int NT, int EPI>
+cudaError_t launch_gemv(const GemvArgs& a, int epi, int nt, int wf, int grid, cudaStream_t s,
+                        bool pdl) {
+  if (wf == WF_Q4) {
+    if (!a.qscale) return cudaErrorInvalidValue;
+    return launch_gemv_wf<WF_Q4>(a, epi, nt, grid, s, pdl);
+  }
+  return launch_gemv_wf<WF_I8>(a, epi, nt, grid, s, pdl);
+}
+
+template <int NT, int EPI, int WF>
 static int bps_t() {
-  const size_t sm = gemv_dyn_smem<NT>();
+  const size_t sm = gemv_dyn_smem<NT, WF>();
   if (sm > 48 * 1024)
-    cudaFuncSetAttribute(k_gemv<NT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    cudaFuncSetAttribute(k_gemv<NT, EPI, WF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)sm);
   int n = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<NT, EPI>, kGemvWarps * 32, sm);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<NT, EPI, WF>, kGemvWarps * 32, sm);
   return n;
 }
 
 // Occupancy of a GEMV variant; also raises its dynamic shared-memory limit,
 // so it is called once per variant outside any stream capture.
-template <int NT>
+template <int NT, int WF>
 static int bps_nt(int epi) {
   switch (epi) {
-    case EPI_STORE: return bps_t<NT, EPI_STORE>();
-    case EPI_RESID: return bps_t<NT, EPI_RESID>();
-    case EPI_SWIGLU: return bps_t<NT, EPI_SWIGLU>();
-    case EPI_QKV: return bps_t<NT, EPI_QKV>();
-    case EPI_LMHEAD: return bps_t<NT, EPI_LMHEAD>();
+    case EPI_STORE: return bps_t<NT, EPI_STORE, WF>();
+    case EPI_RESID: return bps_t<NT, EPI_RESID, WF>();
+    case EPI_SWIGLU: return bps_t<NT, EPI_SWIGLU, WF>();
+    case EPI_QKV: return bps_t<NT, EPI_QKV, WF>();
+    case EPI_LMHEAD: return bps_t<NT, EPI_LMHEAD, WF>();
   }
   return 0;
+}
+
+template <int WF>
+static int bps_wf(int epi, int nt) {
+  switch (nt) {
+    case 1: return bps_nt<1, WF>(epi);
+    case 2: return bps_nt<2, WF>(epi);
+    case 3: return bps_nt<3, WF>(epi);
+    case 6: return bps_nt<6, WF>(epi);
+  }
+  return 0;
+}
+
+int gemv_blocks_per_sm(int epi, int nt, int wf) {
+  return wf == WF_Q4 ? bps_wf<WF_Q4>(epi, nt) : bps_wf<WF_I8>(epi, nt);
 }
 
 size_t gemv_ws_ints_per_stripe(int nt) { return (size_t)16 * 8 * nt; }
 
-int gemv_blocks_per_sm(int epi, int nt) {
-  switch (nt) {
-    case 1: return bps_nt<1>(epi);
-    case 2: return bps_nt<2>(epi);
-    case 3: return bps_nt<3>(epi);
-    case 6: return bps_nt<6>(epi);
-  }
-  return 0;
-}
 
 // ------------------------------------------------------------ quantize
 // Encodes the next GEMV's B operand.  Every CTA first recomputes, for all M
@@ -1166,10 +1289,23 @@ __global__ void __launch_bounds__(256) k_embed(EmbedArgs a) {
   float ss = 0.0f;
   uint32_t mx = 0u;  // max|h*w| as float bits (NaN/inf win)
   const bool in = id < (uint32_t)a.vocab;
-  const int8_t* q = in ? a.emb_q + (size_t)id * a.d : nullptr;
-  const float sc = in ? a.emb_scale[id] : 0.0f;
+  const bool q4 = a.emb_q4 != nullptr;
+  const int8_t* q = (in && !q4) ? a.emb_q + (size_t)id * a.d : nullptr;
+  const uint8_t* q4row = (in && q4) ? a.emb_q4 + (size_t)id * (a.d / 32) * kQ4BlockBytes : nullptr;
+  const float sc = (in && !q4) ? a.emb_scale[id] : 0.0f;
   for (int i = threadIdx.x; i < a.d; i += blockDim.x) {
-    const float v = in ? __fmul_rn((float)q[i], sc) : 0.0f;
+    float v = 0.0f;
+    if (q4row) {
+      // dequantize_q4_0 (dequant.rs:33-44): (code - 8) as f32 * d
+      const uint8_t* blk = q4row + (i >> 5) * kQ4BlockBytes;
+      const int j = i & 31;
+      const uint32_t byte = blk[2 + (j & 15)];
+      const int code = (int)(j < 16 ? (byte & 0x0Fu) : (byte >> 4)) - 8;
+      const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+      v = __fmul_rn((float)code, d);
+    } else if (q) {
+      v = __fmul_rn((float)q[i], sc);
+    }
     h[i] = v;
     ss = __fadd_rn(ss, __fmul_rn(v, v));
     mx = max(mx, __float_as_uint(fabsf(__fmul_rn(v, a.st_w ? a.st_w[i] : 1.0f))));
@@ -1312,6 +1448,50 @@ cudaError_t launch_pack_int8(const int8_t* src, long long src_ld, const float* s
   if (e != cudaSuccess) return e;
   const int n = n_stripes * 16;
   k_pack_scale<<<(n + 255) / 256, 256, 0, s>>>(src_scale, row_map, n, dst_scale);
+  return cudaGetLastError();
+}
+
+// One thread per (stripe, k-block, lane): gathers the nibbles of A registers
+// a0..a3 (rows g, g+8; columns 4t..4t+3 and 16+4t..16+4t+3 of the block) from
+// the q4_0 source.  In a source block, element j < 16 is the low nibble of
+// qs[j] and element 16 + j its high nibble (dequant.rs:33-44).
+__global__ void k_pack_q4(const uint8_t* __restrict__ src, const int* __restrict__ row_map,
+                          int n_stripes, int KB, uint2* __restrict__ dst,
+                          uint32_t* __restrict__ dst_scale) {
+  const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long total = (long long)n_stripes * KB * 32;
+  if (gid >= total) return;
+  const int lane = (int)(gid & 31);
+  const long long sk = gid >> 5;
+  const int kb = (int)(sk % KB);
+  const int stripe = (int)(sk / KB);
+  const int g = lane >> 2, t = lane & 3;
+  const int ra = row_map[stripe * 16 + g];
+  const int rb = row_map[stripe * 16 + g + 8];
+  const uint8_t* ba = ra >= 0 ? src + ((long long)ra * KB + kb) * kQ4BlockBytes : nullptr;
+  const uint8_t* bb = rb >= 0 ? src + ((long long)rb * KB + kb) * kQ4BlockBytes : nullptr;
+  uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    const uint32_t qa = ba ? ba[2 + 4 * t + b] : 0x88u;  // padding rows: codes 8 (value 0)
+    const uint32_t qb = bb ? bb[2 + 4 * t + b] : 0x88u;
+    w0 |= ((qa & 0x0Fu) | ((qb & 0x0Fu) << 4)) << (8 * b);
+    w1 |= ((qa >> 4) | (qb & 0xF0u)) << (8 * b);
+  }
+  dst[gid] = make_uint2(w0, w1);
+  if (t == 0) {
+    const uint32_t da = ba ? (uint32_t)ba[0] | ((uint32_t)ba[1] << 8) : 0u;
+    const uint32_t db = bb ? (uint32_t)bb[0] | ((uint32_t)bb[1] << 8) : 0u;
+    dst_scale[sk * 8 + g] = da | (db << 16);
+  }
+}
+
+cudaError_t launch_pack_q4(const uint8_t* src, const int* row_map, int n_stripes, int KB,
+                           uint2* dst, uint32_t* dst_scale, cudaStream_t s) {
+  const long long total = (long long)n_stripes * KB * 32;
+  const int bs = 256;
+  k_pack_q4<<<(unsigned)((total + bs - 1) / bs), bs, 0, s>>>(src, row_map, n_stripes, KB, dst,
+                                                             dst_scale);
   return cudaGetLastError();
 }
 

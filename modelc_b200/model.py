@@ -137,15 +137,50 @@ def dequant_int8_rows(q: np.ndarray, scale: np.ndarray) -> np.ndarray:
     return (q.astype(np.float32) * scale.astype(np.float32)[:, None]).astype(np.float32)
 
 
+def quantize_q4_0(x: np.ndarray) -> np.ndarray:
+    """ggml's q4_0 rule (the format parsers/gguf/dequant.rs:23-46 reads):
+    per block of 32 consecutive weights, d = (the signed value of largest
+    magnitude, first on ties) / -8, codes = trunc(x / d + 8.5) clamped to 15,
+    d stored as fp16.  Returns uint8 [rows, cols/32 * 18] for [rows, cols]."""
+    x = np.ascontiguousarray(x, np.float32)
+    rows, cols = x.shape
+    if cols % 32:
+        raise ValueError("q4_0 needs cols % 32 == 0")
+    b = x.reshape(rows, cols // 32, 32)
+    idx = np.argmax(np.abs(b), axis=2)  # first index of the largest |x|
+    mx = np.take_along_axis(b, idx[..., None], axis=2)[..., 0]
+    d = (mx / np.float32(-8.0)).astype(np.float32)
+    with np.errstate(divide="ignore"):
+        inv = np.where(d != 0, np.float32(1.0) / d, np.float32(0.0)).astype(np.float32)
+    v = (b * inv[..., None]).astype(np.float32) + np.float32(8.5)
+    q = np.minimum(np.trunc(v).astype(np.int32), 15).astype(np.uint8)
+    out = np.empty((rows, cols // 32, 18), np.uint8)
+    out[..., 0:2] = d.astype(np.float16).view(np.uint8).reshape(rows, cols // 32, 2)
+    out[..., 2:] = q[..., :16] | (q[..., 16:] << 4)
+    return out.reshape(rows, cols // 32 * 18)
+
+
+def dequant_q4_0(blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """dequant.rs:33-44: (code - 8) as f32 * d, low nibbles first."""
+    b = np.ascontiguousarray(blocks, np.uint8).reshape(rows, cols // 32, 18)
+    d = b[..., 0:2].copy().view(np.float16).astype(np.float32)  # [rows, nb, 1]
+    qs = b[..., 2:].astype(np.int32)
+    lo = (qs & 0x0F) - 8
+    hi = (qs >> 4) - 8
+    v = np.concatenate([lo, hi], axis=2).astype(np.float32) * d
+    return v.reshape(rows, cols).astype(np.float32)
+
+
 @dataclass
 class QTensor:
-    dtype: str                 # "f32" | "i8_row" | "i8_tensor"
+    dtype: str                 # "f32" | "i8_row" | "i8_tensor" | "q4_0"
     data: np.ndarray
     scales: np.ndarray | None = None
+    qshape: tuple | None = None  # logical [rows, cols] of q4_0 blocks
 
     @property
     def shape(self):
-        return self.data.shape
+        return tuple(self.qshape) if self.qshape is not None else self.data.shape
 
     def dequant(self) -> np.ndarray:
         if self.dtype == "f32":
@@ -154,6 +189,8 @@ class QTensor:
             return dequant_int8_rows(self.data, self.scales)
         if self.dtype == "i8_tensor":
             return (self.data.astype(np.float32) * np.float32(self.scales)).astype(np.float32)
+        if self.dtype == "q4_0":
+            return dequant_q4_0(self.data, *self.shape)
         raise ValueError(self.dtype)
 
 
@@ -172,6 +209,8 @@ def synth_weights(cfg: LlamaConfig, seed: int, std: float = 0.02, fmt: str = "i8
         if fmt == "i8_row":
             q, s = quantize_int8_rows(w)
             out[name] = QTensor("i8_row", q, s)
+        elif fmt == "q4_0":
+            out[name] = QTensor("q4_0", quantize_q4_0(w), None, shape)
         elif fmt == "f32":
             out[name] = QTensor("f32", w)
         else:
@@ -179,11 +218,29 @@ def synth_weights(cfg: LlamaConfig, seed: int, std: float = 0.02, fmt: str = "i8
     return out
 
 
+def _q4_0_torch(w):
+    """quantize_q4_0 in torch (same rule, f32 arithmetic) for device tensors."""
+    import torch
+    rows, cols = w.shape
+    b = w.view(rows, cols // 32, 32)
+    idx = b.abs().argmax(dim=2, keepdim=True)  # first maximal index
+    mx = b.gather(2, idx)[..., 0]
+    d = mx / -8.0
+    inv = torch.where(d != 0, 1.0 / d, torch.zeros_like(d))
+    v = b * inv[..., None] + 8.5
+    q = v.trunc().to(torch.int32).clamp_(max=15).to(torch.uint8)
+    out = torch.empty((rows, cols // 32, 18), dtype=torch.uint8, device=w.device)
+    out[..., 0:2] = d.to(torch.float16).contiguous().view(torch.uint8).view(rows, cols // 32, 2)
+    out[..., 2:] = q[..., :16] | (q[..., 16:] << 4)
+    return out.view(rows, cols // 32 * 18)
+
+
 def synth_weights_torch(cfg: LlamaConfig, seed: int, device, std: float = 0.02,
-                        tied: bool = False) -> dict:
+                        tied: bool = False, fmt: str = "i8_row") -> dict:
     """The same distribution generated on the GPU (for the multi-GB shapes):
     torch.randn per tensor from one seeded CUDA generator, then the per-row
-    int8 rule in f32 arithmetic.  Returns name -> (dtype, tensor, scales)."""
+    int8 rule (or q4_0) in f32 arithmetic.  Returns name -> (dtype, tensor,
+    scales); q4_0 entries are ("q4_0", blocks, (rows, cols))."""
     import torch
     g = torch.Generator(device=device)
     g.manual_seed(seed)
@@ -194,6 +251,16 @@ def synth_weights_torch(cfg: LlamaConfig, seed: int, device, std: float = 0.02,
             out[name] = ("f32", torch.ones(shape, dtype=torch.float32, device=device), None)
             continue
         rows = shape[0]
+        if fmt == "q4_0":
+            blk = torch.empty((rows, shape[1] // 32 * 18), dtype=torch.uint8, device=device)
+            step = max(1, (1 << 28) // shape[1])
+            for r0 in range(0, rows, step):
+                w = torch.randn((min(step, rows - r0), shape[1]), generator=g, device=device,
+                                dtype=torch.float32) * std
+                blk[r0:r0 + w.shape[0]] = _q4_0_torch(w)
+                del w
+            out[name] = ("q4_0", blk, tuple(shape))
+            continue
         q = torch.empty(shape, dtype=torch.int8, device=device)
         sc = torch.empty(rows, dtype=torch.float32, device=device)
         step = max(1, (1 << 28) // shape[1])
@@ -220,7 +287,8 @@ def _cfg_struct(cfg: LlamaConfig) -> _lib.ModelCfg:
                          cfg.head_dim, cfg.ffn, cfg.vocab, cfg.rope_theta, cfg.eps)
 
 
-_DT = {"f32": _lib.DTYPE_F32, "i8_tensor": _lib.DTYPE_I8_TENSOR, "i8_row": _lib.DTYPE_I8_ROW}
+_DT = {"f32": _lib.DTYPE_F32, "i8_tensor": _lib.DTYPE_I8_TENSOR, "i8_row": _lib.DTYPE_I8_ROW,
+       "q4_0": _lib.DTYPE_Q4_0}
 
 
 def _desc_arrays(tensors: dict):
@@ -233,12 +301,17 @@ def _desc_arrays(tensors: dict):
             if t.scales is not None:
                 sc = np.ascontiguousarray(np.atleast_1d(np.asarray(t.scales, np.float32)))
             keep += [data, sc]
-            shape = list(data.shape) + [0] * (2 - data.ndim)
-            descs.append(_lib.TensorDesc(name.encode(), _DT[t.dtype], _lib.MEM_HOST, data.ndim,
+            shape = list(t.shape) + [0] * (2 - len(t.shape))
+            descs.append(_lib.TensorDesc(name.encode(), _DT[t.dtype], _lib.MEM_HOST, len(t.shape),
                                          (C.c_int64 * 2)(*shape), data.ctypes.data,
                                          sc.ctypes.data if sc is not None else None))
         else:
             dt, ten, sc = t
+            if dt == "q4_0":  # sc carries the logical (rows, cols)
+                keep += [ten]
+                descs.append(_lib.TensorDesc(name.encode(), _DT[dt], _lib.MEM_DEVICE, 2,
+                                             (C.c_int64 * 2)(*sc), ten.data_ptr(), None))
+                continue
             keep += [ten, sc]
             shape = list(ten.shape) + [0] * (2 - ten.dim())
             descs.append(_lib.TensorDesc(name.encode(), _DT[dt], _lib.MEM_DEVICE, ten.dim(),
