@@ -102,9 +102,17 @@ typedef struct mc_spec_cfg {
   int32_t bonus;        /* 0: reference verify (gamma positions, no bonus
                            token, generate.rs:695-726); 1: gamma+1 positions
                            with the bonus token */
-  float temperature;    /* 0 = greedy (the only mode of this build) */
+  float temperature;    /* 0 = greedy; > 0 = sampling at this temperature
+                           (draft and target, no top-p / min-p) */
   uint64_t seed;
   volatile int32_t* cancel;  /* optional; checked between rounds (generate.rs:639) */
+  int32_t accept_mode;  /* temperature > 0 only.  0: accept draft x with
+                           probability min(1, p(x)/q(x)), else emit a sample of
+                           max(0, p - q) (distribution-preserving); 1: the
+                           reference's rule, accept when the target's own
+                           sample equals x (generate.rs:695-726).  Random
+                           numbers: Philox4x32-10 keyed by seed, counter
+                           (slot, round). */
 } mc_spec_cfg;
 
 /* Load (quantize-free) weights to the device and repack them for the
@@ -163,6 +171,9 @@ MC_API mc_status mc_spec_read(mc_session* s, uint32_t* out, int32_t cap, int32_t
 /* Restart decoding from the primed prompt: the prompt's KV is kept, the
  * generated tokens and round log are dropped. */
 MC_API mc_status mc_spec_rewind(mc_session* s);
+/* Reseed the stochastic rounds (GenerationConfig::seed per request,
+ * generate.rs:146-167); applies from the next round. */
+MC_API mc_status mc_spec_set_seed(mc_session* s, uint64_t seed);
 /* Enqueue n verify forwards (gamma or gamma+1 positions at the current
  * target length, no acceptance, no state change) on the session stream and
  * return immediately: for timing the verify forward with stream events. */

@@ -27,6 +27,7 @@ EXPORTS = [
     "mc_linear_create", "mc_linear_destroy", "mc_linear_run", "mc_linear_weight_bytes",
     "mc_last_error", "mc_version", "mc_spec_rewind", "mc_spec_verify_launch",
     "mc_session_stream", "mc_session_round_launches", "mc_linear_run_static",
+    "mc_spec_set_seed",
 ]
 
 
@@ -52,7 +53,7 @@ class TensorDesc(C.Structure):
 class SpecCfg(C.Structure):
     _fields_ = [("gamma", C.c_int32), ("max_context", C.c_int32), ("bonus", C.c_int32),
                 ("temperature", C.c_float), ("seed", C.c_uint64),
-                ("cancel", C.POINTER(C.c_int32))]
+                ("cancel", C.POINTER(C.c_int32)), ("accept_mode", C.c_int32)]
 
 
 _lib = None
@@ -93,6 +94,7 @@ def lib():
         "mc_last_error": (C.c_size_t, [C.c_char_p, C.c_size_t]),
         "mc_spec_rewind": (i32, [vp]),
         "mc_spec_verify_launch": (i32, [vp, i32]),
+        "mc_spec_set_seed": (i32, [vp, C.c_uint64]),
         "mc_session_stream": (vp, [vp]),
         "mc_session_round_launches": (i32, [vp]),
         "mc_version": (C.c_char_p, []),

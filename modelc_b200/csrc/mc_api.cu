@@ -625,6 +625,7 @@ struct mc_session {
   float* attn = nullptr;
   float* act = nullptr;
   float* logits = nullptr;
+  float* dlogits = nullptr;  // draft logits of a stochastic round [kMaxTokens][V]
   int* ws = nullptr;
   int* cnt = nullptr;
   float* part_o = nullptr;
@@ -751,6 +752,7 @@ static mc_status session_alloc(mc_session* s) {
   CK(cudaMemset(s->attn, 0, (size_t)M * hq * 4));
   CKS(s->al.alloc(&s->act, (size_t)M * std::max(F, 1)));
   CKS(s->al.alloc(&s->logits, (size_t)M * V));
+  if (s->cfg.temperature > 0.0f) CKS(s->al.alloc(&s->dlogits, (size_t)kMaxTokens * V));
   CKS(s->al.alloc(&s->ws, (size_t)stripes * 32 * 24));
   CK(cudaMemset(s->ws, 0, (size_t)stripes * 32 * 24 * 4));
   CKS(s->al.alloc(&s->cnt, (size_t)stripes));
@@ -799,8 +801,13 @@ extern "C" mc_status mc_session_create(const mc_weights* target, const mc_weight
   if (cfg->gamma < 0 || cfg->gamma + 1 > kMaxTokens)
     return set_err(MC_E_INVALID, "gamma %d outside [0, %d]", cfg->gamma, kMaxTokens - 1);
   if (cfg->max_context <= 0) return set_err(MC_E_INVALID, "max_context must be positive");
-  if (cfg->temperature > 0.0f)
-    return set_err(MC_E_INVALID, "stochastic acceptance is not built yet; use temperature 0");
+  if (!(cfg->temperature >= 0.0f) || !isfinite(cfg->temperature))
+    return set_err(MC_E_INVALID, "temperature must be finite and >= 0");
+  if (cfg->accept_mode != 0 && cfg->accept_mode != 1)
+    return set_err(MC_E_INVALID, "accept_mode must be 0 (min(1,p/q)) or 1 (sample == draft)");
+  if (cfg->temperature > 0.0f && target->V > kSampleMaxVocab)
+    return set_err(MC_E_SHAPE, "vocab %d above the sampler's limit %d", target->V,
+                   kSampleMaxVocab);
   if (draft && (draft->V != target->V))
     return set_err(MC_E_SHAPE, "draft vocab %d != target vocab %d", draft->V, target->V);
   CK(cudaSetDevice(target->dev));
@@ -1135,14 +1142,14 @@ static int forward_launches(const mc_weights* W) {
   return n;
 }
 
-static mc_status enq_verify(mc_session* s) {
+static mc_status enq_verify(mc_session* s, float* logits = nullptr) {
   const int vm = s->cfg.gamma + (s->cfg.bonus ? 1 : 0);
   EmbedArgs ea{};
   ea.src = SRC_VERIFY;
   ea.ctx = s->ctx;
   ea.off = &s->st->ctx_len;
   ea.keys = s->st->dkeys;
-  return enq_forward(s, s->tw, s->tkv, vm, ea, &s->st->lt, 0, s->st->tkeys, nullptr);
+  return enq_forward(s, s->tw, s->tkv, vm, ea, &s->st->lt, 0, s->st->tkeys, logits);
 }
 
 static mc_status capture_verify(mc_session* s) {
@@ -1171,6 +1178,8 @@ static mc_status capture_round(mc_session* s) {
   SpecState* st = s->st;
   CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
   mc_status rc = MC_OK;
+  const bool stochastic = s->cfg.temperature > 0.0f;
+  const int V = s->tw->V;
   for (int j = 0; j < dsteps && rc == MC_OK; ++j) {
     EmbedArgs ea{};
     if (j == 0) {
@@ -1181,11 +1190,19 @@ static mc_status capture_round(mc_session* s) {
       ea.src = SRC_KEYS;
       ea.keys = &st->dkeys[j - 1];
     }
-    rc = enq_forward(s, s->dw, s->dkv, 1, ea, &st->ld, j, &st->dkeys[j], nullptr);
+    float* dl = stochastic && j < g ? s->dlogits + (size_t)j * V : nullptr;
+    rc = enq_forward(s, s->dw, s->dkv, 1, ea, &st->ld, j, &st->dkeys[j], dl);
+    if (rc == MC_OK && dl) {  // x_j ~ softmax(q_j / T) replaces the argmax key
+      cudaError_t e = launch_sample_draft(st, dl, V, j, &st->dkeys[j], s->stream, true);
+      if (e != cudaSuccess) rc = set_err(MC_E_CUDA, "draft sample: %s", cudaGetErrorString(e));
+    }
   }
-  if (rc == MC_OK) rc = enq_verify(s);
+  if (rc == MC_OK) rc = enq_verify(s, stochastic ? s->logits : nullptr);
   if (rc == MC_OK) {
-    cudaError_t e = launch_accept_greedy(st, s->ctx, s->acc_log, vm, s->stream, true);
+    cudaError_t e = stochastic
+                        ? launch_accept_stochastic(st, s->ctx, s->acc_log, vm, s->logits,
+                                                   s->dlogits, V, s->stream, true)
+                        : launch_accept_greedy(st, s->ctx, s->acc_log, vm, s->stream, true);
     if (e != cudaSuccess) rc = set_err(MC_E_CUDA, "accept launch: %s", cudaGetErrorString(e));
   }
   cudaGraph_t graph = nullptr;
@@ -1198,8 +1215,27 @@ static mc_status capture_round(mc_session* s) {
   e = cudaGraphInstantiate(&s->round_exec, graph, 0);
   cudaGraphDestroy(graph);
   if (e != cudaSuccess) return set_err(MC_E_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
-  s->round_launches = dsteps * forward_launches(s->dw) + forward_launches(s->tw) + 1;
+  s->round_launches = dsteps * forward_launches(s->dw) + forward_launches(s->tw) + 1 +
+                      (stochastic ? g : 0);
   return MC_OK;
+}
+
+// Round state right after priming n_prompt tokens.
+static SpecState fresh_state(const mc_session* s, int n_prompt) {
+  SpecState h{};
+  h.ctx_len = n_prompt;
+  h.lt = n_prompt;
+  h.ld = n_prompt - 1;
+  h.generated = 0;
+  h.prompt_len = n_prompt;
+  h.gamma = s->cfg.gamma;
+  h.bonus = s->cfg.bonus ? 1 : 0;
+  h.rounds_cap = s->cap;
+  h.accept_mode = s->cfg.accept_mode;
+  h.temperature = s->cfg.temperature;
+  h.seed_lo = (uint32_t)s->cfg.seed;
+  h.seed_hi = (uint32_t)(s->cfg.seed >> 32);
+  return h;
 }
 
 extern "C" mc_status mc_spec_prime(mc_session* s, const uint32_t* prompt, int32_t n_prompt) {
@@ -1233,15 +1269,7 @@ extern "C" mc_status mc_spec_prime(mc_session* s, const uint32_t* prompt, int32_
     ea.ids = s->ctx + c0;
     CKS(enq_forward(s, s->dw, s->dkv, M, ea, s->pos + 1, 0, s->st->dkeys, nullptr));
   }
-  SpecState h{};
-  h.ctx_len = n_prompt;
-  h.lt = n_prompt;
-  h.ld = n_prompt - 1;
-  h.generated = 0;
-  h.prompt_len = n_prompt;
-  h.gamma = s->cfg.gamma;
-  h.bonus = s->cfg.bonus ? 1 : 0;
-  h.rounds_cap = s->cap;
+  SpecState h = fresh_state(s, n_prompt);
   CK(cudaMemcpyAsync(s->st, &h, sizeof(h), cudaMemcpyHostToDevice, s->stream));
   CK(cudaStreamSynchronize(s->stream));
   s->lt = n_prompt;
@@ -1299,18 +1327,22 @@ extern "C" mc_status mc_spec_read(mc_session* s, uint32_t* out, int32_t cap, int
 extern "C" mc_status mc_spec_rewind(mc_session* s) {
   if (!s || !s->prompt_len) return set_err(MC_E_INVALID, "call mc_spec_prime first");
   CK(cudaSetDevice(s->dev));
-  SpecState h{};
-  h.ctx_len = s->prompt_len;
-  h.lt = s->prompt_len;
-  h.ld = s->prompt_len - 1;
-  h.prompt_len = s->prompt_len;
-  h.gamma = s->cfg.gamma;
-  h.bonus = s->cfg.bonus ? 1 : 0;
-  h.rounds_cap = s->cap;
+  SpecState h = fresh_state(s, s->prompt_len);
   CK(cudaMemcpyAsync(s->st, &h, sizeof(h), cudaMemcpyHostToDevice, s->stream));
   CK(cudaStreamSynchronize(s->stream));
   s->lt = h.lt;
   s->ld = h.ld;
+  return MC_OK;
+}
+
+extern "C" mc_status mc_spec_set_seed(mc_session* s, uint64_t seed) {
+  if (!s) return set_err(MC_E_INVALID, "null session");
+  s->cfg.seed = seed;
+  if (!s->prompt_len) return MC_OK;  // taken at the next mc_spec_prime
+  CK(cudaSetDevice(s->dev));
+  const uint32_t v[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
+  CK(cudaMemcpyAsync(&s->st->seed_lo, v, sizeof(v), cudaMemcpyHostToDevice, s->stream));
+  CK(cudaStreamSynchronize(s->stream));
   return MC_OK;
 }
 
@@ -1328,7 +1360,8 @@ extern "C" void* mc_session_stream(mc_session* s) { return s ? (void*)s->stream 
 extern "C" int32_t mc_session_round_launches(const mc_session* s) {
   if (!s || !s->dw) return 0;
   const int dsteps = s->cfg.gamma + (s->cfg.bonus ? 1 : 0);
-  return dsteps * forward_launches(s->dw) + forward_launches(s->tw) + 1;
+  return dsteps * forward_launches(s->dw) + forward_launches(s->tw) + 1 +
+         (s->cfg.temperature > 0.0f ? s->cfg.gamma : 0);
 }
 
 extern "C" mc_status mc_speculative_generate(mc_session* s, const uint32_t* prompt,

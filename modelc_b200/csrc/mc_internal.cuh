@@ -187,7 +187,10 @@ struct SpecState {
   int n_rounds;
   int bonus;
   int rounds_cap;
-  int pad[6];
+  int accept_mode;     // stochastic: 0 = min(1, p/q) + residual, 1 = sample == draft
+  float temperature;   // > 0: stochastic rounds
+  uint32_t seed_lo, seed_hi;
+  int pad[2];
   unsigned long long tkeys[kMaxTokens];
   unsigned long long dkeys[kMaxTokens];
 };
@@ -219,6 +222,15 @@ cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_accept_greedy(SpecState* st, uint32_t* ctx, int* acc_log,
                                  int vm, cudaStream_t s, bool pdl);
 cudaError_t launch_set_int(int* p, int v, cudaStream_t s);
+// Stochastic rounds: sample draft step j from softmax(logits / T) into
+// *key_out (as an argmax key), and the acceptance of a whole round from the
+// verify logits tlog [vm][V] and the draft logits dlog [gamma][V].
+cudaError_t launch_sample_draft(SpecState* st, const float* logits, int V, int j,
+                                unsigned long long* key_out, cudaStream_t s, bool pdl);
+cudaError_t launch_accept_stochastic(SpecState* st, uint32_t* ctx, int* acc_log, int vm,
+                                     const float* tlog, const float* dlog, int V,
+                                     cudaStream_t s, bool pdl);
+constexpr int kSampleMaxVocab = 256 * 1024;  // tiles of 1024 staged in shared memory
 size_t attention_smem_bytes(int G, int M, int hdp, int page);
 size_t gemv_ws_ints_per_stripe(int nt);
 cudaError_t prepare_kernels(size_t quant_smem, size_t attn_smem);

@@ -1392,6 +1392,272 @@ cudaError_t launch_accept_greedy(SpecState* st, uint32_t* ctx, int* acc_log, int
   return cudaLaunchKernelEx(&cfg, k_accept_greedy, st, ctx, acc_log, vm);
 }
 
+// ------------------------------------------------------------ sampling
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC 2011): ten rounds of
+// (hi0, lo0) = M0 * c0, (hi1, lo1) = M1 * c2, c = (hi1^c1^k0, lo1, hi0^c3^k1,
+// lo0), key advanced by the Weyl constants between rounds.  Counter
+// (slot, round, 0, 0), key = seed; uniform = top 24 bits * 2^-24.  Slots per
+// round: draft sample j -> j, acceptance test j -> 32 + j, residual / target
+// / bonus sample j -> 64 + j.
+__device__ __forceinline__ float philox_uniform(uint32_t seed_lo, uint32_t seed_hi,
+                                                uint32_t round, uint32_t slot) {
+  uint32_t c0 = slot, c1 = round, c2 = 0u, c3 = 0u, k0 = seed_lo, k1 = seed_hi;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    if (r > 0) {
+      k0 += 0x9E3779B9u;
+      k1 += 0xBB67AE85u;
+    }
+    const uint32_t lo0 = 0xD2511F53u * c0, hi0 = __umulhi(0xD2511F53u, c0);
+    const uint32_t lo1 = 0xCD9E8D57u * c2, hi1 = __umulhi(0xCD9E8D57u, c2);
+    const uint32_t n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+    c0 = n0;
+    c1 = lo1;
+    c2 = n2;
+    c3 = lo0;
+  }
+  return (float)(c0 >> 8) * (1.0f / 16777216.0f);
+}
+
+constexpr int kSampThreads = 1024;  // 32 warps; tile t = elements [1024 t, 1024 t + 1024)
+constexpr int kSampTiles = kSampleMaxVocab / 1024;
+
+struct SampSmem {
+  float red[32];
+  int ired[32];
+  float tile[kSampTiles];
+  int tile_last[kSampTiles];
+  float bcast[4];
+  int ibcast[4];  // [0] tile of the target, [1] fallback index, [2] index found
+};
+
+__device__ float block_max(const float* row, int V, SampSmem& sm) {
+  float m = -INFINITY;
+  for (int v = threadIdx.x; v < V; v += kSampThreads) m = fmaxf(m, row[v]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) sm.red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float x = sm.red[threadIdx.x];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+    if (threadIdx.x == 0) sm.bcast[0] = x;
+  }
+  __syncthreads();
+  return sm.bcast[0];
+}
+
+// Sums of the weights w(v) >= 0 per tile (warp w takes tiles w, w+32, ...;
+// lane l adds elements 32 i + l of its tile in i order, then an xor tree),
+// the last positive index of each tile, and their total in tile order.
+template <class W>
+__device__ float tile_sums(W w, int V, SampSmem& sm) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = (V + 1023) >> 10;
+  for (int t = warp; t < nt; t += 32) {
+    float s = 0.0f;
+    int last = -1;
+    for (int i = 0; i < 32; ++i) {
+      const int v = (t << 10) + i * 32 + lane;
+      if (v < V) {
+        const float x = w(v);
+        s = __fadd_rn(s, x);
+        if (x > 0.0f) last = v;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+      last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+    }
+    if (lane == 0) {
+      sm.tile[t] = s;
+      sm.tile_last[t] = last;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.0f;
+    for (int t = 0; t < nt; ++t) tot = __fadd_rn(tot, sm.tile[t]);
+    sm.bcast[1] = tot;
+  }
+  __syncthreads();
+  return sm.bcast[1];
+}
+
+// Inverse CDF in index order over w (tile sums already in sm.tile, total
+// `tot`): the first v whose running sum exceeds u * tot; if rounding leaves
+// none, the last positive weight.  Returns v to every thread.
+template <class W>
+__device__ int inv_cdf(W w, int V, float tot, float u, SampSmem& sm) {
+  const int nt = (V + 1023) >> 10;
+  if (threadIdx.x == 0) {
+    const float tau = __fmul_rn(u, tot);
+    float c = 0.0f;
+    int kt = -1, fallback = -1;
+    for (int t = 0; t < nt; ++t) {
+      if (sm.tile_last[t] >= 0) fallback = sm.tile_last[t];
+      if (kt < 0 && __fadd_rn(c, sm.tile[t]) > tau) {
+        kt = t;
+      } else if (kt < 0) {
+        c = __fadd_rn(c, sm.tile[t]);
+      }
+    }
+    sm.ibcast[0] = kt;
+    sm.ibcast[1] = fallback < 0 ? 0 : fallback;
+    sm.bcast[2] = __fsub_rn(tau, c);  // remaining mass inside tile kt
+  }
+  __syncthreads();
+  const int kt = sm.ibcast[0];
+  int res = sm.ibcast[1];
+  if (kt >= 0 && threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const float rem = sm.bcast[2];
+    float c = 0.0f;
+    int found = -1;
+    for (int i = 0; i < 32 && found < 0; ++i) {
+      const int v = (kt << 10) + i * 32 + lane;
+      const float x = v < V ? w(v) : 0.0f;
+      float sc = x;  // inclusive scan over lanes (index order within the row)
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, sc, o);
+        if (lane >= o) sc = __fadd_rn(sc, y);
+      }
+      const float run = __fadd_rn(c, sc);
+      const unsigned hit = __ballot_sync(0xffffffffu, run > rem && x > 0.0f);
+      if (hit) found = (kt << 10) + i * 32 + (__ffs(hit) - 1);
+      c = __fadd_rn(c, __shfl_sync(0xffffffffu, sc, 31));
+    }
+    if (lane == 0) sm.ibcast[2] = found >= 0 ? found : -2;
+  }
+  __syncthreads();
+  if (kt >= 0) {
+    const int f = sm.ibcast[2];
+    res = f >= 0 ? f : (sm.tile_last[kt] >= 0 ? sm.tile_last[kt] : res);
+  }
+  __syncthreads();
+  return res;
+}
+
+__global__ void __launch_bounds__(kSampThreads) k_sample_draft(SpecState* st, const float* row,
+                                                               int V, int j,
+                                                               unsigned long long* key_out) {
+  __shared__ SampSmem sm;
+  grid_launch_dependents();
+  grid_wait();
+  const float t = st->temperature;
+  const float mx = block_max(row, V, sm);
+  auto w = [&](int v) { return expf(__fdiv_rn(__fsub_rn(__ldcg(row + v), mx), t)); };
+  const float tot = tile_sums(w, V, sm);
+  const float u = philox_uniform(st->seed_lo, st->seed_hi, (uint32_t)st->n_rounds, (uint32_t)j);
+  const int x = inv_cdf(w, V, tot, u, sm);
+  if (threadIdx.x == 0) *key_out = argmax_key(0.0f, (uint32_t)x);
+}
+
+__global__ void __launch_bounds__(kSampThreads) k_accept_stochastic(
+    SpecState* st, uint32_t* ctx, int* acc_log, int vm, const float* tlog, const float* dlog,
+    int V) {
+  __shared__ SampSmem sm;
+  grid_launch_dependents();
+  grid_wait();
+  const int g = st->gamma;
+  const float t = st->temperature;
+  const uint32_t rnd = (uint32_t)st->n_rounds, s0 = st->seed_lo, s1 = st->seed_hi;
+  int a = 0, y = -1;
+  for (int j = 0; j < g; ++j) {
+    const float* p = tlog + (size_t)j * V;
+    const float* q = dlog + (size_t)j * V;
+    const uint32_t x = min(key_index(st->dkeys[j]), (uint32_t)(V - 1));
+    const float u_res = philox_uniform(s0, s1, rnd, 64u + (uint32_t)j);
+    const float mp = block_max(p, V, sm);
+    auto wp = [&](int v) { return expf(__fdiv_rn(__fsub_rn(__ldcg(p + v), mp), t)); };
+    const float sp = tile_sums(wp, V, sm);
+    if (st->accept_mode == 1) {
+      // the reference's rule (generate.rs:695-726): the target's own sample
+      const int z = inv_cdf(wp, V, sp, u_res, sm);
+      if ((uint32_t)z == x) {
+        ++a;
+        continue;
+      }
+      y = z;
+      break;
+    }
+    const float mq = block_max(q, V, sm);
+    auto wq = [&](int v) { return expf(__fdiv_rn(__fsub_rn(__ldcg(q + v), mq), t)); };
+    const float sq = tile_sums(wq, V, sm);
+    const float ep = wp((int)x), eq = wq((int)x);
+    const float u = philox_uniform(s0, s1, rnd, 32u + (uint32_t)j);
+    if (__fmul_rn(__fmul_rn(u, eq), sp) < __fmul_rn(ep, sq)) {  // u < p(x) / q(x)
+      ++a;
+      continue;
+    }
+    auto wr = [&](int v) {
+      return fmaxf(__fsub_rn(__fdiv_rn(wp(v), sp), __fdiv_rn(wq(v), sq)), 0.0f);
+    };
+    const float rs = tile_sums(wr, V, sm);
+    if (rs > 0.0f) {
+      y = inv_cdf(wr, V, rs, u_res, sm);
+    } else {
+      tile_sums(wp, V, sm);
+      y = inv_cdf(wp, V, sp, u_res, sm);
+    }
+    break;
+  }
+  if (y < 0 && a == g && vm > g) {  // bonus token from the last verify position
+    const float* p = tlog + (size_t)g * V;
+    const float mp = block_max(p, V, sm);
+    auto wp = [&](int v) { return expf(__fdiv_rn(__fsub_rn(__ldcg(p + v), mp), t)); };
+    const float sp = tile_sums(wp, V, sm);
+    y = inv_cdf(wp, V, sp, philox_uniform(s0, s1, rnd, 64u + (uint32_t)g), sm);
+  }
+  if (threadIdx.x != 0) return;
+  const int len = st->ctx_len;
+  for (int j = 0; j < a; ++j) ctx[len + j] = key_index(st->dkeys[j]);
+  int emitted = a;
+  if (y >= 0) {
+    ctx[len + a] = (uint32_t)y;
+    emitted = a + 1;
+  }
+  st->ctx_len = len + emitted;
+  st->lt += (a + 1 < vm) ? a + 1 : vm;
+  st->ld = st->ctx_len - 1;
+  st->generated += emitted;
+  if (acc_log && st->n_rounds < st->rounds_cap) acc_log[st->n_rounds] = a;
+  st->n_rounds += 1;
+}
+
+template <class K, class... Args>
+static cudaError_t launch_one_block(K kernel, int threads, cudaStream_t s, bool pdl,
+                                    Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(threads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+cudaError_t launch_sample_draft(SpecState* st, const float* logits, int V, int j,
+                                unsigned long long* key_out, cudaStream_t s, bool pdl) {
+  if (V <= 0 || V > kSampleMaxVocab) return cudaErrorInvalidValue;
+  return launch_one_block(k_sample_draft, kSampThreads, s, pdl, st, logits, V, j, key_out);
+}
+
+cudaError_t launch_accept_stochastic(SpecState* st, uint32_t* ctx, int* acc_log, int vm,
+                                     const float* tlog, const float* dlog, int V,
+                                     cudaStream_t s, bool pdl) {
+  if (V <= 0 || V > kSampleMaxVocab) return cudaErrorInvalidValue;
+  return launch_one_block(k_accept_stochastic, kSampThreads, s, pdl, st, ctx, acc_log, vm, tlog,
+                          dlog, V);
+}
+
 __global__ void k_set_int(int* p, int v) { *p = v; }
 cudaError_t launch_set_int(int* p, int v, cudaStream_t s) {
   k_set_int<<<1, 1, 0, s>>>(p, v);

@@ -24,6 +24,7 @@ class GenerationConfig:
     gamma: int = 0
     seed: int = 0
     bonus: bool = False   # False: the reference verify (no bonus token)
+    accept_mode: int = 0  # temperature > 0: 0 = min(1, p/q), 1 = sample == draft
 
 
 def _u32(a) -> np.ndarray:
@@ -38,12 +39,12 @@ class Session:
 
     def __init__(self, target: Weights, draft: Weights | None = None, gamma: int = 4,
                  max_context: int = 2048, bonus: bool = False, temperature: float = 0.0,
-                 seed: int = 0):
+                 seed: int = 0, accept_mode: int = 0):
         self.target, self.draft = target, draft
         self.gamma = gamma
         self._cancel = C.c_int32(0)
         cfg = _lib.SpecCfg(gamma, max_context, int(bonus), temperature, seed,
-                           C.pointer(self._cancel))
+                           C.pointer(self._cancel), accept_mode)
         h = C.c_void_p()
         check(lib().mc_session_create(target.handle, draft.handle if draft else None,
                                       C.byref(cfg), C.byref(h)))
@@ -117,6 +118,10 @@ class Session:
         """Back to the primed prompt (its KV kept)."""
         check(lib().mc_spec_rewind(self.handle))
 
+    def set_seed(self, seed: int):
+        """Seed of the stochastic rounds from the next round on."""
+        check(lib().mc_spec_set_seed(self.handle, seed))
+
     def verify_launch(self, n: int):
         """Enqueue n verify forwards on the session stream (timing only)."""
         check(lib().mc_spec_verify_launch(self.handle, n))
@@ -158,10 +163,10 @@ class LlamaDraftModel:
 def speculative_generate(target: Weights, draft: Weights, prompt, config: GenerationConfig,
                          max_context: int | None = None):
     """generate.rs:598-767 with a transformer draft; returns (ids, accepted)."""
-    if config.temperature > 0:
-        raise NotImplementedError("stochastic acceptance is not built yet")
     cap = max_context or (len(prompt) + config.max_tokens + config.gamma + 8)
-    s = Session(target, draft, gamma=config.gamma, max_context=cap, bonus=config.bonus)
+    s = Session(target, draft, gamma=config.gamma, max_context=cap, bonus=config.bonus,
+                temperature=config.temperature, seed=config.seed,
+                accept_mode=config.accept_mode)
     try:
         return s.speculative_generate(prompt, config.max_tokens)
     finally:

@@ -967,3 +967,201 @@ int oracle_speculative_generate(const oracle_model* m, int draft_kind,
   free(ix.keys); free(ix.next);
   return ncopy;
 }
+
+/* ---------------- stochastic speculative sampling ----------------
+ * Not in the reference (its verify is "target sample == draft", Q4); this is
+ * the min(1, p/q) scheme with residual resampling (Leviathan, Kalman, Matias,
+ * ICML 2023; Chen et al. 2023) that the device implements, restated here as
+ * the statistical reference, plus the reference-compatible sample-and-match
+ * rule on the same random stream.
+ *
+ * Random stream: Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random
+ * numbers: as easy as 1, 2, 3", SC 2011): ten rounds of
+ *   (hi0, lo0) = M0 * c0, (hi1, lo1) = M1 * c2,
+ *   c = (hi1 ^ c1 ^ k0, lo1, hi0 ^ c3 ^ k1, lo0),
+ * with the key advanced by the Weyl constants between rounds. */
+static void philox_round(uint32_t c[4], const uint32_t k[2]) {
+  const uint64_t p0 = (uint64_t)0xD2511F53u * c[0];
+  const uint64_t p1 = (uint64_t)0xCD9E8D57u * c[2];
+  const uint32_t hi0 = (uint32_t)(p0 >> 32), lo0 = (uint32_t)p0;
+  const uint32_t hi1 = (uint32_t)(p1 >> 32), lo1 = (uint32_t)p1;
+  const uint32_t n0 = hi1 ^ c[1] ^ k[0], n2 = hi0 ^ c[3] ^ k[1];
+  c[0] = n0;
+  c[1] = lo1;
+  c[2] = n2;
+  c[3] = lo0;
+}
+
+void oracle_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]) {
+  uint32_t c[4] = {ctr[0], ctr[1], ctr[2], ctr[3]};
+  uint32_t k[2] = {key[0], key[1]};
+  for (int r = 0; r < 10; ++r) {
+    if (r > 0) {
+      k[0] += 0x9E3779B9u;
+      k[1] += 0xBB67AE85u;
+    }
+    philox_round(c, k);
+  }
+  memcpy(out, c, sizeof(c));
+}
+
+/* Uniform in [0, 1) with 24 random bits for (seed, round, slot).  Slots per
+ * round: draft sample j -> j, acceptance test of position j -> 32 + j,
+ * residual / target / bonus sample at position j -> 64 + j. */
+float oracle_philox_uniform(uint64_t seed, uint32_t round, uint32_t slot) {
+  const uint32_t ctr[4] = {slot, round, 0u, 0u};
+  const uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
+  uint32_t o[4];
+  oracle_philox4x32_10(ctr, key, o);
+  return (float)(o[0] >> 8) * (1.0f / 16777216.0f);
+}
+
+/* max and sum of e_v = exp((l_v - max) / T), sequential. */
+static void temp_stats(const float* l, int n, float t, float* mx, float* sum) {
+  float m = -INFINITY;
+  for (int v = 0; v < n; ++v)
+    if (l[v] > m) m = l[v];
+  float s = 0.0f;
+  for (int v = 0; v < n; ++v) s += expf((l[v] - m) / t);
+  *mx = m;
+  *sum = s;
+}
+
+/* Inverse CDF over non-negative weights w (total s): the first v whose
+ * running sum exceeds u * s; the last positive weight if rounding leaves
+ * none. */
+static int inv_cdf(const float* w, int n, float s, float u) {
+  const float tau = u * s;
+  float c = 0.0f;
+  int last = 0;
+  for (int v = 0; v < n; ++v) {
+    if (w[v] > 0.0f) last = v;
+    c += w[v];
+    if (c > tau) return v;
+  }
+  return last;
+}
+
+static int sample_temp(const float* l, int n, float t, float u, float* scratch) {
+  float mx, s;
+  temp_stats(l, n, t, &mx, &s);
+  for (int v = 0; v < n; ++v) scratch[v] = expf((l[v] - mx) / t);
+  return inv_cdf(scratch, n, s, u);
+}
+
+/* The transformer draft sampling gamma tokens at temperature t; q logits of
+ * every step go to qlog[j * vocab]. */
+int oracle_llama_draft_sample(oracle_llama_draft* d, const uint32_t* ctx, int n, int gamma,
+                              float t, uint64_t seed, uint32_t round, uint32_t* out,
+                              float* qlog) {
+  if (n <= 0 || gamma <= 0) return 0;
+  if (n + gamma > d->kv->cap) return 0;
+  const int V = d->m->vocab;
+  float* w = (float*)malloc(sizeof(float) * (size_t)V);
+  int p = 0;
+  while (p < d->kv->len && p < n && d->cached[p] == ctx[p]) ++p;
+  if (p > n - 1) p = n - 1;
+  oracle_kv_truncate(d->kv, p);
+  for (int i = p; i < n; ++i) draft_step(d, ctx[i]);
+  for (int j = 0; j < gamma; ++j) {
+    memcpy(qlog + (size_t)j * V, d->logits, sizeof(float) * (size_t)V);
+    out[j] = (uint32_t)sample_temp(d->logits, V, t, oracle_philox_uniform(seed, round, (uint32_t)j), w);
+    if (j + 1 < gamma) draft_step(d, out[j]);
+  }
+  free(w);
+  return gamma;
+}
+
+/* speculative_generate with a sampling transformer draft.  accept_mode 0:
+ * accept draft x at position j when u < p_j(x) / q_j(x), else emit a sample
+ * of max(0, p_j - q_j) and end the round; accept_mode 1 (the reference's
+ * rule, generate.rs:695-726): accept when the target's own sample at j equals
+ * x, else emit that sample.  Round structure, prime (quirk Q1), budget check
+ * and bonus as oracle_speculative_generate. */
+int oracle_speculative_sample(const oracle_model* m, oracle_llama_draft* drafter,
+                              const uint32_t* prompt, int n_prompt, const oracle_gen_cfg* cfg,
+                              int accept_mode, uint32_t* out, int cap, int* accepted,
+                              int* n_rounds, int rounds_cap) {
+  if (n_rounds) *n_rounds = 0;
+  if (n_prompt <= 0 || cfg->gamma <= 0 || cfg->temperature <= 0.0f) return 0;
+  const int gamma = cfg->gamma, V = m->vocab;
+  const float t = cfg->temperature;
+  const int tcap = n_prompt + cfg->max_tokens + gamma + 2;
+  uint32_t* tok = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)tcap);
+  memcpy(tok, prompt, sizeof(uint32_t) * (size_t)n_prompt);
+  int len = n_prompt;
+  const int prompt_len = n_prompt;
+  oracle_kv* kv = oracle_kv_new(m->n_layers, m->n_kv_heads * m->head_dim, tcap + 1);
+  float* logits = (float*)malloc(sizeof(float) * (size_t)V);
+  float* qlog = (float*)malloc(sizeof(float) * (size_t)V * (size_t)gamma);
+  float* w = (float*)malloc(sizeof(float) * (size_t)V);
+  float* e = (float*)malloc(sizeof(float) * (size_t)m->hidden);
+  uint32_t* draft = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)gamma);
+  for (int i = 0; i < n_prompt; ++i) {
+    oracle_token_embedding(m, prompt[i], e);
+    oracle_forward(m, e, kv, logits);
+  }
+  int rounds = 0;
+  while (len - prompt_len < cfg->max_tokens) {
+    if (is_cancelled(cfg)) break;
+    const uint32_t r = (uint32_t)rounds;
+    oracle_llama_draft_sample(drafter, tok, len, gamma, t, cfg->seed, r, draft, qlog);
+    int acc = 0;
+    for (int j = 0; j < gamma; ++j) {
+      oracle_token_embedding(m, tok[len - 1], e);
+      oracle_forward(m, e, kv, logits);
+      const float u_res = oracle_philox_uniform(cfg->seed, r, 64u + (uint32_t)j);
+      if (accept_mode == 1) {
+        const int y = sample_temp(logits, V, t, u_res, w);
+        if ((uint32_t)y == draft[j]) {
+          tok[len++] = draft[j];
+          acc++;
+          continue;
+        }
+        tok[len++] = (uint32_t)y;
+        break;
+      }
+      float mp, sp, mq, sq;
+      temp_stats(logits, V, t, &mp, &sp);
+      const float* q = qlog + (size_t)j * V;
+      temp_stats(q, V, t, &mq, &sq);
+      const uint32_t x = draft[j];
+      const float ep = expf((logits[x] - mp) / t), eq = expf((q[x] - mq) / t);
+      const float u = oracle_philox_uniform(cfg->seed, r, 32u + (uint32_t)j);
+      if (u * eq * sp < ep * sq) {
+        tok[len++] = x;
+        acc++;
+        continue;
+      }
+      float rs = 0.0f;
+      for (int v = 0; v < V; ++v) {
+        const float pv = expf((logits[v] - mp) / t) / sp, qv = expf((q[v] - mq) / t) / sq;
+        w[v] = fmaxf(pv - qv, 0.0f);
+        rs += w[v];
+      }
+      int y;
+      if (rs > 0.0f) {
+        y = inv_cdf(w, V, rs, u_res);
+      } else {
+        y = sample_temp(logits, V, t, u_res, w);
+      }
+      tok[len++] = (uint32_t)y;
+      break;
+    }
+    if (cfg->bonus && acc == gamma) {
+      oracle_token_embedding(m, tok[len - 1], e);
+      oracle_forward(m, e, kv, logits);
+      const float u = oracle_philox_uniform(cfg->seed, r, 64u + (uint32_t)gamma);
+      tok[len++] = (uint32_t)sample_temp(logits, V, t, u, w);
+    }
+    if (accepted && rounds < rounds_cap) accepted[rounds] = acc;
+    rounds++;
+  }
+  const int gen = len - prompt_len;
+  const int ncopy = gen < cap ? gen : cap;
+  memcpy(out, tok + prompt_len, sizeof(uint32_t) * (size_t)ncopy);
+  if (n_rounds) *n_rounds = rounds;
+  oracle_kv_free(kv);
+  free(logits); free(qlog); free(w); free(e); free(draft); free(tok);
+  return ncopy;
+}

@@ -111,6 +111,12 @@ def lib():
             C.POINTER(Model), C.c_int, C.c_void_p, _u32p, C.c_int,
             C.POINTER(GenCfg), _u32p, C.c_int, C.POINTER(C.c_int),
             C.POINTER(C.c_int), C.c_int]
+        L.oracle_philox4x32_10.argtypes = [_u32p, _u32p, _u32p]
+        L.oracle_philox_uniform.restype = C.c_float
+        L.oracle_philox_uniform.argtypes = [C.c_uint64, C.c_uint32, C.c_uint32]
+        L.oracle_speculative_sample.argtypes = [
+            C.POINTER(Model), C.c_void_p, _u32p, C.c_int, C.POINTER(GenCfg), C.c_int, _u32p,
+            C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_int]
         _lib = L
     return _lib
 
@@ -378,6 +384,35 @@ class OracleModel:
                                               len(prompt), C.byref(cfg), u32ptr(out), cap,
                                               acc, C.byref(nr), cap + 1)
         return out[:n].tolist(), [acc[i] for i in range(min(nr.value, cap + 1))]
+
+
+    def speculative_sample(self, prompt, max_tokens, gamma, draft, temperature, seed,
+                           accept_mode=0, bonus=False):
+        """Stochastic speculative decoding with a sampling transformer draft
+        (accept_mode 0: min(1, p/q) with residual resampling; 1: the
+        reference's target-sample == draft rule).  Returns (tokens, accepted)."""
+        prompt = np.ascontiguousarray(np.asarray(prompt, np.uint32))
+        cfg = self._cfg(max_tokens, temperature, gamma, seed, 0.0, 0.0, 0, int(bonus))
+        cap = max_tokens + gamma + 2
+        out = np.zeros(cap, np.uint32)
+        acc = (C.c_int * (cap + 1))()
+        nr = C.c_int()
+        n = lib().oracle_speculative_sample(C.byref(self.m), draft.handle, u32ptr(prompt),
+                                            len(prompt), C.byref(cfg), accept_mode,
+                                            u32ptr(out), cap, acc, C.byref(nr), cap + 1)
+        return out[:n].tolist(), [acc[i] for i in range(min(nr.value, cap + 1))]
+
+
+def philox4x32_10(ctr, key):
+    c = np.ascontiguousarray(np.asarray(ctr, np.uint32))
+    k = np.ascontiguousarray(np.asarray(key, np.uint32))
+    o = np.zeros(4, np.uint32)
+    lib().oracle_philox4x32_10(u32ptr(c), u32ptr(k), u32ptr(o))
+    return o.tolist()
+
+
+def philox_uniform(seed, rnd, slot):
+    return float(lib().oracle_philox_uniform(seed, rnd, slot))
 
 
 class OracleKV:
