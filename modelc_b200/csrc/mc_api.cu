@@ -653,7 +653,12 @@ struct mc_session {
   cudaGraphExec_t verify_exec = nullptr;
   int round_launches = 0;
   int bps[2][5][7] = {};
+  // MC_TRACE builds: timeline slots handed to the launches of one capture
+  bool trace_on = false;
+  int trace_next = 0;
 };
+
+static int trace_slot(mc_session* s) { return s->trace_on ? ++s->trace_next : 0; }
 
 static int bps_of(mc_session* s, int epi, int nt, int wf) {
   int& b = s->bps[wf][epi][nt];
@@ -664,11 +669,15 @@ static int bps_of(mc_session* s, int epi, int nt, int wf) {
 // CTAs per GEMV launch.  q4_0 partial sums are f32 and the grid sets their
 // k-split, so a q4_0 grid must not depend on the token count: it uses the
 // smallest occupancy over all token tiles.
+#ifndef MC_GEMV_MAX_BPS
+#define MC_GEMV_MAX_BPS 0  // 0: as many CTAs per SM as occupancy allows
+#endif
 template <class BpsFn>
 static int gemv_grid(const PMat& W, int nsm, int nt, BpsFn bps) {
   int b = bps(nt);
   if (W.fmt == WF_Q4)
     for (int t : {1, 2, 3, 6}) b = std::min(b, bps(t));
+  if (MC_GEMV_MAX_BPS > 0) b = std::min(b, MC_GEMV_MAX_BPS);
   return std::min(W.n_stripes, nsm * std::max(b, 1));
 }
 
@@ -886,11 +895,16 @@ static mc_status enq_quant(mc_session* s, const float* h, int ld, int d, int M, 
   q.KB = (d + 31) / 32;
   q.nt = nt_for_tokens(M);
   q.xexp = s->xexp;
+  q.trace_slot = trace_slot(s);
   CK(launch_quant(q, s->stream, true));
   return MC_OK;
 }
 
-constexpr long long kNextPrefetch = 24ll << 20;  // L2 bytes warmed for the next GEMV
+#ifndef MC_NEXT_PREFETCH_MB
+#define MC_NEXT_PREFETCH_MB 24
+#endif
+// L2 bytes of the next GEMV's weights warmed by the running one
+constexpr long long kNextPrefetch = (long long)MC_NEXT_PREFETCH_MB << 20;
 
 static mc_status enq_gemv(mc_session* s, const PMat& W, int epi, int M, GemvArgs a,
                           const PMat* next = nullptr) {
@@ -912,6 +926,7 @@ static mc_status enq_gemv(mc_session* s, const PMat& W, int epi, int M, GemvArgs
   a.ws = s->ws;
   a.cnt = s->cnt;
   a.err = s->err;
+  a.trace_slot = trace_slot(s);
   const int nt = nt_for_tokens(M);
   const int grid = gemv_grid(W, s->nsm, nt, [&](int t) { return bps_of(s, epi, t, W.fmt); });
   CK(launch_gemv(a, epi, nt, W.fmt, grid, s->stream, true));
@@ -952,6 +967,7 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
   ea.st_np = 1;
   ea.st_amax = slot(0);
   ea.st_w = enc_w[0];
+  ea.trace_slot = trace_slot(s);
   CK(launch_embed(ea, s->stream, true));
   int prod_np = 1;  // sum-of-squares partials written by the last h producer
   // residual producers fill st_* for the encoder that follows them
@@ -994,6 +1010,7 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       a.page = kPage;
       a.sq = Lw.sq;
       a.sk = Lw.sk;
+      a.kv_prefetch = 1;
       CKS(enq_gemv(s, Lw.qkv, EPI_QKV, M, a, nxt()));
       AttnArgs t{};
       t.q = s->qb;
@@ -1014,6 +1031,7 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       t.cnt = s->acnt;
       t.out = s->attn;
       t.st_amax = slot(ej);
+      t.trace_slot = trace_slot(s);
       CK(launch_attention(t, s->stream, true));
       io = io_for(ej, 0);
       CKS(enq_quant(s, s->attn, W->H * W->hdp, W->H * W->hdp, M, nullptr, 0.0f, 0, &io));
@@ -1155,7 +1173,12 @@ static mc_status enq_verify(mc_session* s, float* logits = nullptr) {
 static mc_status capture_verify(mc_session* s) {
   if (s->verify_exec) return MC_OK;
   CK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+#ifdef MC_TRACE
+  s->trace_on = true;
+  s->trace_next = 0;
+#endif
   mc_status rc = enq_verify(s);
+  s->trace_on = false;
   cudaGraph_t graph = nullptr;
   cudaError_t e = cudaStreamEndCapture(s->stream, &graph);
   if (rc != MC_OK) {
@@ -1568,3 +1591,12 @@ extern "C" mc_status mc_linear_run_static(mc_linear* l, const float* x_dev, int3
   }
   return MC_OK;
 }
+
+#ifdef MC_TRACE
+// Timeline of the verify graph's launches (trace builds only; not part of
+// the public header).
+extern "C" MC_API int32_t mc_trace_reset(void) { return trace_reset() == cudaSuccess ? MC_OK : MC_E_CUDA; }
+extern "C" MC_API int32_t mc_trace_read(unsigned long long* out, int32_t n) {
+  return trace_read(out, n) == cudaSuccess ? MC_OK : MC_E_CUDA;
+}
+#endif

@@ -103,6 +103,8 @@ struct GemvArgs {
   const float* rope_sin;
   int half_p, hdp, H, Hkv, page;
   int sq, sk;            // Q and K stripe counts
+  int kv_prefetch;       // QKV: warm L2 with this layer's K/V pages for the attention
+  int trace_slot;        // MC_TRACE builds: 1 + timeline slot, 0 = untraced
 };
 
 struct QuantArgs {
@@ -126,6 +128,7 @@ struct QuantArgs {
   int np, np_stride;
   const unsigned* amax;
   unsigned* amax_next;
+  int trace_slot;        // MC_TRACE builds: 1 + timeline slot, 0 = untraced
 };
 
 struct AttnArgs {
@@ -143,6 +146,7 @@ struct AttnArgs {
   int* cnt;              // [Hkv]
   float* out;            // [M][H][hdp]
   unsigned* st_amax;     // max |out| per token (float bits, atomicMax) or nullptr
+  int trace_slot;        // MC_TRACE builds: 1 + timeline slot, 0 = untraced
 };
 
 enum EmbedSrc : int {
@@ -174,6 +178,7 @@ struct EmbedArgs {
   const float* st_w;
   unsigned* st_zero;
   int n_st_zero;
+  int trace_slot;        // MC_TRACE builds: 1 + timeline slot, 0 = untraced
 };
 
 struct SpecState {
@@ -231,6 +236,13 @@ cudaError_t launch_accept_stochastic(SpecState* st, uint32_t* ctx, int* acc_log,
                                      const float* tlog, const float* dlog, int V,
                                      cudaStream_t s, bool pdl);
 constexpr int kSampleMaxVocab = 256 * 1024;  // tiles of 1024 staged in shared memory
+
+// Timeline of traced launches (MC_TRACE builds only): per slot the earliest
+// CTA start, the earliest return from the dependency wait and the latest CTA
+// end, in %globaltimer nanoseconds.
+constexpr int kTraceSlots = 4096;
+cudaError_t trace_reset();
+cudaError_t trace_read(unsigned long long* out, int n);  // n slots x 3 values
 size_t attention_smem_bytes(int G, int M, int hdp, int page);
 size_t gemv_ws_ints_per_stripe(int nt);
 cudaError_t prepare_kernels(size_t quant_smem, size_t attn_smem);

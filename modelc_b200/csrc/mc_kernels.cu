@@ -21,6 +21,97 @@
 
 namespace mc {
 
+// ------------------------------------------------------------ tracing
+#ifdef MC_TRACE
+struct TraceRec {
+  unsigned long long start, waited, end;
+};
+__device__ TraceRec g_trace[kTraceSlots];
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#define MC_TRACE_T0                          \
+  const unsigned long long mc_t0 = gtimer(); \
+  unsigned long long mc_tp = mc_t0;          \
+  (void)mc_tp;
+// per-phase time summed over CTAs (divide by the CTAs that reached it)
+__device__ unsigned long long g_phase[kTraceSlots][8];
+__device__ unsigned int g_phase_n[kTraceSlots][8];
+#define MC_TRACE_PHASE(ts, k, tprev)                                   \
+  do {                                                                 \
+    if ((ts) > 0 && threadIdx.x == 0) {                                \
+      const unsigned long long tn = gtimer();                          \
+      atomicAdd(&g_phase[(ts) - 1][k], tn - (tprev));                  \
+      atomicAdd(&g_phase_n[(ts) - 1][k], 1u);                          \
+      (tprev) = tn;                                                    \
+    }                                                                  \
+  } while (0)
+#define MC_TRACE_WAITED(ts)                                 \
+  do {                                                      \
+    if ((ts) > 0 && threadIdx.x == 0) {                     \
+      atomicMin(&g_trace[(ts) - 1].start, mc_t0);           \
+      atomicMin(&g_trace[(ts) - 1].waited, gtimer());       \
+    }                                                       \
+  } while (0)
+// called by every thread of the CTA at a common exit point
+#define MC_TRACE_END(ts)                                                    \
+  do {                                                                      \
+    __syncthreads();                                                        \
+    if ((ts) > 0 && threadIdx.x == 0) atomicMax(&g_trace[(ts) - 1].end, gtimer()); \
+  } while (0)
+#else
+#define MC_TRACE_T0
+#define MC_TRACE_WAITED(ts) \
+  do {                      \
+  } while (0)
+#define MC_TRACE_END(ts) \
+  do {                   \
+  } while (0)
+#define MC_TRACE_PHASE(ts, k, tprev) \
+  do {                               \
+  } while (0)
+#endif
+
+cudaError_t trace_reset() {
+#ifdef MC_TRACE
+  static TraceRec h[kTraceSlots];
+  static unsigned long long z[kTraceSlots][8];
+  static unsigned int zn[kTraceSlots][8];
+  for (auto& r : h) r = TraceRec{~0ull, ~0ull, 0ull};
+  cudaError_t e = cudaMemcpyToSymbol(g_phase, z, sizeof(z));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_phase_n, zn, sizeof(zn));
+  if (e != cudaSuccess) return e;
+  return cudaMemcpyToSymbol(g_trace, h, sizeof(h));
+#else
+  return cudaErrorNotSupported;
+#endif
+}
+
+cudaError_t trace_read(unsigned long long* out, int n) {
+#ifdef MC_TRACE
+  if (n > kTraceSlots) n = kTraceSlots;
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_trace, (size_t)n * sizeof(TraceRec));
+  if (e != cudaSuccess) return e;
+  // then per slot 8 phase sums and 8 counts
+  static unsigned long long ph[kTraceSlots][8];
+  static unsigned int pn[kTraceSlots][8];
+  e = cudaMemcpyFromSymbol(ph, g_phase, sizeof(ph));
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(pn, g_phase_n, sizeof(pn));
+  for (int i = 0; i < n && e == cudaSuccess; ++i)
+    for (int k = 0; k < 8; ++k) {
+      out[3 * n + 16 * i + k] = ph[i][k];
+      out[3 * n + 16 * i + 8 + k] = pn[i][k];
+    }
+  return e;
+#else
+  (void)out;
+  (void)n;
+  return cudaErrorNotSupported;
+#endif
+}
+
 // ------------------------------------------------------------ PTX helpers
 // Weight stream: read once per forward, so it bypasses L1 and is marked
 // evict-first in L2 (it must not evict the next GEMV's prefetched lines).
@@ -546,6 +637,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   __shared__ int sm_exp[kMaxTokens];
   __shared__ unsigned long long sm_keys[kMaxTokens];
 
+  MC_TRACE_T0
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int s0 = (int)((long long)a.n_stripes * blockIdx.x / gridDim.x);
@@ -613,7 +705,27 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
       }
     }
   }
+  // Warm L2 with the K/V pages the attention after this QKV projection reads
+  // (positions below the ones this grid appends were written by earlier
+  // launches; the position counter is final two launches back).
+  if constexpr (EPI == EPI_QKV) {
+    if (a.kv_prefetch && lane == 2) {
+      const int L = *a.pos_ptr + a.pos_add + a.M;
+      const int np = (L + a.page - 1) / a.page;
+      const long long blk = (long long)a.page * a.hdp;  // floats of one (page, kv head)
+      const long long items = (long long)np * 2 * a.Hkv;
+      const long long nw = (long long)gridDim.x * kGemvWarps;
+      for (long long i = (long long)blockIdx.x * kGemvWarps + warp; i < items; i += nw) {
+        const int pg = (int)(i / (2 * a.Hkv));
+        const int rem = (int)(i - (long long)pg * 2 * a.Hkv);
+        const float* base = (rem & 1) ? a.vc : a.kc;
+        const float* p = base + ((long long)a.page_table[pg] * a.Hkv + (rem >> 1)) * blk;
+        prefetch_l2_bulk(p, (uint32_t)(blk * 4));
+      }
+    }
+  }
   grid_wait();
+  MC_TRACE_WAITED(a.trace_slot);
   if (threadIdx.x < a.M) sm_exp[threadIdx.x] = __ldcg(a.xexp + threadIdx.x);
   __syncthreads();
 
@@ -748,6 +860,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
     if (threadIdx.x < a.M && sm_keys[threadIdx.x])
       atomicMax(a.keys + threadIdx.x, sm_keys[threadIdx.x]);
   }
+  MC_TRACE_END(a.trace_slot);
 }
 
 template <int NT, int EPI, int WF>
@@ -860,8 +973,10 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
   __shared__ int s_e[kMaxTokens];
   __shared__ uint32_t s_bad;
   extern __shared__ float s_x[];
+  MC_TRACE_T0
   grid_launch_dependents();
   grid_wait();
+  MC_TRACE_WAITED(a.trace_slot);
   const StatArgs sa{a.h, a.ld, a.d, a.M, a.w, a.wlen, a.eps, a.do_norm};
   // this CTA's k-blocks
   const int kbs = (a.KB + gridDim.x - 1) / gridDim.x;
@@ -901,6 +1016,7 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
     encode_digits(sa, a.nt, kb0, kb1, s_mul, s_e,
                   [&](int m, int k) { return load_act4(a.h, a.ld, a.d, m, k); },
                   [&](size_t wi, uint32_t v) { xq[wi] = v; });
+    MC_TRACE_END(a.trace_slot);
     return;
   }
   // no producer statistics: reduce over the whole vector here, capturing
@@ -919,6 +1035,7 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
                   return r;
                 },
                 [&](size_t wi, uint32_t v) { xq[wi] = v; });
+  MC_TRACE_END(a.trace_slot);
 }
 
 cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl) {
@@ -952,17 +1069,20 @@ cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl) {
 // positions <= pos0 + m.  Scores are dot / sqrt(head_dim) (transformer.rs:
 // 959-966); the softmax subtracts the row max (transformer.rs:985-1000).
 // Pages are combined by the last CTA of each KV head (flash-decoding split).
-constexpr int kAttnThreads = 256;
+constexpr int kAttnThreads = 512;
 
 // RB: query rows per thread (all of them valid: R is a multiple of the
 // number of row groups in both passes, checked by the launcher).
 template <int RB>
-__global__ void __launch_bounds__(kAttnThreads, 2) k_attention(AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads, 1) k_attention(AttnArgs a) {
+  MC_TRACE_T0
   extern __shared__ float smem[];
   __shared__ float s_m[128], s_l[128];
   __shared__ int s_last;
   grid_launch_dependents();
   grid_wait();
+  MC_TRACE_WAITED(a.trace_slot);
+  MC_TRACE_PHASE(a.trace_slot, 0, mc_tp);
   const int kvh = blockIdx.x, chunk = blockIdx.y;
   const int G = a.H / a.Hkv;
   const int R = G * a.M;
@@ -973,7 +1093,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attention(AttnArgs a) {
   const int pos0 = *a.pos_ptr + a.pos_add;
   const int L = pos0 + a.M;
   const int n_chunks = (L + P - 1) / P;
-  if (chunk >= n_chunks) return;
+  if (chunk >= n_chunks) {
+    MC_TRACE_END(a.trace_slot);
+    return;
+  }
   const int t0 = chunk * P;
   const int nt = min(P, L - t0);
   const int ks = hdp + 4;  // K row stride: float4-aligned, conflict-free float4 reads
@@ -1031,6 +1154,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attention(AttnArgs a) {
       reinterpret_cast<float4*>(sv)[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   }
   __syncthreads();
+  MC_TRACE_PHASE(a.trace_slot, 1, mc_tp);
   // scores: thread -> position t and rows rq, rq+RG, ... (RB of them)
   {
     const int t = threadIdx.x % P;
@@ -1063,6 +1187,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attention(AttnArgs a) {
     }
   }
   __syncthreads();
+  MC_TRACE_PHASE(a.trace_slot, 2, mc_tp);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int row = warp; row < Rp; row += blockDim.x >> 5) {
     float mx = -INFINITY;
@@ -1081,6 +1206,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attention(AttnArgs a) {
     if (lane == 0) { s_m[row] = mx; s_l[row] = sum; }
   }
   __syncthreads();
+  MC_TRACE_PHASE(a.trace_slot, 3, mc_tp);
   // P.V: thread -> column c and rows rq, rq+RG, ... ; four positions per step
   const size_t pbase = ((size_t)kvh * a.max_chunks + chunk) * R;
   {
@@ -1111,40 +1237,52 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attention(AttnArgs a) {
     a.part_ml[(pbase + row) * 2] = s_m[row];
     a.part_ml[(pbase + row) * 2 + 1] = s_l[row];
   }
-  __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) s_last = (atomicAdd(a.cnt + kvh, 1) == n_chunks - 1);
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  // combine the pages of this KV head.  All (m_c, l_c) pairs are loaded in
-  // one round; page c contributes e^(m_c - M) * (sum_t e^(s_t - m_c) v_t) to
-  // the numerator and e^(m_c - M) * l_c to the denominator.
-  float* sml = sk;  // reuse the K tile area: [R][n_chunks][2]
-  for (int i = threadIdx.x; i < R * n_chunks; i += blockDim.x) {
-    const int row = i / n_chunks, c = i - row * n_chunks;
-    const float2 v = __ldcg(reinterpret_cast<const float2*>(a.part_ml) +
-                            (((size_t)kvh * a.max_chunks + c) * R + row));
-    sml[2 * i] = v.x;
-    sml[2 * i + 1] = v.y;
+  MC_TRACE_PHASE(a.trace_slot, 4, mc_tp);
+  // the CTA's partials are ordered before its arrival (one fence per CTA);
+  // the last arriver fences again before reading the others' partials
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int last = (atomicAdd(a.cnt + kvh, 1) == n_chunks - 1);
+    if (last) __threadfence();
+    s_last = last;
   }
   __syncthreads();
+  MC_TRACE_PHASE(a.trace_slot, 5, mc_tp);
+  if (!s_last) {
+    MC_TRACE_END(a.trace_slot);
+    return;
+  }
+  // combine the pages of this KV head: one warp per row, lanes over pages
+  // (max_chunks <= 64 = 2 per lane).  Page c contributes
+  // e^(m_c - M) * (sum_t e^(s_t - m_c) v_t) to the numerator and
+  // e^(m_c - M) * l_c to the denominator; fully masked pages (m_c = -inf)
+  // contribute exactly zero.
   float* wgt = ss;  // [R][n_chunks]
-  for (int row = threadIdx.x; row < R; row += blockDim.x) {
-    float M_ = -INFINITY;
-    for (int c = 0; c < n_chunks; ++c) M_ = fmaxf(M_, sml[2 * (row * n_chunks + c)]);
-    float l = 0.0f;
-    for (int c = 0; c < n_chunks; ++c) {
-      const float mc = sml[2 * (row * n_chunks + c)];
-      const float w = (mc == -INFINITY) ? 0.0f : expf(mc - M_);
-      wgt[row * n_chunks + c] = w;
-      l += w * sml[2 * (row * n_chunks + c) + 1];
+  {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float2* ml = reinterpret_cast<const float2*>(a.part_ml) + (size_t)kvh * a.max_chunks * R;
+    for (int row = warp; row < R; row += kAttnThreads / 32) {
+      float2 v0 = make_float2(-INFINITY, 0.0f), v1 = make_float2(-INFINITY, 0.0f);
+      if (lane < n_chunks) v0 = __ldcg(ml + (size_t)lane * R + row);
+      if (lane + 32 < n_chunks) v1 = __ldcg(ml + (size_t)(lane + 32) * R + row);
+      float M_ = fmaxf(v0.x, v1.x);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) M_ = fmaxf(M_, __shfl_xor_sync(0xffffffffu, M_, o));
+      const float w0 = (v0.x == -INFINITY) ? 0.0f : expf(v0.x - M_);
+      const float w1 = (v1.x == -INFINITY) ? 0.0f : expf(v1.x - M_);
+      if (lane < n_chunks) wgt[row * n_chunks + lane] = w0;
+      if (lane + 32 < n_chunks) wgt[row * n_chunks + lane + 32] = w1;
+      float l = __fadd_rn(__fmul_rn(w0, v0.y), __fmul_rn(w1, v1.y));
+#pragma unroll
+      for (int o = 16; o; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
+      if (lane == 0) s_l[row] = l;
     }
-    s_l[row] = l;
   }
   __shared__ uint32_t s_mx[kMaxTokens];  // max |out| per token, float bits
   if (threadIdx.x < kMaxTokens) s_mx[threadIdx.x] = 0u;
   __syncthreads();
+  MC_TRACE_PHASE(a.trace_slot, 6, mc_tp);
   {
     // thread -> 4 columns of one row; pages summed in order with eight
     // float4 loads in flight.  Rp is a multiple of the rows a warp spans, so
@@ -1209,6 +1347,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attention(AttnArgs a) {
     if (threadIdx.x < a.M) atomicMax(a.st_amax + threadIdx.x, s_mx[threadIdx.x]);
   }
   if (threadIdx.x == 0) atomicExch(a.cnt + kvh, 0);
+  MC_TRACE_PHASE(a.trace_slot, 7, mc_tp);
+  MC_TRACE_END(a.trace_slot);
 }
 
 size_t attention_smem_bytes(int G, int M, int hdp, int page) {
@@ -1274,8 +1414,10 @@ cudaError_t prepare_kernels(size_t quant_smem, size_t attn_smem) {
 
 // ------------------------------------------------------------ embedding
 __global__ void __launch_bounds__(256) k_embed(EmbedArgs a) {
+  MC_TRACE_T0
   grid_launch_dependents();
   grid_wait();
+  MC_TRACE_WAITED(a.trace_slot);
   const int m = blockIdx.x;
   uint32_t id;
   switch (a.src) {
@@ -1332,6 +1474,7 @@ __global__ void __launch_bounds__(256) k_embed(EmbedArgs a) {
       a.st_amax[m] = u;
     }
   }
+  MC_TRACE_END(a.trace_slot);
 }
 
 cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t s, bool pdl) {
