@@ -864,12 +864,39 @@ static mc_status check_err(int* err) {
   return MC_OK;
 }
 
+#ifndef MC_NEXT_PREFETCH_MB
+#define MC_NEXT_PREFETCH_MB 24
+#endif
+// L2 bytes of the next GEMV's weights warmed by the running one
+constexpr long long kNextPrefetch = (long long)MC_NEXT_PREFETCH_MB << 20;
+// Kernels that leave HBM idle (attention, encoders) warm L2 with the part of
+// an upcoming GEMV's weights beyond what the GEMV before it prefetches.
+#ifndef MC_IDLE_PREFETCH_MB
+#define MC_IDLE_PREFETCH_MB 32
+#endif
+constexpr long long kIdlePrefetch = (long long)MC_IDLE_PREFETCH_MB << 20;
+
+static long long packed_bytes(const PMat& W) {
+  return (long long)W.n_stripes * W.KB * (W.fmt == WF_Q4 ? kFragBytes / 2 : kFragBytes);
+}
+// [kNextPrefetch, kNextPrefetch + cap) of W's packed codes, clipped
+static void idle_prefetch(const PMat* W, long long cap, const void** p, long long* bytes) {
+  *p = nullptr;
+  *bytes = 0;
+  if (!W || !W->w || cap <= 0) return;
+  const long long total = packed_bytes(*W);
+  if (total <= kNextPrefetch) return;
+  *p = reinterpret_cast<const char*>(W->w) + kNextPrefetch;
+  *bytes = std::min(total - kNextPrefetch, cap);
+}
+
 // Statistics an encoder takes from its producer (see QuantArgs).
 struct StatIO {
   const float* pss;
   int np;
   const unsigned* amax;
   unsigned* amax_next;
+  const PMat* pf = nullptr;  // upcoming GEMV to warm in L2 (idle_prefetch)
 };
 
 static mc_status enq_quant(mc_session* s, const float* h, int ld, int d, int M, const float* w,
@@ -882,6 +909,7 @@ static mc_status enq_quant(mc_session* s, const float* h, int ld, int d, int M, 
     q.np_stride = io->np;
     q.amax = io->amax;
     q.amax_next = io->amax_next;
+    idle_prefetch(io->pf, kIdlePrefetch, &q.pf, &q.pf_bytes);
   }
   q.h = h;
   q.ld = ld;
@@ -900,11 +928,8 @@ static mc_status enq_quant(mc_session* s, const float* h, int ld, int d, int M, 
   return MC_OK;
 }
 
-#ifndef MC_NEXT_PREFETCH_MB
-#define MC_NEXT_PREFETCH_MB 24
-#endif
-// L2 bytes of the next GEMV's weights warmed by the running one
-constexpr long long kNextPrefetch = (long long)MC_NEXT_PREFETCH_MB << 20;
+
+
 
 static mc_status enq_gemv(mc_session* s, const PMat& W, int epi, int M, GemvArgs a,
                           const PMat* next = nullptr) {
@@ -961,7 +986,7 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
   size_t ej = 0;  // next encoder
   auto slot = [&](size_t j) { return s->st_amax + (j & 1) * kMaxTokens; };
   auto io_for = [&](size_t j, int np) {
-    return StatIO{s->st_pss, np, slot(j), slot(j + 1)};
+    return StatIO{s->st_pss, np, slot(j), slot(j + 1), nullptr};
   };
   ea.st_pss = s->st_pss;
   ea.st_np = 1;
@@ -1031,6 +1056,8 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       t.cnt = s->acnt;
       t.out = s->attn;
       t.st_amax = slot(ej);
+      // the gate/up projection after O: its weights beyond the O GEMV's prefetch
+      idle_prefetch(Lw.mlp ? &Lw.gu : nullptr, kIdlePrefetch, &t.pf, &t.pf_bytes);
       t.trace_slot = trace_slot(s);
       CK(launch_attention(t, s->stream, true));
       io = io_for(ej, 0);
@@ -1054,6 +1081,7 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       g.st_amax = slot(ej);
       CKS(enq_gemv(s, Lw.gu, EPI_SWIGLU, M, g, nxt()));
       io = io_for(ej, 0);
+      io.pf = &Lw.down;  // the down weights beyond the gate/up GEMV's prefetch
       CKS(enq_quant(s, s->act, F, F, M, nullptr, 0.0f, 0, &io));
       ++ej;
       GemvArgs dn{};

@@ -128,6 +128,8 @@ struct QuantArgs {
   int np, np_stride;
   const unsigned* amax;
   unsigned* amax_next;
+  const void* pf;        // L2 prefetch of upcoming weights, or nullptr
+  long long pf_bytes;
   int trace_slot;        // MC_TRACE builds: 1 + timeline slot, 0 = untraced
 };
 
@@ -146,6 +148,8 @@ struct AttnArgs {
   int* cnt;              // [Hkv]
   float* out;            // [M][H][hdp]
   unsigned* st_amax;     // max |out| per token (float bits, atomicMax) or nullptr
+  const void* pf;        // L2 prefetch of upcoming weights while HBM is idle, or nullptr
+  long long pf_bytes;
   int trace_slot;        // MC_TRACE builds: 1 + timeline slot, 0 = untraced
 };
 

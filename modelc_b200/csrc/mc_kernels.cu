@@ -168,6 +168,19 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) 
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes)
                : "memory");
 }
+// This CTA's share of an L2 prefetch of `bytes` at p (16-byte multiples,
+// 32 KB per instruction), issued by one thread.
+__device__ __forceinline__ void prefetch_share(const void* p, long long bytes, int cta, int n_ctas) {
+  const long long share = (bytes / n_ctas) & ~15ll;
+  if (share < 16) return;
+  const char* q = reinterpret_cast<const char*>(p) + share * cta;
+  for (long long left = share; left >= 16;) {
+    const uint32_t b = (uint32_t)min(left, 32768ll) & ~15u;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(q), "r"(b) : "memory");
+    q += b;
+    left -= b;
+  }
+}
 __device__ __forceinline__ void red_add(int* p, int v) {
   asm volatile("red.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -739,6 +752,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
     int stripe, k0, k1;
     unit_range(u, stripe, k0, k1);
     const int n = k1 - k0;
+
     if (n <= 0) {  // empty k-range (K shorter than the split): contributes nothing
       pre = false;
       continue;
@@ -974,6 +988,7 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
   __shared__ uint32_t s_bad;
   extern __shared__ float s_x[];
   MC_TRACE_T0
+  if (a.pf && threadIdx.x == 0) prefetch_share(a.pf, a.pf_bytes, blockIdx.x, gridDim.x);
   grid_launch_dependents();
   grid_wait();
   MC_TRACE_WAITED(a.trace_slot);
@@ -1079,6 +1094,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attention(AttnArgs a) {
   extern __shared__ float smem[];
   __shared__ float s_m[128], s_l[128];
   __shared__ int s_last;
+  if (a.pf && threadIdx.x == 0)
+    prefetch_share(a.pf, a.pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
   grid_launch_dependents();
   grid_wait();
   MC_TRACE_WAITED(a.trace_slot);
