@@ -647,7 +647,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
       reinterpret_cast<Acc (*)[16 * COLS]>(gemv_smem + kGemvWarps * 16 * (COLS + 1));
   __shared__ int sm_cnt[kTileSlots];
   __shared__ float sm_scale[kMaxCtaStripes * 16];
-  __shared__ int sm_exp[kMaxTokens];
+  __shared__ int sm_exp[kGemvWarps][kMaxTokens];  // per warp: filled at its first epilogue
   __shared__ unsigned long long sm_keys[kMaxTokens];
 
   MC_TRACE_T0
@@ -737,10 +737,20 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
       }
     }
   }
+  __syncthreads();  // shared tiles, counters and scales are initialised
   grid_wait();
   MC_TRACE_WAITED(a.trace_slot);
-  if (threadIdx.x < a.M) sm_exp[threadIdx.x] = __ldcg(a.xexp + threadIdx.x);
-  __syncthreads();
+  // The token exponents are only needed by the epilogue: issue the load now,
+  // consume it there, so its L2 round trip overlaps the first batches.
+  const int xe = lane < a.M ? __ldcg(a.xexp + lane) : 0;
+  bool xe_staged = false;
+  auto stage_exp = [&]() {
+    if (!xe_staged) {
+      if (lane < kMaxTokens) sm_exp[warp][lane] = xe;
+      __syncwarp();
+      xe_staged = true;
+    }
+  };
 
   unsigned long long kmax[(8 * kMaxTokens) / 32];
 #pragma unroll
@@ -802,7 +812,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
         sm_epi[warp][g + 8][t * 8 + 2 * tq + 1] = acc[t][3];
       }
       __syncwarp();
-      gemv_epilogue<NT, EPI>(a, stripe, &sm_epi[warp][0][0], COLS + 1, lane, kmax, scl, sm_exp);
+      stage_exp();
+      gemv_epilogue<NT, EPI>(a, stripe, &sm_epi[warp][0][0], COLS + 1, lane, kmax, scl,
+                             sm_exp[warp]);
       __syncwarp();
     } else {
       // F <= 8 and ns < 8, so a stripe's slot is its index in the CTA
@@ -847,10 +859,12 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
             sm_epi[warp][i / COLS][i % COLS] = v;
           }
           __syncwarp();
+          stage_exp();
           gemv_epilogue<NT, EPI>(a, stripe, &sm_epi[warp][0][0], COLS + 1, lane, kmax, scl,
-                                 sm_exp);
+                                 sm_exp[warp]);
         } else {
-          gemv_epilogue<NT, EPI>(a, stripe, sm_tile[slot], COLS, lane, kmax, scl, sm_exp);
+          stage_exp();
+          gemv_epilogue<NT, EPI>(a, stripe, sm_tile[slot], COLS, lane, kmax, scl, sm_exp[warp]);
         }
       }
       __syncwarp();
@@ -999,6 +1013,7 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
   const int lo = kb0 * 32, hi = kb0 * 32 + max(kb1 - kb0, 0) * 32;
   uint32_t* xq = reinterpret_cast<uint32_t*>(a.xq);
   if (a.use_stats) {
+    auto src4 = [&](int m, int k) { return load_act4(a.h, a.ld, a.d, m, k); };
     // statistics from the producing kernel: one warp per token sums the
     // partials in a fixed order (lane-strided, then an xor-shuffle tree)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1028,8 +1043,7 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
     if (blockIdx.x == 0 && a.amax_next && threadIdx.x < kMaxTokens) a.amax_next[threadIdx.x] = 0u;
     __syncthreads();
     if (blockIdx.x == 0 && threadIdx.x < a.M) a.xexp[threadIdx.x] = s_e[threadIdx.x];
-    encode_digits(sa, a.nt, kb0, kb1, s_mul, s_e,
-                  [&](int m, int k) { return load_act4(a.h, a.ld, a.d, m, k); },
+    encode_digits(sa, a.nt, kb0, kb1, s_mul, s_e, src4,
                   [&](size_t wi, uint32_t v) { xq[wi] = v; });
     MC_TRACE_END(a.trace_slot);
     return;
