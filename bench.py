@@ -19,8 +19,10 @@ the GPU.  Inputs (7.5 GB of weights) exceed the 126 MB L2 on every step.
 
 ``--impl reference`` times the reference's CPU algorithm (the oracle's
 bit-identical row-parallel linear on all host cores) on the same workload.
-Multi-GPU (torchrun): independent replicas, one request per GPU (weak
-scaling); value = tokens of all ranks / max-over-ranks time.
+Multi-GPU (torchrun, N ranks): one request with the target tensor-parallel
+over the N GPUs (NCCL all-reduce after each row-parallel projection; strong
+scaling), value = that request's tokens / max-over-ranks time.  --replicas
+instead runs N independent requests (weak scaling).
 """
 from __future__ import annotations
 
@@ -39,6 +41,40 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "spec-decode tokens/s, 8B-shape int8 bs1; verify-kernel HBM GB/s vs 8 TB/s"
 PROMPT_LEN, NEW_TOKENS, GAMMA = 1024, 256, 4
 WORKLOAD = "llama3-8b-shape int8-row target + 2-layer int8 draft, bs1, prompt 1024, gamma 4, greedy, 256 new"
+
+
+class Workload:
+    """One speculative-decoding benchmark configuration (shapes, formats,
+    seeds and run lengths of the reference's benchmark table)."""
+
+    def __init__(self, name, metric, desc, target, draft, fmt, draft_fmt, prompt_len, new_tokens,
+                 gamma, temperature=0.0, seed=0, accept_mode=0):
+        self.name, self.metric, self.desc = name, metric, desc
+        self.target, self.draft = target, draft
+        self.fmt, self.draft_fmt = fmt, draft_fmt
+        self.prompt_len, self.new_tokens, self.gamma = prompt_len, new_tokens, gamma
+        self.temperature, self.seed, self.accept_mode = temperature, seed, accept_mode
+
+
+def workloads():
+    from dataclasses import replace
+    import modelc_b200 as mb
+    return {
+        "llama3-8b": Workload("llama3-8b", METRIC, WORKLOAD, mb.LLAMA3_8B,
+                              mb.LLAMA3_8B.with_layers(2), "i8_row", "i8_row", PROMPT_LEN,
+                              NEW_TOKENS, GAMMA),
+        "tinyllama": Workload(
+            "tinyllama", "spec-decode tokens/s, TinyLlama-1.1B-shape q4_0 bs1, stochastic T=0.8",
+            "tinyllama-1.1b-shape q4_0 target + 2-layer q4_0 draft, bs1, prompt 512, gamma 5, "
+            "min(1,p/q) acceptance at T=0.8 (top-p off, Philox seed 7), 256 new",
+            mb.TINYLLAMA, mb.TINYLLAMA.with_layers(2), "q4_0", "q4_0", 512, 256, 5,
+            temperature=0.8, seed=7),
+        "llama2-70b": Workload(
+            "llama2-70b", "spec-decode tokens/s, 70B-shape q4_0 bs1 (1 GPU)",
+            "llama2-70b-shape q4_0 target + llama3-8b-shape int8 draft (vocab 32000), bs1, "
+            "prompt 2048, gamma 4, greedy, 256 new",
+            mb.LLAMA2_70B, replace(mb.LLAMA3_8B, vocab=32000), "q4_0", "i8_row", 2048, 256, 4),
+    }
 
 
 def dist_env():
@@ -112,15 +148,16 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------- CPU
-def cpu_sample(n_threads: int, kv_len: int = 1100):
-    """Time the CPU oracle on a bounded sample of the workload: one target
-    decoder layer and the LM head (f32 dequantized weights, as the reference
-    holds them) for a single-token forward at KV length ~1100, repeated.
-    Per-token cost extrapolates to 32 target layers + head per verify
-    forward plus gamma 2-layer+head draft forwards per round."""
+def cpu_sample(n_threads: int, kv_len: int = 1100, cfg=None):
+    """Time the CPU oracle on a bounded sample of the workload: one decoder
+    layer of `cfg` and its LM head (f32 dequantized weights, as the reference
+    holds them) for a single-token forward at KV length kv_len, repeated.
+    Per-token cost extrapolates to the target's layers + head per verify
+    forward plus gamma draft forwards per round."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as o
-    from modelc_b200.model import LLAMA3_8B as cfg
+    if cfg is None:
+        from modelc_b200.model import LLAMA3_8B as cfg
     rng = np.random.default_rng(0)
     d, f, v = cfg.hidden, cfg.ffn, cfg.vocab
     hd, nh, nkv = cfg.head_dim, cfg.n_heads, cfg.n_kv_heads
@@ -160,48 +197,68 @@ def cpu_sample(n_threads: int, kv_len: int = 1100):
     return t_layer, t_head, reps_l, reps_h
 
 
-def cpu_tokens_per_s(t_layer, t_head, rounds, tokens, accepted):
-    """Reference cost model: per round gamma draft forwards (2 layers + head)
-    and the sequential verify's target forwards (min(a+1, gamma) per round,
-    generate.rs:695-726); tokens = emitted tokens."""
-    t_draft = 2 * t_layer + t_head
-    t_target = 32 * t_layer + t_head
-    target_fwd = sum(min(a + 1, GAMMA) for a in accepted) if accepted else rounds
-    total = rounds * GAMMA * t_draft + target_fwd * t_target
+def cpu_tokens_per_s(t_layer, t_head, rounds, tokens, accepted, gamma=GAMMA, target_layers=32,
+                     draft_layers=2, t_draft_layer=None, t_draft_head=None):
+    """Reference cost model: per round gamma draft forwards (draft layers +
+    head) and the sequential verify's target forwards (min(a+1, gamma) per
+    round, generate.rs:695-726); tokens = emitted tokens."""
+    t_draft = draft_layers * (t_draft_layer if t_draft_layer is not None else t_layer) + (
+        t_draft_head if t_draft_head is not None else t_head)
+    t_target = target_layers * t_layer + t_head
+    target_fwd = sum(min(a + 1, gamma) for a in accepted) if accepted else rounds
+    total = rounds * gamma * t_draft + target_fwd * t_target
     return tokens / total
 
 
 # ---------------------------------------------------------------------- GPU
-def build_models(device_index: int, layers: int | None = None):
+def build_models(device_index: int, layers: int | None = None, wl: Workload | None = None,
+                 tp: tuple = (0, 1)):
+    """Random-init weights N(0, 0.02) generated on the GPU (target seed 0,
+    draft seed 1) and a uniform prompt (seed 2).  tp = (rank, world) keeps
+    this rank's tensor-parallel shard of the target; the draft is replicated."""
     import torch
     import modelc_b200 as mb
+    wl = wl or workloads()["llama3-8b"]
     dev = torch.device("cuda", device_index)
-    cfg = mb.LLAMA3_8B if not layers else mb.LLAMA3_8B.with_layers(layers)
-    dcfg = cfg.with_layers(2)
-    tt = mb.synth_weights_torch(cfg, seed=0, device=dev)
-    target = mb.Weights(tt, cfg, device=device_index)
+    cfg = wl.target if not layers else wl.target.with_layers(layers)
+    dcfg = wl.draft
+    tt = mb.synth_weights_torch(cfg, seed=0, device=dev, fmt=wl.fmt)
+    target = mb.Weights(tt, cfg, device=device_index, tp_rank=tp[0], tp_world=tp[1])
     del tt
-    dt = mb.synth_weights_torch(dcfg, seed=1, device=dev)
+    torch.cuda.empty_cache()
+    dt = mb.synth_weights_torch(dcfg, seed=1, device=dev, fmt=wl.draft_fmt)
     draft = mb.Weights(dt, dcfg, device=device_index)
     del dt
     torch.cuda.empty_cache()
     g = torch.Generator(device="cpu")
     g.manual_seed(2)
-    prompt = torch.randint(0, cfg.vocab, (PROMPT_LEN,), generator=g).numpy().astype(np.uint32)
+    prompt = torch.randint(0, cfg.vocab, (wl.prompt_len,), generator=g).numpy().astype(np.uint32)
     return cfg, target, draft, prompt
 
 
 def run_ours(args):
     import torch
     import modelc_b200 as mb
+    wl = workloads()[args.config]
+    PROMPT_LEN, NEW_TOKENS, GAMMA = wl.prompt_len, wl.new_tokens, wl.gamma
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
+    # N > 1: one request, target tensor-parallel over the N GPUs (strong
+    # scaling); --replicas: N independent requests (weak scaling)
+    tp = world > 1 and not args.replicas
     if world > 1:
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
-    cfg, target, draft, prompt = build_models(local)
+    cfg, target, draft, prompt = build_models(local, wl=wl, tp=(rank, world) if tp else (0, 1))
     max_ctx = PROMPT_LEN + NEW_TOKENS + 2 * GAMMA + 8
-    sess = mb.Session(target, draft, gamma=GAMMA, max_context=max_ctx)
+    sess = mb.Session(target, draft, gamma=GAMMA, max_context=max_ctx,
+                      temperature=wl.temperature, seed=wl.seed, accept_mode=wl.accept_mode)
+    if tp:
+        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(mb.tp_unique_id()), dtype=torch.uint8))
+        torch.distributed.broadcast(uid, 0)
+        sess.tp_init(bytes(uid.cpu().numpy().tobytes()), rank, world)
     stream = torch.cuda.ExternalStream(sess.stream_ptr, device=torch.device("cuda", local))
 
     def barrier():
@@ -238,7 +295,8 @@ def run_ours(args):
     n_local = torch.tensor([float(tokens)], device="cuda")
     if world > 1:
         torch.distributed.all_reduce(t_local, op=torch.distributed.ReduceOp.MAX)
-        torch.distributed.all_reduce(n_local, op=torch.distributed.ReduceOp.SUM)
+        if not tp:  # replicas: every rank's tokens; TP: one request's tokens
+            torch.distributed.all_reduce(n_local, op=torch.distributed.ReduceOp.SUM)
     t_total, tok_total = float(t_local.item()), float(n_local.item())
     value = tok_total / t_total
     ms_per_step = t_total * 1e3 / args.steps
@@ -258,15 +316,16 @@ def run_ours(args):
     e1.record(stream)
     torch.cuda.synchronize()
     t_ver = e0.elapsed_time(e1) / 1e3 / n_ver
-    kv_bytes = 2 * cfg.n_layers * (kv_len + vm) * cfg.n_kv_heads * cfg.head_dim * 4
-    act_bytes = 2 * cfg.n_layers * vm * (3 * cfg.hidden + 2 * cfg.ffn) * 4
+    shards = world if tp else 1  # bytes this GPU reads
+    kv_bytes = 2 * cfg.n_layers * (kv_len + vm) * cfg.n_kv_heads * cfg.head_dim * 4 // shards
+    act_bytes = 2 * cfg.n_layers * vm * (3 * cfg.hidden + 2 * cfg.ffn // shards) * 4
     algo = target.streamed_bytes + kv_bytes + act_bytes
     peak, peak_kind = measured_peaks()
     achieved = algo / t_ver / 1e9
     traffic = profile_traffic()
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "traffic": traffic,
-            "peak_source": peak_kind, "kernel": "verify forward (k_gemv + fused kernels, 291 launches)",
+            "peak_source": peak_kind, "kernel": "verify forward (k_gemv + fused kernels)",
             "algorithmic_bytes": algo, "ms": round(t_ver * 1e3, 4)}
 
     # ---- end to end through the C ABI (host buffers, prime included)
@@ -284,34 +343,45 @@ def run_ours(args):
     e2e_local = torch.tensor([statistics.mean(e2e_ms) / 1e3], device="cuda")
     if world > 1:
         torch.distributed.all_reduce(e2e_local, op=torch.distributed.ReduceOp.MAX)
-    e2e_value = len(toks) * world / float(e2e_local.item())
+    e2e_value = len(toks) * (1 if tp else world) / float(e2e_local.item())
 
     line = None
     if rank == 0:
         cpu = None
-        if not args.no_cpu:
+        if not args.no_cpu and world == 1:
             nthr = os.cpu_count() or 1
-            t_layer, t_head, rl, rh = cpu_sample(nthr)
-            cpu = {"value": round(cpu_tokens_per_s(t_layer, t_head, rounds, tokens, accepted), 5),
-                   "unit": "tokens/s", "cores": nthr, "kind": "port",
-                   "sample": (f"oracle row-parallel f32 forward of 1 target layer at KV 1100 "
+            kvl = PROMPT_LEN + 76
+            t_layer, t_head, rl, rh = cpu_sample(nthr, kvl, cfg)
+            same = (wl.draft.hidden, wl.draft.ffn, wl.draft.vocab) == (cfg.hidden, cfg.ffn, cfg.vocab)
+            tdl, tdh = (t_layer, t_head) if same else cpu_sample(nthr, kvl, wl.draft)[:2]
+            v = cpu_tokens_per_s(t_layer, t_head, rounds, tokens, accepted, GAMMA, cfg.n_layers,
+                                 wl.draft.n_layers, tdl, tdh)
+            cpu = {"value": round(v, 5), "unit": "tokens/s", "cores": nthr, "kind": "port",
+                   "sample": (f"oracle row-parallel f32 forward of 1 target layer at KV {kvl} "
                               f"({t_layer * 1e3:.1f} ms, {rl} reps) + LM head ({t_head * 1e3:.1f} ms, "
-                              f"{rh} reps), extrapolated to 32 layers + head per target forward and "
-                              f"{GAMMA} 2-layer drafts per round with this run's acceptance")}
+                              f"{rh} reps), extrapolated to {cfg.n_layers} layers + head per target "
+                              f"forward and {GAMMA} {wl.draft.n_layers}-layer drafts per round with "
+                              f"this run's acceptance")}
         clocks = clk.summary()
+        wbytes = target.streamed_bytes
         line = {
-            "metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
+            "metric": wl.metric, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+            "dtype": "int8" if wl.fmt == "i8_row" else "q4_0",
             "data": "synthetic (random-init weights N(0,0.02), uniform prompt ids)",
-            "config": {"workload": WORKLOAD, "target": cfg.name, "draft_layers": 2,
+            "config": {"workload": wl.desc, "target": cfg.name, "draft_layers": wl.draft.n_layers,
                        "prompt_len": PROMPT_LEN, "new_tokens": NEW_TOKENS, "gamma": GAMMA,
-                       "batch": 1, "parallelism": f"replicas{world}" if world > 1 else "single",
-                       "l2": "inputs larger than L2 (7.5 GB int8 weights per verify)"},
+                       "temperature": wl.temperature, "batch": 1,
+                       "parallelism": (f"tp{world}" if tp else f"replicas{world}") if world > 1
+                       else "single",
+                       "l2": f"inputs larger than L2 ({wbytes / 1e9:.2f} GB of weights per verify)"},
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "includes": "prime (1024-token prefill) + decode"},
+                    "d2h_bytes_per_step": d2h,
+                    "includes": f"prime ({PROMPT_LEN}-token prefill) + decode"},
             "clocks": clocks, "gpu_launches": int(launches * world),
+            "roofline_scope": "per GPU (this rank's weight shard)" if tp else "one GPU",
             "acceptance": {"rounds": rounds, "tokens": tokens,
                            "mean_accepted": round(float(np.mean(accepted)) if accepted else 0.0, 4)},
         }
@@ -346,6 +416,65 @@ def run_profile(args):
     sess.decode(2)
     torch.cuda.synchronize()
     sess.close()
+
+
+def run_sweep(args):
+    """Isolated verify-step projection Y = X . dequant(W)^T through the public
+    mc_linear_run: X is M x 4096 N(0, 1), W is N x 4096 N(0, 0.02) as per-row
+    int8 or q4_0.  Enough weight copies rotate (at least 4, more than L2) that
+    every call streams W from HBM.  Achieved GB/s counts the weight codes and
+    scales once per call plus X and Y; TFLOP/s = 2 M N K / time."""
+    import torch
+    import modelc_b200 as mb
+    from modelc_b200.model import _q4_0_torch
+    torch.cuda.set_device(0)
+    peak, peak_kind = measured_peaks()
+    K = 4096
+    ms_list = [1, 5, 8, 16, 40, 64]
+    for fmt in ("i8_row", "q4_0"):
+        for n in (4096, 14336, 128256):
+            g = torch.Generator(device="cuda")
+            g.manual_seed(n)
+            wb = n * K // 32 * 18 if fmt == "q4_0" else n * K + 4 * n
+            copies = max(4, -(-300_000_000 // wb))
+            lins = []
+            for c in range(copies):
+                w = torch.randn((n, K), generator=g, device="cuda") * 0.02
+                if fmt == "q4_0":
+                    t = ("q4_0", _q4_0_torch(w), (n, K))
+                else:
+                    amax = w.abs().amax(dim=1)
+                    sc = torch.where(amax > 0, amax / 127.0, torch.ones_like(amax))
+                    q = torch.round(w / sc[:, None]).clamp_(-127, 127).to(torch.int8)
+                    t = ("i8_row", q, sc)
+                lins.append(mb.Linear(t))
+                del w, t
+            torch.cuda.empty_cache()
+            for m in ms_list:
+                x = torch.randn((m, K), generator=g, device="cuda")
+                y = torch.empty((m, n), device="cuda")
+                st = torch.cuda.current_stream().cuda_stream
+                for l in lins:
+                    l.run_ptr(x.data_ptr(), m, y.data_ptr(), st)
+                reps = 4 * copies
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for r in range(reps):
+                    lins[r % copies].run_ptr(x.data_ptr(), m, y.data_ptr(), st)
+                e1.record()
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / reps
+                algo = wb + 4 * m * K + 4 * m * n
+                print(json.dumps({"sweep": "projection", "fmt": fmt, "M": m, "N": n, "K": K,
+                                  "us": round(us, 2), "GB_s": round(algo / us / 1e3, 1),
+                                  "hbm_frac": round(algo / us / 1e3 / peak, 3),
+                                  "TFLOP_s": round(2 * m * n * K / us / 1e6, 2),
+                                  "peak_gbs": peak, "peak_source": peak_kind,
+                                  "copies": copies}), flush=True)
+            for l in lins:
+                l.close()
+            del lins
+            torch.cuda.empty_cache()
 
 
 def run_reference(args):
@@ -387,10 +516,18 @@ def main():
     ap.add_argument("--profile", action="store_true", help="short run for ncu launch lists")
     ap.add_argument("--layers", type=int, default=None,
                     help="--profile only: target layers (fewer = smaller device footprint)")
+    ap.add_argument("--config", default="llama3-8b", choices=["llama3-8b", "tinyllama", "llama2-70b"],
+                    help="workload (default: the headline 8B int8 batch-1 configuration)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1: independent requests per GPU instead of tensor parallelism")
+    ap.add_argument("--sweep", action="store_true",
+                    help="isolated quantized-projection sweep (one JSON line per point)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.profile:
+    if args.sweep:
+        run_sweep(args)
+    elif args.profile:
         run_profile(args)
     elif args.impl == "reference":
         run_reference(args)

@@ -74,6 +74,13 @@ typedef struct mc_model_cfg {
   int32_t vocab;
   float rope_theta;   /* GENERAL only */
   float eps;          /* GENERAL only */
+  int32_t tp_rank;    /* tensor parallelism (Megatron): this rank's shard of */
+  int32_t tp_world;   /* tp_world (0 or 1 = no sharding).  Column-parallel
+                         q/k/v (by heads) and gate/up (by FFN rows),
+                         row-parallel o and down (one all-reduce each),
+                         vocab-parallel LM head; embedding and norms
+                         replicated.  Requires n_heads, n_kv_heads, ffn and
+                         vocab divisible by tp_world. */
 } mc_model_cfg;
 
 /* One tensor, as the reference's TensorData {shape, dtype, data}
@@ -171,6 +178,16 @@ MC_API mc_status mc_spec_read(mc_session* s, uint32_t* out, int32_t cap, int32_t
 /* Restart decoding from the primed prompt: the prompt's KV is kept, the
  * generated tokens and round log are dropped. */
 MC_API mc_status mc_spec_rewind(mc_session* s);
+/* Tensor parallelism.  mc_tp_unique_id creates the communicator id on one
+ * rank (the host distributes its 128 bytes to all ranks); every rank then
+ * calls mc_session_tp_init on a session whose target weights were loaded
+ * with tp_world > 1 (the draft stays replicated: tp_world 0 or 1).  The
+ * all-reduces run on the session stream, inside its CUDA graphs.  Greedy
+ * decoding only; every rank computes the same tokens.  NCCL (libnccl.so.2)
+ * is loaded when first needed. */
+MC_API mc_status mc_tp_unique_id(char id_out[128]);
+MC_API mc_status mc_session_tp_init(mc_session* s, const char id[128], int32_t rank,
+                             int32_t world);
 /* Reseed the stochastic rounds (GenerationConfig::seed per request,
  * generate.rs:146-167); applies from the next round. */
 MC_API mc_status mc_spec_set_seed(mc_session* s, uint64_t seed);

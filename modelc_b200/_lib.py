@@ -27,7 +27,7 @@ EXPORTS = [
     "mc_linear_create", "mc_linear_destroy", "mc_linear_run", "mc_linear_weight_bytes",
     "mc_last_error", "mc_version", "mc_spec_rewind", "mc_spec_verify_launch",
     "mc_session_stream", "mc_session_round_launches", "mc_linear_run_static",
-    "mc_spec_set_seed",
+    "mc_spec_set_seed", "mc_tp_unique_id", "mc_session_tp_init",
 ]
 
 
@@ -41,7 +41,7 @@ class ModelCfg(C.Structure):
     _fields_ = [("mode", C.c_int32), ("n_layers", C.c_int32), ("hidden", C.c_int32),
                 ("n_heads", C.c_int32), ("n_kv_heads", C.c_int32), ("head_dim", C.c_int32),
                 ("ffn", C.c_int32), ("vocab", C.c_int32), ("rope_theta", C.c_float),
-                ("eps", C.c_float)]
+                ("eps", C.c_float), ("tp_rank", C.c_int32), ("tp_world", C.c_int32)]
 
 
 class TensorDesc(C.Structure):
@@ -95,6 +95,10 @@ def lib():
         "mc_spec_rewind": (i32, [vp]),
         "mc_spec_verify_launch": (i32, [vp, i32]),
         "mc_spec_set_seed": (i32, [vp, C.c_uint64]),
+        "mc_tp_unique_id": (i32, [C.c_char_p]),
+        "mc_session_tp_init": (i32, [vp, C.c_char_p, i32, i32]),
+        "mc_tp_unique_id": (i32, [C.c_char_p]),
+        "mc_session_tp_init": (i32, [vp, C.c_char_p, i32, i32]),
         "mc_session_stream": (vp, [vp]),
         "mc_session_round_launches": (i32, [vp]),
         "mc_version": (C.c_char_p, []),

@@ -6,6 +6,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <dlfcn.h>
+
 #include <algorithm>
 #include <mutex>
 #include <string>
@@ -97,6 +99,57 @@ struct Allocs {
 
 static inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
+// ------------------------------------------------------------------ NCCL
+// Loaded on first use (tensor parallelism only) from the process's
+// libnccl.so.2, so single-GPU users need no NCCL.  Types restated from the
+// NCCL API: an opaque communicator, a 128-byte unique id, int enums.
+namespace nccl {
+typedef void* Comm;
+struct UniqueId {
+  char internal[128];
+};
+constexpr int kFloat32 = 7, kUint64 = 5, kSum = 0, kMax = 2;
+typedef int (*GetUniqueIdFn)(UniqueId*);
+typedef int (*CommInitRankFn)(Comm*, int, UniqueId, int);
+typedef int (*AllReduceFn)(const void*, void*, size_t, int, int, Comm, cudaStream_t);
+typedef int (*CommDestroyFn)(Comm);
+typedef const char* (*ErrorStringFn)(int);
+struct Api {
+  GetUniqueIdFn get_unique_id = nullptr;
+  CommInitRankFn comm_init_rank = nullptr;
+  AllReduceFn all_reduce = nullptr;
+  CommDestroyFn comm_destroy = nullptr;
+  ErrorStringFn error_string = nullptr;
+};
+static Api g_api;
+static std::mutex g_mu;
+
+static mc_status load() {
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_api.all_reduce) return MC_OK;
+  void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);  // the one torch loaded
+  if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+  if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+  if (!h) return set_err(MC_E_NCCL, "libnccl.so.2 not found: %s", dlerror());
+  Api a;
+  a.get_unique_id = (GetUniqueIdFn)dlsym(h, "ncclGetUniqueId");
+  a.comm_init_rank = (CommInitRankFn)dlsym(h, "ncclCommInitRank");
+  a.all_reduce = (AllReduceFn)dlsym(h, "ncclAllReduce");
+  a.comm_destroy = (CommDestroyFn)dlsym(h, "ncclCommDestroy");
+  a.error_string = (ErrorStringFn)dlsym(h, "ncclGetErrorString");
+  if (!a.get_unique_id || !a.comm_init_rank || !a.all_reduce || !a.comm_destroy)
+    return set_err(MC_E_NCCL, "libnccl.so.2 lacks the expected entry points");
+  g_api = a;
+  return MC_OK;
+}
+
+static mc_status check(int r, const char* what) {
+  if (r == 0) return MC_OK;
+  return set_err(MC_E_NCCL, "%s: %s", what,
+                 g_api.error_string ? g_api.error_string(r) : "nccl error");
+}
+}  // namespace nccl
+
 // ------------------------------------------------------------------ packed matrices
 struct PMat {
   int N = 0, K = 0;  // logical rows / cols
@@ -105,8 +158,21 @@ struct PMat {
   int4* w = nullptr;
   float* scale = nullptr;      // WF_I8 row scales
   uint32_t* qscale = nullptr;  // WF_Q4 block scales
+  int4* wtc = nullptr;         // WF_I8: copy in the tcgen05 operand layout (9..16 tokens)
   long long algo_bytes = 0;  // codes + scales actually used
 };
+
+// k-split of a tcgen05 GEMM: enough CTAs to fill the SMs, each with at least
+// 16 k-steps.
+static int tc_ksplit(const PMat& W, int nsm) {
+  const int tiles = (W.n_stripes + 7) / 8;
+  int k = std::max(1, nsm / std::max(tiles, 1));
+  return std::max(1, std::min(k, W.KB / 16));
+}
+
+// Projections of more than 8 tokens run on the tcgen05 tensor cores when the
+// matrix has the canonical-layout copy (int8 weights).
+static bool use_tc(const PMat& W, int M) { return M > 8 && M <= kMaxTokens && W.wtc; }
 
 // Source matrix staged on the device: int8 [rows][cols] + f32 row scales, or
 // q4_0 blocks [rows][cols/32][18] (fmt WF_Q4).
@@ -295,12 +361,15 @@ static mc_status pack_matrix(const SrcI8& src, const std::vector<int>& row_map,
   out->K = n_real_cols;
   out->algo_bytes = (long long)n_real_rows * n_real_cols + 4ll * n_real_rows;
   if (src.fmt == WF_Q4) {
-    // q4_0 keeps its blocks: columns can only be taken in place
-    for (size_t c = 0; c < col_map.size(); ++c)
-      if (col_map[c] != (c < (size_t)src.cols ? (int)c : -1) || (int)col_map.size() != src.cols)
-        return set_err(MC_E_SHAPE,
-                       "q4_0 matrix %dx%d cannot be re-laid-out (head_dim must be a "
-                       "multiple of 16 for q4_0 attention weights)", src.rows, src.cols);
+    // q4_0 keeps its blocks: a contiguous, block-aligned column range only
+    const int c0 = col_map.empty() ? 0 : col_map[0];
+    bool ok = c0 >= 0 && c0 % 32 == 0 && col_map.size() % 32 == 0 &&
+              c0 + (long long)col_map.size() <= src.cols;
+    for (size_t c = 0; ok && c < col_map.size(); ++c) ok = col_map[c] == c0 + (int)c;
+    if (!ok)
+      return set_err(MC_E_SHAPE,
+                     "q4_0 matrix %dx%d cannot be re-laid-out (head_dim must be a multiple of "
+                     "16, and tensor-parallel slices multiples of 32 columns)", src.rows, src.cols);
     out->fmt = WF_Q4;
     out->algo_bytes = (long long)n_real_rows * n_real_cols / 32 * kQ4BlockBytes;
     const size_t units = (size_t)out->n_stripes * out->KB * 32;
@@ -309,7 +378,7 @@ static mc_status pack_matrix(const SrcI8& src, const std::vector<int>& row_map,
     int* drm = nullptr;
     CK(cudaMalloc(&drm, row_map.size() * 4));
     cudaMemcpy(drm, row_map.data(), row_map.size() * 4, cudaMemcpyHostToDevice);
-    cudaError_t e = launch_pack_q4(src.q4, drm, out->n_stripes, out->KB,
+    cudaError_t e = launch_pack_q4(src.q4, drm, out->n_stripes, out->KB, src.cols / 32, c0 / 32,
                                    reinterpret_cast<uint2*>(out->w), out->qscale, 0);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     cudaFree(drm);
@@ -326,9 +395,15 @@ static mc_status pack_matrix(const SrcI8& src, const std::vector<int>& row_map,
   cudaMemcpy(dcm, col_map.data(), col_map.size() * 4, cudaMemcpyHostToDevice);
   cudaError_t e = launch_pack_int8(src.q, src.cols, src.s, drm, dcm, out->n_stripes, out->KB,
                                    out->w, out->scale, 0);
+  const int n_tiles = (out->n_stripes + 7) / 8;
+  mc_status st = MC_OK;
+  if (e == cudaSuccess) st = al.alloc(&out->wtc, (size_t)n_tiles * out->KB * (kTcTileRows * 32 / 16));
+  if (e == cudaSuccess && st == MC_OK)
+    e = launch_pack_tc(src.q, src.cols, drm, dcm, (int)row_map.size(), n_tiles, out->KB, out->wtc, 0);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   cudaFree(drm);
   cudaFree(dcm);
+  if (st != MC_OK) return st;
   if (e != cudaSuccess) return set_err(MC_E_CUDA, "packing failed: %s", cudaGetErrorString(e));
   return MC_OK;
 }
@@ -359,6 +434,10 @@ struct mc_weights {
   int8_t* emb_q = nullptr;
   float* emb_scale = nullptr;
   uint8_t* emb_q4 = nullptr;  // q4_0 embedding blocks (emb_q unused then)
+  // tensor parallelism: H, Hkv, F above are this rank's shares; the LM head
+  // holds vocabulary rows [head_row0, head_row0 + V_loc)
+  int tp_rank = 0, tp_world = 1;
+  int V_loc = 0, head_row0 = 0;
   Allocs al;
   long long algo_bytes_per_forward = 0;  // streamed weight bytes of one forward
 };
@@ -414,6 +493,24 @@ static mc_status load_model(const mc_tensor_desc* ts, size_t n, const mc_model_c
   W->half = W->hd / 2;
   W->half_p = round_up(W->half, 8);
   W->hdp = 2 * W->half_p;
+  // tensor-parallel shard (global sizes Hg, Hkvg, Fg; local H, Hkv, F)
+  const int R = cfg->tp_world > 1 ? cfg->tp_world : 1;
+  const int rank = R > 1 ? cfg->tp_rank : 0;
+  if (rank < 0 || rank >= R) return set_err(MC_E_INVALID, "tp_rank %d outside [0, %d)", rank, R);
+  if (W->H % R || W->Hkv % R || W->F % R || W->V % R)
+    return set_err(MC_E_SHAPE, "heads %d/%d, ffn %d and vocab %d must divide by tp_world %d",
+                   W->H, W->Hkv, W->F, W->V, R);
+  if (R > 1 && (W->F / R) % 32)
+    return set_err(MC_E_SHAPE, "ffn / tp_world = %d must be a multiple of 32", W->F / R);
+  const int Hg = W->H, Hkvg = W->Hkv, Fg = W->F;
+  W->tp_world = R;
+  W->tp_rank = rank;
+  W->H = Hg / R;
+  W->Hkv = Hkvg / R;
+  W->F = Fg / R;
+  W->V_loc = W->V / R;
+  W->head_row0 = rank * W->V_loc;
+  const int h0 = rank * W->H, kv0 = rank * W->Hkv, f0 = rank * W->F;
   const int H = W->H, Hkv = W->Hkv, hd = W->hd, half = W->half, half_p = W->half_p,
             hdp = W->hdp, d = W->d, F = W->F;
   Allocs& al = W->al;
@@ -476,10 +573,10 @@ static mc_status load_model(const mc_tensor_desc* ts, size_t n, const mc_model_c
       CKS(stage_matrix(tk, &sk));
       CKS(stage_matrix(tv, &sv));
       CKS(stage_matrix(to, &so));
-      if (sq.rows != H * hd || sk.rows != Hkv * hd || sv.rows != Hkv * hd || sq.cols != d ||
-          so.rows != d || so.cols != H * hd)
+      if (sq.rows != Hg * hd || sk.rows != Hkvg * hd || sv.rows != Hkvg * hd || sq.cols != d ||
+          so.rows != d || so.cols != Hg * hd)
         return set_err(MC_E_SHAPE, "layer %d attention shapes do not match H=%d Hkv=%d hd=%d d=%d",
-                       l, H, Hkv, hd, d);
+                       l, Hg, Hkvg, hd, d);
       SrcI8 cat;
       CKS(concat_rows({&sq, &sk, &sv}, &cat));
       const int per_head = half_p / 8;
@@ -491,7 +588,7 @@ static mc_status load_model(const mc_tensor_desc* ts, size_t n, const mc_model_c
         const bool isq = s < Lw.sq;
         const int s2 = isq ? s : s - Lw.sq;
         const int hh = s2 / per_head, j = s2 % per_head;
-        const int base = isq ? hh * hd : H * hd + hh * hd;
+        const int base = isq ? (h0 + hh) * hd : Hg * hd + (kv0 + hh) * hd;
         for (int g = 0; g < 8; ++g) {
           const int i = 8 * j + g;
           rm[s * 16 + g] = i < half ? base + i : -1;
@@ -502,7 +599,8 @@ static mc_status load_model(const mc_tensor_desc* ts, size_t n, const mc_model_c
         const int hh = s / per_head, j = s % per_head;
         for (int r = 0; r < 16; ++r) {
           const int src = padded_src(16 * j + r, half, half_p);
-          rm[(Lw.sq + Lw.sk + s) * 16 + r] = src < 0 ? -1 : (H + Hkv) * hd + hh * hd + src;
+          rm[(Lw.sq + Lw.sk + s) * 16 + r] =
+              src < 0 ? -1 : (Hg + Hkvg) * hd + (kv0 + hh) * hd + src;
         }
       }
       CKS(pack_matrix(cat, rm, identity_map(d, round_up(d, 32)), (H + 2 * Hkv) * hd, d, al,
@@ -514,7 +612,7 @@ static mc_status load_model(const mc_tensor_desc* ts, size_t n, const mc_model_c
       for (int hh = 0; hh < H; ++hh)
         for (int pp = 0; pp < hdp; ++pp) {
           const int src = padded_src(pp, half, half_p);
-          cm[hh * hdp + pp] = src < 0 ? -1 : hh * hd + src;
+          cm[hh * hdp + pp] = src < 0 ? -1 : (h0 + hh) * hd + src;
         }
       CKS(pack_matrix(so, identity_map(d, round_up(d, 16)), cm, d, H * hd, al, &Lw.o));
       bytes += Lw.qkv.algo_bytes + Lw.o.algo_bytes;
@@ -529,9 +627,9 @@ static mc_status load_model(const mc_tensor_desc* ts, size_t n, const mc_model_c
       CKS(stage_matrix(tg, &sg));
       CKS(stage_matrix(tu, &su));
       CKS(stage_matrix(td, &sdn));
-      if (sg.rows != F || su.rows != F || sg.cols != d || su.cols != d || sdn.rows != d ||
-          sdn.cols != F)
-        return set_err(MC_E_SHAPE, "layer %d MLP shapes do not match d=%d ffn=%d", l, d, F);
+      if (sg.rows != Fg || su.rows != Fg || sg.cols != d || su.cols != d || sdn.rows != d ||
+          sdn.cols != Fg)
+        return set_err(MC_E_SHAPE, "layer %d MLP shapes do not match d=%d ffn=%d", l, d, Fg);
       SrcI8 cat;
       CKS(concat_rows({&sg, &su}, &cat));
       const int ns = (F + 7) / 8;
@@ -539,12 +637,14 @@ static mc_status load_model(const mc_tensor_desc* ts, size_t n, const mc_model_c
       for (int s = 0; s < ns; ++s)
         for (int g = 0; g < 8; ++g) {
           const int i = 8 * s + g;
-          rm[s * 16 + g] = i < F ? i : -1;
-          rm[s * 16 + g + 8] = i < F ? F + i : -1;
+          rm[s * 16 + g] = i < F ? f0 + i : -1;
+          rm[s * 16 + g + 8] = i < F ? Fg + f0 + i : -1;
         }
       CKS(pack_matrix(cat, rm, identity_map(d, round_up(d, 32)), 2 * F, d, al, &Lw.gu));
-      CKS(pack_matrix(sdn, identity_map(d, round_up(d, 16)), identity_map(F, round_up(F, 32)), d,
-                      F, al, &Lw.down));
+      std::vector<int> dcm = identity_map(F, round_up(F, 32));
+      for (int& c : dcm)
+        if (c >= 0) c += f0;
+      CKS(pack_matrix(sdn, identity_map(d, round_up(d, 16)), dcm, d, F, al, &Lw.down));
       bytes += Lw.gu.algo_bytes + Lw.down.algo_bytes;
     }
   }
@@ -556,8 +656,10 @@ static mc_status load_model(const mc_tensor_desc* ts, size_t n, const mc_model_c
     CKS(stage_matrix(th, &sh));
     if (sh.rows != W->V || sh.cols != d)
       return set_err(MC_E_SHAPE, "lm_head is %dx%d, expected %dx%d", sh.rows, sh.cols, W->V, d);
-    CKS(pack_matrix(sh, identity_map(W->V, round_up(W->V, 16)), identity_map(d, round_up(d, 32)),
-                    W->V, d, al, &W->head));
+    std::vector<int> hrm = identity_map(W->V_loc, round_up(W->V_loc, 16));
+    for (int& r : hrm)
+      if (r >= 0) r += W->head_row0;
+    CKS(pack_matrix(sh, hrm, identity_map(d, round_up(d, 32)), W->V_loc, d, al, &W->head));
     W->has_head = true;
     bytes += W->head.algo_bytes;
   }
@@ -656,6 +758,9 @@ struct mc_session {
   // MC_TRACE builds: timeline slots handed to the launches of one capture
   bool trace_on = false;
   int trace_next = 0;
+  // tensor parallelism (target weights sharded over tp_world ranks)
+  nccl::Comm comm = nullptr;
+  float* tp_part = nullptr;  // [kMaxTokens][d] partial sums of o / down
 };
 
 static int trace_slot(mc_session* s) { return s->trace_on ? ++s->trace_next : 0; }
@@ -775,6 +880,7 @@ static mc_status session_alloc(mc_session* s) {
   CK(cudaMemset(s->st_amax, 0, (size_t)2 * kMaxTokens * 4));
   s->st_np_cap = std::max(stripes, 1);
   CKS(s->al.alloc(&s->st_pss, (size_t)kMaxTokens * s->st_np_cap));
+  if (s->tw->tp_world > 1) CKS(s->al.alloc(&s->tp_part, (size_t)kMaxTokens * s->tw->d));
   CKS(s->al.alloc(&s->acnt, (size_t)hkv));
   CK(cudaMemset(s->acnt, 0, (size_t)hkv * 4));
   CKS(alloc_kv(s, s->tw, &s->tkv));
@@ -787,6 +893,7 @@ static mc_status session_alloc(mc_session* s) {
     asm_ = std::max(asm_, attention_smem_bytes(W->H / W->Hkv, kChunk, W->hdp, kPage));
   }
   CK(prepare_kernels(qsm, asm_));
+  CK(prepare_tc());
   for (int wf : {(int)WF_I8, (int)WF_Q4})
     for (int epi = 0; epi < 5; ++epi)
       for (int nt : {1, 2, 3, 6}) bps_of(s, epi, nt, wf);
@@ -819,6 +926,10 @@ extern "C" mc_status mc_session_create(const mc_weights* target, const mc_weight
                    kSampleMaxVocab);
   if (draft && (draft->V != target->V))
     return set_err(MC_E_SHAPE, "draft vocab %d != target vocab %d", draft->V, target->V);
+  if (draft && draft->tp_world > 1)
+    return set_err(MC_E_INVALID, "the draft model is replicated: load it with tp_world 1");
+  if (target->tp_world > 1 && cfg->temperature > 0.0f)
+    return set_err(MC_E_INVALID, "tensor-parallel sessions decode greedily (temperature 0)");
   CK(cudaSetDevice(target->dev));
   mc_session* s = new mc_session();
   s->tw = target;
@@ -848,6 +959,7 @@ extern "C" mc_status mc_session_destroy(mc_session* s) {
   if (s->stream) cudaStreamSynchronize(s->stream);
   if (s->round_exec) cudaGraphExecDestroy(s->round_exec);
   if (s->verify_exec) cudaGraphExecDestroy(s->verify_exec);
+  if (s->comm) nccl::g_api.comm_destroy(s->comm);  // after the graphs holding its calls
   if (s->h_ids) cudaFreeHost(s->h_ids);
   if (s->stream) cudaStreamDestroy(s->stream);
   s->al.free_all();
@@ -900,8 +1012,9 @@ struct StatIO {
 };
 
 static mc_status enq_quant(mc_session* s, const float* h, int ld, int d, int M, const float* w,
-                           float eps, int do_norm, const StatIO* io = nullptr) {
+                           float eps, int do_norm, const StatIO* io = nullptr, bool tc = false) {
   QuantArgs q{};
+  q.tc_layout = tc ? 1 : 0;
   if (io) {
     q.use_stats = 1;
     q.pss = io->pss;
@@ -953,6 +1066,11 @@ static mc_status enq_gemv(mc_session* s, const PMat& W, int epi, int M, GemvArgs
   a.err = s->err;
   a.trace_slot = trace_slot(s);
   const int nt = nt_for_tokens(M);
+  if (use_tc(W, M)) {
+    a.wtc = W.wtc;
+    CK(launch_gemm_tc(a, epi, tc_ksplit(W, s->nsm), s->stream, true));
+    return MC_OK;
+  }
   const int grid = gemv_grid(W, s->nsm, nt, [&](int t) { return bps_of(s, epi, t, W.fmt); });
   CK(launch_gemv(a, epi, nt, W.fmt, grid, s->stream, true));
   return MC_OK;
@@ -964,6 +1082,9 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
                              EmbedArgs ea, const int* pos_ptr, int pos_add,
                              unsigned long long* keys, float* logits_dev) {
   if (!W->has_head) return set_err(MC_E_NO_HEAD, "model has no lm_head and no embedding");
+  const bool tp = W->tp_world > 1;
+  if (tp && !s->comm) return set_err(MC_E_INVALID, "tensor-parallel weights: call mc_session_tp_init");
+  if (tp && logits_dev) return set_err(MC_E_INVALID, "tensor-parallel forwards return argmax only");
   ea.emb_q = W->emb_q;
   ea.emb_scale = W->emb_scale;
   ea.emb_q4 = W->emb_q4;
@@ -1003,6 +1124,36 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
     g.st_w = enc_w[ej];
     prod_np = Wm.n_stripes;
   };
+  // o / down: h += W x (+ statistics); row-parallel across ranks: partial
+  // sums, one all-reduce, then the residual add and the statistics
+  auto residual_gemv = [&](const PMat& Wm, const PMat* next) -> mc_status {
+    const int d = W->d;
+    GemvArgs g{};
+    g.ldo = d;
+    g.n_out = d;
+    if (!tp) {
+      g.out = s->h;
+      resid_stats(g, Wm);
+      return enq_gemv(s, Wm, EPI_RESID, M, g, next);
+    }
+    g.out = s->tp_part;
+    CKS(enq_gemv(s, Wm, EPI_STORE, M, g, next));
+    CKS(nccl::check(nccl::g_api.all_reduce(s->tp_part, s->tp_part, (size_t)M * d, nccl::kFloat32,
+                                           nccl::kSum, s->comm, s->stream),
+                    "all-reduce of row-parallel partial sums"));
+    ResidArgs r{};
+    r.h = s->h;
+    r.y = s->tp_part;
+    r.d = d;
+    r.M = M;
+    r.pss = s->st_pss;
+    r.amax = slot(ej);
+    r.w = enc_w[ej];
+    r.trace_slot = trace_slot(s);
+    CK(launch_resid_stats(r, s->stream, true));
+    prod_np = (d + kResidBlock - 1) / kResidBlock;
+    return MC_OK;
+  };
   const int d = W->d, F = W->F;
   // the GEMVs of this forward in launch order (each warms L2 for the next)
   std::vector<const PMat*> seq;
@@ -1017,7 +1168,8 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
     const LayerW& Lw = W->layers[l];
     if (Lw.attn) {
       StatIO io = io_for(ej, prod_np);
-      CKS(enq_quant(s, s->h, d, d, M, Lw.attn_norm, W->eps, Lw.attn_norm ? 1 : 0, &io));
+      CKS(enq_quant(s, s->h, d, d, M, Lw.attn_norm, W->eps, Lw.attn_norm ? 1 : 0, &io,
+                    use_tc(Lw.qkv, M)));
       ++ej;
       GemvArgs a{};
       a.q_out = s->qb;
@@ -1061,18 +1213,15 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       t.trace_slot = trace_slot(s);
       CK(launch_attention(t, s->stream, true));
       io = io_for(ej, 0);
-      CKS(enq_quant(s, s->attn, W->H * W->hdp, W->H * W->hdp, M, nullptr, 0.0f, 0, &io));
+      CKS(enq_quant(s, s->attn, W->H * W->hdp, W->H * W->hdp, M, nullptr, 0.0f, 0, &io,
+                    use_tc(Lw.o, M)));
       ++ej;
-      GemvArgs o{};
-      o.out = s->h;
-      o.ldo = d;
-      o.n_out = d;
-      resid_stats(o, Lw.o);
-      CKS(enq_gemv(s, Lw.o, EPI_RESID, M, o, nxt()));
+      CKS(residual_gemv(Lw.o, nxt()));
     }
     if (Lw.mlp) {
       StatIO io = io_for(ej, prod_np);
-      CKS(enq_quant(s, s->h, d, d, M, Lw.mlp_norm, W->eps, Lw.mlp_norm ? 1 : 0, &io));
+      CKS(enq_quant(s, s->h, d, d, M, Lw.mlp_norm, W->eps, Lw.mlp_norm ? 1 : 0, &io,
+                    use_tc(Lw.gu, M)));
       ++ej;
       GemvArgs g{};
       g.out = s->act;
@@ -1082,24 +1231,25 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       CKS(enq_gemv(s, Lw.gu, EPI_SWIGLU, M, g, nxt()));
       io = io_for(ej, 0);
       io.pf = &Lw.down;  // the down weights beyond the gate/up GEMV's prefetch
-      CKS(enq_quant(s, s->act, F, F, M, nullptr, 0.0f, 0, &io));
+      CKS(enq_quant(s, s->act, F, F, M, nullptr, 0.0f, 0, &io, use_tc(Lw.down, M)));
       ++ej;
-      GemvArgs dn{};
-      dn.out = s->h;
-      dn.ldo = d;
-      dn.n_out = d;
-      resid_stats(dn, Lw.down);
-      CKS(enq_gemv(s, Lw.down, EPI_RESID, M, dn, nxt()));
+      CKS(residual_gemv(Lw.down, nxt()));
     }
   }
   StatIO io = io_for(ej, prod_np);
-  CKS(enq_quant(s, s->h, d, d, M, W->final_norm, W->eps, W->final_norm ? 1 : 0, &io));
+  CKS(enq_quant(s, s->h, d, d, M, W->final_norm, W->eps, W->final_norm ? 1 : 0, &io,
+                use_tc(W->head, M)));
   GemvArgs hd{};
   hd.out = logits_dev;
   hd.ldo = W->V;
-  hd.n_out = W->V;
+  hd.n_out = W->V_loc;
   hd.keys = keys;
+  hd.row_offset = W->head_row0;
   CKS(enq_gemv(s, W->head, EPI_LMHEAD, M, hd));
+  if (tp)  // vocab-parallel head: the largest (value, lowest index) key wins
+    CKS(nccl::check(nccl::g_api.all_reduce(keys, keys, (size_t)M, nccl::kUint64, nccl::kMax,
+                                           s->comm, s->stream),
+                    "all-reduce of argmax keys"));
   return MC_OK;
 }
 
@@ -1386,6 +1536,33 @@ extern "C" mc_status mc_spec_rewind(mc_session* s) {
   return MC_OK;
 }
 
+extern "C" mc_status mc_tp_unique_id(char id_out[128]) {
+  if (!id_out) return set_err(MC_E_INVALID, "null argument");
+  CKS(nccl::load());
+  nccl::UniqueId id;
+  CKS(nccl::check(nccl::g_api.get_unique_id(&id), "ncclGetUniqueId"));
+  memcpy(id_out, id.internal, sizeof(id.internal));
+  return MC_OK;
+}
+
+extern "C" mc_status mc_session_tp_init(mc_session* s, const char id[128], int32_t rank,
+                                        int32_t world) {
+  if (!s || !id) return set_err(MC_E_INVALID, "null argument");
+  if (s->comm) return set_err(MC_E_INVALID, "tensor parallelism already initialised");
+  if (world != s->tw->tp_world || rank != s->tw->tp_rank)
+    return set_err(MC_E_INVALID, "rank %d of %d does not match the weights' shard %d of %d", rank,
+                   world, s->tw->tp_rank, s->tw->tp_world);
+  if (world < 2) return set_err(MC_E_INVALID, "tp_world must be at least 2");
+  CKS(nccl::load());
+  CK(cudaSetDevice(s->dev));
+  nccl::UniqueId uid;
+  memcpy(uid.internal, id, sizeof(uid.internal));
+  nccl::Comm comm = nullptr;
+  CKS(nccl::check(nccl::g_api.comm_init_rank(&comm, world, uid, rank), "ncclCommInitRank"));
+  s->comm = comm;
+  return MC_OK;
+}
+
 extern "C" mc_status mc_spec_set_seed(mc_session* s, uint64_t seed) {
   if (!s) return set_err(MC_E_INVALID, "null session");
   s->cfg.seed = seed;
@@ -1462,7 +1639,7 @@ extern "C" mc_status mc_linear_create(const mc_tensor_desc* w, int32_t device, m
                      identity_map(src.cols, round_up(src.cols, 32)), src.rows, src.cols, L->al,
                      &L->m);
   const int kp = round_up(src.cols, 32);
-  if (st == MC_OK && prepare_kernels(0, 0) != cudaSuccess)
+  if (st == MC_OK && (prepare_kernels(0, 0) != cudaSuccess || prepare_tc() != cudaSuccess))
     st = set_err(MC_E_CUDA, "kernel preparation failed");
   if (st == MC_OK) st = L->al.alloc(&L->xq, (size_t)kp * 48);
   if (st == MC_OK) st = L->al.alloc(&L->xexp, (size_t)kMaxTokens);
@@ -1514,6 +1691,7 @@ extern "C" mc_status mc_linear_run(mc_linear* l, const float* x_dev, int32_t m, 
     q.KB = l->m.KB;
     q.nt = nt_for_tokens(M);
     q.xexp = l->xexp;
+    q.tc_layout = use_tc(l->m, M) ? 1 : 0;
     CK(launch_quant(q, s, true));
     GemvArgs a{};
     a.w = l->m.w;
@@ -1531,7 +1709,12 @@ extern "C" mc_status mc_linear_run(mc_linear* l, const float* x_dev, int32_t m, 
     a.ldo = l->m.N;
     a.n_out = l->m.N;
     const int nt = nt_for_tokens(M);
-    CK(launch_gemv(a, EPI_STORE, nt, l->m.fmt, linear_grid(l, nt), s, true));
+    if (use_tc(l->m, M)) {
+      a.wtc = l->m.wtc;
+      CK(launch_gemm_tc(a, EPI_STORE, tc_ksplit(l->m, l->nsm), s, true));
+    } else {
+      CK(launch_gemv(a, EPI_STORE, nt, l->m.fmt, linear_grid(l, nt), s, true));
+    }
   }
   return MC_OK;
 }

@@ -61,7 +61,7 @@ enum Epi : int {
   EPI_RESID = 1,   // out[m][row] += y           (O and down projections)
   EPI_SWIGLU = 2,  // act[m][i] = silu(gate)*up  (gate/up rows interleaved)
   EPI_QKV = 3,     // RoPE(q), RoPE(k) -> q buffer and paged KV, v -> KV
-  EPI_LMHEAD = 4,  // logits + first-index argmax keys
+  EPI_LMHEAD = 4,  // logits + first-index argmax keys (row index + row_offset)
 };
 
 struct GemvArgs {
@@ -104,6 +104,8 @@ struct GemvArgs {
   int half_p, hdp, H, Hkv, page;
   int sq, sk;            // Q and K stripe counts
   int kv_prefetch;       // QKV: warm L2 with this layer's K/V pages for the attention
+  int row_offset;        // LMHEAD: global vocabulary index of packed row 0
+  const int4* wtc;       // tcgen05 path: weights in the canonical layout (k_gemm_tc)
   int trace_slot;        // MC_TRACE builds: 1 + timeline slot, 0 = untraced
 };
 
@@ -123,6 +125,7 @@ struct QuantArgs {
   // Producer-side statistics (use_stats != 0): sum of squares as np partials
   // pss[m * np_stride + j], and max |x * w| as float bits amax[m]; the kernel
   // then zeroes amax_next[0..kMaxTokens) for the following producer.
+  int tc_layout;         // write the tcgen05 B-operand layout (see digit_word)
   int use_stats;
   const float* pss;
   int np, np_stride;
@@ -185,6 +188,22 @@ struct EmbedArgs {
   int trace_slot;        // MC_TRACE builds: 1 + timeline slot, 0 = untraced
 };
 
+// Tensor parallelism: after the all-reduce of a row-parallel projection's
+// partial sums, h += y and the next encoder's statistics (as the RESID
+// epilogue produces them): pss[m * n_blk + blk] over 1024-element blocks and
+// max |h * w| folded into amax[m].
+struct ResidArgs {
+  float* h;              // [M][d]
+  const float* y;        // [M][d] reduced partial sums
+  int d, M;
+  float* pss;
+  unsigned* amax;
+  const float* w;        // next RMSNorm weight or nullptr
+  int trace_slot;
+};
+cudaError_t launch_resid_stats(const ResidArgs& a, cudaStream_t s, bool pdl);
+constexpr int kResidBlock = 1024;
+
 struct SpecState {
   int ctx_len;
   int lt;          // target KV length
@@ -225,6 +244,14 @@ __host__ __device__ inline uint32_t key_index(unsigned long long k) {
 cudaError_t launch_gemv(const GemvArgs& a, int epi, int nt, int wf, int grid,
                         cudaStream_t s, bool pdl);
 int gemv_blocks_per_sm(int epi, int nt, int wf);
+// tcgen05 GEMM for 9..16 tokens: grid (128-row tiles, ksplit); the digits
+// must be encoded with QuantArgs::tc_layout; ksplit > 1 merges through ws/cnt.
+cudaError_t launch_gemm_tc(const GemvArgs& a, int epi, int ksplit, cudaStream_t s, bool pdl);
+cudaError_t launch_pack_tc(const int8_t* src, long long src_ld, const int* row_map,
+                           const int* col_map, int n_rows, int n_tiles, int KB, int4* dst,
+                           cudaStream_t s);
+cudaError_t prepare_tc();  // shared-memory limit of the tcgen05 GEMM (outside capture)
+constexpr int kTcTileRows = 128;
 cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t s, bool pdl);
@@ -254,9 +281,11 @@ cudaError_t launch_pack_int8(const int8_t* src, long long src_ld,
                              const float* src_scale, const int* row_map,
                              const int* col_map, int n_stripes, int KB,
                              int4* dst, float* dst_scale, cudaStream_t s);
-// q4_0 source [rows][KB] blocks of 18 bytes -> WF_Q4 stripes through row_map
-// (size n_stripes*16, -1 = padding row: zero scale, codes 8).
+// q4_0 source [rows][src_KB] blocks of 18 bytes -> WF_Q4 stripes of the KB
+// blocks starting at block kb_off, rows through row_map (size n_stripes*16,
+// -1 = padding row: zero scale, codes 8).
 cudaError_t launch_pack_q4(const uint8_t* src, const int* row_map, int n_stripes, int KB,
-                           uint2* dst, uint32_t* dst_scale, cudaStream_t s);
+                           int src_KB, int kb_off, uint2* dst, uint32_t* dst_scale,
+                           cudaStream_t s);
 
 }  // namespace mc

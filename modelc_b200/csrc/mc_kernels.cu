@@ -392,10 +392,20 @@ __device__ __forceinline__ void token_stats(const StatArgs& a, float (*red_ss)[k
 // past d); dst(word, value) stores a word.
 constexpr int kEncBatch = 8;
 
+// Word index of the 4 digit bytes of column c, k-block kb, k = kk..kk+3
+// (kk % 4 == 0).  mma.sync layout: [kb][lane][tile][reg], lane = (c%8)*4 +
+// (kk%16)/4, the B fragment of m16n8k32.  tcgen05 layout (tc): the canonical
+// K-major no-swizzle tile [kb][c/8][kk/16][c%8][16 bytes], i.e. 8-column x
+// 16-byte core matrices, the two K halves 128 bytes apart, column groups 256.
+__device__ __forceinline__ size_t digit_word(int kb, int c, int kk, int nt, bool tc) {
+  if (tc) return ((((size_t)kb * nt + (c >> 3)) * 2 + (kk >> 4)) * 32) + (c & 7) * 4 + ((kk & 15) >> 2);
+  return (((size_t)kb * 32 + (c & 7) * 4 + ((kk & 15) >> 2)) * nt + (c >> 3)) * 2 + (kk >> 4);
+}
+
 template <class Src4, class Dst>
 __device__ __forceinline__ void encode_digits(const StatArgs& a, int nt, int kb0, int kb1,
                                               const float* s_mul, const int* s_e, Src4 src4,
-                                              Dst dst) {
+                                              Dst dst, bool tc = false) {
   const int M = a.M, d = a.d;
   const int pad_cols = 8 * nt - 3 * M;
   const int ngroups = (kb1 - kb0) * 8;
@@ -420,11 +430,8 @@ __device__ __forceinline__ void encode_digits(const StatArgs& a, int nt, int kb0
       const int q = task / ngroups;  // token (q < M) or padding column (q >= M)
       const int kb = kb0 + (grp >> 3);
       const int kk = (grp & 7) * 4;
-      const int reg = kk >> 4, t = (kk & 15) >> 2;
       if (q >= M) {
-        const int c = 3 * M + (q - M);
-        const int tile = c >> 3, ln = (c & 7) * 4 + t;
-        dst((((size_t)kb * 32 + ln) * nt + tile) * 2 + reg, 0u);
+        dst(digit_word(kb, 3 * M + (q - M), kk, nt, tc), 0u);
         continue;
       }
       const int m = q;
@@ -452,11 +459,7 @@ __device__ __forceinline__ void encode_digits(const StatArgs& a, int nt, int kb0
       }
       const uint32_t wd[3] = {w0, w1, w2};
 #pragma unroll
-      for (int dg = 0; dg < 3; ++dg) {
-        const int c = 3 * m + dg;
-        const int tile = c >> 3, ln = (c & 7) * 4 + t;
-        dst((((size_t)kb * 32 + ln) * nt + tile) * 2 + reg, wd[dg]);
-      }
+      for (int dg = 0; dg < 3; ++dg) dst(digit_word(kb, 3 * m + dg, kk, nt, tc), wd[dg]);
     }
   }
 }
@@ -533,7 +536,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
           }
           if constexpr (EPI == EPI_LMHEAD) {
             if (!isnan(y0)) {
-              unsigned long long k = argmax_key(y0, (uint32_t)prow);
+              unsigned long long k = argmax_key(y0, (uint32_t)(prow + a.row_offset));
               kmax[it] = k > kmax[it] ? k : kmax[it];
             }
           }
@@ -549,7 +552,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
           }
           if constexpr (EPI == EPI_LMHEAD) {
             if (!isnan(y1)) {
-              unsigned long long k = argmax_key(y1, (uint32_t)(prow + 8));
+              unsigned long long k = argmax_key(y1, (uint32_t)(prow + 8 + a.row_offset));
               kmax[it] = k > kmax[it] ? k : kmax[it];
             }
           }
@@ -1044,7 +1047,7 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
     __syncthreads();
     if (blockIdx.x == 0 && threadIdx.x < a.M) a.xexp[threadIdx.x] = s_e[threadIdx.x];
     encode_digits(sa, a.nt, kb0, kb1, s_mul, s_e, src4,
-                  [&](size_t wi, uint32_t v) { xq[wi] = v; });
+                  [&](size_t wi, uint32_t v) { xq[wi] = v; }, a.tc_layout != 0);
     MC_TRACE_END(a.trace_slot);
     return;
   }
@@ -1063,7 +1066,7 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
                   r.w = k + 3 < a.d ? p[3] : 0.0f;
                   return r;
                 },
-                [&](size_t wi, uint32_t v) { xq[wi] = v; });
+                [&](size_t wi, uint32_t v) { xq[wi] = v; }, a.tc_layout != 0);
   MC_TRACE_END(a.trace_slot);
 }
 
@@ -1400,8 +1403,9 @@ static int attention_rb(int R, int hdp, int page) {
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
   const int G = a.H / a.Hkv;
   const int R = G * a.M;
+  // the combine's page weights [R][n_chunks] reuse the score tile [Rp][page]
   if (a.page != 64 || a.max_chunks > a.page || a.hdp > 128 || (a.hdp & 3) ||
-      (kAttnThreads % a.hdp) || (size_t)R * a.max_chunks * 2 > (size_t)a.page * (a.hdp + 4))
+      (kAttnThreads % a.hdp))
     return cudaErrorInvalidValue;
   const int rgmax = std::max(kAttnThreads / a.page, kAttnThreads / a.hdp);
   const int Rp = (R + rgmax - 1) / rgmax * rgmax;
@@ -1832,6 +1836,65 @@ cudaError_t launch_accept_stochastic(SpecState* st, uint32_t* ctx, int* acc_log,
                           dlog, V);
 }
 
+// grid (ceil(d / 1024), M), 256 threads: h += y on one 1024-element block of
+// one token, its sum of squares (fixed order: 4 strided elements per thread,
+// then warp and block trees) and max |h * w|.
+__global__ void __launch_bounds__(256) k_resid_stats(ResidArgs a) {
+  MC_TRACE_T0
+  grid_launch_dependents();
+  grid_wait();
+  MC_TRACE_WAITED(a.trace_slot);
+  const int m = blockIdx.y, blk = blockIdx.x;
+  float ss = 0.0f;
+  uint32_t mx = 0u;
+  for (int j = 0; j < kResidBlock / 256; ++j) {
+    const int i = blk * kResidBlock + j * 256 + threadIdx.x;
+    if (i < a.d) {
+      float* hp = a.h + (size_t)m * a.d + i;
+      const float v = __fadd_rn(*hp, __ldcg(a.y + (size_t)m * a.d + i));
+      *hp = v;
+      ss = __fadd_rn(ss, __fmul_rn(v, v));
+      mx = max(mx, __float_as_uint(fabsf(__fmul_rn(v, a.w ? a.w[i] : 1.0f))));
+    }
+  }
+  __shared__ float rs[8];
+  __shared__ uint32_t rm[8];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    rs[threadIdx.x >> 5] = ss;
+    rm[threadIdx.x >> 5] = mx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.0f;
+    uint32_t u = 0u;
+    for (int w = 0; w < 8; ++w) {
+      t = __fadd_rn(t, rs[w]);
+      u = max(u, rm[w]);
+    }
+    a.pss[(size_t)m * gridDim.x + blk] = t;
+    atomicMax(a.amax + m, u);
+  }
+  MC_TRACE_END(a.trace_slot);
+}
+
+cudaError_t launch_resid_stats(const ResidArgs& a, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.d + kResidBlock - 1) / kResidBlock, a.M);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_resid_stats, a);
+}
+
 __global__ void k_set_int(int* p, int v) { *p = v; }
 cudaError_t launch_set_int(int* p, int v, cudaStream_t s) {
   k_set_int<<<1, 1, 0, s>>>(p, v);
@@ -1896,7 +1959,7 @@ cudaError_t launch_pack_int8(const int8_t* src, long long src_ld, const float* s
 // the q4_0 source.  In a source block, element j < 16 is the low nibble of
 // qs[j] and element 16 + j its high nibble (dequant.rs:33-44).
 __global__ void k_pack_q4(const uint8_t* __restrict__ src, const int* __restrict__ row_map,
-                          int n_stripes, int KB, uint2* __restrict__ dst,
+                          int n_stripes, int KB, int src_KB, int kb_off, uint2* __restrict__ dst,
                           uint32_t* __restrict__ dst_scale) {
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long total = (long long)n_stripes * KB * 32;
@@ -1908,8 +1971,8 @@ __global__ void k_pack_q4(const uint8_t* __restrict__ src, const int* __restrict
   const int g = lane >> 2, t = lane & 3;
   const int ra = row_map[stripe * 16 + g];
   const int rb = row_map[stripe * 16 + g + 8];
-  const uint8_t* ba = ra >= 0 ? src + ((long long)ra * KB + kb) * kQ4BlockBytes : nullptr;
-  const uint8_t* bb = rb >= 0 ? src + ((long long)rb * KB + kb) * kQ4BlockBytes : nullptr;
+  const uint8_t* ba = ra >= 0 ? src + ((long long)ra * src_KB + kb_off + kb) * kQ4BlockBytes : nullptr;
+  const uint8_t* bb = rb >= 0 ? src + ((long long)rb * src_KB + kb_off + kb) * kQ4BlockBytes : nullptr;
   uint32_t w0 = 0, w1 = 0;
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
@@ -1927,12 +1990,337 @@ __global__ void k_pack_q4(const uint8_t* __restrict__ src, const int* __restrict
 }
 
 cudaError_t launch_pack_q4(const uint8_t* src, const int* row_map, int n_stripes, int KB,
-                           uint2* dst, uint32_t* dst_scale, cudaStream_t s) {
+                           int src_KB, int kb_off, uint2* dst, uint32_t* dst_scale,
+                           cudaStream_t s) {
   const long long total = (long long)n_stripes * KB * 32;
   const int bs = 256;
-  k_pack_q4<<<(unsigned)((total + bs - 1) / bs), bs, 0, s>>>(src, row_map, n_stripes, KB, dst,
-                                                             dst_scale);
+  k_pack_q4<<<(unsigned)((total + bs - 1) / bs), bs, 0, s>>>(src, row_map, n_stripes, KB, src_KB,
+                                                             kb_off, dst, dst_scale);
   return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ tcgen05 GEMM
+// Projections of 9..16 tokens (48 digit columns) on the 5th-generation tensor
+// cores: D[128 rows][48] += A[128][32 k] * B[48][32 k] per tcgen05.mma.kind::i8
+// (exact int32 in tensor memory).  One CTA per 128-row tile (and k-split):
+// thread 0 streams A (the weight copy in the canonical layout, below) and B
+// (the digits, encoded in the same layout) into a 4-stage shared-memory ring
+// with cp.async.bulk + mbarrier transaction counts; thread 32 issues the MMAs
+// and releases each stage with tcgen05.commit.  Afterwards the 4 warps read
+// their 32 tensor-memory lanes (tcgen05.ld 32x32b) and run the same stripe
+// epilogue as the GEMV, so results are identical to it bit for bit.
+//
+// Canonical K-major, no-swizzle operand layout per 32-column k-step:
+// [row / 8][k / 16][row % 8][16 bytes] (core matrices of 8 rows x 16 bytes,
+// the two K halves 128 bytes apart = LBO, 8-row groups 256 bytes apart = SBO).
+constexpr int kTcRows = 128;
+constexpr int kTcN = 48;
+constexpr int kTcChunk = 8;    // k-steps per stage
+constexpr int kTcStages = 4;
+constexpr int kTcAStep = kTcRows * 32;  // bytes of A per k-step
+constexpr int kTcBStep = kTcN * 32;     // bytes of B per k-step
+constexpr uint32_t kTcTmemCols = 64;
+constexpr long long kTcSpin = 1ll << 22;  // try_wait rounds before giving up
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(b)),
+               "r"(bytes)
+               : "memory");
+}
+// Bounded wait for the completion of the phase with this parity.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+  uint32_t done = 0;
+  for (long long i = 0; i < kTcSpin && !done; ++i)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(b)), "r"(parity)
+        : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(b))
+      : "memory");
+}
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
+  // start address, LBO 128 B, SBO 256 B (16-byte units), descriptor version 1
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(128 >> 4) << 16) |
+         ((uint64_t)(256 >> 4) << 32) | (1ull << 46);
+}
+// kind::i8 instruction descriptor: s32 accumulator, signed A and B, both
+// K-major, N = 48, M = 128.
+constexpr uint32_t kTcIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcN >> 3) << 17) |
+                              ((uint32_t)(kTcRows >> 4) << 24);
+__device__ __forceinline__ void umma_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(kTcIdesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* b) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_addr(b))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+constexpr size_t kTcSmem =
+    (size_t)kTcStages * kTcChunk * (kTcAStep + kTcBStep) + 4 * 2 * 16 * (kTcN + 1) * sizeof(int);
+
+template <int EPI>
+__global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
+  constexpr int COLS = kTcN;
+  extern __shared__ __align__(128) uint8_t tc_smem[];
+  uint8_t* smA = tc_smem;
+  uint8_t* smB = tc_smem + (size_t)kTcStages * kTcChunk * kTcAStep;
+  int (*sm_t)[2][16][COLS + 1] = reinterpret_cast<int (*)[2][16][COLS + 1]>(
+      tc_smem + (size_t)kTcStages * kTcChunk * (kTcAStep + kTcBStep));
+  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], done;
+  __shared__ uint32_t tmem_base;
+  __shared__ int sm_exp[kMaxTokens], s_issued, s_consumed, s_fail;
+  __shared__ unsigned long long sm_keys[kMaxTokens];
+  MC_TRACE_T0
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, nsplit = gridDim.y, split = blockIdx.y;
+  const int KB = a.KB;
+  const int k0 = (int)((long long)KB * split / nsplit), k1 = (int)((long long)KB * (split + 1) / nsplit);
+  const int nk = k1 - k0;
+  const int n_chunks = (nk + kTcChunk - 1) / kTcChunk;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(&tmem_base)),
+                 "r"(kTcTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    s_issued = s_consumed = s_fail = 0;
+  }
+  if (threadIdx.x < kMaxTokens) sm_keys[threadIdx.x] = 0ull;
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base;
+  const uint8_t* wsrc = reinterpret_cast<const uint8_t*>(a.wtc) + ((size_t)tile * KB + k0) * kTcAStep;
+  const uint8_t* xsrc = a.x + (size_t)k0 * kTcBStep;
+  if (threadIdx.x == 0)  // the weights are independent of the producer grid
+    prefetch_l2_bulk(wsrc, (uint32_t)min((long long)nk * kTcAStep, 1ll << 20));
+  grid_wait();
+  MC_TRACE_WAITED(a.trace_slot);
+  if (threadIdx.x < a.M) sm_exp[threadIdx.x] = __ldcg(a.xexp + threadIdx.x);
+
+  if (threadIdx.x == 0) {  // producer
+    int i = 0;
+    for (; i < n_chunks; ++i) {
+      const int s = i % kTcStages;
+      if (i >= kTcStages && !mbar_wait(&empty[s], ((i / kTcStages) - 1) & 1)) {
+        s_fail = 1;
+        break;
+      }
+      const int steps = min(kTcChunk, nk - i * kTcChunk);
+      mbar_expect_tx(&full[s], (uint32_t)steps * (kTcAStep + kTcBStep));
+      bulk_load(smA + (size_t)s * kTcChunk * kTcAStep, wsrc + (size_t)i * kTcChunk * kTcAStep,
+                (uint32_t)steps * kTcAStep, &full[s]);
+      bulk_load(smB + (size_t)s * kTcChunk * kTcBStep, xsrc + (size_t)i * kTcChunk * kTcBStep,
+                (uint32_t)steps * kTcBStep, &full[s]);
+    }
+    s_issued = i;
+  } else if (threadIdx.x == 32) {  // MMA issuer
+    int i = 0;
+    for (; i < n_chunks; ++i) {
+      const int s = i % kTcStages;
+      if (!mbar_wait(&full[s], (i / kTcStages) & 1)) {
+        s_fail = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int steps = min(kTcChunk, nk - i * kTcChunk);
+      const uint32_t a0 = smem_addr(smA + (size_t)s * kTcChunk * kTcAStep);
+      const uint32_t b0 = smem_addr(smB + (size_t)s * kTcChunk * kTcBStep);
+      for (int j = 0; j < steps; ++j)
+        umma_i8(tmem, umma_desc(a0 + j * kTcAStep), umma_desc(b0 + j * kTcBStep),
+                (i > 0 || j > 0) ? 1u : 0u);
+      umma_commit(&empty[s]);
+    }
+    s_consumed = i;
+    umma_commit(&done);  // tracks completion of every MMA issued above
+  }
+  __syncthreads();
+  // one thread waits for the MMAs (and, after a failed wait, drains copies
+  // issued but never consumed); the verdict is block-uniform, as the
+  // .aligned tensor-memory loads below require
+  if (threadIdx.x == 0) {
+    for (int i = s_consumed; i < s_issued; ++i) mbar_wait(&full[i % kTcStages], (i / kTcStages) & 1);
+    if (!mbar_wait(&done, 0)) s_fail = 1;
+  }
+  __syncthreads();
+  const bool ok = !s_fail;
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  unsigned long long kmax[(8 * kMaxTokens) / 32];
+#pragma unroll
+  for (int i = 0; i < (8 * kMaxTokens) / 32; ++i) kmax[i] = 0ull;
+  if (ok && nk > 0) {
+    uint32_t acc[COLS];
+    const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll
+    for (int c = 0; c < COLS; c += 16) tmem_ld16(taddr + c, acc + c);
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    // this thread holds row 32 * warp + lane: stripe 2 * warp + lane / 16
+    const int sel = lane >> 4, r = lane & 15;
+#pragma unroll
+    for (int c = 0; c < COLS; ++c) sm_t[warp][sel][r][c] = (int)acc[c];
+    __syncwarp();
+    for (int h = 0; h < 2; ++h) {
+      const int stripe = tile * 8 + warp * 2 + h;
+      if (stripe >= a.n_stripes) break;  // warp-uniform
+      int* t = &sm_t[warp][h][0][0];
+      bool run = true;
+      if (nsplit > 1) {
+        // merge the k-splits through the zeroed global tile (exact integers)
+        int* gt = a.ws + (size_t)stripe * 16 * COLS;
+        for (int i = lane; i < 16 * COLS; i += 32) atomicAdd(gt + i, t[(i / COLS) * (COLS + 1) + i % COLS]);
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+          __threadfence();
+          last = (atomicAdd(a.cnt + stripe, 1) == nsplit - 1);
+          if (last) __threadfence();
+        }
+        run = __shfl_sync(0xffffffffu, last, 0) != 0;
+        if (run) {
+          for (int i = lane; i < 16 * COLS; i += 32)
+            t[(i / COLS) * (COLS + 1) + i % COLS] = atomicExch(gt + i, 0);
+          if (lane == 0) atomicExch(a.cnt + stripe, 0);
+          __syncwarp();
+        }
+      }
+      if (run) gemv_epilogue<6, EPI>(a, stripe, t, COLS + 1, lane, kmax, a.scale, sm_exp);
+      __syncwarp();
+    }
+  } else if (!ok && threadIdx.x == 0 && a.err) {
+    atomicExch(a.err, 1);
+  }
+  grid_launch_dependents();
+  if constexpr (EPI == EPI_LMHEAD) {
+#pragma unroll
+    for (int it = 0; it < (8 * kMaxTokens) / 32; ++it) {
+      unsigned long long k = kmax[it];
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
+        k = k2 > k ? k2 : k;
+      }
+      const int m = (it * 32 + lane) >> 3;
+      if ((lane & 7) == 0 && m < a.M && k) atomicMax(&sm_keys[m], k);
+    }
+    __syncthreads();
+    if (threadIdx.x < a.M && sm_keys[threadIdx.x]) atomicMax(a.keys + threadIdx.x, sm_keys[threadIdx.x]);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTcTmemCols)
+                 : "memory");
+  MC_TRACE_END(a.trace_slot);
+}
+
+// One 16-byte row segment per thread: (tile, k-step, row group, K half, row).
+__global__ void k_pack_tc(const int8_t* __restrict__ src, long long src_ld,
+                          const int* __restrict__ row_map, const int* __restrict__ col_map,
+                          int n_rows, int n_tiles, int KB, int4* __restrict__ dst) {
+  const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long total = (long long)n_tiles * KB * (kTcAStep / 16);
+  if (gid >= total) return;
+  const int seg = (int)(gid % (kTcAStep / 16));  // g * 16 + h * 8 + r
+  const long long tk = gid / (kTcAStep / 16);
+  const int kb = (int)(tk % KB), t = (int)(tk / KB);
+  const int g = seg >> 4, h = (seg >> 3) & 1, r = seg & 7;
+  const int prow = t * kTcRows + g * 8 + r;
+  const int row = prow < n_rows ? row_map[prow] : -1;
+  uint32_t w[4] = {0, 0, 0, 0};
+  if (row >= 0)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int c = col_map[kb * 32 + h * 16 + j];
+      const uint32_t b = c >= 0 ? (uint8_t)src[(long long)row * src_ld + c] : 0u;
+      w[j >> 2] |= b << (8 * (j & 3));
+    }
+  dst[gid] = make_int4((int)w[0], (int)w[1], (int)w[2], (int)w[3]);
+}
+
+cudaError_t launch_pack_tc(const int8_t* src, long long src_ld, const int* row_map,
+                           const int* col_map, int n_rows, int n_tiles, int KB, int4* dst,
+                           cudaStream_t s) {
+  const long long total = (long long)n_tiles * KB * (kTcAStep / 16);
+  k_pack_tc<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(src, src_ld, row_map, col_map, n_rows,
+                                                             n_tiles, KB, dst);
+  return cudaGetLastError();
+}
+
+template <int EPI>
+static cudaError_t launch_tc_t(const GemvArgs& a, int ksplit, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.n_stripes + 7) / 8, ksplit);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = kTcSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_gemm_tc<EPI>, a);
+}
+
+cudaError_t launch_gemm_tc(const GemvArgs& a, int epi, int ksplit, cudaStream_t s, bool pdl) {
+  if (!a.wtc || a.M > kMaxTokens || a.M < 1 || ksplit < 1 || (ksplit > 1 && (!a.ws || !a.cnt)))
+    return cudaErrorInvalidValue;
+  switch (epi) {
+    case EPI_STORE: return launch_tc_t<EPI_STORE>(a, ksplit, s, pdl);
+    case EPI_RESID: return launch_tc_t<EPI_RESID>(a, ksplit, s, pdl);
+    case EPI_SWIGLU: return launch_tc_t<EPI_SWIGLU>(a, ksplit, s, pdl);
+    case EPI_QKV: return launch_tc_t<EPI_QKV>(a, ksplit, s, pdl);
+    case EPI_LMHEAD: return launch_tc_t<EPI_LMHEAD>(a, ksplit, s, pdl);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t prepare_tc() {
+  for (auto f : {k_gemm_tc<EPI_STORE>, k_gemm_tc<EPI_RESID>, k_gemm_tc<EPI_SWIGLU>,
+                 k_gemm_tc<EPI_QKV>, k_gemm_tc<EPI_LMHEAD>}) {
+    cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace mc

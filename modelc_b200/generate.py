@@ -118,6 +118,12 @@ class Session:
         """Back to the primed prompt (its KV kept)."""
         check(lib().mc_spec_rewind(self.handle))
 
+    def tp_init(self, unique_id: bytes, rank: int, world: int):
+        """Join the tensor-parallel group (target weights loaded with the
+        same tp_rank / tp_world); unique_id comes from tp_unique_id() on one
+        rank, shared by the host."""
+        check(lib().mc_session_tp_init(self.handle, bytes(unique_id), rank, world))
+
     def set_seed(self, seed: int):
         """Seed of the stochastic rounds from the next round on."""
         check(lib().mc_spec_set_seed(self.handle, seed))
@@ -147,6 +153,14 @@ class Session:
             self.close()
         except Exception:
             pass
+
+
+def tp_unique_id() -> bytes:
+    """128-byte id of a new tensor-parallel communicator (one rank calls it;
+    the host distributes it)."""
+    buf = C.create_string_buffer(128)
+    check(lib().mc_tp_unique_id(buf))
+    return buf.raw
 
 
 class LlamaDraftModel:

@@ -282,9 +282,10 @@ def synth_weights_torch(cfg: LlamaConfig, seed: int, device, std: float = 0.02,
 
 
 # ------------------------------------------------------------------ device weights
-def _cfg_struct(cfg: LlamaConfig) -> _lib.ModelCfg:
+def _cfg_struct(cfg: LlamaConfig, tp_rank: int = 0, tp_world: int = 1) -> _lib.ModelCfg:
     return _lib.ModelCfg(cfg.mode, cfg.n_layers, cfg.hidden, cfg.n_heads, cfg.n_kv_heads,
-                         cfg.head_dim, cfg.ffn, cfg.vocab, cfg.rope_theta, cfg.eps)
+                         cfg.head_dim, cfg.ffn, cfg.vocab, cfg.rope_theta, cfg.eps, tp_rank,
+                         tp_world)
 
 
 _DT = {"f32": _lib.DTYPE_F32, "i8_tensor": _lib.DTYPE_I8_TENSOR, "i8_row": _lib.DTYPE_I8_ROW,
@@ -325,11 +326,16 @@ class Weights:
     """Device-resident, repacked weights (the reference's Runtime,
     runtime/serve.rs:9-11, without the f32 dequantization)."""
 
-    def __init__(self, tensors: dict, cfg: LlamaConfig, device: int = 0):
+    def __init__(self, tensors: dict, cfg: LlamaConfig, device: int = 0, tp_rank: int = 0,
+                 tp_world: int = 1):
+        """tp_world > 1 keeps this rank's tensor-parallel shard (Megatron:
+        column-parallel q/k/v and gate/up, row-parallel o and down, vocab-
+        parallel head) of the full tensors given."""
         self.cfg = cfg
+        self.tp_rank, self.tp_world = tp_rank, tp_world
         arr, n, keep = _desc_arrays(tensors)
         h = C.c_void_p()
-        c = _cfg_struct(cfg)
+        c = _cfg_struct(cfg, tp_rank, tp_world)
         check(lib().mc_weights_load(arr, n, C.byref(c), device, C.byref(h)))
         del keep
         self.handle = h
