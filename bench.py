@@ -259,6 +259,10 @@ def run_ours(args):
             uid.copy_(torch.frombuffer(bytearray(mb.tp_unique_id()), dtype=torch.uint8))
         torch.distributed.broadcast(uid, 0)
         sess.tp_init(bytes(uid.cpu().numpy().tobytes()), rank, world)
+        if not args.tp_nccl:  # fused NVLink reduction of the row-parallel projections
+            handles = [None] * world
+            torch.distributed.all_gather_object(handles, sess.tp_ipc_handle())
+            sess.tp_open_peers(handles)
     stream = torch.cuda.ExternalStream(sess.stream_ptr, device=torch.device("cuda", local))
 
     def barrier():
@@ -373,7 +377,8 @@ def run_ours(args):
             "config": {"workload": wl.desc, "target": cfg.name, "draft_layers": wl.draft.n_layers,
                        "prompt_len": PROMPT_LEN, "new_tokens": NEW_TOKENS, "gamma": GAMMA,
                        "temperature": wl.temperature, "batch": 1,
-                       "parallelism": (f"tp{world}" if tp else f"replicas{world}") if world > 1
+                       "parallelism": ((f"tp{world}" + ("-nccl" if args.tp_nccl else "-nvlink"))
+                                       if tp else f"replicas{world}") if world > 1
                        else "single",
                        "l2": f"inputs larger than L2 ({wbytes / 1e9:.2f} GB of weights per verify)"},
             "roofline": roof, "cpu_baseline": cpu,
@@ -385,6 +390,8 @@ def run_ours(args):
             "acceptance": {"rounds": rounds, "tokens": tokens,
                            "mean_accepted": round(float(np.mean(accepted)) if accepted else 0.0, 4)},
         }
+    if world > 1:
+        torch.distributed.barrier()  # peers may still write into this rank's buffers
     sess.close()
     if world > 1:
         torch.distributed.barrier()
@@ -518,6 +525,8 @@ def main():
                     help="--profile only: target layers (fewer = smaller device footprint)")
     ap.add_argument("--config", default="llama3-8b", choices=["llama3-8b", "tinyllama", "llama2-70b"],
                     help="workload (default: the headline 8B int8 batch-1 configuration)")
+    ap.add_argument("--tp-nccl", action="store_true",
+                    help="tensor parallelism: NCCL all-reduces instead of the fused NVLink reduction")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: independent requests per GPU instead of tensor parallelism")
     ap.add_argument("--sweep", action="store_true",

@@ -188,6 +188,16 @@ MC_API mc_status mc_spec_rewind(mc_session* s);
 MC_API mc_status mc_tp_unique_id(char id_out[128]);
 MC_API mc_status mc_session_tp_init(mc_session* s, const char id[128], int32_t rank,
                              int32_t world);
+/* Fused tensor-parallel reduction over NVLink (instead of NCCL all-reduces
+ * for the row-parallel projections): every rank exports its reduce buffer
+ * (64-byte CUDA IPC handle), the host gathers the handles of all ranks in
+ * rank order (world x 64 bytes) and each rank opens its peers before its
+ * first decode.  The row-parallel GEMV then stores its partial rows into
+ * every rank's buffer and a reduce kernel adds them in rank order (bounded
+ * waits; an expired wait returns MC_E_TIMEOUT).  All ranks must reach the
+ * host barrier before any destroys its session. */
+MC_API mc_status mc_session_tp_ipc_handle(mc_session* s, char handle_out[64]);
+MC_API mc_status mc_session_tp_open_peers(mc_session* s, const char* handles);
 /* Reseed the stochastic rounds (GenerationConfig::seed per request,
  * generate.rs:146-167); applies from the next round. */
 MC_API mc_status mc_spec_set_seed(mc_session* s, uint64_t seed);

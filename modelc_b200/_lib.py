@@ -27,7 +27,8 @@ EXPORTS = [
     "mc_linear_create", "mc_linear_destroy", "mc_linear_run", "mc_linear_weight_bytes",
     "mc_last_error", "mc_version", "mc_spec_rewind", "mc_spec_verify_launch",
     "mc_session_stream", "mc_session_round_launches", "mc_linear_run_static",
-    "mc_spec_set_seed", "mc_tp_unique_id", "mc_session_tp_init",
+    "mc_spec_set_seed", "mc_tp_unique_id", "mc_session_tp_init", "mc_session_tp_ipc_handle",
+    "mc_session_tp_open_peers",
 ]
 
 
@@ -97,8 +98,12 @@ def lib():
         "mc_spec_set_seed": (i32, [vp, C.c_uint64]),
         "mc_tp_unique_id": (i32, [C.c_char_p]),
         "mc_session_tp_init": (i32, [vp, C.c_char_p, i32, i32]),
+        "mc_session_tp_ipc_handle": (i32, [vp, C.c_char_p]),
+        "mc_session_tp_open_peers": (i32, [vp, C.c_char_p]),
         "mc_tp_unique_id": (i32, [C.c_char_p]),
         "mc_session_tp_init": (i32, [vp, C.c_char_p, i32, i32]),
+        "mc_session_tp_ipc_handle": (i32, [vp, C.c_char_p]),
+        "mc_session_tp_open_peers": (i32, [vp, C.c_char_p]),
         "mc_session_stream": (vp, [vp]),
         "mc_session_round_launches": (i32, [vp]),
         "mc_version": (C.c_char_p, []),

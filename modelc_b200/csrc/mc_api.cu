@@ -171,8 +171,12 @@ static int tc_ksplit(const PMat& W, int nsm) {
 }
 
 // Projections of more than 8 tokens run on the tcgen05 tensor cores when the
-// matrix has the canonical-layout copy (int8 weights).
-static bool use_tc(const PMat& W, int M) { return M > 8 && M <= kMaxTokens && W.wtc; }
+// matrix has the canonical-layout copy (int8 weights) and at least 8192 rows
+// (64 tiles of 128): below that the few tiles and their k-split merges are
+// latency-bound and the GEMV is faster (measured 27 vs 34 us at 4096x4096).
+static bool use_tc(const PMat& W, int M) {
+  return M > 8 && M <= kMaxTokens && W.wtc && W.n_stripes >= 512;
+}
 
 // Source matrix staged on the device: int8 [rows][cols] + f32 row scales, or
 // q4_0 blocks [rows][cols/32][18] (fmt WF_Q4).
@@ -754,13 +758,22 @@ struct mc_session {
   cudaGraphExec_t round_exec = nullptr;
   cudaGraphExec_t verify_exec = nullptr;
   int round_launches = 0;
-  int bps[2][5][7] = {};
+  int bps[2][6][7] = {};
   // MC_TRACE builds: timeline slots handed to the launches of one capture
   bool trace_on = false;
   int trace_next = 0;
   // tensor parallelism (target weights sharded over tp_world ranks)
   nccl::Comm comm = nullptr;
   float* tp_part = nullptr;  // [kMaxTokens][d] partial sums of o / down
+  // P2P reduce region (IPC-exported; see TPArgs), peers' regions once opened
+  void* tp_region = nullptr;
+  size_t tp_red_bytes = 0;
+  unsigned* tp_epoch = nullptr;
+  int* tp_cnt_gemv = nullptr;
+  int* tp_cnt_red = nullptr;
+  bool tp_p2p = false;
+  TPArgs tp{};
+  std::vector<void*> tp_opened;  // peers' regions mapped here
 };
 
 static int trace_slot(mc_session* s) { return s->trace_on ? ++s->trace_next : 0; }
@@ -880,7 +893,22 @@ static mc_status session_alloc(mc_session* s) {
   CK(cudaMemset(s->st_amax, 0, (size_t)2 * kMaxTokens * 4));
   s->st_np_cap = std::max(stripes, 1);
   CKS(s->al.alloc(&s->st_pss, (size_t)kMaxTokens * s->st_np_cap));
-  if (s->tw->tp_world > 1) CKS(s->al.alloc(&s->tp_part, (size_t)kMaxTokens * s->tw->d));
+  if (s->tw->tp_world > 1) {
+    const int R = s->tw->tp_world, dd = s->tw->d;
+    CKS(s->al.alloc(&s->tp_part, (size_t)kMaxTokens * dd));
+    // reduce region: partial slots then flags, one allocation for one IPC handle
+    s->tp_red_bytes = (size_t)2 * R * kMaxTokens * dd * sizeof(float);
+    const size_t bytes = s->tp_red_bytes + 2 * kMaxTP * sizeof(unsigned);
+    CK(cudaMalloc(&s->tp_region, bytes));
+    CK(cudaMemset(s->tp_region, 0, bytes));
+    CKS(s->al.alloc(&s->tp_epoch, 1));
+    const unsigned one = 1u;  // epochs start at 1; flags start at 0
+    CK(cudaMemcpy(s->tp_epoch, &one, 4, cudaMemcpyHostToDevice));
+    CKS(s->al.alloc(&s->tp_cnt_gemv, 1));
+    CKS(s->al.alloc(&s->tp_cnt_red, 1));
+    CK(cudaMemset(s->tp_cnt_gemv, 0, 4));
+    CK(cudaMemset(s->tp_cnt_red, 0, 4));
+  }
   CKS(s->al.alloc(&s->acnt, (size_t)hkv));
   CK(cudaMemset(s->acnt, 0, (size_t)hkv * 4));
   CKS(alloc_kv(s, s->tw, &s->tkv));
@@ -895,7 +923,7 @@ static mc_status session_alloc(mc_session* s) {
   CK(prepare_kernels(qsm, asm_));
   CK(prepare_tc());
   for (int wf : {(int)WF_I8, (int)WF_Q4})
-    for (int epi = 0; epi < 5; ++epi)
+    for (int epi = 0; epi < 6; ++epi)
       for (int nt : {1, 2, 3, 6}) bps_of(s, epi, nt, wf);
   CKS(s->al.alloc(&s->st, 1));
   CK(cudaMemset(s->st, 0, sizeof(SpecState)));
@@ -960,6 +988,8 @@ extern "C" mc_status mc_session_destroy(mc_session* s) {
   if (s->round_exec) cudaGraphExecDestroy(s->round_exec);
   if (s->verify_exec) cudaGraphExecDestroy(s->verify_exec);
   if (s->comm) nccl::g_api.comm_destroy(s->comm);  // after the graphs holding its calls
+  for (void* p : s->tp_opened) cudaIpcCloseMemHandle(p);
+  if (s->tp_region) cudaFree(s->tp_region);
   if (s->h_ids) cudaFreeHost(s->h_ids);
   if (s->stream) cudaStreamDestroy(s->stream);
   s->al.free_all();
@@ -1136,12 +1166,26 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       resid_stats(g, Wm);
       return enq_gemv(s, Wm, EPI_RESID, M, g, next);
     }
+    ResidArgs r{};
+    if (s->tp_p2p) {  // fused: the GEMV stores its rows into every rank's buffer
+      g.tp = s->tp;
+      CKS(enq_gemv(s, Wm, EPI_TP, M, g, next));
+      r.h = s->h;
+      r.d = d;
+      r.M = M;
+      r.pss = s->st_pss;
+      r.amax = slot(ej);
+      r.w = enc_w[ej];
+      r.trace_slot = trace_slot(s);
+      CK(launch_tp_reduce(r, s->tp, s->tp_epoch, s->tp_cnt_red, s->stream, true));
+      prod_np = (d + kResidBlock - 1) / kResidBlock;
+      return MC_OK;
+    }
     g.out = s->tp_part;
     CKS(enq_gemv(s, Wm, EPI_STORE, M, g, next));
     CKS(nccl::check(nccl::g_api.all_reduce(s->tp_part, s->tp_part, (size_t)M * d, nccl::kFloat32,
                                            nccl::kSum, s->comm, s->stream),
                     "all-reduce of row-parallel partial sums"));
-    ResidArgs r{};
     r.h = s->h;
     r.y = s->tp_part;
     r.d = d;
@@ -1560,6 +1604,58 @@ extern "C" mc_status mc_session_tp_init(mc_session* s, const char id[128], int32
   nccl::Comm comm = nullptr;
   CKS(nccl::check(nccl::g_api.comm_init_rank(&comm, world, uid, rank), "ncclCommInitRank"));
   s->comm = comm;
+  return MC_OK;
+}
+
+extern "C" mc_status mc_session_tp_ipc_handle(mc_session* s, char handle_out[64]) {
+  if (!s || !handle_out) return set_err(MC_E_INVALID, "null argument");
+  if (!s->tp_region) return set_err(MC_E_INVALID, "session has no tensor-parallel target");
+  CK(cudaSetDevice(s->dev));
+  cudaIpcMemHandle_t h;
+  CK(cudaIpcGetMemHandle(&h, s->tp_region));
+  static_assert(sizeof(h) == 64, "IPC handle size");
+  memcpy(handle_out, &h, 64);
+  return MC_OK;
+}
+
+extern "C" mc_status mc_session_tp_open_peers(mc_session* s, const char* handles) {
+  if (!s || !handles) return set_err(MC_E_INVALID, "null argument");
+  if (!s->tp_region) return set_err(MC_E_INVALID, "session has no tensor-parallel target");
+  if (s->tp_p2p) return set_err(MC_E_INVALID, "peers already open");
+  if (s->round_exec || s->verify_exec)
+    return set_err(MC_E_INVALID, "open the peers before the first decode");
+  const int R = s->tw->tp_world, rank = s->tw->tp_rank;
+  if (R > kMaxTP) return set_err(MC_E_INVALID, "tp_world %d above %d for peer reduction", R, kMaxTP);
+  CK(cudaSetDevice(s->dev));
+  TPArgs t{};
+  t.rank = rank;
+  t.world = R;
+  t.d = s->tw->d;
+  t.epoch = s->tp_epoch;
+  t.cnt = s->tp_cnt_gemv;
+  t.err = s->err;
+  for (int r = 0; r < R; ++r) {
+    char* base = nullptr;
+    if (r == rank) {
+      base = (char*)s->tp_region;
+    } else {
+      cudaIpcMemHandle_t h;
+      memcpy(&h, handles + 64 * r, 64);
+      void* p = nullptr;
+      cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess) {
+        for (void* q : s->tp_opened) cudaIpcCloseMemHandle(q);
+        s->tp_opened.clear();
+        return set_err(MC_E_CUDA, "opening rank %d's reduce buffer: %s", r, cudaGetErrorString(e));
+      }
+      s->tp_opened.push_back(p);
+      base = (char*)p;
+    }
+    t.red[r] = (float*)base;
+    t.flag[r] = (unsigned*)(base + s->tp_red_bytes);
+  }
+  s->tp = t;
+  s->tp_p2p = true;
   return MC_OK;
 }
 

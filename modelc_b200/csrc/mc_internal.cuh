@@ -62,6 +62,24 @@ enum Epi : int {
   EPI_SWIGLU = 2,  // act[m][i] = silu(gate)*up  (gate/up rows interleaved)
   EPI_QKV = 3,     // RoPE(q), RoPE(k) -> q buffer and paged KV, v -> KV
   EPI_LMHEAD = 4,  // logits + first-index argmax keys (row index + row_offset)
+  EPI_TP = 5,      // row-parallel partial sums stored into every rank's reduce buffer
+};
+
+// Tensor-parallel reduce buffers (one region per rank, opened by the peers
+// through CUDA IPC): partial sums [2 sets][R senders][kMaxTokens][d] floats,
+// then flags [2 sets][kMaxTP] epochs.  A row-parallel GEMV (EPI_TP) of epoch
+// e stores its rows into set e % 2, slot `rank`, of every rank, and its last
+// CTA publishes e in every rank's flags; the reduce kernel waits for all R
+// flags, adds the slots in rank order (identical bits on every rank), then
+// does h += sum and the next encoder's statistics.
+constexpr int kMaxTP = 8;
+struct TPArgs {
+  float* red[kMaxTP];      // every rank's reduce region (index = rank)
+  unsigned* flag[kMaxTP];  // every rank's flags
+  int rank, world, d;
+  const unsigned* epoch;   // this rank's epoch counter
+  int* cnt;                // CTA arrival counter of the GEMV (zeroed)
+  int* err;
 };
 
 struct GemvArgs {
@@ -106,6 +124,7 @@ struct GemvArgs {
   int kv_prefetch;       // QKV: warm L2 with this layer's K/V pages for the attention
   int row_offset;        // LMHEAD: global vocabulary index of packed row 0
   const int4* wtc;       // tcgen05 path: weights in the canonical layout (k_gemm_tc)
+  TPArgs tp;             // EPI_TP
   int trace_slot;        // MC_TRACE builds: 1 + timeline slot, 0 = untraced
 };
 
@@ -202,6 +221,11 @@ struct ResidArgs {
   int trace_slot;
 };
 cudaError_t launch_resid_stats(const ResidArgs& a, cudaStream_t s, bool pdl);
+// The reduce step of EPI_TP (waits for the peers with a bounded spin, then
+// h += sum of the R partials and the statistics as k_resid_stats); advances
+// the epoch.
+cudaError_t launch_tp_reduce(const ResidArgs& a, const TPArgs& t, unsigned* epoch, int* cnt,
+                             cudaStream_t s, bool pdl);
 constexpr int kResidBlock = 1024;
 
 struct SpecState {

@@ -523,7 +523,16 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
       const float sc0 = scale ? scale[prow] : 1.0f, sc1 = scale ? scale[prow + 8] : 1.0f;
       const float y0 = combine_digits(tile + r * ld, m, sc0, e);
       const float y1 = combine_digits(tile + (r + 8) * ld, m, sc1, e);
-      if constexpr (EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_LMHEAD) {
+      if constexpr (EPI == EPI_TP) {
+        // this rank's partial rows into slot `rank` of every rank's buffer
+        const TPArgs& t = a.tp;
+        const size_t off = (((size_t)(__ldcg(t.epoch) & 1u) * t.world + t.rank) * kMaxTokens + m) * t.d;
+        for (int r = 0; r < t.world; ++r) {
+          float* o = t.red[r] + off;
+          if (prow < a.n_out) o[prow] = y0;
+          if (prow + 8 < a.n_out) o[prow + 8] = y1;
+        }
+      } else if constexpr (EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_LMHEAD) {
         float* o = a.out ? a.out + (size_t)m * a.ldo : nullptr;
         if (prow < a.n_out) {
           if constexpr (EPI == EPI_RESID) {
@@ -629,6 +638,26 @@ constexpr int kMaxCtaStripes = 64; // scales staged per CTA (before the wait)
 // order-free) in one tile per stripe; q4_0 sums are f32, so every unit keeps
 // its own partial tile and the last warp adds them in k order (results do
 // not depend on arrival order).
+// End of a row-parallel GEMV: the block barrier orders the CTA's peer stores
+// before thread 0's system-scope fence (release is cumulative over them),
+// then the grid's last CTA publishes the epoch in every rank's flags.
+__device__ __forceinline__ void tp_publish(const TPArgs& t) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const int n = gridDim.x * gridDim.y;
+    if (atomicAdd(t.cnt, 1) == n - 1) {
+      __threadfence_system();
+      const unsigned e = __ldcg(t.epoch);
+      for (int r = 0; r < t.world; ++r)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(t.flag[r] + (e & 1u) * kMaxTP + t.rank),
+                     "r"(e)
+                     : "memory");
+      atomicExch(t.cnt, 0);
+    }
+  }
+}
+
 constexpr int kMaxSplitUnits = 16;  // units per CTA when F > 1 (ns * F <= 14)
 
 template <int NT, int WF>
@@ -891,6 +920,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
     if (threadIdx.x < a.M && sm_keys[threadIdx.x])
       atomicMax(a.keys + threadIdx.x, sm_keys[threadIdx.x]);
   }
+  if constexpr (EPI == EPI_TP) tp_publish(a.tp);
   MC_TRACE_END(a.trace_slot);
 }
 
@@ -917,6 +947,7 @@ static cudaError_t launch_gemv_nt(const GemvArgs& a, int epi, int grid, cudaStre
     case EPI_SWIGLU: return launch_gemv_t<NT, EPI_SWIGLU, WF>(a, grid, s, pdl);
     case EPI_QKV: return launch_gemv_t<NT, EPI_QKV, WF>(a, grid, s, pdl);
     case EPI_LMHEAD: return launch_gemv_t<NT, EPI_LMHEAD, WF>(a, grid, s, pdl);
+    case EPI_TP: return launch_gemv_t<NT, EPI_TP, WF>(a, grid, s, pdl);
   }
   return cudaErrorInvalidValue;
 }
@@ -963,6 +994,7 @@ static int bps_nt(int epi) {
     case EPI_SWIGLU: return bps_t<NT, EPI_SWIGLU, WF>();
     case EPI_QKV: return bps_t<NT, EPI_QKV, WF>();
     case EPI_LMHEAD: return bps_t<NT, EPI_LMHEAD, WF>();
+    case EPI_TP: return bps_t<NT, EPI_TP, WF>();
   }
   return 0;
 }
@@ -1895,6 +1927,95 @@ cudaError_t launch_resid_stats(const ResidArgs& a, cudaStream_t s, bool pdl) {
   return cudaLaunchKernelEx(&cfg, k_resid_stats, a);
 }
 
+// grid (ceil(d / 1024), M), 256 threads: wait (bounded) for the R partials of
+// this epoch, h += their sum in rank order, statistics as k_resid_stats; the
+// last CTA advances the epoch.
+__global__ void __launch_bounds__(256) k_tp_reduce(ResidArgs a, TPArgs t, unsigned* epoch,
+                                                   int* cnt) {
+  MC_TRACE_T0
+  grid_launch_dependents();
+  grid_wait();
+  MC_TRACE_WAITED(a.trace_slot);
+  __shared__ int s_ok;
+  const unsigned e = __ldcg(epoch);
+  const unsigned* fl = t.flag[t.rank] + (e & 1u) * kMaxTP;
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    for (int r = 0; r < t.world && ok; ++r) {
+      unsigned v = 0;
+      long long spin = 0;
+      for (; spin < (1ll << 24); ++spin) {
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(fl + r) : "memory");
+        if (v == e) break;
+      }
+      if (v != e) ok = 0;
+    }
+    if (!ok && t.err) atomicExch(t.err, 1);
+    s_ok = ok;
+  }
+  __syncthreads();
+  const int m = blockIdx.y, blk = blockIdx.x;
+  const float* red = t.red[t.rank] + (size_t)(e & 1u) * t.world * kMaxTokens * a.d;
+  float ss = 0.0f;
+  uint32_t mx = 0u;
+  for (int j = 0; j < kResidBlock / 256; ++j) {
+    const int i = blk * kResidBlock + j * 256 + threadIdx.x;
+    if (i < a.d) {
+      float sum = 0.0f;
+      for (int r = 0; r < t.world; ++r)
+        sum = __fadd_rn(sum, __ldcg(red + ((size_t)r * kMaxTokens + m) * a.d + i));
+      float* hp = a.h + (size_t)m * a.d + i;
+      const float v = __fadd_rn(*hp, s_ok ? sum : __int_as_float(0x7fc00000));
+      *hp = v;
+      ss = __fadd_rn(ss, __fmul_rn(v, v));
+      mx = max(mx, __float_as_uint(fabsf(__fmul_rn(v, a.w ? a.w[i] : 1.0f))));
+    }
+  }
+  __shared__ float rs[8];
+  __shared__ uint32_t rm[8];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    rs[threadIdx.x >> 5] = ss;
+    rm[threadIdx.x >> 5] = mx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tt = 0.0f;
+    uint32_t u = 0u;
+    for (int w = 0; w < 8; ++w) {
+      tt = __fadd_rn(tt, rs[w]);
+      u = max(u, rm[w]);
+    }
+    a.pss[(size_t)m * gridDim.x + blk] = tt;
+    atomicMax(a.amax + m, u);
+    __threadfence();
+    if (atomicAdd(cnt, 1) == (int)(gridDim.x * gridDim.y) - 1) {  // every CTA has read e
+      atomicExch(epoch, e + 1u);
+      atomicExch(cnt, 0);
+    }
+  }
+  MC_TRACE_END(a.trace_slot);
+}
+
+cudaError_t launch_tp_reduce(const ResidArgs& a, const TPArgs& t, unsigned* epoch, int* cnt,
+                             cudaStream_t s, bool pdl) {
+  if (t.world < 2 || t.world > kMaxTP) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.d + kResidBlock - 1) / kResidBlock, a.M);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_tp_reduce, a, t, epoch, cnt);
+}
+
 __global__ void k_set_int(int* p, int v) { *p = v; }
 cudaError_t launch_set_int(int* p, int v, cudaStream_t s) {
   k_set_int<<<1, 1, 0, s>>>(p, v);
@@ -2244,6 +2365,7 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
     __syncthreads();
     if (threadIdx.x < a.M && sm_keys[threadIdx.x]) atomicMax(a.keys + threadIdx.x, sm_keys[threadIdx.x]);
   }
+  if constexpr (EPI == EPI_TP) tp_publish(a.tp);
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 0)
@@ -2310,13 +2432,14 @@ cudaError_t launch_gemm_tc(const GemvArgs& a, int epi, int ksplit, cudaStream_t 
     case EPI_SWIGLU: return launch_tc_t<EPI_SWIGLU>(a, ksplit, s, pdl);
     case EPI_QKV: return launch_tc_t<EPI_QKV>(a, ksplit, s, pdl);
     case EPI_LMHEAD: return launch_tc_t<EPI_LMHEAD>(a, ksplit, s, pdl);
+    case EPI_TP: return launch_tc_t<EPI_TP>(a, ksplit, s, pdl);
   }
   return cudaErrorInvalidValue;
 }
 
 cudaError_t prepare_tc() {
   for (auto f : {k_gemm_tc<EPI_STORE>, k_gemm_tc<EPI_RESID>, k_gemm_tc<EPI_SWIGLU>,
-                 k_gemm_tc<EPI_QKV>, k_gemm_tc<EPI_LMHEAD>}) {
+                 k_gemm_tc<EPI_QKV>, k_gemm_tc<EPI_LMHEAD>, k_gemm_tc<EPI_TP>}) {
     cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
     if (e != cudaSuccess) return e;
   }

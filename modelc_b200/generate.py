@@ -124,6 +124,18 @@ class Session:
         rank, shared by the host."""
         check(lib().mc_session_tp_init(self.handle, bytes(unique_id), rank, world))
 
+    def tp_ipc_handle(self) -> bytes:
+        """64-byte IPC handle of this rank's reduce buffer (fused reduction)."""
+        buf = C.create_string_buffer(64)
+        check(lib().mc_session_tp_ipc_handle(self.handle, buf))
+        return buf.raw
+
+    def tp_open_peers(self, handles):
+        """Open every rank's reduce buffer (handles in rank order); switches the
+        row-parallel reductions from NCCL to the fused NVLink path."""
+        blob = b"".join(bytes(h) for h in handles)
+        check(lib().mc_session_tp_open_peers(self.handle, blob))
+
     def set_seed(self, seed: int):
         """Seed of the stochastic rounds from the next round on."""
         check(lib().mc_spec_set_seed(self.handle, seed))

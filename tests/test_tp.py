@@ -8,8 +8,10 @@ whose per-rank argmax keys merge with a MAX all-reduce into the global
 first-index argmax (generate.rs:1088-1098 tie rule).
 
 GPU (needs 2 devices; skipped otherwise): two ranks, each with its shard of
-the target and a replicated draft, decode greedily with NCCL all-reduces in
-the round graph and produce exactly the oracle's tokens and accepted counts.
+the target and a replicated draft, decode greedily - with NCCL all-reduces
+in the round graph, and with the fused NVLink reduction (partial rows stored
+into every rank's buffer by the GEMV) - and produce exactly the oracle's
+tokens and accepted counts.
 """
 import os
 import sys
@@ -96,25 +98,38 @@ def test_megatron_sharding_reproduces_unsharded_gloo():
     assert all(shape for *_, shape in res)
 
 
-def _gpu_rank(rank, world, uid, cfg_args, prompt, gamma, q):
+def _gpu_rank(rank, world, uid, cfg_args, prompt, gamma, fused, port, q):
     import torch
+    import torch.distributed as dist
     import modelc_b200 as mb
     from modelc_b200.model import LlamaConfig
     torch.cuda.set_device(rank)
-    cfg = LlamaConfig(*cfg_args)
-    tw = mb.synth_weights(cfg, seed=0)
-    dw = mb.synth_weights(cfg.with_layers(1), seed=1)
-    W = mb.Weights(tw, cfg, device=rank, tp_rank=rank, tp_world=world)
-    D = mb.Weights(dw, cfg.with_layers(1), device=rank)
-    s = mb.Session(W, D, gamma=gamma, max_context=128)
-    s.tp_init(uid, rank, world)
-    toks, acc = s.speculative_generate(prompt, 24)
-    s.close()
-    q.put((rank, toks, acc))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = LlamaConfig(*cfg_args)
+        tw = mb.synth_weights(cfg, seed=0)
+        dw = mb.synth_weights(cfg.with_layers(1), seed=1)
+        W = mb.Weights(tw, cfg, device=rank, tp_rank=rank, tp_world=world)
+        D = mb.Weights(dw, cfg.with_layers(1), device=rank)
+        s = mb.Session(W, D, gamma=gamma, max_context=128)
+        s.tp_init(uid, rank, world)
+        if fused:
+            handles = [None] * world
+            dist.all_gather_object(handles, s.tp_ipc_handle())
+            s.tp_open_peers(handles)
+        toks, acc = s.speculative_generate(prompt, 24)
+        dist.barrier()  # no rank frees its reduce buffer while a peer may write it
+        s.close()
+        q.put((rank, toks, acc))
+    finally:
+        dist.destroy_process_group()
 
 
 @pytest.mark.gpu
-def test_tp2_spec_decode_matches_oracle():
+@pytest.mark.parametrize("fused", [False, True], ids=["nccl", "fused-nvlink"])
+def test_tp2_spec_decode_matches_oracle(fused):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -139,7 +154,9 @@ def test_tp2_spec_decode_matches_oracle():
     q = ctx.Queue()
     args = (cfg.n_layers, cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn,
             cfg.vocab, cfg.rope_theta, cfg.eps, cfg.mode, cfg.name)
-    procs = [ctx.Process(target=_gpu_rank, args=(r, 2, uid, args, prompt, 4, q)) for r in range(2)]
+    port = 31000 + (os.getpid() % 2000) + (7 if fused else 0)
+    procs = [ctx.Process(target=_gpu_rank, args=(r, 2, uid, args, prompt, 4, fused, port, q))
+             for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
