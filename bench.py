@@ -48,12 +48,13 @@ class Workload:
     seeds and run lengths of the reference's benchmark table)."""
 
     def __init__(self, name, metric, desc, target, draft, fmt, draft_fmt, prompt_len, new_tokens,
-                 gamma, temperature=0.0, seed=0, accept_mode=0):
+                 gamma, temperature=0.0, seed=0, accept_mode=0, batch=1):
         self.name, self.metric, self.desc = name, metric, desc
         self.target, self.draft = target, draft
         self.fmt, self.draft_fmt = fmt, draft_fmt
         self.prompt_len, self.new_tokens, self.gamma = prompt_len, new_tokens, gamma
         self.temperature, self.seed, self.accept_mode = temperature, seed, accept_mode
+        self.batch = batch  # concurrent requests
 
 
 def workloads():
@@ -63,6 +64,12 @@ def workloads():
         "llama3-8b": Workload("llama3-8b", METRIC, WORKLOAD, mb.LLAMA3_8B,
                               mb.LLAMA3_8B.with_layers(2), "i8_row", "i8_row", PROMPT_LEN,
                               NEW_TOKENS, GAMMA),
+        "llama3-8b-bs8": Workload(
+            "llama3-8b-bs8", "spec-decode tokens/s, 8B-shape int8 bs8 (8 concurrent requests)",
+            "llama3-8b-shape int8-row target + 2-layer int8 draft, 8 concurrent requests, "
+            "prompts 1024, gamma 4, greedy, 256 new each",
+            mb.LLAMA3_8B, mb.LLAMA3_8B.with_layers(2), "i8_row", "i8_row", PROMPT_LEN, NEW_TOKENS,
+            GAMMA, batch=8),
         "tinyllama": Workload(
             "tinyllama", "spec-decode tokens/s, TinyLlama-1.1B-shape q4_0 bs1, stochastic T=0.8",
             "tinyllama-1.1b-shape q4_0 target + 2-layer q4_0 draft, bs1, prompt 512, gamma 5, "
@@ -232,8 +239,9 @@ def build_models(device_index: int, layers: int | None = None, wl: Workload | No
     torch.cuda.empty_cache()
     g = torch.Generator(device="cpu")
     g.manual_seed(2)
-    prompt = torch.randint(0, cfg.vocab, (wl.prompt_len,), generator=g).numpy().astype(np.uint32)
-    return cfg, target, draft, prompt
+    prompts = [torch.randint(0, cfg.vocab, (wl.prompt_len,), generator=g).numpy().astype(np.uint32)
+               for _ in range(wl.batch)]
+    return cfg, target, draft, prompts[0] if wl.batch == 1 else prompts
 
 
 def run_ours(args):
@@ -250,9 +258,12 @@ def run_ours(args):
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     cfg, target, draft, prompt = build_models(local, wl=wl, tp=(rank, world) if tp else (0, 1))
+    B = wl.batch
+    prompts = prompt if B > 1 else [prompt]
     max_ctx = PROMPT_LEN + NEW_TOKENS + 2 * GAMMA + 8
     sess = mb.Session(target, draft, gamma=GAMMA, max_context=max_ctx,
-                      temperature=wl.temperature, seed=wl.seed, accept_mode=wl.accept_mode)
+                      temperature=wl.temperature, seed=wl.seed, accept_mode=wl.accept_mode,
+                      n_requests=B)
     if tp:
         uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
         if rank == 0:
@@ -272,7 +283,8 @@ def run_ours(args):
         torch.cuda.synchronize()
 
     # ---- device-resident decode: prime once, each step decodes 256 tokens
-    sess.prime(prompt)
+    # (per request)
+    sess.prime_batch(prompts)
     for _ in range(args.warmup):
         sess.rewind()
         sess.decode(NEW_TOKENS)
@@ -286,13 +298,16 @@ def run_ours(args):
             sess.rewind()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            n = sess.decode(NEW_TOKENS)
+            sess.decode(NEW_TOKENS)
             e1.record(stream)
             ev.append((e0, e1))
-            toks, acc = sess.read()
-            tokens += len(toks)
-            rounds += len(acc)
-            accepted += acc
+            step_rounds = 0
+            for z in range(B):
+                toks, acc = sess.read(request=z)
+                tokens += len(toks)
+                accepted += acc
+                step_rounds = max(step_rounds, len(acc))
+            rounds += step_rounds  # rounds run (every request takes part in each)
     barrier()
     ms = sum(a.elapsed_time(b) for a, b in ev)
     t_local = torch.tensor([ms / 1e3], device="cuda")
@@ -305,6 +320,7 @@ def run_ours(args):
     value = tok_total / t_total
     ms_per_step = t_total * 1e3 / args.steps
     launches = rounds * sess.round_launches
+    req_rounds = len(accepted)  # request-rounds (the CPU reference runs each)
 
     # ---- verify-forward roofline (dominant kernel set), stream events
     sess.rewind()
@@ -321,8 +337,8 @@ def run_ours(args):
     torch.cuda.synchronize()
     t_ver = e0.elapsed_time(e1) / 1e3 / n_ver
     shards = world if tp else 1  # bytes this GPU reads
-    kv_bytes = 2 * cfg.n_layers * (kv_len + vm) * cfg.n_kv_heads * cfg.head_dim * 4 // shards
-    act_bytes = 2 * cfg.n_layers * vm * (3 * cfg.hidden + 2 * cfg.ffn // shards) * 4
+    kv_bytes = B * 2 * cfg.n_layers * (kv_len + vm) * cfg.n_kv_heads * cfg.head_dim * 4 // shards
+    act_bytes = B * 2 * cfg.n_layers * vm * (3 * cfg.hidden + 2 * cfg.ffn // shards) * 4
     algo = target.streamed_bytes + kv_bytes + act_bytes
     peak, peak_kind = measured_peaks()
     achieved = algo / t_ver / 1e9
@@ -334,20 +350,24 @@ def run_ours(args):
 
     # ---- end to end through the C ABI (host buffers, prime included)
     e2e_ms = []
-    h2d = PROMPT_LEN * 4
+    h2d = B * PROMPT_LEN * 4
     for i in range(max(1, min(args.steps, 3)) + 1):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        toks, acc = sess.speculative_generate(prompt, NEW_TOKENS)
+        if B == 1:
+            res = [sess.speculative_generate(prompt, NEW_TOKENS)]
+        else:
+            res = sess.speculative_generate_batch(prompts, NEW_TOKENS)
         e1.record(stream)
         torch.cuda.synchronize()
         if i > 0:
             e2e_ms.append(e0.elapsed_time(e1))
-    d2h = (len(toks) + len(acc)) * 4
+    e2e_tokens = sum(len(t) for t, _ in res)
+    d2h = sum(len(t) + len(a) for t, a in res) * 4
     e2e_local = torch.tensor([statistics.mean(e2e_ms) / 1e3], device="cuda")
     if world > 1:
         torch.distributed.all_reduce(e2e_local, op=torch.distributed.ReduceOp.MAX)
-    e2e_value = len(toks) * (1 if tp else world) / float(e2e_local.item())
+    e2e_value = e2e_tokens * (1 if tp else world) / float(e2e_local.item())
 
     line = None
     if rank == 0:
@@ -358,8 +378,8 @@ def run_ours(args):
             t_layer, t_head, rl, rh = cpu_sample(nthr, kvl, cfg)
             same = (wl.draft.hidden, wl.draft.ffn, wl.draft.vocab) == (cfg.hidden, cfg.ffn, cfg.vocab)
             tdl, tdh = (t_layer, t_head) if same else cpu_sample(nthr, kvl, wl.draft)[:2]
-            v = cpu_tokens_per_s(t_layer, t_head, rounds, tokens, accepted, GAMMA, cfg.n_layers,
-                                 wl.draft.n_layers, tdl, tdh)
+            v = cpu_tokens_per_s(t_layer, t_head, req_rounds, tokens, accepted, GAMMA,
+                                 cfg.n_layers, wl.draft.n_layers, tdl, tdh)
             cpu = {"value": round(v, 5), "unit": "tokens/s", "cores": nthr, "kind": "port",
                    "sample": (f"oracle row-parallel f32 forward of 1 target layer at KV {kvl} "
                               f"({t_layer * 1e3:.1f} ms, {rl} reps) + LM head ({t_head * 1e3:.1f} ms, "
@@ -376,7 +396,7 @@ def run_ours(args):
             "data": "synthetic (random-init weights N(0,0.02), uniform prompt ids)",
             "config": {"workload": wl.desc, "target": cfg.name, "draft_layers": wl.draft.n_layers,
                        "prompt_len": PROMPT_LEN, "new_tokens": NEW_TOKENS, "gamma": GAMMA,
-                       "temperature": wl.temperature, "batch": 1,
+                       "temperature": wl.temperature, "batch": B,
                        "parallelism": ((f"tp{world}" + ("-nccl" if args.tp_nccl else "-nvlink"))
                                        if tp else f"replicas{world}") if world > 1
                        else "single",
@@ -387,7 +407,7 @@ def run_ours(args):
                     "includes": f"prime ({PROMPT_LEN}-token prefill) + decode"},
             "clocks": clocks, "gpu_launches": int(launches * world),
             "roofline_scope": "per GPU (this rank's weight shard)" if tp else "one GPU",
-            "acceptance": {"rounds": rounds, "tokens": tokens,
+            "acceptance": {"rounds": rounds, "request_rounds": req_rounds, "tokens": tokens,
                            "mean_accepted": round(float(np.mean(accepted)) if accepted else 0.0, 4)},
         }
     if world > 1:
@@ -412,8 +432,8 @@ def run_profile(args):
                       max_context=PROMPT_LEN + NEW_TOKENS + 2 * GAMMA + 8)
     sess.prime(prompt)
     torch.cuda.synchronize()
-    chunks_t = -(-PROMPT_LEN // 16)
-    chunks_d = -(-(PROMPT_LEN - 1) // 16)
+    chunks_t = -(-PROMPT_LEN // 64)  # prefill forwards of up to 64 tokens
+    chunks_d = -(-(PROMPT_LEN - 1) // 64)
     per_t = (sess.round_launches - 1 - GAMMA * 21)
     print(json.dumps({"prime_launches": chunks_t * (1 + per_t) + chunks_d * (1 + 21),
                       "verify_launches": per_t, "round_launches": sess.round_launches}),
@@ -523,7 +543,8 @@ def main():
     ap.add_argument("--profile", action="store_true", help="short run for ncu launch lists")
     ap.add_argument("--layers", type=int, default=None,
                     help="--profile only: target layers (fewer = smaller device footprint)")
-    ap.add_argument("--config", default="llama3-8b", choices=["llama3-8b", "tinyllama", "llama2-70b"],
+    ap.add_argument("--config", default="llama3-8b",
+                    choices=["llama3-8b", "llama3-8b-bs8", "tinyllama", "llama2-70b"],
                     help="workload (default: the headline 8B int8 batch-1 configuration)")
     ap.add_argument("--tp-nccl", action="store_true",
                     help="tensor parallelism: NCCL all-reduces instead of the fused NVLink reduction")

@@ -120,6 +120,13 @@ typedef struct mc_spec_cfg {
                            sample equals x (generate.rs:695-726).  Random
                            numbers: Philox4x32-10 keyed by seed, counter
                            (slot, round). */
+  int32_t n_requests;   /* concurrent requests B (0 or 1: one).  B > 1: B
+                           independent greedy requests, each with its own KV
+                           capacity max_context, decoded in lock step: every
+                           round runs the gamma draft steps over B tokens,
+                           one verify forward over B x (gamma or gamma+1)
+                           positions, and B acceptances.  B x (gamma +
+                           bonus) <= 64. */
 } mc_spec_cfg;
 
 /* Load (quantize-free) weights to the device and repack them for the
@@ -169,12 +176,32 @@ MC_API mc_status mc_speculative_generate(mc_session* s, const uint32_t* prompt,
                                   int32_t* accepted, int32_t accepted_cap,
                                   int32_t* n_rounds);
 
+/* Batched speculative_generate: n_requests (= the session's B) prompts,
+ * concatenated in `prompts` with lengths `lens`.  Request z's generated ids go
+ * to out + z * out_stride (up to out_stride ids, count in n_out[z]), its
+ * per-round accepted counts to accepted + z * accepted_stride (NULL: not
+ * returned) and its round count to n_rounds[z] (may be NULL).  Every request
+ * produces exactly the tokens it would produce alone. */
+MC_API mc_status mc_speculative_generate_batch(mc_session* s, const uint32_t* prompts,
+                                        const int32_t* lens, int32_t n_requests,
+                                        int32_t max_tokens, uint32_t* out,
+                                        int32_t out_stride, int32_t* n_out,
+                                        int32_t* accepted, int32_t accepted_stride,
+                                        int32_t* n_rounds);
+
 /* Device-resident variants for measurement: prompt already primed with
- * mc_spec_prime; mc_spec_decode runs the round loop only. */
+ * mc_spec_prime; mc_spec_decode runs the round loop only (every request
+ * until it holds >= max_tokens generated ids; n_generated = their sum). */
 MC_API mc_status mc_spec_prime(mc_session* s, const uint32_t* prompt, int32_t n_prompt);
+MC_API mc_status mc_spec_prime_batch(mc_session* s, const uint32_t* prompts,
+                              const int32_t* lens, int32_t n_requests);
 MC_API mc_status mc_spec_decode(mc_session* s, int32_t max_tokens, int32_t* n_generated);
 MC_API mc_status mc_spec_read(mc_session* s, uint32_t* out, int32_t cap, int32_t* n_out,
                        int32_t* accepted, int32_t accepted_cap, int32_t* n_rounds);
+/* mc_spec_read for request z of a batched session. */
+MC_API mc_status mc_spec_read_request(mc_session* s, int32_t z, uint32_t* out, int32_t cap,
+                               int32_t* n_out, int32_t* accepted, int32_t accepted_cap,
+                               int32_t* n_rounds);
 /* Restart decoding from the primed prompt: the prompt's KV is kept, the
  * generated tokens and round log are dropped. */
 MC_API mc_status mc_spec_rewind(mc_session* s);

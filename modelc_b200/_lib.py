@@ -28,7 +28,8 @@ EXPORTS = [
     "mc_last_error", "mc_version", "mc_spec_rewind", "mc_spec_verify_launch",
     "mc_session_stream", "mc_session_round_launches", "mc_linear_run_static",
     "mc_spec_set_seed", "mc_tp_unique_id", "mc_session_tp_init", "mc_session_tp_ipc_handle",
-    "mc_session_tp_open_peers",
+    "mc_session_tp_open_peers", "mc_speculative_generate_batch", "mc_spec_prime_batch",
+    "mc_spec_read_request",
 ]
 
 
@@ -54,7 +55,8 @@ class TensorDesc(C.Structure):
 class SpecCfg(C.Structure):
     _fields_ = [("gamma", C.c_int32), ("max_context", C.c_int32), ("bonus", C.c_int32),
                 ("temperature", C.c_float), ("seed", C.c_uint64),
-                ("cancel", C.POINTER(C.c_int32)), ("accept_mode", C.c_int32)]
+                ("cancel", C.POINTER(C.c_int32)), ("accept_mode", C.c_int32),
+                ("n_requests", C.c_int32)]
 
 
 _lib = None
@@ -100,10 +102,10 @@ def lib():
         "mc_session_tp_init": (i32, [vp, C.c_char_p, i32, i32]),
         "mc_session_tp_ipc_handle": (i32, [vp, C.c_char_p]),
         "mc_session_tp_open_peers": (i32, [vp, C.c_char_p]),
-        "mc_tp_unique_id": (i32, [C.c_char_p]),
-        "mc_session_tp_init": (i32, [vp, C.c_char_p, i32, i32]),
-        "mc_session_tp_ipc_handle": (i32, [vp, C.c_char_p]),
-        "mc_session_tp_open_peers": (i32, [vp, C.c_char_p]),
+        "mc_speculative_generate_batch": (i32, [vp, u32p, i32p, i32, i32, u32p, i32, i32p, i32p,
+                                                i32, i32p]),
+        "mc_spec_prime_batch": (i32, [vp, u32p, i32p, i32]),
+        "mc_spec_read_request": (i32, [vp, i32, u32p, i32, i32p, i32p, i32, i32p]),
         "mc_session_stream": (vp, [vp]),
         "mc_session_round_launches": (i32, [vp]),
         "mc_version": (C.c_char_p, []),

@@ -170,12 +170,69 @@ static int tc_ksplit(const PMat& W, int nsm) {
   return std::max(1, std::min(k, W.KB / 16));
 }
 
-// Projections of more than 8 tokens run on the tcgen05 tensor cores when the
-// matrix has the canonical-layout copy (int8 weights) and at least 8192 rows
-// (64 tiles of 128): below that the few tiles and their k-split merges are
-// latency-bound and the GEMV is faster (measured 27 vs 34 us at 4096x4096).
+// Projections run on the tcgen05 tensor cores when the matrix has the
+// canonical-layout copy (int8 weights) and either more than 16 tokens (the
+// GEMV would stream the weights once per 16) or 9..16 tokens and at least
+// 8192 rows (64 tiles of 128): below that the few tiles and their k-split
+// merges are latency-bound and the GEMV is faster (measured 27 vs 34 us at
+// 4096x4096).
 static bool use_tc(const PMat& W, int M) {
-  return M > 8 && M <= kMaxTokens && W.wtc && W.n_stripes >= 512;
+  if (!W.wtc || M > kMaxTokens) return false;
+  if (M > kGroupTokens) return true;
+  return M > 8 && W.n_stripes >= 512;
+}
+
+// CTAs per GEMV launch.  q4_0 partial sums are f32 and the grid sets their
+// k-split, so a q4_0 grid must not depend on the token count: it uses the
+// smallest occupancy over all token tiles.
+#ifndef MC_GEMV_MAX_BPS
+#define MC_GEMV_MAX_BPS 0  // 0: as many CTAs per SM as occupancy allows
+#endif
+template <class BpsFn>
+static int gemv_grid(const PMat& W, int nsm, int nt, BpsFn bps) {
+  int b = bps(nt);
+  if (W.fmt == WF_Q4)
+    for (int t : {1, 2, 3, 6}) b = std::min(b, bps(t));
+  if (MC_GEMV_MAX_BPS > 0) b = std::min(b, MC_GEMV_MAX_BPS);
+  return std::min(W.n_stripes, nsm * std::max(b, 1));
+}
+
+// One projection of M <= kMaxTokens tokens whose digits the encoder wrote
+// for it: the tcgen05 GEMM, or the GEMV once per group of 16 tokens (each
+// group's digits are their own operand block).  a carries the epilogue, the
+// workspace and the next-matrix prefetch; the prefetch goes with the last
+// group.
+template <class BpsFn>
+static cudaError_t run_projection(const PMat& W, int epi, int M, GemvArgs a, int nsm,
+                                  cudaStream_t st, BpsFn bps) {
+  a.w = W.w;
+  a.scale = W.scale;
+  a.qscale = W.qscale;
+  a.KB = W.KB;
+  a.n_stripes = W.n_stripes;
+  if (use_tc(W, M)) {
+    a.wtc = W.wtc;
+    a.M = M;
+    a.m0 = 0;
+    return launch_gemm_tc(a, epi, tc_ksplit(W, nsm), st, true);
+  }
+  const int nt = nt_for_tokens(M);
+  const int G = groups_for_tokens(M);
+  const uint8_t* x = a.x;
+  const int* xexp = a.xexp;
+  const void* next_w = a.next_w;
+  const size_t group_bytes = (size_t)W.KB * 64 * nt * 4;
+  const int grid = gemv_grid(W, nsm, nt, bps);
+  for (int g = 0; g < G; ++g) {
+    a.x = x + g * group_bytes;
+    a.xexp = xexp + g * kGroupTokens;
+    a.m0 = g * kGroupTokens;
+    a.M = std::min(kGroupTokens, M - a.m0);
+    a.next_w = (g == G - 1) ? next_w : nullptr;
+    cudaError_t e = launch_gemv(a, epi, nt, W.fmt, grid, st, true);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 // Source matrix staged on the device: int8 [rows][cols] + f32 row scales, or
@@ -492,7 +549,7 @@ static mc_status load_model(const mc_tensor_desc* ts, size_t n, const mc_model_c
   if (W->H <= 0 || W->Hkv <= 0 || W->hd <= 0 || W->H % W->Hkv)
     return set_err(MC_E_SHAPE, "bad head geometry H=%d Hkv=%d hd=%d", W->H, W->Hkv, W->hd);
   if (W->hd % 2) return set_err(MC_E_SHAPE, "odd head_dim %d is not supported", W->hd);
-  if (W->H / W->Hkv * kMaxTokens > 128)
+  if (W->H / W->Hkv > 128)  // query rows of one attention CTA
     return set_err(MC_E_SHAPE, "query group %d too large", W->H / W->Hkv);
   W->half = W->hd / 2;
   W->half_p = round_up(W->half, 8);
@@ -708,8 +765,8 @@ struct KVSet {
   float* k = nullptr;
   float* v = nullptr;
   size_t layer_stride = 0;  // floats per layer
-  int* page_table = nullptr;
-  int n_pages = 0;
+  int* page_table = nullptr;  // [requests][n_pages]
+  int n_pages = 0;            // pages per request
   float* rope_cos = nullptr;
   float* rope_sin = nullptr;
 };
@@ -718,7 +775,9 @@ struct mc_session {
   const mc_weights* tw = nullptr;
   const mc_weights* dw = nullptr;
   mc_spec_cfg cfg{};
-  int cap = 0;
+  int B = 1;           // concurrent requests
+  int cap = 0;         // KV capacity per request (tokens)
+  int ctx_stride = 0;  // ids between the requests' contexts (and round logs)
   int dev = 0;
   int nsm = 0;
   cudaStream_t stream = nullptr;
@@ -744,15 +803,17 @@ struct mc_session {
   float* st_pss = nullptr;      // [kMaxTokens][max stripes]
   int st_np_cap = 0;
   KVSet tkv, dkv;
-  // device-resident speculative state
-  SpecState* st = nullptr;
-  uint32_t* ctx = nullptr;
-  int* acc_log = nullptr;
+  // device-resident speculative state, one per request
+  SpecState* st = nullptr;      // [B]
+  uint32_t* ctx = nullptr;      // [B][ctx_stride]
+  int* acc_log = nullptr;       // [B][ctx_stride]
+  unsigned long long* fkeys = nullptr;  // argmax keys of plain forwards [kMaxTokens]
   uint32_t* ids = nullptr;
   int* pos = nullptr;  // [2]: target / draft length for the plain forward API
-  // host mirrors
+  // host mirrors (request 0 for the plain forward API)
   int lt = 0, ld = 0;
   int prompt_len = 0;
+  std::vector<int> prompt_lens;  // per request
   std::vector<uint32_t> draft_tokens;  // tokens in the draft KV (mc_draft)
   uint32_t* h_ids = nullptr;           // pinned staging
   cudaGraphExec_t round_exec = nullptr;
@@ -784,32 +845,20 @@ static int bps_of(mc_session* s, int epi, int nt, int wf) {
   return b;
 }
 
-// CTAs per GEMV launch.  q4_0 partial sums are f32 and the grid sets their
-// k-split, so a q4_0 grid must not depend on the token count: it uses the
-// smallest occupancy over all token tiles.
-#ifndef MC_GEMV_MAX_BPS
-#define MC_GEMV_MAX_BPS 0  // 0: as many CTAs per SM as occupancy allows
-#endif
-template <class BpsFn>
-static int gemv_grid(const PMat& W, int nsm, int nt, BpsFn bps) {
-  int b = bps(nt);
-  if (W.fmt == WF_Q4)
-    for (int t : {1, 2, 3, 6}) b = std::min(b, bps(t));
-  if (MC_GEMV_MAX_BPS > 0) b = std::min(b, MC_GEMV_MAX_BPS);
-  return std::min(W.n_stripes, nsm * std::max(b, 1));
-}
-
+// Paged K/V of every request: request z owns pages [z * n_pages, (z + 1) *
+// n_pages), listed in row z of the page table.
 static mc_status alloc_kv(mc_session* s, const mc_weights* W, KVSet* kv) {
   kv->n_pages = (s->cap + kPage - 1) / kPage;
-  kv->layer_stride = (size_t)kv->n_pages * W->Hkv * kPage * W->hdp;
+  const int pages = kv->n_pages * s->B;
+  kv->layer_stride = (size_t)pages * W->Hkv * kPage * W->hdp;
   const size_t total = kv->layer_stride * std::max(W->L, 1);
   CKS(s->al.alloc(&kv->k, total));
   CKS(s->al.alloc(&kv->v, total));
   CK(cudaMemset(kv->k, 0, total * 4));
   CK(cudaMemset(kv->v, 0, total * 4));
-  CKS(s->al.alloc(&kv->page_table, (size_t)kv->n_pages));
-  std::vector<int> pt(kv->n_pages);
-  for (int i = 0; i < kv->n_pages; ++i) pt[i] = i;
+  CKS(s->al.alloc(&kv->page_table, (size_t)pages));
+  std::vector<int> pt(pages);
+  for (int i = 0; i < pages; ++i) pt[i] = i;
   CK(cudaMemcpy(kv->page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice));
   // RoPE factors computed on the host with libm exactly as transformer.rs:926-927:
   // theta = pos * base^(-i/half) in f32, then sin/cos.
@@ -864,26 +913,30 @@ static mc_status session_alloc(mc_session* s) {
     F = std::max(F, W->F);
     V = std::max(V, W->V);
     stripes = std::max(stripes, max_stripes(W));
-    const size_t rows = (size_t)(W->H / W->Hkv) * kChunk;
+    // attention partials: query blocks x block capacity < 2 x tokens per
+    // forward (blocks of qblk <= seq_len tokens)
+    const size_t rows = (size_t)(W->H / W->Hkv) * 2 * kMaxTokens;
     po = std::max(po, (size_t)W->Hkv * rows * W->hdp);
     pml = std::max(pml, (size_t)W->Hkv * rows * 2);
     hkv = std::max(hkv, W->Hkv);
   }
-  const int M = kChunk;
+  const int M = kMaxTokens;
   CKS(s->al.alloc(&s->h, (size_t)M * d));
-  CKS(s->al.alloc(&s->xq, (size_t)kp * 8 * 6));
-  CK(cudaMemset(s->xq, 0, (size_t)kp * 8 * 6));
+  // digits: 48 bytes per input column per group of 16 tokens
+  CKS(s->al.alloc(&s->xq, (size_t)kp * 48 * kMaxGroups));
+  CK(cudaMemset(s->xq, 0, (size_t)kp * 48 * kMaxGroups));
   CKS(s->al.alloc(&s->xexp, (size_t)M));
   CKS(s->al.alloc(&s->qb, (size_t)M * hq));
   CKS(s->al.alloc(&s->attn, (size_t)M * hq));
   CK(cudaMemset(s->attn, 0, (size_t)M * hq * 4));
   CKS(s->al.alloc(&s->act, (size_t)M * std::max(F, 1)));
   CKS(s->al.alloc(&s->logits, (size_t)M * V));
-  if (s->cfg.temperature > 0.0f) CKS(s->al.alloc(&s->dlogits, (size_t)kMaxTokens * V));
-  CKS(s->al.alloc(&s->ws, (size_t)stripes * 32 * 24));
-  CK(cudaMemset(s->ws, 0, (size_t)stripes * 32 * 24 * 4));
-  CKS(s->al.alloc(&s->cnt, (size_t)stripes));
-  CK(cudaMemset(s->cnt, 0, (size_t)stripes * 4));
+  if (s->cfg.temperature > 0.0f) CKS(s->al.alloc(&s->dlogits, (size_t)kGroupTokens * V));
+  // split-K workspace: one 16 x 48 int tile and counter per (stripe, group)
+  CKS(s->al.alloc(&s->ws, (size_t)stripes * kMaxGroups * 16 * 48));
+  CK(cudaMemset(s->ws, 0, (size_t)stripes * kMaxGroups * 16 * 48 * 4));
+  CKS(s->al.alloc(&s->cnt, (size_t)stripes * kMaxGroups));
+  CK(cudaMemset(s->cnt, 0, (size_t)stripes * kMaxGroups * 4));
   const int n_pages = (s->cap + kPage - 1) / kPage;
   CKS(s->al.alloc(&s->part_o, po * n_pages));
   CKS(s->al.alloc(&s->part_ml, pml * n_pages));
@@ -909,8 +962,8 @@ static mc_status session_alloc(mc_session* s) {
     CK(cudaMemset(s->tp_cnt_gemv, 0, 4));
     CK(cudaMemset(s->tp_cnt_red, 0, 4));
   }
-  CKS(s->al.alloc(&s->acnt, (size_t)hkv));
-  CK(cudaMemset(s->acnt, 0, (size_t)hkv * 4));
+  CKS(s->al.alloc(&s->acnt, (size_t)hkv * 2 * kMaxTokens));
+  CK(cudaMemset(s->acnt, 0, (size_t)hkv * 2 * kMaxTokens * 4));
   CKS(alloc_kv(s, s->tw, &s->tkv));
   if (s->dw) CKS(alloc_kv(s, s->dw, &s->dkv));
   // kernel limits and occupancy are settled here, never inside a capture
@@ -918,21 +971,24 @@ static mc_status session_alloc(mc_session* s) {
   for (const mc_weights* W : ws) {
     if (!W) continue;
     qsm = std::max(qsm, (size_t)max_kp(W) * sizeof(float));
-    asm_ = std::max(asm_, attention_smem_bytes(W->H / W->Hkv, kChunk, W->hdp, kPage));
+    const int G = W->H / W->Hkv;
+    asm_ = std::max(asm_, attention_smem_bytes(G, attention_qblk(G, kMaxTokens), W->hdp, kPage));
   }
   CK(prepare_kernels(qsm, asm_));
   CK(prepare_tc());
   for (int wf : {(int)WF_I8, (int)WF_Q4})
     for (int epi = 0; epi < 6; ++epi)
       for (int nt : {1, 2, 3, 6}) bps_of(s, epi, nt, wf);
-  CKS(s->al.alloc(&s->st, 1));
-  CK(cudaMemset(s->st, 0, sizeof(SpecState)));
-  CKS(s->al.alloc(&s->ctx, (size_t)s->cap + 8));
-  CKS(s->al.alloc(&s->acc_log, (size_t)s->cap + 8));
+  CKS(s->al.alloc(&s->st, (size_t)s->B));
+  CK(cudaMemset(s->st, 0, sizeof(SpecState) * s->B));
+  s->ctx_stride = s->cap + 8;
+  CKS(s->al.alloc(&s->ctx, (size_t)s->B * s->ctx_stride));
+  CKS(s->al.alloc(&s->acc_log, (size_t)s->B * s->ctx_stride));
+  CKS(s->al.alloc(&s->fkeys, (size_t)kMaxTokens));
   CKS(s->al.alloc(&s->ids, (size_t)M));
   CKS(s->al.alloc(&s->pos, 2));
   CK(cudaMemset(s->pos, 0, 8));
-  CK(cudaMallocHost(&s->h_ids, (size_t)std::max(s->cap, M) * 4));
+  CK(cudaMallocHost(&s->h_ids, (size_t)std::max(s->B * s->ctx_stride, M) * 4));
   return MC_OK;
 }
 
@@ -942,8 +998,14 @@ extern "C" mc_status mc_session_create(const mc_weights* target, const mc_weight
   *out = nullptr;
   if (draft && draft->dev != target->dev)
     return set_err(MC_E_INVALID, "target and draft live on different devices");
-  if (cfg->gamma < 0 || cfg->gamma + 1 > kMaxTokens)
-    return set_err(MC_E_INVALID, "gamma %d outside [0, %d]", cfg->gamma, kMaxTokens - 1);
+  if (cfg->gamma < 0 || cfg->gamma + 1 > kGroupTokens)
+    return set_err(MC_E_INVALID, "gamma %d outside [0, %d]", cfg->gamma, kGroupTokens - 1);
+  const int B = std::max(1, (int)cfg->n_requests);
+  if (cfg->n_requests < 0 || B * (cfg->gamma + (cfg->bonus ? 1 : 0)) > kMaxTokens)
+    return set_err(MC_E_INVALID, "%d requests x %d verify positions exceed %d tokens per forward",
+                   B, cfg->gamma + (cfg->bonus ? 1 : 0), kMaxTokens);
+  if (B > 1 && cfg->temperature > 0.0f)
+    return set_err(MC_E_INVALID, "batched sessions decode greedily (temperature 0)");
   if (cfg->max_context <= 0) return set_err(MC_E_INVALID, "max_context must be positive");
   if (!(cfg->temperature >= 0.0f) || !isfinite(cfg->temperature))
     return set_err(MC_E_INVALID, "temperature must be finite and >= 0");
@@ -963,6 +1025,7 @@ extern "C" mc_status mc_session_create(const mc_weights* target, const mc_weight
   s->tw = target;
   s->dw = draft;
   s->cfg = *cfg;
+  s->B = B;
   s->dev = target->dev;
   s->cap = round_up(cfg->max_context + kChunk + 2, kPage);
   cudaDeviceGetAttribute(&s->nsm, cudaDevAttrMultiProcessorCount, s->dev);
@@ -1083,34 +1146,26 @@ static mc_status enq_gemv(mc_session* s, const PMat& W, int epi, int M, GemvArgs
                                                                                : kFragBytes);
     a.next_pf_bytes = std::min(a.next_bytes, kNextPrefetch);
   }
-  a.w = W.w;
-  a.scale = W.scale;
-  a.qscale = W.qscale;
   a.x = s->xq;
   a.xexp = s->xexp;
-  a.KB = W.KB;
-  a.n_stripes = W.n_stripes;
-  a.M = M;
   a.ws = s->ws;
   a.cnt = s->cnt;
   a.err = s->err;
   a.trace_slot = trace_slot(s);
-  const int nt = nt_for_tokens(M);
-  if (use_tc(W, M)) {
-    a.wtc = W.wtc;
-    CK(launch_gemm_tc(a, epi, tc_ksplit(W, s->nsm), s->stream, true));
-    return MC_OK;
-  }
-  const int grid = gemv_grid(W, s->nsm, nt, [&](int t) { return bps_of(s, epi, t, W.fmt); });
-  CK(launch_gemv(a, epi, nt, W.fmt, grid, s->stream, true));
+  CK(run_projection(W, epi, M, a, s->nsm, s->stream,
+                    [&](int t) { return bps_of(s, epi, t, W.fmt); }));
   return MC_OK;
 }
 
 // One batched forward of M tokens through W (forward_llama_cached,
-// transformer.rs:64-96, for M positions at once).
+// transformer.rs:64-96, for M positions at once): sm.seq_len tokens of each
+// of M / sm.seq_len sequences, whose positions, KV page-table rows and key
+// slots sm maps (one sequence: sm.seq_len = M).
 static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv, int M,
-                             EmbedArgs ea, const int* pos_ptr, int pos_add,
+                             SeqMap sm, EmbedArgs ea, const int* pos_ptr, int pos_add,
                              unsigned long long* keys, float* logits_dev) {
+  if (M < 1 || M > kMaxTokens || sm.seq_len < 1 || M % sm.seq_len)
+    return set_err(MC_E_INVALID, "forward of %d tokens in sequences of %d", M, sm.seq_len);
   if (!W->has_head) return set_err(MC_E_NO_HEAD, "model has no lm_head and no embedding");
   const bool tp = W->tp_world > 1;
   if (tp && !s->comm) return set_err(MC_E_INVALID, "tensor-parallel weights: call mc_session_tp_init");
@@ -1122,6 +1177,8 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
   ea.vocab = W->V;
   ea.M = M;
   ea.h = s->h;
+  ea.seq = sm;
+  ea.ctx_stride = s->ctx_stride;
   ea.zero_keys = keys;
   ea.n_zero = keys ? M : 0;
   // Encoders in launch order with the RMSNorm weight each applies (nullptr:
@@ -1167,7 +1224,9 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       return enq_gemv(s, Wm, EPI_RESID, M, g, next);
     }
     ResidArgs r{};
-    if (s->tp_p2p) {  // fused: the GEMV stores its rows into every rank's buffer
+    // fused: the GEMV stores its rows into every rank's buffer (one launch,
+    // whose last CTA publishes the epoch: not for the per-group GEMV passes)
+    if (s->tp_p2p && (M <= kGroupTokens || use_tc(Wm, M))) {
       g.tp = s->tp;
       CKS(enq_gemv(s, Wm, EPI_TP, M, g, next));
       r.h = s->h;
@@ -1222,6 +1281,7 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       a.page_table = kv.page_table;
       a.pos_ptr = pos_ptr;
       a.pos_add = pos_add;
+      a.seq = sm;
       a.rope_cos = kv.rope_cos;
       a.rope_sin = kv.rope_sin;
       a.half_p = W->half_p;
@@ -1240,6 +1300,8 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       t.page_table = kv.page_table;
       t.pos_ptr = pos_ptr;
       t.pos_add = pos_add;
+      t.seq = sm;
+      t.qblk = attention_qblk(W->H / W->Hkv, sm.seq_len);
       t.M = M;
       t.H = W->H;
       t.Hkv = W->Hkv;
@@ -1288,12 +1350,18 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
   hd.ldo = W->V;
   hd.n_out = W->V_loc;
   hd.keys = keys;
+  hd.seq = sm;
   hd.row_offset = W->head_row0;
   CKS(enq_gemv(s, W->head, EPI_LMHEAD, M, hd));
-  if (tp)  // vocab-parallel head: the largest (value, lowest index) key wins
-    CKS(nccl::check(nccl::g_api.all_reduce(keys, keys, (size_t)M, nccl::kUint64, nccl::kMax,
-                                           s->comm, s->stream),
-                    "all-reduce of argmax keys"));
+  if (tp) {  // vocab-parallel head: the largest (value, lowest index) key wins
+    // the key slots of each sequence are contiguous (seq_len of them)
+    const int n_seq = M / sm.seq_len;
+    for (int z = 0; z < n_seq; ++z)
+      CKS(nccl::check(nccl::g_api.all_reduce(keys + (size_t)z * sm.key_stride,
+                                             keys + (size_t)z * sm.key_stride, (size_t)sm.seq_len,
+                                             nccl::kUint64, nccl::kMax, s->comm, s->stream),
+                      "all-reduce of argmax keys"));
+  }
   return MC_OK;
 }
 
@@ -1314,7 +1382,8 @@ static mc_status forward_api(mc_session* s, int which, const uint32_t* ids, int 
     EmbedArgs ea{};
     ea.src = SRC_IDS;
     ea.ids = s->ids;
-    CKS(enq_forward(s, W, kv, M, ea, s->pos + which, 0, s->st->tkeys, logits ? s->logits : nullptr));
+    CKS(enq_forward(s, W, kv, M, SeqMap{M, 0, 0, 0}, ea, s->pos + which, 0, s->fkeys,
+                    logits ? s->logits : nullptr));
     if (logits)
       CK(cudaMemcpyAsync(logits + (size_t)c0 * W->V, s->logits, (size_t)M * W->V * 4,
                          cudaMemcpyDeviceToHost, s->stream));
@@ -1364,7 +1433,7 @@ extern "C" mc_status mc_draft(mc_session* s, const uint32_t* context, int32_t n,
   for (int j = 0; j < gamma; ++j) {
     unsigned long long key = 0;
     const int last = (int)((rest.size() - 1) % kChunk);
-    CK(cudaMemcpy(&key, &s->st->tkeys[last], 8, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(&key, &s->fkeys[last], 8, cudaMemcpyDeviceToHost));
     out[j] = key_index(key);
     if (j + 1 < gamma) {
       rest.assign(1, out[j]);
@@ -1382,6 +1451,8 @@ static int forward_launches(const mc_weights* W) {
   return n;
 }
 
+// Verify forward of every request: vm positions each (request z's tokens are
+// z * vm .. z * vm + vm - 1), at the request's own target length.
 static mc_status enq_verify(mc_session* s, float* logits = nullptr) {
   const int vm = s->cfg.gamma + (s->cfg.bonus ? 1 : 0);
   EmbedArgs ea{};
@@ -1389,7 +1460,8 @@ static mc_status enq_verify(mc_session* s, float* logits = nullptr) {
   ea.ctx = s->ctx;
   ea.off = &s->st->ctx_len;
   ea.keys = s->st->dkeys;
-  return enq_forward(s, s->tw, s->tkv, vm, ea, &s->st->lt, 0, s->st->tkeys, logits);
+  const SeqMap sm{vm, kStateInts, s->tkv.n_pages, kStateKeys};
+  return enq_forward(s, s->tw, s->tkv, vm * s->B, sm, ea, &s->st->lt, 0, s->st->tkeys, logits);
 }
 
 static mc_status capture_verify(mc_session* s) {
@@ -1425,6 +1497,8 @@ static mc_status capture_round(mc_session* s) {
   mc_status rc = MC_OK;
   const bool stochastic = s->cfg.temperature > 0.0f;
   const int V = s->tw->V;
+  // draft step j: one token per request (request z's at its draft length + j)
+  const SeqMap dsm{1, kStateInts, s->dkv.n_pages, kStateKeys};
   for (int j = 0; j < dsteps && rc == MC_OK; ++j) {
     EmbedArgs ea{};
     if (j == 0) {
@@ -1436,7 +1510,7 @@ static mc_status capture_round(mc_session* s) {
       ea.keys = &st->dkeys[j - 1];
     }
     float* dl = stochastic && j < g ? s->dlogits + (size_t)j * V : nullptr;
-    rc = enq_forward(s, s->dw, s->dkv, 1, ea, &st->ld, j, &st->dkeys[j], dl);
+    rc = enq_forward(s, s->dw, s->dkv, s->B, dsm, ea, &st->ld, j, &st->dkeys[j], dl);
     if (rc == MC_OK && dl) {  // x_j ~ softmax(q_j / T) replaces the argmax key
       cudaError_t e = launch_sample_draft(st, dl, V, j, &st->dkeys[j], s->stream, true);
       if (e != cudaSuccess) rc = set_err(MC_E_CUDA, "draft sample: %s", cudaGetErrorString(e));
@@ -1447,7 +1521,8 @@ static mc_status capture_round(mc_session* s) {
     cudaError_t e = stochastic
                         ? launch_accept_stochastic(st, s->ctx, s->acc_log, vm, s->logits,
                                                    s->dlogits, V, s->stream, true)
-                        : launch_accept_greedy(st, s->ctx, s->acc_log, vm, s->stream, true);
+                        : launch_accept_greedy(st, s->ctx, s->acc_log, vm, s->B, s->ctx_stride,
+                                               s->ctx_stride, s->stream, true);
     if (e != cudaSuccess) rc = set_err(MC_E_CUDA, "accept launch: %s", cudaGetErrorString(e));
   }
   cudaGraph_t graph = nullptr;
@@ -1483,100 +1558,154 @@ static SpecState fresh_state(const mc_session* s, int n_prompt) {
   return h;
 }
 
-extern "C" mc_status mc_spec_prime(mc_session* s, const uint32_t* prompt, int32_t n_prompt) {
-  if (!s || (!prompt && n_prompt > 0) || n_prompt < 0) return set_err(MC_E_INVALID, "bad arguments");
-  if (!s->dw) return set_err(MC_E_INVALID, "speculative decoding needs a draft model");
-  if (s->cfg.gamma < 1) return set_err(MC_E_INVALID, "gamma must be >= 1");
-  if (n_prompt == 0) return set_err(MC_E_INVALID, "empty prompt (generate.rs:609-611 returns nothing)");
-  if (n_prompt + s->cfg.gamma + 2 > s->cap)
-    return set_err(MC_E_CAPACITY, "prompt of %d does not fit KV capacity %d", n_prompt, s->cap);
-  CK(cudaSetDevice(s->dev));
-  s->prompt_len = n_prompt;
-  s->draft_tokens.clear();
-  memcpy(s->h_ids, prompt, (size_t)n_prompt * 4);
-  CK(cudaMemcpyAsync(s->ctx, s->h_ids, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, s->stream));
-  // prime the target (generate.rs:629-636): every prompt token, logits discarded
+// Prime request z (generate.rs:629-636): its prompt through the target and,
+// all but the last token, through the draft, into its own KV pages.
+static mc_status prime_request(mc_session* s, int z, int n_prompt) {
+  uint32_t* ctx = s->ctx + (size_t)z * s->ctx_stride;
+  KVSet tkv = s->tkv, dkv = s->dkv;
+  tkv.page_table += (size_t)z * tkv.n_pages;
+  dkv.page_table += (size_t)z * dkv.n_pages;
   for (int c0 = 0; c0 < n_prompt; c0 += kChunk) {
     const int M = std::min(kChunk, n_prompt - c0);
     CK(launch_set_int(s->pos, c0, s->stream));
     EmbedArgs ea{};
     ea.src = SRC_IDS;
-    ea.ids = s->ctx + c0;
-    CKS(enq_forward(s, s->tw, s->tkv, M, ea, s->pos, 0, s->st->tkeys, nullptr));
+    ea.ids = ctx + c0;
+    CKS(enq_forward(s, s->tw, tkv, M, SeqMap{M, 0, 0, 0}, ea, s->pos, 0, s->fkeys, nullptr));
   }
-  // prime the draft with all but the last prompt token (the first round
-  // forwards the last one)
+  // the draft gets all but the last prompt token (the first round forwards it)
   for (int c0 = 0; c0 < n_prompt - 1; c0 += kChunk) {
     const int M = std::min(kChunk, n_prompt - 1 - c0);
     CK(launch_set_int(s->pos + 1, c0, s->stream));
     EmbedArgs ea{};
     ea.src = SRC_IDS;
-    ea.ids = s->ctx + c0;
-    CKS(enq_forward(s, s->dw, s->dkv, M, ea, s->pos + 1, 0, s->st->dkeys, nullptr));
+    ea.ids = ctx + c0;
+    CKS(enq_forward(s, s->dw, dkv, M, SeqMap{M, 0, 0, 0}, ea, s->pos + 1, 0, s->fkeys, nullptr));
   }
-  SpecState h = fresh_state(s, n_prompt);
-  CK(cudaMemcpyAsync(s->st, &h, sizeof(h), cudaMemcpyHostToDevice, s->stream));
-  CK(cudaStreamSynchronize(s->stream));
-  s->lt = n_prompt;
-  s->ld = n_prompt - 1;
   return MC_OK;
 }
 
+extern "C" mc_status mc_spec_prime_batch(mc_session* s, const uint32_t* prompts,
+                                         const int32_t* lens, int32_t n_requests) {
+  if (!s || !lens || !prompts) return set_err(MC_E_INVALID, "bad arguments");
+  if (n_requests != s->B)
+    return set_err(MC_E_INVALID, "%d prompts for a session of %d requests", n_requests, s->B);
+  if (!s->dw) return set_err(MC_E_INVALID, "speculative decoding needs a draft model");
+  if (s->cfg.gamma < 1) return set_err(MC_E_INVALID, "gamma must be >= 1");
+  for (int z = 0; z < n_requests; ++z) {
+    if (lens[z] <= 0) return set_err(MC_E_INVALID, "empty prompt (generate.rs:609-611 returns nothing)");
+    if (lens[z] + s->cfg.gamma + 2 > s->cap)
+      return set_err(MC_E_CAPACITY, "prompt of %d does not fit KV capacity %d", lens[z], s->cap);
+  }
+  CK(cudaSetDevice(s->dev));
+  s->prompt_len = lens[0];
+  s->prompt_lens.assign(lens, lens + n_requests);
+  s->draft_tokens.clear();
+  size_t off = 0;
+  for (int z = 0; z < n_requests; ++z) {
+    memcpy(s->h_ids + (size_t)z * s->ctx_stride, prompts + off, (size_t)lens[z] * 4);
+    off += (size_t)lens[z];
+  }
+  CK(cudaMemcpyAsync(s->ctx, s->h_ids, (size_t)n_requests * s->ctx_stride * 4,
+                     cudaMemcpyHostToDevice, s->stream));
+  for (int z = 0; z < n_requests; ++z) CKS(prime_request(s, z, lens[z]));
+  std::vector<SpecState> h(n_requests);
+  for (int z = 0; z < n_requests; ++z) h[z] = fresh_state(s, lens[z]);
+  CK(cudaMemcpyAsync(s->st, h.data(), sizeof(SpecState) * n_requests, cudaMemcpyHostToDevice,
+                     s->stream));
+  CK(cudaStreamSynchronize(s->stream));
+  s->lt = lens[0];
+  s->ld = lens[0] - 1;
+  return MC_OK;
+}
+
+extern "C" mc_status mc_spec_prime(mc_session* s, const uint32_t* prompt, int32_t n_prompt) {
+  if (!s || (!prompt && n_prompt > 0) || n_prompt < 0) return set_err(MC_E_INVALID, "bad arguments");
+  if (s->B != 1) return set_err(MC_E_INVALID, "batched session: use mc_spec_prime_batch");
+  return mc_spec_prime_batch(s, prompt, &n_prompt, 1);
+}
+
+// Round loop of every request until each holds >= max_tokens generated ids.
+// The reference checks the budget only at round start (generate.rs:638):
+// each request's acceptance leaves it unchanged once its budget is spent, and
+// launching ceil(max remaining / max_emit) rounds per batch keeps every
+// launched round one that the request with the most left would also run.
 extern "C" mc_status mc_spec_decode(mc_session* s, int32_t max_tokens, int32_t* n_generated) {
   if (!s || max_tokens < 0) return set_err(MC_E_INVALID, "bad arguments");
   if (!s->prompt_len) return set_err(MC_E_INVALID, "call mc_spec_prime first");
   CK(cudaSetDevice(s->dev));
   CKS(capture_round(s));
+  const int B = s->B;
   const int max_emit = s->cfg.gamma + (s->cfg.bonus ? 1 : 0);
-  SpecState h{};
-  CK(cudaMemcpy(&h, s->st, sizeof(h), cudaMemcpyDeviceToHost));
-  // The reference checks the budget only at round start (generate.rs:638);
-  // launching ceil(remaining / max_emit) rounds per batch keeps every launched
-  // round one the reference would also run.
-  while (h.generated < max_tokens) {
+  std::vector<SpecState> h(B);
+  CK(cudaMemcpy(h.data(), s->st, sizeof(SpecState) * B, cudaMemcpyDeviceToHost));
+  for (int z = 0; z < B; ++z)
+    CK(cudaMemcpyAsync(&s->st[z].max_tokens, &max_tokens, 4, cudaMemcpyHostToDevice, s->stream));
+  for (;;) {
     if (s->cfg.cancel && *s->cfg.cancel) return set_err(MC_E_CANCELLED, "cancelled");
-    const int remaining = max_tokens - h.generated;
-    if (h.ctx_len + max_emit * ((remaining + max_emit - 1) / max_emit) + 2 > s->cap ||
-        h.ctx_len + remaining + max_emit + 2 > s->cap)
-      return set_err(MC_E_CAPACITY, "generation would exceed KV capacity %d", s->cap);
-    const int R = (remaining + max_emit - 1) / max_emit;
+    int most = 0;
+    for (int z = 0; z < B; ++z) most = std::max(most, max_tokens - h[z].generated);
+    if (most <= 0) break;
+    const int R = (most + max_emit - 1) / max_emit;
+    for (int z = 0; z < B; ++z) {
+      const int remaining = max_tokens - h[z].generated;
+      if (remaining <= 0) continue;
+      const int growth = std::min(max_emit * R, remaining + max_emit - 1);
+      if (h[z].ctx_len + growth + max_emit + 2 > s->cap)
+        return set_err(MC_E_CAPACITY, "generation would exceed KV capacity %d", s->cap);
+    }
     for (int r = 0; r < R; ++r) CK(cudaGraphLaunch(s->round_exec, s->stream));
-    CK(cudaMemcpyAsync(&h, s->st, sizeof(h), cudaMemcpyDeviceToHost, s->stream));
+    CK(cudaMemcpyAsync(h.data(), s->st, sizeof(SpecState) * B, cudaMemcpyDeviceToHost, s->stream));
     CK(cudaStreamSynchronize(s->stream));
     CKS(check_err(s->err));
   }
-  s->lt = h.lt;
-  s->ld = h.ld;
-  if (n_generated) *n_generated = h.generated;
+  s->lt = h[0].lt;
+  s->ld = h[0].ld;
+  if (n_generated) {
+    int total = 0;
+    for (int z = 0; z < B; ++z) total += h[z].generated;
+    *n_generated = total;
+  }
   return MC_OK;
 }
 
-extern "C" mc_status mc_spec_read(mc_session* s, uint32_t* out, int32_t cap, int32_t* n_out,
-                                  int32_t* accepted, int32_t accepted_cap, int32_t* n_rounds) {
+extern "C" mc_status mc_spec_read_request(mc_session* s, int32_t z, uint32_t* out, int32_t cap,
+                                          int32_t* n_out, int32_t* accepted, int32_t accepted_cap,
+                                          int32_t* n_rounds) {
   if (!s) return set_err(MC_E_INVALID, "null session");
+  if (z < 0 || z >= s->B) return set_err(MC_E_INVALID, "request %d outside [0, %d)", z, s->B);
   CK(cudaSetDevice(s->dev));
   SpecState h{};
-  CK(cudaMemcpy(&h, s->st, sizeof(h), cudaMemcpyDeviceToHost));
+  CK(cudaMemcpy(&h, s->st + z, sizeof(h), cudaMemcpyDeviceToHost));
+  const uint32_t* ctx = s->ctx + (size_t)z * s->ctx_stride;
   const int gen = h.ctx_len - h.prompt_len;
   const int nc = std::max(0, std::min(gen, (int)cap));
-  if (out && nc) CK(cudaMemcpy(out, s->ctx + h.prompt_len, (size_t)nc * 4, cudaMemcpyDeviceToHost));
+  if (out && nc) CK(cudaMemcpy(out, ctx + h.prompt_len, (size_t)nc * 4, cudaMemcpyDeviceToHost));
   if (n_out) *n_out = nc;
   if (accepted && accepted_cap > 0) {
     const int na = std::min(h.n_rounds, (int)accepted_cap);
-    if (na) CK(cudaMemcpy(accepted, s->acc_log, (size_t)na * 4, cudaMemcpyDeviceToHost));
+    if (na)
+      CK(cudaMemcpy(accepted, s->acc_log + (size_t)z * s->ctx_stride, (size_t)na * 4,
+                    cudaMemcpyDeviceToHost));
   }
   if (n_rounds) *n_rounds = h.n_rounds;
   return MC_OK;
 }
 
+extern "C" mc_status mc_spec_read(mc_session* s, uint32_t* out, int32_t cap, int32_t* n_out,
+                                  int32_t* accepted, int32_t accepted_cap, int32_t* n_rounds) {
+  return mc_spec_read_request(s, 0, out, cap, n_out, accepted, accepted_cap, n_rounds);
+}
+
 extern "C" mc_status mc_spec_rewind(mc_session* s) {
   if (!s || !s->prompt_len) return set_err(MC_E_INVALID, "call mc_spec_prime first");
   CK(cudaSetDevice(s->dev));
-  SpecState h = fresh_state(s, s->prompt_len);
-  CK(cudaMemcpyAsync(s->st, &h, sizeof(h), cudaMemcpyHostToDevice, s->stream));
+  std::vector<SpecState> h(s->B);
+  for (int z = 0; z < s->B; ++z) h[z] = fresh_state(s, s->prompt_lens[z]);
+  CK(cudaMemcpyAsync(s->st, h.data(), sizeof(SpecState) * s->B, cudaMemcpyHostToDevice, s->stream));
   CK(cudaStreamSynchronize(s->stream));
-  s->lt = h.lt;
-  s->ld = h.ld;
+  s->lt = h[0].lt;
+  s->ld = h[0].ld;
   return MC_OK;
 }
 
@@ -1700,6 +1829,23 @@ extern "C" mc_status mc_speculative_generate(mc_session* s, const uint32_t* prom
   return mc_spec_read(s, out, cap, n_out, accepted, accepted_cap, n_rounds);
 }
 
+extern "C" mc_status mc_speculative_generate_batch(mc_session* s, const uint32_t* prompts,
+                                                   const int32_t* lens, int32_t n_requests,
+                                                   int32_t max_tokens, uint32_t* out,
+                                                   int32_t out_stride, int32_t* n_out,
+                                                   int32_t* accepted, int32_t accepted_stride,
+                                                   int32_t* n_rounds) {
+  if (!s || !n_out || out_stride < 0 || (accepted && accepted_stride < 0))
+    return set_err(MC_E_INVALID, "bad arguments");
+  CKS(mc_spec_prime_batch(s, prompts, lens, n_requests));
+  CKS(mc_spec_decode(s, max_tokens, nullptr));
+  for (int z = 0; z < n_requests; ++z)
+    CKS(mc_spec_read_request(s, z, out ? out + (size_t)z * out_stride : nullptr, out_stride,
+                             &n_out[z], accepted ? accepted + (size_t)z * accepted_stride : nullptr,
+                             accepted ? accepted_stride : 0, n_rounds ? &n_rounds[z] : nullptr));
+  return MC_OK;
+}
+
 // ------------------------------------------------------------------ standalone linear
 struct mc_linear {
   int dev = 0;
@@ -1737,15 +1883,16 @@ extern "C" mc_status mc_linear_create(const mc_tensor_desc* w, int32_t device, m
   const int kp = round_up(src.cols, 32);
   if (st == MC_OK && (prepare_kernels(0, 0) != cudaSuccess || prepare_tc() != cudaSuccess))
     st = set_err(MC_E_CUDA, "kernel preparation failed");
-  if (st == MC_OK) st = L->al.alloc(&L->xq, (size_t)kp * 48);
+  if (st == MC_OK) st = L->al.alloc(&L->xq, (size_t)kp * 48 * kMaxGroups);
   if (st == MC_OK) st = L->al.alloc(&L->xexp, (size_t)kMaxTokens);
-  if (st == MC_OK) st = L->al.alloc(&L->ws, (size_t)L->m.n_stripes * 32 * 24);
-  if (st == MC_OK) st = L->al.alloc(&L->cnt, (size_t)L->m.n_stripes);
+  if (st == MC_OK) st = L->al.alloc(&L->ws, (size_t)L->m.n_stripes * kMaxGroups * 16 * 48);
+  if (st == MC_OK) st = L->al.alloc(&L->cnt, (size_t)L->m.n_stripes * kMaxGroups);
   if (st == MC_OK) st = L->al.alloc(&L->err, 1);
   if (st == MC_OK && cudaMemset(L->err, 0, 4) != cudaSuccess) st = set_err(MC_E_CUDA, "memset");
-  if (st == MC_OK && (cudaMemset(L->xq, 0, (size_t)kp * 48) != cudaSuccess ||
-                      cudaMemset(L->ws, 0, (size_t)L->m.n_stripes * 32 * 24 * 4) != cudaSuccess ||
-                      cudaMemset(L->cnt, 0, (size_t)L->m.n_stripes * 4) != cudaSuccess))
+  if (st == MC_OK &&
+      (cudaMemset(L->xq, 0, (size_t)kp * 48 * kMaxGroups) != cudaSuccess ||
+       cudaMemset(L->ws, 0, (size_t)L->m.n_stripes * kMaxGroups * 16 * 48 * 4) != cudaSuccess ||
+       cudaMemset(L->cnt, 0, (size_t)L->m.n_stripes * kMaxGroups * 4) != cudaSuccess))
     st = set_err(MC_E_CUDA, "memset failed");
   cudaDeviceGetAttribute(&L->nsm, cudaDevAttrMultiProcessorCount, device);
   if (st == MC_OK)
@@ -1790,27 +1937,19 @@ extern "C" mc_status mc_linear_run(mc_linear* l, const float* x_dev, int32_t m, 
     q.tc_layout = use_tc(l->m, M) ? 1 : 0;
     CK(launch_quant(q, s, true));
     GemvArgs a{};
-    a.w = l->m.w;
-    a.scale = l->m.scale;
-    a.qscale = l->m.qscale;
     a.x = l->xq;
     a.xexp = l->xexp;
-    a.KB = l->m.KB;
-    a.n_stripes = l->m.n_stripes;
-    a.M = M;
     a.ws = l->ws;
     a.cnt = l->cnt;
     a.err = l->err;
     a.out = y_dev + (size_t)r0 * l->m.N;
     a.ldo = l->m.N;
     a.n_out = l->m.N;
-    const int nt = nt_for_tokens(M);
-    if (use_tc(l->m, M)) {
-      a.wtc = l->m.wtc;
-      CK(launch_gemm_tc(a, EPI_STORE, tc_ksplit(l->m, l->nsm), s, true));
-    } else {
-      CK(launch_gemv(a, EPI_STORE, nt, l->m.fmt, linear_grid(l, nt), s, true));
-    }
+    CK(run_projection(l->m, EPI_STORE, M, a, l->nsm, s, [&](int t) {
+      int& b = l->bps[l->m.fmt][t];
+      if (!b) b = std::max(1, gemv_blocks_per_sm(EPI_STORE, t, l->m.fmt));
+      return b;
+    }));
   }
   return MC_OK;
 }
@@ -1869,8 +2008,8 @@ extern "C" mc_status mc_linear_run_static(mc_linear* l, const float* x_dev, int3
   uint8_t* xq = scratch;
   int* xexp = reinterpret_cast<int*>(scratch + kStaticXqBytes);
   cudaStream_t s = (cudaStream_t)stream;
-  for (int r0 = 0; r0 < m; r0 += kMaxTokens) {
-    const int M = std::min(kMaxTokens, m - r0);
+  for (int r0 = 0; r0 < m; r0 += kGroupTokens) {  // the scratch holds one token group
+    const int M = std::min(kGroupTokens, m - r0);
     const int nt = nt_for_tokens(M);
     QuantArgs q{};
     q.h = x_dev + (size_t)r0 * l->m.K;

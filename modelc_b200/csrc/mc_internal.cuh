@@ -32,14 +32,44 @@ constexpr int kFragBytes = 512;
 // digits X = d0*2^14 + d1*2^7 + d2.  Column c = 3*token + digit of the B
 // operand; NT n8-tiles cover 8*NT columns.
 constexpr int kDigits = 3;
-constexpr int kMaxTokens = 16;  // tokens per GEMV launch (NT <= 6)
+constexpr int kGroupTokens = 16;  // tokens per operand group (NT <= 6, 48 columns)
+constexpr int kMaxGroups = 4;
+constexpr int kMaxTokens = kGroupTokens * kMaxGroups;  // tokens per forward
 constexpr int kExpNonFinite = -100000;  // exponent marking a non-finite row
 
+// n8 tiles of one operand group: up to 16 tokens in 1, 2, 3 or 6 tiles;
+// larger forwards are cut into groups of 16 tokens of 6 tiles each.
 __host__ __device__ inline int nt_for_tokens(int m) {
+  if (m > kGroupTokens) return 6;
   int cols = kDigits * m;
   int nt = (cols + 7) / 8;
   if (nt == 4 || nt == 5) nt = 6;
   return nt;  // 1, 2, 3 or 6
+}
+__host__ __device__ inline int groups_for_tokens(int m) {
+  return (m + kGroupTokens - 1) / kGroupTokens;
+}
+
+// Token -> sequence map of one forward over n_seq sequences of seq_len
+// tokens each (one sequence: seq_len = M, strides unused).  Token m is
+// offset i = m % seq_len of sequence z = m / seq_len, at position
+// pos_ptr[z * pos_stride] + pos_add + i, with KV pages
+// page_table[z * pt_stride + ...]; its argmax key goes to
+// keys[z * key_stride + i].
+struct SeqMap {
+  int seq_len;
+  int pos_stride;   // ints between the sequences' position counters
+  int pt_stride;    // page-table entries per sequence
+  int key_stride;   // 64-bit keys between the sequences' key arrays
+};
+__host__ __device__ inline int seq_of(const SeqMap& s, int m) {
+  return s.seq_len > 0 ? m / s.seq_len : 0;
+}
+__host__ __device__ inline int seq_off(const SeqMap& s, int m) {
+  return s.seq_len > 0 ? m % s.seq_len : m;
+}
+__host__ __device__ inline int key_slot(const SeqMap& s, int m) {
+  return seq_of(s, m) * s.key_stride + seq_off(s, m);
 }
 
 // Packed weight formats.
@@ -86,13 +116,14 @@ struct GemvArgs {
   const int4* w;         // packed weights (WF_Q4: 8 bytes per lane per k-block)
   const float* scale;    // WF_I8: [n_stripes*16] per packed row (0 on padding rows)
   const uint32_t* qscale;// WF_Q4: [n_stripes][KB][8] fp16 pairs (rows g, g+8)
-  const uint8_t* x;      // packed activation digits [KB][32][8*NT]
-  const int* xexp;       // [M] exponents
+  const uint8_t* x;      // packed activation digits of this launch's group [KB][32][8*NT]
+  const int* xexp;       // [M] exponents of this launch's tokens
   int KB;                // k-blocks per stripe
   int n_stripes;
-  int M;                 // tokens
-  int* ws;               // split-K partial sums [n_stripes][16][8*NT] (zeroed)
-  int* cnt;              // [n_stripes] k-block arrival counters (zeroed)
+  int M;                 // tokens of this launch (GEMV: <= 16; tcgen05 GEMM: <= 64)
+  int m0;                // forward-wide index of this launch's first token
+  int* ws;               // split-K partial sums [n_stripes][groups][16][48] (zeroed)
+  int* cnt;              // [n_stripes][groups] k-block arrival counters (zeroed)
   int* err;              // set to 1 when a bounded device wait expires
   // Statistics for the next activation encoding, produced by the RESID and
   // SWIGLU epilogues: per-stripe sum of squares st_pss[m * st_np + stripe]
@@ -115,8 +146,9 @@ struct GemvArgs {
   float* kc;             // layer K pages [page][Hkv][P][hdp]
   float* vc;
   const int* page_table;
-  const int* pos_ptr;    // first position = *pos_ptr + pos_add
+  const int* pos_ptr;    // token positions: SeqMap
   int pos_add;
+  SeqMap seq;            // token -> sequence (QKV positions and pages, LMHEAD keys)
   const float* rope_cos; // [pos][half_p]
   const float* rope_sin;
   int half_p, hdp, H, Hkv, page;
@@ -162,12 +194,14 @@ struct AttnArgs {
   const int* page_table;
   const int* pos_ptr;
   int pos_add;
+  SeqMap seq;
+  int qblk;              // tokens of one sequence per CTA (query block)
   int M, H, Hkv, hdp, page;
   float inv_scale_den;   // sqrt(head_dim) (divisor, transformer.rs:966)
   int max_chunks;
-  float* part_o;         // [Hkv][max_chunks][G*M][hdp]
-  float* part_ml;        // [Hkv][max_chunks][G*M][2]
-  int* cnt;              // [Hkv]
+  float* part_o;         // [blocks][Hkv][max_chunks][G*qblk][hdp]
+  float* part_ml;        // [blocks][Hkv][max_chunks][G*qblk][2]
+  int* cnt;              // [blocks][Hkv]
   float* out;            // [M][H][hdp]
   unsigned* st_amax;     // max |out| per token (float bits, atomicMax) or nullptr
   const void* pf;        // L2 prefetch of upcoming weights while HBM is idle, or nullptr
@@ -175,11 +209,14 @@ struct AttnArgs {
   int trace_slot;        // MC_TRACE builds: 1 + timeline slot, 0 = untraced
 };
 
+// Token m = (sequence z, offset i) by EmbedArgs::seq; each sequence z has
+// its context at ctx + z * ctx_stride, its counter at off[z * seq.pos_stride]
+// and its keys at keys + z * seq.key_stride.
 enum EmbedSrc : int {
   SRC_IDS = 0,     // ids[m]
-  SRC_CTX_AT = 1,  // ctx[*off + m]
-  SRC_KEYS = 2,    // argmax key keys[m]
-  SRC_VERIFY = 3,  // m == 0 ? ctx[*len - 1] : key keys[m-1]
+  SRC_CTX_AT = 1,  // ctx_z[off_z + i]
+  SRC_KEYS = 2,    // argmax key keys_z[i]
+  SRC_VERIFY = 3,  // i == 0 ? ctx_z[len_z - 1] : key keys_z[i - 1]
 };
 
 struct EmbedArgs {
@@ -188,14 +225,16 @@ struct EmbedArgs {
   const uint32_t* ctx;
   const int* off;        // SRC_CTX_AT offset / SRC_VERIFY context length
   const unsigned long long* keys;
+  SeqMap seq;
+  int ctx_stride;
   uint32_t* ids_out;     // optional: resolved ids [M]
   const int8_t* emb_q;   // [vocab][d] int8
   const float* emb_scale;// [vocab]
   const uint8_t* emb_q4; // or q4_0 blocks [vocab][d/32][18] (then emb_q unused)
   int d, vocab, M;
   float* h;              // [M][d]
-  unsigned long long* zero_keys;  // keys this forward will produce
-  int n_zero;
+  unsigned long long* zero_keys;  // keys this forward will produce (key_slot of
+  int n_zero;                     // tokens 0..n_zero-1 by seq)
   // statistics of h for the first encoding: st_pss[m * st_np] = sum(h*h),
   // st_amax[m] = max |h * st_w| (plain stores); st_zero[0..n_st_zero) zeroed
   float* st_pss;
@@ -243,9 +282,13 @@ struct SpecState {
   float temperature;   // > 0: stochastic rounds
   uint32_t seed_lo, seed_hi;
   int pad[2];
-  unsigned long long tkeys[kMaxTokens];
-  unsigned long long dkeys[kMaxTokens];
+  unsigned long long tkeys[kGroupTokens];
+  unsigned long long dkeys[kGroupTokens];
 };
+// SpecState stride in ints and in keys (sequences of a batched session)
+constexpr int kStateInts = (int)(sizeof(SpecState) / sizeof(int));
+constexpr int kStateKeys = (int)(sizeof(SpecState) / sizeof(unsigned long long));
+static_assert(sizeof(SpecState) % sizeof(unsigned long long) == 0, "SpecState stride");
 
 // Argmax keys: larger key = larger value, ties -> smaller index.
 __host__ __device__ inline unsigned long long argmax_key(float v, uint32_t idx) {
@@ -268,8 +311,9 @@ __host__ __device__ inline uint32_t key_index(unsigned long long k) {
 cudaError_t launch_gemv(const GemvArgs& a, int epi, int nt, int wf, int grid,
                         cudaStream_t s, bool pdl);
 int gemv_blocks_per_sm(int epi, int nt, int wf);
-// tcgen05 GEMM for 9..16 tokens: grid (128-row tiles, ksplit); the digits
-// must be encoded with QuantArgs::tc_layout; ksplit > 1 merges through ws/cnt.
+// tcgen05 GEMM for 9..64 tokens: grid (128-row tiles, ksplit), 48 digit
+// columns per group of 16 tokens; the digits must be encoded with
+// QuantArgs::tc_layout; ksplit > 1 merges through ws/cnt.
 cudaError_t launch_gemm_tc(const GemvArgs& a, int epi, int ksplit, cudaStream_t s, bool pdl);
 cudaError_t launch_pack_tc(const int8_t* src, long long src_ld, const int* row_map,
                            const int* col_map, int n_rows, int n_tiles, int KB, int4* dst,
@@ -279,8 +323,11 @@ constexpr int kTcTileRows = 128;
 cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t s, bool pdl);
-cudaError_t launch_accept_greedy(SpecState* st, uint32_t* ctx, int* acc_log,
-                                 int vm, cudaStream_t s, bool pdl);
+// One CTA per sequence z of a batch: st + z, ctx + z * ctx_stride,
+// acc_log + z * log_stride.  A sequence whose budget is spent (generated >=
+// max_tokens > 0) is left unchanged.
+cudaError_t launch_accept_greedy(SpecState* st, uint32_t* ctx, int* acc_log, int vm, int n_seq,
+                                 int ctx_stride, int log_stride, cudaStream_t s, bool pdl);
 cudaError_t launch_set_int(int* p, int v, cudaStream_t s);
 // Stochastic rounds: sample draft step j from softmax(logits / T) into
 // *key_out (as an argmax key), and the acceptance of a whole round from the
@@ -298,7 +345,8 @@ constexpr int kSampleMaxVocab = 256 * 1024;  // tiles of 1024 staged in shared m
 constexpr int kTraceSlots = 4096;
 cudaError_t trace_reset();
 cudaError_t trace_read(unsigned long long* out, int n);  // n slots x 3 values
-size_t attention_smem_bytes(int G, int M, int hdp, int page);
+size_t attention_smem_bytes(int G, int qblk, int hdp, int page);
+int attention_qblk(int G, int seq_len);  // tokens per attention CTA
 size_t gemv_ws_ints_per_stripe(int nt);
 cudaError_t prepare_kernels(size_t quant_smem, size_t attn_smem);
 cudaError_t launch_pack_int8(const int8_t* src, long long src_ld,

@@ -289,7 +289,10 @@ struct StatArgs {
 };
 
 // Slice capture: if cap != nullptr, elements [lo, hi) of every token are also
-// stored to cap[m * (hi - lo) + (i - lo)].
+// stored to cap[m * (hi - lo) + (i - lo)].  Tokens are reduced in groups of
+// kStatTokens (one register partial per token of the group; the grouping
+// does not change any token's reduction order).
+constexpr int kStatTokens = 8;
 __device__ __forceinline__ void token_stats(const StatArgs& a, float (*red_ss)[kMaxTokens],
                                             float (*red_hw)[kMaxTokens], uint32_t* s_bad,
                                             float* s_mul, int* s_e, float* cap, int lo, int hi) {
@@ -297,67 +300,72 @@ __device__ __forceinline__ void token_stats(const StatArgs& a, float (*red_ss)[k
   const bool vec = ((a.ld & 3) == 0) && ((d & 3) == 0) &&
                    ((reinterpret_cast<uintptr_t>(a.h) & 15) == 0);
   const int span = hi - lo;
-  if (threadIdx.x == 0) *s_bad = 0u;
+  if (threadIdx.x < kMaxTokens / kStatTokens) s_bad[threadIdx.x] = 0u;
   __syncthreads();
-  uint32_t bad = 0u;
-  for (int v = threadIdx.x; v < kStatLanes; v += blockDim.x) {
-    float ss[kMaxTokens], hw[kMaxTokens];
+  for (int g0 = 0; g0 < M; g0 += kStatTokens) {
+    const int MG = min(kStatTokens, M - g0);
+    uint32_t bad = 0u;
+    for (int v = threadIdx.x; v < kStatLanes; v += blockDim.x) {
+      float ss[kStatTokens], hw[kStatTokens];
 #pragma unroll
-    for (int m = 0; m < kMaxTokens; ++m) { ss[m] = 0.0f; hw[m] = 0.0f; }
-    if (vec) {
+      for (int m = 0; m < kStatTokens; ++m) { ss[m] = 0.0f; hw[m] = 0.0f; }
+      if (vec) {
 #pragma unroll 4
-      for (int i = v * 4; i < d; i += kStatLanes * 4) {
-        float4 wv = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
-        if (a.do_norm && a.w) {
-          wv.x = i < a.wlen ? a.w[i] : 1.0f;
-          wv.y = i + 1 < a.wlen ? a.w[i + 1] : 1.0f;
-          wv.z = i + 2 < a.wlen ? a.w[i + 2] : 1.0f;
-          wv.w = i + 3 < a.wlen ? a.w[i + 3] : 1.0f;
+        for (int i = v * 4; i < d; i += kStatLanes * 4) {
+          float4 wv = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+          if (a.do_norm && a.w) {
+            wv.x = i < a.wlen ? a.w[i] : 1.0f;
+            wv.y = i + 1 < a.wlen ? a.w[i + 1] : 1.0f;
+            wv.z = i + 2 < a.wlen ? a.w[i + 2] : 1.0f;
+            wv.w = i + 3 < a.wlen ? a.w[i + 3] : 1.0f;
+          }
+#pragma unroll
+          for (int m = 0; m < kStatTokens; ++m)
+            if (m < MG) {
+              const int mt = g0 + m;
+              const float4 x = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)mt * a.ld + i));
+              if (cap && i >= lo && i < hi) *reinterpret_cast<float4*>(cap + mt * span + (i - lo)) = x;
+              ss[m] = __fadd_rn(ss[m], __fmul_rn(x.x, x.x));
+              ss[m] = __fadd_rn(ss[m], __fmul_rn(x.y, x.y));
+              ss[m] = __fadd_rn(ss[m], __fmul_rn(x.z, x.z));
+              ss[m] = __fadd_rn(ss[m], __fmul_rn(x.w, x.w));
+              hw[m] = fmaxf(hw[m], fmaxf(fmaxf(fabsf(__fmul_rn(x.x, wv.x)), fabsf(__fmul_rn(x.y, wv.y))),
+                                         fmaxf(fabsf(__fmul_rn(x.z, wv.z)), fabsf(__fmul_rn(x.w, wv.w)))));
+              if (!(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w))) bad |= 1u << m;
+            }
         }
+      } else {
+        for (int i = v; i < d; i += kStatLanes) {
+          const float wi = (a.do_norm && a.w && i < a.wlen) ? a.w[i] : 1.0f;
 #pragma unroll
-        for (int m = 0; m < kMaxTokens; ++m)
-          if (m < M) {
-            const float4 x = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)m * a.ld + i));
-            if (cap && i >= lo && i < hi) *reinterpret_cast<float4*>(cap + m * span + (i - lo)) = x;
-            ss[m] = __fadd_rn(ss[m], __fmul_rn(x.x, x.x));
-            ss[m] = __fadd_rn(ss[m], __fmul_rn(x.y, x.y));
-            ss[m] = __fadd_rn(ss[m], __fmul_rn(x.z, x.z));
-            ss[m] = __fadd_rn(ss[m], __fmul_rn(x.w, x.w));
-            hw[m] = fmaxf(hw[m], fmaxf(fmaxf(fabsf(__fmul_rn(x.x, wv.x)), fabsf(__fmul_rn(x.y, wv.y))),
-                                       fmaxf(fabsf(__fmul_rn(x.z, wv.z)), fabsf(__fmul_rn(x.w, wv.w)))));
-            if (!(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w))) bad |= 1u << m;
-          }
+          for (int m = 0; m < kStatTokens; ++m)
+            if (m < MG) {
+              const int mt = g0 + m;
+              const float x = __ldcg(a.h + (size_t)mt * a.ld + i);
+              if (cap && i >= lo && i < hi) cap[mt * span + (i - lo)] = x;
+              ss[m] = __fadd_rn(ss[m], __fmul_rn(x, x));
+              hw[m] = fmaxf(hw[m], fabsf(__fmul_rn(x, wi)));
+              if (!isfinite(x)) bad |= 1u << m;
+            }
+        }
       }
-    } else {
-      for (int i = v; i < d; i += kStatLanes) {
-        const float wi = (a.do_norm && a.w && i < a.wlen) ? a.w[i] : 1.0f;
+      const int vw = v >> 5;
 #pragma unroll
-        for (int m = 0; m < kMaxTokens; ++m)
-          if (m < M) {
-            const float x = __ldcg(a.h + (size_t)m * a.ld + i);
-            if (cap && i >= lo && i < hi) cap[m * span + (i - lo)] = x;
-            ss[m] = __fadd_rn(ss[m], __fmul_rn(x, x));
-            hw[m] = fmaxf(hw[m], fabsf(__fmul_rn(x, wi)));
-            if (!isfinite(x)) bad |= 1u << m;
+      for (int m = 0; m < kStatTokens; ++m) {
+        if (m < MG) {
+          float x = ss[m], y = hw[m];
+#pragma unroll
+          for (int o = 16; o; o >>= 1) {
+            x += __shfl_xor_sync(0xffffffffu, x, o);
+            y = fmaxf(y, __shfl_xor_sync(0xffffffffu, y, o));
           }
+          if ((v & 31) == 0) { red_ss[vw][g0 + m] = x; red_hw[vw][g0 + m] = y; }
+        }
       }
     }
-    const int vw = v >> 5;
-#pragma unroll
-    for (int m = 0; m < kMaxTokens; ++m) {
-      if (m < M) {
-        float x = ss[m], y = hw[m];
-#pragma unroll
-        for (int o = 16; o; o >>= 1) {
-          x += __shfl_xor_sync(0xffffffffu, x, o);
-          y = fmaxf(y, __shfl_xor_sync(0xffffffffu, y, o));
-        }
-        if ((v & 31) == 0) { red_ss[vw][m] = x; red_hw[vw][m] = y; }
-      }
-    }
+    bad = __reduce_or_sync(0xffffffffu, bad);
+    if ((threadIdx.x & 31) == 0 && bad) atomicOr(s_bad + g0 / kStatTokens, bad);
   }
-  bad = __reduce_or_sync(0xffffffffu, bad);
-  if ((threadIdx.x & 31) == 0 && bad) atomicOr(s_bad, bad);
   __syncthreads();
   if (threadIdx.x < M) {
     const int m = threadIdx.x;
@@ -367,7 +375,7 @@ __device__ __forceinline__ void token_stats(const StatArgs& a, float (*red_ss)[k
     if (a.do_norm) rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(x, (float)(d > 1 ? d : 1)), a.eps));
     const float amax = a.do_norm ? y / rms : y;
     int e = 0;
-    if (((*s_bad >> m) & 1u) || !isfinite(amax)) {
+    if (((s_bad[m / kStatTokens] >> (m % kStatTokens)) & 1u) || !isfinite(amax)) {
       e = kExpNonFinite;
     } else if (amax > 0.0f) {
       int E;
@@ -401,13 +409,24 @@ __device__ __forceinline__ size_t digit_word(int kb, int c, int kk, int nt, bool
   if (tc) return ((((size_t)kb * nt + (c >> 3)) * 2 + (kk >> 4)) * 32) + (c & 7) * 4 + ((kk & 15) >> 2);
   return (((size_t)kb * 32 + (c & 7) * 4 + ((kk & 15) >> 2)) * nt + (c >> 3)) * 2 + (kk >> 4);
 }
+// Word index of column c of a forward of `groups` token groups: the tcgen05
+// layout spans all groups (nt * groups tiles); the mma.sync layout keeps each
+// group's 8 * nt columns in its own block of KB * 64 * nt words, the operand
+// of one GEMV launch.
+__device__ __forceinline__ size_t digit_index(int kb, int c, int kk, int nt, int groups, int KB,
+                                              bool tc) {
+  if (tc) return digit_word(kb, c, kk, nt * groups, true);
+  const int g = c / (8 * nt);
+  return (size_t)g * KB * 64 * nt + digit_word(kb, c - g * 8 * nt, kk, nt, false);
+}
 
 template <class Src4, class Dst>
-__device__ __forceinline__ void encode_digits(const StatArgs& a, int nt, int kb0, int kb1,
+__device__ __forceinline__ void encode_digits(const StatArgs& a, int nt, int KB, int kb0, int kb1,
                                               const float* s_mul, const int* s_e, Src4 src4,
                                               Dst dst, bool tc = false) {
   const int M = a.M, d = a.d;
-  const int pad_cols = 8 * nt - 3 * M;
+  const int groups = groups_for_tokens(M);
+  const int pad_cols = 8 * nt * groups - 3 * M;
   const int ngroups = (kb1 - kb0) * 8;
   const int tasks = ngroups * (M + pad_cols);
   for (int t0 = threadIdx.x; t0 < tasks; t0 += blockDim.x * kEncBatch) {
@@ -431,7 +450,7 @@ __device__ __forceinline__ void encode_digits(const StatArgs& a, int nt, int kb0
       const int kb = kb0 + (grp >> 3);
       const int kk = (grp & 7) * 4;
       if (q >= M) {
-        dst(digit_word(kb, 3 * M + (q - M), kk, nt, tc), 0u);
+        dst(digit_index(kb, 3 * M + (q - M), kk, nt, groups, KB, tc), 0u);
         continue;
       }
       const int m = q;
@@ -459,7 +478,7 @@ __device__ __forceinline__ void encode_digits(const StatArgs& a, int nt, int kb0
       }
       const uint32_t wd[3] = {w0, w1, w2};
 #pragma unroll
-      for (int dg = 0; dg < 3; ++dg) dst(digit_word(kb, 3 * m + dg, kk, nt, tc), wd[dg]);
+      for (int dg = 0; dg < 3; ++dg) dst(digit_index(kb, 3 * m + dg, kk, nt, groups, KB, tc), wd[dg]);
     }
   }
 }
@@ -497,21 +516,24 @@ struct GemvCfg {
 
 constexpr int kGemvWarps = 8;
 
-// Epilogue of a finished stripe from a row-major [16][ld] int tile, run by
-// one warp.  Lane (it, lane) handles rows r and r+8 of token m, with
+// Epilogue of a finished stripe from a row-major [16][ld] int tile holding
+// MG <= 16 tokens (forward-wide tokens m0 .. m0 + MG - 1), run by one warp.
+// Lane (it, lane) handles rows r and r+8 of tile token m, with
 // idx = it*32 + lane, r = idx & 7, m = idx >> 3; the 8 lanes of a token form
-// one shuffle group for the encoding statistics.
+// one shuffle group for the encoding statistics.  xexp holds the tile's
+// token exponents.
 template <int NT, int EPI, typename T>
 __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, const T* tile,
                                               int ld, int lane, unsigned long long* kmax,
-                                              const float* scale, const int* xexp) {
-  const int M = a.M;
+                                              const float* scale, const int* xexp, int m0,
+                                              int MG) {
 #pragma unroll
-  for (int it = 0; it < (8 * kMaxTokens) / 32; ++it) {
-    if (it * 32 >= 8 * M) break;  // warp-uniform
+  for (int it = 0; it < (8 * kGroupTokens) / 32; ++it) {
+    if (it * 32 >= 8 * MG) break;  // warp-uniform
     const int idx = it * 32 + lane;
-    const bool valid = idx < 8 * M;
+    const bool valid = idx < 8 * MG;
     const int r = idx & 7, m = valid ? (idx >> 3) : 0;
+    const int mt = m0 + m;  // forward-wide token
     const int prow = stripe * 16 + r;
     // statistics contribution of this lane: sum(h*h) and max|h*w| kept as
     // float bits, whose unsigned order matches |x| and lets NaN/inf win
@@ -526,14 +548,14 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
       if constexpr (EPI == EPI_TP) {
         // this rank's partial rows into slot `rank` of every rank's buffer
         const TPArgs& t = a.tp;
-        const size_t off = (((size_t)(__ldcg(t.epoch) & 1u) * t.world + t.rank) * kMaxTokens + m) * t.d;
+        const size_t off = (((size_t)(__ldcg(t.epoch) & 1u) * t.world + t.rank) * kMaxTokens + mt) * t.d;
         for (int r = 0; r < t.world; ++r) {
           float* o = t.red[r] + off;
           if (prow < a.n_out) o[prow] = y0;
           if (prow + 8 < a.n_out) o[prow + 8] = y1;
         }
       } else if constexpr (EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_LMHEAD) {
-        float* o = a.out ? a.out + (size_t)m * a.ldo : nullptr;
+        float* o = a.out ? a.out + (size_t)mt * a.ldo : nullptr;
         if (prow < a.n_out) {
           if constexpr (EPI == EPI_RESID) {
             const float h0 = __fadd_rn(o[prow], y0);
@@ -570,14 +592,15 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
         const int i = stripe * 8 + r;  // row r = gate_i, row r+8 = up_i
         if (i < a.n_out) {
           const float act = silu_mul(y0, y1);
-          a.out[(size_t)m * a.ldo + i] = act;
+          a.out[(size_t)mt * a.ldo + i] = act;
           st_mx = __float_as_uint(fabsf(act));
         }
       } else if constexpr (EPI == EPI_QKV) {
-        const int pos = *a.pos_ptr + a.pos_add + m;
+        const int z = seq_of(a.seq, mt);
+        const int pos = a.pos_ptr[z * a.seq.pos_stride] + a.pos_add + seq_off(a.seq, mt);
         const int per_head = a.half_p >> 3;  // stripes per head (Q/K) = hdp/16
         const int slot = pos % a.page;
-        const int pg = a.page_table[pos / a.page];
+        const int pg = a.page_table[z * a.seq.pt_stride + pos / a.page];
         if (stripe < a.sq + a.sk) {
           // rows r and r+8 are the RoPE pair (i, i + half) (transformer.rs:921-938)
           const bool isq = stripe < a.sq;
@@ -589,7 +612,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
           const float o0 = __fsub_rn(__fmul_rn(y0, c), __fmul_rn(y1, sn));
           const float o1 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, c));
           if (isq) {
-            float* q = a.q_out + ((size_t)m * a.H + hh) * a.hdp;
+            float* q = a.q_out + ((size_t)mt * a.H + hh) * a.hdp;
             q[i] = o0;
             q[a.half_p + i] = o1;
           } else {
@@ -616,8 +639,8 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
           st_mx = max(st_mx, __shfl_xor_sync(0xffffffffu, st_mx, off, 8));
         }
         if (valid && r == 0) {
-          if constexpr (EPI == EPI_RESID) a.st_pss[(size_t)m * a.st_np + stripe] = st_sq;
-          atomicMax(a.st_amax + m, st_mx);
+          if constexpr (EPI == EPI_RESID) a.st_pss[(size_t)mt * a.st_np + stripe] = st_sq;
+          atomicMax(a.st_amax + mt, st_mx);
         }
       }
     }
@@ -679,8 +702,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
       reinterpret_cast<Acc (*)[16 * COLS]>(gemv_smem + kGemvWarps * 16 * (COLS + 1));
   __shared__ int sm_cnt[kTileSlots];
   __shared__ float sm_scale[kMaxCtaStripes * 16];
-  __shared__ int sm_exp[kGemvWarps][kMaxTokens];  // per warp: filled at its first epilogue
-  __shared__ unsigned long long sm_keys[kMaxTokens];
+  __shared__ int sm_exp[kGemvWarps][kGroupTokens];  // per warp: filled at its first epilogue
+  __shared__ unsigned long long sm_keys[kGroupTokens];
 
   MC_TRACE_T0
   const int lane = threadIdx.x & 31;
@@ -692,7 +715,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   const int n_units = ns * F;
 
   if (threadIdx.x < kTileSlots) sm_cnt[threadIdx.x] = 0;
-  if (threadIdx.x < kMaxTokens) sm_keys[threadIdx.x] = 0ull;
+  if (threadIdx.x < kGroupTokens) sm_keys[threadIdx.x] = 0ull;
   if (!Q4 && F > 1)
     for (int i = threadIdx.x; i < kTileSlots * 16 * COLS; i += blockDim.x) (&sm_tile[0][0])[i] = 0;
   const bool scale_smem = !Q4 && ns <= kMaxCtaStripes;
@@ -755,17 +778,21 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   // launches; the position counter is final two launches back).
   if constexpr (EPI == EPI_QKV) {
     if (a.kv_prefetch && lane == 2) {
-      const int L = *a.pos_ptr + a.pos_add + a.M;
-      const int np = (L + a.page - 1) / a.page;
       const long long blk = (long long)a.page * a.hdp;  // floats of one (page, kv head)
-      const long long items = (long long)np * 2 * a.Hkv;
       const long long nw = (long long)gridDim.x * kGemvWarps;
-      for (long long i = (long long)blockIdx.x * kGemvWarps + warp; i < items; i += nw) {
-        const int pg = (int)(i / (2 * a.Hkv));
-        const int rem = (int)(i - (long long)pg * 2 * a.Hkv);
-        const float* base = (rem & 1) ? a.vc : a.kc;
-        const float* p = base + ((long long)a.page_table[pg] * a.Hkv + (rem >> 1)) * blk;
-        prefetch_l2_bulk(p, (uint32_t)(blk * 4));
+      const int z0 = seq_of(a.seq, a.m0), z1 = seq_of(a.seq, a.m0 + a.M - 1);
+      for (int z = z0; z <= z1; ++z) {  // the sequences of this launch's tokens
+        const int L = a.pos_ptr[z * a.seq.pos_stride] + a.pos_add + a.seq.seq_len;
+        const int np = (L + a.page - 1) / a.page;
+        const int* pt = a.page_table + z * a.seq.pt_stride;
+        const long long items = (long long)np * 2 * a.Hkv;
+        for (long long i = (long long)blockIdx.x * kGemvWarps + warp; i < items; i += nw) {
+          const int pg = (int)(i / (2 * a.Hkv));
+          const int rem = (int)(i - (long long)pg * 2 * a.Hkv);
+          const float* base = (rem & 1) ? a.vc : a.kc;
+          const float* p = base + ((long long)pt[pg] * a.Hkv + (rem >> 1)) * blk;
+          prefetch_l2_bulk(p, (uint32_t)(blk * 4));
+        }
       }
     }
   }
@@ -778,15 +805,15 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   bool xe_staged = false;
   auto stage_exp = [&]() {
     if (!xe_staged) {
-      if (lane < kMaxTokens) sm_exp[warp][lane] = xe;
+      if (lane < kGroupTokens) sm_exp[warp][lane] = xe;
       __syncwarp();
       xe_staged = true;
     }
   };
 
-  unsigned long long kmax[(8 * kMaxTokens) / 32];
+  unsigned long long kmax[(8 * kGroupTokens) / 32];
 #pragma unroll
-  for (int i = 0; i < (8 * kMaxTokens) / 32; ++i) kmax[i] = 0ull;
+  for (int i = 0; i < (8 * kGroupTokens) / 32; ++i) kmax[i] = 0ull;
   const float* scl = Q4 ? nullptr : (scale_smem ? sm_scale - s0 * 16 : a.scale);
 
   bool pre = true;
@@ -846,7 +873,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
       __syncwarp();
       stage_exp();
       gemv_epilogue<NT, EPI>(a, stripe, &sm_epi[warp][0][0], COLS + 1, lane, kmax, scl,
-                             sm_exp[warp]);
+                             sm_exp[warp], a.m0, a.M);
       __syncwarp();
     } else {
       // F <= 8 and ns < 8, so a stripe's slot is its index in the CTA
@@ -893,10 +920,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
           __syncwarp();
           stage_exp();
           gemv_epilogue<NT, EPI>(a, stripe, &sm_epi[warp][0][0], COLS + 1, lane, kmax, scl,
-                                 sm_exp[warp]);
+                                 sm_exp[warp], a.m0, a.M);
         } else {
           stage_exp();
-          gemv_epilogue<NT, EPI>(a, stripe, sm_tile[slot], COLS, lane, kmax, scl, sm_exp[warp]);
+          gemv_epilogue<NT, EPI>(a, stripe, sm_tile[slot], COLS, lane, kmax, scl, sm_exp[warp],
+                                 a.m0, a.M);
         }
       }
       __syncwarp();
@@ -906,7 +934,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
 
   if constexpr (EPI == EPI_LMHEAD) {
 #pragma unroll
-    for (int it = 0; it < (8 * kMaxTokens) / 32; ++it) {
+    for (int it = 0; it < (8 * kGroupTokens) / 32; ++it) {
       unsigned long long k = kmax[it];
 #pragma unroll
       for (int o = 1; o < 8; o <<= 1) {
@@ -918,7 +946,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
     }
     __syncthreads();
     if (threadIdx.x < a.M && sm_keys[threadIdx.x])
-      atomicMax(a.keys + threadIdx.x, sm_keys[threadIdx.x]);
+      atomicMax(a.keys + key_slot(a.seq, a.m0 + threadIdx.x), sm_keys[threadIdx.x]);
   }
   if constexpr (EPI == EPI_TP) tp_publish(a.tp);
   MC_TRACE_END(a.trace_slot);
@@ -966,6 +994,10 @@ static cudaError_t launch_gemv_wf(const GemvArgs& a, int epi, int nt, int grid, 
 
 cudaError_t launch_gemv(const GemvArgs& a, int epi, int nt, int wf, int grid, cudaStream_t s,
                         bool pdl) {
+  // one token group per launch: its tiles, exponents and keys are 16 wide
+  if (a.M < 1 || a.M > kGroupTokens || 8 * nt < kDigits * a.M || a.m0 < 0 ||
+      a.m0 + a.M > kMaxTokens)
+    return cudaErrorInvalidValue;
   if (wf == WF_Q4) {
     if (!a.qscale) return cudaErrorInvalidValue;
     return launch_gemv_wf<WF_Q4>(a, epi, nt, grid, s, pdl);
@@ -1029,12 +1061,15 @@ constexpr int kQuantThreads = 512;
 constexpr int kQuantMaxCtas = 64;
 static int g_attn_smem = 48 * 1024;  // attention dynamic smem limit set so far
 
+// STATS: the producer supplied the statistics (use_stats); otherwise the
+// kernel reduces them itself (two instances keep the forward's one lean).
+template <bool STATS>
 __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
   __shared__ float red_ss[kStatWarps][kMaxTokens];
   __shared__ float red_hw[kStatWarps][kMaxTokens];
   __shared__ float s_mul[kMaxTokens];
   __shared__ int s_e[kMaxTokens];
-  __shared__ uint32_t s_bad;
+  __shared__ uint32_t s_bad[kMaxTokens / kStatTokens];
   extern __shared__ float s_x[];
   MC_TRACE_T0
   if (a.pf && threadIdx.x == 0) prefetch_share(a.pf, a.pf_bytes, blockIdx.x, gridDim.x);
@@ -1047,7 +1082,7 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
   const int kb0 = blockIdx.x * kbs, kb1 = min(a.KB, kb0 + kbs);
   const int lo = kb0 * 32, hi = kb0 * 32 + max(kb1 - kb0, 0) * 32;
   uint32_t* xq = reinterpret_cast<uint32_t*>(a.xq);
-  if (a.use_stats) {
+  if constexpr (STATS) {
     auto src4 = [&](int m, int k) { return load_act4(a.h, a.ld, a.d, m, k); };
     // statistics from the producing kernel: one warp per token sums the
     // partials in a fixed order (lane-strided, then an xor-shuffle tree)
@@ -1078,17 +1113,17 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
     if (blockIdx.x == 0 && a.amax_next && threadIdx.x < kMaxTokens) a.amax_next[threadIdx.x] = 0u;
     __syncthreads();
     if (blockIdx.x == 0 && threadIdx.x < a.M) a.xexp[threadIdx.x] = s_e[threadIdx.x];
-    encode_digits(sa, a.nt, kb0, kb1, s_mul, s_e, src4,
+    encode_digits(sa, a.nt, a.KB, kb0, kb1, s_mul, s_e, src4,
                   [&](size_t wi, uint32_t v) { xq[wi] = v; }, a.tc_layout != 0);
     MC_TRACE_END(a.trace_slot);
     return;
-  }
+  } else {
   // no producer statistics: reduce over the whole vector here, capturing
   // this CTA's slice in shared memory
-  token_stats(sa, red_ss, red_hw, &s_bad, s_mul, s_e, s_x, lo, hi);
+  token_stats(sa, red_ss, red_hw, s_bad, s_mul, s_e, s_x, lo, hi);
   if (blockIdx.x == 0 && threadIdx.x < a.M) a.xexp[threadIdx.x] = s_e[threadIdx.x];
   const int span = hi - lo;
-  encode_digits(sa, a.nt, kb0, kb1, s_mul, s_e,
+  encode_digits(sa, a.nt, a.KB, kb0, kb1, s_mul, s_e,
                 [&](int m, int k) {
                   const float* p = s_x + m * span + (k - lo);
                   float4 r;
@@ -1100,14 +1135,18 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
                 },
                 [&](size_t wi, uint32_t v) { xq[wi] = v; }, a.tc_layout != 0);
   MC_TRACE_END(a.trace_slot);
+  }
 }
 
 cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl) {
   if (a.M < 1 || a.M > kMaxTokens) return cudaErrorInvalidValue;
-  const int words = a.KB * 32 * 2 * a.nt;
+  if (a.nt != nt_for_tokens(a.M)) return cudaErrorInvalidValue;
+  const int words = a.KB * 32 * 2 * a.nt * groups_for_tokens(a.M);
   int ctas = (words + kQuantThreads - 1) / kQuantThreads;
   ctas = ctas < 1 ? 1 : (ctas > kQuantMaxCtas ? kQuantMaxCtas : ctas);
-  const int kbs_fit = (40 * 1024) / (a.M * 32 * (int)sizeof(float));  // staged slice <= 40 KB
+  // staged slice <= 32 KB: with the 8.8 KB of static statistics arrays it
+  // stays under the 48 KB default shared-memory limit
+  const int kbs_fit = (32 * 1024) / (a.M * 32 * (int)sizeof(float));
   if (kbs_fit < 1) return cudaErrorInvalidConfiguration;
   const int need = (a.KB + kbs_fit - 1) / kbs_fit;
   ctas = ctas < need ? need : ctas;
@@ -1117,22 +1156,26 @@ cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl) {
   cfg.gridDim = dim3(ctas);
   cfg.blockDim = dim3(kQuantThreads);
   cfg.dynamicSmemBytes = a.use_stats ? 0 : (size_t)a.M * kbs * 32 * sizeof(float);
-  if (cfg.dynamicSmemBytes > 48 * 1024) return cudaErrorInvalidConfiguration;
+  if (cfg.dynamicSmemBytes > 32 * 1024) return cudaErrorInvalidConfiguration;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_quant, a);
+  return a.use_stats ? cudaLaunchKernelEx(&cfg, k_quant<true>, a)
+                     : cudaLaunchKernelEx(&cfg, k_quant<false>, a);
 }
 
 // ------------------------------------------------------------ attention
-// One CTA per (KV head, KV page of 64 positions).  Query rows are the G
-// query heads sharing the KV head times the M new tokens; token m sees
-// positions <= pos0 + m.  Scores are dot / sqrt(head_dim) (transformer.rs:
-// 959-966); the softmax subtracts the row max (transformer.rs:985-1000).
-// Pages are combined by the last CTA of each KV head (flash-decoding split).
+// One CTA per (KV head, KV page of 64 positions, query block).  A query
+// block is up to qblk consecutive new tokens of one sequence (sequence z =
+// block / blocks per sequence); its query rows are the G query heads sharing
+// the KV head times those tokens, and token i of the sequence sees positions
+// <= pos_z + i.  Scores are dot / sqrt(head_dim) (transformer.rs:959-966);
+// the softmax subtracts the row max (transformer.rs:985-1000).  Pages are
+// combined by the last CTA of each (query block, KV head) (flash-decoding
+// split).
 constexpr int kAttnThreads = 512;
 
 // RB: query rows per thread (all of them valid: R is a multiple of the
@@ -1149,16 +1192,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attention(AttnArgs a) {
   grid_wait();
   MC_TRACE_WAITED(a.trace_slot);
   MC_TRACE_PHASE(a.trace_slot, 0, mc_tp);
-  const int kvh = blockIdx.x, chunk = blockIdx.y;
+  const int kvh = blockIdx.x, chunk = blockIdx.y, zb = blockIdx.z;
   const int G = a.H / a.Hkv;
-  const int R = G * a.M;
+  const int n_qb = (a.seq.seq_len + a.qblk - 1) / a.qblk;
+  const int z = zb / n_qb, i0 = (zb - z * n_qb) * a.qblk;
+  const int Mq = min(a.qblk, a.seq.seq_len - i0);  // tokens of this block
+  const int mt0 = z * a.seq.seq_len + i0;           // forward-wide first token
+  const int R = G * Mq;
+  const int Rs = G * a.qblk;                        // row stride of the partials
   const int hdp = a.hdp, P = a.page;
   // rows padded with zero queries to a multiple of both passes' row groups
+  // (from the block capacity, as the launcher chose RB)
   const int rgmax = max(kAttnThreads / P, kAttnThreads / hdp);
-  const int Rp = (R + rgmax - 1) / rgmax * rgmax;
-  const int pos0 = *a.pos_ptr + a.pos_add;
-  const int L = pos0 + a.M;
+  const int Rp = (Rs + rgmax - 1) / rgmax * rgmax;
+  const int pos0 = a.pos_ptr[z * a.seq.pos_stride] + a.pos_add + i0;
+  const int L = pos0 + Mq;
   const int n_chunks = (L + P - 1) / P;
+  const int cslot = zb * a.Hkv + kvh;  // (query block, KV head)
   if (chunk >= n_chunks) {
     MC_TRACE_END(a.trace_slot);
     return;
@@ -1171,7 +1221,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attention(AttnArgs a) {
   float* sv = sk + (size_t)P * ks;     // [P][hdp]
   float* ss = sv + (size_t)P * hdp;    // [Rp][P]
 
-  const int pg = a.page_table[chunk];
+  const int pg = a.page_table[z * a.seq.pt_stride + chunk];
   const float4* kbase = reinterpret_cast<const float4*>(a.kc + ((size_t)pg * a.Hkv + kvh) * P * hdp);
   const float4* vbase = reinterpret_cast<const float4*>(a.vc + ((size_t)pg * a.Hkv + kvh) * P * hdp);
   const int h4 = hdp >> 2;
@@ -1195,7 +1245,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attention(AttnArgs a) {
         if (i < R * h4) {
           const int row = i / h4, c4 = i - row * h4;
           const int m = row / G, gi = row - m * G;
-          qr[u] = __ldcg(reinterpret_cast<const float4*>(a.q + ((size_t)m * a.H + kvh * G + gi) * hdp) + c4);
+          qr[u] = __ldcg(reinterpret_cast<const float4*>(a.q + ((size_t)(mt0 + m) * a.H + kvh * G + gi) * hdp) + c4);
         }
       }
 #pragma unroll
@@ -1274,7 +1324,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attention(AttnArgs a) {
   __syncthreads();
   MC_TRACE_PHASE(a.trace_slot, 3, mc_tp);
   // P.V: thread -> column c and rows rq, rq+RG, ... ; four positions per step
-  const size_t pbase = ((size_t)kvh * a.max_chunks + chunk) * R;
+  const size_t pbase = ((size_t)cslot * a.max_chunks + chunk) * Rs;
   {
     const int c = threadIdx.x % hdp;
     const int RG = kAttnThreads / hdp;
@@ -1309,7 +1359,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attention(AttnArgs a) {
   // the last arriver fences again before reading the others' partials
   if (threadIdx.x == 0) {
     __threadfence();
-    const int last = (atomicAdd(a.cnt + kvh, 1) == n_chunks - 1);
+    const int last = (atomicAdd(a.cnt + cslot, 1) == n_chunks - 1);
     if (last) __threadfence();
     s_last = last;
   }
@@ -1327,11 +1377,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attention(AttnArgs a) {
   float* wgt = ss;  // [R][n_chunks]
   {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const float2* ml = reinterpret_cast<const float2*>(a.part_ml) + (size_t)kvh * a.max_chunks * R;
+    const float2* ml = reinterpret_cast<const float2*>(a.part_ml) + (size_t)cslot * a.max_chunks * Rs;
     for (int row = warp; row < R; row += kAttnThreads / 32) {
       float2 v0 = make_float2(-INFINITY, 0.0f), v1 = make_float2(-INFINITY, 0.0f);
-      if (lane < n_chunks) v0 = __ldcg(ml + (size_t)lane * R + row);
-      if (lane + 32 < n_chunks) v1 = __ldcg(ml + (size_t)(lane + 32) * R + row);
+      if (lane < n_chunks) v0 = __ldcg(ml + (size_t)lane * Rs + row);
+      if (lane + 32 < n_chunks) v1 = __ldcg(ml + (size_t)(lane + 32) * Rs + row);
       float M_ = fmaxf(v0.x, v1.x);
 #pragma unroll
       for (int o = 16; o; o >>= 1) M_ = fmaxf(M_, __shfl_xor_sync(0xffffffffu, M_, o));
@@ -1345,8 +1395,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attention(AttnArgs a) {
       if (lane == 0) s_l[row] = l;
     }
   }
-  __shared__ uint32_t s_mx[kMaxTokens];  // max |out| per token, float bits
-  if (threadIdx.x < kMaxTokens) s_mx[threadIdx.x] = 0u;
+  __shared__ uint32_t s_mx[128];  // max |out| per token of the block, float bits
+  if (threadIdx.x < 128) s_mx[threadIdx.x] = 0u;
   __syncthreads();
   MC_TRACE_PHASE(a.trace_slot, 6, mc_tp);
   {
@@ -1358,8 +1408,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attention(AttnArgs a) {
     const int c4 = threadIdx.x % h4;
     const int seg = min(h4, 32);  // lanes of a warp that share a row
     const float4* base =
-        reinterpret_cast<const float4*>(a.part_o) + (size_t)kvh * a.max_chunks * R * h4 + c4;
-    const size_t cs4 = (size_t)R * h4;
+        reinterpret_cast<const float4*>(a.part_o) + (size_t)cslot * a.max_chunks * Rs * h4 + c4;
+    const size_t cs4 = (size_t)Rs * h4;
     for (int row = threadIdx.x / h4; row < Rp; row += RGc) {
       const bool live = row < R;
       const int rr = live ? row : R - 1;
@@ -1397,7 +1447,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attention(AttnArgs a) {
         o.z = __fdiv_rn(acc.z, l);
         o.w = __fdiv_rn(acc.w, l);
         const int m = row / G, gi = row - m * G;
-        reinterpret_cast<float4*>(a.out + ((size_t)m * a.H + kvh * G + gi) * hdp)[c4] = o;
+        reinterpret_cast<float4*>(a.out + ((size_t)(mt0 + m) * a.H + kvh * G + gi) * hdp)[c4] = o;
         bits = max(max(__float_as_uint(fabsf(o.x)), __float_as_uint(fabsf(o.y))),
                    max(__float_as_uint(fabsf(o.z)), __float_as_uint(fabsf(o.w))));
       }
@@ -1410,16 +1460,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attention(AttnArgs a) {
   }
   if (a.st_amax) {
     __syncthreads();
-    if (threadIdx.x < a.M) atomicMax(a.st_amax + threadIdx.x, s_mx[threadIdx.x]);
+    if (threadIdx.x < Mq) atomicMax(a.st_amax + mt0 + threadIdx.x, s_mx[threadIdx.x]);
   }
-  if (threadIdx.x == 0) atomicExch(a.cnt + kvh, 0);
+  if (threadIdx.x == 0) atomicExch(a.cnt + cslot, 0);
   MC_TRACE_PHASE(a.trace_slot, 7, mc_tp);
   MC_TRACE_END(a.trace_slot);
 }
 
-size_t attention_smem_bytes(int G, int M, int hdp, int page) {
+size_t attention_smem_bytes(int G, int qblk, int hdp, int page) {
   const int rgmax = std::max(kAttnThreads / page, kAttnThreads / hdp);
-  const size_t R = (size_t)((G * M + rgmax - 1) / rgmax * rgmax);
+  const size_t R = (size_t)((G * qblk + rgmax - 1) / rgmax * rgmax);
   return (R * hdp + (size_t)page * (hdp + 4) + (size_t)page * hdp + R * page) * sizeof(float);
 }
 
@@ -1432,9 +1482,19 @@ static int attention_rb(int R, int hdp, int page) {
   return 0;
 }
 
+// Tokens of one sequence per attention CTA: query rows G * qblk <= 128.
+int attention_qblk(int G, int seq_len) {
+  const int cap = std::max(1, 128 / std::max(G, 1));
+  return std::max(1, std::min(seq_len, cap));
+}
+
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
   const int G = a.H / a.Hkv;
-  const int R = G * a.M;
+  if (a.seq.seq_len < 1 || a.qblk < 1 || a.qblk > a.seq.seq_len || a.M % a.seq.seq_len)
+    return cudaErrorInvalidValue;
+  const int n_seq = a.M / a.seq.seq_len;
+  const int n_qb = (a.seq.seq_len + a.qblk - 1) / a.qblk;
+  const int R = G * a.qblk;
   // the combine's page weights [R][n_chunks] reuse the score tile [Rp][page]
   if (a.page != 64 || a.max_chunks > a.page || a.hdp > 128 || (a.hdp & 3) ||
       (kAttnThreads % a.hdp))
@@ -1444,10 +1504,10 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
   if (Rp > 128) return cudaErrorInvalidValue;
   const int rb = attention_rb(Rp, a.hdp, a.page);
   if (rb == 0) return cudaErrorInvalidValue;
-  const size_t smem = attention_smem_bytes(G, a.M, a.hdp, a.page);
+  const size_t smem = attention_smem_bytes(G, a.qblk, a.hdp, a.page);
   if (smem > (size_t)g_attn_smem) return cudaErrorInvalidConfiguration;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.Hkv, a.max_chunks);
+  cfg.gridDim = dim3(a.Hkv, a.max_chunks, n_seq * n_qb);
   cfg.blockDim = dim3(kAttnThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -1486,12 +1546,15 @@ __global__ void __launch_bounds__(256) k_embed(EmbedArgs a) {
   grid_wait();
   MC_TRACE_WAITED(a.trace_slot);
   const int m = blockIdx.x;
+  const int z = seq_of(a.seq, m), si = seq_off(a.seq, m);
+  const uint32_t* ctx = a.ctx + (size_t)z * a.ctx_stride;
+  const unsigned long long* keys = a.keys + (size_t)z * a.seq.key_stride;
   uint32_t id;
   switch (a.src) {
     case SRC_IDS: id = a.ids[m]; break;
-    case SRC_CTX_AT: id = a.ctx[*a.off + m]; break;
-    case SRC_KEYS: id = key_index(a.keys[m]); break;
-    default: id = (m == 0) ? a.ctx[*a.off - 1] : key_index(a.keys[m - 1]); break;
+    case SRC_CTX_AT: id = ctx[a.off[z * a.seq.pos_stride] + si]; break;
+    case SRC_KEYS: id = key_index(keys[si]); break;
+    default: id = (si == 0) ? ctx[a.off[z * a.seq.pos_stride] - 1] : key_index(keys[si - 1]); break;
   }
   if (a.ids_out && threadIdx.x == 0) a.ids_out[m] = id;
   float* h = a.h + (size_t)m * a.d;
@@ -1520,7 +1583,7 @@ __global__ void __launch_bounds__(256) k_embed(EmbedArgs a) {
     mx = max(mx, __float_as_uint(fabsf(__fmul_rn(v, a.st_w ? a.st_w[i] : 1.0f))));
   }
   if (m == 0)
-    for (int i = threadIdx.x; i < a.n_zero; i += blockDim.x) a.zero_keys[i] = 0ull;
+    for (int j = threadIdx.x; j < a.n_zero; j += blockDim.x) a.zero_keys[key_slot(a.seq, j)] = 0ull;
   if (m == 0)
     for (int i = threadIdx.x; i < a.n_st_zero; i += blockDim.x) a.st_zero[i] = 0u;
   if (a.st_amax) {
@@ -1566,10 +1629,17 @@ cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t s, bool pdl) {
 // by a further forward; with the bonus (vm == gamma+1) the target's token after
 // d_gamma is pushed as well.  KV lengths are rolled back to what a
 // sequential verify would have forwarded.
-__global__ void k_accept_greedy(SpecState* st, uint32_t* ctx, int* acc_log, int vm) {
+__global__ void k_accept_greedy(SpecState* st_all, uint32_t* ctx_all, int* acc_log_all, int vm,
+                                int ctx_stride, int log_stride) {
   grid_launch_dependents();
   grid_wait();
   if (threadIdx.x != 0) return;
+  const int z = blockIdx.x;
+  SpecState* st = st_all + z;
+  uint32_t* ctx = ctx_all + (size_t)z * ctx_stride;
+  int* acc_log = acc_log_all ? acc_log_all + (size_t)z * log_stride : nullptr;
+  // a request whose budget is spent takes no more rounds (generate.rs:638)
+  if (st->max_tokens > 0 && st->generated >= st->max_tokens) return;
   const int g = st->gamma;
   int a = 0;
   while (a < g && key_index(st->tkeys[a]) == key_index(st->dkeys[a])) ++a;
@@ -1588,10 +1658,10 @@ __global__ void k_accept_greedy(SpecState* st, uint32_t* ctx, int* acc_log, int 
   st->n_rounds += 1;
 }
 
-cudaError_t launch_accept_greedy(SpecState* st, uint32_t* ctx, int* acc_log, int vm,
-                                 cudaStream_t s, bool pdl) {
+cudaError_t launch_accept_greedy(SpecState* st, uint32_t* ctx, int* acc_log, int vm, int n_seq,
+                                 int ctx_stride, int log_stride, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(1);
+  cfg.gridDim = dim3(n_seq);
   cfg.blockDim = dim3(32);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -1599,7 +1669,7 @@ cudaError_t launch_accept_greedy(SpecState* st, uint32_t* ctx, int* acc_log, int
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_accept_greedy, st, ctx, acc_log, vm);
+  return cudaLaunchKernelEx(&cfg, k_accept_greedy, st, ctx, acc_log, vm, ctx_stride, log_stride);
 }
 
 // ------------------------------------------------------------ sampling
@@ -2121,27 +2191,41 @@ cudaError_t launch_pack_q4(const uint8_t* src, const int* row_map, int n_stripes
 }
 
 // ------------------------------------------------------------ tcgen05 GEMM
-// Projections of 9..16 tokens (48 digit columns) on the 5th-generation tensor
-// cores: D[128 rows][48] += A[128][32 k] * B[48][32 k] per tcgen05.mma.kind::i8
-// (exact int32 in tensor memory).  One CTA per 128-row tile (and k-split):
+// Projections of 9..64 tokens (48 digit columns per group of 16 tokens, G
+// groups) on the 5th-generation tensor cores: D[128 rows][48 G] +=
+// A[128][32 k] * B[48 G][32 k] per tcgen05.mma.kind::i8 (exact int32 in
+// tensor memory).  One CTA per 128-row tile (and k-split):
 // thread 0 streams A (the weight copy in the canonical layout, below) and B
 // (the digits, encoded in the same layout) into a 4-stage shared-memory ring
 // with cp.async.bulk + mbarrier transaction counts; thread 32 issues the MMAs
 // and releases each stage with tcgen05.commit.  Afterwards the 4 warps read
-// their 32 tensor-memory lanes (tcgen05.ld 32x32b) and run the same stripe
-// epilogue as the GEMV, so results are identical to it bit for bit.
+// their 32 tensor-memory lanes (tcgen05.ld 32x32b), one token group at a
+// time, and run the same stripe epilogue as the GEMV, so results are
+// identical to it bit for bit.
 //
 // Canonical K-major, no-swizzle operand layout per 32-column k-step:
 // [row / 8][k / 16][row % 8][16 bytes] (core matrices of 8 rows x 16 bytes,
 // the two K halves 128 bytes apart = LBO, 8-row groups 256 bytes apart = SBO).
 constexpr int kTcRows = 128;
-constexpr int kTcN = 48;
-constexpr int kTcChunk = 8;    // k-steps per stage
 constexpr int kTcStages = 4;
 constexpr int kTcAStep = kTcRows * 32;  // bytes of A per k-step
-constexpr int kTcBStep = kTcN * 32;     // bytes of B per k-step
-constexpr uint32_t kTcTmemCols = 64;
 constexpr long long kTcSpin = 1ll << 22;  // try_wait rounds before giving up
+constexpr int kTcGroupCols = 48;        // digit columns of one token group
+// shared staging of one token group's accumulators: [warp][half][16][49]
+constexpr size_t kTcStageBytes = (size_t)4 * 2 * 16 * (kTcGroupCols + 1) * sizeof(int);
+template <int G>
+struct TcCfg {
+  static constexpr int N = kTcGroupCols * G;  // MMA N (multiple of 16, <= 256)
+  static constexpr int BStep = N * 32;        // bytes of B per k-step
+  static constexpr int Chunk = G == 1 ? 8 : (G == 2 ? 6 : (G == 3 ? 5 : 4));  // k-steps per stage
+  static constexpr uint32_t TmemCols = G == 1 ? 64 : (G == 2 ? 128 : 256);     // power of 2 >= N
+  static constexpr size_t Smem = (size_t)kTcStages * Chunk * (kTcAStep + BStep) + kTcStageBytes;
+  // kind::i8 instruction descriptor: s32 accumulator, signed A and B, both
+  // K-major, N, M = 128.
+  static constexpr uint32_t Idesc = (2u << 4) | (1u << 7) | (1u << 10) |
+                                    ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
+  static_assert(Smem <= 227 * 1024 - 2048, "tcgen05 GEMM shared memory");
+};
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -2179,16 +2263,13 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(128 >> 4) << 16) |
          ((uint64_t)(256 >> 4) << 32) | (1ull << 46);
 }
-// kind::i8 instruction descriptor: s32 accumulator, signed A and B, both
-// K-major, N = 48, M = 128.
-constexpr uint32_t kTcIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcN >> 3) << 17) |
-                              ((uint32_t)(kTcRows >> 4) << 24);
-__device__ __forceinline__ void umma_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+__device__ __forceinline__ void umma_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                        uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-      "l"(a), "l"(b), "r"(kTcIdesc), "r"(acc)
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t* b) {
@@ -2206,17 +2287,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 
-constexpr size_t kTcSmem =
-    (size_t)kTcStages * kTcChunk * (kTcAStep + kTcBStep) + 4 * 2 * 16 * (kTcN + 1) * sizeof(int);
-
-template <int EPI>
+template <int EPI, int G>
 __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
-  constexpr int COLS = kTcN;
+  using C = TcCfg<G>;
+  constexpr int GC = kTcGroupCols;
   extern __shared__ __align__(128) uint8_t tc_smem[];
   uint8_t* smA = tc_smem;
-  uint8_t* smB = tc_smem + (size_t)kTcStages * kTcChunk * kTcAStep;
-  int (*sm_t)[2][16][COLS + 1] = reinterpret_cast<int (*)[2][16][COLS + 1]>(
-      tc_smem + (size_t)kTcStages * kTcChunk * (kTcAStep + kTcBStep));
+  uint8_t* smB = tc_smem + (size_t)kTcStages * C::Chunk * kTcAStep;
+  int (*sm_t)[2][16][GC + 1] = reinterpret_cast<int (*)[2][16][GC + 1]>(
+      tc_smem + (size_t)kTcStages * C::Chunk * (kTcAStep + C::BStep));
   __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], done;
   __shared__ uint32_t tmem_base;
   __shared__ int sm_exp[kMaxTokens], s_issued, s_consumed, s_fail;
@@ -2227,12 +2306,12 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
   const int KB = a.KB;
   const int k0 = (int)((long long)KB * split / nsplit), k1 = (int)((long long)KB * (split + 1) / nsplit);
   const int nk = k1 - k0;
-  const int n_chunks = (nk + kTcChunk - 1) / kTcChunk;
+  const int n_chunks = (nk + C::Chunk - 1) / C::Chunk;
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_addr(&tmem_base)),
-                 "r"(kTcTmemCols)
+                 "r"(C::TmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -2251,7 +2330,7 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = tmem_base;
   const uint8_t* wsrc = reinterpret_cast<const uint8_t*>(a.wtc) + ((size_t)tile * KB + k0) * kTcAStep;
-  const uint8_t* xsrc = a.x + (size_t)k0 * kTcBStep;
+  const uint8_t* xsrc = a.x + (size_t)k0 * C::BStep;
   if (threadIdx.x == 0)  // the weights are independent of the producer grid
     prefetch_l2_bulk(wsrc, (uint32_t)min((long long)nk * kTcAStep, 1ll << 20));
   grid_wait();
@@ -2266,12 +2345,12 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
         s_fail = 1;
         break;
       }
-      const int steps = min(kTcChunk, nk - i * kTcChunk);
-      mbar_expect_tx(&full[s], (uint32_t)steps * (kTcAStep + kTcBStep));
-      bulk_load(smA + (size_t)s * kTcChunk * kTcAStep, wsrc + (size_t)i * kTcChunk * kTcAStep,
+      const int steps = min(C::Chunk, nk - i * C::Chunk);
+      mbar_expect_tx(&full[s], (uint32_t)steps * (kTcAStep + C::BStep));
+      bulk_load(smA + (size_t)s * C::Chunk * kTcAStep, wsrc + (size_t)i * C::Chunk * kTcAStep,
                 (uint32_t)steps * kTcAStep, &full[s]);
-      bulk_load(smB + (size_t)s * kTcChunk * kTcBStep, xsrc + (size_t)i * kTcChunk * kTcBStep,
-                (uint32_t)steps * kTcBStep, &full[s]);
+      bulk_load(smB + (size_t)s * C::Chunk * C::BStep, xsrc + (size_t)i * C::Chunk * C::BStep,
+                (uint32_t)steps * C::BStep, &full[s]);
     }
     s_issued = i;
   } else if (threadIdx.x == 32) {  // MMA issuer
@@ -2283,11 +2362,11 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int steps = min(kTcChunk, nk - i * kTcChunk);
-      const uint32_t a0 = smem_addr(smA + (size_t)s * kTcChunk * kTcAStep);
-      const uint32_t b0 = smem_addr(smB + (size_t)s * kTcChunk * kTcBStep);
+      const int steps = min(C::Chunk, nk - i * C::Chunk);
+      const uint32_t a0 = smem_addr(smA + (size_t)s * C::Chunk * kTcAStep);
+      const uint32_t b0 = smem_addr(smB + (size_t)s * C::Chunk * C::BStep);
       for (int j = 0; j < steps; ++j)
-        umma_i8(tmem, umma_desc(a0 + j * kTcAStep), umma_desc(b0 + j * kTcBStep),
+        umma_i8(tmem, umma_desc(a0 + j * kTcAStep), umma_desc(b0 + j * C::BStep), C::Idesc,
                 (i > 0 || j > 0) ? 1u : 0u);
       umma_commit(&empty[s]);
     }
@@ -2305,45 +2384,68 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
   __syncthreads();
   const bool ok = !s_fail;
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  unsigned long long kmax[(8 * kMaxTokens) / 32];
-#pragma unroll
-  for (int i = 0; i < (8 * kMaxTokens) / 32; ++i) kmax[i] = 0ull;
+  unsigned long long kmax[(8 * kGroupTokens) / 32];
   if (ok && nk > 0) {
-    uint32_t acc[COLS];
     const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-#pragma unroll
-    for (int c = 0; c < COLS; c += 16) tmem_ld16(taddr + c, acc + c);
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
     // this thread holds row 32 * warp + lane: stripe 2 * warp + lane / 16
     const int sel = lane >> 4, r = lane & 15;
+    for (int g = 0; g < G; ++g) {
+      const int gm0 = g * kGroupTokens;
+      if (gm0 >= a.M) break;  // block-uniform
+      const int MG = min(kGroupTokens, a.M - gm0);
 #pragma unroll
-    for (int c = 0; c < COLS; ++c) sm_t[warp][sel][r][c] = (int)acc[c];
-    __syncwarp();
-    for (int h = 0; h < 2; ++h) {
-      const int stripe = tile * 8 + warp * 2 + h;
-      if (stripe >= a.n_stripes) break;  // warp-uniform
-      int* t = &sm_t[warp][h][0][0];
-      bool run = true;
-      if (nsplit > 1) {
-        // merge the k-splits through the zeroed global tile (exact integers)
-        int* gt = a.ws + (size_t)stripe * 16 * COLS;
-        for (int i = lane; i < 16 * COLS; i += 32) atomicAdd(gt + i, t[(i / COLS) * (COLS + 1) + i % COLS]);
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) {
-          __threadfence();
-          last = (atomicAdd(a.cnt + stripe, 1) == nsplit - 1);
-          if (last) __threadfence();
-        }
-        run = __shfl_sync(0xffffffffu, last, 0) != 0;
-        if (run) {
-          for (int i = lane; i < 16 * COLS; i += 32)
-            t[(i / COLS) * (COLS + 1) + i % COLS] = atomicExch(gt + i, 0);
-          if (lane == 0) atomicExch(a.cnt + stripe, 0);
+      for (int i = 0; i < (8 * kGroupTokens) / 32; ++i) kmax[i] = 0ull;
+      uint32_t acc[GC];
+#pragma unroll
+      for (int c = 0; c < GC; c += 16) tmem_ld16(taddr + g * GC + c, acc + c);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+      for (int c = 0; c < GC; ++c) sm_t[warp][sel][r][c] = (int)acc[c];
+      __syncwarp();
+      for (int h = 0; h < 2; ++h) {
+        const int stripe = tile * 8 + warp * 2 + h;
+        if (stripe >= a.n_stripes) break;  // warp-uniform
+        int* t = &sm_t[warp][h][0][0];
+        bool run = true;
+        if (nsplit > 1) {
+          // merge the k-splits through the zeroed global tile of this
+          // (stripe, group) (exact integers)
+          const size_t vs = (size_t)stripe * G + g;
+          int* gt = a.ws + vs * 16 * GC;
+          for (int i = lane; i < 16 * GC; i += 32) atomicAdd(gt + i, t[(i / GC) * (GC + 1) + i % GC]);
           __syncwarp();
+          int last = 0;
+          if (lane == 0) {
+            __threadfence();
+            last = (atomicAdd(a.cnt + vs, 1) == nsplit - 1);
+            if (last) __threadfence();
+          }
+          run = __shfl_sync(0xffffffffu, last, 0) != 0;
+          if (run) {
+            for (int i = lane; i < 16 * GC; i += 32)
+              t[(i / GC) * (GC + 1) + i % GC] = atomicExch(gt + i, 0);
+            if (lane == 0) atomicExch(a.cnt + vs, 0);
+            __syncwarp();
+          }
+        }
+        if (run)
+          gemv_epilogue<6, EPI>(a, stripe, t, GC + 1, lane, kmax, a.scale, sm_exp + gm0,
+                                a.m0 + gm0, MG);
+        __syncwarp();
+      }
+      if constexpr (EPI == EPI_LMHEAD) {
+#pragma unroll
+        for (int it = 0; it < (8 * kGroupTokens) / 32; ++it) {
+          unsigned long long k = kmax[it];
+#pragma unroll
+          for (int o = 1; o < 8; o <<= 1) {
+            unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
+            k = k2 > k ? k2 : k;
+          }
+          const int m = (it * 32 + lane) >> 3;
+          if ((lane & 7) == 0 && m < MG && k) atomicMax(&sm_keys[gm0 + m], k);
         }
       }
-      if (run) gemv_epilogue<6, EPI>(a, stripe, t, COLS + 1, lane, kmax, a.scale, sm_exp);
       __syncwarp();
     }
   } else if (!ok && threadIdx.x == 0 && a.err) {
@@ -2351,26 +2453,16 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
   }
   grid_launch_dependents();
   if constexpr (EPI == EPI_LMHEAD) {
-#pragma unroll
-    for (int it = 0; it < (8 * kMaxTokens) / 32; ++it) {
-      unsigned long long k = kmax[it];
-#pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
-        unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
-        k = k2 > k ? k2 : k;
-      }
-      const int m = (it * 32 + lane) >> 3;
-      if ((lane & 7) == 0 && m < a.M && k) atomicMax(&sm_keys[m], k);
-    }
     __syncthreads();
-    if (threadIdx.x < a.M && sm_keys[threadIdx.x]) atomicMax(a.keys + threadIdx.x, sm_keys[threadIdx.x]);
+    if (threadIdx.x < a.M && sm_keys[threadIdx.x])
+      atomicMax(a.keys + key_slot(a.seq, a.m0 + threadIdx.x), sm_keys[threadIdx.x]);
   }
   if constexpr (EPI == EPI_TP) tp_publish(a.tp);
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(kTcTmemCols)
+                 "r"(C::TmemCols)
                  : "memory");
   MC_TRACE_END(a.trace_slot);
 }
@@ -2408,42 +2500,63 @@ cudaError_t launch_pack_tc(const int8_t* src, long long src_ld, const int* row_m
   return cudaGetLastError();
 }
 
-template <int EPI>
+template <int EPI, int G>
 static cudaError_t launch_tc_t(const GemvArgs& a, int ksplit, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((a.n_stripes + 7) / 8, ksplit);
   cfg.blockDim = dim3(128);
-  cfg.dynamicSmemBytes = kTcSmem;
+  cfg.dynamicSmemBytes = TcCfg<G>::Smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_gemm_tc<EPI>, a);
+  return cudaLaunchKernelEx(&cfg, k_gemm_tc<EPI, G>, a);
+}
+
+template <int G>
+static cudaError_t launch_tc_g(const GemvArgs& a, int epi, int ksplit, cudaStream_t s, bool pdl) {
+  switch (epi) {
+    case EPI_STORE: return launch_tc_t<EPI_STORE, G>(a, ksplit, s, pdl);
+    case EPI_RESID: return launch_tc_t<EPI_RESID, G>(a, ksplit, s, pdl);
+    case EPI_SWIGLU: return launch_tc_t<EPI_SWIGLU, G>(a, ksplit, s, pdl);
+    case EPI_QKV: return launch_tc_t<EPI_QKV, G>(a, ksplit, s, pdl);
+    case EPI_LMHEAD: return launch_tc_t<EPI_LMHEAD, G>(a, ksplit, s, pdl);
+    case EPI_TP: return launch_tc_t<EPI_TP, G>(a, ksplit, s, pdl);
+  }
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_gemm_tc(const GemvArgs& a, int epi, int ksplit, cudaStream_t s, bool pdl) {
   if (!a.wtc || a.M > kMaxTokens || a.M < 1 || ksplit < 1 || (ksplit > 1 && (!a.ws || !a.cnt)))
     return cudaErrorInvalidValue;
-  switch (epi) {
-    case EPI_STORE: return launch_tc_t<EPI_STORE>(a, ksplit, s, pdl);
-    case EPI_RESID: return launch_tc_t<EPI_RESID>(a, ksplit, s, pdl);
-    case EPI_SWIGLU: return launch_tc_t<EPI_SWIGLU>(a, ksplit, s, pdl);
-    case EPI_QKV: return launch_tc_t<EPI_QKV>(a, ksplit, s, pdl);
-    case EPI_LMHEAD: return launch_tc_t<EPI_LMHEAD>(a, ksplit, s, pdl);
-    case EPI_TP: return launch_tc_t<EPI_TP>(a, ksplit, s, pdl);
+  switch (groups_for_tokens(a.M)) {
+    case 1: return launch_tc_g<1>(a, epi, ksplit, s, pdl);
+    case 2: return launch_tc_g<2>(a, epi, ksplit, s, pdl);
+    case 3: return launch_tc_g<3>(a, epi, ksplit, s, pdl);
+    case 4: return launch_tc_g<4>(a, epi, ksplit, s, pdl);
   }
   return cudaErrorInvalidValue;
 }
 
-cudaError_t prepare_tc() {
-  for (auto f : {k_gemm_tc<EPI_STORE>, k_gemm_tc<EPI_RESID>, k_gemm_tc<EPI_SWIGLU>,
-                 k_gemm_tc<EPI_QKV>, k_gemm_tc<EPI_LMHEAD>, k_gemm_tc<EPI_TP>}) {
-    cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+template <int G>
+static cudaError_t prepare_tc_g() {
+  for (auto f : {k_gemm_tc<EPI_STORE, G>, k_gemm_tc<EPI_RESID, G>, k_gemm_tc<EPI_SWIGLU, G>,
+                 k_gemm_tc<EPI_QKV, G>, k_gemm_tc<EPI_LMHEAD, G>, k_gemm_tc<EPI_TP, G>}) {
+    cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)TcCfg<G>::Smem);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
+}
+
+cudaError_t prepare_tc() {
+  cudaError_t e = prepare_tc_g<1>();
+  if (e == cudaSuccess) e = prepare_tc_g<2>();
+  if (e == cudaSuccess) e = prepare_tc_g<3>();
+  if (e == cudaSuccess) e = prepare_tc_g<4>();
+  return e;
 }
 
 }  // namespace mc

@@ -32,19 +32,22 @@ def _u32(a) -> np.ndarray:
 
 
 class Session:
-    """One request's device state: target KV, draft KV, speculative state.
+    """Device state of n_requests concurrent requests (default one): target
+    KV, draft KV and speculative state per request.
 
     Mirrors the reference's per-request ``Option<KvCache>`` (generate.rs:
-    617-627) plus the draft model's cache."""
+    617-627) plus the draft model's cache; a batched session decodes its
+    requests in lock step, each exactly as it would decode alone."""
 
     def __init__(self, target: Weights, draft: Weights | None = None, gamma: int = 4,
                  max_context: int = 2048, bonus: bool = False, temperature: float = 0.0,
-                 seed: int = 0, accept_mode: int = 0):
+                 seed: int = 0, accept_mode: int = 0, n_requests: int = 1):
         self.target, self.draft = target, draft
         self.gamma = gamma
+        self.n_requests = n_requests
         self._cancel = C.c_int32(0)
         cfg = _lib.SpecCfg(gamma, max_context, int(bonus), temperature, seed,
-                           C.pointer(self._cancel), accept_mode)
+                           C.pointer(self._cancel), accept_mode, n_requests)
         h = C.c_void_p()
         check(lib().mc_session_create(target.handle, draft.handle if draft else None,
                                       C.byref(cfg), C.byref(h)))
@@ -96,22 +99,51 @@ class Session:
             acc.ctypes.data_as(C.POINTER(C.c_int32)), len(acc), C.byref(n_rounds)))
         return out[: n_out.value].tolist(), acc[: min(n_rounds.value, len(acc))].tolist()
 
+    def speculative_generate_batch(self, prompts, max_tokens: int):
+        """Batched speculative_generate over this session's n_requests
+        prompts; returns one (generated ids, accepted per round) per prompt."""
+        p = _u32(np.concatenate([_u32(x) for x in prompts]))
+        lens = np.ascontiguousarray([len(x) for x in prompts], dtype=np.int32)
+        B = len(prompts)
+        stride = max_tokens + self.gamma + 2
+        out = np.zeros((B, stride), np.uint32)
+        acc = np.zeros((B, stride + 1), np.int32)
+        n_out = np.zeros(B, np.int32)
+        n_rounds = np.zeros(B, np.int32)
+        i32p = C.POINTER(C.c_int32)
+        check(lib().mc_speculative_generate_batch(
+            self.handle, p.ctypes.data_as(C.POINTER(C.c_uint32)), lens.ctypes.data_as(i32p), B,
+            max_tokens, out.ctypes.data_as(C.POINTER(C.c_uint32)), stride,
+            n_out.ctypes.data_as(i32p), acc.ctypes.data_as(i32p), stride + 1,
+            n_rounds.ctypes.data_as(i32p)))
+        return [(out[z, : n_out[z]].tolist(), acc[z, : min(n_rounds[z], stride + 1)].tolist())
+                for z in range(B)]
+
     def prime(self, prompt):
         p = _u32(prompt)
         check(lib().mc_spec_prime(self.handle, p.ctypes.data_as(C.POINTER(C.c_uint32)), len(p)))
+
+    def prime_batch(self, prompts):
+        """Prime one prompt per request (n_requests of them)."""
+        p = _u32(np.concatenate([_u32(x) for x in prompts]))
+        lens = np.ascontiguousarray([len(x) for x in prompts], dtype=np.int32)
+        check(lib().mc_spec_prime_batch(self.handle, p.ctypes.data_as(C.POINTER(C.c_uint32)),
+                                        lens.ctypes.data_as(C.POINTER(C.c_int32)), len(prompts)))
 
     def decode(self, max_tokens: int) -> int:
         n = C.c_int32()
         check(lib().mc_spec_decode(self.handle, max_tokens, C.byref(n)))
         return n.value
 
-    def read(self, cap: int = 1 << 16):
+    def read(self, cap: int = 1 << 16, request: int = 0):
+        """(generated ids, accepted per round) of one request."""
         out = np.zeros(cap, np.uint32)
         acc = np.zeros(cap, np.int32)
         n_out, n_rounds = C.c_int32(), C.c_int32()
-        check(lib().mc_spec_read(self.handle, out.ctypes.data_as(C.POINTER(C.c_uint32)), cap,
-                                 C.byref(n_out), acc.ctypes.data_as(C.POINTER(C.c_int32)), cap,
-                                 C.byref(n_rounds)))
+        check(lib().mc_spec_read_request(self.handle, request,
+                                         out.ctypes.data_as(C.POINTER(C.c_uint32)), cap,
+                                         C.byref(n_out), acc.ctypes.data_as(C.POINTER(C.c_int32)),
+                                         cap, C.byref(n_rounds)))
         return out[: n_out.value].tolist(), acc[: min(n_rounds.value, cap)].tolist()
 
     def rewind(self):
