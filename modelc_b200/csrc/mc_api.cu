@@ -163,11 +163,11 @@ struct PMat {
 };
 
 // k-split of a tcgen05 GEMM: enough CTAs to fill the SMs, each with at least
-// 16 k-steps.
+// 16 k-steps; the splits of a tile form one cluster (at most 8 CTAs).
 static int tc_ksplit(const PMat& W, int nsm) {
   const int tiles = (W.n_stripes + 7) / 8;
   int k = std::max(1, nsm / std::max(tiles, 1));
-  return std::max(1, std::min(k, W.KB / 16));
+  return std::max(1, std::min({k, W.KB / 16, kTcMaxSplit}));
 }
 
 // Projections run on the tcgen05 tensor cores when the matrix has the
@@ -1853,6 +1853,7 @@ struct mc_linear {
   Allocs al;
   uint8_t* xq = nullptr;
   int* xexp = nullptr;
+  unsigned* amax = nullptr;  // per-token max |x| for the encoder
   int* ws = nullptr;
   int* cnt = nullptr;
   int* err = nullptr;
@@ -1885,6 +1886,7 @@ extern "C" mc_status mc_linear_create(const mc_tensor_desc* w, int32_t device, m
     st = set_err(MC_E_CUDA, "kernel preparation failed");
   if (st == MC_OK) st = L->al.alloc(&L->xq, (size_t)kp * 48 * kMaxGroups);
   if (st == MC_OK) st = L->al.alloc(&L->xexp, (size_t)kMaxTokens);
+  if (st == MC_OK) st = L->al.alloc(&L->amax, (size_t)kMaxTokens);
   if (st == MC_OK) st = L->al.alloc(&L->ws, (size_t)L->m.n_stripes * kMaxGroups * 16 * 48);
   if (st == MC_OK) st = L->al.alloc(&L->cnt, (size_t)L->m.n_stripes * kMaxGroups);
   if (st == MC_OK) st = L->al.alloc(&L->err, 1);
@@ -1925,6 +1927,7 @@ extern "C" mc_status mc_linear_run(mc_linear* l, const float* x_dev, int32_t m, 
   cudaStream_t s = (cudaStream_t)stream;
   for (int r0 = 0; r0 < m; r0 += kMaxTokens) {
     const int M = std::min(kMaxTokens, m - r0);
+    CK(launch_act_amax(x_dev + (size_t)r0 * l->m.K, l->m.K, l->m.K, M, l->amax, s, true));
     QuantArgs q{};
     q.h = x_dev + (size_t)r0 * l->m.K;
     q.ld = l->m.K;
@@ -1935,6 +1938,8 @@ extern "C" mc_status mc_linear_run(mc_linear* l, const float* x_dev, int32_t m, 
     q.nt = nt_for_tokens(M);
     q.xexp = l->xexp;
     q.tc_layout = use_tc(l->m, M) ? 1 : 0;
+    q.use_stats = 1;  // max |x| per token from k_act_amax; no norm, no partial sums
+    q.amax = l->amax;
     CK(launch_quant(q, s, true));
     GemvArgs a{};
     a.x = l->xq;

@@ -320,7 +320,12 @@ cudaError_t launch_pack_tc(const int8_t* src, long long src_ld, const int* row_m
                            cudaStream_t s);
 cudaError_t prepare_tc();  // shared-memory limit of the tcgen05 GEMM (outside capture)
 constexpr int kTcTileRows = 128;
+constexpr int kTcMaxSplit = 8;  // k-split CTAs of one tile = one cluster (portable size)
 cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl);
+// amax[m] = max |x[m][0..d)| as float bits, m < M (the statistics of an
+// un-normalised encoding, QuantArgs::use_stats with np = 0)
+cudaError_t launch_act_amax(const float* x, int ld, int d, int M, unsigned* amax, cudaStream_t s,
+                            bool pdl);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t s, bool pdl);
 // One CTA per sequence z of a batch: st + z, ctx + z * ctx_stride,

@@ -1138,6 +1138,51 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
   }
 }
 
+// Per-token max |x| (float bits; NaN and inf order above every finite value)
+// of un-normalised activations, one CTA per token: the statistics the
+// encoder takes from a producer, for standalone projections.
+__global__ void __launch_bounds__(256) k_act_amax(const float* __restrict__ x, int ld, int d,
+                                                  unsigned* __restrict__ amax) {
+  grid_launch_dependents();
+  grid_wait();
+  const float* row = x + (size_t)blockIdx.x * ld;
+  uint32_t mx = 0u;
+  const bool vec = ((ld & 3) == 0) && ((d & 3) == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0);
+  if (vec) {
+    for (int i = threadIdx.x * 4; i < d; i += blockDim.x * 4) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(row + i));
+      mx = max(max(mx, __float_as_uint(fabsf(v.x))), __float_as_uint(fabsf(v.y)));
+      mx = max(max(mx, __float_as_uint(fabsf(v.z))), __float_as_uint(fabsf(v.w)));
+    }
+  } else {
+    for (int i = threadIdx.x; i < d; i += blockDim.x) mx = max(mx, __float_as_uint(fabsf(__ldcg(row + i))));
+  }
+  mx = __reduce_max_sync(0xffffffffu, mx);
+  __shared__ uint32_t red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t m = 0u;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = max(m, red[w]);
+    amax[blockIdx.x] = m;
+  }
+}
+
+cudaError_t launch_act_amax(const float* x, int ld, int d, int M, unsigned* amax, cudaStream_t s,
+                            bool pdl) {
+  if (M < 1 || M > kMaxTokens) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(M);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_act_amax, x, ld, d, amax);
+}
+
 cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl) {
   if (a.M < 1 || a.M > kMaxTokens) return cudaErrorInvalidValue;
   if (a.nt != nt_for_tokens(a.M)) return cudaErrorInvalidValue;
@@ -1178,10 +1223,23 @@ cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl) {
 // split).
 constexpr int kAttnThreads = 512;
 
+// 16-byte global -> shared copy that holds no registers (L2 only, as __ldcg).
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(smem_dst)),
+               "l"(gsrc)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 // RB: query rows per thread (all of them valid: R is a multiple of the
-// number of row groups in both passes, checked by the launcher).
+// number of row groups in both passes, checked by the launcher).  Small row
+// counts (RB <= 2: up to 32 query rows, the verify of a batch of requests)
+// run two CTAs per SM.
 template <int RB>
-__global__ void __launch_bounds__(kAttnThreads, 1) k_attention(AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads, RB <= 2 ? 2 : 1) k_attention(AttnArgs a) {
   MC_TRACE_T0
   extern __shared__ float smem[];
   __shared__ float s_m[128], s_l[128];
@@ -1225,15 +1283,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attention(AttnArgs a) {
   const float4* kbase = reinterpret_cast<const float4*>(a.kc + ((size_t)pg * a.Hkv + kvh) * P * hdp);
   const float4* vbase = reinterpret_cast<const float4*>(a.vc + ((size_t)pg * a.Hkv + kvh) * P * hdp);
   const int h4 = hdp >> 2;
-  // issue every K/V/q load of this CTA before the first shared store
+  // K/V copies go straight to shared memory (cp.async, no registers held);
+  // the q loads follow while they are in flight
   {
-    constexpr int kMaxLd = 8;  // P * hdp / 4 / threads for hdp <= 128
-    float4 kr[kMaxLd], vr[kMaxLd];
     const int n4 = nt * h4;
-#pragma unroll
-    for (int u = 0; u < kMaxLd; ++u) {
-      const int i = threadIdx.x + u * kAttnThreads;
-      if (i < n4) { kr[u] = __ldcg(kbase + i); vr[u] = __ldcg(vbase + i); }
+    for (int i = threadIdx.x; i < n4; i += kAttnThreads) {
+      const int t = i / h4, c4 = i - t * h4;
+      cp_async16(sk + (size_t)t * ks + 4 * c4, kbase + i);
+      cp_async16(reinterpret_cast<float4*>(sv) + i, vbase + i);
     }
     // q: four loads in flight per batch (the K/V loads above are already out)
     for (int i0 = threadIdx.x; i0 < Rp * h4; i0 += 4 * kAttnThreads) {
@@ -1254,20 +1311,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attention(AttnArgs a) {
         if (i < Rp * h4) reinterpret_cast<float4*>(sq)[i] = qr[u];
       }
     }
-#pragma unroll
-    for (int u = 0; u < kMaxLd; ++u) {
-      const int i = threadIdx.x + u * kAttnThreads;
-      if (i < n4) {
-        const int t = i / h4, c4 = i - t * h4;
-        *reinterpret_cast<float4*>(sk + (size_t)t * ks + 4 * c4) = kr[u];
-        reinterpret_cast<float4*>(sv)[i] = vr[u];
-      }
-    }
     // the P.V pass steps 4 positions at a time: zero V rows past the last
     // position (their probabilities are 0, and 0 * stale data could be NaN)
     const int ntr = (nt + 3) & ~3;
     for (int i = nt * h4 + threadIdx.x; i < ntr * h4; i += blockDim.x)
       reinterpret_cast<float4*>(sv)[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    cp_async_wait_all();
   }
   __syncthreads();
   MC_TRACE_PHASE(a.trace_slot, 1, mc_tp);
@@ -2207,24 +2256,34 @@ cudaError_t launch_pack_q4(const uint8_t* src, const int* row_map, int n_stripes
 // [row / 8][k / 16][row % 8][16 bytes] (core matrices of 8 rows x 16 bytes,
 // the two K halves 128 bytes apart = LBO, 8-row groups 256 bytes apart = SBO).
 constexpr int kTcRows = 128;
-constexpr int kTcStages = 4;
+#ifndef MC_TC_STAGES
+#define MC_TC_STAGES 4  // shared-memory ring stages of the tcgen05 GEMM
+#endif
+constexpr int kTcStages = MC_TC_STAGES;
+constexpr int kTcRingBudget = 180 * 1024;  // bytes of ring per CTA (one CTA per SM)
 constexpr int kTcAStep = kTcRows * 32;  // bytes of A per k-step
 constexpr long long kTcSpin = 1ll << 22;  // try_wait rounds before giving up
 constexpr int kTcGroupCols = 48;        // digit columns of one token group
-// shared staging of one token group's accumulators: [warp][half][16][49]
-constexpr size_t kTcStageBytes = (size_t)4 * 2 * 16 * (kTcGroupCols + 1) * sizeof(int);
 template <int G>
 struct TcCfg {
   static constexpr int N = kTcGroupCols * G;  // MMA N (multiple of 16, <= 256)
   static constexpr int BStep = N * 32;        // bytes of B per k-step
-  static constexpr int Chunk = G == 1 ? 8 : (G == 2 ? 6 : (G == 3 ? 5 : 4));  // k-steps per stage
+  // k-steps per stage: as many as the ring budget allows (at most 8)
+  static constexpr int ChunkFit = kTcRingBudget / (kTcStages * (kTcAStep + BStep));
+  static constexpr int Chunk = ChunkFit > 8 ? 8 : (ChunkFit < 1 ? 1 : ChunkFit);
   static constexpr uint32_t TmemCols = G == 1 ? 64 : (G == 2 ? 128 : 256);     // power of 2 >= N
-  static constexpr size_t Smem = (size_t)kTcStages * Chunk * (kTcAStep + BStep) + kTcStageBytes;
+  static constexpr size_t Ring = (size_t)kTcStages * Chunk * (kTcAStep + BStep);
+  // after the main loop the ring holds this CTA's partial tile [128][N + 4]
+  // (read by the cluster's peers) and per-warp stripe sums [4][16][N + 4]
+  static constexpr int LDP = N + 4;  // int row stride: 16-byte rows, conflict-free v4 stores
+  static constexpr size_t PartBytes = (size_t)kTcRows * LDP * sizeof(int);
+  static constexpr size_t SumBytes = (size_t)4 * 16 * LDP * sizeof(int);
+  static constexpr size_t Smem = Ring > PartBytes + SumBytes ? Ring : PartBytes + SumBytes;
+  static_assert(Smem <= 227 * 1024 - 2048, "tcgen05 GEMM shared memory");
   // kind::i8 instruction descriptor: s32 accumulator, signed A and B, both
   // K-major, N, M = 128.
   static constexpr uint32_t Idesc = (2u << 4) | (1u << 7) | (1u << 10) |
                                     ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
-  static_assert(Smem <= 227 * 1024 - 2048, "tcgen05 GEMM shared memory");
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -2277,6 +2336,30 @@ __device__ __forceinline__ void umma_commit(uint64_t* b) {
                    smem_addr(b))
                : "memory");
 }
+// Thread-block cluster helpers: rank in the cluster, a full cluster barrier
+// (release / acquire), and 16-byte loads from a peer CTA's shared memory.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
+                   "memory");
+}
+__device__ __forceinline__ uint32_t peer_addr(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ int4 ld_peer_v4(uint32_t addr) {
+  int4 v;
+  asm volatile("ld.shared::cluster.v4.s32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
@@ -2291,17 +2374,20 @@ template <int EPI, int G>
 __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
   using C = TcCfg<G>;
   constexpr int GC = kTcGroupCols;
+  constexpr int N = C::N, LDP = C::LDP;
   extern __shared__ __align__(128) uint8_t tc_smem[];
   uint8_t* smA = tc_smem;
   uint8_t* smB = tc_smem + (size_t)kTcStages * C::Chunk * kTcAStep;
-  int (*sm_t)[2][16][GC + 1] = reinterpret_cast<int (*)[2][16][GC + 1]>(
-      tc_smem + (size_t)kTcStages * C::Chunk * (kTcAStep + C::BStep));
+  // reused after the main loop: partial tile, then per-warp stripe sums
+  int* part = reinterpret_cast<int*>(tc_smem);
+  int* sums = reinterpret_cast<int*>(tc_smem + C::PartBytes);
   __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], done;
   __shared__ uint32_t tmem_base;
   __shared__ int sm_exp[kMaxTokens], s_issued, s_consumed, s_fail;
   __shared__ unsigned long long sm_keys[kMaxTokens];
   MC_TRACE_T0
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // the k-split CTAs of a tile form one cluster (grid y = cluster y)
   const int tile = blockIdx.x, nsplit = gridDim.y, split = blockIdx.y;
   const int KB = a.KB;
   const int k0 = (int)((long long)KB * split / nsplit), k1 = (int)((long long)KB * (split + 1) / nsplit);
@@ -2331,8 +2417,17 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
   const uint32_t tmem = tmem_base;
   const uint8_t* wsrc = reinterpret_cast<const uint8_t*>(a.wtc) + ((size_t)tile * KB + k0) * kTcAStep;
   const uint8_t* xsrc = a.x + (size_t)k0 * C::BStep;
-  if (threadIdx.x == 0)  // the weights are independent of the producer grid
-    prefetch_l2_bulk(wsrc, (uint32_t)min((long long)nk * kTcAStep, 1ll << 20));
+  // The weights never depend on the producer grid: the first ring stages'
+  // weight copies go out before the dependency wait (their activation
+  // copies, after it, complete the same transaction counts).
+  const int pre = min(n_chunks, kTcStages);
+  if (threadIdx.x == 0)
+    for (int i = 0; i < pre; ++i) {
+      const int steps = min(C::Chunk, nk - i * C::Chunk);
+      mbar_expect_tx(&full[i], (uint32_t)steps * (kTcAStep + C::BStep));
+      bulk_load(smA + (size_t)i * C::Chunk * kTcAStep, wsrc + (size_t)i * C::Chunk * kTcAStep,
+                (uint32_t)steps * kTcAStep, &full[i]);
+    }
   grid_wait();
   MC_TRACE_WAITED(a.trace_slot);
   if (threadIdx.x < a.M) sm_exp[threadIdx.x] = __ldcg(a.xexp + threadIdx.x);
@@ -2341,14 +2436,16 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
     int i = 0;
     for (; i < n_chunks; ++i) {
       const int s = i % kTcStages;
-      if (i >= kTcStages && !mbar_wait(&empty[s], ((i / kTcStages) - 1) & 1)) {
-        s_fail = 1;
-        break;
-      }
       const int steps = min(C::Chunk, nk - i * C::Chunk);
-      mbar_expect_tx(&full[s], (uint32_t)steps * (kTcAStep + C::BStep));
-      bulk_load(smA + (size_t)s * C::Chunk * kTcAStep, wsrc + (size_t)i * C::Chunk * kTcAStep,
-                (uint32_t)steps * kTcAStep, &full[s]);
+      if (i >= pre) {
+        if (!mbar_wait(&empty[s], ((i / kTcStages) - 1) & 1)) {
+          s_fail = 1;
+          break;
+        }
+        mbar_expect_tx(&full[s], (uint32_t)steps * (kTcAStep + C::BStep));
+        bulk_load(smA + (size_t)s * C::Chunk * kTcAStep, wsrc + (size_t)i * C::Chunk * kTcAStep,
+                  (uint32_t)steps * kTcAStep, &full[s]);
+      }
       bulk_load(smB + (size_t)s * C::Chunk * C::BStep, xsrc + (size_t)i * C::Chunk * C::BStep,
                 (uint32_t)steps * C::BStep, &full[s]);
     }
@@ -2384,76 +2481,101 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
   __syncthreads();
   const bool ok = !s_fail;
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  unsigned long long kmax[(8 * kGroupTokens) / 32];
-  if (ok && nk > 0) {
+  if (!ok && threadIdx.x == 0 && a.err) atomicExch(a.err, 1);
+  // 1) this CTA's partial tile in the idle ring: thread (warp, lane) holds
+  //    accumulator row 32 * warp + lane (an empty k-range contributes 0)
+  {
     const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-    // this thread holds row 32 * warp + lane: stripe 2 * warp + lane / 16
-    const int sel = lane >> 4, r = lane & 15;
-    for (int g = 0; g < G; ++g) {
-      const int gm0 = g * kGroupTokens;
-      if (gm0 >= a.M) break;  // block-uniform
-      const int MG = min(kGroupTokens, a.M - gm0);
+    int* prow = part + (size_t)(warp * 32 + lane) * LDP;
+    const bool have = ok && nk > 0;  // block-uniform
+#pragma unroll 1
+    for (int c = 0; c < N; c += GC) {  // one token group (three loads) per wait
+      uint32_t v[GC];
+      if (have) {
 #pragma unroll
-      for (int i = 0; i < (8 * kGroupTokens) / 32; ++i) kmax[i] = 0ull;
-      uint32_t acc[GC];
+        for (int j = 0; j < GC; j += 16) tmem_ld16(taddr + c + j, v + j);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      } else {
 #pragma unroll
-      for (int c = 0; c < GC; c += 16) tmem_ld16(taddr + g * GC + c, acc + c);
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-      for (int c = 0; c < GC; ++c) sm_t[warp][sel][r][c] = (int)acc[c];
-      __syncwarp();
-      for (int h = 0; h < 2; ++h) {
-        const int stripe = tile * 8 + warp * 2 + h;
-        if (stripe >= a.n_stripes) break;  // warp-uniform
-        int* t = &sm_t[warp][h][0][0];
-        bool run = true;
-        if (nsplit > 1) {
-          // merge the k-splits through the zeroed global tile of this
-          // (stripe, group) (exact integers)
-          const size_t vs = (size_t)stripe * G + g;
-          int* gt = a.ws + vs * 16 * GC;
-          for (int i = lane; i < 16 * GC; i += 32) atomicAdd(gt + i, t[(i / GC) * (GC + 1) + i % GC]);
-          __syncwarp();
-          int last = 0;
-          if (lane == 0) {
-            __threadfence();
-            last = (atomicAdd(a.cnt + vs, 1) == nsplit - 1);
-            if (last) __threadfence();
-          }
-          run = __shfl_sync(0xffffffffu, last, 0) != 0;
-          if (run) {
-            for (int i = lane; i < 16 * GC; i += 32)
-              t[(i / GC) * (GC + 1) + i % GC] = atomicExch(gt + i, 0);
-            if (lane == 0) atomicExch(a.cnt + vs, 0);
-            __syncwarp();
-          }
-        }
-        if (run)
-          gemv_epilogue<6, EPI>(a, stripe, t, GC + 1, lane, kmax, a.scale, sm_exp + gm0,
-                                a.m0 + gm0, MG);
-        __syncwarp();
+        for (int j = 0; j < GC; ++j) v[j] = 0u;
       }
-      if constexpr (EPI == EPI_LMHEAD) {
 #pragma unroll
-        for (int it = 0; it < (8 * kGroupTokens) / 32; ++it) {
-          unsigned long long k = kmax[it];
-#pragma unroll
-          for (int o = 1; o < 8; o <<= 1) {
-            unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
-            k = k2 > k ? k2 : k;
-          }
-          const int m = (it * 32 + lane) >> 3;
-          if ((lane & 7) == 0 && m < MG && k) atomicMax(&sm_keys[gm0 + m], k);
-        }
-      }
-      __syncwarp();
+      for (int j = 0; j < GC; j += 4)
+        *reinterpret_cast<int4*>(prow + c + j) =
+            make_int4((int)v[j], (int)v[j + 1], (int)v[j + 2], (int)v[j + 3]);
     }
-  } else if (!ok && threadIdx.x == 0 && a.err) {
-    atomicExch(a.err, 1);
+  }
+  // 2) every partial tile of the cluster is staged
+  if (nsplit > 1) cluster_sync_all(); else __syncthreads();
+  // 3) this CTA finishes stripes rank, rank + nsplit, ... of the tile: the
+  //    exact int32 sum of the cluster's partial rows (read through
+  //    distributed shared memory), then the stripe epilogue of each group
+  unsigned long long kmax[(8 * kGroupTokens) / 32];
+  const int rank = nsplit > 1 ? (int)cluster_rank() : 0;
+  int* wsum = sums + (size_t)warp * 16 * LDP;
+  constexpr int V4 = N / 4;  // 16-byte units per row
+  for (int j = warp; ; j += 4) {
+    const int st_local = rank + j * nsplit;  // stripe within the tile
+    if (st_local >= 8) break;                // warp-uniform
+    const int stripe = tile * 8 + st_local;
+    if (stripe >= a.n_stripes) break;
+    const int* prows = part + (size_t)st_local * 16 * LDP;
+    const uint32_t base = smem_addr(prows);
+    for (int i = lane; i < 16 * V4; i += 32) {
+      const int r = i / V4, c4 = i - r * V4;
+      const int off = r * LDP + c4 * 4;
+      int4 acc;
+      if (nsplit > 1) {
+        // every peer's load in flight before the first add
+        int4 v[kTcMaxSplit];
+#pragma unroll
+        for (int q = 0; q < kTcMaxSplit; ++q)
+          if (q < nsplit) v[q] = ld_peer_v4(peer_addr(base + (uint32_t)off * 4u, (uint32_t)q));
+        acc = v[0];
+#pragma unroll
+        for (int q = 1; q < kTcMaxSplit; ++q)
+          if (q < nsplit) {
+            acc.x += v[q].x;
+            acc.y += v[q].y;
+            acc.z += v[q].z;
+            acc.w += v[q].w;
+          }
+      } else {
+        acc = *reinterpret_cast<const int4*>(prows + off);
+      }
+      *reinterpret_cast<int4*>(wsum + off) = acc;
+    }
+    __syncwarp();
+    if (ok) {
+      for (int g = 0; g < G; ++g) {
+        const int gm0 = g * kGroupTokens;
+        if (gm0 >= a.M) break;  // warp-uniform
+        const int MG = min(kGroupTokens, a.M - gm0);
+#pragma unroll
+        for (int i = 0; i < (8 * kGroupTokens) / 32; ++i) kmax[i] = 0ull;
+        gemv_epilogue<6, EPI>(a, stripe, wsum + g * GC, LDP, lane, kmax, a.scale, sm_exp + gm0,
+                              a.m0 + gm0, MG);
+        if constexpr (EPI == EPI_LMHEAD) {
+#pragma unroll
+          for (int it = 0; it < (8 * kGroupTokens) / 32; ++it) {
+            unsigned long long k = kmax[it];
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+              unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
+              k = k2 > k ? k2 : k;
+            }
+            const int m = (it * 32 + lane) >> 3;
+            if ((lane & 7) == 0 && m < MG && k) atomicMax(&sm_keys[gm0 + m], k);
+          }
+        }
+      }
+    }
+    __syncwarp();
   }
   grid_launch_dependents();
+  // 4) no CTA leaves while a peer may still read its partial tile
+  if (nsplit > 1) cluster_sync_all(); else __syncthreads();
   if constexpr (EPI == EPI_LMHEAD) {
-    __syncthreads();
     if (threadIdx.x < a.M && sm_keys[threadIdx.x])
       atomicMax(a.keys + key_slot(a.seq, a.m0 + threadIdx.x), sm_keys[threadIdx.x]);
   }
@@ -2507,11 +2629,15 @@ static cudaError_t launch_tc_t(const GemvArgs& a, int ksplit, cudaStream_t s, bo
   cfg.blockDim = dim3(128);
   cfg.dynamicSmemBytes = TcCfg<G>::Smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;  // the k-splits of a tile
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = (unsigned)ksplit;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, k_gemm_tc<EPI, G>, a);
 }
 
@@ -2529,7 +2655,7 @@ static cudaError_t launch_tc_g(const GemvArgs& a, int epi, int ksplit, cudaStrea
 }
 
 cudaError_t launch_gemm_tc(const GemvArgs& a, int epi, int ksplit, cudaStream_t s, bool pdl) {
-  if (!a.wtc || a.M > kMaxTokens || a.M < 1 || ksplit < 1 || (ksplit > 1 && (!a.ws || !a.cnt)))
+  if (!a.wtc || a.M > kMaxTokens || a.M < 1 || ksplit < 1 || ksplit > kTcMaxSplit)
     return cudaErrorInvalidValue;
   switch (groups_for_tokens(a.M)) {
     case 1: return launch_tc_g<1>(a, epi, ksplit, s, pdl);
