@@ -458,7 +458,8 @@ static mc_status pack_matrix(const SrcI8& src, const std::vector<int>& row_map,
                                    out->w, out->scale, 0);
   const int n_tiles = (out->n_stripes + 7) / 8;
   mc_status st = MC_OK;
-  if (e == cudaSuccess) st = al.alloc(&out->wtc, (size_t)n_tiles * out->KB * (kTcTileRows * 32 / 16));
+  // swizzled tcgen05 copy: 128 x 128 bytes (1024 int4) per tile and K atom
+  if (e == cudaSuccess) st = al.alloc(&out->wtc, (size_t)n_tiles * tc_atoms(out->KB) * 1024);
   if (e == cudaSuccess && st == MC_OK)
     e = launch_pack_tc(src.q, src.cols, drm, dcm, (int)row_map.size(), n_tiles, out->KB, out->wtc, 0);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -883,10 +884,12 @@ static mc_status alloc_kv(mc_session* s, const mc_weights* W, KVSet* kv) {
   return MC_OK;
 }
 
+// Widest activation (input columns), rounded to whole 128-column K atoms of
+// the tcgen05 digit layout.
 static int max_kp(const mc_weights* W) {
-  int m = round_up(W->d, 32);
-  m = std::max(m, round_up(W->H * W->hdp, 32));
-  m = std::max(m, round_up(W->F, 32));
+  int m = round_up(W->d, 128);
+  m = std::max(m, round_up(W->H * W->hdp, 128));
+  m = std::max(m, round_up(W->F, 128));
   return m;
 }
 
@@ -1881,7 +1884,7 @@ extern "C" mc_status mc_linear_create(const mc_tensor_desc* w, int32_t device, m
     st = pack_matrix(src, identity_map(src.rows, round_up(src.rows, 16)),
                      identity_map(src.cols, round_up(src.cols, 32)), src.rows, src.cols, L->al,
                      &L->m);
-  const int kp = round_up(src.cols, 32);
+  const int kp = round_up(src.cols, 128);  // whole K atoms of the tcgen05 digit layout
   if (st == MC_OK && (prepare_kernels(0, 0) != cudaSuccess || prepare_tc() != cudaSuccess))
     st = set_err(MC_E_CUDA, "kernel preparation failed");
   if (st == MC_OK) st = L->al.alloc(&L->xq, (size_t)kp * 48 * kMaxGroups);

@@ -321,6 +321,11 @@ cudaError_t launch_pack_tc(const int8_t* src, long long src_ld, const int* row_m
 cudaError_t prepare_tc();  // shared-memory limit of the tcgen05 GEMM (outside capture)
 constexpr int kTcTileRows = 128;
 constexpr int kTcMaxSplit = 8;  // k-split CTAs of one tile = one cluster (portable size)
+// The tcgen05 operands are K-major with the 128-byte swizzle: K runs in atoms
+// of 128 bytes (4 k-blocks of 32); the weight copy is [tile][atom][128 rows]
+// [128 bytes], the digits [atom][column][128 bytes], 16-byte chunk c of row r
+// stored at chunk c ^ (r % 8).  K is padded to whole atoms (zero weights).
+__host__ __device__ inline int tc_atoms(int KB) { return (KB + 3) / 4; }
 cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl);
 // amax[m] = max |x[m][0..d)| as float bits, m < M (the statistics of an
 // un-normalised encoding, QuantArgs::use_stats with np = 0)

@@ -402,11 +402,14 @@ constexpr int kEncBatch = 8;
 
 // Word index of the 4 digit bytes of column c, k-block kb, k = kk..kk+3
 // (kk % 4 == 0).  mma.sync layout: [kb][lane][tile][reg], lane = (c%8)*4 +
-// (kk%16)/4, the B fragment of m16n8k32.  tcgen05 layout (tc): the canonical
-// K-major no-swizzle tile [kb][c/8][kk/16][c%8][16 bytes], i.e. 8-column x
-// 16-byte core matrices, the two K halves 128 bytes apart, column groups 256.
+// (kk%16)/4, the B fragment of m16n8k32.  tcgen05 layout (tc): K-major with
+// the 128-byte swizzle, [kb/4][column][128 bytes] with the row's 16-byte
+// chunk q = (kb%4)*2 + kk/16 stored at q ^ (column % 8).
 __device__ __forceinline__ size_t digit_word(int kb, int c, int kk, int nt, bool tc) {
-  if (tc) return ((((size_t)kb * nt + (c >> 3)) * 2 + (kk >> 4)) * 32) + (c & 7) * 4 + ((kk & 15) >> 2);
+  if (tc) {
+    const int q = ((kb & 3) << 1) | (kk >> 4);
+    return ((size_t)(kb >> 2) * (8 * nt) + c) * 32 + (size_t)(((q ^ (c & 7)) << 2) + ((kk & 15) >> 2));
+  }
   return (((size_t)kb * 32 + (c & 7) * 4 + ((kk & 15) >> 2)) * nt + (c >> 3)) * 2 + (kk >> 4);
 }
 // Word index of column c of a forward of `groups` token groups: the tcgen05
@@ -521,36 +524,89 @@ constexpr int kGemvWarps = 8;
 // Lane (it, lane) handles rows r and r+8 of tile token m, with
 // idx = it*32 + lane, r = idx & 7, m = idx >> 3; the 8 lanes of a token form
 // one shuffle group for the encoding statistics.  xexp holds the tile's
-// token exponents.
+// token exponents; tok (or nullptr) its tokens' (position, KV page), resolved
+// ahead for the QKV epilogue.  A lane's rows are the same in every
+// iteration, so all its global loads (row scales, next-norm weights, then per
+// iteration the residual rows or the RoPE factors) are issued before the
+// arithmetic.
 template <int NT, int EPI, typename T>
 __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, const T* tile,
                                               int ld, int lane, unsigned long long* kmax,
                                               const float* scale, const int* xexp, int m0,
-                                              int MG) {
+                                              int MG, const int2* tok = nullptr) {
+  constexpr int NIT = (8 * kGroupTokens) / 32;
+  const int r = lane & 7;
+  const int prow = stripe * 16 + r;
+  // q4_0 tiles carry their block scales already; int8 tiles take the row scale
+  const float sc0 = scale ? scale[prow] : 1.0f, sc1 = scale ? scale[prow + 8] : 1.0f;
+  float w0 = 1.0f, w1 = 1.0f;  // next RMSNorm weight of the rows (RESID statistics)
+  if constexpr (EPI == EPI_RESID) {
+    if (a.st_w) {
+      if (prow < a.n_out) w0 = a.st_w[prow];
+      if (prow + 8 < a.n_out) w1 = a.st_w[prow + 8];
+    }
+  }
+  // per iteration: RESID the current h rows; QKV position, page, cos, sin
+  float p0[NIT], p1[NIT];
+  int ppos[NIT], ppg[NIT];
+  // QKV geometry of this stripe and lane (rows r and r+8 are the RoPE pair
+  // (i, i + half), transformer.rs:921-938; V stripes hold 16 plain rows)
+  const int per_head = a.half_p >> 3;  // stripes per head (Q/K) = hdp/16
+  const bool rope = stripe < a.sq + a.sk;
+  const bool isq = stripe < a.sq;
+  const int s2 = rope ? (isq ? stripe : stripe - a.sq) : stripe - a.sq - a.sk;
+  const int hh = per_head > 0 ? s2 / per_head : 0;
+  const int ri = (s2 - hh * per_head) * (rope ? 8 : 16) + r;  // i (RoPE) or j (V)
 #pragma unroll
-  for (int it = 0; it < (8 * kGroupTokens) / 32; ++it) {
+  for (int it = 0; it < NIT; ++it) {
+    const int m = it * 4 + (lane >> 3);
+    p0[it] = p1[it] = 0.0f;
+    ppos[it] = ppg[it] = 0;
+    if (it * 32 >= 8 * MG || m >= MG) continue;
+    const int mt = m0 + m;
+    if constexpr (EPI == EPI_RESID) {
+      const float* o = a.out + (size_t)mt * a.ldo;
+      if (prow < a.n_out) p0[it] = o[prow];
+      if (prow + 8 < a.n_out) p1[it] = o[prow + 8];
+    } else if constexpr (EPI == EPI_QKV) {
+      int pos, pg;
+      if (tok) {
+        pos = tok[m].x;
+        pg = tok[m].y;
+      } else {
+        const int z = seq_of(a.seq, mt);
+        pos = a.pos_ptr[z * a.seq.pos_stride] + a.pos_add + seq_off(a.seq, mt);
+        pg = a.page_table[z * a.seq.pt_stride + pos / a.page];
+      }
+      ppos[it] = pos;
+      ppg[it] = pg;
+      if (rope) {
+        p0[it] = a.rope_cos[(size_t)pos * a.half_p + ri];
+        p1[it] = a.rope_sin[(size_t)pos * a.half_p + ri];
+      }
+    }
+  }
+#pragma unroll
+  for (int it = 0; it < NIT; ++it) {
     if (it * 32 >= 8 * MG) break;  // warp-uniform
     const int idx = it * 32 + lane;
     const bool valid = idx < 8 * MG;
-    const int r = idx & 7, m = valid ? (idx >> 3) : 0;
+    const int m = valid ? (idx >> 3) : 0;
     const int mt = m0 + m;  // forward-wide token
-    const int prow = stripe * 16 + r;
     // statistics contribution of this lane: sum(h*h) and max|h*w| kept as
     // float bits, whose unsigned order matches |x| and lets NaN/inf win
     float st_sq = 0.0f;
     uint32_t st_mx = 0u;
     if (valid) {
       const int e = xexp[m];
-      // q4_0 tiles carry their block scales already; int8 tiles take the row scale
-      const float sc0 = scale ? scale[prow] : 1.0f, sc1 = scale ? scale[prow + 8] : 1.0f;
       const float y0 = combine_digits(tile + r * ld, m, sc0, e);
       const float y1 = combine_digits(tile + (r + 8) * ld, m, sc1, e);
       if constexpr (EPI == EPI_TP) {
         // this rank's partial rows into slot `rank` of every rank's buffer
         const TPArgs& t = a.tp;
         const size_t off = (((size_t)(__ldcg(t.epoch) & 1u) * t.world + t.rank) * kMaxTokens + mt) * t.d;
-        for (int r = 0; r < t.world; ++r) {
-          float* o = t.red[r] + off;
+        for (int q = 0; q < t.world; ++q) {
+          float* o = t.red[q] + off;
           if (prow < a.n_out) o[prow] = y0;
           if (prow + 8 < a.n_out) o[prow + 8] = y1;
         }
@@ -558,10 +614,10 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
         float* o = a.out ? a.out + (size_t)mt * a.ldo : nullptr;
         if (prow < a.n_out) {
           if constexpr (EPI == EPI_RESID) {
-            const float h0 = __fadd_rn(o[prow], y0);
+            const float h0 = __fadd_rn(p0[it], y0);
             o[prow] = h0;
             st_sq = __fmul_rn(h0, h0);
-            st_mx = __float_as_uint(fabsf(__fmul_rn(h0, a.st_w ? a.st_w[prow] : 1.0f)));
+            st_mx = __float_as_uint(fabsf(__fmul_rn(h0, w0)));
           } else if (o) {
             o[prow] = y0;
           }
@@ -574,10 +630,10 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
         }
         if (prow + 8 < a.n_out) {
           if constexpr (EPI == EPI_RESID) {
-            const float h1 = __fadd_rn(o[prow + 8], y1);
+            const float h1 = __fadd_rn(p1[it], y1);
             o[prow + 8] = h1;
             st_sq = __fadd_rn(st_sq, __fmul_rn(h1, h1));
-            st_mx = max(st_mx, __float_as_uint(fabsf(__fmul_rn(h1, a.st_w ? a.st_w[prow + 8] : 1.0f))));
+            st_mx = max(st_mx, __float_as_uint(fabsf(__fmul_rn(h1, w1))));
           } else if (o) {
             o[prow + 8] = y1;
           }
@@ -596,37 +652,25 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
           st_mx = __float_as_uint(fabsf(act));
         }
       } else if constexpr (EPI == EPI_QKV) {
-        const int z = seq_of(a.seq, mt);
-        const int pos = a.pos_ptr[z * a.seq.pos_stride] + a.pos_add + seq_off(a.seq, mt);
-        const int per_head = a.half_p >> 3;  // stripes per head (Q/K) = hdp/16
+        const int pos = ppos[it], pg = ppg[it];
         const int slot = pos % a.page;
-        const int pg = a.page_table[z * a.seq.pt_stride + pos / a.page];
-        if (stripe < a.sq + a.sk) {
-          // rows r and r+8 are the RoPE pair (i, i + half) (transformer.rs:921-938)
-          const bool isq = stripe < a.sq;
-          const int s2 = isq ? stripe : stripe - a.sq;
-          const int hh = s2 / per_head;
-          const int i = (s2 - hh * per_head) * 8 + r;
-          const float c = a.rope_cos[(size_t)pos * a.half_p + i];
-          const float sn = a.rope_sin[(size_t)pos * a.half_p + i];
+        if (rope) {
+          const float c = p0[it], sn = p1[it];
           const float o0 = __fsub_rn(__fmul_rn(y0, c), __fmul_rn(y1, sn));
           const float o1 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, c));
           if (isq) {
             float* q = a.q_out + ((size_t)mt * a.H + hh) * a.hdp;
-            q[i] = o0;
-            q[a.half_p + i] = o1;
+            q[ri] = o0;
+            q[a.half_p + ri] = o1;
           } else {
             float* k = a.kc + (((size_t)pg * a.Hkv + hh) * a.page + slot) * a.hdp;
-            k[i] = o0;
-            k[a.half_p + i] = o1;
+            k[ri] = o0;
+            k[a.half_p + ri] = o1;
           }
         } else {
-          const int s2 = stripe - a.sq - a.sk;
-          const int hh = s2 / per_head;
-          const int j = (s2 - hh * per_head) * 16 + r;
           float* v = a.vc + (((size_t)pg * a.Hkv + hh) * a.page + slot) * a.hdp;
-          v[j] = y0;
-          v[j + 8] = y1;
+          v[ri] = y0;
+          v[ri + 8] = y1;
         }
       }
     }
@@ -1235,11 +1279,11 @@ __device__ __forceinline__ void cp_async_wait_all() {
 }
 
 // RB: query rows per thread (all of them valid: R is a multiple of the
-// number of row groups in both passes, checked by the launcher).  Small row
-// counts (RB <= 2: up to 32 query rows, the verify of a batch of requests)
-// run two CTAs per SM.
-template <int RB>
-__global__ void __launch_bounds__(kAttnThreads, RB <= 2 ? 2 : 1) k_attention(AttnArgs a) {
+// number of row groups in both passes, checked by the launcher).  MINB: CTAs
+// per SM the registers are sized for -- 2 for grids of several waves with
+// few rows per CTA (the verify of a batch of requests), else 1.
+template <int RB, int MINB>
+__global__ void __launch_bounds__(kAttnThreads, MINB) k_attention(AttnArgs a) {
   MC_TRACE_T0
   extern __shared__ float smem[];
   __shared__ float s_m[128], s_l[128];
@@ -1565,11 +1609,21 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  static int nsm = 0;
+  if (!nsm) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    nsm = nsm > 0 ? nsm : 148;
+  }
+  const bool two = rb <= 2 && (long long)a.Hkv * a.max_chunks * n_seq * n_qb > 2LL * nsm;
   switch (rb) {
-    case 8: return cudaLaunchKernelEx(&cfg, k_attention<8>, a);
-    case 4: return cudaLaunchKernelEx(&cfg, k_attention<4>, a);
-    case 2: return cudaLaunchKernelEx(&cfg, k_attention<2>, a);
-    default: return cudaLaunchKernelEx(&cfg, k_attention<1>, a);
+    case 8: return cudaLaunchKernelEx(&cfg, k_attention<8, 1>, a);
+    case 4: return cudaLaunchKernelEx(&cfg, k_attention<4, 1>, a);
+    case 2: return two ? cudaLaunchKernelEx(&cfg, k_attention<2, 2>, a)
+                       : cudaLaunchKernelEx(&cfg, k_attention<2, 1>, a);
+    default: return two ? cudaLaunchKernelEx(&cfg, k_attention<1, 2>, a)
+                        : cudaLaunchKernelEx(&cfg, k_attention<1, 1>, a);
   }
 }
 
@@ -1578,7 +1632,8 @@ cudaError_t prepare_kernels(size_t quant_smem, size_t attn_smem) {
   (void)quant_smem;
 
   if (attn_smem > (size_t)g_attn_smem) {
-    for (auto f : {k_attention<8>, k_attention<4>, k_attention<2>, k_attention<1>}) {
+    for (auto f : {k_attention<8, 1>, k_attention<4, 1>, k_attention<2, 1>, k_attention<1, 1>,
+                   k_attention<2, 2>, k_attention<1, 2>}) {
       cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)attn_smem);
       if (e != cudaSuccess) return e;
@@ -2252,14 +2307,12 @@ cudaError_t launch_pack_q4(const uint8_t* src, const int* row_map, int n_stripes
 // time, and run the same stripe epilogue as the GEMV, so results are
 // identical to it bit for bit.
 //
-// Canonical K-major, no-swizzle operand layout per 32-column k-step:
-// [row / 8][k / 16][row % 8][16 bytes] (core matrices of 8 rows x 16 bytes,
-// the two K halves 128 bytes apart = LBO, 8-row groups 256 bytes apart = SBO).
+// Operands are K-major with the 128-byte swizzle (atoms of 8 rows x 128
+// bytes of K = 4 k-steps, 8-row groups 1024 bytes apart = SBO; the MMA of
+// k-step j of an atom starts 32 j bytes into it), so the tensor cores read
+// shared memory without bank conflicts.
 constexpr int kTcRows = 128;
-#ifndef MC_TC_STAGES
-#define MC_TC_STAGES 4  // shared-memory ring stages of the tcgen05 GEMM
-#endif
-constexpr int kTcStages = MC_TC_STAGES;
+constexpr int kTcMaxStages = 8;
 constexpr int kTcRingBudget = 180 * 1024;  // bytes of ring per CTA (one CTA per SM)
 constexpr int kTcAStep = kTcRows * 32;  // bytes of A per k-step
 constexpr long long kTcSpin = 1ll << 22;  // try_wait rounds before giving up
@@ -2268,18 +2321,27 @@ template <int G>
 struct TcCfg {
   static constexpr int N = kTcGroupCols * G;  // MMA N (multiple of 16, <= 256)
   static constexpr int BStep = N * 32;        // bytes of B per k-step
-  // k-steps per stage: as many as the ring budget allows (at most 8)
-  static constexpr int ChunkFit = kTcRingBudget / (kTcStages * (kTcAStep + BStep));
-  static constexpr int Chunk = ChunkFit > 8 ? 8 : (ChunkFit < 1 ? 1 : ChunkFit);
-  static constexpr uint32_t TmemCols = G == 1 ? 64 : (G == 2 ? 128 : 256);     // power of 2 >= N
-  static constexpr size_t Ring = (size_t)kTcStages * Chunk * (kTcAStep + BStep);
+  static constexpr int AtomA = kTcRows * 128;  // bytes of one A atom (4 k-steps)
+  static constexpr int AtomB = N * 128;
+  static constexpr int Chunk = G == 1 ? 8 : 4;  // k-steps per stage (whole atoms)
+  static constexpr int StageBytes = Chunk * (kTcAStep + BStep);
+  static constexpr int StagesFit = kTcRingBudget / StageBytes;
+  static constexpr int Stages = StagesFit > kTcMaxStages ? kTcMaxStages : StagesFit;
+  // independent accumulators, k-step j into accumulator j % NAcc: MMAs into
+  // one accumulator serialize, so consecutive k-steps go to different ones
+  // (summed exactly in the epilogue)
+  static constexpr int NAcc = G <= 2 ? 4 : (G == 3 ? 3 : 2);
+  static constexpr uint32_t TmemCols = G == 1 ? 256 : 512;  // power of 2 >= NAcc * N
+  static constexpr size_t Ring = (size_t)Stages * StageBytes;
   // after the main loop the ring holds this CTA's partial tile [128][N + 4]
   // (read by the cluster's peers) and per-warp stripe sums [4][16][N + 4]
   static constexpr int LDP = N + 4;  // int row stride: 16-byte rows, conflict-free v4 stores
   static constexpr size_t PartBytes = (size_t)kTcRows * LDP * sizeof(int);
   static constexpr size_t SumBytes = (size_t)4 * 16 * LDP * sizeof(int);
-  static constexpr size_t Smem = Ring > PartBytes + SumBytes ? Ring : PartBytes + SumBytes;
+  // + 1 KB to align the ring to the 1024-byte swizzle atoms
+  static constexpr size_t Smem = (Ring > PartBytes + SumBytes ? Ring : PartBytes + SumBytes) + 1024;
   static_assert(Smem <= 227 * 1024 - 2048, "tcgen05 GEMM shared memory");
+  static_assert(Stages >= 2 && (Chunk & 3) == 0, "tcgen05 GEMM ring");
   // kind::i8 instruction descriptor: s32 accumulator, signed A and B, both
   // K-major, N, M = 128.
   static constexpr uint32_t Idesc = (2u << 4) | (1u << 7) | (1u << 10) |
@@ -2318,9 +2380,10 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
-  // start address, LBO 128 B, SBO 256 B (16-byte units), descriptor version 1
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(128 >> 4) << 16) |
-         ((uint64_t)(256 >> 4) << 32) | (1ull << 46);
+  // start address, LBO 1 (unused by swizzled K-major), SBO 1024 B (16-byte
+  // units), descriptor version 1, layout 128-byte swizzle
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         (1ull << 46) | (2ull << 61);
 }
 __device__ __forceinline__ void umma_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
                                         uint32_t acc) {
@@ -2375,23 +2438,26 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
   using C = TcCfg<G>;
   constexpr int GC = kTcGroupCols;
   constexpr int N = C::N, LDP = C::LDP;
-  extern __shared__ __align__(128) uint8_t tc_smem[];
+  extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
+  // the swizzle atoms need 1024-byte alignment (the allocation has 1 KB slack)
+  uint8_t* tc_smem = tc_smem_raw + ((1024u - (smem_addr(tc_smem_raw) & 1023u)) & 1023u);
   uint8_t* smA = tc_smem;
-  uint8_t* smB = tc_smem + (size_t)kTcStages * C::Chunk * kTcAStep;
+  uint8_t* smB = tc_smem + (size_t)C::Stages * C::Chunk * kTcAStep;
   // reused after the main loop: partial tile, then per-warp stripe sums
   int* part = reinterpret_cast<int*>(tc_smem);
   int* sums = reinterpret_cast<int*>(tc_smem + C::PartBytes);
-  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], done;
+  __shared__ __align__(8) uint64_t full[kTcMaxStages], empty[kTcMaxStages], done;
   __shared__ uint32_t tmem_base;
   __shared__ int sm_exp[kMaxTokens], s_issued, s_consumed, s_fail;
   __shared__ unsigned long long sm_keys[kMaxTokens];
+  __shared__ int2 sm_tok[EPI == EPI_QKV ? kMaxTokens : 1];  // (position, KV page) per token
   MC_TRACE_T0
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // the k-split CTAs of a tile form one cluster (grid y = cluster y)
   const int tile = blockIdx.x, nsplit = gridDim.y, split = blockIdx.y;
-  const int KB = a.KB;
-  const int k0 = (int)((long long)KB * split / nsplit), k1 = (int)((long long)KB * (split + 1) / nsplit);
-  const int nk = k1 - k0;
+  const int KA = tc_atoms(a.KB);  // K atoms (4 k-steps each; padding is zero weights)
+  const int a0 = (int)((long long)KA * split / nsplit), a1 = (int)((long long)KA * (split + 1) / nsplit);
+  const int nk = 4 * (a1 - a0);  // k-steps of this split
   const int n_chunks = (nk + C::Chunk - 1) / C::Chunk;
 
   if (warp == 0) {
@@ -2402,7 +2468,7 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < C::Stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -2415,12 +2481,12 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = tmem_base;
-  const uint8_t* wsrc = reinterpret_cast<const uint8_t*>(a.wtc) + ((size_t)tile * KB + k0) * kTcAStep;
-  const uint8_t* xsrc = a.x + (size_t)k0 * C::BStep;
+  const uint8_t* wsrc = reinterpret_cast<const uint8_t*>(a.wtc) + ((size_t)tile * KA + a0) * C::AtomA;
+  const uint8_t* xsrc = a.x + (size_t)a0 * C::AtomB;
   // The weights never depend on the producer grid: the first ring stages'
   // weight copies go out before the dependency wait (their activation
   // copies, after it, complete the same transaction counts).
-  const int pre = min(n_chunks, kTcStages);
+  const int pre = min(n_chunks, C::Stages);
   if (threadIdx.x == 0)
     for (int i = 0; i < pre; ++i) {
       const int steps = min(C::Chunk, nk - i * C::Chunk);
@@ -2430,15 +2496,25 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
     }
   grid_wait();
   MC_TRACE_WAITED(a.trace_slot);
+  MC_TRACE_PHASE(a.trace_slot, 0, mc_tp);
   if (threadIdx.x < a.M) sm_exp[threadIdx.x] = __ldcg(a.xexp + threadIdx.x);
+  if constexpr (EPI == EPI_QKV) {
+    // warps 2-3 resolve positions and pages while the pipeline runs
+    const int m = (int)threadIdx.x - 64;
+    if (m >= 0 && m < a.M) {
+      const int mt = a.m0 + m, z = seq_of(a.seq, mt);
+      const int pos = a.pos_ptr[z * a.seq.pos_stride] + a.pos_add + seq_off(a.seq, mt);
+      sm_tok[m] = make_int2(pos, a.page_table[z * a.seq.pt_stride + pos / a.page]);
+    }
+  }
 
   if (threadIdx.x == 0) {  // producer
     int i = 0;
     for (; i < n_chunks; ++i) {
-      const int s = i % kTcStages;
+      const int s = i % C::Stages;
       const int steps = min(C::Chunk, nk - i * C::Chunk);
       if (i >= pre) {
-        if (!mbar_wait(&empty[s], ((i / kTcStages) - 1) & 1)) {
+        if (!mbar_wait(&empty[s], ((i / C::Stages) - 1) & 1)) {
           s_fail = 1;
           break;
         }
@@ -2450,21 +2526,26 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
                 (uint32_t)steps * C::BStep, &full[s]);
     }
     s_issued = i;
+    MC_TRACE_PHASE(a.trace_slot, 1, mc_tp);
   } else if (threadIdx.x == 32) {  // MMA issuer
     int i = 0;
     for (; i < n_chunks; ++i) {
-      const int s = i % kTcStages;
-      if (!mbar_wait(&full[s], (i / kTcStages) & 1)) {
+      const int s = i % C::Stages;
+      if (!mbar_wait(&full[s], (i / C::Stages) & 1)) {
         s_fail = 1;
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int steps = min(C::Chunk, nk - i * C::Chunk);
-      const uint32_t a0 = smem_addr(smA + (size_t)s * C::Chunk * kTcAStep);
-      const uint32_t b0 = smem_addr(smB + (size_t)s * C::Chunk * C::BStep);
-      for (int j = 0; j < steps; ++j)
-        umma_i8(tmem, umma_desc(a0 + j * kTcAStep), umma_desc(b0 + j * C::BStep), C::Idesc,
-                (i > 0 || j > 0) ? 1u : 0u);
+      const uint32_t sa = smem_addr(smA + (size_t)s * C::Chunk * kTcAStep);
+      const uint32_t sb = smem_addr(smB + (size_t)s * C::Chunk * C::BStep);
+      // k-step j: atom j / 4, 32 (j % 4) bytes into its 128-byte rows
+      for (int j = 0; j < steps; ++j) {
+        const int kidx = i * C::Chunk + j;
+        umma_i8(tmem + (uint32_t)((kidx % C::NAcc) * N), umma_desc(sa + (j >> 2) * C::AtomA + (j & 3) * 32),
+                umma_desc(sb + (j >> 2) * C::AtomB + (j & 3) * 32), C::Idesc,
+                kidx >= C::NAcc ? 1u : 0u);
+      }
       umma_commit(&empty[s]);
     }
     s_consumed = i;
@@ -2475,8 +2556,9 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
   // issued but never consumed); the verdict is block-uniform, as the
   // .aligned tensor-memory loads below require
   if (threadIdx.x == 0) {
-    for (int i = s_consumed; i < s_issued; ++i) mbar_wait(&full[i % kTcStages], (i / kTcStages) & 1);
+    for (int i = s_consumed; i < s_issued; ++i) mbar_wait(&full[i % C::Stages], (i / C::Stages) & 1);
     if (!mbar_wait(&done, 0)) s_fail = 1;
+    MC_TRACE_PHASE(a.trace_slot, 2, mc_tp);
   }
   __syncthreads();
   const bool ok = !s_fail;
@@ -2489,11 +2571,20 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
     int* prow = part + (size_t)(warp * 32 + lane) * LDP;
     const bool have = ok && nk > 0;  // block-uniform
 #pragma unroll 1
-    for (int c = 0; c < N; c += GC) {  // one token group (three loads) per wait
+    for (int c = 0; c < N; c += GC) {  // one token group per wait, summed over accumulators
       uint32_t v[GC];
       if (have) {
 #pragma unroll
         for (int j = 0; j < GC; j += 16) tmem_ld16(taddr + c + j, v + j);
+#pragma unroll 1
+        for (int q = 1; q < C::NAcc; ++q) {  // nk >= 4 >= NAcc: every accumulator written
+          uint32_t u[GC];
+#pragma unroll
+          for (int j = 0; j < GC; j += 16) tmem_ld16(taddr + (uint32_t)(q * N) + c + j, u + j);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int j = 0; j < GC; ++j) v[j] += u[j];
+        }
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
       } else {
 #pragma unroll
@@ -2507,6 +2598,7 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
   }
   // 2) every partial tile of the cluster is staged
   if (nsplit > 1) cluster_sync_all(); else __syncthreads();
+  MC_TRACE_PHASE(a.trace_slot, 3, mc_tp);
   // 3) this CTA finishes stripes rank, rank + nsplit, ... of the tile: the
   //    exact int32 sum of the cluster's partial rows (read through
   //    distributed shared memory), then the stripe epilogue of each group
@@ -2554,7 +2646,7 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
 #pragma unroll
         for (int i = 0; i < (8 * kGroupTokens) / 32; ++i) kmax[i] = 0ull;
         gemv_epilogue<6, EPI>(a, stripe, wsum + g * GC, LDP, lane, kmax, a.scale, sm_exp + gm0,
-                              a.m0 + gm0, MG);
+                              a.m0 + gm0, MG, EPI == EPI_QKV ? sm_tok + gm0 : nullptr);
         if constexpr (EPI == EPI_LMHEAD) {
 #pragma unroll
           for (int it = 0; it < (8 * kGroupTokens) / 32; ++it) {
@@ -2572,9 +2664,11 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
     }
     __syncwarp();
   }
+  MC_TRACE_PHASE(a.trace_slot, 4, mc_tp);
   grid_launch_dependents();
   // 4) no CTA leaves while a peer may still read its partial tile
   if (nsplit > 1) cluster_sync_all(); else __syncthreads();
+  MC_TRACE_PHASE(a.trace_slot, 5, mc_tp);
   if constexpr (EPI == EPI_LMHEAD) {
     if (threadIdx.x < a.M && sm_keys[threadIdx.x])
       atomicMax(a.keys + key_slot(a.seq, a.m0 + threadIdx.x), sm_keys[threadIdx.x]);
@@ -2589,24 +2683,27 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
   MC_TRACE_END(a.trace_slot);
 }
 
-// One 16-byte row segment per thread: (tile, k-step, row group, K half, row).
+// One 16-byte chunk per thread of the swizzled weight copy: (tile, atom,
+// row r, stored chunk p) holds K bytes 16 (p ^ (r % 8)) .. + 16 of the atom;
+// columns past the map (K padding) and padding rows are zero.
 __global__ void k_pack_tc(const int8_t* __restrict__ src, long long src_ld,
                           const int* __restrict__ row_map, const int* __restrict__ col_map,
-                          int n_rows, int n_tiles, int KB, int4* __restrict__ dst) {
+                          int n_cols, int n_rows, int n_tiles, int KA, int4* __restrict__ dst) {
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const long long total = (long long)n_tiles * KB * (kTcAStep / 16);
+  const long long total = (long long)n_tiles * KA * (kTcRows * 8);
   if (gid >= total) return;
-  const int seg = (int)(gid % (kTcAStep / 16));  // g * 16 + h * 8 + r
-  const long long tk = gid / (kTcAStep / 16);
-  const int kb = (int)(tk % KB), t = (int)(tk / KB);
-  const int g = seg >> 4, h = (seg >> 3) & 1, r = seg & 7;
-  const int prow = t * kTcRows + g * 8 + r;
+  const int seg = (int)(gid % (kTcRows * 8));
+  const long long ta = gid / (kTcRows * 8);
+  const int atom = (int)(ta % KA), t = (int)(ta / KA);
+  const int r = seg >> 3, lc = (seg & 7) ^ (r & 7);
+  const int prow = t * kTcRows + r;
   const int row = prow < n_rows ? row_map[prow] : -1;
   uint32_t w[4] = {0, 0, 0, 0};
   if (row >= 0)
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      const int c = col_map[kb * 32 + h * 16 + j];
+      const int k = atom * 128 + lc * 16 + j;
+      const int c = k < n_cols ? col_map[k] : -1;
       const uint32_t b = c >= 0 ? (uint8_t)src[(long long)row * src_ld + c] : 0u;
       w[j >> 2] |= b << (8 * (j & 3));
     }
@@ -2616,9 +2713,10 @@ __global__ void k_pack_tc(const int8_t* __restrict__ src, long long src_ld,
 cudaError_t launch_pack_tc(const int8_t* src, long long src_ld, const int* row_map,
                            const int* col_map, int n_rows, int n_tiles, int KB, int4* dst,
                            cudaStream_t s) {
-  const long long total = (long long)n_tiles * KB * (kTcAStep / 16);
-  k_pack_tc<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(src, src_ld, row_map, col_map, n_rows,
-                                                             n_tiles, KB, dst);
+  const int KA = tc_atoms(KB);
+  const long long total = (long long)n_tiles * KA * (kTcRows * 8);
+  k_pack_tc<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(src, src_ld, row_map, col_map, KB * 32,
+                                                             n_rows, n_tiles, KA, dst);
   return cudaGetLastError();
 }
 
