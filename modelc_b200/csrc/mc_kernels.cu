@@ -528,20 +528,42 @@ constexpr int kGemvWarps = 8;
 // ahead for the QKV epilogue.  A lane's rows are the same in every
 // iteration, so all its global loads (row scales, next-norm weights, then per
 // iteration the residual rows or the RoPE factors) are issued before the
-// arithmetic.
+// arithmetic -- or read from `pre`, the same values staged in shared memory
+// while the tile's main loop ran.
+struct EpiPre {
+  int row0;            // first row of the staged tile
+  const float* scale;  // [128] row scales
+  const float* w;      // [128] next RMSNorm weights (RESID)
+  const float* h;      // [tokens][128] residual rows (RESID), token index from m0 of the launch
+  const float* cs;     // [tokens][64] RoPE cos of (stripe, pair row) (QKV)
+  const float* sn;
+};
+
 template <int NT, int EPI, typename T>
 __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, const T* tile,
                                               int ld, int lane, unsigned long long* kmax,
                                               const float* scale, const int* xexp, int m0,
-                                              int MG, const int2* tok = nullptr) {
+                                              int MG, const int2* tok = nullptr,
+                                              const EpiPre* pre = nullptr) {
   constexpr int NIT = (8 * kGroupTokens) / 32;
   const int r = lane & 7;
   const int prow = stripe * 16 + r;
+  const int lrow = pre ? prow - pre->row0 : 0;  // row within the staged tile
   // q4_0 tiles carry their block scales already; int8 tiles take the row scale
-  const float sc0 = scale ? scale[prow] : 1.0f, sc1 = scale ? scale[prow + 8] : 1.0f;
+  float sc0 = 1.0f, sc1 = 1.0f;
+  if (pre) {
+    sc0 = pre->scale[lrow];
+    sc1 = pre->scale[lrow + 8];
+  } else if (scale) {
+    sc0 = scale[prow];
+    sc1 = scale[prow + 8];
+  }
   float w0 = 1.0f, w1 = 1.0f;  // next RMSNorm weight of the rows (RESID statistics)
   if constexpr (EPI == EPI_RESID) {
-    if (a.st_w) {
+    if (pre) {
+      w0 = pre->w[lrow];
+      w1 = pre->w[lrow + 8];
+    } else if (a.st_w) {
       if (prow < a.n_out) w0 = a.st_w[prow];
       if (prow + 8 < a.n_out) w1 = a.st_w[prow + 8];
     }
@@ -565,9 +587,15 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
     if (it * 32 >= 8 * MG || m >= MG) continue;
     const int mt = m0 + m;
     if constexpr (EPI == EPI_RESID) {
-      const float* o = a.out + (size_t)mt * a.ldo;
-      if (prow < a.n_out) p0[it] = o[prow];
-      if (prow + 8 < a.n_out) p1[it] = o[prow + 8];
+      if (pre) {
+        const float* hr = pre->h + (size_t)(mt - a.m0) * kTcTileRows;
+        p0[it] = hr[lrow];
+        p1[it] = hr[lrow + 8];
+      } else {
+        const float* o = a.out + (size_t)mt * a.ldo;
+        if (prow < a.n_out) p0[it] = o[prow];
+        if (prow + 8 < a.n_out) p1[it] = o[prow + 8];
+      }
     } else if constexpr (EPI == EPI_QKV) {
       int pos, pg;
       if (tok) {
@@ -581,8 +609,14 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
       ppos[it] = pos;
       ppg[it] = pg;
       if (rope) {
-        p0[it] = a.rope_cos[(size_t)pos * a.half_p + ri];
-        p1[it] = a.rope_sin[(size_t)pos * a.half_p + ri];
+        if (pre) {
+          const int q = (stripe * 8 + r) - pre->row0 / 2;  // (stripe, pair row) in the tile
+          p0[it] = pre->cs[(size_t)(mt - a.m0) * 64 + q];
+          p1[it] = pre->sn[(size_t)(mt - a.m0) * 64 + q];
+        } else {
+          p0[it] = a.rope_cos[(size_t)pos * a.half_p + ri];
+          p1[it] = a.rope_sin[(size_t)pos * a.half_p + ri];
+        }
       }
     }
   }
@@ -2333,13 +2367,13 @@ struct TcCfg {
   static constexpr int NAcc = G <= 2 ? 4 : (G == 3 ? 3 : 2);
   static constexpr uint32_t TmemCols = G == 1 ? 256 : 512;  // power of 2 >= NAcc * N
   static constexpr size_t Ring = (size_t)Stages * StageBytes;
-  // after the main loop the ring holds this CTA's partial tile [128][N + 4]
-  // (read by the cluster's peers) and per-warp stripe sums [4][16][N + 4]
+  // after the main loop the ring receives, from every CTA of the cluster,
+  // the partial rows of the stripes this CTA finishes: [source][owned rows]
+  // [N + 4] ints, at most 7 sources x 2 stripes x 16 rows
   static constexpr int LDP = N + 4;  // int row stride: 16-byte rows, conflict-free v4 stores
-  static constexpr size_t PartBytes = (size_t)kTcRows * LDP * sizeof(int);
-  static constexpr size_t SumBytes = (size_t)4 * 16 * LDP * sizeof(int);
+  static constexpr size_t RecvBytes = (size_t)224 * LDP * sizeof(int);
   // + 1 KB to align the ring to the 1024-byte swizzle atoms
-  static constexpr size_t Smem = (Ring > PartBytes + SumBytes ? Ring : PartBytes + SumBytes) + 1024;
+  static constexpr size_t Smem = (Ring > RecvBytes ? Ring : RecvBytes) + 1024;
   static_assert(Smem <= 227 * 1024 - 2048, "tcgen05 GEMM shared memory");
   static_assert(Stages >= 2 && (Chunk & 3) == 0, "tcgen05 GEMM ring");
   // kind::i8 instruction descriptor: s32 accumulator, signed A and B, both
@@ -2415,6 +2449,11 @@ __device__ __forceinline__ uint32_t peer_addr(uint32_t saddr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
+__device__ __forceinline__ void st_peer_v4(uint32_t addr, int4 v) {
+  asm volatile("st.shared::cluster.v4.s32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
 __device__ __forceinline__ int4 ld_peer_v4(uint32_t addr) {
   int4 v;
   asm volatile("ld.shared::cluster.v4.s32 {%0, %1, %2, %3}, [%4];"
@@ -2443,14 +2482,19 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
   uint8_t* tc_smem = tc_smem_raw + ((1024u - (smem_addr(tc_smem_raw) & 1023u)) & 1023u);
   uint8_t* smA = tc_smem;
   uint8_t* smB = tc_smem + (size_t)C::Stages * C::Chunk * kTcAStep;
-  // reused after the main loop: partial tile, then per-warp stripe sums
-  int* part = reinterpret_cast<int*>(tc_smem);
-  int* sums = reinterpret_cast<int*>(tc_smem + C::PartBytes);
+  // reused after the main loop: the receive buffer of the partial rows
+  int* recv = reinterpret_cast<int*>(tc_smem);
   __shared__ __align__(8) uint64_t full[kTcMaxStages], empty[kTcMaxStages], done;
   __shared__ uint32_t tmem_base;
   __shared__ int sm_exp[kMaxTokens], s_issued, s_consumed, s_fail;
   __shared__ unsigned long long sm_keys[kMaxTokens];
   __shared__ int2 sm_tok[EPI == EPI_QKV ? kMaxTokens : 1];  // (position, KV page) per token
+  // epilogue inputs staged during the main loop (EpiPre)
+  __shared__ float sm_scl[kTcRows];
+  __shared__ float sm_w[EPI == EPI_RESID ? kTcRows : 1];
+  __shared__ __align__(16) float sm_h[EPI == EPI_RESID ? kMaxTokens * kTcRows : 1];
+  __shared__ float sm_cs[EPI == EPI_QKV ? kMaxTokens * 64 : 1];
+  __shared__ float sm_sn[EPI == EPI_QKV ? kMaxTokens * 64 : 1];
   MC_TRACE_T0
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // the k-split CTAs of a tile form one cluster (grid y = cluster y)
@@ -2498,13 +2542,57 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
   MC_TRACE_WAITED(a.trace_slot);
   MC_TRACE_PHASE(a.trace_slot, 0, mc_tp);
   if (threadIdx.x < a.M) sm_exp[threadIdx.x] = __ldcg(a.xexp + threadIdx.x);
-  if constexpr (EPI == EPI_QKV) {
-    // warps 2-3 resolve positions and pages while the pipeline runs
-    const int m = (int)threadIdx.x - 64;
-    if (m >= 0 && m < a.M) {
-      const int mt = a.m0 + m, z = seq_of(a.seq, mt);
-      const int pos = a.pos_ptr[z * a.seq.pos_stride] + a.pos_add + seq_off(a.seq, mt);
-      sm_tok[m] = make_int2(pos, a.page_table[z * a.seq.pt_stride + pos / a.page]);
+  // warps 2-3 stage everything the epilogue reads while the pipeline runs:
+  // row scales, next-norm weights and residual rows of the tile (RESID), the
+  // tokens' positions, pages and RoPE factors (QKV)
+  const int row0 = tile * kTcRows;
+  if (threadIdx.x >= 64) {
+    const int t = (int)threadIdx.x - 64;
+    if constexpr (EPI == EPI_QKV) {
+      if (t < a.M) {
+        const int mt = a.m0 + t, z = seq_of(a.seq, mt);
+        const int pos = a.pos_ptr[z * a.seq.pos_stride] + a.pos_add + seq_off(a.seq, mt);
+        sm_tok[t] = make_int2(pos, a.page_table[z * a.seq.pt_stride + pos / a.page]);
+      }
+      asm volatile("bar.sync 1, 64;" ::: "memory");  // warps 2-3: token table ready
+      const int per_head = a.half_p >> 3;
+      for (int i = t; i < a.M * 64; i += 64) {
+        const int m = i >> 6, q = i & 63;
+        const int gs = tile * 8 + (q >> 3), rr = q & 7;
+        float c = 1.0f, sn = 0.0f;
+        if (gs < a.n_stripes && gs < a.sq + a.sk && per_head > 0) {
+          const int s2 = gs < a.sq ? gs : gs - a.sq;
+          const int hh = s2 / per_head;
+          const int ri = (s2 - hh * per_head) * 8 + rr;
+          const size_t at = (size_t)sm_tok[m].x * a.half_p + ri;
+          c = a.rope_cos[at];
+          sn = a.rope_sin[at];
+        }
+        sm_cs[i] = c;
+        sm_sn[i] = sn;
+      }
+    }
+    for (int r = t; r < kTcRows; r += 64) {
+      const int gr = row0 + r;
+      sm_scl[r] = gr < a.n_stripes * 16 ? a.scale[gr] : 0.0f;
+      if constexpr (EPI == EPI_RESID) sm_w[r] = (a.st_w && gr < a.n_out) ? a.st_w[gr] : 1.0f;
+    }
+    if constexpr (EPI == EPI_RESID) {
+      // residual rows: 16-byte loads where the token's row segment allows
+      const bool vec = ((a.ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.out) & 15) == 0) &&
+                       row0 + kTcRows <= a.n_out;
+      if (vec) {
+        for (int i = t; i < a.M * (kTcRows / 4); i += 64) {
+          const int m = i / (kTcRows / 4), c4 = i - m * (kTcRows / 4);
+          reinterpret_cast<float4*>(sm_h)[i] = *reinterpret_cast<const float4*>(
+              a.out + (size_t)(a.m0 + m) * a.ldo + row0 + 4 * c4);
+        }
+      } else {
+        for (int i = t; i < a.M * kTcRows; i += 64) {
+          const int m = i / kTcRows, gr = row0 + (i - m * kTcRows);
+          sm_h[i] = gr < a.n_out ? a.out[(size_t)(a.m0 + m) * a.ldo + gr] : 0.0f;
+        }
+      }
     }
   }
 
@@ -2564,11 +2652,21 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
   const bool ok = !s_fail;
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   if (!ok && threadIdx.x == 0 && a.err) atomicExch(a.err, 1);
-  // 1) this CTA's partial tile in the idle ring: thread (warp, lane) holds
-  //    accumulator row 32 * warp + lane (an empty k-range contributes 0)
+  // 1) every CTA of the cluster is past its main loop: the rings are idle
+  if (nsplit > 1) cluster_sync_all(); else __syncthreads();
+  MC_TRACE_PHASE(a.trace_slot, 3, mc_tp);
+  // 2) push: thread (warp, lane) holds accumulator row R = 32 * warp + lane of
+  //    stripe R / 16, which CTA (R / 16) % nsplit finishes; the row goes to
+  //    slot `rank` of that CTA's receive buffer (remote stores do not stall;
+  //    an empty k-range contributes 0)
+  const int rank = nsplit > 1 ? (int)cluster_rank() : 0;
   {
     const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-    int* prow = part + (size_t)(warp * 32 + lane) * LDP;
+    const int R = warp * 32 + lane, s = R >> 4;
+    const int owner = s % nsplit, li = s / nsplit;
+    const int owned = (8 - owner + nsplit - 1) / nsplit;  // stripes the owner finishes
+    const int drow = (rank * owned + li) * 16 + (R & 15);
+    const uint32_t dst = smem_addr(recv + (size_t)drow * LDP);
     const bool have = ok && nk > 0;  // block-uniform
 #pragma unroll 1
     for (int c = 0; c < N; c += GC) {  // one token group per wait, summed over accumulators
@@ -2590,53 +2688,49 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
 #pragma unroll
         for (int j = 0; j < GC; ++j) v[j] = 0u;
       }
+      if (nsplit > 1) {
 #pragma unroll
-      for (int j = 0; j < GC; j += 4)
-        *reinterpret_cast<int4*>(prow + c + j) =
-            make_int4((int)v[j], (int)v[j + 1], (int)v[j + 2], (int)v[j + 3]);
+        for (int j = 0; j < GC; j += 4)
+          st_peer_v4(peer_addr(dst + (uint32_t)(c + j) * 4u, (uint32_t)owner),
+                     make_int4((int)v[j], (int)v[j + 1], (int)v[j + 2], (int)v[j + 3]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < GC; j += 4)
+          *reinterpret_cast<int4*>(recv + (size_t)drow * LDP + c + j) =
+              make_int4((int)v[j], (int)v[j + 1], (int)v[j + 2], (int)v[j + 3]);
+      }
     }
   }
-  // 2) every partial tile of the cluster is staged
+  MC_TRACE_PHASE(a.trace_slot, 4, mc_tp);
+  // 3) every push has landed
   if (nsplit > 1) cluster_sync_all(); else __syncthreads();
-  MC_TRACE_PHASE(a.trace_slot, 3, mc_tp);
-  // 3) this CTA finishes stripes rank, rank + nsplit, ... of the tile: the
-  //    exact int32 sum of the cluster's partial rows (read through
-  //    distributed shared memory), then the stripe epilogue of each group
+  MC_TRACE_PHASE(a.trace_slot, 5, mc_tp);
+  // 4) this CTA finishes stripes rank, rank + nsplit, ...: the exact int32
+  //    sum of the sources' rows (local shared memory) into slot 0, then the
+  //    stripe epilogue of each token group
   unsigned long long kmax[(8 * kGroupTokens) / 32];
-  const int rank = nsplit > 1 ? (int)cluster_rank() : 0;
-  int* wsum = sums + (size_t)warp * 16 * LDP;
+  const int owned = (8 - rank + nsplit - 1) / nsplit;
   constexpr int V4 = N / 4;  // 16-byte units per row
-  for (int j = warp; ; j += 4) {
+  for (int j = warp; j < owned; j += 4) {
     const int st_local = rank + j * nsplit;  // stripe within the tile
-    if (st_local >= 8) break;                // warp-uniform
     const int stripe = tile * 8 + st_local;
-    if (stripe >= a.n_stripes) break;
-    const int* prows = part + (size_t)st_local * 16 * LDP;
-    const uint32_t base = smem_addr(prows);
-    for (int i = lane; i < 16 * V4; i += 32) {
-      const int r = i / V4, c4 = i - r * V4;
-      const int off = r * LDP + c4 * 4;
-      int4 acc;
-      if (nsplit > 1) {
-        // every peer's load in flight before the first add
-        int4 v[kTcMaxSplit];
-#pragma unroll
-        for (int q = 0; q < kTcMaxSplit; ++q)
-          if (q < nsplit) v[q] = ld_peer_v4(peer_addr(base + (uint32_t)off * 4u, (uint32_t)q));
-        acc = v[0];
-#pragma unroll
-        for (int q = 1; q < kTcMaxSplit; ++q)
-          if (q < nsplit) {
-            acc.x += v[q].x;
-            acc.y += v[q].y;
-            acc.z += v[q].z;
-            acc.w += v[q].w;
-          }
-      } else {
-        acc = *reinterpret_cast<const int4*>(prows + off);
+    if (stripe >= a.n_stripes) break;  // warp-uniform
+    int* rows0 = recv + (size_t)(j * 16) * LDP;  // slot 0 rows of this stripe
+    if (nsplit > 1)
+      for (int i = lane; i < 16 * V4; i += 32) {
+        const int r = i / V4, c4 = i - r * V4;
+        const size_t off = (size_t)r * LDP + c4 * 4;
+        int4 acc = *reinterpret_cast<const int4*>(rows0 + off);
+        for (int q = 1; q < nsplit; ++q) {
+          const int4 v = *reinterpret_cast<const int4*>(recv + (size_t)((q * owned + j) * 16) * LDP + off);
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
+        }
+        *reinterpret_cast<int4*>(rows0 + off) = acc;
       }
-      *reinterpret_cast<int4*>(wsum + off) = acc;
-    }
+    int* wsum = rows0;
     __syncwarp();
     if (ok) {
       for (int g = 0; g < G; ++g) {
@@ -2645,8 +2739,9 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
         const int MG = min(kGroupTokens, a.M - gm0);
 #pragma unroll
         for (int i = 0; i < (8 * kGroupTokens) / 32; ++i) kmax[i] = 0ull;
+        const EpiPre pre{row0, sm_scl, sm_w, sm_h, sm_cs, sm_sn};
         gemv_epilogue<6, EPI>(a, stripe, wsum + g * GC, LDP, lane, kmax, a.scale, sm_exp + gm0,
-                              a.m0 + gm0, MG, EPI == EPI_QKV ? sm_tok + gm0 : nullptr);
+                              a.m0 + gm0, MG, EPI == EPI_QKV ? sm_tok + gm0 : nullptr, &pre);
         if constexpr (EPI == EPI_LMHEAD) {
 #pragma unroll
           for (int it = 0; it < (8 * kGroupTokens) / 32; ++it) {
@@ -2664,11 +2759,10 @@ __global__ void __launch_bounds__(128, 1) k_gemm_tc(GemvArgs a) {
     }
     __syncwarp();
   }
-  MC_TRACE_PHASE(a.trace_slot, 4, mc_tp);
+  MC_TRACE_PHASE(a.trace_slot, 6, mc_tp);
   grid_launch_dependents();
-  // 4) no CTA leaves while a peer may still read its partial tile
-  if (nsplit > 1) cluster_sync_all(); else __syncthreads();
-  MC_TRACE_PHASE(a.trace_slot, 5, mc_tp);
+  __syncthreads();
+  MC_TRACE_PHASE(a.trace_slot, 7, mc_tp);
   if constexpr (EPI == EPI_LMHEAD) {
     if (threadIdx.x < a.M && sm_keys[threadIdx.x])
       atomicMax(a.keys + key_slot(a.seq, a.m0 + threadIdx.x), sm_keys[threadIdx.x]);
