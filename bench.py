@@ -445,6 +445,76 @@ def run_profile(args):
     sess.close()
 
 
+def run_timeline(args):
+    """In-situ timeline of one verify forward (MC_TRACE build of the library):
+    per launch the first CTA's start, its release from griddepcontrol.wait and
+    the last CTA's end (%globaltimer), summed per kernel kind; plus per-phase
+    times (thread 0 of each CTA) of the attention and the tcgen05 GEMMs.
+    Single GPU; --config selects the workload (batch included)."""
+    import ctypes as C
+    import torch
+    import modelc_b200 as mb
+    import modelc_b200._lib as L
+    L.use_trace_library()
+    lib = L.lib()
+    wl = workloads()[args.config]
+    torch.cuda.set_device(0)
+    cfg, target, draft, prompt = build_models(0, wl=wl)
+    B = wl.batch
+    prompts = prompt if B > 1 else [prompt]
+    sess = mb.Session(target, draft, gamma=wl.gamma,
+                      max_context=wl.prompt_len + wl.new_tokens + 2 * wl.gamma + 8, n_requests=B)
+    sess.prime_batch(prompts)
+    sess.decode(8)
+    sess.verify_launch(3)
+    torch.cuda.synchronize()
+    names = ["embed"]
+    for _ in range(cfg.n_layers):
+        names += ["quant_attn", "qkv", "attention", "quant_o", "o", "quant_mlp", "gu", "quant_act",
+                  "down"]
+    names += ["quant_final", "head"]
+    n = len(names)
+    for _ in range(3):  # the last of three repetitions
+        L.check(lib.mc_trace_reset())
+        sess.verify_launch(1)
+        torch.cuda.synchronize()
+        buf = (C.c_ulonglong * (19 * n))()
+        L.check(lib.mc_trace_read(buf, n))
+    raw = np.array(buf, dtype=np.float64)
+    a = raw[:3 * n].reshape(n, 3)
+    ph = raw[3 * n:].reshape(n, 16)
+    a = (a - a[0, 0]) / 1e3  # us
+    exe = a[:, 2] - a[:, 1]
+    gap = np.r_[0.0, a[1:, 1] - a[:-1, 2]]
+    print(f"workload: {wl.desc}")
+    print(f"verify forward critical path {a[-1, 2]:.1f} us over {n} launches")
+    print(f"{'kind':12s} {'n':>4s} {'exec avg':>9s} {'gap avg':>8s} {'exec sum':>9s} {'gap sum':>8s}")
+    kinds = {}
+    for i, nm in enumerate(names):
+        k = kinds.setdefault(nm, [0, 0.0, 0.0])
+        k[0] += 1
+        k[1] += exe[i]
+        k[2] += gap[i]
+    for nm, (c, e, g) in kinds.items():
+        print(f"{nm:12s} {c:4d} {e / c:9.2f} {g / c:8.2f} {e:9.1f} {g:8.1f}")
+    gemm_ph = ["launch->wait", "weights issued", "mma done", "cluster: all mma done",
+               "tmem read + push", "pushes landed", "sums + epilogue", "end barrier"]
+    attn_ph = ["launch->wait", "load K/V/q", "scores", "softmax", "PV + partials", "arrive",
+               "combine prep", "combine"]
+    for kind in ["qkv", "o", "gu", "down", "head", "attention"]:
+        idx = [i for i, nm in enumerate(names) if nm == kind]
+        sums, cnts = ph[idx, :8].sum(0), ph[idx, 8:].sum(0)
+        if cnts.sum() == 0:
+            continue
+        labels = attn_ph if kind == "attention" else gemm_ph
+        print(f"{kind} phases (avg us per CTA reaching it; CTAs per launch):")
+        for k in range(8):
+            if cnts[k]:
+                print(f"  {k} {labels[k]:22s} {sums[k] / cnts[k] / 1e3:7.2f}   "
+                      f"{cnts[k] / len(idx):7.1f}")
+    sess.close()
+
+
 def run_sweep(args):
     """Isolated verify-step projection Y = X . dequant(W)^T through the public
     mc_linear_run: X is M x 4096 N(0, 1), W is N x 4096 N(0, 0.02) as per-row
@@ -457,9 +527,9 @@ def run_sweep(args):
     torch.cuda.set_device(0)
     peak, peak_kind = measured_peaks()
     K = 4096
-    ms_list = [1, 5, 8, 16, 40, 64]
-    for fmt in ("i8_row", "q4_0"):
-        for n in (4096, 14336, 128256):
+    ms_list = [args.sweep_m] if args.sweep_m else [1, 5, 8, 16, 40, 64]
+    for fmt in ((args.sweep_fmt,) if args.sweep_fmt else ("i8_row", "q4_0")):
+        for n in ((args.sweep_n,) if args.sweep_n else (4096, 14336, 128256)):
             g = torch.Generator(device="cuda")
             g.manual_seed(n)
             wb = n * K // 32 * 18 if fmt == "q4_0" else n * K + 4 * n
@@ -550,13 +620,21 @@ def main():
                     help="tensor parallelism: NCCL all-reduces instead of the fused NVLink reduction")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: independent requests per GPU instead of tensor parallelism")
+    ap.add_argument("--timeline", action="store_true",
+                    help="in-situ per-kernel timeline of one verify forward (MC_TRACE build)")
     ap.add_argument("--sweep", action="store_true",
                     help="isolated quantized-projection sweep (one JSON line per point)")
+    ap.add_argument("--sweep-fmt", default=None, choices=["i8_row", "q4_0"],
+                    help="--sweep: this weight format only")
+    ap.add_argument("--sweep-n", type=int, default=None, help="--sweep: this N only")
+    ap.add_argument("--sweep-m", type=int, default=None, help="--sweep: this M only")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.sweep:
         run_sweep(args)
+    elif args.timeline:
+        run_timeline(args)
     elif args.profile:
         run_profile(args)
     elif args.impl == "reference":

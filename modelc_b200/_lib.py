@@ -62,15 +62,30 @@ class SpecCfg(C.Structure):
 _lib = None
 
 
+def use_trace_library() -> None:
+    """Load the MC_TRACE build (libmodelc_cuda_trace.so, built on demand)
+    instead of the product library; must precede the first lib() call."""
+    global LIB_PATH
+    if _lib is not None:
+        raise RuntimeError("the CUDA library is already loaded")
+    from . import build as _build
+    LIB_PATH = _build.build(trace=True)
+
+
 def lib():
     """Load the CUDA library (building it first if the sources are newer)."""
     global _lib
     if _lib is not None:
         return _lib
     from . import build as _build
-    if not os.path.exists(LIB_PATH) or _build._stale():
+    if LIB_PATH == _build.LIB and (not os.path.exists(LIB_PATH) or _build._stale()):
         _build.build()
     L = C.CDLL(LIB_PATH)
+    if hasattr(L, "mc_trace_reset"):  # MC_TRACE builds only
+        L.mc_trace_reset.restype = C.c_int32
+        L.mc_trace_reset.argtypes = []
+        L.mc_trace_read.restype = C.c_int32
+        L.mc_trace_read.argtypes = [C.POINTER(C.c_ulonglong), C.c_int32]
     vp, i32, i64, u32p = C.c_void_p, C.c_int32, C.c_int64, C.POINTER(C.c_uint32)
     i32p, fp = C.POINTER(C.c_int32), C.POINTER(C.c_float)
     sig = {
