@@ -1301,6 +1301,105 @@ cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl) {
 // split).
 constexpr int kAttnThreads = 512;
 
+// Last arriver of one (query block, KV head): combine the pages' partials
+// into the output, one warp per row and lanes over pages for the weights
+// (max_chunks <= 64 = 2 per lane).  Page c contributes
+// e^(m_c - M) * (sum_t e^(s_t - m_c) v_t) to the numerator and
+// e^(m_c - M) * l_c to the denominator; fully masked pages (m_c = -inf)
+// contribute exactly zero.  Then thread -> 4 columns of one row, pages summed
+// in order with eight float4 loads in flight; Rp (>= R) is a multiple of the
+// rows a warp spans, so the row loop and the shuffles stay warp-uniform.
+// wgt: shared [R][n_chunks]; s_l: shared [>= R]; s_mx: shared [>= Mq].
+__device__ __forceinline__ void attn_combine(const AttnArgs& a, int kvh, int cslot, int n_chunks,
+                                             int R, int Rp, int Rs, int G, int mt0, int Mq,
+                                             float* wgt, float* s_l, uint32_t* s_mx) {
+  const int hdp = a.hdp;
+  const int nthr = blockDim.x;
+  {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float2* ml = reinterpret_cast<const float2*>(a.part_ml) + (size_t)cslot * a.max_chunks * Rs;
+    for (int row = warp; row < R; row += nthr / 32) {
+      float2 v0 = make_float2(-INFINITY, 0.0f), v1 = make_float2(-INFINITY, 0.0f);
+      if (lane < n_chunks) v0 = __ldcg(ml + (size_t)lane * Rs + row);
+      if (lane + 32 < n_chunks) v1 = __ldcg(ml + (size_t)(lane + 32) * Rs + row);
+      float M_ = fmaxf(v0.x, v1.x);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) M_ = fmaxf(M_, __shfl_xor_sync(0xffffffffu, M_, o));
+      const float w0 = (v0.x == -INFINITY) ? 0.0f : expf(v0.x - M_);
+      const float w1 = (v1.x == -INFINITY) ? 0.0f : expf(v1.x - M_);
+      if (lane < n_chunks) wgt[row * n_chunks + lane] = w0;
+      if (lane + 32 < n_chunks) wgt[row * n_chunks + lane + 32] = w1;
+      float l = __fadd_rn(__fmul_rn(w0, v0.y), __fmul_rn(w1, v1.y));
+#pragma unroll
+      for (int o = 16; o; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
+      if (lane == 0) s_l[row] = l;
+    }
+  }
+  for (int i = threadIdx.x; i < Mq; i += nthr) s_mx[i] = 0u;
+  __syncthreads();
+  {
+    const int h4 = hdp >> 2;
+    const int RGc = nthr / h4;
+    const int c4 = threadIdx.x % h4;
+    const int seg = min(h4, 32);  // lanes of a warp that share a row
+    const float4* base =
+        reinterpret_cast<const float4*>(a.part_o) + (size_t)cslot * a.max_chunks * Rs * h4 + c4;
+    const size_t cs4 = (size_t)Rs * h4;
+    for (int row = threadIdx.x / h4; row < Rp; row += RGc) {
+      const bool live = row < R;
+      const int rr = live ? row : R - 1;
+      const float* wr = wgt + rr * n_chunks;
+      const float4* src = base + (size_t)rr * h4;
+      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      int ch = 0;
+      for (; ch + 8 <= n_chunks; ch += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = __ldcg(src + (size_t)(ch + u) * cs4);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float w = wr[ch + u];
+          acc.x = __fmaf_rn(v[u].x, w, acc.x);
+          acc.y = __fmaf_rn(v[u].y, w, acc.y);
+          acc.z = __fmaf_rn(v[u].z, w, acc.z);
+          acc.w = __fmaf_rn(v[u].w, w, acc.w);
+        }
+      }
+      for (; ch < n_chunks; ++ch) {
+        const float4 v = __ldcg(src + (size_t)ch * cs4);
+        const float w = wr[ch];
+        acc.x = __fmaf_rn(v.x, w, acc.x);
+        acc.y = __fmaf_rn(v.y, w, acc.y);
+        acc.z = __fmaf_rn(v.z, w, acc.z);
+        acc.w = __fmaf_rn(v.w, w, acc.w);
+      }
+      uint32_t bits = 0u;
+      if (live) {
+        const float l = s_l[row];
+        float4 o;
+        o.x = __fdiv_rn(acc.x, l);
+        o.y = __fdiv_rn(acc.y, l);
+        o.z = __fdiv_rn(acc.z, l);
+        o.w = __fdiv_rn(acc.w, l);
+        const int m = row / G, gi = row - m * G;
+        reinterpret_cast<float4*>(a.out + ((size_t)(mt0 + m) * a.H + kvh * G + gi) * hdp)[c4] = o;
+        bits = max(max(__float_as_uint(fabsf(o.x)), __float_as_uint(fabsf(o.y))),
+                   max(__float_as_uint(fabsf(o.z)), __float_as_uint(fabsf(o.w))));
+      }
+      if (a.st_amax) {
+        for (int off = 1; off < seg; off <<= 1)
+          bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, off));
+        if (live && (threadIdx.x % seg) == 0) atomicMax(s_mx + row / G, bits);
+      }
+    }
+  }
+  if (a.st_amax) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < Mq; i += nthr) atomicMax(a.st_amax + mt0 + i, s_mx[i]);
+  }
+  if (threadIdx.x == 0) atomicExch(a.cnt + cslot, 0);
+}
+
 // 16-byte global -> shared copy that holds no registers (L2 only, as __ldcg).
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
@@ -1496,102 +1595,288 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) k_attention(AttnArgs a) {
     MC_TRACE_END(a.trace_slot);
     return;
   }
-  // combine the pages of this KV head: one warp per row, lanes over pages
-  // (max_chunks <= 64 = 2 per lane).  Page c contributes
-  // e^(m_c - M) * (sum_t e^(s_t - m_c) v_t) to the numerator and
-  // e^(m_c - M) * l_c to the denominator; fully masked pages (m_c = -inf)
-  // contribute exactly zero.
-  float* wgt = ss;  // [R][n_chunks]
-  {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const float2* ml = reinterpret_cast<const float2*>(a.part_ml) + (size_t)cslot * a.max_chunks * Rs;
-    for (int row = warp; row < R; row += kAttnThreads / 32) {
-      float2 v0 = make_float2(-INFINITY, 0.0f), v1 = make_float2(-INFINITY, 0.0f);
-      if (lane < n_chunks) v0 = __ldcg(ml + (size_t)lane * Rs + row);
-      if (lane + 32 < n_chunks) v1 = __ldcg(ml + (size_t)(lane + 32) * Rs + row);
-      float M_ = fmaxf(v0.x, v1.x);
-#pragma unroll
-      for (int o = 16; o; o >>= 1) M_ = fmaxf(M_, __shfl_xor_sync(0xffffffffu, M_, o));
-      const float w0 = (v0.x == -INFINITY) ? 0.0f : expf(v0.x - M_);
-      const float w1 = (v1.x == -INFINITY) ? 0.0f : expf(v1.x - M_);
-      if (lane < n_chunks) wgt[row * n_chunks + lane] = w0;
-      if (lane + 32 < n_chunks) wgt[row * n_chunks + lane + 32] = w1;
-      float l = __fadd_rn(__fmul_rn(w0, v0.y), __fmul_rn(w1, v1.y));
-#pragma unroll
-      for (int o = 16; o; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
-      if (lane == 0) s_l[row] = l;
-    }
-  }
   __shared__ uint32_t s_mx[128];  // max |out| per token of the block, float bits
-  if (threadIdx.x < 128) s_mx[threadIdx.x] = 0u;
-  __syncthreads();
-  MC_TRACE_PHASE(a.trace_slot, 6, mc_tp);
-  {
-    // thread -> 4 columns of one row; pages summed in order with eight
-    // float4 loads in flight.  Rp is a multiple of the rows a warp spans, so
-    // the row loop and the shuffles below are warp-uniform.
-    const int h4 = hdp >> 2;
-    const int RGc = kAttnThreads / h4;
-    const int c4 = threadIdx.x % h4;
-    const int seg = min(h4, 32);  // lanes of a warp that share a row
-    const float4* base =
-        reinterpret_cast<const float4*>(a.part_o) + (size_t)cslot * a.max_chunks * Rs * h4 + c4;
-    const size_t cs4 = (size_t)Rs * h4;
-    for (int row = threadIdx.x / h4; row < Rp; row += RGc) {
-      const bool live = row < R;
-      const int rr = live ? row : R - 1;
-      const float* wr = wgt + rr * n_chunks;
-      const float4* src = base + (size_t)rr * h4;
-      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      int ch = 0;
-      for (; ch + 8 <= n_chunks; ch += 8) {
-        float4 v[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) v[u] = __ldcg(src + (size_t)(ch + u) * cs4);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const float w = wr[ch + u];
-          acc.x = __fmaf_rn(v[u].x, w, acc.x);
-          acc.y = __fmaf_rn(v[u].y, w, acc.y);
-          acc.z = __fmaf_rn(v[u].z, w, acc.z);
-          acc.w = __fmaf_rn(v[u].w, w, acc.w);
-        }
-      }
-      for (; ch < n_chunks; ++ch) {
-        const float4 v = __ldcg(src + (size_t)ch * cs4);
-        const float w = wr[ch];
-        acc.x = __fmaf_rn(v.x, w, acc.x);
-        acc.y = __fmaf_rn(v.y, w, acc.y);
-        acc.z = __fmaf_rn(v.z, w, acc.z);
-        acc.w = __fmaf_rn(v.w, w, acc.w);
-      }
-      uint32_t bits = 0u;
-      if (live) {
-        const float l = s_l[row];
-        float4 o;
-        o.x = __fdiv_rn(acc.x, l);
-        o.y = __fdiv_rn(acc.y, l);
-        o.z = __fdiv_rn(acc.z, l);
-        o.w = __fdiv_rn(acc.w, l);
-        const int m = row / G, gi = row - m * G;
-        reinterpret_cast<float4*>(a.out + ((size_t)(mt0 + m) * a.H + kvh * G + gi) * hdp)[c4] = o;
-        bits = max(max(__float_as_uint(fabsf(o.x)), __float_as_uint(fabsf(o.y))),
-                   max(__float_as_uint(fabsf(o.z)), __float_as_uint(fabsf(o.w))));
-      }
-      if (a.st_amax) {
-        for (int off = 1; off < seg; off <<= 1)
-          bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, off));
-        if (live && (threadIdx.x % seg) == 0) atomicMax(s_mx + row / G, bits);
-      }
-    }
-  }
-  if (a.st_amax) {
-    __syncthreads();
-    if (threadIdx.x < Mq) atomicMax(a.st_amax + mt0 + threadIdx.x, s_mx[threadIdx.x]);
-  }
-  if (threadIdx.x == 0) atomicExch(a.cnt + cslot, 0);
+  attn_combine(a, kvh, cslot, n_chunks, R, Rp, Rs, G, mt0, Mq, ss, s_l, s_mx);
   MC_TRACE_PHASE(a.trace_slot, 7, mc_tp);
   MC_TRACE_END(a.trace_slot);
+}
+
+// ------------------------------------------------------------ attention on the tensor cores
+// The same split as k_attention (one CTA per (KV head, page, query block)),
+// for up to 64 query rows and head dims of 32, 64 or 128: q.K^T and P.V on
+// mma.sync m16n8k8 TF32 with each f32 operand split into a TF32 high part
+// and a TF32 remainder (hi*hi + hi*lo + lo*hi: f32-level products).  Eight
+// warps run the MMAs -- one 8-position n-tile of scores each, then the head
+// dimension for P.V -- and all 16 warps stage K/V/q and run the combine; the
+// softmax reduces rows over quads (shuffles) and warps (shared).  Partials
+// (m, l, o) and the last-arriver combine are those of k_attention.
+constexpr int kAttnTcThreads = 512;
+constexpr int kAttnTcMmaWarps = 8;
+
+__device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
+  uint32_t h, l;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+  const float r = x - __uint_as_float(h);
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(l) : "f"(r));
+  hi = h;
+  lo = l;
+}
+__device__ __forceinline__ void mma_tf32(float* d, const uint32_t* a, const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+// d += a * b with a = ah + al, b = bh + bl (the al*bl term dropped)
+__device__ __forceinline__ void mma_3xtf32(float* d, const uint32_t* ah, const uint32_t* al,
+                                           const uint32_t* bh, const uint32_t* bl) {
+  mma_tf32(d, al, bh);
+  mma_tf32(d, ah, bl);
+  mma_tf32(d, ah, bh);
+}
+
+// MT: 16-row m-tiles (query rows <= 16 MT); HD: head dim (hdp)
+template <int MT, int HD>
+__global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_tc(AttnArgs a) {
+  constexpr int P = 64;
+  constexpr int KS = HD + 4;   // K / q row stride: conflict-free fragment loads
+  constexpr int VS = HD + 8;   // V row stride (B fragments walk positions)
+  constexpr int PS = P + 4;    // P row stride
+  constexpr int RM = 16 * MT;  // padded query rows
+  constexpr int NW = kAttnTcMmaWarps;
+  constexpr int PV_WARPS = HD / 8 < NW ? HD / 8 : NW;  // warps with P.V columns
+  constexpr int NT_PV = HD / (8 * PV_WARPS);           // 8-column n-tiles each
+  MC_TRACE_T0
+  extern __shared__ __align__(16) float asmem[];
+  float* sK = asmem;               // [64][KS]
+  float* sV = sK + P * KS;         // [64][VS]
+  float* sQ = sV + P * VS;         // [RM][KS]
+  float* sP = sQ + RM * KS;        // [RM][PS]
+  __shared__ float s_red[NW][RM];
+  __shared__ float s_m[RM], s_l[RM];
+  __shared__ uint32_t s_mx[64];
+  __shared__ int s_last;
+  if (a.pf && threadIdx.x == 0)
+    prefetch_share(a.pf, a.pf_bytes, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
+                   gridDim.x * gridDim.y * gridDim.z);
+  grid_launch_dependents();
+  grid_wait();
+  MC_TRACE_WAITED(a.trace_slot);
+  MC_TRACE_PHASE(a.trace_slot, 0, mc_tp);
+  const int kvh = blockIdx.x, chunk = blockIdx.y, zb = blockIdx.z;
+  const int G = a.H / a.Hkv;
+  const int n_qb = (a.seq.seq_len + a.qblk - 1) / a.qblk;
+  const int z = zb / n_qb, i0 = (zb - z * n_qb) * a.qblk;
+  const int Mq = min(a.qblk, a.seq.seq_len - i0);
+  const int mt0 = z * a.seq.seq_len + i0;
+  const int R = G * Mq;
+  const int Rs = G * a.qblk;
+  const int pos0 = a.pos_ptr[z * a.seq.pos_stride] + a.pos_add + i0;
+  const int L = pos0 + Mq;
+  const int n_chunks = (L + P - 1) / P;
+  const int cslot = zb * a.Hkv + kvh;
+  if (chunk >= n_chunks) {
+    MC_TRACE_END(a.trace_slot);
+    return;
+  }
+  const int t0 = chunk * P;
+  const int nt = min(P, L - t0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  {
+    const int pg = a.page_table[z * a.seq.pt_stride + chunk];
+    const float4* kbase = reinterpret_cast<const float4*>(a.kc + ((size_t)pg * a.Hkv + kvh) * P * HD);
+    const float4* vbase = reinterpret_cast<const float4*>(a.vc + ((size_t)pg * a.Hkv + kvh) * P * HD);
+    constexpr int H4 = HD / 4;
+    for (int i = threadIdx.x; i < nt * H4; i += kAttnTcThreads) {
+      const int t = i / H4, c4 = i - t * H4;
+      cp_async16(sK + t * KS + 4 * c4, kbase + i);
+      cp_async16(sV + t * VS + 4 * c4, vbase + i);
+    }
+    // rows past the page's last position: zero K and V (probability 0 times
+    // stale data could be NaN); their scores are masked
+    for (int i = nt * H4 + threadIdx.x; i < P * H4; i += kAttnTcThreads) {
+      const int t = i / H4, c4 = i - t * H4;
+      *reinterpret_cast<float4*>(sV + t * VS + 4 * c4) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      *reinterpret_cast<float4*>(sK + t * KS + 4 * c4) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    for (int i = threadIdx.x; i < RM * H4; i += kAttnTcThreads) {
+      const int row = i / H4, c4 = i - row * H4;
+      float4 q = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (row < R) {
+        const int m = row / G, gi = row - m * G;
+        q = __ldcg(reinterpret_cast<const float4*>(a.q + ((size_t)(mt0 + m) * a.H + kvh * G + gi) * HD) + c4);
+      }
+      *reinterpret_cast<float4*>(sQ + row * KS + 4 * c4) = q;
+    }
+    cp_async_wait_all();
+  }
+  __syncthreads();
+  MC_TRACE_PHASE(a.trace_slot, 1, mc_tp);
+  // scores: MMA warp w -> positions 8 w .. 8 w + 7 (one n-tile) of every row
+  const bool mma_warp = warp < NW;
+  float sc[MT][4];
+#pragma unroll
+  for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sc[mi][e] = 0.0f;
+  if (mma_warp) {
+#pragma unroll 4
+    for (int kk = 0; kk < HD / 8; ++kk) {
+      uint32_t bh[2], bl[2];
+      const float* kr = sK + (8 * warp + g) * KS + 8 * kk;
+      tf32_split(kr[tq], bh[0], bl[0]);
+      tf32_split(kr[tq + 4], bh[1], bl[1]);
+#pragma unroll
+      for (int mi = 0; mi < MT; ++mi) {
+        uint32_t ah[4], al[4];
+        const float* q0 = sQ + (16 * mi + g) * KS + 8 * kk;
+        const float* q1 = q0 + 8 * KS;
+        tf32_split(q0[tq], ah[0], al[0]);
+        tf32_split(q1[tq], ah[1], al[1]);
+        tf32_split(q0[tq + 4], ah[2], al[2]);
+        tf32_split(q1[tq + 4], ah[3], al[3]);
+        mma_3xtf32(sc[mi], ah, al, bh, bl);
+      }
+    }
+    // scale (a division, transformer.rs:966), mask, and the row maxima
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = 16 * mi + g + 8 * h;
+        const int m = min(row, max(R - 1, 0)) / G;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int t = 8 * warp + 2 * tq + e;
+          float v = __fdiv_rn(sc[mi][2 * h + e], a.inv_scale_den);
+          if (row >= R || t >= nt || t0 + t > pos0 + m) v = -INFINITY;
+          sc[mi][2 * h + e] = v;
+          mx = fmaxf(mx, v);
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        if (tq == 0) s_red[warp][row] = mx;
+      }
+  }
+  __syncthreads();
+  if (threadIdx.x < RM) {
+    float mx = s_red[0][threadIdx.x];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) mx = fmaxf(mx, s_red[w][threadIdx.x]);
+    s_m[threadIdx.x] = mx;
+  }
+  __syncthreads();
+  // probabilities e^(s - max) into sP, and the row sums
+  if (mma_warp) {
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = 16 * mi + g + 8 * h;
+        const float M_ = s_m[row];
+        float sum = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float v = sc[mi][2 * h + e];
+          const float p = (v == -INFINITY) ? 0.0f : expf(v - M_);
+          sP[row * PS + 8 * warp + 2 * tq + e] = p;
+          sum += p;
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        if (tq == 0) s_red[warp][row] = sum;
+      }
+  }
+  __syncthreads();
+  if (threadIdx.x < RM) {
+    float l = s_red[0][threadIdx.x];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) l += s_red[w][threadIdx.x];
+    s_l[threadIdx.x] = l;
+  }
+  MC_TRACE_PHASE(a.trace_slot, 2, mc_tp);
+  // P.V: warp w < PV_WARPS -> head-dim columns 8 NT_PV w .. 8 NT_PV (w + 1)
+  float acc[MT][NT_PV][4];
+#pragma unroll
+  for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+    for (int nj = 0; nj < NT_PV; ++nj)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[mi][nj][e] = 0.0f;
+  const int c0 = warp * 8 * NT_PV;
+  if (warp < PV_WARPS) {
+#pragma unroll 2
+    for (int kk = 0; kk < P / 8; ++kk) {
+      uint32_t bh[NT_PV][2], bl[NT_PV][2];
+#pragma unroll
+      for (int nj = 0; nj < NT_PV; ++nj) {
+        const float* v0 = sV + (8 * kk + tq) * VS + c0 + 8 * nj + g;
+        tf32_split(v0[0], bh[nj][0], bl[nj][0]);
+        tf32_split(v0[4 * VS], bh[nj][1], bl[nj][1]);
+      }
+#pragma unroll
+      for (int mi = 0; mi < MT; ++mi) {
+        uint32_t ah[4], al[4];
+        const float* p0 = sP + (16 * mi + g) * PS + 8 * kk;
+        const float* p1 = p0 + 8 * PS;
+        tf32_split(p0[tq], ah[0], al[0]);
+        tf32_split(p1[tq], ah[1], al[1]);
+        tf32_split(p0[tq + 4], ah[2], al[2]);
+        tf32_split(p1[tq + 4], ah[3], al[3]);
+#pragma unroll
+        for (int nj = 0; nj < NT_PV; ++nj) mma_3xtf32(acc[mi][nj], ah, al, bh[nj], bl[nj]);
+      }
+    }
+  }
+  MC_TRACE_PHASE(a.trace_slot, 3, mc_tp);
+  const size_t pbase = ((size_t)cslot * a.max_chunks + chunk) * Rs;
+  if (warp < PV_WARPS)
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = 16 * mi + g + 8 * h;
+        if (row < R)
+#pragma unroll
+          for (int nj = 0; nj < NT_PV; ++nj)
+            *reinterpret_cast<float2*>(a.part_o + (pbase + row) * HD + c0 + 8 * nj + 2 * tq) =
+                make_float2(acc[mi][nj][2 * h], acc[mi][nj][2 * h + 1]);
+      }
+  __syncthreads();  // s_l complete
+  for (int row = threadIdx.x; row < R; row += kAttnTcThreads) {
+    a.part_ml[(pbase + row) * 2] = s_m[row];
+    a.part_ml[(pbase + row) * 2 + 1] = s_l[row];
+  }
+  __syncthreads();
+  MC_TRACE_PHASE(a.trace_slot, 4, mc_tp);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int last = (atomicAdd(a.cnt + cslot, 1) == n_chunks - 1);
+    if (last) __threadfence();
+    s_last = last;
+  }
+  __syncthreads();
+  MC_TRACE_PHASE(a.trace_slot, 5, mc_tp);
+  if (!s_last) {
+    MC_TRACE_END(a.trace_slot);
+    return;
+  }
+  // the page weights [R][n_chunks <= 64] reuse the dead K/V/q/P region
+  // (at least 4096 floats for every instance)
+  const int h4 = HD / 4;
+  const int span = h4 >= 32 ? 1 : 32 / h4;  // rows one warp spans in the column pass
+  const int Rpc = (R + span - 1) / span * span;
+  attn_combine(a, kvh, cslot, n_chunks, R, Rpc, Rs, G, mt0, Mq, asmem, s_l, s_mx);
+  MC_TRACE_PHASE(a.trace_slot, 7, mc_tp);
+  MC_TRACE_END(a.trace_slot);
+}
+
+size_t attention_tc_smem_bytes(int mt, int hd) {
+  return ((size_t)64 * (hd + 4) + (size_t)64 * (hd + 8) + (size_t)16 * mt * (hd + 4) +
+          (size_t)16 * mt * 68) * sizeof(float);
 }
 
 size_t attention_smem_bytes(int G, int qblk, int hdp, int page) {
@@ -1609,10 +1894,38 @@ static int attention_rb(int R, int hdp, int page) {
   return 0;
 }
 
-// Tokens of one sequence per attention CTA: query rows G * qblk <= 128.
+// Tokens of one sequence per attention CTA: query rows G * qblk <= 64 (the
+// tensor-core kernel's limit, for every forward of a model alike).
 int attention_qblk(int G, int seq_len) {
-  const int cap = std::max(1, 128 / std::max(G, 1));
+  const int cap = std::max(1, 64 / std::max(G, 1));
   return std::max(1, std::min(seq_len, cap));
+}
+
+static int g_attn_tc_smem = 48 * 1024;  // tensor-core attention dynamic smem limit set so far
+
+template <int MT, int HD>
+static cudaError_t launch_attention_tc(const AttnArgs& a, dim3 grid, cudaStream_t s, bool pdl) {
+  const size_t smem = attention_tc_smem_bytes(MT, HD);
+  if (smem > (size_t)g_attn_tc_smem) return cudaErrorInvalidConfiguration;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kAttnTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_attention_tc<MT, HD>, a);
+}
+
+template <int HD>
+static cudaError_t launch_attention_tc_hd(const AttnArgs& a, int R, dim3 grid, cudaStream_t s,
+                                          bool pdl) {
+  if (R <= 16) return launch_attention_tc<1, HD>(a, grid, s, pdl);
+  if (R <= 32) return launch_attention_tc<2, HD>(a, grid, s, pdl);
+  return launch_attention_tc<4, HD>(a, grid, s, pdl);
 }
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
@@ -1621,6 +1934,18 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     return cudaErrorInvalidValue;
   const int n_seq = a.M / a.seq.seq_len;
   const int n_qb = (a.seq.seq_len + a.qblk - 1) / a.qblk;
+  // tensor-core kernel: up to 64 query rows per block, head dims 32 / 64 / 128
+  // (the block size depends only on the model, so every forward of a model
+  // takes the same kernel)
+  if (a.page == 64 && a.max_chunks <= 64 && G * a.qblk <= 64 &&
+      (a.hdp == 32 || a.hdp == 64 || a.hdp == 128)) {
+    const dim3 grid(a.Hkv, a.max_chunks, n_seq * n_qb);
+    switch (a.hdp) {
+      case 32: return launch_attention_tc_hd<32>(a, G * a.qblk, grid, s, pdl);
+      case 64: return launch_attention_tc_hd<64>(a, G * a.qblk, grid, s, pdl);
+      default: return launch_attention_tc_hd<128>(a, G * a.qblk, grid, s, pdl);
+    }
+  }
   const int R = G * a.qblk;
   // the combine's page weights [R][n_chunks] reuse the score tile [Rp][page]
   if (a.page != 64 || a.max_chunks > a.page || a.hdp > 128 || (a.hdp & 3) ||
@@ -1662,8 +1987,25 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
 }
 
 // Raise the dynamic shared-memory limit once, outside any stream capture.
+template <int HD>
+static cudaError_t prepare_attention_tc_hd() {
+  for (auto f : {k_attention_tc<1, HD>, k_attention_tc<2, HD>, k_attention_tc<4, HD>}) {
+    cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)attention_tc_smem_bytes(4, 128));
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
 cudaError_t prepare_kernels(size_t quant_smem, size_t attn_smem) {
   (void)quant_smem;
+  if (g_attn_tc_smem < (int)attention_tc_smem_bytes(4, 128)) {
+    cudaError_t e = prepare_attention_tc_hd<32>();
+    if (e == cudaSuccess) e = prepare_attention_tc_hd<64>();
+    if (e == cudaSuccess) e = prepare_attention_tc_hd<128>();
+    if (e != cudaSuccess) return e;
+    g_attn_tc_smem = (int)attention_tc_smem_bytes(4, 128);
+  }
 
   if (attn_smem > (size_t)g_attn_smem) {
     for (auto f : {k_attention<8, 1>, k_attention<4, 1>, k_attention<2, 1>, k_attention<1, 1>,
