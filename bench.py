@@ -499,8 +499,8 @@ def run_timeline(args):
         print(f"{nm:12s} {c:4d} {e / c:9.2f} {g / c:8.2f} {e:9.1f} {g:8.1f}")
     gemm_ph = ["launch->wait", "weights issued", "mma done", "cluster: all mma done",
                "tmem read + push", "pushes landed", "sums + epilogue", "end barrier"]
-    attn_ph = ["launch->wait", "load K/V/q", "scores", "softmax", "PV + partials", "arrive",
-               "combine prep", "combine"]
+    attn_ph = ["launch->wait", "load K/V/q", "scores + softmax", "P.V", "partials out",
+               "arrive", "-", "combine (last CTA)"]
     for kind in ["qkv", "o", "gu", "down", "head", "attention"]:
         idx = [i for i, nm in enumerate(names) if nm == kind]
         sums, cnts = ph[idx, :8].sum(0), ph[idx, 8:].sum(0)
