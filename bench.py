@@ -422,8 +422,9 @@ def run_ours(args):
 
 def run_profile(args):
     """Short run for ncu launch lists: prime the 1024-token prompt, then
-    3 verify forwards and 2 speculative rounds.  Launch counts before the
-    verify forwards are printed so a capture can skip exactly to them."""
+    3 verify forwards, one more inside the NVTX range "verify" (select it with
+    ncu --nvtx --nvtx-include verify/), and 2 speculative rounds.  Launch
+    counts before the verify forwards are printed as well."""
     import torch
     import modelc_b200 as mb
     torch.cuda.set_device(0)
@@ -440,6 +441,10 @@ def run_profile(args):
           flush=True)
     sess.verify_launch(3)
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("verify")
+    sess.verify_launch(1)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     sess.decode(2)
     torch.cuda.synchronize()
     sess.close()
