@@ -1166,13 +1166,25 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
     // partials in a fixed order (lane-strided, then an xor-shuffle tree)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int m = warp; m < a.M; m += blockDim.x >> 5) {
+      const unsigned mxb = lane == 0 ? __ldcg(a.amax + m) : 0u;  // issued with the partials
       float ss = 0.0f;
-      if (a.do_norm)
-        for (int j = lane; j < a.np; j += 32) ss = __fadd_rn(ss, __ldcg(a.pss + (size_t)m * a.np_stride + j));
+      if (a.do_norm) {
+        // the lane's partials j = lane, lane + 32, ... in batches of 8 whose
+        // loads are all in flight before the (in-order) adds
+        const float* pr = a.pss + (size_t)m * a.np_stride;
+        for (int j0 = lane; j0 < a.np; j0 += 32 * 8) {
+          float v[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) v[u] = j0 + 32 * u < a.np ? __ldcg(pr + j0 + 32 * u) : 0.0f;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            if (j0 + 32 * u < a.np) ss = __fadd_rn(ss, v[u]);
+        }
+      }
 #pragma unroll
       for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
       if (lane == 0) {
-        const float mx = __uint_as_float(__ldcg(a.amax + m));
+        const float mx = __uint_as_float(mxb);
         float rms = 1.0f;
         if (a.do_norm) rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)(a.d > 1 ? a.d : 1)), a.eps));
         const float amax = a.do_norm ? mx / rms : mx;
@@ -1651,8 +1663,9 @@ __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_t
   extern __shared__ __align__(16) float asmem[];
   float* sK = asmem;               // [64][KS]
   float* sV = sK + P * KS;         // [64][VS]
-  float* sQ = sV + P * VS;         // [RM][KS]
-  float* sP = sQ + RM * KS;        // [RM][PS]
+  float* sQ = sV + P * VS;         // [RM][KS] q, then its TF32 high parts
+  float* sQl = sQ + RM * KS;       // [RM][KS] TF32 remainders of q
+  float* sP = sQl + RM * KS;       // [RM][PS]
   __shared__ float s_red[NW][RM];
   __shared__ float s_m[RM], s_l[RM];
   __shared__ uint32_t s_mx[64];
@@ -1710,11 +1723,22 @@ __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_t
       }
       *reinterpret_cast<float4*>(sQ + row * KS + 4 * c4) = q;
     }
-    cp_async_wait_all();
   }
+  __syncthreads();  // q in shared memory (its own loads; cp.async still in flight)
+  // q split once for all MMA warps: TF32 high part in place, remainder aside
+  for (int i = threadIdx.x; i < RM * HD; i += kAttnTcThreads) {
+    const int row = i / HD, c = i - row * HD;
+    uint32_t h, l;
+    tf32_split(sQ[row * KS + c], h, l);
+    sQ[row * KS + c] = __uint_as_float(h);
+    sQl[row * KS + c] = __uint_as_float(l);
+  }
+  cp_async_wait_all();
   __syncthreads();
   MC_TRACE_PHASE(a.trace_slot, 1, mc_tp);
-  // scores: MMA warp w -> positions 8 w .. 8 w + 7 (one n-tile) of every row
+  // scores: MMA warp w -> positions 8 w .. 8 w + 7 (one n-tile) of every row;
+  // the three products (lo*hi, hi*lo, hi*hi) accumulate separately (shorter
+  // dependent MMA chains) and are added small terms first
   const bool mma_warp = warp < NW;
   float sc[MT][4];
 #pragma unroll
@@ -1722,6 +1746,11 @@ __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_t
 #pragma unroll
     for (int e = 0; e < 4; ++e) sc[mi][e] = 0.0f;
   if (mma_warp) {
+    float s_lh[MT][4], s_hl[MT][4];
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s_lh[mi][e] = s_hl[mi][e] = 0.0f;
 #pragma unroll 4
     for (int kk = 0; kk < HD / 8; ++kk) {
       uint32_t bh[2], bl[2];
@@ -1730,16 +1759,20 @@ __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_t
       tf32_split(kr[tq + 4], bh[1], bl[1]);
 #pragma unroll
       for (int mi = 0; mi < MT; ++mi) {
-        uint32_t ah[4], al[4];
-        const float* q0 = sQ + (16 * mi + g) * KS + 8 * kk;
-        const float* q1 = q0 + 8 * KS;
-        tf32_split(q0[tq], ah[0], al[0]);
-        tf32_split(q1[tq], ah[1], al[1]);
-        tf32_split(q0[tq + 4], ah[2], al[2]);
-        tf32_split(q1[tq + 4], ah[3], al[3]);
-        mma_3xtf32(sc[mi], ah, al, bh, bl);
+        const int o0 = (16 * mi + g) * KS + 8 * kk, o1 = o0 + 8 * KS;
+        const uint32_t ah[4] = {__float_as_uint(sQ[o0 + tq]), __float_as_uint(sQ[o1 + tq]),
+                                __float_as_uint(sQ[o0 + tq + 4]), __float_as_uint(sQ[o1 + tq + 4])};
+        const uint32_t al[4] = {__float_as_uint(sQl[o0 + tq]), __float_as_uint(sQl[o1 + tq]),
+                                __float_as_uint(sQl[o0 + tq + 4]), __float_as_uint(sQl[o1 + tq + 4])};
+        mma_tf32(s_lh[mi], al, bh);
+        mma_tf32(s_hl[mi], ah, bl);
+        mma_tf32(sc[mi], ah, bh);
       }
     }
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[mi][e] = (s_lh[mi][e] + s_hl[mi][e]) + sc[mi][e];
     // scale (a division, transformer.rs:966), mask, and the row maxima
 #pragma unroll
     for (int mi = 0; mi < MT; ++mi)
@@ -1875,7 +1908,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_t
 }
 
 size_t attention_tc_smem_bytes(int mt, int hd) {
-  return ((size_t)64 * (hd + 4) + (size_t)64 * (hd + 8) + (size_t)16 * mt * (hd + 4) +
+  return ((size_t)64 * (hd + 4) + (size_t)64 * (hd + 8) + (size_t)2 * 16 * mt * (hd + 4) +
           (size_t)16 * mt * 68) * sizeof(float);
 }
 
