@@ -100,6 +100,8 @@ typedef struct mc_tensor_desc {
 typedef struct mc_weights mc_weights;
 typedef struct mc_session mc_session;
 typedef struct mc_linear mc_linear;
+typedef struct mc_mlp_drafter mc_mlp_drafter;
+typedef struct mc_ngram_drafter mc_ngram_drafter;
 
 /* Speculative session configuration (GenerationConfig, generate.rs:65-167,
  * restricted to the fields the speculative step reads). */
@@ -163,6 +165,32 @@ MC_API mc_status mc_kv_truncate(mc_session* s, int32_t len);
  * decode of gamma tokens after context (KV of the common prefix reused). */
 MC_API mc_status mc_draft(mc_session* s, const uint32_t* context, int32_t n,
                    int32_t gamma, uint32_t* out, int32_t* n_out);
+
+/* MlpDraftModel (draft.rs:28-147) on the device: MlpDraftModel::from_runtime's
+ * tensors (draft.fc1.weight [dh][d], draft.fc1.bias [dh], draft.fc2.weight
+ * [V][dh], draft.fc2.bias [V], and draft.embed.weight or the target's
+ * model.embed_tokens.weight / transformer.wte.weight [V][d]), all f32.
+ * mc_mlp_draft is DraftModel::draft at temperature 0: gamma <= 16 greedy
+ * steps from the context's last token, logits bit-identical to the
+ * reference's sequential f32 sums. */
+MC_API mc_status mc_mlp_draft_create(const mc_tensor_desc* tensors, size_t n, int32_t device,
+                              mc_mlp_drafter** out);
+MC_API mc_status mc_mlp_draft(mc_mlp_drafter* d, const uint32_t* context, int32_t n,
+                       int32_t gamma, uint32_t* out, int32_t* n_out);
+MC_API mc_status mc_mlp_draft_destroy(mc_mlp_drafter* d);
+
+/* The n-gram drafter of speculative_generate (build_ngram_index +
+ * draft_tokens + most_frequent, generate.rs:771-841) on the device: the
+ * index is the history's windows of `ngram` tokens; up to gamma <= 16 steps,
+ * each the most frequent continuation of the current last `ngram` tokens,
+ * stopping at the first key without one.  Count ties go to the continuation
+ * seen first (the reference leaves them to HashMap iteration order).
+ * max_tokens bounds the history length. */
+MC_API mc_status mc_ngram_draft_create(int32_t ngram, int32_t max_tokens, int32_t device,
+                                mc_ngram_drafter** out);
+MC_API mc_status mc_ngram_draft(mc_ngram_drafter* d, const uint32_t* tokens, int32_t n_tokens,
+                         int32_t gamma, uint32_t* out, int32_t* n_out);
+MC_API mc_status mc_ngram_draft_destroy(mc_ngram_drafter* d);
 
 /* speculative_generate (generate.rs:598-767) with the draft model given at
  * session creation: prime the prompt, then rounds of draft -> batched verify

@@ -29,7 +29,8 @@ EXPORTS = [
     "mc_session_stream", "mc_session_round_launches", "mc_linear_run_static",
     "mc_spec_set_seed", "mc_tp_unique_id", "mc_session_tp_init", "mc_session_tp_ipc_handle",
     "mc_session_tp_open_peers", "mc_speculative_generate_batch", "mc_spec_prime_batch",
-    "mc_spec_read_request",
+    "mc_spec_read_request", "mc_mlp_draft_create", "mc_mlp_draft", "mc_mlp_draft_destroy",
+    "mc_ngram_draft_create", "mc_ngram_draft", "mc_ngram_draft_destroy",
 ]
 
 
@@ -121,6 +122,12 @@ def lib():
                                                 i32, i32p]),
         "mc_spec_prime_batch": (i32, [vp, u32p, i32p, i32]),
         "mc_spec_read_request": (i32, [vp, i32, u32p, i32, i32p, i32p, i32, i32p]),
+        "mc_mlp_draft_create": (i32, [C.POINTER(TensorDesc), C.c_size_t, i32, C.POINTER(vp)]),
+        "mc_mlp_draft": (i32, [vp, u32p, i32, i32, u32p, i32p]),
+        "mc_mlp_draft_destroy": (i32, [vp]),
+        "mc_ngram_draft_create": (i32, [i32, i32, i32, C.POINTER(vp)]),
+        "mc_ngram_draft": (i32, [vp, u32p, i32, i32, u32p, i32p]),
+        "mc_ngram_draft_destroy": (i32, [vp]),
         "mc_session_stream": (vp, [vp]),
         "mc_session_round_launches": (i32, [vp]),
         "mc_version": (C.c_char_p, []),

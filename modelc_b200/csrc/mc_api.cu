@@ -31,6 +31,14 @@ static mc_status set_err(mc_status st, const char* fmt, ...) {
   return st;
 }
 
+namespace mc {
+// The calling thread's error message, for the library's other sources.
+mc_status set_error(mc_status st, const char* msg) {
+  g_err = msg;
+  return st;
+}
+}  // namespace mc
+
 #define CK(call)                                                                    \
   do {                                                                              \
     cudaError_t e_ = (call);                                                        \

@@ -327,6 +327,8 @@ constexpr int kTcMaxSplit = 8;  // k-split CTAs of one tile = one cluster (porta
 // stored at chunk c ^ (r % 8).  K is padded to whole atoms (zero weights).
 __host__ __device__ inline int tc_atoms(int KB) { return (KB + 3) / 4; }
 cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl);
+// Records msg as the calling thread's error (mc_last_error) and returns st.
+int32_t set_error(int32_t st, const char* msg);
 // amax[m] = max |x[m][0..d)| as float bits, m < M (the statistics of an
 // un-normalised encoding, QuantArgs::use_stats with np = 0)
 cudaError_t launch_act_amax(const float* x, int ld, int d, int M, unsigned* amax, cudaStream_t s,

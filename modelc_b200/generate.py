@@ -218,6 +218,74 @@ class LlamaDraftModel:
         return self.session.draft_tokens(context, gamma)
 
 
+class MlpDraftModel:
+    """MlpDraftModel (draft.rs:28-147) on the device, greedy: ``tensors``
+    maps the names MlpDraftModel::from_runtime looks up (draft.fc1.weight,
+    draft.fc1.bias, draft.fc2.weight, draft.fc2.bias and draft.embed.weight or
+    model.embed_tokens.weight) to f32 numpy arrays.  ``draft(context, gamma)``
+    returns the reference's tokens bit for bit."""
+
+    def __init__(self, tensors: dict, device: int = 0):
+        from .model import QTensor, _desc_arrays
+        qt = {k: QTensor("f32", np.ascontiguousarray(np.asarray(v, np.float32)))
+              for k, v in tensors.items()}
+        arr, n, self._keep = _desc_arrays(qt)
+        h = C.c_void_p()
+        check(lib().mc_mlp_draft_create(arr, n, device, C.byref(h)))
+        self.handle = h
+
+    def draft(self, context, gamma: int):
+        ctx = _u32(context)
+        out = np.zeros(max(gamma, 1), np.uint32)
+        n = C.c_int32()
+        check(lib().mc_mlp_draft(self.handle, ctx.ctypes.data_as(C.POINTER(C.c_uint32)),
+                                 len(ctx), gamma, out.ctypes.data_as(C.POINTER(C.c_uint32)),
+                                 C.byref(n)))
+        return out[: n.value].tolist()
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().mc_mlp_draft_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class NgramDraftModel:
+    """The n-gram drafter of speculative_generate (generate.rs:771-841) on
+    the device: ``draft(tokens, gamma)`` drafts from the index of ``tokens``'
+    windows of ``n`` tokens (ties: the continuation seen first)."""
+
+    def __init__(self, n: int = 3, max_tokens: int = 1 << 16, device: int = 0):
+        h = C.c_void_p()
+        check(lib().mc_ngram_draft_create(n, max_tokens, device, C.byref(h)))
+        self.handle = h
+
+    def draft(self, tokens, gamma: int):
+        t = _u32(tokens)
+        out = np.zeros(max(gamma, 1), np.uint32)
+        n = C.c_int32()
+        check(lib().mc_ngram_draft(self.handle, t.ctypes.data_as(C.POINTER(C.c_uint32)), len(t),
+                                   gamma, out.ctypes.data_as(C.POINTER(C.c_uint32)),
+                                   C.byref(n)))
+        return out[: n.value].tolist()
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().mc_ngram_draft_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def speculative_generate(target: Weights, draft: Weights, prompt, config: GenerationConfig,
                          max_context: int | None = None):
     """generate.rs:598-767 with a transformer draft; returns (ids, accepted)."""
