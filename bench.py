@@ -98,12 +98,15 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def profile_traffic():
-    """Per-launch DRAM bytes of the verify forward from the committed ncu summary."""
+def profile_traffic(workload, parallelism):
+    """Per-launch DRAM bytes of the verify forward from the committed ncu
+    summary, or None when that capture was of another workload."""
     p = os.path.join(ROOT, "profiles", "verify_traffic.json")
     if os.path.exists(p):
         with open(p) as f:
-            return json.load(f).get("verify_forward_dram_bytes")
+            d = json.load(f)
+        if d.get("workload") == workload and d.get("parallelism") == parallelism:
+            return d.get("verify_forward_dram_bytes")
     return None
 
 
@@ -342,7 +345,10 @@ def run_ours(args):
     algo = target.streamed_bytes + kv_bytes + act_bytes
     peak, peak_kind = measured_peaks()
     achieved = algo / t_ver / 1e9
-    traffic = profile_traffic()
+    parallelism = (((f"tp{world}" + ("-nccl" if args.tp_nccl else "-nvlink"))
+                    if tp else f"replicas{world}") if world > 1 else "single")
+    # each replica runs the single-GPU forward, so the single-GPU capture holds
+    traffic = profile_traffic(args.config, "single" if not tp else parallelism)
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "traffic": traffic,
             "peak_source": peak_kind, "kernel": "verify forward (k_gemv + fused kernels)",
@@ -397,9 +403,7 @@ def run_ours(args):
             "config": {"workload": wl.desc, "target": cfg.name, "draft_layers": wl.draft.n_layers,
                        "prompt_len": PROMPT_LEN, "new_tokens": NEW_TOKENS, "gamma": GAMMA,
                        "temperature": wl.temperature, "batch": B,
-                       "parallelism": ((f"tp{world}" + ("-nccl" if args.tp_nccl else "-nvlink"))
-                                       if tp else f"replicas{world}") if world > 1
-                       else "single",
+                       "parallelism": parallelism,
                        "l2": f"inputs larger than L2 ({wbytes / 1e9:.2f} GB of weights per verify)"},
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
