@@ -112,7 +112,7 @@ typedef struct mc_spec_cfg {
                            token, generate.rs:695-726); 1: gamma+1 positions
                            with the bonus token */
   float temperature;    /* 0 = greedy; > 0 = sampling at this temperature
-                           (draft and target, no top-p / min-p) */
+                           (draft and target) */
   uint64_t seed;
   volatile int32_t* cancel;  /* optional; checked between rounds (generate.rs:639) */
   int32_t accept_mode;  /* temperature > 0 only.  0: accept draft x with
@@ -129,6 +129,10 @@ typedef struct mc_spec_cfg {
                            one verify forward over B x (gamma or gamma+1)
                            positions, and B acceptances.  B x (gamma +
                            bonus) <= 64. */
+  float top_p;          /* temperature > 0: top-p filter on every draft and
+                           target distribution when 0 < top_p < 1
+                           (generate.rs:961-963), as mc_sample_rows states it */
+  float min_p;          /* likewise min-p when 0 < min_p < 1 (generate.rs:964-966) */
 } mc_spec_cfg;
 
 /* Load (quantize-free) weights to the device and repack them for the
@@ -302,6 +306,26 @@ MC_API int64_t mc_linear_weight_bytes(const mc_linear* l);
  * one stream or synchronise between them. */
 MC_API mc_status mc_linear_run_static(mc_linear* l, const float* x_dev, int32_t m,
                                float* y_dev, void* stream);
+
+/* One token per row of logits (device memory, n_rows x vocab, f32), written
+ * to tokens_dev (device, n_rows) on `stream` (a cudaStream_t as void*).
+ * Replaces sample (generate.rs:948-969, the penalty- and constraint-free path
+ * of sample_constrained, :982-1027):
+ *   temperature <= 0: argmax (generate.rs:1088-1098): the first strict
+ *     maximum; NaN and -inf never win; 0 when no entry does;
+ *   temperature > 0: softmax(l / T), then top-p (generate.rs:1034-1063) when
+ *     0 < top_p < 1, then min-p (generate.rs:1071-1086) when 0 < min_p < 1,
+ *     then an inverse-CDF draw.  The filters are restated on the exact
+ *     weights e_v = exp((l_v - max) / T): top-p keeps the shortest prefix of
+ *     (e desc, index asc) whose integer mass sum floor(e_v 2^32) reaches
+ *     ceil(top_p x total); min-p drops e_v < min_p.  The uniform of row r is
+ *     Philox4x32-10 keyed by seed with counter (slot r, round), the stream
+ *     of the stochastic sessions, in place of the reference's
+ *     StdRng::seed_from_u64(seed + step).
+ * vocab <= 262144. */
+MC_API mc_status mc_sample_rows(const float* logits_dev, int32_t n_rows, int32_t vocab,
+                                float temperature, float top_p, float min_p, uint64_t seed,
+                                uint32_t round, uint32_t* tokens_dev, void* stream);
 
 MC_API size_t mc_last_error(char* buf, size_t cap);
 MC_API const char* mc_version(void);

@@ -5,8 +5,8 @@ The compute path is ``libmodelc_cuda.so`` (hand-written CUDA, C ABI in
 """
 from ._lib import McError, lib, last_error  # noqa: F401
 from .generate import (GenerationConfig, LlamaDraftModel, MlpDraftModel,  # noqa: F401
-                       NgramDraftModel, Session, forward_llama_cached, speculative_generate,
-                       tp_unique_id)
+                       NgramDraftModel, Session, forward_llama_cached, sample_rows,
+                       speculative_generate, tp_unique_id)
 from .model import (LLAMA2_70B, LLAMA3_8B, PRESETS, TINY, TINYLLAMA,  # noqa: F401
                     LlamaConfig, Linear, QTensor, Weights, quantize_int8_rows,
                     quantize_int8_tensor, synth_weights, synth_weights_torch)

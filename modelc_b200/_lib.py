@@ -30,7 +30,7 @@ EXPORTS = [
     "mc_spec_set_seed", "mc_tp_unique_id", "mc_session_tp_init", "mc_session_tp_ipc_handle",
     "mc_session_tp_open_peers", "mc_speculative_generate_batch", "mc_spec_prime_batch",
     "mc_spec_read_request", "mc_mlp_draft_create", "mc_mlp_draft", "mc_mlp_draft_destroy",
-    "mc_ngram_draft_create", "mc_ngram_draft", "mc_ngram_draft_destroy",
+    "mc_ngram_draft_create", "mc_ngram_draft", "mc_ngram_draft_destroy", "mc_sample_rows",
 ]
 
 
@@ -57,7 +57,7 @@ class SpecCfg(C.Structure):
     _fields_ = [("gamma", C.c_int32), ("max_context", C.c_int32), ("bonus", C.c_int32),
                 ("temperature", C.c_float), ("seed", C.c_uint64),
                 ("cancel", C.POINTER(C.c_int32)), ("accept_mode", C.c_int32),
-                ("n_requests", C.c_int32)]
+                ("n_requests", C.c_int32), ("top_p", C.c_float), ("min_p", C.c_float)]
 
 
 _lib = None
@@ -128,6 +128,8 @@ def lib():
         "mc_ngram_draft_create": (i32, [i32, i32, i32, C.POINTER(vp)]),
         "mc_ngram_draft": (i32, [vp, u32p, i32, i32, u32p, i32p]),
         "mc_ngram_draft_destroy": (i32, [vp]),
+        "mc_sample_rows": (i32, [vp, i32, i32, C.c_float, C.c_float, C.c_float, C.c_uint64,
+                                 C.c_uint32, vp, vp]),
         "mc_session_stream": (vp, [vp]),
         "mc_session_round_launches": (i32, [vp]),
         "mc_version": (C.c_char_p, []),

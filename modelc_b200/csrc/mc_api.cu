@@ -1566,6 +1566,8 @@ static SpecState fresh_state(const mc_session* s, int n_prompt) {
   h.temperature = s->cfg.temperature;
   h.seed_lo = (uint32_t)s->cfg.seed;
   h.seed_hi = (uint32_t)(s->cfg.seed >> 32);
+  h.top_p = s->cfg.top_p;
+  h.min_p = s->cfg.min_p;
   return h;
 }
 
@@ -2062,3 +2064,23 @@ extern "C" MC_API int32_t mc_trace_read(unsigned long long* out, int32_t n) {
   return trace_read(out, n) == cudaSuccess ? MC_OK : MC_E_CUDA;
 }
 #endif
+
+// generate.rs:948-969 sample, one token per row of device logits.
+extern "C" mc_status mc_sample_rows(const float* logits_dev, int32_t n_rows, int32_t vocab,
+                                    float temperature, float top_p, float min_p, uint64_t seed,
+                                    uint32_t round, uint32_t* tokens_dev, void* stream) {
+  if (n_rows < 0 || (n_rows > 0 && (!logits_dev || !tokens_dev)))
+    return set_err(MC_E_INVALID, "bad arguments");
+  if (vocab <= 0 || vocab > kSampleMaxVocab)
+    return set_err(MC_E_SHAPE, "vocab %d outside [1, %d]", vocab, kSampleMaxVocab);
+  if (!isfinite(temperature)) return set_err(MC_E_INVALID, "temperature must be finite");
+  if (n_rows == 0) return MC_OK;
+  cudaPointerAttributes pa{};
+  CK(cudaPointerGetAttributes(&pa, logits_dev));
+  if (pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged)
+    return set_err(MC_E_INVALID, "logits must be device memory");
+  CK(cudaSetDevice(pa.device));
+  CK(launch_sample_rows(logits_dev, n_rows, vocab, temperature, top_p, min_p, seed, round,
+                        tokens_dev, (cudaStream_t)stream));
+  return MC_OK;
+}

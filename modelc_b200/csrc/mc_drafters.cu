@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(kMlpFc2Threads) k_mlp_fc2(const float* __restr
       sum = b2[i];
       for (int j = 0; j < dh; ++j) sum = __fadd_rn(sum, __fmul_rn(row[j], sh[j]));
     }
-    if (!isnan(sum)) k = argmax_key(sum, (uint32_t)i);
+    if (sum > -INFINITY) k = argmax_key(__fadd_rn(sum, 0.0f), (uint32_t)i);
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) {

@@ -281,7 +281,8 @@ struct SpecState {
   int accept_mode;     // stochastic: 0 = min(1, p/q) + residual, 1 = sample == draft
   float temperature;   // > 0: stochastic rounds
   uint32_t seed_lo, seed_hi;
-  int pad[2];
+  float top_p;         // applied when in (0, 1) (generate.rs:961-963)
+  float min_p;         // applied when in (0, 1) (generate.rs:964-966)
   unsigned long long tkeys[kGroupTokens];
   unsigned long long dkeys[kGroupTokens];
 };
@@ -344,6 +345,9 @@ cudaError_t launch_set_int(int* p, int v, cudaStream_t s);
 // Stochastic rounds: sample draft step j from softmax(logits / T) into
 // *key_out (as an argmax key), and the acceptance of a whole round from the
 // verify logits tlog [vm][V] and the draft logits dlog [gamma][V].
+cudaError_t launch_sample_rows(const float* logits, int rows, int V, float t, float top_p,
+                               float min_p, uint64_t seed, uint32_t rnd, uint32_t* out,
+                               cudaStream_t s);
 cudaError_t launch_sample_draft(SpecState* st, const float* logits, int V, int j,
                                 unsigned long long* key_out, cudaStream_t s, bool pdl);
 cudaError_t launch_accept_stochastic(SpecState* st, uint32_t* ctx, int* acc_log, int vm,

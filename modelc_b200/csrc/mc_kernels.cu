@@ -15,6 +15,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <climits>
 #include <type_traits>
 
 #include "mc_internal.cuh"
@@ -656,8 +657,9 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
             o[prow] = y0;
           }
           if constexpr (EPI == EPI_LMHEAD) {
-            if (!isnan(y0)) {
-              unsigned long long k = argmax_key(y0, (uint32_t)(prow + a.row_offset));
+            if (y0 > -INFINITY) {  // NaN and -inf never win (generate.rs:1088-1098)
+              unsigned long long k =
+                  argmax_key(__fadd_rn(y0, 0.0f), (uint32_t)(prow + a.row_offset));
               kmax[it] = k > kmax[it] ? k : kmax[it];
             }
           }
@@ -672,8 +674,9 @@ __device__ __forceinline__ void gemv_epilogue(const GemvArgs& a, int stripe, con
             o[prow + 8] = y1;
           }
           if constexpr (EPI == EPI_LMHEAD) {
-            if (!isnan(y1)) {
-              unsigned long long k = argmax_key(y1, (uint32_t)(prow + 8 + a.row_offset));
+            if (y1 > -INFINITY) {
+              unsigned long long k =
+                  argmax_key(__fadd_rn(y1, 0.0f), (uint32_t)(prow + 8 + a.row_offset));
               kmax[it] = k > kmax[it] ? k : kmax[it];
             }
           }
@@ -2215,13 +2218,18 @@ __device__ __forceinline__ float philox_uniform(uint32_t seed_lo, uint32_t seed_
 constexpr int kSampThreads = 1024;  // 32 warps; tile t = elements [1024 t, 1024 t + 1024)
 constexpr int kSampTiles = kSampleMaxVocab / 1024;
 
+constexpr int kCutBins = 4096;  // radix digits of 12 bits (the last pass 8)
+
 struct SampSmem {
   float red[32];
   int ired[32];
   float tile[kSampTiles];
   int tile_last[kSampTiles];
   float bcast[4];
-  int ibcast[4];  // [0] tile of the target, [1] fallback index, [2] index found
+  int ibcast[4];  // [0] tile of the target, [1] fallback index, [2] index found, [3] bin
+  unsigned long long hist[kCutBins];  // top-p: integer mass per radix digit
+  unsigned long long wsum[32];
+  unsigned long long ubcast[2];
 };
 
 __device__ float block_max(const float* row, int V, SampSmem& sm) {
@@ -2335,6 +2343,167 @@ __device__ int inv_cdf(W w, int V, float tot, float u, SampSmem& sm) {
   return res;
 }
 
+// ---- top-p and min-p (generate.rs:1034-1063 apply_top_p, :1071-1086
+// apply_min_p), restated on e_v = exp((l_v - max) / T), whose maximum is 1,
+// so that every decision is exact and order-independent:
+//   top-p (0 < top_p < 1): order v by (e_v descending, v ascending), as the
+//     reference's stable descending sort does; each v has the integer mass
+//     m_v = floor(e_v * 2^32); keep the shortest prefix whose mass reaches
+//     T = ceil(top_p * sum m_v) (one double rounding).  A three-pass radix
+//     select over the bits of e_v (12 + 12 + 8 bits; integer mass histograms
+//     in shared memory) finds the e at which the prefix ends, and one more
+//     pass the last index kept when the prefix ends inside a run of equal e.
+//   min-p (0 < min_p < 1): drop e_v < min_p, i.e. p_v < min_p * max p.
+// The sampler draws from the kept e_v unnormalised, so the reference's
+// renormalisations need no pass of their own.
+struct Cut {
+  uint32_t key;  // keep v iff bits(e_v) > key, or == key and v <= last ...
+  int last;
+  float min_e;   // ... and e_v >= min_e
+};
+
+__device__ __forceinline__ unsigned long long cut_mass(float e) {
+  return __float2ull_rz(__fmul_rn(e, 4294967296.0f));
+}
+
+__device__ __forceinline__ float cut_weight(const Cut& c, float e, int v) {
+  const uint32_t k = __float_as_uint(e);
+  return (e >= c.min_e && (k > c.key || (k == c.key && v <= c.last))) ? e : 0.0f;
+}
+
+// Exclusive prefix sum over the block in thread order; *total gets the sum.
+__device__ unsigned long long block_excl_scan(unsigned long long x, SampSmem& sm,
+                                              unsigned long long* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned long long inc = x;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) sm.wsum[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    const unsigned long long w = sm.wsum[lane];
+    unsigned long long wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned long long y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    sm.wsum[lane] = wi - w;
+    if (lane == 31) sm.ubcast[0] = wi;
+  }
+  __syncthreads();
+  const unsigned long long r = sm.wsum[warp] + inc - x;
+  *total = sm.ubcast[0];
+  __syncthreads();
+  return r;
+}
+
+// Index of the k-th (1-based, ascending) v with pred(v); INT_MAX if none.
+template <class P>
+__device__ int kth_index(P pred, int V, int k, SampSmem& sm) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = (V + 1023) >> 10;
+  for (int t = warp; t < nt; t += 32) {
+    int c = 0;
+    for (int i = 0; i < 32; ++i) {
+      const int v = (t << 10) + i * 32 + lane;
+      c += __popc(__ballot_sync(0xffffffffu, v < V && pred(v)));
+    }
+    if (lane == 0) sm.tile_last[t] = c;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int r = k, kt = -1;
+    for (int t = 0; t < nt; ++t) {
+      if (r <= sm.tile_last[t]) {
+        kt = t;
+        break;
+      }
+      r -= sm.tile_last[t];
+    }
+    sm.ibcast[0] = kt;
+    sm.ibcast[1] = r;
+    sm.ibcast[2] = INT_MAX;
+  }
+  __syncthreads();
+  const int kt = sm.ibcast[0];
+  if (kt >= 0 && threadIdx.x < 32) {
+    int r = sm.ibcast[1];
+    for (int i = 0; i < 32; ++i) {
+      const int v = (kt << 10) + i * 32 + lane;
+      const unsigned m = __ballot_sync(0xffffffffu, v < V && pred(v));
+      const int c = __popc(m);
+      if (r <= c) {
+        if (((m >> lane) & 1u) && __popc(m & ((1u << lane) - 1u)) == r - 1) sm.ibcast[2] = v;
+        break;
+      }
+      r -= c;
+    }
+  }
+  __syncthreads();
+  const int res = sm.ibcast[2];
+  __syncthreads();
+  return res;
+}
+
+template <class E>
+__device__ Cut make_cut(E e, int V, float top_p, float min_p, SampSmem& sm) {
+  Cut c{0u, INT_MAX, (min_p > 0.0f && min_p < 1.0f) ? min_p : 0.0f};
+  if (!(top_p > 0.0f && top_p < 1.0f)) return c;
+  uint32_t pfx = 0u, pmask = 0u;
+  unsigned long long need = 0ull;
+  int bin = 0;
+#pragma unroll 1
+  for (int pass = 0; pass < 3; ++pass) {
+    const int shift = pass == 0 ? 20 : (pass == 1 ? 8 : 0);
+    const int nb = pass == 2 ? 256 : kCutBins;
+    for (int i = threadIdx.x; i < nb; i += kSampThreads) sm.hist[i] = 0ull;
+    __syncthreads();
+    for (int v = threadIdx.x; v < V; v += kSampThreads) {
+      const float x = e(v);
+      const uint32_t k = __float_as_uint(x);
+      if ((k & pmask) == pfx) atomicAdd(&sm.hist[(k >> shift) & (uint32_t)(nb - 1)], cut_mass(x));
+    }
+    __syncthreads();
+    // thread t holds digits nb-1-4t .. nb-4-4t: thread order = descending e
+    const int hi = nb - 1 - 4 * (int)threadIdx.x;
+    unsigned long long loc = 0ull;
+    if (hi >= 0)
+      for (int b = 0; b < 4; ++b) loc += sm.hist[hi - b];
+    unsigned long long tot;
+    unsigned long long ex = block_excl_scan(loc, sm, &tot);
+    if (pass == 0) need = (unsigned long long)ceil(__dmul_rn((double)top_p, (double)tot));
+    if (hi >= 0 && ex < need && need <= ex + loc) {  // exactly one thread
+      for (int b = 0; b < 4; ++b) {
+        const unsigned long long h = sm.hist[hi - b];
+        if (ex + h >= need) {
+          sm.ubcast[1] = need - ex;
+          sm.ibcast[3] = hi - b;
+          break;
+        }
+        ex += h;
+      }
+    }
+    __syncthreads();
+    need = sm.ubcast[1];  // mass still to take inside the chosen digit
+    bin = sm.ibcast[3];
+    pfx |= (uint32_t)bin << shift;
+    pmask |= (uint32_t)(nb - 1) << shift;
+  }
+  // every v in the last digit has e = pfx and the same mass
+  const unsigned long long m1 = cut_mass(__uint_as_float(pfx));
+  const unsigned long long cnt = m1 ? sm.hist[bin] / m1 : 0ull;
+  const unsigned long long k = m1 ? (need + m1 - 1) / m1 : 0ull;
+  __syncthreads();
+  c.key = pfx;
+  if (k < cnt)
+    c.last = kth_index([&](int v) { return __float_as_uint(e(v)) == pfx; }, V, (int)k, sm);
+  return c;
+}
+
 __global__ void __launch_bounds__(kSampThreads) k_sample_draft(SpecState* st, const float* row,
                                                                int V, int j,
                                                                unsigned long long* key_out) {
@@ -2343,7 +2512,9 @@ __global__ void __launch_bounds__(kSampThreads) k_sample_draft(SpecState* st, co
   grid_wait();
   const float t = st->temperature;
   const float mx = block_max(row, V, sm);
-  auto w = [&](int v) { return expf(__fdiv_rn(__fsub_rn(__ldcg(row + v), mx), t)); };
+  auto e = [&](int v) { return expf(__fdiv_rn(__fsub_rn(__ldcg(row + v), mx), t)); };
+  const Cut c = make_cut(e, V, st->top_p, st->min_p, sm);
+  auto w = [&](int v) { return cut_weight(c, e(v), v); };
   const float tot = tile_sums(w, V, sm);
   const float u = philox_uniform(st->seed_lo, st->seed_hi, (uint32_t)st->n_rounds, (uint32_t)j);
   const int x = inv_cdf(w, V, tot, u, sm);
@@ -2357,7 +2528,7 @@ __global__ void __launch_bounds__(kSampThreads) k_accept_stochastic(
   grid_launch_dependents();
   grid_wait();
   const int g = st->gamma;
-  const float t = st->temperature;
+  const float t = st->temperature, top_p = st->top_p, min_p = st->min_p;
   const uint32_t rnd = (uint32_t)st->n_rounds, s0 = st->seed_lo, s1 = st->seed_hi;
   int a = 0, y = -1;
   for (int j = 0; j < g; ++j) {
@@ -2366,7 +2537,9 @@ __global__ void __launch_bounds__(kSampThreads) k_accept_stochastic(
     const uint32_t x = min(key_index(st->dkeys[j]), (uint32_t)(V - 1));
     const float u_res = philox_uniform(s0, s1, rnd, 64u + (uint32_t)j);
     const float mp = block_max(p, V, sm);
-    auto wp = [&](int v) { return expf(__fdiv_rn(__fsub_rn(__ldcg(p + v), mp), t)); };
+    auto ep = [&](int v) { return expf(__fdiv_rn(__fsub_rn(__ldcg(p + v), mp), t)); };
+    const Cut cp = make_cut(ep, V, top_p, min_p, sm);
+    auto wp = [&](int v) { return cut_weight(cp, ep(v), v); };
     const float sp = tile_sums(wp, V, sm);
     if (st->accept_mode == 1) {
       // the reference's rule (generate.rs:695-726): the target's own sample
@@ -2379,11 +2552,13 @@ __global__ void __launch_bounds__(kSampThreads) k_accept_stochastic(
       break;
     }
     const float mq = block_max(q, V, sm);
-    auto wq = [&](int v) { return expf(__fdiv_rn(__fsub_rn(__ldcg(q + v), mq), t)); };
+    auto eq_ = [&](int v) { return expf(__fdiv_rn(__fsub_rn(__ldcg(q + v), mq), t)); };
+    const Cut cq = make_cut(eq_, V, top_p, min_p, sm);
+    auto wq = [&](int v) { return cut_weight(cq, eq_(v), v); };
     const float sq = tile_sums(wq, V, sm);
-    const float ep = wp((int)x), eq = wq((int)x);
+    const float px = wp((int)x), qx = wq((int)x);
     const float u = philox_uniform(s0, s1, rnd, 32u + (uint32_t)j);
-    if (__fmul_rn(__fmul_rn(u, eq), sp) < __fmul_rn(ep, sq)) {  // u < p(x) / q(x)
+    if (__fmul_rn(__fmul_rn(u, qx), sp) < __fmul_rn(px, sq)) {  // u < p(x) / q(x)
       ++a;
       continue;
     }
@@ -2402,7 +2577,9 @@ __global__ void __launch_bounds__(kSampThreads) k_accept_stochastic(
   if (y < 0 && a == g && vm > g) {  // bonus token from the last verify position
     const float* p = tlog + (size_t)g * V;
     const float mp = block_max(p, V, sm);
-    auto wp = [&](int v) { return expf(__fdiv_rn(__fsub_rn(__ldcg(p + v), mp), t)); };
+    auto ep = [&](int v) { return expf(__fdiv_rn(__fsub_rn(__ldcg(p + v), mp), t)); };
+    const Cut cp = make_cut(ep, V, top_p, min_p, sm);
+    auto wp = [&](int v) { return cut_weight(cp, ep(v), v); };
     const float sp = tile_sums(wp, V, sm);
     y = inv_cdf(wp, V, sp, philox_uniform(s0, s1, rnd, 64u + (uint32_t)g), sm);
   }
@@ -2449,6 +2626,52 @@ cudaError_t launch_accept_stochastic(SpecState* st, uint32_t* ctx, int* acc_log,
   if (V <= 0 || V > kSampleMaxVocab) return cudaErrorInvalidValue;
   return launch_one_block(k_accept_stochastic, kSampThreads, s, pdl, st, ctx, acc_log, vm, tlog,
                           dlog, V);
+}
+
+// One CTA per row of logits (generate.rs:948-969 sample): temperature <= 0
+// is the reference's argmax (first strict maximum; NaN and -inf never win;
+// 0 when nothing does), otherwise softmax(l / T) after top-p and min-p,
+// drawn by inverse CDF with the Philox uniform of (seed, round, slot = row).
+__global__ void __launch_bounds__(kSampThreads) k_sample_rows(const float* logits, int V,
+                                                              float t, float top_p, float min_p,
+                                                              uint32_t s0, uint32_t s1,
+                                                              uint32_t rnd, uint32_t* out) {
+  __shared__ SampSmem sm;
+  const float* row = logits + (size_t)blockIdx.x * V;
+  if (!(t > 0.0f)) {
+    unsigned long long best = 0ull;
+    for (int v = threadIdx.x; v < V; v += kSampThreads) {
+      const float x = row[v];
+      if (x > -INFINITY) best = max(best, argmax_key(__fadd_rn(x, 0.0f), (uint32_t)v));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if ((threadIdx.x & 31) == 0) sm.wsum[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      unsigned long long b = sm.wsum[threadIdx.x];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
+      if (threadIdx.x == 0) out[blockIdx.x] = key_index(b);
+    }
+    return;
+  }
+  const float mx = block_max(row, V, sm);
+  auto e = [&](int v) { return expf(__fdiv_rn(__fsub_rn(__ldcg(row + v), mx), t)); };
+  const Cut c = make_cut(e, V, top_p, min_p, sm);
+  auto w = [&](int v) { return cut_weight(c, e(v), v); };
+  const float tot = tile_sums(w, V, sm);
+  const int y = inv_cdf(w, V, tot, philox_uniform(s0, s1, rnd, blockIdx.x), sm);
+  if (threadIdx.x == 0) out[blockIdx.x] = (uint32_t)y;
+}
+
+cudaError_t launch_sample_rows(const float* logits, int rows, int V, float t, float top_p,
+                               float min_p, uint64_t seed, uint32_t rnd, uint32_t* out,
+                               cudaStream_t s) {
+  if (V <= 0 || V > kSampleMaxVocab || rows <= 0) return cudaErrorInvalidValue;
+  k_sample_rows<<<rows, kSampThreads, 0, s>>>(logits, V, t, top_p, min_p, (uint32_t)seed,
+                                             (uint32_t)(seed >> 32), rnd, out);
+  return cudaGetLastError();
 }
 
 // grid (ceil(d / 1024), M), 256 threads: h += y on one 1024-element block of

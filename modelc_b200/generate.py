@@ -25,6 +25,8 @@ class GenerationConfig:
     seed: int = 0
     bonus: bool = False   # False: the reference verify (no bonus token)
     accept_mode: int = 0  # temperature > 0: 0 = min(1, p/q), 1 = sample == draft
+    top_p: float = 0.0    # temperature > 0: applied when in (0, 1) (generate.rs:961-963)
+    min_p: float = 0.0    # temperature > 0: applied when in (0, 1) (generate.rs:964-966)
 
 
 def _u32(a) -> np.ndarray:
@@ -41,13 +43,14 @@ class Session:
 
     def __init__(self, target: Weights, draft: Weights | None = None, gamma: int = 4,
                  max_context: int = 2048, bonus: bool = False, temperature: float = 0.0,
-                 seed: int = 0, accept_mode: int = 0, n_requests: int = 1):
+                 seed: int = 0, accept_mode: int = 0, n_requests: int = 1,
+                 top_p: float = 0.0, min_p: float = 0.0):
         self.target, self.draft = target, draft
         self.gamma = gamma
         self.n_requests = n_requests
         self._cancel = C.c_int32(0)
         cfg = _lib.SpecCfg(gamma, max_context, int(bonus), temperature, seed,
-                           C.pointer(self._cancel), accept_mode, n_requests)
+                           C.pointer(self._cancel), accept_mode, n_requests, top_p, min_p)
         h = C.c_void_p()
         check(lib().mc_session_create(target.handle, draft.handle if draft else None,
                                       C.byref(cfg), C.byref(h)))
@@ -292,11 +295,28 @@ def speculative_generate(target: Weights, draft: Weights, prompt, config: Genera
     cap = max_context or (len(prompt) + config.max_tokens + config.gamma + 8)
     s = Session(target, draft, gamma=config.gamma, max_context=cap, bonus=config.bonus,
                 temperature=config.temperature, seed=config.seed,
-                accept_mode=config.accept_mode)
+                accept_mode=config.accept_mode, top_p=config.top_p, min_p=config.min_p)
     try:
         return s.speculative_generate(prompt, config.max_tokens)
     finally:
         s.close()
+
+
+def sample_rows(logits, temperature: float = 0.0, top_p: float = 0.0, min_p: float = 0.0,
+                seed: int = 0, round: int = 0):
+    """generate.rs:948-969 sample, one token per row of a CUDA f32 tensor
+    [rows, vocab]: argmax at temperature <= 0, else softmax(l / T) after
+    top-p and min-p with the Philox uniform of (seed, round, row).  Returns a
+    CUDA int32 tensor of token ids (uint32 values below 2^31)."""
+    import torch
+    x = logits.contiguous()
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    out = torch.empty(x.shape[0], dtype=torch.int32, device=x.device)
+    check(lib().mc_sample_rows(x.data_ptr(), x.shape[0], x.shape[1], temperature, top_p, min_p,
+                               seed, round, out.data_ptr(),
+                               torch.cuda.current_stream(x.device).cuda_stream))
+    return out
 
 
 def forward_llama_cached(session: Session, ids):

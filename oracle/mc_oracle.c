@@ -1042,18 +1042,74 @@ static int inv_cdf(const float* w, int n, float s, float u) {
   return last;
 }
 
-static int sample_temp(const float* l, int n, float t, float u, float* scratch) {
+/* Weights of softmax(l / T) after top-p (generate.rs:1034-1063) and min-p
+ * (generate.rs:1071-1086), restated on e_v = exp((l_v - max) / T), whose
+ * maximum is 1, so that every decision is exact:
+ *   top-p (0 < top_p < 1): order v by (e_v descending, v ascending), as the
+ *     reference's stable descending sort does; give each v the integer mass
+ *     m_v = floor(e_v * 2^32); keep the shortest prefix whose mass sum
+ *     reaches T = ceil(top_p * sum_v m_v) (the sum in double, one rounding);
+ *   min-p (0 < min_p < 1): drop v with e_v < min_p (p_v < min_p * max_v p_v
+ *     with max e = 1), applied after top-p as the reference does.
+ * The renormalisations of the reference are left to the sampler, which
+ * draws from unnormalised weights.  Returns the sum of the weights in index
+ * order. */
+float oracle_filtered_weights(const float* l, int n, float t, float top_p, float min_p,
+                              float* w) {
   float mx, s;
   temp_stats(l, n, t, &mx, &s);
-  for (int v = 0; v < n; ++v) scratch[v] = expf((l[v] - mx) / t);
+  for (int v = 0; v < n; ++v) w[v] = expf((l[v] - mx) / t);
+  if (top_p > 0.0f && top_p < 1.0f && n > 0) {
+    prob_idx* idx = (prob_idx*)malloc(sizeof(prob_idx) * (size_t)n);
+    unsigned long long total = 0;
+    for (int v = 0; v < n; ++v) {
+      idx[v].p = w[v];
+      idx[v].i = v;
+      total += (unsigned long long)(w[v] * 4294967296.0f);
+    }
+    qsort(idx, (size_t)n, sizeof(prob_idx), cmp_prob_desc);
+    const unsigned long long target = (unsigned long long)ceil((double)top_p * (double)total);
+    unsigned long long cum = 0;
+    int keep = 0;
+    while (keep < n) {
+      cum += (unsigned long long)(idx[keep].p * 4294967296.0f);
+      ++keep;
+      if (cum >= target) break;
+    }
+    for (int j = keep; j < n; ++j) w[idx[j].i] = 0.0f;
+    free(idx);
+  }
+  if (min_p > 0.0f && min_p < 1.0f)
+    for (int v = 0; v < n; ++v)
+      if (w[v] < min_p) w[v] = 0.0f;
+  float sum = 0.0f;
+  for (int v = 0; v < n; ++v) sum += w[v];
+  return sum;
+}
+
+static int sample_filt(const float* l, int n, float t, float top_p, float min_p, float u,
+                       float* scratch) {
+  const float s = oracle_filtered_weights(l, n, t, top_p, min_p, scratch);
   return inv_cdf(scratch, n, s, u);
+}
+
+/* One token from logits at temperature t (> 0) after top-p and min-p, with
+ * the uniform of (seed, round, slot); t <= 0 is greedy (generate.rs:948-969). */
+uint32_t oracle_sample_philox(const float* l, int n, float t, float top_p, float min_p,
+                              uint64_t seed, uint32_t round, uint32_t slot) {
+  if (n <= 0) return 0;
+  if (!(t > 0.0f)) return (uint32_t)oracle_argmax(l, n);
+  float* w = (float*)malloc(sizeof(float) * (size_t)n);
+  const int y = sample_filt(l, n, t, top_p, min_p, oracle_philox_uniform(seed, round, slot), w);
+  free(w);
+  return (uint32_t)y;
 }
 
 /* The transformer draft sampling gamma tokens at temperature t; q logits of
  * every step go to qlog[j * vocab]. */
 int oracle_llama_draft_sample(oracle_llama_draft* d, const uint32_t* ctx, int n, int gamma,
-                              float t, uint64_t seed, uint32_t round, uint32_t* out,
-                              float* qlog) {
+                              float t, float top_p, float min_p, uint64_t seed, uint32_t round,
+                              uint32_t* out, float* qlog) {
   if (n <= 0 || gamma <= 0) return 0;
   if (n + gamma > d->kv->cap) return 0;
   const int V = d->m->vocab;
@@ -1065,7 +1121,8 @@ int oracle_llama_draft_sample(oracle_llama_draft* d, const uint32_t* ctx, int n,
   for (int i = p; i < n; ++i) draft_step(d, ctx[i]);
   for (int j = 0; j < gamma; ++j) {
     memcpy(qlog + (size_t)j * V, d->logits, sizeof(float) * (size_t)V);
-    out[j] = (uint32_t)sample_temp(d->logits, V, t, oracle_philox_uniform(seed, round, (uint32_t)j), w);
+    out[j] = (uint32_t)sample_filt(d->logits, V, t, top_p, min_p,
+                                   oracle_philox_uniform(seed, round, (uint32_t)j), w);
     if (j + 1 < gamma) draft_step(d, out[j]);
   }
   free(w);
@@ -1077,7 +1134,9 @@ int oracle_llama_draft_sample(oracle_llama_draft* d, const uint32_t* ctx, int n,
  * of max(0, p_j - q_j) and end the round; accept_mode 1 (the reference's
  * rule, generate.rs:695-726): accept when the target's own sample at j equals
  * x, else emit that sample.  Round structure, prime (quirk Q1), budget check
- * and bonus as oracle_speculative_generate. */
+ * and bonus as oracle_speculative_generate.  Every distribution (draft q,
+ * target p, bonus) is softmax(l / T) after cfg->top_p and cfg->min_p as
+ * oracle_filtered_weights restates them. */
 int oracle_speculative_sample(const oracle_model* m, oracle_llama_draft* drafter,
                               const uint32_t* prompt, int n_prompt, const oracle_gen_cfg* cfg,
                               int accept_mode, uint32_t* out, int cap, int* accepted,
@@ -1095,8 +1154,11 @@ int oracle_speculative_sample(const oracle_model* m, oracle_llama_draft* drafter
   float* logits = (float*)malloc(sizeof(float) * (size_t)V);
   float* qlog = (float*)malloc(sizeof(float) * (size_t)V * (size_t)gamma);
   float* w = (float*)malloc(sizeof(float) * (size_t)V);
+  float* wp = (float*)malloc(sizeof(float) * (size_t)V);
+  float* wq = (float*)malloc(sizeof(float) * (size_t)V);
   float* e = (float*)malloc(sizeof(float) * (size_t)m->hidden);
   uint32_t* draft = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)gamma);
+  const float tp = cfg->top_p, mn = cfg->min_p;
   for (int i = 0; i < n_prompt; ++i) {
     oracle_token_embedding(m, prompt[i], e);
     oracle_forward(m, e, kv, logits);
@@ -1105,14 +1167,14 @@ int oracle_speculative_sample(const oracle_model* m, oracle_llama_draft* drafter
   while (len - prompt_len < cfg->max_tokens) {
     if (is_cancelled(cfg)) break;
     const uint32_t r = (uint32_t)rounds;
-    oracle_llama_draft_sample(drafter, tok, len, gamma, t, cfg->seed, r, draft, qlog);
+    oracle_llama_draft_sample(drafter, tok, len, gamma, t, tp, mn, cfg->seed, r, draft, qlog);
     int acc = 0;
     for (int j = 0; j < gamma; ++j) {
       oracle_token_embedding(m, tok[len - 1], e);
       oracle_forward(m, e, kv, logits);
       const float u_res = oracle_philox_uniform(cfg->seed, r, 64u + (uint32_t)j);
       if (accept_mode == 1) {
-        const int y = sample_temp(logits, V, t, u_res, w);
+        const int y = sample_filt(logits, V, t, tp, mn, u_res, w);
         if ((uint32_t)y == draft[j]) {
           tok[len++] = draft[j];
           acc++;
@@ -1121,12 +1183,11 @@ int oracle_speculative_sample(const oracle_model* m, oracle_llama_draft* drafter
         tok[len++] = (uint32_t)y;
         break;
       }
-      float mp, sp, mq, sq;
-      temp_stats(logits, V, t, &mp, &sp);
-      const float* q = qlog + (size_t)j * V;
-      temp_stats(q, V, t, &mq, &sq);
+      /* p and q after the same filters; the draft sampled x from q */
+      const float sp = oracle_filtered_weights(logits, V, t, tp, mn, wp);
+      const float sq = oracle_filtered_weights(qlog + (size_t)j * V, V, t, tp, mn, wq);
       const uint32_t x = draft[j];
-      const float ep = expf((logits[x] - mp) / t), eq = expf((q[x] - mq) / t);
+      const float ep = wp[x], eq = wq[x];
       const float u = oracle_philox_uniform(cfg->seed, r, 32u + (uint32_t)j);
       if (u * eq * sp < ep * sq) {
         tok[len++] = x;
@@ -1135,16 +1196,10 @@ int oracle_speculative_sample(const oracle_model* m, oracle_llama_draft* drafter
       }
       float rs = 0.0f;
       for (int v = 0; v < V; ++v) {
-        const float pv = expf((logits[v] - mp) / t) / sp, qv = expf((q[v] - mq) / t) / sq;
-        w[v] = fmaxf(pv - qv, 0.0f);
+        w[v] = fmaxf(wp[v] / sp - wq[v] / sq, 0.0f);
         rs += w[v];
       }
-      int y;
-      if (rs > 0.0f) {
-        y = inv_cdf(w, V, rs, u_res);
-      } else {
-        y = sample_temp(logits, V, t, u_res, w);
-      }
+      const int y = rs > 0.0f ? inv_cdf(w, V, rs, u_res) : inv_cdf(wp, V, sp, u_res);
       tok[len++] = (uint32_t)y;
       break;
     }
@@ -1152,7 +1207,7 @@ int oracle_speculative_sample(const oracle_model* m, oracle_llama_draft* drafter
       oracle_token_embedding(m, tok[len - 1], e);
       oracle_forward(m, e, kv, logits);
       const float u = oracle_philox_uniform(cfg->seed, r, 64u + (uint32_t)gamma);
-      tok[len++] = (uint32_t)sample_temp(logits, V, t, u, w);
+      tok[len++] = (uint32_t)sample_filt(logits, V, t, tp, mn, u, w);
     }
     if (accepted && rounds < rounds_cap) accepted[rounds] = acc;
     rounds++;
@@ -1162,6 +1217,6 @@ int oracle_speculative_sample(const oracle_model* m, oracle_llama_draft* drafter
   memcpy(out, tok + prompt_len, sizeof(uint32_t) * (size_t)ncopy);
   if (n_rounds) *n_rounds = rounds;
   oracle_kv_free(kv);
-  free(logits); free(qlog); free(w); free(e); free(draft); free(tok);
+  free(logits); free(qlog); free(w); free(wp); free(wq); free(e); free(draft); free(tok);
   return ncopy;
 }

@@ -166,9 +166,13 @@ int oracle_speculative_generate(const oracle_model* m, int draft_kind,
 /* ---------------- stochastic speculative sampling (not in the reference) */
 void oracle_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]);
 float oracle_philox_uniform(uint64_t seed, uint32_t round, uint32_t slot);
+float oracle_filtered_weights(const float* l, int n, float t, float top_p, float min_p,
+                              float* w);
+uint32_t oracle_sample_philox(const float* l, int n, float t, float top_p, float min_p,
+                              uint64_t seed, uint32_t round, uint32_t slot);
 int oracle_llama_draft_sample(oracle_llama_draft* d, const uint32_t* ctx, int n, int gamma,
-                              float t, uint64_t seed, uint32_t round, uint32_t* out,
-                              float* qlog);
+                              float t, float top_p, float min_p, uint64_t seed, uint32_t round,
+                              uint32_t* out, float* qlog);
 int oracle_speculative_sample(const oracle_model* m, oracle_llama_draft* drafter,
                               const uint32_t* prompt, int n_prompt, const oracle_gen_cfg* cfg,
                               int accept_mode, uint32_t* out, int cap, int* accepted,

@@ -114,6 +114,12 @@ def lib():
         L.oracle_philox4x32_10.argtypes = [_u32p, _u32p, _u32p]
         L.oracle_philox_uniform.restype = C.c_float
         L.oracle_philox_uniform.argtypes = [C.c_uint64, C.c_uint32, C.c_uint32]
+        L.oracle_filtered_weights.restype = C.c_float
+        L.oracle_filtered_weights.argtypes = [_fp, C.c_int, C.c_float, C.c_float, C.c_float,
+                                              _fp]
+        L.oracle_sample_philox.restype = C.c_uint32
+        L.oracle_sample_philox.argtypes = [_fp, C.c_int, C.c_float, C.c_float, C.c_float,
+                                           C.c_uint64, C.c_uint32, C.c_uint32]
         L.oracle_speculative_sample.argtypes = [
             C.POINTER(Model), C.c_void_p, _u32p, C.c_int, C.POINTER(GenCfg), C.c_int, _u32p,
             C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_int]
@@ -387,12 +393,14 @@ class OracleModel:
 
 
     def speculative_sample(self, prompt, max_tokens, gamma, draft, temperature, seed,
-                           accept_mode=0, bonus=False):
+                           accept_mode=0, bonus=False, top_p=0.0, min_p=0.0):
         """Stochastic speculative decoding with a sampling transformer draft
         (accept_mode 0: min(1, p/q) with residual resampling; 1: the
-        reference's target-sample == draft rule).  Returns (tokens, accepted)."""
+        reference's target-sample == draft rule), every distribution after
+        top-p and min-p as filtered_weights states them.  Returns (tokens,
+        accepted)."""
         prompt = np.ascontiguousarray(np.asarray(prompt, np.uint32))
-        cfg = self._cfg(max_tokens, temperature, gamma, seed, 0.0, 0.0, 0, int(bonus))
+        cfg = self._cfg(max_tokens, temperature, gamma, seed, top_p, min_p, 0, int(bonus))
         cap = max_tokens + gamma + 2
         out = np.zeros(cap, np.uint32)
         acc = (C.c_int * (cap + 1))()
@@ -413,6 +421,24 @@ def philox4x32_10(ctr, key):
 
 def philox_uniform(seed, rnd, slot):
     return float(lib().oracle_philox_uniform(seed, rnd, slot))
+
+
+def filtered_weights(logits, temperature, top_p=0.0, min_p=0.0):
+    """exp((l - max) / T) with the top-p and min-p filters applied
+    (mc_oracle.c oracle_filtered_weights); returns (weights, their sum)."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    w = np.empty_like(logits)
+    s = lib().oracle_filtered_weights(fptr(logits), len(logits), temperature, top_p, min_p,
+                                      fptr(w))
+    return w, float(s)
+
+
+def sample_philox(logits, temperature, seed, rnd, slot, top_p=0.0, min_p=0.0):
+    """One token of logits after the filters, with the Philox uniform of
+    (seed, rnd, slot); greedy at temperature <= 0."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    return int(lib().oracle_sample_philox(fptr(logits), len(logits), temperature, top_p,
+                                          min_p, seed, rnd, slot))
 
 
 class OracleKV:
