@@ -1016,30 +1016,83 @@ float oracle_philox_uniform(uint64_t seed, uint32_t round, uint32_t slot) {
   return (float)(o[0] >> 8) * (1.0f / 16777216.0f);
 }
 
-/* max and sum of e_v = exp((l_v - max) / T), sequential. */
-static void temp_stats(const float* l, int n, float t, float* mx, float* sum) {
-  float m = -INFINITY;
-  for (int v = 0; v < n; ++v)
-    if (l[v] > m) m = l[v];
-  float s = 0.0f;
-  for (int v = 0; v < n; ++v) s += expf((l[v] - m) / t);
-  *mx = m;
-  *sum = s;
+/* The device sampler's fixed summation order, which this stochastic scheme
+ * defines (it is not the reference's): weights in tiles of 1024 elements;
+ * in a tile, lane l (0..31) adds elements 32 i + l for i = 0..31 in order,
+ * then the 32 lane sums meet in an xor butterfly (offsets 16, 8, 4, 2, 1);
+ * the tile sums are added in tile order. */
+#define DEV_TILE 1024
+static float dev_tile_sum(const float* w, int n, int tile, int* last) {
+  float s[32], t[32];
+  int lst = -1;
+  for (int l = 0; l < 32; ++l) {
+    float acc = 0.0f;
+    for (int i = 0; i < 32; ++i) {
+      const int v = tile * DEV_TILE + i * 32 + l;
+      if (v < n) {
+        acc += w[v];
+        if (w[v] > 0.0f && v > lst) lst = v;
+      }
+    }
+    s[l] = acc;
+  }
+  for (int o = 16; o; o >>= 1) {
+    for (int l = 0; l < 32; ++l) t[l] = s[l] + s[l ^ o];
+    memcpy(s, t, sizeof(s));
+  }
+  *last = lst;
+  return s[0];
 }
 
-/* Inverse CDF over non-negative weights w (total s): the first v whose
- * running sum exceeds u * s; the last positive weight if rounding leaves
- * none. */
+static float dev_sum(const float* w, int n) {
+  float tot = 0.0f;
+  int last;
+  for (int t = 0; t * DEV_TILE < n; ++t) tot += dev_tile_sum(w, n, t, &last);
+  return tot;
+}
+
+/* Inverse CDF over non-negative weights w with total s (dev_sum), as the
+ * device walks it: tau = u * s; the first tile whose running tile sum
+ * exceeds tau; inside it, 32-element rows scanned across lanes by the
+ * Hillis-Steele inclusive scan (offsets 1, 2, 4, 8, 16), the first positive
+ * element whose running sum exceeds the remainder.  If rounding leaves no
+ * such element: the last positive element of that tile, else of the row. */
 static int inv_cdf(const float* w, int n, float s, float u) {
+  const int nt = (n + DEV_TILE - 1) / DEV_TILE;
+  float tile[256];
+  int tlast[256];
+  for (int t = 0; t < nt; ++t) tile[t] = dev_tile_sum(w, n, t, &tlast[t]);
   const float tau = u * s;
   float c = 0.0f;
-  int last = 0;
-  for (int v = 0; v < n; ++v) {
-    if (w[v] > 0.0f) last = v;
-    c += w[v];
-    if (c > tau) return v;
+  int kt = -1, fallback = -1;
+  for (int t = 0; t < nt; ++t) {
+    if (tlast[t] >= 0) fallback = tlast[t];
+    if (kt < 0 && c + tile[t] > tau) {
+      kt = t;
+    } else if (kt < 0) {
+      c += tile[t];
+    }
   }
-  return last;
+  if (fallback < 0) fallback = 0;
+  if (kt < 0) return fallback;
+  const float rem = tau - c;
+  float run = 0.0f;
+  for (int i = 0; i < 32; ++i) {
+    float x[32], sc[32], nx[32];
+    for (int l = 0; l < 32; ++l) {
+      const int v = kt * DEV_TILE + i * 32 + l;
+      x[l] = v < n ? w[v] : 0.0f;
+      sc[l] = x[l];
+    }
+    for (int o = 1; o < 32; o <<= 1) {
+      for (int l = 0; l < 32; ++l) nx[l] = l >= o ? sc[l] + sc[l - o] : sc[l];
+      memcpy(sc, nx, sizeof(sc));
+    }
+    for (int l = 0; l < 32; ++l)
+      if (run + sc[l] > rem && x[l] > 0.0f) return kt * DEV_TILE + i * 32 + l;
+    run += sc[31];
+  }
+  return tlast[kt] >= 0 ? tlast[kt] : fallback;
 }
 
 /* Weights of softmax(l / T) after top-p (generate.rs:1034-1063) and min-p
@@ -1052,12 +1105,13 @@ static int inv_cdf(const float* w, int n, float s, float u) {
  *   min-p (0 < min_p < 1): drop v with e_v < min_p (p_v < min_p * max_v p_v
  *     with max e = 1), applied after top-p as the reference does.
  * The renormalisations of the reference are left to the sampler, which
- * draws from unnormalised weights.  Returns the sum of the weights in index
- * order. */
+ * draws from unnormalised weights.  Returns the sum of the weights in the
+ * device sampler's order (dev_sum). */
 float oracle_filtered_weights(const float* l, int n, float t, float top_p, float min_p,
                               float* w) {
-  float mx, s;
-  temp_stats(l, n, t, &mx, &s);
+  float mx = -INFINITY;
+  for (int v = 0; v < n; ++v)
+    if (l[v] > mx) mx = l[v];
   for (int v = 0; v < n; ++v) w[v] = expf((l[v] - mx) / t);
   if (top_p > 0.0f && top_p < 1.0f && n > 0) {
     prob_idx* idx = (prob_idx*)malloc(sizeof(prob_idx) * (size_t)n);
@@ -1082,9 +1136,7 @@ float oracle_filtered_weights(const float* l, int n, float t, float top_p, float
   if (min_p > 0.0f && min_p < 1.0f)
     for (int v = 0; v < n; ++v)
       if (w[v] < min_p) w[v] = 0.0f;
-  float sum = 0.0f;
-  for (int v = 0; v < n; ++v) sum += w[v];
-  return sum;
+  return dev_sum(w, n);
 }
 
 static int sample_filt(const float* l, int n, float t, float top_p, float min_p, float u,
@@ -1194,11 +1246,8 @@ int oracle_speculative_sample(const oracle_model* m, oracle_llama_draft* drafter
         acc++;
         continue;
       }
-      float rs = 0.0f;
-      for (int v = 0; v < V; ++v) {
-        w[v] = fmaxf(wp[v] / sp - wq[v] / sq, 0.0f);
-        rs += w[v];
-      }
+      for (int v = 0; v < V; ++v) w[v] = fmaxf(wp[v] / sp - wq[v] / sq, 0.0f);
+      const float rs = dev_sum(w, V);
       const int y = rs > 0.0f ? inv_cdf(w, V, rs, u_res) : inv_cdf(wp, V, sp, u_res);
       tok[len++] = (uint32_t)y;
       break;
