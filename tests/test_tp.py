@@ -7,11 +7,11 @@ and down (partial sums + one all-reduce), and the vocab-parallel LM head
 whose per-rank argmax keys merge with a MAX all-reduce into the global
 first-index argmax (generate.rs:1088-1098 tie rule).
 
-GPU (needs 2 devices; skipped otherwise): two ranks, each with its shard of
-the target and a replicated draft, decode greedily - with NCCL all-reduces
-in the round graph, and with the fused NVLink reduction (partial rows stored
-into every rank's buffer by the GEMV) - and produce exactly the oracle's
-tokens and accepted counts.
+GPU (2, 4 and 8 ranks, each skipped without that many devices): every rank
+holds its shard of the target and a replicated draft and decodes greedily -
+with NCCL all-reduces in the round graph, and with the fused NVLink
+reduction (partial rows stored into every rank's buffer by the GEMV) - and
+produces exactly the oracle's tokens and accepted counts.
 """
 import os
 import sys
@@ -127,17 +127,24 @@ def _gpu_rank(rank, world, uid, cfg_args, prompt, gamma, fused, port, q):
         dist.destroy_process_group()
 
 
+# per world size: a GQA shape whose heads, KV heads and FFN rows divide
+# evenly (8 ranks: one KV head each; vocab shards of uneven stripe counts)
+TP_CFGS = {2: (2, 128, 4, 2, 32, 192, 260), 4: (2, 256, 8, 4, 32, 384, 520),
+           8: (2, 256, 8, 8, 32, 512, 1032)}
+
+
 @pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("fused", [False, True], ids=["nccl", "fused-nvlink"])
-def test_tp2_spec_decode_matches_oracle(fused):
+def test_tp_spec_decode_matches_oracle(world, fused):
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     import oracle as o
     import modelc_b200 as mb
     from modelc_b200.model import LlamaConfig, MODE_GENERAL
-    cfg = LlamaConfig(2, 128, 4, 2, 32, 192, 260, 500000.0, 1e-5, MODE_GENERAL, "tp-gqa")
+    cfg = LlamaConfig(*TP_CFGS[world], 500000.0, 1e-5, MODE_GENERAL, f"tp{world}-gqa")
     prompt = np.random.default_rng(11).integers(0, cfg.vocab, 13).tolist()
     tw = mb.synth_weights(cfg, seed=0)
     dw = mb.synth_weights(cfg.with_layers(1), seed=1)
@@ -154,9 +161,9 @@ def test_tp2_spec_decode_matches_oracle(fused):
     q = ctx.Queue()
     args = (cfg.n_layers, cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn,
             cfg.vocab, cfg.rope_theta, cfg.eps, cfg.mode, cfg.name)
-    port = 31000 + (os.getpid() % 2000) + (7 if fused else 0)
-    procs = [ctx.Process(target=_gpu_rank, args=(r, 2, uid, args, prompt, 4, fused, port, q))
-             for r in range(2)]
+    port = 31000 + (os.getpid() % 2000) + (7 if fused else 0) + 13 * world
+    procs = [ctx.Process(target=_gpu_rank, args=(r, world, uid, args, prompt, 4, fused, port, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
