@@ -10,6 +10,10 @@
  *     number of sessions and host threads (the reference's RwLock<Runtime>).
  *   - mc_session owns one request's KV cache, draft state and stream; it is
  *     not thread-safe: one host thread per session (one KvCache per request).
+ * Entry points that touch a device make that device (the handle's, or the
+ * one mc_sample_rows' pointers live on) current for the calling thread and
+ * leave it current; a host thread that drives several devices selects its
+ * own device again afterwards.
  * All functions return MC_OK (0) or a negative mc_status; mc_last_error()
  * returns the calling thread's last error message.  There is no CPU
  * fallback: without a usable sm_100 device every entry point fails with

@@ -1322,14 +1322,33 @@ constexpr int kAttnThreads = 512;
 // e^(m_c - M) * (sum_t e^(s_t - m_c) v_t) to the numerator and
 // e^(m_c - M) * l_c to the denominator; fully masked pages (m_c = -inf)
 // contribute exactly zero.  Then thread -> 4 columns of one row, pages summed
-// in order with eight float4 loads in flight; Rp (>= R) is a multiple of the
-// rows a warp spans, so the row loop and the shuffles stay warp-uniform.
+// in order with eight float4 loads in flight (the first kPre pages of the
+// thread's first row loaded before the weights); Rp (>= R) is a multiple of
+// the rows a warp spans, so the row loop and the shuffles stay warp-uniform.
 // wgt: shared [R][n_chunks]; s_l: shared [>= R]; s_mx: shared [>= Mq].
+template <int kPre>
 __device__ __forceinline__ void attn_combine(const AttnArgs& a, int kvh, int cslot, int n_chunks,
                                              int R, int Rp, int Rs, int G, int mt0, int Mq,
                                              float* wgt, float* s_l, uint32_t* s_mx) {
   const int hdp = a.hdp;
   const int nthr = blockDim.x;
+  const int h4 = hdp >> 2;
+  const int RGc = nthr / h4;
+  const int c4 = threadIdx.x % h4;
+  const int row0 = threadIdx.x / h4;  // this thread's first output row
+  const float4* base =
+      reinterpret_cast<const float4*>(a.part_o) + (size_t)cslot * a.max_chunks * Rs * h4 + c4;
+  const size_t cs4 = (size_t)Rs * h4;
+  // the first kPre pages of that row do not depend on the weights: their
+  // loads overlap the weight computation below
+  float4 pre[kPre > 0 ? kPre : 1];
+  {
+    const float4* src = base + (size_t)min(row0, R - 1) * h4;
+#pragma unroll
+    for (int u = 0; u < kPre; ++u)
+      pre[u] = (u < n_chunks && row0 < Rp) ? __ldcg(src + (size_t)u * cs4)
+                                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
   {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float2* ml = reinterpret_cast<const float2*>(a.part_ml) + (size_t)cslot * a.max_chunks * Rs;
@@ -1353,20 +1372,26 @@ __device__ __forceinline__ void attn_combine(const AttnArgs& a, int kvh, int csl
   for (int i = threadIdx.x; i < Mq; i += nthr) s_mx[i] = 0u;
   __syncthreads();
   {
-    const int h4 = hdp >> 2;
-    const int RGc = nthr / h4;
-    const int c4 = threadIdx.x % h4;
     const int seg = min(h4, 32);  // lanes of a warp that share a row
-    const float4* base =
-        reinterpret_cast<const float4*>(a.part_o) + (size_t)cslot * a.max_chunks * Rs * h4 + c4;
-    const size_t cs4 = (size_t)Rs * h4;
-    for (int row = threadIdx.x / h4; row < Rp; row += RGc) {
+    for (int row = row0; row < Rp; row += RGc) {
       const bool live = row < R;
       const int rr = live ? row : R - 1;
       const float* wr = wgt + rr * n_chunks;
       const float4* src = base + (size_t)rr * h4;
       float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       int ch = 0;
+      if (kPre > 0 && row == row0) {  // pages 0..kPre-1 came in with the weights
+#pragma unroll
+        for (int u = 0; u < kPre; ++u)
+          if (u < n_chunks) {
+            const float w = wr[u];
+            acc.x = __fmaf_rn(pre[u].x, w, acc.x);
+            acc.y = __fmaf_rn(pre[u].y, w, acc.y);
+            acc.z = __fmaf_rn(pre[u].z, w, acc.z);
+            acc.w = __fmaf_rn(pre[u].w, w, acc.w);
+          }
+        ch = min(n_chunks, kPre);
+      }
       for (; ch + 8 <= n_chunks; ch += 8) {
         float4 v[8];
 #pragma unroll
@@ -1421,6 +1446,14 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
                    (uint32_t)__cvta_generic_to_shared(smem_dst)),
                "l"(gsrc)
                : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// Wait until at most N of this thread's committed copy groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
@@ -1611,7 +1644,7 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) k_attention(AttnArgs a) {
     return;
   }
   __shared__ uint32_t s_mx[128];  // max |out| per token of the block, float bits
-  attn_combine(a, kvh, cslot, n_chunks, R, Rp, Rs, G, mt0, Mq, ss, s_l, s_mx);
+  attn_combine<0>(a, kvh, cslot, n_chunks, R, Rp, Rs, G, mt0, Mq, ss, s_l, s_mx);
   MC_TRACE_PHASE(a.trace_slot, 7, mc_tp);
   MC_TRACE_END(a.trace_slot);
 }
@@ -1705,11 +1738,18 @@ __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_t
     const float4* kbase = reinterpret_cast<const float4*>(a.kc + ((size_t)pg * a.Hkv + kvh) * P * HD);
     const float4* vbase = reinterpret_cast<const float4*>(a.vc + ((size_t)pg * a.Hkv + kvh) * P * HD);
     constexpr int H4 = HD / 4;
+    // two copy groups: K (needed by the scores) then V (needed after the
+    // softmax), so the V copies land while the scores are computed
     for (int i = threadIdx.x; i < nt * H4; i += kAttnTcThreads) {
       const int t = i / H4, c4 = i - t * H4;
       cp_async16(sK + t * KS + 4 * c4, kbase + i);
+    }
+    cp_async_commit();
+    for (int i = threadIdx.x; i < nt * H4; i += kAttnTcThreads) {
+      const int t = i / H4, c4 = i - t * H4;
       cp_async16(sV + t * VS + 4 * c4, vbase + i);
     }
+    cp_async_commit();
     // rows past the page's last position: zero K and V (probability 0 times
     // stale data could be NaN); their scores are masked
     for (int i = nt * H4 + threadIdx.x; i < P * H4; i += kAttnTcThreads) {
@@ -1736,7 +1776,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_t
     sQ[row * KS + c] = __uint_as_float(h);
     sQl[row * KS + c] = __uint_as_float(l);
   }
-  cp_async_wait_all();
+  cp_async_wait_group<1>();  // K landed (V may still be in flight)
   __syncthreads();
   MC_TRACE_PHASE(a.trace_slot, 1, mc_tp);
   // scores: MMA warp w -> positions 8 w .. 8 w + 7 (one n-tile) of every row;
@@ -1826,6 +1866,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_t
         if (tq == 0) s_red[warp][row] = sum;
       }
   }
+  cp_async_wait_group<0>();  // V landed; the barrier publishes it with sP
   __syncthreads();
   if (threadIdx.x < RM) {
     float l = s_red[0][threadIdx.x];
@@ -1905,7 +1946,9 @@ __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_t
   const int h4 = HD / 4;
   const int span = h4 >= 32 ? 1 : 32 / h4;  // rows one warp spans in the column pass
   const int Rpc = (R + span - 1) / span * span;
-  attn_combine(a, kvh, cslot, n_chunks, R, Rpc, Rs, G, mt0, Mq, asmem, s_l, s_mx);
+  // (pages preloaded where the registers allow it without spilling)
+  attn_combine<HD == 128 ? 4 : 0>(a, kvh, cslot, n_chunks, R, Rpc, Rs, G, mt0, Mq, asmem, s_l,
+                                  s_mx);
   MC_TRACE_PHASE(a.trace_slot, 7, mc_tp);
   MC_TRACE_END(a.trace_slot);
 }
@@ -2081,22 +2124,42 @@ __global__ void __launch_bounds__(256) k_embed(EmbedArgs a) {
   const int8_t* q = (in && !q4) ? a.emb_q + (size_t)id * a.d : nullptr;
   const uint8_t* q4row = (in && q4) ? a.emb_q4 + (size_t)id * (a.d / 32) * kQ4BlockBytes : nullptr;
   const float sc = (in && !q4) ? a.emb_scale[id] : 0.0f;
-  for (int i = threadIdx.x; i < a.d; i += blockDim.x) {
-    float v = 0.0f;
-    if (q4row) {
-      // dequantize_q4_0 (dequant.rs:33-44): (code - 8) as f32 * d
-      const uint8_t* blk = q4row + (i >> 5) * kQ4BlockBytes;
-      const int j = i & 31;
-      const uint32_t byte = blk[2 + (j & 15)];
-      const int code = (int)(j < 16 ? (byte & 0x0Fu) : (byte >> 4)) - 8;
-      const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
-      v = __fmul_rn((float)code, d);
-    } else if (q) {
-      v = __fmul_rn((float)q[i], sc);
+  // the row is read from HBM: a batch of kEmbBatch elements per thread has
+  // all its loads in flight before the first use; the sums keep the
+  // element order i = tid, tid + 256, ...
+  constexpr int kEmbBatch = 16;
+  for (int i0 = threadIdx.x; i0 < a.d; i0 += blockDim.x * kEmbBatch) {
+    float v[kEmbBatch], wv[kEmbBatch];
+#pragma unroll
+    for (int u = 0; u < kEmbBatch; ++u) {
+      const int i = i0 + u * blockDim.x;
+      v[u] = 0.0f;
+      wv[u] = 1.0f;
+      if (i < a.d) {
+        if (q4row) {
+          // dequantize_q4_0 (dequant.rs:33-44): (code - 8) as f32 * d
+          const uint8_t* blk = q4row + (i >> 5) * kQ4BlockBytes;
+          const int j = i & 31;
+          const uint32_t byte = blk[2 + (j & 15)];
+          const int code = (int)(j < 16 ? (byte & 0x0Fu) : (byte >> 4)) - 8;
+          const float dq =
+              __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+          v[u] = __fmul_rn((float)code, dq);
+        } else if (q) {
+          v[u] = __fmul_rn((float)q[i], sc);
+        }
+        if (a.st_w) wv[u] = a.st_w[i];
+      }
     }
-    h[i] = v;
-    ss = __fadd_rn(ss, __fmul_rn(v, v));
-    mx = max(mx, __float_as_uint(fabsf(__fmul_rn(v, a.st_w ? a.st_w[i] : 1.0f))));
+#pragma unroll
+    for (int u = 0; u < kEmbBatch; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i < a.d) {
+        h[i] = v[u];
+        ss = __fadd_rn(ss, __fmul_rn(v[u], v[u]));
+        mx = max(mx, __float_as_uint(fabsf(__fmul_rn(v[u], wv[u]))));
+      }
+    }
   }
   if (m == 0)
     for (int j = threadIdx.x; j < a.n_zero; j += blockDim.x) a.zero_keys[key_slot(a.seq, j)] = 0ull;
