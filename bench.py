@@ -510,12 +510,16 @@ def run_timeline(args):
                "tmem read + push", "pushes landed", "sums + epilogue", "end barrier"]
     attn_ph = ["launch->wait", "load K/V/q", "scores + softmax", "P.V", "partials out",
                "arrive", "-", "combine (last CTA)"]
-    for kind in ["qkv", "o", "gu", "down", "head", "attention"]:
+    quant_ph = ["launch->wait", "producer stats in", "barrier", "encode + stores", "-", "-",
+                "-", "-"]
+    for kind in ["qkv", "o", "gu", "down", "head", "attention", "quant_attn", "quant_o",
+                 "quant_mlp", "quant_act"]:
         idx = [i for i, nm in enumerate(names) if nm == kind]
         sums, cnts = ph[idx, :8].sum(0), ph[idx, 8:].sum(0)
         if cnts.sum() == 0:
             continue
-        labels = attn_ph if kind == "attention" else gemm_ph
+        labels = (attn_ph if kind == "attention" else
+                  quant_ph if kind.startswith("quant") else gemm_ph)
         print(f"{kind} phases (avg us per CTA reaching it; CTAs per launch):")
         for k in range(8):
             if cnts[k]:

@@ -1157,6 +1157,7 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
   grid_launch_dependents();
   grid_wait();
   MC_TRACE_WAITED(a.trace_slot);
+  MC_TRACE_PHASE(a.trace_slot, 0, mc_tp);
   const StatArgs sa{a.h, a.ld, a.d, a.M, a.w, a.wlen, a.eps, a.do_norm};
   // this CTA's k-blocks
   const int kbs = (a.KB + gridDim.x - 1) / gridDim.x;
@@ -1204,10 +1205,13 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
       }
     }
     if (blockIdx.x == 0 && a.amax_next && threadIdx.x < kMaxTokens) a.amax_next[threadIdx.x] = 0u;
+    MC_TRACE_PHASE(a.trace_slot, 1, mc_tp);
     __syncthreads();
+    MC_TRACE_PHASE(a.trace_slot, 2, mc_tp);
     if (blockIdx.x == 0 && threadIdx.x < a.M) a.xexp[threadIdx.x] = s_e[threadIdx.x];
     encode_digits(sa, a.nt, a.KB, kb0, kb1, s_mul, s_e, src4,
                   [&](size_t wi, uint32_t v) { xq[wi] = v; }, a.tc_layout != 0);
+    MC_TRACE_PHASE(a.trace_slot, 3, mc_tp);
     MC_TRACE_END(a.trace_slot);
     return;
   } else {
