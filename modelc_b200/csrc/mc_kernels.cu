@@ -487,6 +487,95 @@ __device__ __forceinline__ void encode_digits(const StatArgs& a, int nt, int KB,
   }
 }
 
+// encode_digits for an encoder whose statistics come from the producer:
+// the first batch's activations and RMSNorm weights do not depend on those
+// statistics, so they are loaded before ready() (which computes s_mul / s_e
+// and ends with a block barrier) and their round trip overlaps it.  The
+// digits are those of encode_digits, bit for bit.
+template <class Src4, class Dst, class Ready>
+__device__ __forceinline__ void encode_digits_early(const StatArgs& a, int nt, int KB, int kb0,
+                                                    int kb1, const float* s_mul, const int* s_e,
+                                                    Src4 src4, Dst dst, bool tc, Ready ready) {
+  const int M = a.M, d = a.d;
+  const int groups = groups_for_tokens(M);
+  const int pad_cols = 8 * nt * groups - 3 * M;
+  const int ngroups = (kb1 - kb0) * 8;
+  const int tasks = ngroups * (M + pad_cols);
+  const bool use_w = a.do_norm && a.w;
+  float4 v[kEncBatch], wv[kEncBatch];
+  auto load = [&](int t0) {
+#pragma unroll
+    for (int u = 0; u < kEncBatch; ++u) {
+      const int task = t0 + u * blockDim.x;
+      v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      wv[u] = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+      if (task < tasks) {
+        const int grp = task % ngroups, q = task / ngroups;
+        if (q < M) {
+          const int k = (kb0 + (grp >> 3)) * 32 + (grp & 7) * 4;
+          v[u] = src4(q, k);
+          if (use_w) {
+            const float* wp = a.w + k;
+            if (k + 3 < a.wlen && ((reinterpret_cast<uintptr_t>(wp) & 15) == 0)) {
+              wv[u] = __ldg(reinterpret_cast<const float4*>(wp));
+            } else {
+              wv[u].x = k < a.wlen ? __ldg(wp) : 1.0f;
+              wv[u].y = k + 1 < a.wlen ? __ldg(wp + 1) : 1.0f;
+              wv[u].z = k + 2 < a.wlen ? __ldg(wp + 2) : 1.0f;
+              wv[u].w = k + 3 < a.wlen ? __ldg(wp + 3) : 1.0f;
+            }
+          }
+        }
+      }
+    }
+  };
+  load(threadIdx.x);
+  ready();
+  for (int t0 = threadIdx.x; t0 < tasks; t0 += blockDim.x * kEncBatch) {
+    if (t0 != (int)threadIdx.x) load(t0);
+#pragma unroll
+    for (int u = 0; u < kEncBatch; ++u) {
+      const int task = t0 + u * blockDim.x;
+      if (task >= tasks) continue;
+      const int grp = task % ngroups;
+      const int q = task / ngroups;  // token (q < M) or padding column (q >= M)
+      const int kb = kb0 + (grp >> 3);
+      const int kk = (grp & 7) * 4;
+      if (q >= M) {
+        dst(digit_index(kb, 3 * M + (q - M), kk, nt, groups, KB, tc), 0u);
+        continue;
+      }
+      const int m = q;
+      uint32_t w0 = 0, w1 = 0, w2 = 0;
+      if (s_e[m] != kExpNonFinite) {
+        const float mul = s_mul[m];
+        const float vv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        const float ww[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int k = kb * 32 + kk + j;
+          int X = 0;
+          if (k < d) {
+            float x = vv[j];
+            if (a.do_norm) x = __fmul_rn(x, ww[j]);
+            X = __float2int_rn(__fmul_rn(x, mul));
+          }
+          const int d2 = ((X + 64) & 127) - 64;
+          const int X1 = (X - d2) >> 7;
+          const int d1 = ((X1 + 64) & 127) - 64;
+          const int d0 = (X1 - d1) >> 7;
+          w0 |= (uint32_t)(d0 & 0xff) << (8 * j);
+          w1 |= (uint32_t)(d1 & 0xff) << (8 * j);
+          w2 |= (uint32_t)(d2 & 0xff) << (8 * j);
+        }
+      }
+      const uint32_t wd[3] = {w0, w1, w2};
+#pragma unroll
+      for (int dg = 0; dg < 3; ++dg) dst(digit_index(kb, 3 * m + dg, kk, nt, groups, KB, tc), wd[dg]);
+    }
+  }
+}
+
 // Four consecutive activations of token m starting at k (k % 4 == 0), zero
 // past d; vectorised when the row is float4-aligned.  Read through L2: the
 // producing kernel may have finished after this grid was scheduled.
@@ -1166,51 +1255,53 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
   uint32_t* xq = reinterpret_cast<uint32_t*>(a.xq);
   if constexpr (STATS) {
     auto src4 = [&](int m, int k) { return load_act4(a.h, a.ld, a.d, m, k); };
-    // statistics from the producing kernel: one warp per token sums the
-    // partials in a fixed order (lane-strided, then an xor-shuffle tree)
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int m = warp; m < a.M; m += blockDim.x >> 5) {
-      const unsigned mxb = lane == 0 ? __ldcg(a.amax + m) : 0u;  // issued with the partials
-      float ss = 0.0f;
-      if (a.do_norm) {
-        // the lane's partials j = lane, lane + 32, ... in batches of 8 whose
-        // loads are all in flight before the (in-order) adds
-        const float* pr = a.pss + (size_t)m * a.np_stride;
-        for (int j0 = lane; j0 < a.np; j0 += 32 * 8) {
-          float v[8];
+    auto ready = [&]() {
+      // statistics from the producing kernel: one warp per token sums the
+      // partials in a fixed order (lane-strided, then an xor-shuffle tree)
+      const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+      for (int m = warp; m < a.M; m += blockDim.x >> 5) {
+        const unsigned mxb = lane == 0 ? __ldcg(a.amax + m) : 0u;  // issued with the partials
+        float ss = 0.0f;
+        if (a.do_norm) {
+          // the lane's partials j = lane, lane + 32, ... in batches of 8 whose
+          // loads are all in flight before the (in-order) adds
+          const float* pr = a.pss + (size_t)m * a.np_stride;
+          for (int j0 = lane; j0 < a.np; j0 += 32 * 8) {
+            float v[8];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) v[u] = j0 + 32 * u < a.np ? __ldcg(pr + j0 + 32 * u) : 0.0f;
+            for (int u = 0; u < 8; ++u) v[u] = j0 + 32 * u < a.np ? __ldcg(pr + j0 + 32 * u) : 0.0f;
 #pragma unroll
-          for (int u = 0; u < 8; ++u)
-            if (j0 + 32 * u < a.np) ss = __fadd_rn(ss, v[u]);
+            for (int u = 0; u < 8; ++u)
+              if (j0 + 32 * u < a.np) ss = __fadd_rn(ss, v[u]);
+          }
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+        if (lane == 0) {
+          const float mx = __uint_as_float(mxb);
+          float rms = 1.0f;
+          if (a.do_norm) rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)(a.d > 1 ? a.d : 1)), a.eps));
+          const float amax = a.do_norm ? mx / rms : mx;
+          int e = 0;
+          if (!isfinite(amax)) {  // a NaN/inf element makes the bit-max non-finite
+            e = kExpNonFinite;
+          } else if (amax > 0.0f) {
+            int E;
+            frexpf(amax * 1.0000002f, &E);
+            e = 20 - E;
+          }
+          s_mul[m] = (e != kExpNonFinite) ? ldexpf(a.do_norm ? 1.0f / rms : 1.0f, e) : 0.0f;
+          s_e[m] = e;
         }
       }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-      if (lane == 0) {
-        const float mx = __uint_as_float(mxb);
-        float rms = 1.0f;
-        if (a.do_norm) rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)(a.d > 1 ? a.d : 1)), a.eps));
-        const float amax = a.do_norm ? mx / rms : mx;
-        int e = 0;
-        if (!isfinite(amax)) {  // a NaN/inf element makes the bit-max non-finite
-          e = kExpNonFinite;
-        } else if (amax > 0.0f) {
-          int E;
-          frexpf(amax * 1.0000002f, &E);
-          e = 20 - E;
-        }
-        s_mul[m] = (e != kExpNonFinite) ? ldexpf(a.do_norm ? 1.0f / rms : 1.0f, e) : 0.0f;
-        s_e[m] = e;
-      }
-    }
-    if (blockIdx.x == 0 && a.amax_next && threadIdx.x < kMaxTokens) a.amax_next[threadIdx.x] = 0u;
-    MC_TRACE_PHASE(a.trace_slot, 1, mc_tp);
-    __syncthreads();
-    MC_TRACE_PHASE(a.trace_slot, 2, mc_tp);
-    if (blockIdx.x == 0 && threadIdx.x < a.M) a.xexp[threadIdx.x] = s_e[threadIdx.x];
-    encode_digits(sa, a.nt, a.KB, kb0, kb1, s_mul, s_e, src4,
-                  [&](size_t wi, uint32_t v) { xq[wi] = v; }, a.tc_layout != 0);
+      if (blockIdx.x == 0 && a.amax_next && threadIdx.x < kMaxTokens) a.amax_next[threadIdx.x] = 0u;
+      MC_TRACE_PHASE(a.trace_slot, 1, mc_tp);
+      __syncthreads();
+      MC_TRACE_PHASE(a.trace_slot, 2, mc_tp);
+      if (blockIdx.x == 0 && threadIdx.x < a.M) a.xexp[threadIdx.x] = s_e[threadIdx.x];
+    };
+    encode_digits_early(sa, a.nt, a.KB, kb0, kb1, s_mul, s_e, src4,
+                        [&](size_t wi, uint32_t v) { xq[wi] = v; }, a.tc_layout != 0, ready);
     MC_TRACE_PHASE(a.trace_slot, 3, mc_tp);
     MC_TRACE_END(a.trace_slot);
     return;
