@@ -1174,7 +1174,7 @@ static mc_status enq_gemv(mc_session* s, const PMat& W, int epi, int M, GemvArgs
 // slots sm maps (one sequence: sm.seq_len = M).
 static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv, int M,
                              SeqMap sm, EmbedArgs ea, const int* pos_ptr, int pos_add,
-                             unsigned long long* keys, float* logits_dev) {
+                             unsigned long long* keys, float* logits_dev, bool kv_pre = false) {
   if (M < 1 || M > kMaxTokens || sm.seq_len < 1 || M % sm.seq_len)
     return set_err(MC_E_INVALID, "forward of %d tokens in sequences of %d", M, sm.seq_len);
   if (!W->has_head) return set_err(MC_E_NO_HEAD, "model has no lm_head and no embedding");
@@ -1313,6 +1313,7 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       t.pos_add = pos_add;
       t.seq = sm;
       t.qblk = attention_qblk(W->H / W->Hkv, sm.seq_len);
+      t.kv_pre = kv_pre ? 1 : 0;
       t.M = M;
       t.H = W->H;
       t.Hkv = W->Hkv;
@@ -1472,7 +1473,11 @@ static mc_status enq_verify(mc_session* s, float* logits = nullptr) {
   ea.off = &s->st->ctx_len;
   ea.keys = s->st->dkeys;
   const SeqMap sm{vm, kStateInts, s->tkv.n_pages, kStateKeys};
-  return enq_forward(s, s->tw, s->tkv, vm * s->B, sm, ea, &s->st->lt, 0, s->st->tkeys, logits);
+  // captured alone in a graph: the target K/V below each request's length
+  // (and the length itself) were written by earlier graph launches or
+  // stream work, which completes before this graph starts
+  return enq_forward(s, s->tw, s->tkv, vm * s->B, sm, ea, &s->st->lt, 0, s->st->tkeys, logits,
+                     true);
 }
 
 static mc_status capture_verify(mc_session* s) {

@@ -196,6 +196,11 @@ struct AttnArgs {
   int pos_add;
   SeqMap seq;
   int qblk;              // tokens of one sequence per CTA (query block)
+  int kv_pre;            // 1: every K/V position below a sequence's first new
+                         // position was written before this launch's graph
+                         // began, so those pages may be read before
+                         // griddepcontrol.wait (the verify graph: only its
+                         // own QKV writes target K/V, at the new positions)
   int M, H, Hkv, hdp, page;
   float inv_scale_den;   // sqrt(head_dim) (divisor, transformer.rs:966)
   int max_chunks;

@@ -1417,11 +1417,9 @@ constexpr int kAttnThreads = 512;
 // e^(m_c - M) * (sum_t e^(s_t - m_c) v_t) to the numerator and
 // e^(m_c - M) * l_c to the denominator; fully masked pages (m_c = -inf)
 // contribute exactly zero.  Then thread -> 4 columns of one row, pages summed
-// in order with eight float4 loads in flight (the first kPre pages of the
-// thread's first row loaded before the weights); Rp (>= R) is a multiple of
-// the rows a warp spans, so the row loop and the shuffles stay warp-uniform.
+// in order with eight float4 loads in flight; Rp (>= R) is a multiple of the
+// rows a warp spans, so the row loop and the shuffles stay warp-uniform.
 // wgt: shared [R][n_chunks]; s_l: shared [>= R]; s_mx: shared [>= Mq].
-template <int kPre>
 __device__ __forceinline__ void attn_combine(const AttnArgs& a, int kvh, int cslot, int n_chunks,
                                              int R, int Rp, int Rs, int G, int mt0, int Mq,
                                              float* wgt, float* s_l, uint32_t* s_mx) {
@@ -1434,16 +1432,6 @@ __device__ __forceinline__ void attn_combine(const AttnArgs& a, int kvh, int csl
   const float4* base =
       reinterpret_cast<const float4*>(a.part_o) + (size_t)cslot * a.max_chunks * Rs * h4 + c4;
   const size_t cs4 = (size_t)Rs * h4;
-  // the first kPre pages of that row do not depend on the weights: their
-  // loads overlap the weight computation below
-  float4 pre[kPre > 0 ? kPre : 1];
-  {
-    const float4* src = base + (size_t)min(row0, R - 1) * h4;
-#pragma unroll
-    for (int u = 0; u < kPre; ++u)
-      pre[u] = (u < n_chunks && row0 < Rp) ? __ldcg(src + (size_t)u * cs4)
-                                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  }
   {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float2* ml = reinterpret_cast<const float2*>(a.part_ml) + (size_t)cslot * a.max_chunks * Rs;
@@ -1475,18 +1463,6 @@ __device__ __forceinline__ void attn_combine(const AttnArgs& a, int kvh, int csl
       const float4* src = base + (size_t)rr * h4;
       float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       int ch = 0;
-      if (kPre > 0 && row == row0) {  // pages 0..kPre-1 came in with the weights
-#pragma unroll
-        for (int u = 0; u < kPre; ++u)
-          if (u < n_chunks) {
-            const float w = wr[u];
-            acc.x = __fmaf_rn(pre[u].x, w, acc.x);
-            acc.y = __fmaf_rn(pre[u].y, w, acc.y);
-            acc.z = __fmaf_rn(pre[u].z, w, acc.z);
-            acc.w = __fmaf_rn(pre[u].w, w, acc.w);
-          }
-        ch = min(n_chunks, kPre);
-      }
       for (; ch + 8 <= n_chunks; ch += 8) {
         float4 v[8];
 #pragma unroll
@@ -1739,7 +1715,7 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) k_attention(AttnArgs a) {
     return;
   }
   __shared__ uint32_t s_mx[128];  // max |out| per token of the block, float bits
-  attn_combine<0>(a, kvh, cslot, n_chunks, R, Rp, Rs, G, mt0, Mq, ss, s_l, s_mx);
+  attn_combine(a, kvh, cslot, n_chunks, R, Rp, Rs, G, mt0, Mq, ss, s_l, s_mx);
   MC_TRACE_PHASE(a.trace_slot, 7, mc_tp);
   MC_TRACE_END(a.trace_slot);
 }
@@ -1804,14 +1780,38 @@ __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_t
   if (a.pf && threadIdx.x == 0)
     prefetch_share(a.pf, a.pf_bytes, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
                    gridDim.x * gridDim.y * gridDim.z);
-  grid_launch_dependents();
-  grid_wait();
-  MC_TRACE_WAITED(a.trace_slot);
-  MC_TRACE_PHASE(a.trace_slot, 0, mc_tp);
   const int kvh = blockIdx.x, chunk = blockIdx.y, zb = blockIdx.z;
   const int G = a.H / a.Hkv;
   const int n_qb = (a.seq.seq_len + a.qblk - 1) / a.qblk;
   const int z = zb / n_qb, i0 = (zb - z * n_qb) * a.qblk;
+  // A page wholly below the sequence's first new position holds final K/V
+  // when kv_pre is set: its copies start before the wait and overlap the
+  // producer's tail (the two copy groups, K then V, as below).
+  bool early = false;
+  if (a.kv_pre) {
+    const int base = a.pos_ptr[z * a.seq.pos_stride] + a.pos_add;
+    if ((chunk + 1) * P <= base) {
+      const int pg = a.page_table[z * a.seq.pt_stride + chunk];
+      const float4* kb4 = reinterpret_cast<const float4*>(a.kc + ((size_t)pg * a.Hkv + kvh) * P * HD);
+      const float4* vb4 = reinterpret_cast<const float4*>(a.vc + ((size_t)pg * a.Hkv + kvh) * P * HD);
+      constexpr int H4 = HD / 4;
+      for (int i = threadIdx.x; i < P * H4; i += kAttnTcThreads) {
+        const int t = i / H4, c4 = i - t * H4;
+        cp_async16(sK + t * KS + 4 * c4, kb4 + i);
+      }
+      cp_async_commit();
+      for (int i = threadIdx.x; i < P * H4; i += kAttnTcThreads) {
+        const int t = i / H4, c4 = i - t * H4;
+        cp_async16(sV + t * VS + 4 * c4, vb4 + i);
+      }
+      cp_async_commit();
+      early = true;
+    }
+  }
+  grid_launch_dependents();
+  grid_wait();
+  MC_TRACE_WAITED(a.trace_slot);
+  MC_TRACE_PHASE(a.trace_slot, 0, mc_tp);
   const int Mq = min(a.qblk, a.seq.seq_len - i0);
   const int mt0 = z * a.seq.seq_len + i0;
   const int R = G * Mq;
@@ -1829,22 +1829,24 @@ __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_t
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tq = lane & 3;
   {
-    const int pg = a.page_table[z * a.seq.pt_stride + chunk];
-    const float4* kbase = reinterpret_cast<const float4*>(a.kc + ((size_t)pg * a.Hkv + kvh) * P * HD);
-    const float4* vbase = reinterpret_cast<const float4*>(a.vc + ((size_t)pg * a.Hkv + kvh) * P * HD);
     constexpr int H4 = HD / 4;
-    // two copy groups: K (needed by the scores) then V (needed after the
-    // softmax), so the V copies land while the scores are computed
-    for (int i = threadIdx.x; i < nt * H4; i += kAttnTcThreads) {
-      const int t = i / H4, c4 = i - t * H4;
-      cp_async16(sK + t * KS + 4 * c4, kbase + i);
+    if (!early) {
+      const int pg = a.page_table[z * a.seq.pt_stride + chunk];
+      const float4* kbase = reinterpret_cast<const float4*>(a.kc + ((size_t)pg * a.Hkv + kvh) * P * HD);
+      const float4* vbase = reinterpret_cast<const float4*>(a.vc + ((size_t)pg * a.Hkv + kvh) * P * HD);
+      // two copy groups: K (needed by the scores) then V (needed after the
+      // softmax), so the V copies land while the scores are computed
+      for (int i = threadIdx.x; i < nt * H4; i += kAttnTcThreads) {
+        const int t = i / H4, c4 = i - t * H4;
+        cp_async16(sK + t * KS + 4 * c4, kbase + i);
+      }
+      cp_async_commit();
+      for (int i = threadIdx.x; i < nt * H4; i += kAttnTcThreads) {
+        const int t = i / H4, c4 = i - t * H4;
+        cp_async16(sV + t * VS + 4 * c4, vbase + i);
+      }
+      cp_async_commit();
     }
-    cp_async_commit();
-    for (int i = threadIdx.x; i < nt * H4; i += kAttnTcThreads) {
-      const int t = i / H4, c4 = i - t * H4;
-      cp_async16(sV + t * VS + 4 * c4, vbase + i);
-    }
-    cp_async_commit();
     // rows past the page's last position: zero K and V (probability 0 times
     // stale data could be NaN); their scores are masked
     for (int i = nt * H4 + threadIdx.x; i < P * H4; i += kAttnTcThreads) {
@@ -2041,9 +2043,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_t
   const int h4 = HD / 4;
   const int span = h4 >= 32 ? 1 : 32 / h4;  // rows one warp spans in the column pass
   const int Rpc = (R + span - 1) / span * span;
-  // (pages preloaded where the registers allow it without spilling)
-  attn_combine<HD == 128 ? 4 : 0>(a, kvh, cslot, n_chunks, R, Rpc, Rs, G, mt0, Mq, asmem, s_l,
-                                  s_mx);
+  attn_combine(a, kvh, cslot, n_chunks, R, Rpc, Rs, G, mt0, Mq, asmem, s_l, s_mx);
   MC_TRACE_PHASE(a.trace_slot, 7, mc_tp);
   MC_TRACE_END(a.trace_slot);
 }
