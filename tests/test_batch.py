@@ -166,3 +166,22 @@ def test_linear_wide_matches_oracle_and_is_batch_invariant(fmt, n, k, m):
     for sl in [slice(0, 1), slice(3, 12), slice(5, 21), slice(m - 17, m)]:
         yi = lin(xt[sl].contiguous()).cpu().numpy()
         assert np.array_equal(yi, y[sl]), sl
+
+
+def test_linear_token_counts_across_routes():
+    """A matrix of 8192 rows runs 1..8 tokens on the GEMV (two and three
+    digit tiles) and 9..64 on the tcgen05 GEMM: every slice must equal the
+    same rows of one 20-token call bit for bit, and match the oracle."""
+    import torch
+    w, x = _lin_case(8192, 512, 20, seed=5)
+    q, sc = mb.quantize_int8_rows(w)
+    lin = mb.Linear(mb.QTensor("i8_row", q, sc))
+    wd = o.dequant_int8_rows(q, sc)
+    xt = torch.from_numpy(x).cuda()
+    y = lin(xt).cpu().numpy()
+    wn = np.linalg.norm(wd.astype(np.float64), axis=1)
+    for i in range(20):
+        tol = 1e-4 * wn * np.linalg.norm(x[i].astype(np.float64)) + 1e-30
+        assert (np.abs(y[i].astype(np.float64) - o.linear(wd, x[i])) <= tol).all(), i
+    for a, b in [(0, 1), (1, 6), (2, 8), (3, 11), (2, 12), (4, 20)]:
+        assert np.array_equal(lin(xt[a:b].contiguous()).cpu().numpy(), y[a:b]), (a, b)
