@@ -111,7 +111,10 @@ typedef struct mc_ngram_drafter mc_ngram_drafter;
  * restricted to the fields the speculative step reads). */
 typedef struct mc_spec_cfg {
   int32_t gamma;        /* draft tokens per round (GenerationConfig::gamma) */
-  int32_t max_context;  /* KV capacity in tokens (prompt + generated + gamma) */
+  int32_t max_context;  /* KV capacity in tokens (prompt + generated + gamma),
+                           at most 4030 per request in this build (64 KV
+                           pages of 64 positions, less one prefill chunk);
+                           larger values return MC_E_CAPACITY */
   int32_t bonus;        /* 0: reference verify (gamma positions, no bonus
                            token, generate.rs:695-726); 1: gamma+1 positions
                            with the bonus token */
@@ -232,6 +235,11 @@ MC_API mc_status mc_spec_prime(mc_session* s, const uint32_t* prompt, int32_t n_
 MC_API mc_status mc_spec_prime_batch(mc_session* s, const uint32_t* prompts,
                               const int32_t* lens, int32_t n_requests);
 MC_API mc_status mc_spec_decode(mc_session* s, int32_t max_tokens, int32_t* n_generated);
+/* mc_spec_decode (and mc_speculative_generate) look at the cancel flag of
+ * mc_spec_cfg before every batch of at most 64 rounds (generate.rs:639 looks
+ * before every round) and return MC_E_CANCELLED with the rounds run so far
+ * kept: mc_spec_read returns them, and after the flag is lowered the session
+ * continues or rewinds as usual. */
 MC_API mc_status mc_spec_read(mc_session* s, uint32_t* out, int32_t cap, int32_t* n_out,
                        int32_t* accepted, int32_t accepted_cap, int32_t* n_rounds);
 /* mc_spec_read for request z of a batched session. */
@@ -251,16 +259,29 @@ MC_API mc_status mc_spec_rewind(mc_session* s);
 MC_API mc_status mc_tp_unique_id(char id_out[128]);
 MC_API mc_status mc_session_tp_init(mc_session* s, const char id[128], int32_t rank,
                              int32_t world);
-/* Fused tensor-parallel reduction over NVLink (instead of NCCL all-reduces
- * for the row-parallel projections): every rank exports its reduce buffer
- * (64-byte CUDA IPC handle), the host gathers the handles of all ranks in
- * rank order (world x 64 bytes) and each rank opens its peers before its
- * first decode.  The row-parallel GEMV then stores its partial rows into
- * every rank's buffer and a reduce kernel adds them in rank order (bounded
- * waits; an expired wait returns MC_E_TIMEOUT).  All ranks must reach the
- * host barrier before any destroys its session. */
+/* Fused tensor-parallel reduction over NVLink (instead of NCCL all-reduces):
+ * every rank exports its exchange buffer (64-byte CUDA IPC handle), the host
+ * gathers the handles of all ranks in rank order (world x 64 bytes) and each
+ * rank opens its peers before its first decode (a handle exported by another
+ * session of the same process is opened directly, so ranks may also be one
+ * host thread per GPU).  The row-parallel GEMV then stores its partial rows
+ * into every rank's buffer and a reduce kernel adds them in rank order; the
+ * vocab-parallel LM head exchanges its per-token argmax keys the same way.
+ * Every cross-rank wait is bounded (mc_session_set_wait_timeout); an expired
+ * wait returns MC_E_TIMEOUT.  With open peers an int8 target needs no NCCL
+ * (mc_session_tp_init is then optional); q4_0 forwards of more than 16
+ * tokens still reduce through NCCL.  All ranks must reach the host barrier
+ * before any destroys its session. */
 MC_API mc_status mc_session_tp_ipc_handle(mc_session* s, char handle_out[64]);
 MC_API mc_status mc_session_tp_open_peers(mc_session* s, const char* handles);
+/* Limit, in milliseconds, of every bounded device wait of this session (a
+ * tensor-parallel peer's flag in the fused reduction and the vocab-parallel
+ * head; default 5000).  A wait that expires raises the session's error word:
+ * the call returns MC_E_TIMEOUT, every later wait of the session gives up at
+ * once, and the session stays failed (its ranks' epochs are out of step):
+ * destroy it.  The CUDA context stays usable.  The reference has no device
+ * waits; this stands in for a peer that failed in the middle of a request. */
+MC_API mc_status mc_session_set_wait_timeout(mc_session* s, int32_t ms);
 /* Reseed the stochastic rounds (GenerationConfig::seed per request,
  * generate.rs:146-167); applies from the next round. */
 MC_API mc_status mc_spec_set_seed(mc_session* s, uint64_t seed);
@@ -286,12 +307,11 @@ MC_API mc_status mc_linear_run(mc_linear* l, const float* x_dev, int32_t m,
 MC_API int64_t mc_linear_weight_bytes(const mc_linear* l);
 
 /* Allocation-free variant of mc_linear_run.  It has no counterpart in the
- * reference, which has no device path at all.  Same arguments, kernels and
- * results as mc_linear_run, but the activation scratch (the packed digit
- * operand and the per-token exponents) lives in one fixed device array
- * compiled into this library, 768 KiB + 256 B per device, instead of in
- * buffers owned by the handle, and the call itself allocates no device or
- * host memory.
+ * reference, which has no device path at all.  Same arguments as
+ * mc_linear_run, but the activation scratch (the packed digit operand and
+ * the per-token exponents) lives in one fixed device array compiled into
+ * this library, 768 KiB + 256 B per device, instead of in buffers owned by
+ * the handle, and the call itself allocates no device or host memory.
  *
  * It exists for callers that may allocate at start-up (mc_linear_create
  * packs the weights then) but not when they run a projection. One example
@@ -301,13 +321,22 @@ MC_API int64_t mc_linear_weight_bytes(const mc_linear* l);
  * other streams, where cudaMalloc/cudaFree may synchronise the whole device
  * and stall them.
  *
+ * Route: the encoder computes each token's statistics itself and the GEMV
+ * runs once per group of up to 16 tokens, streaming the weights once per
+ * group; it never takes the tcgen05 GEMM that mc_linear_run uses for more
+ * than 16 tokens (or 9-16 tokens on matrices of 8192+ rows).  Both routes sum
+ * exactly in int32, so the results agree with mc_linear_run's; for m > 16
+ * the static call is slower.
+ *
  * Limit: in_features <= 16384; a larger matrix returns MC_E_CAPACITY and
- * launches nothing.  The first call on each device does the set-up (looks
- * up the array's device address and clears it once), so make that first
- * call before any stream capture.  All calls on one device share the array:
- * calls that overlap in time (different streams or threads with no ordering
- * between them) race on it and corrupt each other's results; issue them on
- * one stream or synchronise between them. */
+ * launches nothing.  The first call on each device looks up the array's
+ * device address (a host-side lookup; no clear, no launch), so make that
+ * first call before any stream capture.  The address is kept for the life
+ * of the process: cudaDeviceReset on that device is not supported while the
+ * library is in use.  All calls on one device share the array: calls that
+ * overlap in time (different streams or threads with no ordering between
+ * them) race on it and corrupt each other's results; issue them on one
+ * stream or synchronise between them. */
 MC_API mc_status mc_linear_run_static(mc_linear* l, const float* x_dev, int32_t m,
                                float* y_dev, void* stream);
 

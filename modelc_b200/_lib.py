@@ -31,6 +31,7 @@ EXPORTS = [
     "mc_session_tp_open_peers", "mc_speculative_generate_batch", "mc_spec_prime_batch",
     "mc_spec_read_request", "mc_mlp_draft_create", "mc_mlp_draft", "mc_mlp_draft_destroy",
     "mc_ngram_draft_create", "mc_ngram_draft", "mc_ngram_draft_destroy", "mc_sample_rows",
+    "mc_session_set_wait_timeout",
 ]
 
 
@@ -118,6 +119,7 @@ def lib():
         "mc_session_tp_init": (i32, [vp, C.c_char_p, i32, i32]),
         "mc_session_tp_ipc_handle": (i32, [vp, C.c_char_p]),
         "mc_session_tp_open_peers": (i32, [vp, C.c_char_p]),
+        "mc_session_set_wait_timeout": (i32, [vp, i32]),
         "mc_speculative_generate_batch": (i32, [vp, u32p, i32p, i32, i32, u32p, i32, i32p, i32p,
                                                 i32, i32p]),
         "mc_spec_prime_batch": (i32, [vp, u32p, i32p, i32]),

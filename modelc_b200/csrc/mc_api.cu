@@ -768,6 +768,7 @@ extern "C" int64_t mc_weights_bytes(const mc_weights* w) {
 
 // ------------------------------------------------------------------ sessions
 constexpr int kPage = 64;       // KV positions per page
+constexpr int kMaxAttnPages = 64;  // pages one attention launch combines per request
 constexpr int kChunk = kMaxTokens;  // prefill tokens per forward launch
 
 struct KVSet {
@@ -843,7 +844,12 @@ struct mc_session {
   int* tp_cnt_red = nullptr;
   bool tp_p2p = false;
   TPArgs tp{};
-  std::vector<void*> tp_opened;  // peers' regions mapped here
+  std::vector<void*> tp_opened;  // peers' regions mapped here (CUDA IPC)
+  size_t tp_keyx_off = 0, tp_kflag_off = 0;  // key slots and key flags in the region
+  unsigned* tp_kepoch = nullptr;
+  // limit of every bounded device wait, in nanoseconds (device word)
+  long long* wait_ns = nullptr;
+  bool failed = false;  // an earlier bounded wait expired: the session is unusable
 };
 
 static int trace_slot(mc_session* s) { return s->trace_on ? ++s->trace_next : 0; }
@@ -912,6 +918,22 @@ static int max_stripes(const mc_weights* W) {
   return m;
 }
 
+// Default limit of a bounded device wait (a peer's flag in tensor
+// parallelism): far above any healthy wait, short enough that a missing peer
+// ends in an error instead of a stalled GPU.
+constexpr long long kDefaultWaitNs = 5000000000ll;
+
+// Exchange regions this process exported (mc_session_tp_ipc_handle): a peer
+// in the same process (one thread per GPU) opens them directly, since CUDA
+// IPC cannot map an allocation into the process that made it.
+struct ExportedRegion {
+  char handle[64];
+  int dev;
+  void* ptr;
+};
+static std::mutex g_export_mu;
+static std::vector<ExportedRegion> g_exports;
+
 static mc_status session_alloc(mc_session* s) {
   const mc_weights* ws[2] = {s->tw, s->dw};
   int d = 0, kp = 0, hq = 0, F = 0, V = 0, stripes = 0, hkv = 0;
@@ -953,6 +975,9 @@ static mc_status session_alloc(mc_session* s) {
   CKS(s->al.alloc(&s->part_ml, pml * n_pages));
   CKS(s->al.alloc(&s->err, 1));
   CK(cudaMemset(s->err, 0, 4));
+  CKS(s->al.alloc(&s->wait_ns, 1));
+  const long long wait_default = kDefaultWaitNs;
+  CK(cudaMemcpy(s->wait_ns, &wait_default, sizeof(wait_default), cudaMemcpyHostToDevice));
   CKS(s->al.alloc(&s->st_amax, (size_t)2 * kMaxTokens));
   CK(cudaMemset(s->st_amax, 0, (size_t)2 * kMaxTokens * 4));
   s->st_np_cap = std::max(stripes, 1);
@@ -960,14 +985,19 @@ static mc_status session_alloc(mc_session* s) {
   if (s->tw->tp_world > 1) {
     const int R = s->tw->tp_world, dd = s->tw->d;
     CKS(s->al.alloc(&s->tp_part, (size_t)kMaxTokens * dd));
-    // reduce region: partial slots then flags, one allocation for one IPC handle
+    // exchange region: partial slots, their flags, key slots, key flags; one
+    // allocation for one IPC handle
     s->tp_red_bytes = (size_t)2 * R * kMaxTokens * dd * sizeof(float);
-    const size_t bytes = s->tp_red_bytes + 2 * kMaxTP * sizeof(unsigned);
+    s->tp_keyx_off = (s->tp_red_bytes + 2 * kMaxTP * sizeof(unsigned) + 255) / 256 * 256;
+    s->tp_kflag_off = s->tp_keyx_off + (size_t)2 * kMaxTP * kMaxTokens * sizeof(unsigned long long);
+    const size_t bytes = s->tp_kflag_off + 2 * kMaxTP * sizeof(unsigned);
     CK(cudaMalloc(&s->tp_region, bytes));
     CK(cudaMemset(s->tp_region, 0, bytes));
     CKS(s->al.alloc(&s->tp_epoch, 1));
+    CKS(s->al.alloc(&s->tp_kepoch, 1));
     const unsigned one = 1u;  // epochs start at 1; flags start at 0
     CK(cudaMemcpy(s->tp_epoch, &one, 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(s->tp_kepoch, &one, 4, cudaMemcpyHostToDevice));
     CKS(s->al.alloc(&s->tp_cnt_gemv, 1));
     CKS(s->al.alloc(&s->tp_cnt_red, 1));
     CK(cudaMemset(s->tp_cnt_gemv, 0, 4));
@@ -1018,6 +1048,11 @@ extern "C" mc_status mc_session_create(const mc_weights* target, const mc_weight
   if (B > 1 && cfg->temperature > 0.0f)
     return set_err(MC_E_INVALID, "batched sessions decode greedily (temperature 0)");
   if (cfg->max_context <= 0) return set_err(MC_E_INVALID, "max_context must be positive");
+  if (round_up(cfg->max_context + kChunk + 2, kPage) / kPage > kMaxAttnPages)
+    return set_err(MC_E_CAPACITY,
+                   "max_context %d above this build's limit %d (the attention combines at most "
+                   "%d KV pages of %d positions per request)",
+                   cfg->max_context, kMaxAttnPages * kPage - kChunk - 2, kMaxAttnPages, kPage);
   if (!(cfg->temperature >= 0.0f) || !isfinite(cfg->temperature))
     return set_err(MC_E_INVALID, "temperature must be finite and >= 0");
   if (cfg->accept_mode != 0 && cfg->accept_mode != 1)
@@ -1063,6 +1098,12 @@ extern "C" mc_status mc_session_destroy(mc_session* s) {
   if (s->verify_exec) cudaGraphExecDestroy(s->verify_exec);
   if (s->comm) nccl::g_api.comm_destroy(s->comm);  // after the graphs holding its calls
   for (void* p : s->tp_opened) cudaIpcCloseMemHandle(p);
+  if (s->tp_region) {
+    std::lock_guard<std::mutex> lock(g_export_mu);
+    for (size_t i = 0; i < g_exports.size();)
+      if (g_exports[i].ptr == s->tp_region) g_exports.erase(g_exports.begin() + i);
+      else ++i;
+  }
   if (s->tp_region) cudaFree(s->tp_region);
   if (s->h_ids) cudaFreeHost(s->h_ids);
   if (s->stream) cudaStreamDestroy(s->stream);
@@ -1072,11 +1113,22 @@ extern "C" mc_status mc_session_destroy(mc_session* s) {
 }
 
 // ------------------------------------------------------------------ forward
-// A raised device error flag means a bounded wait expired inside a kernel.
-static mc_status check_err(int* err) {
+// A raised device error flag means a bounded wait expired inside a kernel
+// (a tensor-parallel peer that never published, or a stalled copy).  The
+// session's cross-rank epochs are then out of step, so it stays failed.
+static mc_status check_err(mc_session* s) {
   int v = 0;
-  CK(cudaMemcpy(&v, err, 4, cudaMemcpyDeviceToHost));
-  if (v) return set_err(MC_E_TIMEOUT, "a bounded device wait expired (pipeline stalled)");
+  CK(cudaMemcpy(&v, s->err, 4, cudaMemcpyDeviceToHost));
+  if (v) {
+    s->failed = true;
+    return set_err(MC_E_TIMEOUT, "a bounded device wait expired (a peer never arrived or the "
+                                 "pipeline stalled); destroy this session");
+  }
+  return MC_OK;
+}
+static mc_status check_usable(const mc_session* s) {
+  if (s->failed)
+    return set_err(MC_E_TIMEOUT, "an earlier bounded device wait expired; destroy this session");
   return MC_OK;
 }
 
@@ -1179,7 +1231,9 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
     return set_err(MC_E_INVALID, "forward of %d tokens in sequences of %d", M, sm.seq_len);
   if (!W->has_head) return set_err(MC_E_NO_HEAD, "model has no lm_head and no embedding");
   const bool tp = W->tp_world > 1;
-  if (tp && !s->comm) return set_err(MC_E_INVALID, "tensor-parallel weights: call mc_session_tp_init");
+  if (tp && !s->comm && !s->tp_p2p)
+    return set_err(MC_E_INVALID,
+                   "tensor-parallel weights: call mc_session_tp_init or mc_session_tp_open_peers");
   if (tp && logits_dev) return set_err(MC_E_INVALID, "tensor-parallel forwards return argmax only");
   ea.emb_q = W->emb_q;
   ea.emb_scale = W->emb_scale;
@@ -1251,6 +1305,9 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       prod_np = (d + kResidBlock - 1) / kResidBlock;
       return MC_OK;
     }
+    if (!s->comm)
+      return set_err(MC_E_INVALID, "this forward (%d tokens of q4_0 weights) reduces with NCCL: "
+                     "call mc_session_tp_init", M);
     g.out = s->tp_part;
     CKS(enq_gemv(s, Wm, EPI_STORE, M, g, next));
     CKS(nccl::check(nccl::g_api.all_reduce(s->tp_part, s->tp_part, (size_t)M * d, nccl::kFloat32,
@@ -1365,7 +1422,9 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
   hd.seq = sm;
   hd.row_offset = W->head_row0;
   CKS(enq_gemv(s, W->head, EPI_LMHEAD, M, hd));
-  if (tp) {  // vocab-parallel head: the largest (value, lowest index) key wins
+  if (tp && s->tp_p2p) {  // vocab-parallel head over peer memory (bounded waits)
+    CK(launch_tp_keys(s->tp, keys, M / sm.seq_len, sm.seq_len, sm.key_stride, s->stream, true));
+  } else if (tp) {  // vocab-parallel head: the largest (value, lowest index) key wins
     // the key slots of each sequence are contiguous (seq_len of them)
     const int n_seq = M / sm.seq_len;
     for (int z = 0; z < n_seq; ++z)
@@ -1385,6 +1444,7 @@ static mc_status forward_api(mc_session* s, int which, const uint32_t* ids, int 
   int& len = which ? s->ld : s->lt;
   if (n < 0 || (n > 0 && !ids)) return set_err(MC_E_INVALID, "bad ids");
   if (len + n > s->cap - 1) return set_err(MC_E_CAPACITY, "KV capacity %d exceeded", s->cap);
+  CKS(check_usable(s));
   CK(cudaSetDevice(s->dev));
   for (int c0 = 0; c0 < n; c0 += kChunk) {
     const int M = std::min(kChunk, n - c0);
@@ -1400,7 +1460,7 @@ static mc_status forward_api(mc_session* s, int which, const uint32_t* ids, int 
       CK(cudaMemcpyAsync(logits + (size_t)c0 * W->V, s->logits, (size_t)M * W->V * 4,
                          cudaMemcpyDeviceToHost, s->stream));
     CK(cudaStreamSynchronize(s->stream));
-    CKS(check_err(s->err));
+    CKS(check_err(s));
     len += M;
   }
   if (which) s->draft_tokens.insert(s->draft_tokens.end(), ids, ids + n);
@@ -1615,6 +1675,7 @@ extern "C" mc_status mc_spec_prime_batch(mc_session* s, const uint32_t* prompts,
     if (lens[z] + s->cfg.gamma + 2 > s->cap)
       return set_err(MC_E_CAPACITY, "prompt of %d does not fit KV capacity %d", lens[z], s->cap);
   }
+  CKS(check_usable(s));
   CK(cudaSetDevice(s->dev));
   s->prompt_len = lens[0];
   s->prompt_lens.assign(lens, lens + n_requests);
@@ -1632,6 +1693,7 @@ extern "C" mc_status mc_spec_prime_batch(mc_session* s, const uint32_t* prompts,
   CK(cudaMemcpyAsync(s->st, h.data(), sizeof(SpecState) * n_requests, cudaMemcpyHostToDevice,
                      s->stream));
   CK(cudaStreamSynchronize(s->stream));
+  CKS(check_err(s));
   s->lt = lens[0];
   s->ld = lens[0] - 1;
   return MC_OK;
@@ -1648,9 +1710,11 @@ extern "C" mc_status mc_spec_prime(mc_session* s, const uint32_t* prompt, int32_
 // each request's acceptance leaves it unchanged once its budget is spent, and
 // launching ceil(max remaining / max_emit) rounds per batch keeps every
 // launched round one that the request with the most left would also run.
+constexpr int kRoundsPerBatch = 64;
 extern "C" mc_status mc_spec_decode(mc_session* s, int32_t max_tokens, int32_t* n_generated) {
   if (!s || max_tokens < 0) return set_err(MC_E_INVALID, "bad arguments");
   if (!s->prompt_len) return set_err(MC_E_INVALID, "call mc_spec_prime first");
+  CKS(check_usable(s));
   CK(cudaSetDevice(s->dev));
   CKS(capture_round(s));
   const int B = s->B;
@@ -1664,7 +1728,8 @@ extern "C" mc_status mc_spec_decode(mc_session* s, int32_t max_tokens, int32_t* 
     int most = 0;
     for (int z = 0; z < B; ++z) most = std::max(most, max_tokens - h[z].generated);
     if (most <= 0) break;
-    const int R = (most + max_emit - 1) / max_emit;
+    // at most kRoundsPerBatch rounds between two looks at the cancel flag
+    const int R = std::min((most + max_emit - 1) / max_emit, kRoundsPerBatch);
     for (int z = 0; z < B; ++z) {
       const int remaining = max_tokens - h[z].generated;
       if (remaining <= 0) continue;
@@ -1675,7 +1740,7 @@ extern "C" mc_status mc_spec_decode(mc_session* s, int32_t max_tokens, int32_t* 
     for (int r = 0; r < R; ++r) CK(cudaGraphLaunch(s->round_exec, s->stream));
     CK(cudaMemcpyAsync(h.data(), s->st, sizeof(SpecState) * B, cudaMemcpyDeviceToHost, s->stream));
     CK(cudaStreamSynchronize(s->stream));
-    CKS(check_err(s->err));
+    CKS(check_err(s));
   }
   s->lt = h[0].lt;
   s->ld = h[0].ld;
@@ -1762,6 +1827,16 @@ extern "C" mc_status mc_session_tp_ipc_handle(mc_session* s, char handle_out[64]
   CK(cudaIpcGetMemHandle(&h, s->tp_region));
   static_assert(sizeof(h) == 64, "IPC handle size");
   memcpy(handle_out, &h, 64);
+  std::lock_guard<std::mutex> lock(g_export_mu);
+  bool known = false;
+  for (const ExportedRegion& x : g_exports) known |= x.ptr == s->tp_region;
+  if (!known) {
+    ExportedRegion x{};
+    memcpy(x.handle, &h, 64);
+    x.dev = s->dev;
+    x.ptr = s->tp_region;
+    g_exports.push_back(x);
+  }
   return MC_OK;
 }
 
@@ -1779,12 +1854,34 @@ extern "C" mc_status mc_session_tp_open_peers(mc_session* s, const char* handles
   t.world = R;
   t.d = s->tw->d;
   t.epoch = s->tp_epoch;
+  t.kepoch = s->tp_kepoch;
   t.cnt = s->tp_cnt_gemv;
   t.err = s->err;
+  t.wait_ns = s->wait_ns;
   for (int r = 0; r < R; ++r) {
     char* base = nullptr;
+    ExportedRegion local{};
+    bool in_process = false;
+    if (r != rank) {
+      std::lock_guard<std::mutex> lock(g_export_mu);
+      for (const ExportedRegion& x : g_exports)
+        if (!memcmp(x.handle, handles + 64 * r, 64)) {
+          local = x;
+          in_process = true;
+        }
+    }
     if (r == rank) {
       base = (char*)s->tp_region;
+    } else if (in_process) {  // a peer session of this process: its pointer as is
+      if (local.dev != s->dev) {
+        int can = 0;
+        CK(cudaDeviceCanAccessPeer(&can, s->dev, local.dev));
+        if (!can) return set_err(MC_E_CUDA, "device %d cannot access device %d", s->dev, local.dev);
+        cudaError_t e = cudaDeviceEnablePeerAccess(local.dev, 0);
+        if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+        else CK(e);
+      }
+      base = (char*)local.ptr;
     } else {
       cudaIpcMemHandle_t h;
       memcpy(&h, handles + 64 * r, 64);
@@ -1800,6 +1897,8 @@ extern "C" mc_status mc_session_tp_open_peers(mc_session* s, const char* handles
     }
     t.red[r] = (float*)base;
     t.flag[r] = (unsigned*)(base + s->tp_red_bytes);
+    t.keyx[r] = (unsigned long long*)(base + s->tp_keyx_off);
+    t.kflag[r] = (unsigned*)(base + s->tp_kflag_off);
   }
   s->tp = t;
   s->tp_p2p = true;
@@ -1827,6 +1926,15 @@ extern "C" mc_status mc_spec_verify_launch(mc_session* s, int32_t n) {
 }
 
 extern "C" void* mc_session_stream(mc_session* s) { return s ? (void*)s->stream : nullptr; }
+
+extern "C" mc_status mc_session_set_wait_timeout(mc_session* s, int32_t ms) {
+  if (!s || ms < 1) return set_err(MC_E_INVALID, "bad arguments");
+  CK(cudaSetDevice(s->dev));
+  const long long ns = (long long)ms * 1000000ll;
+  CK(cudaMemcpyAsync(s->wait_ns, &ns, sizeof(ns), cudaMemcpyHostToDevice, s->stream));
+  CK(cudaStreamSynchronize(s->stream));
+  return MC_OK;
+}
 
 extern "C" int32_t mc_session_round_launches(const mc_session* s) {
   if (!s || !s->dw) return 0;
@@ -1993,10 +2101,14 @@ static std::mutex g_static_mu;
 static unsigned char* g_static_ptr[kStaticMaxDevices];
 
 // Set-up, once per device, with that device current: the array's device
-// address, and one clear of the whole array.  Afterwards nothing has to be
-// zero at the start of a call: every call's encoder rewrites all digit words
-// the GEMV reads (padding columns of the last n8 tile included) and the
-// exponents of its tokens.
+// address.  Nothing in the array has to be zero at the start of a call, so
+// there is no clear (a clear on another stream than the caller's would not be
+// ordered before the first encoder): every call's encoder rewrites all digit
+// words the GEMV reads, the zero digits of columns past in_features and the
+// padding columns of the last n8 tile included, and the exponents of its
+// tokens.  The address is cached for the life of the process, so
+// cudaDeviceReset on a device is not supported while this library is in use
+// there: the module is reloaded and the array may move.
 static mc_status static_scratch(int dev, unsigned char** out) {
   if (dev < 0 || dev >= kStaticMaxDevices)
     return set_err(MC_E_INVALID, "device %d outside [0, %d)", dev, kStaticMaxDevices);
@@ -2006,10 +2118,6 @@ static mc_status static_scratch(int dev, unsigned char** out) {
     cudaError_t e = cudaGetSymbolAddress((void**)&ptr, g_static_scratch);
     if (e != cudaSuccess || !ptr)
       return set_err(MC_E_CUDA, "static scratch address on device %d: %s", dev,
-                     cudaGetErrorString(e));
-    e = cudaMemset(ptr, 0, kStaticBytes);
-    if (e != cudaSuccess)
-      return set_err(MC_E_CUDA, "static scratch clear on device %d: %s", dev,
                      cudaGetErrorString(e));
     g_static_ptr[dev] = ptr;
   }

@@ -95,21 +95,30 @@ enum Epi : int {
   EPI_TP = 5,      // row-parallel partial sums stored into every rank's reduce buffer
 };
 
-// Tensor-parallel reduce buffers (one region per rank, opened by the peers
-// through CUDA IPC): partial sums [2 sets][R senders][kMaxTokens][d] floats,
-// then flags [2 sets][kMaxTP] epochs.  A row-parallel GEMV (EPI_TP) of epoch
-// e stores its rows into set e % 2, slot `rank`, of every rank, and its last
+// Tensor-parallel exchange buffers (one region per rank, opened by the peers
+// through CUDA IPC, or directly when the peer lives in the same process):
+// partial sums [2 sets][R senders][kMaxTokens][d] floats, then flags [2
+// sets][kMaxTP] epochs, then argmax keys [2 sets][kMaxTP senders][kMaxTokens]
+// and their flags [2 sets][kMaxTP].  A row-parallel GEMV (EPI_TP) of epoch e
+// stores its rows into set e % 2, slot `rank`, of every rank, and its last
 // CTA publishes e in every rank's flags; the reduce kernel waits for all R
 // flags, adds the slots in rank order (identical bits on every rank), then
-// does h += sum and the next encoder's statistics.
+// does h += sum and the next encoder's statistics.  The vocab-parallel LM
+// head exchanges its per-token argmax keys the same way (k_tp_keys).  Every
+// wait is bounded by *wait_ns nanoseconds; an expired wait raises *err, and
+// once *err is raised later waits give up at once.
 constexpr int kMaxTP = 8;
 struct TPArgs {
   float* red[kMaxTP];      // every rank's reduce region (index = rank)
   unsigned* flag[kMaxTP];  // every rank's flags
+  unsigned long long* keyx[kMaxTP];  // every rank's key slots
+  unsigned* kflag[kMaxTP];           // every rank's key flags
   int rank, world, d;
   const unsigned* epoch;   // this rank's epoch counter
+  unsigned* kepoch;        // this rank's key-exchange epoch counter
   int* cnt;                // CTA arrival counter of the GEMV (zeroed)
   int* err;
+  const long long* wait_ns;  // limit of each bounded wait (device word)
 };
 
 struct GemvArgs {
@@ -270,6 +279,10 @@ cudaError_t launch_resid_stats(const ResidArgs& a, cudaStream_t s, bool pdl);
 // the epoch.
 cudaError_t launch_tp_reduce(const ResidArgs& a, const TPArgs& t, unsigned* epoch, int* cnt,
                              cudaStream_t s, bool pdl);
+// Vocab-parallel LM head over peer memory: the max over the ranks of the
+// argmax keys of n_seq sequences of seq_len tokens (key_stride apart).
+cudaError_t launch_tp_keys(const TPArgs& t, unsigned long long* keys, int n_seq, int seq_len,
+                           int key_stride, cudaStream_t s, bool pdl);
 constexpr int kResidBlock = 1024;
 
 struct SpecState {

@@ -2891,6 +2891,37 @@ cudaError_t launch_resid_stats(const ResidArgs& a, cudaStream_t s, bool pdl) {
   return cudaLaunchKernelEx(&cfg, k_resid_stats, a);
 }
 
+// Waits until *p == e (acquire at system scope, so the peer's stores that
+// precede its release are visible) for at most limit_ns nanoseconds of
+// %globaltimer; a fixed poll count bounds it as well, should the timer not
+// advance.  Returns false when the wait expired.
+__device__ __forceinline__ bool bounded_wait_eq(const unsigned* p, unsigned e, long long limit_ns) {
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (long long i = 0; i < (1ll << 24); ++i) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    if (v == e) return true;
+    if ((i & 31) == 31) {
+      unsigned long long t1;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+      if ((long long)(t1 - t0) > limit_ns) return false;
+    }
+  }
+  return false;
+}
+
+// One thread: waits (bounded) until flags[r] == e for every rank r; gives up
+// at once when the error word is already raised (an earlier wait expired),
+// and raises it when a wait expires.
+__device__ __forceinline__ int tp_wait_all(const TPArgs& t, const unsigned* flags, unsigned e) {
+  int ok = !(t.err && *(volatile int*)t.err);
+  const long long limit = t.wait_ns ? *(const volatile long long*)t.wait_ns : 5000000000ll;
+  for (int r = 0; r < t.world && ok; ++r) ok = bounded_wait_eq(flags + r, e, limit);
+  if (!ok && t.err) atomicExch(t.err, 1);
+  return ok;
+}
+
 // grid (ceil(d / 1024), M), 256 threads: wait (bounded) for the R partials of
 // this epoch, h += their sum in rank order, statistics as k_resid_stats; the
 // last CTA advances the epoch.
@@ -2903,20 +2934,7 @@ __global__ void __launch_bounds__(256) k_tp_reduce(ResidArgs a, TPArgs t, unsign
   __shared__ int s_ok;
   const unsigned e = __ldcg(epoch);
   const unsigned* fl = t.flag[t.rank] + (e & 1u) * kMaxTP;
-  if (threadIdx.x == 0) {
-    int ok = 1;
-    for (int r = 0; r < t.world && ok; ++r) {
-      unsigned v = 0;
-      long long spin = 0;
-      for (; spin < (1ll << 24); ++spin) {
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(fl + r) : "memory");
-        if (v == e) break;
-      }
-      if (v != e) ok = 0;
-    }
-    if (!ok && t.err) atomicExch(t.err, 1);
-    s_ok = ok;
-  }
+  if (threadIdx.x == 0) s_ok = tp_wait_all(t, fl, e);
   __syncthreads();
   const int m = blockIdx.y, blk = blockIdx.x;
   const float* red = t.red[t.rank] + (size_t)(e & 1u) * t.world * kMaxTokens * a.d;
@@ -2978,6 +2996,66 @@ cudaError_t launch_tp_reduce(const ResidArgs& a, const TPArgs& t, unsigned* epoc
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, k_tp_reduce, a, t, epoch, cnt);
+}
+
+// One CTA of 64 threads, one per token (n_seq * seq_len <= kMaxTokens): this
+// rank's argmax keys go into slot `rank` of key set e % 2 in every rank's
+// buffer, then its flag e; after a bounded wait for every rank's flag each
+// key becomes the largest over the ranks (the largest logit, ties to the
+// lowest global index).  On an expired wait the keys stay this rank's own
+// and the error word is raised.
+__global__ void __launch_bounds__(kMaxTokens) k_tp_keys(TPArgs t, unsigned long long* keys,
+                                                        int n_seq, int seq_len, int key_stride) {
+  grid_launch_dependents();
+  grid_wait();
+  __shared__ int s_ok;
+  const unsigned e = *(volatile unsigned*)t.kepoch;
+  const int set = (int)(e & 1u);
+  const int n = n_seq * seq_len;
+  const int i = threadIdx.x;
+  const size_t kidx = i < n ? (size_t)(i / seq_len) * key_stride + i % seq_len : 0;
+  if (i < n) {
+    const unsigned long long k = __ldcg(keys + kidx);
+    for (int r = 0; r < t.world; ++r)
+      t.keyx[r][((size_t)set * kMaxTP + t.rank) * kMaxTokens + i] = k;
+  }
+  __syncthreads();
+  if (i == 0) {
+    __threadfence_system();
+    for (int r = 0; r < t.world; ++r)
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(t.kflag[r] + set * kMaxTP + t.rank),
+                   "r"(e)
+                   : "memory");
+    s_ok = tp_wait_all(t, t.kflag[t.rank] + set * kMaxTP, e);
+  }
+  __syncthreads();
+  if (i < n && s_ok) {
+    const unsigned long long* in = t.keyx[t.rank] + (size_t)set * kMaxTP * kMaxTokens + i;
+    unsigned long long m = 0ull;
+    for (int r = 0; r < t.world; ++r) {
+      const unsigned long long k = __ldcg(in + (size_t)r * kMaxTokens);
+      m = k > m ? k : m;
+    }
+    keys[kidx] = m;
+  }
+  __syncthreads();
+  if (i == 0) *(volatile unsigned*)t.kepoch = e + 1u;
+}
+
+cudaError_t launch_tp_keys(const TPArgs& t, unsigned long long* keys, int n_seq, int seq_len,
+                           int key_stride, cudaStream_t s, bool pdl) {
+  if (t.world < 2 || t.world > kMaxTP || n_seq * seq_len > kMaxTokens || n_seq * seq_len < 1)
+    return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kMaxTokens);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_tp_keys, t, keys, n_seq, seq_len, key_stride);
 }
 
 __global__ void k_set_int(int* p, int v) { *p = v; }

@@ -171,6 +171,10 @@ class Session:
         blob = b"".join(bytes(h) for h in handles)
         check(lib().mc_session_tp_open_peers(self.handle, blob))
 
+    def set_wait_timeout(self, ms: int):
+        """Limit of every bounded device wait (a tensor-parallel peer's flag)."""
+        check(lib().mc_session_set_wait_timeout(self.handle, ms))
+
     def set_seed(self, seed: int):
         """Seed of the stochastic rounds from the next round on."""
         check(lib().mc_spec_set_seed(self.handle, seed))
@@ -188,7 +192,12 @@ class Session:
         return int(lib().mc_session_round_launches(self.handle))
 
     def cancel(self):
+        """Raise the cancel flag: a running or later decode returns
+        MC_E_CANCELLED at its next look (at most every 64 rounds)."""
         self._cancel.value = 1
+
+    def uncancel(self):
+        self._cancel.value = 0
 
     def close(self):
         if getattr(self, "handle", None):

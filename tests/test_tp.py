@@ -9,9 +9,12 @@ first-index argmax (generate.rs:1088-1098 tie rule).
 
 GPU (2, 4 and 8 ranks, each skipped without that many devices): every rank
 holds its shard of the target and a replicated draft and decodes greedily -
-with NCCL all-reduces in the round graph, and with the fused NVLink
-reduction (partial rows stored into every rank's buffer by the GEMV) - and
-produces exactly the oracle's tokens and accepted counts.
+with NCCL all-reduces in the round graph; with the fused NVLink exchange
+(partial rows stored into every rank's buffer by the GEMV, argmax keys
+merged over peer memory) next to an NCCL communicator; and with the fused
+exchange alone, no NCCL at all - and produces exactly the oracle's tokens and
+accepted counts.  Two ranks also run as two host threads of one process,
+whose exchange buffers open each other directly.
 """
 import os
 import sys
@@ -114,7 +117,8 @@ def _gpu_rank(rank, world, uid, cfg_args, prompt, gamma, fused, port, q):
         W = mb.Weights(tw, cfg, device=rank, tp_rank=rank, tp_world=world)
         D = mb.Weights(dw, cfg.with_layers(1), device=rank)
         s = mb.Session(W, D, gamma=gamma, max_context=128)
-        s.tp_init(uid, rank, world)
+        if fused != "fused-only":
+            s.tp_init(uid, rank, world)
         if fused:
             handles = [None] * world
             dist.all_gather_object(handles, s.tp_ipc_handle())
@@ -133,14 +137,7 @@ TP_CFGS = {2: (2, 128, 4, 2, 32, 192, 260), 4: (2, 256, 8, 4, 32, 384, 520),
            8: (2, 256, 8, 8, 32, 512, 1032)}
 
 
-@pytest.mark.gpu
-@pytest.mark.parametrize("world", [2, 4, 8])
-@pytest.mark.parametrize("fused", [False, True], ids=["nccl", "fused-nvlink"])
-def test_tp_spec_decode_matches_oracle(world, fused):
-    import torch
-    if torch.cuda.device_count() < world:
-        pytest.skip(f"needs {world} GPUs")
-    import torch.multiprocessing as mp
+def _tp_reference(world):
     import oracle as o
     import modelc_b200 as mb
     from modelc_b200.model import LlamaConfig, MODE_GENERAL
@@ -156,12 +153,26 @@ def test_tp_spec_decode_matches_oracle(world, fused):
                              rope_base=c.rope_theta, eps=c.eps)
     ref, racc = om(tw, cfg).speculative_generate(
         prompt, 24, 4, o.OracleLlamaDraft(om(dw, cfg.with_layers(1)), 128))
+    return cfg, tw, dw, prompt, ref, racc
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("fused", [False, True, "fused-only"],
+                         ids=["nccl", "fused-nvlink", "fused-only"])
+def test_tp_spec_decode_matches_oracle(world, fused):
+    import torch
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    import modelc_b200 as mb
+    cfg, tw, dw, prompt, ref, racc = _tp_reference(world)
     uid = mb.tp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     args = (cfg.n_layers, cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn,
             cfg.vocab, cfg.rope_theta, cfg.eps, cfg.mode, cfg.name)
-    port = 31000 + (os.getpid() % 2000) + (7 if fused else 0) + 13 * world
+    port = 31000 + (os.getpid() % 2000) + {False: 0, True: 7, "fused-only": 3}[fused] + 13 * world
     procs = [ctx.Process(target=_gpu_rank, args=(r, world, uid, args, prompt, 4, fused, port, q))
              for r in range(world)]
     for p in procs:
@@ -171,5 +182,56 @@ def test_tp_spec_decode_matches_oracle(world, fused):
         p.join(timeout=120)
         assert p.exitcode == 0
     for _, toks, acc in res:
+        assert toks == ref
+        assert acc == racc
+
+
+@pytest.mark.gpu
+def test_tp_ranks_as_threads_of_one_process():
+    """Two ranks as two host threads of this process (one GPU each): their
+    exchange buffers open each other directly (CUDA IPC cannot map an
+    allocation into the process that made it), no NCCL."""
+    import threading
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import modelc_b200 as mb
+    cfg, tw, dw, prompt, ref, racc = _tp_reference(2)
+    sessions, handles, out = [None, None], [None, None], [None, None]
+    errors = []
+    bar = threading.Barrier(2, timeout=120)
+
+    def rank(r):
+        try:
+            W = mb.Weights(tw, cfg, device=r, tp_rank=r, tp_world=2)
+            D = mb.Weights(dw, cfg.with_layers(1), device=r)
+            s = mb.Session(W, D, gamma=4, max_context=128)
+            sessions[r] = (W, D, s)
+            handles[r] = s.tp_ipc_handle()
+            bar.wait()
+            s.tp_open_peers(handles)
+            bar.wait()
+            out[r] = s.speculative_generate(prompt, 24)
+        except Exception as e:  # reported below; the barrier frees the peer
+            errors.append(repr(e))
+            bar.abort()
+        finally:
+            try:
+                bar.wait()  # no rank frees its buffer while the peer may write it
+            except threading.BrokenBarrierError:
+                pass
+
+    th = [threading.Thread(target=rank, args=(r,)) for r in range(2)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join(timeout=300)
+    for trio in sessions:
+        if trio:
+            trio[2].close()
+            trio[0].close()
+            trio[1].close()
+    assert not errors, errors
+    for toks, acc in out:
         assert toks == ref
         assert acc == racc
