@@ -154,9 +154,25 @@ MC_API int64_t mc_weights_bytes(const mc_weights* w);
 
 /* A session = one request: target KV (and draft KV when draft != NULL).
  * Replaces make_kv_cache (generate.rs:18-24) + the per-request state of
- * speculative_generate (generate.rs:598-637). */
+ * speculative_generate (generate.rs:598-637).  The drafter of its rounds is
+ * the transformer draft; with draft == NULL it is the reference's default,
+ * the trigram n-gram index of the context (speculative_generate with
+ * draft_model None, generate.rs:615, :642-646, :771-841): the prompt's
+ * windows, plus after every round or fallback step the window ending at the
+ * last token (update_ngram_index), drafts of up to gamma most-frequent
+ * continuations (count ties: the earliest window), and when no key matches,
+ * one standard generation step (generate.rs:647-693, not counted as a round).
+ * Drafters other than the transformer draft decode greedily (temperature 0). */
 MC_API mc_status mc_session_create(const mc_weights* target, const mc_weights* draft,
                             const mc_spec_cfg* cfg, mc_session** out);
+/* A session whose rounds draft with MlpDraftModel (draft.rs:91-147) on the
+ * device, as modelc's server wires it (serve/mod.rs:151-166 ->
+ * speculative_generate's draft_model, generate.rs:642-646): gamma greedy
+ * steps from the context's last token, then the batched verify and
+ * acceptance.  The drafter is borrowed: keep it alive while the session
+ * exists.  Greedy only (temperature 0). */
+MC_API mc_status mc_session_create_mlp(const mc_weights* target, const mc_mlp_drafter* draft,
+                                const mc_spec_cfg* cfg, mc_session** out);
 MC_API mc_status mc_session_destroy(mc_session* s);
 
 /* Batched forward_llama_cached (transformer.rs:64-96): forwards n token ids

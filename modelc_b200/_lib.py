@@ -31,7 +31,7 @@ EXPORTS = [
     "mc_session_tp_open_peers", "mc_speculative_generate_batch", "mc_spec_prime_batch",
     "mc_spec_read_request", "mc_mlp_draft_create", "mc_mlp_draft", "mc_mlp_draft_destroy",
     "mc_ngram_draft_create", "mc_ngram_draft", "mc_ngram_draft_destroy", "mc_sample_rows",
-    "mc_session_set_wait_timeout",
+    "mc_session_set_wait_timeout", "mc_session_create_mlp",
 ]
 
 
@@ -96,6 +96,7 @@ def lib():
         "mc_weights_destroy": (i32, [vp]),
         "mc_weights_bytes": (i64, [vp]),
         "mc_session_create": (i32, [vp, vp, C.POINTER(SpecCfg), C.POINTER(vp)]),
+        "mc_session_create_mlp": (i32, [vp, vp, C.POINTER(SpecCfg), C.POINTER(vp)]),
         "mc_session_destroy": (i32, [vp]),
         "mc_forward": (i32, [vp, u32p, i32, fp]),
         "mc_draft_forward": (i32, [vp, u32p, i32, fp]),

@@ -850,7 +850,22 @@ struct mc_session {
   // limit of every bounded device wait, in nanoseconds (device word)
   long long* wait_ns = nullptr;
   bool failed = false;  // an earlier bounded wait expired: the session is unusable
+  // drafters without a transformer draft: the MLP drafter (borrowed; the
+  // caller keeps it alive), or, with neither, the n-gram drafter
+  const mc_mlp_drafter* mlp = nullptr;
+  float* mlp_hid = nullptr;  // [B][dh]
+  int* ng = nullptr;         // [B][ctx_stride] n-gram index: window starts
+  int* ng_list = nullptr;    // [B][ctx_stride] n-gram scratch
 };
+
+// The drafter a session's rounds run (DraftModel, draft.rs:18-21; without a
+// draft model speculative_generate drafts from its trigram index,
+// generate.rs:615, :642-646).
+enum DraftKind { DRAFT_LLAMA = 0, DRAFT_MLP = 1, DRAFT_NGRAM = 2 };
+constexpr int kNgram = 3;  // generate.rs:615: let n = 3usize
+static DraftKind draft_kind(const mc_session* s) {
+  return s->dw ? DRAFT_LLAMA : (s->mlp ? DRAFT_MLP : DRAFT_NGRAM);
+}
 
 static int trace_slot(mc_session* s) { return s->trace_on ? ++s->trace_next : 0; }
 
@@ -1024,6 +1039,11 @@ static mc_status session_alloc(mc_session* s) {
   CK(cudaMemset(s->st, 0, sizeof(SpecState) * s->B));
   s->ctx_stride = s->cap + 8;
   CKS(s->al.alloc(&s->ctx, (size_t)s->B * s->ctx_stride));
+  if (!s->dw) {
+    CKS(s->al.alloc(&s->ng, (size_t)s->B * s->ctx_stride));
+    CKS(s->al.alloc(&s->ng_list, (size_t)s->B * s->ctx_stride));
+  }
+  if (s->mlp) CKS(s->al.alloc(&s->mlp_hid, (size_t)s->B * mlp_hidden(s->mlp)));
   CKS(s->al.alloc(&s->acc_log, (size_t)s->B * s->ctx_stride));
   CKS(s->al.alloc(&s->fkeys, (size_t)kMaxTokens));
   CKS(s->al.alloc(&s->ids, (size_t)M));
@@ -1033,10 +1053,19 @@ static mc_status session_alloc(mc_session* s) {
   return MC_OK;
 }
 
-extern "C" mc_status mc_session_create(const mc_weights* target, const mc_weights* draft,
-                                       const mc_spec_cfg* cfg, mc_session** out) {
+static mc_status session_create(const mc_weights* target, const mc_weights* draft,
+                                const mc_mlp_drafter* mlp, const mc_spec_cfg* cfg,
+                                mc_session** out) {
   if (!target || !cfg || !out) return set_err(MC_E_INVALID, "null argument");
   *out = nullptr;
+  if (mlp && mlp_device(mlp) != target->dev)
+    return set_err(MC_E_INVALID, "target and MLP drafter live on different devices");
+  if (mlp && mlp_vocab(mlp) != target->V)
+    return set_err(MC_E_SHAPE, "MLP drafter vocab %d != target vocab %d", mlp_vocab(mlp),
+                   target->V);
+  if (mlp && cfg->temperature > 0.0f)
+    return set_err(MC_E_INVALID, "the MLP drafter drafts greedily: use temperature 0 (the "
+                   "reference samples it with an unseeded generator, draft.rs:140)");
   if (draft && draft->dev != target->dev)
     return set_err(MC_E_INVALID, "target and draft live on different devices");
   if (cfg->gamma < 0 || cfg->gamma + 1 > kGroupTokens)
@@ -1070,6 +1099,7 @@ extern "C" mc_status mc_session_create(const mc_weights* target, const mc_weight
   mc_session* s = new mc_session();
   s->tw = target;
   s->dw = draft;
+  s->mlp = mlp;
   s->cfg = *cfg;
   s->B = B;
   s->dev = target->dev;
@@ -1088,6 +1118,17 @@ extern "C" mc_status mc_session_create(const mc_weights* target, const mc_weight
   }
   *out = s;
   return MC_OK;
+}
+
+extern "C" mc_status mc_session_create(const mc_weights* target, const mc_weights* draft,
+                                       const mc_spec_cfg* cfg, mc_session** out) {
+  return session_create(target, draft, nullptr, cfg, out);
+}
+
+extern "C" mc_status mc_session_create_mlp(const mc_weights* target, const mc_mlp_drafter* draft,
+                                           const mc_spec_cfg* cfg, mc_session** out) {
+  if (!draft) return set_err(MC_E_INVALID, "null MLP drafter");
+  return session_create(target, nullptr, draft, cfg, out);
 }
 
 extern "C" mc_status mc_session_destroy(mc_session* s) {
@@ -1562,6 +1603,20 @@ static mc_status capture_verify(mc_session* s) {
   return MC_OK;
 }
 
+// Kernel launches of one round: the drafter's steps, the verify forward,
+// the acceptance (and the stochastic draft samples).
+static int round_launch_count(const mc_session* s) {
+  const int g = s->cfg.gamma;
+  const int dsteps = g + (s->cfg.bonus ? 1 : 0);
+  int draft = 0;
+  switch (draft_kind(s)) {
+    case DRAFT_LLAMA: draft = dsteps * forward_launches(s->dw); break;
+    case DRAFT_MLP: draft = 2 * g; break;
+    case DRAFT_NGRAM: draft = 1; break;
+  }
+  return draft + forward_launches(s->tw) + 1 + (s->cfg.temperature > 0.0f ? g : 0);
+}
+
 static mc_status capture_round(mc_session* s) {
   if (s->round_exec) return MC_OK;
   const int g = s->cfg.gamma;
@@ -1575,7 +1630,15 @@ static mc_status capture_round(mc_session* s) {
   const int V = s->tw->V;
   // draft step j: one token per request (request z's at its draft length + j)
   const SeqMap dsm{1, kStateInts, s->dkv.n_pages, kStateKeys};
-  for (int j = 0; j < dsteps && rc == MC_OK; ++j) {
+  if (draft_kind(s) == DRAFT_MLP) {
+    cudaError_t e = mlp_round(s->mlp, st, s->ctx, s->ctx_stride, s->B, g, s->mlp_hid, s->stream);
+    if (e != cudaSuccess) rc = set_err(MC_E_CUDA, "MLP draft: %s", cudaGetErrorString(e));
+  } else if (draft_kind(s) == DRAFT_NGRAM) {
+    cudaError_t e = launch_ngram_round(st, s->ctx, s->ng, s->ng_list, s->ctx_stride, s->B,
+                                       s->stream);
+    if (e != cudaSuccess) rc = set_err(MC_E_CUDA, "n-gram draft: %s", cudaGetErrorString(e));
+  }
+  for (int j = 0; j < dsteps && rc == MC_OK && s->dw; ++j) {
     EmbedArgs ea{};
     if (j == 0) {
       ea.src = SRC_CTX_AT;
@@ -1611,8 +1674,7 @@ static mc_status capture_round(mc_session* s) {
   e = cudaGraphInstantiate(&s->round_exec, graph, 0);
   cudaGraphDestroy(graph);
   if (e != cudaSuccess) return set_err(MC_E_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
-  s->round_launches = dsteps * forward_launches(s->dw) + forward_launches(s->tw) + 1 +
-                      (stochastic ? g : 0);
+  s->round_launches = round_launch_count(s);
   return MC_OK;
 }
 
@@ -1633,6 +1695,10 @@ static SpecState fresh_state(const mc_session* s, int n_prompt) {
   h.seed_hi = (uint32_t)(s->cfg.seed >> 32);
   h.top_p = s->cfg.top_p;
   h.min_p = s->cfg.min_p;
+  h.n_draft = s->cfg.gamma;
+  h.ngram = kNgram;
+  h.ng_len = std::max(0, n_prompt - kNgram);  // build_ngram_index over the prompt
+  h.ng_last_len = n_prompt;
   return h;
 }
 
@@ -1652,7 +1718,7 @@ static mc_status prime_request(mc_session* s, int z, int n_prompt) {
     CKS(enq_forward(s, s->tw, tkv, M, SeqMap{M, 0, 0, 0}, ea, s->pos, 0, s->fkeys, nullptr));
   }
   // the draft gets all but the last prompt token (the first round forwards it)
-  for (int c0 = 0; c0 < n_prompt - 1; c0 += kChunk) {
+  for (int c0 = 0; c0 < n_prompt - 1 && s->dw; c0 += kChunk) {
     const int M = std::min(kChunk, n_prompt - 1 - c0);
     CK(launch_set_int(s->pos + 1, c0, s->stream));
     EmbedArgs ea{};
@@ -1668,7 +1734,9 @@ extern "C" mc_status mc_spec_prime_batch(mc_session* s, const uint32_t* prompts,
   if (!s || !lens || !prompts) return set_err(MC_E_INVALID, "bad arguments");
   if (n_requests != s->B)
     return set_err(MC_E_INVALID, "%d prompts for a session of %d requests", n_requests, s->B);
-  if (!s->dw) return set_err(MC_E_INVALID, "speculative decoding needs a draft model");
+  if (!s->dw && s->cfg.temperature > 0.0f)
+    return set_err(MC_E_INVALID, "stochastic rounds need a transformer draft model (their "
+                   "acceptance reads the draft's distributions)");
   if (s->cfg.gamma < 1) return set_err(MC_E_INVALID, "gamma must be >= 1");
   for (int z = 0; z < n_requests; ++z) {
     if (lens[z] <= 0) return set_err(MC_E_INVALID, "empty prompt (generate.rs:609-611 returns nothing)");
@@ -1687,6 +1755,14 @@ extern "C" mc_status mc_spec_prime_batch(mc_session* s, const uint32_t* prompts,
   }
   CK(cudaMemcpyAsync(s->ctx, s->h_ids, (size_t)n_requests * s->ctx_stride * 4,
                      cudaMemcpyHostToDevice, s->stream));
+  if (s->ng) {  // the n-gram index of each prompt: every window start, ascending
+    std::vector<int> starts((size_t)n_requests * s->ctx_stride, 0);
+    for (int z = 0; z < n_requests; ++z)
+      for (int i = 0; i + kNgram < lens[z]; ++i) starts[(size_t)z * s->ctx_stride + i] = i;
+    CK(cudaMemcpyAsync(s->ng, starts.data(), starts.size() * 4, cudaMemcpyHostToDevice,
+                       s->stream));
+    CK(cudaStreamSynchronize(s->stream));  // starts is a host temporary
+  }
   for (int z = 0; z < n_requests; ++z) CKS(prime_request(s, z, lens[z]));
   std::vector<SpecState> h(n_requests);
   for (int z = 0; z < n_requests; ++z) h[z] = fresh_state(s, lens[z]);
@@ -1937,10 +2013,7 @@ extern "C" mc_status mc_session_set_wait_timeout(mc_session* s, int32_t ms) {
 }
 
 extern "C" int32_t mc_session_round_launches(const mc_session* s) {
-  if (!s || !s->dw) return 0;
-  const int dsteps = s->cfg.gamma + (s->cfg.bonus ? 1 : 0);
-  return dsteps * forward_launches(s->dw) + forward_launches(s->tw) + 1 +
-         (s->cfg.temperature > 0.0f ? s->cfg.gamma : 0);
+  return s ? round_launch_count(s) : 0;
 }
 
 extern "C" mc_status mc_speculative_generate(mc_session* s, const uint32_t* prompt,

@@ -43,11 +43,30 @@ constexpr int kMlpFc1Threads = 128;
 constexpr int kMlpFc2Threads = 256;
 constexpr int kNgramThreads = 1024;
 
+// Where the drafter's steps take their tokens and leave their keys.  The
+// standalone drafter: *first, keys[].  Inside a session's round graph
+// (st != nullptr): sequence z = blockIdx.y starts from its context's last
+// token, ctx + z * ctx_stride at st[z].ctx_len - 1, and its keys are
+// st[z].dkeys; hid holds one row of dh per sequence.
+struct MlpIo {
+  const uint32_t* first;
+  unsigned long long* keys;
+  mc::SpecState* st;
+  const uint32_t* ctx;
+  int ctx_stride;
+};
+__device__ __forceinline__ unsigned long long* mlp_keys(const MlpIo& io) {
+  return io.st ? io.st[blockIdx.y].dkeys : io.keys;
+}
 // Token of draft step s: the context's last token, then the previous step's
 // argmax.
-__device__ __forceinline__ uint32_t mlp_token(const uint32_t* first,
-                                              const unsigned long long* keys, int s) {
-  return s == 0 ? *first : key_index(keys[s - 1]);
+__device__ __forceinline__ uint32_t mlp_token(const MlpIo& io, int s) {
+  if (s > 0) return key_index(mlp_keys(io)[s - 1]);
+  if (io.st) {
+    const mc::SpecState* st = io.st + blockIdx.y;
+    return io.ctx[(size_t)blockIdx.y * io.ctx_stride + st->ctx_len - 1];
+  }
+  return *io.first;
 }
 
 // FC1 + ReLU of step s (draft.rs:104-113): hid[i] = max(b1[i] + sum_j
@@ -57,11 +76,13 @@ __device__ __forceinline__ uint32_t mlp_token(const uint32_t* first,
 __global__ void __launch_bounds__(kMlpFc1Threads) k_mlp_fc1(const float* __restrict__ embed,
                                                             const float* __restrict__ w1,
                                                             const float* __restrict__ b1, int V,
-                                                            int d, int dh, const uint32_t* first,
-                                                            const unsigned long long* keys, int s,
+                                                            int d, int dh, MlpIo io, int s,
                                                             float* __restrict__ hid) {
   extern __shared__ float se[];
-  const uint32_t t = mlp_token(first, keys, s);
+  const uint32_t t = mlp_token(io, s);
+  // step s's key collects FC2's atomicMax after this launch: start it at 0
+  if (blockIdx.x == 0 && threadIdx.x == 0) mlp_keys(io)[s] = 0ull;
+  hid += (size_t)blockIdx.y * dh;
   if ((size_t)t * d + d > (size_t)V * d) return;  // block-uniform
   const float* e = embed + (size_t)t * d;
   for (int j = threadIdx.x; j < d; j += blockDim.x) se[j] = e[j];
@@ -87,11 +108,12 @@ __global__ void __launch_bounds__(kMlpFc1Threads) k_mlp_fc1(const float* __restr
 // chosen) folded into keys[s]: one thread per vocabulary row.
 __global__ void __launch_bounds__(kMlpFc2Threads) k_mlp_fc2(const float* __restrict__ w2,
                                                             const float* __restrict__ b2, int V,
-                                                            int d, int dh, const uint32_t* first,
-                                                            unsigned long long* keys, int s,
+                                                            int d, int dh, MlpIo io, int s,
                                                             const float* __restrict__ hid) {
   extern __shared__ float sh[];
-  const uint32_t t = mlp_token(first, keys, s);
+  const uint32_t t = mlp_token(io, s);
+  unsigned long long* keys = mlp_keys(io);
+  hid += (size_t)blockIdx.y * dh;
   const bool in = (size_t)t * d + d <= (size_t)V * d;
   for (int j = threadIdx.x; j < dh; j += blockDim.x) sh[j] = in ? hid[j] : 0.0f;
   __syncthreads();
@@ -114,66 +136,135 @@ __global__ void __launch_bounds__(kMlpFc2Threads) k_mlp_fc2(const float* __restr
   if ((threadIdx.x & 31) == 0 && k) atomicMax(keys + s, k);
 }
 
-// draft_tokens over the index of toks[0, n_tok) (generate.rs:804-841): step
-// g looks up the last n tokens of toks[0, n_tok + g), collects the windows
-// s (s + n < n_tok) whose key matches, and appends the continuation with the
-// highest count -- ties to the one whose first window comes first.  Stops
-// at the first step without a match.  list: scratch of n_tok ints.
+// One step of draft_tokens (generate.rs:804-841) + most_frequent
+// (:832-841), block-wide: among the index entries whose n-token key equals
+// key[0, n) (shared memory), the continuation with the highest count; count
+// ties go to the continuation of the earliest entry (the reference leaves
+// them to HashMap order).  Entry e is the window starting at toks[ent(e)]
+// (key toks[s .. s + n), continuation toks[s + n]); entries ascend.  list:
+// scratch of n_ent ints.  Returns the token, or -1 when no key matches.
+template <class Ent>
+__device__ long long ngram_step(const uint32_t* toks, Ent ent, int n_ent, int n,
+                                const uint32_t* key, int* list, int* s_nm,
+                                unsigned long long* s_best) {
+  if (threadIdx.x == 0) *s_nm = 0;
+  __syncthreads();
+  for (int e = threadIdx.x; e < n_ent; e += blockDim.x) {
+    const int s = ent(e);
+    bool eq = true;
+    for (int q = 0; q < n && eq; ++q) eq = toks[s + q] == key[q];
+    if (eq) list[atomicAdd(s_nm, 1)] = s;
+  }
+  __syncthreads();
+  const int nm = *s_nm;
+  if (nm == 0) return -1;  // block-uniform
+  // (count, -first window) of each match's continuation, packed so that the
+  // largest key is the most frequent, earliest-seen continuation
+  unsigned long long best = 0ull;
+  for (int i = threadIdx.x; i < nm; i += blockDim.x) {
+    const uint32_t c = toks[list[i] + n];
+    unsigned count = 0;
+    int first = 0x7fffffff;
+    for (int j = 0; j < nm; ++j)
+      if (toks[list[j] + n] == c) {
+        ++count;
+        first = min(first, list[j]);
+      }
+    const unsigned long long k = ((unsigned long long)count << 32) |
+                                 (unsigned long long)(0x7fffffffu - (unsigned)first);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const unsigned long long b2 = __shfl_xor_sync(0xffffffffu, best, o);
+    best = b2 > best ? b2 : best;
+  }
+  if ((threadIdx.x & 31) == 0) s_best[threadIdx.x >> 5] = best;
+  __syncthreads();
+  unsigned long long b = 0ull;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) b = s_best[w] > b ? s_best[w] : b;
+  const int first = (int)(0x7fffffffu - (unsigned)(b & 0xffffffffull));
+  __syncthreads();  // s_best and list may be reused by the next step
+  return (long long)toks[first + n];
+}
+
+// draft_tokens over the index of toks[0, n_tok) (build_ngram_index: every
+// window): step g looks up the last n tokens of toks[0, n_tok + g) and
+// appends the continuation ngram_step picks.  Stops at the first step without
+// a match.  list: scratch of n_tok ints.
 __global__ void __launch_bounds__(kNgramThreads) k_ngram_draft(uint32_t* toks, int n_tok, int n,
                                                                int gamma, int* list,
                                                                uint32_t* out, int* n_out) {
   __shared__ int s_nm;
   __shared__ unsigned long long s_best[kNgramThreads / 32];
+  __shared__ uint32_t s_key[32];
   int produced = 0;
   for (int g = 0; g < gamma; ++g) {
     const int clen = n_tok + g;
-    if (clen < n || n < 1) break;  // a short key matches no n-token key (block-uniform)
-    const uint32_t* key = toks + clen - n;
-    if (threadIdx.x == 0) s_nm = 0;
+    if (clen < n || n < 1 || n > 32) break;  // a short key matches no n-token key (block-uniform)
+    if (threadIdx.x < n) s_key[threadIdx.x] = toks[clen - n + threadIdx.x];
     __syncthreads();
-    for (int s = threadIdx.x; s + n < n_tok; s += blockDim.x) {
-      bool eq = true;
-      for (int q = 0; q < n && eq; ++q) eq = toks[s + q] == key[q];
-      if (eq) list[atomicAdd(&s_nm, 1)] = s;
-    }
-    __syncthreads();
-    const int nm = s_nm;
-    if (nm == 0) break;  // block-uniform
-    // (count, -first window) of each match's continuation, packed so that
-    // the largest key is the most frequent, earliest-seen continuation
-    unsigned long long best = 0ull;
-    for (int i = threadIdx.x; i < nm; i += blockDim.x) {
-      const uint32_t c = toks[list[i] + n];
-      unsigned count = 0;
-      int first = n_tok;
-      for (int j = 0; j < nm; ++j)
-        if (toks[list[j] + n] == c) {
-          ++count;
-          first = min(first, list[j]);
-        }
-      const unsigned long long k = ((unsigned long long)count << 32) |
-                                   (unsigned long long)(0x7fffffffu - (unsigned)first);
-      best = k > best ? k : best;
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      const unsigned long long b2 = __shfl_xor_sync(0xffffffffu, best, o);
-      best = b2 > best ? b2 : best;
-    }
-    if ((threadIdx.x & 31) == 0) s_best[threadIdx.x >> 5] = best;
-    __syncthreads();
+    const long long next = ngram_step(toks, [](int e) { return e; }, max(n_tok - n, 0), n, s_key,
+                                      list, &s_nm, s_best);
+    if (next < 0) break;  // block-uniform
     if (threadIdx.x == 0) {
-      unsigned long long b = 0ull;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) b = s_best[w] > b ? s_best[w] : b;
-      const int first = (int)(0x7fffffffu - (unsigned)(b & 0xffffffffull));
-      const uint32_t next = toks[first + n];
-      toks[clen] = next;  // the draft extends the lookup context, not the index
-      out[g] = next;
+      toks[clen] = (uint32_t)next;  // the draft extends the lookup context, not the index
+      out[g] = (uint32_t)next;
     }
     ++produced;
     __syncthreads();
   }
   if (threadIdx.x == 0) *n_out = produced;
+}
+
+// The n-gram drafter of a session's round (see launch_ngram_round): one CTA
+// per sequence.  The index is the prompt's windows plus, per earlier round or
+// fallback step, the window ending at the context's last token
+// (update_ngram_index adds only that one).
+__global__ void __launch_bounds__(kNgramThreads) k_ngram_round(mc::SpecState* st_all,
+                                                               const uint32_t* ctx_all, int* ng_all,
+                                                               int* list_all, int ctx_stride) {
+  __shared__ int s_nm, s_len, s_nent, s_stop;
+  __shared__ unsigned long long s_best[kNgramThreads / 32];
+  __shared__ uint32_t s_tok[32 + mc::kGroupTokens];  // the key window, then the drafts
+  const int z = blockIdx.x;
+  mc::SpecState* st = st_all + z;
+  const uint32_t* ctx = ctx_all + (size_t)z * ctx_stride;
+  int* ng = ng_all + (size_t)z * ctx_stride;
+  int* list = list_all + (size_t)z * ctx_stride;
+  const int n = st->ngram, gamma = st->gamma;
+  if (threadIdx.x == 0) {
+    // a request whose budget is spent takes no more rounds (generate.rs:638)
+    s_stop = (st->max_tokens > 0 && st->generated >= st->max_tokens) || n < 1 || n > 32;
+    const int len = st->ctx_len;
+    if (!s_stop && len > st->ng_last_len) {  // update_ngram_index after the last round
+      if (len >= n + 1) ng[st->ng_len++] = len - (n + 1);
+      st->ng_last_len = len;
+    }
+    s_len = len;
+    s_nent = st->ng_len;
+  }
+  __syncthreads();
+  if (s_stop) return;
+  const int len = s_len;
+  const int base = len - n;  // s_tok[i] holds context position base + i
+  if (threadIdx.x < n) s_tok[threadIdx.x] = base + (int)threadIdx.x >= 0 ? ctx[base + threadIdx.x] : 0u;
+  __syncthreads();
+  int produced = 0;
+  for (int g = 0; g < gamma; ++g) {
+    if (len + g < n) break;  // a short key matches no n-token key (block-uniform)
+    const long long next = ngram_step(ctx, [&](int e) { return ng[e]; }, s_nent, n, s_tok + g,
+                                      list, &s_nm, s_best);
+    if (next < 0) break;  // block-uniform
+    if (threadIdx.x == 0) s_tok[n + g] = (uint32_t)next;
+    ++produced;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    st->n_draft = produced;
+    for (int j = 0; j < mc::kGroupTokens; ++j)
+      st->dkeys[j] = j < produced ? argmax_key(0.0f, s_tok[n + j]) : 0ull;
+  }
 }
 
 #define CK(expr)                                                                        \
@@ -214,6 +305,43 @@ struct mc_ngram_drafter {
   uint32_t* h_buf = nullptr; // pinned staging
   cudaStream_t stream = nullptr;
 };
+
+// gamma draft steps (FC1 + ReLU, then FC2 + argmax) for n_seq sequences
+static cudaError_t mlp_steps(const mc_mlp_drafter* m, const MlpIo& io, int n_seq, int gamma,
+                             float* hid, cudaStream_t stream) {
+  const size_t smem1 = (size_t)m->d * sizeof(float), smem2 = (size_t)m->dh * sizeof(float);
+  const dim3 g1((m->dh + kMlpFc1Threads - 1) / kMlpFc1Threads, n_seq);
+  const dim3 g2((m->V + kMlpFc2Threads - 1) / kMlpFc2Threads, n_seq);
+  for (int s = 0; s < gamma; ++s) {
+    k_mlp_fc1<<<g1, kMlpFc1Threads, smem1, stream>>>(m->embed, m->w1, m->b1, m->V, m->d, m->dh,
+                                                      io, s, hid);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    k_mlp_fc2<<<g2, kMlpFc2Threads, smem2, stream>>>(m->w2, m->b2, m->V, m->d, m->dh, io, s, hid);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+namespace mc {
+// The MLP drafter's gamma steps for every sequence of a session's round:
+// tokens from the contexts, keys into st[z].dkeys, hid: n_seq x dh floats.
+cudaError_t mlp_round(const mc_mlp_drafter* m, SpecState* st, const uint32_t* ctx, int ctx_stride,
+                      int n_seq, int gamma, float* hid, cudaStream_t stream) {
+  const MlpIo io{nullptr, nullptr, st, ctx, ctx_stride};
+  return mlp_steps(m, io, n_seq, gamma, hid, stream);
+}
+int mlp_device(const mc_mlp_drafter* m) { return m->dev; }
+int mlp_vocab(const mc_mlp_drafter* m) { return m->V; }
+int mlp_hidden(const mc_mlp_drafter* m) { return m->dh; }
+
+cudaError_t launch_ngram_round(SpecState* st, const uint32_t* ctx, int* ng, int* list,
+                               int ctx_stride, int n_seq, cudaStream_t s) {
+  k_ngram_round<<<n_seq, kNgramThreads, 0, s>>>(st, ctx, ng, list, ctx_stride);
+  return cudaGetLastError();
+}
+}  // namespace mc
 
 static void mlp_free(mc_mlp_drafter* m) {
   cudaSetDevice(m->dev);
@@ -307,15 +435,8 @@ extern "C" mc_status mc_mlp_draft(mc_mlp_drafter* m, const uint32_t* context, in
   const uint32_t cur = n > 0 ? context[n - 1] : 0u;  // draft.rs:130
   CK(cudaMemcpyAsync(m->first, &cur, sizeof(cur), cudaMemcpyHostToDevice, m->stream));
   CK(cudaMemsetAsync(m->keys, 0, (size_t)gamma * sizeof(unsigned long long), m->stream));
-  const size_t smem1 = (size_t)m->d * sizeof(float), smem2 = (size_t)m->dh * sizeof(float);
-  for (int s = 0; s < gamma; ++s) {
-    k_mlp_fc1<<<(m->dh + kMlpFc1Threads - 1) / kMlpFc1Threads, kMlpFc1Threads, smem1, m->stream>>>(
-        m->embed, m->w1, m->b1, m->V, m->d, m->dh, m->first, m->keys, s, m->hid);
-    CK(cudaGetLastError());
-    k_mlp_fc2<<<(m->V + kMlpFc2Threads - 1) / kMlpFc2Threads, kMlpFc2Threads, smem2, m->stream>>>(
-        m->w2, m->b2, m->V, m->d, m->dh, m->first, m->keys, s, m->hid);
-    CK(cudaGetLastError());
-  }
+  const MlpIo io{m->first, m->keys, nullptr, nullptr, 0};
+  CK(mlp_steps(m, io, 1, gamma, m->hid, m->stream));
   unsigned long long keys[mc::kGroupTokens];
   CK(cudaMemcpyAsync(keys, m->keys, (size_t)gamma * sizeof(unsigned long long),
                      cudaMemcpyDeviceToHost, m->stream));

@@ -301,6 +301,14 @@ struct SpecState {
   uint32_t seed_lo, seed_hi;
   float top_p;         // applied when in (0, 1) (generate.rs:961-963)
   float min_p;         // applied when in (0, 1) (generate.rs:964-966)
+  // draft tokens of this round (gamma for the model drafters; the n-gram
+  // drafter may find fewer, 0 meaning the reference's one-step fallback,
+  // generate.rs:647-693), and the n-gram index: its entry count, the context
+  // length its last update saw, the key length n
+  int n_draft;
+  int ng_len;
+  int ng_last_len;
+  int ngram;
   unsigned long long tkeys[kGroupTokens];
   unsigned long long dkeys[kGroupTokens];
 };
@@ -360,6 +368,27 @@ cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t s, bool pdl);
 cudaError_t launch_accept_greedy(SpecState* st, uint32_t* ctx, int* acc_log, int vm, int n_seq,
                                  int ctx_stride, int log_stride, cudaStream_t s, bool pdl);
 cudaError_t launch_set_int(int* p, int v, cudaStream_t s);
+// The n-gram drafter of speculative_generate inside the round graph
+// (generate.rs:642-646 with no draft model; build_ngram_index,
+// update_ngram_index, draft_tokens, generate.rs:771-841), one CTA per
+// sequence z: first the window ending at the context's last token joins the
+// index when the context grew since the last update, then up to gamma draft
+// tokens into st->dkeys and their count into st->n_draft.  The index of
+// sequence z is ng + z * ctx_stride: ascending window starts into its
+// context; list: scratch of the same size.
+cudaError_t launch_ngram_round(SpecState* st, const uint32_t* ctx, int* ng, int* list,
+                               int ctx_stride, int n_seq, cudaStream_t s);
+}  // namespace mc
+typedef struct mc_mlp_drafter mc_mlp_drafter;
+namespace mc {
+// MlpDraftModel (draft.rs:91-147) inside the round graph: gamma greedy steps
+// for each of n_seq sequences from its context's last token, keys into
+// st[z].dkeys; hid is scratch of n_seq x mlp_hidden floats.
+cudaError_t mlp_round(const mc_mlp_drafter* m, SpecState* st, const uint32_t* ctx, int ctx_stride,
+                      int n_seq, int gamma, float* hid, cudaStream_t stream);
+int mlp_device(const mc_mlp_drafter* m);
+int mlp_vocab(const mc_mlp_drafter* m);
+int mlp_hidden(const mc_mlp_drafter* m);
 // Stochastic rounds: sample draft step j from softmax(logits / T) into
 // *key_out (as an argmax key), and the acceptance of a whole round from the
 // verify logits tlog [vm][V] and the draft logits dlog [gamma][V].

@@ -2315,17 +2315,35 @@ __global__ void k_accept_greedy(SpecState* st_all, uint32_t* ctx_all, int* acc_l
   // a request whose budget is spent takes no more rounds (generate.rs:638)
   if (st->max_tokens > 0 && st->generated >= st->max_tokens) return;
   const int g = st->gamma;
+  const int nd = min(max(st->n_draft, 0), g);  // draft tokens this round
+  const int len = st->ctx_len;
+  if (nd == 0) {
+    // no draft (the n-gram index had no match): one standard generation
+    // step, generate.rs:647-693 -- the target's token after the context's
+    // last token, which the verify's first position computed.  Not a round:
+    // no accepted count is logged.
+    ctx[len] = key_index(st->tkeys[0]);
+    st->ctx_len = len + 1;
+    st->lt += 1;
+    st->ld = len;
+    st->generated += 1;
+    return;
+  }
   int a = 0;
-  while (a < g && key_index(st->tkeys[a]) == key_index(st->dkeys[a])) ++a;
-  int len = st->ctx_len;
+  while (a < nd && key_index(st->tkeys[a]) == key_index(st->dkeys[a])) ++a;
   for (int j = 0; j < a; ++j) ctx[len + j] = key_index(st->dkeys[j]);
-  int emitted = a;
-  if (a < vm) {
+  int emitted = a, forwarded = a + 1;
+  if (a < nd) {  // the first mismatch pushes the target's token
     ctx[len + a] = key_index(st->tkeys[a]);
     emitted = a + 1;
+  } else if (vm > g) {  // every draft accepted: the bonus token (vm == gamma + 1)
+    ctx[len + nd] = key_index(st->tkeys[nd]);
+    emitted = nd + 1;
+  } else {  // the reference: d_nd pushed unverified (quirk Q2)
+    forwarded = nd;
   }
   st->ctx_len = len + emitted;
-  st->lt += (a + 1 < vm) ? a + 1 : vm;
+  st->lt += forwarded;
   st->ld = st->ctx_len - 1;
   st->generated += emitted;
   if (acc_log && st->n_rounds < st->rounds_cap) acc_log[st->n_rounds] = a;

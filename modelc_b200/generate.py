@@ -35,13 +35,15 @@ def _u32(a) -> np.ndarray:
 
 class Session:
     """Device state of n_requests concurrent requests (default one): target
-    KV, draft KV and speculative state per request.
+    KV, draft KV and speculative state per request.  ``draft`` is the
+    drafter of the rounds: a transformer draft (Weights), an MlpDraftModel,
+    or None for the reference's trigram n-gram drafter.
 
     Mirrors the reference's per-request ``Option<KvCache>`` (generate.rs:
     617-627) plus the draft model's cache; a batched session decodes its
     requests in lock step, each exactly as it would decode alone."""
 
-    def __init__(self, target: Weights, draft: Weights | None = None, gamma: int = 4,
+    def __init__(self, target: Weights, draft=None, gamma: int = 4,
                  max_context: int = 2048, bonus: bool = False, temperature: float = 0.0,
                  seed: int = 0, accept_mode: int = 0, n_requests: int = 1,
                  top_p: float = 0.0, min_p: float = 0.0):
@@ -52,8 +54,12 @@ class Session:
         cfg = _lib.SpecCfg(gamma, max_context, int(bonus), temperature, seed,
                            C.pointer(self._cancel), accept_mode, n_requests, top_p, min_p)
         h = C.c_void_p()
-        check(lib().mc_session_create(target.handle, draft.handle if draft else None,
-                                      C.byref(cfg), C.byref(h)))
+        if isinstance(draft, MlpDraftModel):  # MlpDraftModel drives the rounds
+            check(lib().mc_session_create_mlp(target.handle, draft.handle, C.byref(cfg),
+                                              C.byref(h)))
+        else:  # a transformer draft, or None: the reference's trigram drafter
+            check(lib().mc_session_create(target.handle, draft.handle if draft else None,
+                                          C.byref(cfg), C.byref(h)))
         self.handle = h
 
     # -- forward_llama_cached (batched) ------------------------------------
