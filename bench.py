@@ -220,6 +220,134 @@ def cpu_tokens_per_s(t_layer, t_head, rounds, tokens, accepted, gamma=GAMMA, tar
     return tokens / total
 
 
+def _dequant_q4_0_torch(blk, rows, cols):
+    """dequant.rs:33-44 on the device: (code - 8) as f32 * d, low nibbles first."""
+    import torch
+    b = blk.view(rows, cols // 32, 18)
+    d = b[..., 0:2].contiguous().view(torch.float16).float()  # [rows, nb, 1]
+    qs = b[..., 2:].to(torch.int32)
+    v = torch.cat([(qs & 0x0F) - 8, (qs >> 4) - 8], dim=2).float() * d
+    return v.reshape(rows, cols)
+
+
+def host_f32_model(cfg, seed, fmt, device, n_threads, keep=None):
+    """The oracle over f32 host copies of the seeded weights build_models
+    loads on the GPU (the same draw, dequantized on the device exactly as the
+    reference dequantizes at load: int8 rows q * scale, q4_0 (code - 8) * d),
+    so the CPU runs the very model the GPU runs.  keep: a dict that receives
+    the arrays (the oracle model holds pointers into them)."""
+    import torch
+    import modelc_b200 as mb
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as o
+    tt = mb.synth_weights_torch(cfg, seed=seed, device=device, fmt=fmt)
+    w = {} if keep is None else keep
+    for name in list(tt):
+        dt, t, extra = tt.pop(name)
+        if dt == "f32":
+            f = t
+        elif dt == "i8_row":
+            f = t.float() * extra[:, None]
+        else:
+            f = _dequant_q4_0_torch(t, *extra)
+        w[name] = f.cpu().numpy()
+        del t, extra, f
+    torch.cuda.empty_cache()
+    c = cfg.resolved()
+    return o.OracleModel(w, c.n_layers, c.hidden, c.vocab, c.ffn, mode=cfg.mode,
+                         n_heads=c.n_heads, n_kv_heads=c.n_kv_heads, head_dim=c.head_dim,
+                         rope_base=c.rope_theta, eps=c.eps, n_threads=n_threads)
+
+
+def cpu_forward_time(model, kv_len, min_s, min_reps=1):
+    """Seconds per single-token forward of a whole oracle model
+    (forward_llama_cached: every layer, the final norm and the LM head) at
+    KV length kv_len, averaged over at least min_s seconds."""
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal(model.m.hidden).astype(np.float32)
+    kv = model.new_kv(kv_len + 8)
+    reps, t0 = 0, time.perf_counter()
+    while reps < min_reps or time.perf_counter() - t0 < min_s:
+        kv.ptr.contents.len = kv_len  # attend over kv_len cached positions
+        model.forward_embedding(x, kv)
+        reps += 1
+    return (time.perf_counter() - t0) / reps, reps
+
+
+def cpu_round_tokens_per_s(t_target, t_draft, rounds, tokens, accepted, gamma):
+    """The reference's cost of this run's rounds, from whole-forward times:
+    per round gamma draft forwards and the sequential verify's target
+    forwards, min(a + 1, gamma) of them after a accepted drafts
+    (generate.rs:641-726); tokens = emitted tokens."""
+    target_fwd = sum(min(a + 1, gamma) for a in accepted) if accepted else rounds
+    total = rounds * gamma * t_draft + target_fwd * t_target
+    return tokens / total
+
+
+def host_bytes_f32(cfg):
+    pc = cfg.param_counts()
+    return 4 * (cfg.n_layers * pc["layer"] + pc["head"] + pc["embed"])
+
+
+def host_fits(*cfgs):
+    """Whether f32 copies of these models fit comfortably in host memory."""
+    try:
+        import psutil
+        avail = psutil.virtual_memory().available
+    except Exception:
+        return False
+    return sum(host_bytes_f32(c) for c in cfgs) < 0.6 * avail
+
+
+def cpu_baseline_full(wl, cfg, device_index, rounds, tokens, accepted):
+    """The reference's CPU path on this host over the very models the GPU
+    ran (f32 copies of the same seeded weights): whole single-token forwards
+    of the target and the draft at KV length prompt + 76, timed (a) on every
+    host thread with the bit-identical row-parallel linear and (b) on one
+    thread with the reference-faithful scalar linear (linear_with has no
+    threading, transformer.rs:825-843), then composed into this run's rounds
+    (cpu_round_tokens_per_s).  Models too large for host memory (the 70B
+    shape) fall back to one timed layer plus the head, extrapolated."""
+    import torch
+    nthr = os.cpu_count() or 1
+    kvl = wl.prompt_len + 76
+    if not host_fits(cfg, wl.draft):
+        t_layer, t_head, rl, rh = cpu_sample(nthr, kvl, cfg)
+        same = (wl.draft.hidden, wl.draft.ffn, wl.draft.vocab) == (cfg.hidden, cfg.ffn, cfg.vocab)
+        tdl, tdh = (t_layer, t_head) if same else cpu_sample(nthr, kvl, wl.draft)[:2]
+        v = cpu_tokens_per_s(t_layer, t_head, rounds, tokens, accepted, wl.gamma, cfg.n_layers,
+                             wl.draft.n_layers, tdl, tdh)
+        return {"value": round(v, 5), "unit": "tokens/s", "cores": nthr, "kind": "port",
+                "sample": (f"f32 weights of this shape exceed host memory: oracle row-parallel "
+                           f"forward of 1 target layer at KV {kvl} ({t_layer * 1e3:.1f} ms, {rl} "
+                           f"reps) + LM head ({t_head * 1e3:.1f} ms, {rh} reps), extrapolated to "
+                           f"{cfg.n_layers} layers + head and {wl.gamma} drafts per round with "
+                           f"this run's acceptance")}
+    dev = torch.device("cuda", device_index)
+    keep_t, keep_d = {}, {}
+    om_t = host_f32_model(cfg, 0, wl.fmt, dev, nthr, keep_t)
+    om_d = host_f32_model(wl.draft, 1, wl.draft_fmt, dev, nthr, keep_d)
+    tt, nt = cpu_forward_time(om_t, kvl, 8.0, 2)
+    td, nd = cpu_forward_time(om_d, kvl, 3.0, 3)
+    v = cpu_round_tokens_per_s(tt, td, rounds, tokens, accepted, wl.gamma)
+    om_t.m.n_threads = 1
+    om_d.m.n_threads = 1
+    tt1, _ = cpu_forward_time(om_t, kvl, 0.0, 1)
+    td1, _ = cpu_forward_time(om_d, kvl, 0.0, 1)
+    v1 = cpu_round_tokens_per_s(tt1, td1, rounds, tokens, accepted, wl.gamma)
+    return {"value": round(v, 5), "unit": "tokens/s", "cores": nthr, "kind": "port",
+            "sample": (f"oracle over f32 copies of this run's models: whole {cfg.n_layers}-layer "
+                       f"target forward at KV {kvl} {tt * 1e3:.1f} ms ({nt} reps), whole "
+                       f"{wl.draft.n_layers}-layer draft forward {td * 1e3:.1f} ms ({nd} reps), "
+                       f"row-parallel on {nthr} threads, composed into this run's {rounds} "
+                       f"rounds ({wl.gamma} draft forwards + min(a+1, gamma) target forwards "
+                       f"each)"),
+            "single_thread": {"value": round(v1, 6), "unit": "tokens/s", "cores": 1,
+                              "sample": (f"the same with the reference-faithful scalar linear on "
+                                         f"one thread: target forward {tt1:.2f} s, draft forward "
+                                         f"{td1:.2f} s")}}
+
+
 # ---------------------------------------------------------------------- GPU
 def build_models(device_index: int, layers: int | None = None, wl: Workload | None = None,
                  tp: tuple = (0, 1)):
@@ -376,24 +504,15 @@ def run_ours(args):
     e2e_value = e2e_tokens * (1 if tp else world) / float(e2e_local.item())
 
     line = None
+    wbytes = target.streamed_bytes
     if rank == 0:
         cpu = None
         if not args.no_cpu and world == 1:
-            nthr = os.cpu_count() or 1
-            kvl = PROMPT_LEN + 76
-            t_layer, t_head, rl, rh = cpu_sample(nthr, kvl, cfg)
-            same = (wl.draft.hidden, wl.draft.ffn, wl.draft.vocab) == (cfg.hidden, cfg.ffn, cfg.vocab)
-            tdl, tdh = (t_layer, t_head) if same else cpu_sample(nthr, kvl, wl.draft)[:2]
-            v = cpu_tokens_per_s(t_layer, t_head, req_rounds, tokens, accepted, GAMMA,
-                                 cfg.n_layers, wl.draft.n_layers, tdl, tdh)
-            cpu = {"value": round(v, 5), "unit": "tokens/s", "cores": nthr, "kind": "port",
-                   "sample": (f"oracle row-parallel f32 forward of 1 target layer at KV {kvl} "
-                              f"({t_layer * 1e3:.1f} ms, {rl} reps) + LM head ({t_head * 1e3:.1f} ms, "
-                              f"{rh} reps), extrapolated to {cfg.n_layers} layers + head per target "
-                              f"forward and {GAMMA} {wl.draft.n_layers}-layer drafts per round with "
-                              f"this run's acceptance")}
+            sess.close()  # free the device before the CPU legs
+            del target, draft
+            torch.cuda.empty_cache()
+            cpu = cpu_baseline_full(wl, cfg, local, req_rounds, tokens, accepted)
         clocks = clk.summary()
-        wbytes = target.streamed_bytes
         line = {
             "metric": wl.metric, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
@@ -416,7 +535,7 @@ def run_ours(args):
         }
     if world > 1:
         torch.distributed.barrier()  # peers may still write into this rank's buffers
-    sess.close()
+    sess.close()  # (already closed before a CPU leg; closing twice is harmless)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -588,27 +707,62 @@ def run_sweep(args):
 
 
 def run_reference(args):
-    rank, world, _ = dist_env()
+    """The reference's CPU path (the oracle's restatement of
+    speculative_generate's rounds) on this host's cores, on the workload's
+    own models: each step is one round at acceptance 0 (unrelated random-init
+    target and draft: the first draft token is rejected, generate.rs:695-726),
+    i.e. gamma whole draft forwards and one whole target forward at KV length
+    prompt + 76, on every host thread with the bit-identical row-parallel
+    linear.  One token per round."""
+    rank, world, local = dist_env()
     if rank != 0:
         return
+    import torch
+    wl = workloads()[args.config]
     nthr = os.cpu_count() or 1
-    vals = []
-    t0 = time.time()
-    # acceptance of unrelated random-init target/draft models is ~1/vocab:
-    # every round emits one token after one target forward
-    for i in range(args.warmup + args.steps):
-        t_layer, t_head, rl, rh = cpu_sample(nthr)
-        if i >= args.warmup:
-            vals.append(cpu_tokens_per_s(t_layer, t_head, 1, 1, [0]))
-    v = statistics.mean(vals)
-    sample = (f"per step: oracle row-parallel f32 forward of 1 target layer at KV 1100 + LM head, "
-              f"extrapolated to one round (32-layer verify forward + {GAMMA} 2-layer draft "
-              f"forwards) emitting one token")
-    line = {"impl": "reference", "metric": METRIC, "value": round(v, 5), "unit": "tokens/s",
+    kvl = wl.prompt_len + 76
+    t_start = time.time()
+    if host_fits(wl.target, wl.draft):
+        dev = torch.device("cuda", local)
+        keep_t, keep_d = {}, {}
+        om_t = host_f32_model(wl.target, 0, wl.fmt, dev, nthr, keep_t)
+        om_d = host_f32_model(wl.draft, 1, wl.draft_fmt, dev, nthr, keep_d)
+        rng = np.random.default_rng(0)
+        xt = rng.standard_normal(om_t.m.hidden).astype(np.float32)
+        xd = rng.standard_normal(om_d.m.hidden).astype(np.float32)
+        kvt, kvd = om_t.new_kv(kvl + 8), om_d.new_kv(kvl + 8)
+        times = []
+        t0 = time.time()
+        for i in range(args.warmup + args.steps):
+            t1 = time.perf_counter()
+            for _ in range(wl.gamma):
+                kvd.ptr.contents.len = kvl
+                om_d.forward_embedding(xd, kvd)
+            kvt.ptr.contents.len = kvl
+            om_t.forward_embedding(xt, kvt)
+            if i >= args.warmup:
+                times.append(time.perf_counter() - t1)
+        v = 1.0 / statistics.mean(times)
+        ms_step = (time.time() - t0) * 1e3 / (args.warmup + args.steps)
+        sample = (f"per step one round: {wl.gamma} whole {wl.draft.n_layers}-layer draft forwards "
+                  f"+ one whole {wl.target.n_layers}-layer target forward at KV {kvl} (f32 copies of "
+                  f"the workload's seeded models), row-parallel on {nthr} threads; one token")
+    else:
+        vals = []
+        for i in range(args.warmup + args.steps):
+            t_layer, t_head, rl, rh = cpu_sample(nthr, kvl, wl.target)
+            if i >= args.warmup:
+                vals.append(cpu_tokens_per_s(t_layer, t_head, 1, 1, [0], wl.gamma,
+                                             wl.target.n_layers, wl.draft.n_layers))
+        v = statistics.mean(vals)
+        ms_step = (time.time() - t_start) * 1e3 / (args.warmup + args.steps)
+        sample = (f"f32 weights of this shape exceed host memory: per step 1 target layer at KV "
+                  f"{kvl} + LM head, extrapolated to one round emitting one token")
+    line = {"impl": "reference", "metric": wl.metric, "value": round(v, 5), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round((time.time() - t0) * 1e3 / (args.warmup + args.steps), 3),
+            "ms_per_step": round(ms_step, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": WORKLOAD, "target": "llama3-8b"},
+            "data": "synthetic", "config": {"workload": wl.desc, "target": wl.target.name},
             "cpu_baseline": {"value": round(v, 5), "unit": "tokens/s", "cores": nthr, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(v, 5), "unit": "tokens/s", "h2d_bytes_per_step": 0,

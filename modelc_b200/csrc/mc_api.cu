@@ -190,6 +190,18 @@ static bool use_tc(const PMat& W, int M) {
   return M > 8 && W.n_stripes >= 512;
 }
 
+// The GEMV variant of a matrix: int8 matrices of at least 96 MiB (the
+// 8B-shape gate/up projection and LM head) stream their weights through the
+// shared-memory ring, where a deeper stream pays; smaller ones keep register
+// batches, whose first batch before the dependency wait costs the producing
+// encoder less.
+constexpr long long kRingMinBytes = 96ll << 20;
+static int gemv_wf(const PMat& W) {
+  if (W.fmt == WF_I8 && (long long)W.n_stripes * W.KB * kFragBytes >= kRingMinBytes)
+    return WF_I8R;
+  return W.fmt;
+}
+
 // CTAs per GEMV launch.  q4_0 partial sums are f32 and the grid sets their
 // k-split, so a q4_0 grid must not depend on the token count: it uses the
 // smallest occupancy over all token tiles.
@@ -237,7 +249,7 @@ static cudaError_t run_projection(const PMat& W, int epi, int M, GemvArgs a, int
     a.m0 = g * kGroupTokens;
     a.M = std::min(kGroupTokens, M - a.m0);
     a.next_w = (g == G - 1) ? next_w : nullptr;
-    cudaError_t e = launch_gemv(a, epi, nt, W.fmt, grid, st, true);
+    cudaError_t e = launch_gemv(a, epi, nt, gemv_wf(W), grid, st, true);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -797,7 +809,6 @@ struct mc_session {
   uint8_t* xq = nullptr;
   int* xexp = nullptr;
   float* qb = nullptr;
-  float* attn = nullptr;
   float* act = nullptr;
   float* logits = nullptr;
   float* dlogits = nullptr;  // draft logits of a stochastic round [kMaxTokens][V]
@@ -805,7 +816,6 @@ struct mc_session {
   int* cnt = nullptr;
   float* part_o = nullptr;
   float* part_ml = nullptr;
-  int* acnt = nullptr;
   int* err = nullptr;  // device flag raised by an expired bounded wait
   // activation statistics handed from each producer to the next encoder:
   // two max|x*w| slots used alternately, and per-stripe sums of squares
@@ -829,7 +839,7 @@ struct mc_session {
   cudaGraphExec_t round_exec = nullptr;
   cudaGraphExec_t verify_exec = nullptr;
   int round_launches = 0;
-  int bps[2][6][7] = {};
+  int bps[3][6][7] = {};
   // MC_TRACE builds: timeline slots handed to the launches of one capture
   bool trace_on = false;
   int trace_next = 0;
@@ -975,8 +985,6 @@ static mc_status session_alloc(mc_session* s) {
   CK(cudaMemset(s->xq, 0, (size_t)kp * 48 * kMaxGroups));
   CKS(s->al.alloc(&s->xexp, (size_t)M));
   CKS(s->al.alloc(&s->qb, (size_t)M * hq));
-  CKS(s->al.alloc(&s->attn, (size_t)M * hq));
-  CK(cudaMemset(s->attn, 0, (size_t)M * hq * 4));
   CKS(s->al.alloc(&s->act, (size_t)M * std::max(F, 1)));
   CKS(s->al.alloc(&s->logits, (size_t)M * V));
   if (s->cfg.temperature > 0.0f) CKS(s->al.alloc(&s->dlogits, (size_t)kGroupTokens * V));
@@ -1018,8 +1026,6 @@ static mc_status session_alloc(mc_session* s) {
     CK(cudaMemset(s->tp_cnt_gemv, 0, 4));
     CK(cudaMemset(s->tp_cnt_red, 0, 4));
   }
-  CKS(s->al.alloc(&s->acnt, (size_t)hkv * 2 * kMaxTokens));
-  CK(cudaMemset(s->acnt, 0, (size_t)hkv * 2 * kMaxTokens * 4));
   CKS(alloc_kv(s, s->tw, &s->tkv));
   if (s->dw) CKS(alloc_kv(s, s->dw, &s->dkv));
   // kernel limits and occupancy are settled here, never inside a capture
@@ -1032,7 +1038,7 @@ static mc_status session_alloc(mc_session* s) {
   }
   CK(prepare_kernels(qsm, asm_));
   CK(prepare_tc());
-  for (int wf : {(int)WF_I8, (int)WF_Q4})
+  for (int wf : {(int)WF_I8, (int)WF_Q4, (int)WF_I8R})
     for (int epi = 0; epi < 6; ++epi)
       for (int nt : {1, 2, 3, 6}) bps_of(s, epi, nt, wf);
   CKS(s->al.alloc(&s->st, (size_t)s->B));
@@ -1209,8 +1215,22 @@ struct StatIO {
 };
 
 static mc_status enq_quant(mc_session* s, const float* h, int ld, int d, int M, const float* w,
-                           float eps, int do_norm, const StatIO* io = nullptr, bool tc = false) {
+                           float eps, int do_norm, const StatIO* io = nullptr, bool tc = false,
+                           const AttnArgs* att = nullptr) {
   QuantArgs q{};
+  if (att) {  // combine the attention's page partials while encoding
+    q.att_o = att->part_o;
+    q.att_ml = att->part_ml;
+    q.att_chunks = att->max_chunks;
+    q.att_Hkv = att->Hkv;
+    q.att_G = att->H / att->Hkv;
+    q.att_hdp = att->hdp;
+    q.att_qblk = att->qblk;
+    q.att_page = att->page;
+    q.att_seq = att->seq;
+    q.att_pos = att->pos_ptr;
+    q.att_pos_add = att->pos_add;
+  }
   q.tc_layout = tc ? 1 : 0;
   if (io) {
     q.use_stats = 1;
@@ -1257,7 +1277,7 @@ static mc_status enq_gemv(mc_session* s, const PMat& W, int epi, int M, GemvArgs
   a.err = s->err;
   a.trace_slot = trace_slot(s);
   CK(run_projection(W, epi, M, a, s->nsm, s->stream,
-                    [&](int t) { return bps_of(s, epi, t, W.fmt); }));
+                    [&](int t) { return bps_of(s, epi, t, gemv_wf(W)); }));
   return MC_OK;
 }
 
@@ -1421,16 +1441,14 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       t.max_chunks = kv.n_pages;
       t.part_o = s->part_o;
       t.part_ml = s->part_ml;
-      t.cnt = s->acnt;
-      t.out = s->attn;
       t.st_amax = slot(ej);
       // the gate/up projection after O: its weights beyond the O GEMV's prefetch
       idle_prefetch(Lw.mlp ? &Lw.gu : nullptr, kIdlePrefetch, &t.pf, &t.pf_bytes);
       t.trace_slot = trace_slot(s);
       CK(launch_attention(t, s->stream, true));
       io = io_for(ej, 0);
-      CKS(enq_quant(s, s->attn, W->H * W->hdp, W->H * W->hdp, M, nullptr, 0.0f, 0, &io,
-                    use_tc(Lw.o, M)));
+      CKS(enq_quant(s, nullptr, W->H * W->hdp, W->H * W->hdp, M, nullptr, 0.0f, 0, &io,
+                    use_tc(Lw.o, M), &t));
       ++ej;
       CKS(residual_gemv(Lw.o, nxt()));
     }
@@ -2057,13 +2075,13 @@ struct mc_linear {
   int* cnt = nullptr;
   int* err = nullptr;
   int nsm = 0;
-  int bps[2][7] = {};
+  int bps[3][7] = {};
 };
 
 static int linear_grid(mc_linear* l, int nt) {
   return gemv_grid(l->m, l->nsm, nt, [&](int t) {
-    int& b = l->bps[l->m.fmt][t];
-    if (!b) b = std::max(1, gemv_blocks_per_sm(EPI_STORE, t, l->m.fmt));
+    int& b = l->bps[gemv_wf(l->m)][t];
+    if (!b) b = std::max(1, gemv_blocks_per_sm(EPI_STORE, t, gemv_wf(l->m)));
     return b;
   });
 }
@@ -2098,7 +2116,7 @@ extern "C" mc_status mc_linear_create(const mc_tensor_desc* w, int32_t device, m
   cudaDeviceGetAttribute(&L->nsm, cudaDevAttrMultiProcessorCount, device);
   if (st == MC_OK)
     for (int nt : {1, 2, 3, 6})
-      L->bps[L->m.fmt][nt] = std::max(1, gemv_blocks_per_sm(EPI_STORE, nt, L->m.fmt));
+      L->bps[gemv_wf(L->m)][nt] = std::max(1, gemv_blocks_per_sm(EPI_STORE, nt, gemv_wf(L->m)));
   if (st != MC_OK) {
     L->al.free_all();
     delete L;
@@ -2150,8 +2168,8 @@ extern "C" mc_status mc_linear_run(mc_linear* l, const float* x_dev, int32_t m, 
     a.ldo = l->m.N;
     a.n_out = l->m.N;
     CK(run_projection(l->m, EPI_STORE, M, a, l->nsm, s, [&](int t) {
-      int& b = l->bps[l->m.fmt][t];
-      if (!b) b = std::max(1, gemv_blocks_per_sm(EPI_STORE, t, l->m.fmt));
+      int& b = l->bps[gemv_wf(l->m)][t];
+      if (!b) b = std::max(1, gemv_blocks_per_sm(EPI_STORE, t, gemv_wf(l->m)));
       return b;
     }));
   }
@@ -2237,7 +2255,7 @@ extern "C" mc_status mc_linear_run_static(mc_linear* l, const float* x_dev, int3
     a.out = y_dev + (size_t)r0 * l->m.N;
     a.ldo = l->m.N;
     a.n_out = l->m.N;
-    CK(launch_gemv(a, EPI_STORE, nt, l->m.fmt, linear_grid(l, nt), s, true));
+    CK(launch_gemv(a, EPI_STORE, nt, gemv_wf(l->m), linear_grid(l, nt), s, true));
   }
   return MC_OK;
 }

@@ -82,7 +82,10 @@ __host__ __device__ inline int key_slot(const SeqMap& s, int m) {
 //          (w & 0x0F0F0F0F) and ((w >> 4) & 0x0F0F0F0F) are the unsigned
 //          codes.  Block scales: one u32 per (stripe, k-block, g) holding
 //          the fp16 scales of rows g (low half) and g + 8.
-enum WFmt : int { WF_I8 = 0, WF_Q4 = 1 };
+//   WF_I8R: WF_I8 weights streamed through a shared-memory ring by bulk
+//          copies instead of register batches (the GEMV variant for large
+//          matrices); same packing.
+enum WFmt : int { WF_I8 = 0, WF_Q4 = 1, WF_I8R = 2 };
 constexpr int kQ4BlockBytes = 18;  // fp16 scale + 16 bytes of nibbles
 
 // Epilogue kinds of the quantized GEMV.
@@ -119,6 +122,46 @@ struct TPArgs {
   int* cnt;                // CTA arrival counter of the GEMV (zeroed)
   int* err;
   const long long* wait_ns;  // limit of each bounded wait (device word)
+};
+
+struct QuantArgs {
+  const float* h;        // [M][ld]
+  int ld;
+  int d;                 // logical length
+  int M;
+  const float* w;        // RMSNorm weight or nullptr
+  int wlen;
+  float eps;
+  int do_norm;
+  uint8_t* xq;           // packed digits
+  int KB;                // ceil(d/32) (padded k-blocks written)
+  int nt;
+  int* xexp;
+  // Producer-side statistics (use_stats != 0): sum of squares as np partials
+  // pss[m * np_stride + j], and max |x * w| as float bits amax[m]; the kernel
+  // then zeroes amax_next[0..kMaxTokens) for the following producer.
+  int tc_layout;         // write the tcgen05 B-operand layout (see digit_word)
+  int use_stats;
+  const float* pss;
+  int np, np_stride;
+  const unsigned* amax;
+  unsigned* amax_next;
+  const void* pf;        // L2 prefetch of upcoming weights, or nullptr
+  long long pf_bytes;
+  // The O projection's input straight from the attention's page partials
+  // (att_o != nullptr; the partial layout and geometry of AttnArgs): each
+  // (token, head) is combined over its pages here -- weights e^(m_p - M)
+  // with M a max over the pages, denominator sum_p w_p l_p by a fixed
+  // shuffle tree, numerator sum_p w_p o_p in page order, then a division --
+  // and h / ld are unused.  amax is then the attention's bound on each
+  // token's max |output| (AttnArgs::st_amax).
+  const float* att_o;
+  const float* att_ml;
+  int att_chunks, att_Hkv, att_G, att_hdp, att_qblk, att_page;
+  SeqMap att_seq;
+  const int* att_pos;
+  int att_pos_add;
+  int trace_slot;        // MC_TRACE builds: 1 + timeline slot, 0 = untraced
 };
 
 struct GemvArgs {
@@ -166,35 +209,16 @@ struct GemvArgs {
   int row_offset;        // LMHEAD: global vocabulary index of packed row 0
   const int4* wtc;       // tcgen05 path: weights in the canonical layout (k_gemm_tc)
   TPArgs tp;             // EPI_TP
+  // Fused encoder (bar != nullptr): before the main loop every CTA encodes
+  // its slice of the digits this launch reads (enc, the encoder's statistics
+  // path, k-blocks split over the grid like k_quant's), then the grid meets
+  // at a barrier (bar[0] arrivals, bar[1] generation; bounded wait).  The
+  // grid is at most one wave (occupancy), so all its CTAs are resident.
+  QuantArgs enc;
+  unsigned* bar;
   int trace_slot;        // MC_TRACE builds: 1 + timeline slot, 0 = untraced
 };
 
-struct QuantArgs {
-  const float* h;        // [M][ld]
-  int ld;
-  int d;                 // logical length
-  int M;
-  const float* w;        // RMSNorm weight or nullptr
-  int wlen;
-  float eps;
-  int do_norm;
-  uint8_t* xq;           // packed digits
-  int KB;                // ceil(d/32) (padded k-blocks written)
-  int nt;
-  int* xexp;
-  // Producer-side statistics (use_stats != 0): sum of squares as np partials
-  // pss[m * np_stride + j], and max |x * w| as float bits amax[m]; the kernel
-  // then zeroes amax_next[0..kMaxTokens) for the following producer.
-  int tc_layout;         // write the tcgen05 B-operand layout (see digit_word)
-  int use_stats;
-  const float* pss;
-  int np, np_stride;
-  const unsigned* amax;
-  unsigned* amax_next;
-  const void* pf;        // L2 prefetch of upcoming weights, or nullptr
-  long long pf_bytes;
-  int trace_slot;        // MC_TRACE builds: 1 + timeline slot, 0 = untraced
-};
 
 struct AttnArgs {
   const float* q;        // [M][H][hdp]
@@ -213,11 +237,10 @@ struct AttnArgs {
   int M, H, Hkv, hdp, page;
   float inv_scale_den;   // sqrt(head_dim) (divisor, transformer.rs:966)
   int max_chunks;
-  float* part_o;         // [blocks][Hkv][max_chunks][G*qblk][hdp]
-  float* part_ml;        // [blocks][Hkv][max_chunks][G*qblk][2]
-  int* cnt;              // [blocks][Hkv]
-  float* out;            // [M][H][hdp]
-  unsigned* st_amax;     // max |out| per token (float bits, atomicMax) or nullptr
+  float* part_o;         // [blocks][Hkv][max_chunks][G*qblk][hdp]: sum_t e^(s_t - m_p) v_t
+  float* part_ml;        // [blocks][Hkv][max_chunks][G*qblk][2]: (m_p, l_p) of each page p
+  unsigned* st_amax;     // per token: max over its pages and heads of |o_p| / l_p,
+                         // a bound on its max |output| (float bits, atomicMax)
   const void* pf;        // L2 prefetch of upcoming weights while HBM is idle, or nullptr
   long long pf_bytes;
   int trace_slot;        // MC_TRACE builds: 1 + timeline slot, 0 = untraced

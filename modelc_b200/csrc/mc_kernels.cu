@@ -182,6 +182,49 @@ __device__ __forceinline__ void prefetch_share(const void* p, long long bytes, i
     left -= b;
   }
 }
+// mbarriers and bulk copies (cp.async.bulk, completion counted in bytes on
+// an mbarrier): shared by the GEMV's weight ring and the tcgen05 GEMM.
+constexpr long long kMbarSpin = 1ll << 22;  // try_wait rounds before giving up
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(b)),
+               "r"(bytes)
+               : "memory");
+}
+// Bounded wait for the completion of the phase with this parity.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+  uint32_t done = 0;
+  for (long long i = 0; i < kMbarSpin && !done; ++i)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(b)), "r"(parity)
+        : "memory");
+  return done != 0;
+}
+// the same with an L2 cache policy (createpolicy) for the source lines
+__device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, uint32_t bytes,
+                                               uint64_t* b, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(b)), "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(b))
+      : "memory");
+}
 __device__ __forceinline__ void red_add(int* p, int v) {
   asm volatile("red.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -591,6 +634,225 @@ __device__ __forceinline__ float4 load_act4(const float* h, int ld, int d, int m
   return r;
 }
 
+// The O projection's input straight from the attention's page partials
+// (QuantArgs::att_o): the CTA's slice [lo, hi) of every token is combined
+// into shared memory, then encoded.  Output (token m, head h, columns c..c+3)
+// = sum_p e^(m_p - M) o_p / sum_p e^(m_p - M) l_p over the pages p of its
+// query block, M = max_p m_p.  Two adjacent lanes share an output (pages of
+// even and odd index, at most 16 each in flight), their partial sums added
+// even + odd; so each output is one round trip of loads for up to 32 pages.
+// The exponent comes from the attention's bound (amax), read meanwhile.
+__device__ __forceinline__ void attn_combine_encode(const QuantArgs& a, int lo, int hi, int kb0,
+                                                    int kb1, uint32_t* s_bound, float* s_mul,
+                                                    int* s_e, float* s_slice, uint32_t* xq) {
+  if (threadIdx.x < a.M) s_bound[threadIdx.x] = __ldcg(a.amax + threadIdx.x);
+  const int hd = a.att_hdp, G = a.att_G, Rs = G * a.att_qblk;
+  const int n_qb = (a.att_seq.seq_len + a.att_qblk - 1) / a.att_qblk;
+  const int span = hi - lo, q4 = span / 4, n_out = a.M * q4;
+  const size_t cs4 = (size_t)Rs * hd / 4;  // float4s between pages
+  constexpr int B = 16;                     // pages per lane in flight
+  for (int base = 0; base < 2 * n_out; base += blockDim.x) {  // block-uniform trip count
+    const int t = base + (int)threadIdx.x, o = t >> 1, half = t & 1;
+    const bool live = o < n_out;
+    const int m = live ? o / q4 : 0;
+    const int k = lo + 4 * (live ? o - m * q4 : 0);
+    const bool in = live && k < a.d;
+    int nch = 0;
+    const float2* ml = nullptr;
+    const float4* src = nullptr;
+    if (in) {
+      const int hh = k / hd;
+      const int z = seq_of(a.att_seq, m), i = seq_off(a.att_seq, m);
+      const int qb = i / a.att_qblk, i0 = qb * a.att_qblk;
+      const int Mq = min(a.att_qblk, a.att_seq.seq_len - i0);
+      const int L = a.att_pos[z * a.att_seq.pos_stride] + a.att_pos_add + i0 + Mq;
+      nch = min((L + a.att_page - 1) / a.att_page, a.att_chunks);
+      const size_t cslot = (size_t)(z * n_qb + qb) * a.att_Hkv + hh / G;
+      const size_t row = cslot * a.att_chunks * Rs + (size_t)((i - i0) * G + hh % G);
+      ml = reinterpret_cast<const float2*>(a.att_ml) + row;
+      src = reinterpret_cast<const float4*>(a.att_o + row * hd + (k - hh * hd));
+    }
+    // M over every page of the row (both lanes' pages): a pre-pass only when
+    // the pages do not fit one batch
+    float M_ = -INFINITY;
+    if (nch > 2 * B)
+      for (int p = half; p < nch; p += 2) M_ = fmaxf(M_, __ldcg(&ml[(size_t)p * Rs].x));
+    float l = 0.0f;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    // every lane runs the warp's longest page loop (the shuffle below needs
+    // all of them; lanes past their own pages load nothing)
+    for (int p0 = 0; __any_sync(0xffffffffu, p0 < nch); p0 += 2 * B) {
+      float2 mv[B];
+      float4 v[B];
+#pragma unroll
+      for (int u = 0; u < B; ++u) {
+        const int p = p0 + 2 * u + half;
+        mv[u] = p < nch ? __ldcg(ml + (size_t)p * Rs) : make_float2(-INFINITY, 0.0f);
+        v[u] = p < nch ? __ldcg(src + (size_t)p * cs4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+      if (p0 == 0 && nch <= 2 * B) {
+#pragma unroll
+        for (int u = 0; u < B; ++u) M_ = fmaxf(M_, mv[u].x);
+      }
+      if (p0 == 0) M_ = fmaxf(M_, __shfl_xor_sync(0xffffffffu, M_, 1));
+#pragma unroll
+      for (int u = 0; u < B; ++u) {
+        const float w = (mv[u].x == -INFINITY) ? 0.0f : expf(mv[u].x - M_);
+        l = __fadd_rn(l, __fmul_rn(w, mv[u].y));
+        acc.x = __fmaf_rn(v[u].x, w, acc.x);
+        acc.y = __fmaf_rn(v[u].y, w, acc.y);
+        acc.z = __fmaf_rn(v[u].z, w, acc.z);
+        acc.w = __fmaf_rn(v[u].w, w, acc.w);
+      }
+    }
+    // even + odd, in that order on both lanes
+    const float lo_l = __shfl_sync(0xffffffffu, l, (threadIdx.x & 31) & ~1);
+    const float hi_l = __shfl_sync(0xffffffffu, l, (threadIdx.x & 31) | 1);
+    float4 e, q;
+    e.x = __shfl_sync(0xffffffffu, acc.x, (threadIdx.x & 31) & ~1);
+    e.y = __shfl_sync(0xffffffffu, acc.y, (threadIdx.x & 31) & ~1);
+    e.z = __shfl_sync(0xffffffffu, acc.z, (threadIdx.x & 31) & ~1);
+    e.w = __shfl_sync(0xffffffffu, acc.w, (threadIdx.x & 31) & ~1);
+    q.x = __shfl_sync(0xffffffffu, acc.x, (threadIdx.x & 31) | 1);
+    q.y = __shfl_sync(0xffffffffu, acc.y, (threadIdx.x & 31) | 1);
+    q.z = __shfl_sync(0xffffffffu, acc.z, (threadIdx.x & 31) | 1);
+    q.w = __shfl_sync(0xffffffffu, acc.w, (threadIdx.x & 31) | 1);
+    if (live && half == 0) {
+      float4 r = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (in) {
+        const float den = __fadd_rn(lo_l, hi_l);
+        r.x = __fdiv_rn(__fadd_rn(e.x, q.x), den);
+        r.y = __fdiv_rn(__fadd_rn(e.y, q.y), den);
+        r.z = __fdiv_rn(__fadd_rn(e.z, q.z), den);
+        r.w = __fdiv_rn(__fadd_rn(e.w, q.w), den);
+      }
+      *reinterpret_cast<float4*>(s_slice + (size_t)m * span + (k - lo)) = r;
+    }
+  }
+  __syncthreads();
+  // exponents from the bound (no norm), as the encoder's statistics path
+  if (threadIdx.x < a.M) {
+    const int m = threadIdx.x;
+    const float amax = __uint_as_float(s_bound[m]);
+    int e = 0;
+    if (!isfinite(amax)) {
+      e = kExpNonFinite;
+    } else if (amax > 0.0f) {
+      int E;
+      frexpf(amax * 1.0000002f, &E);
+      e = 20 - E;
+    }
+    s_mul[m] = (e != kExpNonFinite) ? ldexpf(1.0f, e) : 0.0f;
+    s_e[m] = e;
+    if (blockIdx.x == 0) a.xexp[m] = e;
+  }
+  if (blockIdx.x == 0 && a.amax_next && threadIdx.x < kMaxTokens) a.amax_next[threadIdx.x] = 0u;
+  __syncthreads();
+  const StatArgs sa{nullptr, 0, a.d, a.M, nullptr, 0, 0.0f, 0};
+  encode_digits(sa, a.nt, a.KB, kb0, kb1, s_mul, s_e,
+                [&](int m, int k) {
+                  const float* p = s_slice + (size_t)m * span + (k - lo);
+                  return make_float4(k < a.d ? p[0] : 0.0f, k + 1 < a.d ? p[1] : 0.0f,
+                                     k + 2 < a.d ? p[2] : 0.0f, k + 3 < a.d ? p[3] : 0.0f);
+                },
+                [&](size_t wi, uint32_t v) { xq[wi] = v; }, a.tc_layout != 0);
+}
+
+// The encoder's statistics path over k-blocks [kb0, kb1) of a.xq: the
+// exponents come from the producer's statistics, then the slice is encoded;
+// block 0 also writes the exponents and zeroes the next producer's max slot.
+// s_mul / s_e: kMaxTokens each (shared).  phase(k) marks trace phases 1-3.
+template <class Phase>
+__device__ __forceinline__ void encode_slice_stats_t(const QuantArgs& a, int kb0, int kb1,
+                                                     float* s_mul, int* s_e, Phase phase) {
+  uint32_t* xq = reinterpret_cast<uint32_t*>(a.xq);
+  const StatArgs sa{a.h, a.ld, a.d, a.M, a.w, a.wlen, a.eps, a.do_norm};
+  auto src4 = [&](int m, int k) { return load_act4(a.h, a.ld, a.d, m, k); };
+  auto ready = [&]() {
+    // statistics from the producing kernel: one warp per token sums the
+    // partials in a fixed order (lane-strided, then an xor-shuffle tree)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int m = warp; m < a.M; m += blockDim.x >> 5) {
+      const unsigned mxb = lane == 0 ? __ldcg(a.amax + m) : 0u;  // issued with the partials
+      float ss = 0.0f;
+      if (a.do_norm) {
+        // the lane's partials j = lane, lane + 32, ... in batches of 8 whose
+        // loads are all in flight before the (in-order) adds
+        const float* pr = a.pss + (size_t)m * a.np_stride;
+        for (int j0 = lane; j0 < a.np; j0 += 32 * 8) {
+          float v[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) v[u] = j0 + 32 * u < a.np ? __ldcg(pr + j0 + 32 * u) : 0.0f;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            if (j0 + 32 * u < a.np) ss = __fadd_rn(ss, v[u]);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+      if (lane == 0) {
+        const float mx = __uint_as_float(mxb);
+        float rms = 1.0f;
+        if (a.do_norm) rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)(a.d > 1 ? a.d : 1)), a.eps));
+        const float amax = a.do_norm ? mx / rms : mx;
+        int e = 0;
+        if (!isfinite(amax)) {  // a NaN/inf element makes the bit-max non-finite
+          e = kExpNonFinite;
+        } else if (amax > 0.0f) {
+          int E;
+          frexpf(amax * 1.0000002f, &E);
+          e = 20 - E;
+        }
+        s_mul[m] = (e != kExpNonFinite) ? ldexpf(a.do_norm ? 1.0f / rms : 1.0f, e) : 0.0f;
+        s_e[m] = e;
+      }
+    }
+    if (blockIdx.x == 0 && a.amax_next && threadIdx.x < kMaxTokens) a.amax_next[threadIdx.x] = 0u;
+    phase(1);
+    __syncthreads();
+    phase(2);
+    if (blockIdx.x == 0 && threadIdx.x < a.M) a.xexp[threadIdx.x] = s_e[threadIdx.x];
+  };
+  encode_digits_early(sa, a.nt, a.KB, kb0, kb1, s_mul, s_e, src4,
+                      [&](size_t wi, uint32_t v) { xq[wi] = v; }, a.tc_layout != 0, ready);
+  phase(3);
+}
+
+// All CTAs of the grid (at most one wave, so all resident) meet here: the
+// last to arrive resets the arrival count and advances the generation; the
+// others wait (acquire) for the generation to change, at most 2 s of
+// %globaltimer, after which the error word is raised and they go on.
+__device__ __forceinline__ void grid_barrier(unsigned* bar, int* err) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned gen;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(gen) : "l"(bar + 1) : "memory");
+    __threadfence();
+    if (atomicAdd(bar, 1u) == gridDim.x - 1) {
+      bar[0] = 0u;  // every CTA has arrived: nobody reads the count until the next use
+      __threadfence();
+      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(bar + 1), "r"(gen + 1u) : "memory");
+    } else {
+      unsigned long long t0;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+      for (long long i = 0;; ++i) {
+        unsigned g;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(bar + 1) : "memory");
+        if (g != gen) break;
+        if ((i & 63) == 63) {
+          unsigned long long t1;
+          asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+          if (t1 - t0 > 2000000000ull || i > (1ll << 26)) {
+            if (err) atomicExch(err, 1);
+            break;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+
 // ------------------------------------------------------------ GEMV
 // Work split: each CTA owns a contiguous range of the linear (stripe,
 // k-block) index (stream-K, balanced to one k-block); its 8 warps own
@@ -853,10 +1115,33 @@ __device__ __forceinline__ void tp_publish(const TPArgs& t) {
 
 constexpr int kMaxSplitUnits = 16;  // units per CTA when F > 1 (ns * F <= 14)
 
+// Weight ring of one warp: NB chunk buffers of up to U k-blocks, filled by
+// cp.async.bulk copies (lane 0) that complete on one mbarrier per buffer.
+// WF_I8 k-block: 512 bytes (each lane's 16-byte A fragment); WF_Q4: 256
+// bytes of nibbles, then (after the chunk's U nibble blocks) 32 bytes of
+// block scales.  The buffers hold what the warp streams next, so the first
+// NB chunks -- the whole slice of a small projection -- load before
+// griddepcontrol.wait, while the producer of its activations still runs.
+// Used by the WF_I8R variant only (large int8 matrices, where the deeper
+// stream pays; the register path is faster for small ones).
+template <int NT, int WF>
+struct GemvRing {
+  static constexpr bool On = WF == WF_I8R;
+  static constexpr int U = GemvCfg<NT>::U;
+  static constexpr int KBW = 512;
+  static constexpr int KBS = 0;
+  static constexpr int ChunkBytes = U * (KBW + KBS);
+  static constexpr int NB = NT <= 2 ? 2 : 3;
+  static constexpr int WarpBytes = On ? NB * ChunkBytes : 0;
+  static constexpr size_t Base = ((((size_t)kGemvWarps * 16 * (8 * NT + 1) +
+                                    (size_t)(WF == WF_Q4 ? kMaxSplitUnits : kTileSlots) * 16 *
+                                        8 * NT) * 4) + 127) / 128 * 128;
+  static constexpr int kMaxNB = 3;
+};
+
 template <int NT, int WF>
 static constexpr size_t gemv_dyn_smem() {
-  return ((size_t)kGemvWarps * 16 * (8 * NT + 1) +
-          (size_t)(WF == WF_Q4 ? kMaxSplitUnits : kTileSlots) * 16 * 8 * NT) * 4;
+  return GemvRing<NT, WF>::Base + (size_t)kGemvWarps * GemvRing<NT, WF>::WarpBytes;
 }
 
 template <int NT, int EPI, int WF>
@@ -864,6 +1149,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   constexpr int U = GemvCfg<NT>::U;
   constexpr int COLS = GemvCfg<NT>::COLS;
   constexpr bool Q4 = WF == WF_Q4;
+  constexpr bool RING = WF == WF_I8R;
   using Acc = typename std::conditional<Q4, float, int>::type;
   extern __shared__ __align__(16) int gemv_smem[];
   // per-warp fragment staging [warp][16][COLS+1], then the k-split area
@@ -874,6 +1160,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   __shared__ float sm_scale[kMaxCtaStripes * 16];
   __shared__ int sm_exp[kGemvWarps][kGroupTokens];  // per warp: filled at its first epilogue
   __shared__ unsigned long long sm_keys[kGroupTokens];
+  __shared__ __align__(8) uint64_t sm_mbar[kGemvWarps][GemvRing<NT, WF>::kMaxNB];
+  using R = GemvRing<NT, WF>;
+  uint8_t* ring = reinterpret_cast<uint8_t*>(gemv_smem) + R::Base;
 
   MC_TRACE_T0
   const int lane = threadIdx.x & 31;
@@ -892,18 +1181,21 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   if (scale_smem)
     for (int i = threadIdx.x; i < ns * 16; i += blockDim.x) sm_scale[i] = a.scale[s0 * 16 + i];
 
-  // Weights never depend on the producer grid: start streaming them (first
-  // batch of this warp's first unit) before the wait.
-  const uint64_t pol = policy_evict_first();
-  int4 wv[Q4 ? 1 : U];
-  uint2 wq[Q4 ? U : 1];
-  uint32_t wsc[Q4 ? U : 1];
   auto unit_range = [&](int u, int& stripe, int& kb0, int& kb1) {
     stripe = s0 + u / F;
     const int part = u - (u / F) * F;
     kb0 = (int)((long long)a.KB * part / F);
     kb1 = (int)((long long)a.KB * (part + 1) / F);
   };
+  // Weights never depend on the producer grid: start streaming them before
+  // the wait.  Register path: the first batch of this warp's first unit.
+  // Ring path (WF_I8R): lane 0 streams this warp's k-blocks (its units u =
+  // warp, warp + 8, ... in order, U per chunk) into the ring, chunk c into
+  // buffer c % NB; the consumer below walks the same order.
+  const uint64_t pol = policy_evict_first();
+  int4 wv[Q4 || RING ? 1 : U];
+  uint2 wq[Q4 ? U : 1];
+  uint32_t wsc[Q4 ? U : 1];
   auto load_batch = [&](int stripe, int kb, int nb) {
     if constexpr (Q4) {
       const uint2* wp = reinterpret_cast<const uint2*>(a.w) + ((size_t)stripe * a.KB + kb) * 32 + lane;
@@ -914,14 +1206,41 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
           wq[j] = ldg_stream2(wp + (size_t)j * 32, pol);
           wsc[j] = ldg_stream1(sp + (size_t)j * 8, pol);
         }
-    } else {
+    } else if constexpr (!RING) {
       const int4* wp = a.w + ((size_t)stripe * a.KB + kb) * 32 + lane;
 #pragma unroll
       for (int j = 0; j < U; ++j)
         if (j < nb) wv[j] = ldg_stream(wp + (size_t)j * 32, pol);
     }
   };
-  if (warp < n_units) {
+  uint8_t* wring = ring + (size_t)warp * R::WarpBytes;
+  uint64_t* mbar = sm_mbar[warp];
+  int pu = warp, pk = 0, pk1 = -1, pstripe = 0;  // producer: unit, next k-block, its end
+  auto issue = [&](int b) {  // lane 0: the next chunk of this warp into buffer b
+    while (pu < n_units && pk >= pk1) {
+      if (pk1 >= 0) pu += kGemvWarps;
+      if (pu >= n_units) break;
+      unit_range(pu, pstripe, pk, pk1);
+    }
+    if (pu >= n_units) return;
+    const int nb = min(U, pk1 - pk);
+    uint8_t* dst = wring + (size_t)b * R::ChunkBytes;
+    const size_t blk = (size_t)pstripe * a.KB + pk;
+    mbar_expect_tx(&mbar[b], (uint32_t)(nb * R::KBW));
+    bulk_load_hint(dst, reinterpret_cast<const uint8_t*>(a.w) + blk * R::KBW,
+                   (uint32_t)(nb * R::KBW), &mbar[b], pol);
+    pk += nb;
+  };
+  if constexpr (RING) {
+    // only the first chunk goes out before the wait: more competes with the
+    // producer (an encoder on the critical path) for memory bandwidth
+    if (lane == 0) {
+      for (int b = 0; b < R::NB; ++b) mbar_init(&mbar[b], 1);
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      issue(0);
+    }
+    __syncwarp();
+  } else if (warp < n_units) {
     int st, k0, k1;
     unit_range(warp, st, k0, k1);
     load_batch(st, k0, min(U, k1 - k0));
@@ -969,6 +1288,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   __syncthreads();  // shared tiles, counters and scales are initialised
   grid_wait();
   MC_TRACE_WAITED(a.trace_slot);
+  if (RING && lane == 0)
+    for (int b = 1; b < R::NB; ++b) issue(b);
   // The token exponents are only needed by the epilogue: issue the load now,
   // consume it there, so its L2 round trip overlaps the first batches.
   const int xe = lane < a.M ? __ldcg(a.xexp + lane) : 0;
@@ -986,7 +1307,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   for (int i = 0; i < (8 * kGroupTokens) / 32; ++i) kmax[i] = 0ull;
   const float* scl = Q4 ? nullptr : (scale_smem ? sm_scale - s0 * 16 : a.scale);
 
-  bool pre = true;
+  int c = 0;        // chunks consumed by this warp (ring path)
+  bool ring_ok = true;
+  bool pre = true;  // the register path's first batch is in flight
   for (int u = warp; u < n_units; u += kGemvWarps) {
     int stripe, k0, k1;
     unit_range(u, stripe, k0, k1);
@@ -1000,14 +1323,17 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0;
     const uint8_t* xp = a.x + ((size_t)k0 * 32 + lane) * COLS;
-    for (int i = 0; i < n; i += U) {
+    for (int i = 0; i < n; i += U, ++c) {
       const int nb = min(U, n - i);
-      if (!pre) load_batch(stripe, k0 + i, nb);
+      if (!RING && !pre) load_batch(stripe, k0 + i, nb);
       pre = false;
       uint32_t xv[U][2 * NT];
 #pragma unroll
       for (int j = 0; j < U; ++j)
         if (j < nb) load_x<NT>(xv[j], xp + (size_t)(i + j) * 32 * COLS);
+      const int b = RING ? c % R::NB : 0;
+      if constexpr (RING) ring_ok &= mbar_wait(&mbar[b], (uint32_t)((c / R::NB) & 1));
+      const uint8_t* cb = wring + (size_t)b * R::ChunkBytes;
 #pragma unroll
       for (int j = 0; j < U; ++j)
         if (j < nb) {
@@ -1026,10 +1352,17 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
               acc[t][3] = __fmaf_rn(small_int_to_float(c[3]), d1, acc[t][3]);
             }
           } else {
+            const int4 w = RING ? *reinterpret_cast<const int4*>(cb + j * R::KBW + lane * 16)
+                                : wv[RING ? 0 : j];
 #pragma unroll
-            for (int t = 0; t < NT; ++t) imma(acc[t], wv[j], xv[j][2 * t], xv[j][2 * t + 1]);
+            for (int t = 0; t < NT; ++t) imma(acc[t], w, xv[j][2 * t], xv[j][2 * t + 1]);
           }
         }
+      if constexpr (RING) {
+        // the MMAs above consumed every lane's fragments: the buffer is free
+        __syncwarp();
+        if (lane == 0) issue(b);
+      }
     }
     const int g = lane >> 2, tq = lane & 3;
     if (F == 1) {
@@ -1101,6 +1434,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
     }
   }
   grid_launch_dependents();
+  if (!ring_ok && lane == 0 && a.err) atomicExch(a.err, 1);
 
   if constexpr (EPI == EPI_LMHEAD) {
 #pragma unroll
@@ -1172,6 +1506,7 @@ cudaError_t launch_gemv(const GemvArgs& a, int epi, int nt, int wf, int grid, cu
     if (!a.qscale) return cudaErrorInvalidValue;
     return launch_gemv_wf<WF_Q4>(a, epi, nt, grid, s, pdl);
   }
+  if (wf == WF_I8R) return launch_gemv_wf<WF_I8R>(a, epi, nt, grid, s, pdl);
   return launch_gemv_wf<WF_I8>(a, epi, nt, grid, s, pdl);
 }
 
@@ -1213,7 +1548,8 @@ static int bps_wf(int epi, int nt) {
 }
 
 int gemv_blocks_per_sm(int epi, int nt, int wf) {
-  return wf == WF_Q4 ? bps_wf<WF_Q4>(epi, nt) : bps_wf<WF_I8>(epi, nt);
+  return wf == WF_Q4 ? bps_wf<WF_Q4>(epi, nt)
+                     : (wf == WF_I8R ? bps_wf<WF_I8R>(epi, nt) : bps_wf<WF_I8>(epi, nt));
 }
 
 size_t gemv_ws_ints_per_stripe(int nt) { return (size_t)16 * 8 * nt; }
@@ -1254,55 +1590,8 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant(QuantArgs a) {
   const int lo = kb0 * 32, hi = kb0 * 32 + max(kb1 - kb0, 0) * 32;
   uint32_t* xq = reinterpret_cast<uint32_t*>(a.xq);
   if constexpr (STATS) {
-    auto src4 = [&](int m, int k) { return load_act4(a.h, a.ld, a.d, m, k); };
-    auto ready = [&]() {
-      // statistics from the producing kernel: one warp per token sums the
-      // partials in a fixed order (lane-strided, then an xor-shuffle tree)
-      const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-      for (int m = warp; m < a.M; m += blockDim.x >> 5) {
-        const unsigned mxb = lane == 0 ? __ldcg(a.amax + m) : 0u;  // issued with the partials
-        float ss = 0.0f;
-        if (a.do_norm) {
-          // the lane's partials j = lane, lane + 32, ... in batches of 8 whose
-          // loads are all in flight before the (in-order) adds
-          const float* pr = a.pss + (size_t)m * a.np_stride;
-          for (int j0 = lane; j0 < a.np; j0 += 32 * 8) {
-            float v[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = j0 + 32 * u < a.np ? __ldcg(pr + j0 + 32 * u) : 0.0f;
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              if (j0 + 32 * u < a.np) ss = __fadd_rn(ss, v[u]);
-          }
-        }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-        if (lane == 0) {
-          const float mx = __uint_as_float(mxb);
-          float rms = 1.0f;
-          if (a.do_norm) rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)(a.d > 1 ? a.d : 1)), a.eps));
-          const float amax = a.do_norm ? mx / rms : mx;
-          int e = 0;
-          if (!isfinite(amax)) {  // a NaN/inf element makes the bit-max non-finite
-            e = kExpNonFinite;
-          } else if (amax > 0.0f) {
-            int E;
-            frexpf(amax * 1.0000002f, &E);
-            e = 20 - E;
-          }
-          s_mul[m] = (e != kExpNonFinite) ? ldexpf(a.do_norm ? 1.0f / rms : 1.0f, e) : 0.0f;
-          s_e[m] = e;
-        }
-      }
-      if (blockIdx.x == 0 && a.amax_next && threadIdx.x < kMaxTokens) a.amax_next[threadIdx.x] = 0u;
-      MC_TRACE_PHASE(a.trace_slot, 1, mc_tp);
-      __syncthreads();
-      MC_TRACE_PHASE(a.trace_slot, 2, mc_tp);
-      if (blockIdx.x == 0 && threadIdx.x < a.M) a.xexp[threadIdx.x] = s_e[threadIdx.x];
-    };
-    encode_digits_early(sa, a.nt, a.KB, kb0, kb1, s_mul, s_e, src4,
-                        [&](size_t wi, uint32_t v) { xq[wi] = v; }, a.tc_layout != 0, ready);
-    MC_TRACE_PHASE(a.trace_slot, 3, mc_tp);
+    encode_slice_stats_t(a, kb0, kb1, s_mul, s_e,
+                         [&](int k) { MC_TRACE_PHASE(a.trace_slot, k, mc_tp); });
     MC_TRACE_END(a.trace_slot);
     return;
   } else {
@@ -1356,6 +1645,26 @@ __global__ void __launch_bounds__(256) k_act_amax(const float* __restrict__ x, i
   }
 }
 
+// The O projection's encoder reading the attention's page partials
+// (QuantArgs::att_o): attn_combine_encode on this CTA's k-blocks.
+__global__ void __launch_bounds__(kQuantThreads) k_quant_att(QuantArgs a) {
+  __shared__ float s_mul[kMaxTokens];
+  __shared__ int s_e[kMaxTokens];
+  __shared__ uint32_t s_bound[kMaxTokens];
+  extern __shared__ float s_x[];
+  MC_TRACE_T0
+  if (a.pf && threadIdx.x == 0) prefetch_share(a.pf, a.pf_bytes, blockIdx.x, gridDim.x);
+  grid_launch_dependents();
+  grid_wait();
+  MC_TRACE_WAITED(a.trace_slot);
+  const int kbs = (a.KB + gridDim.x - 1) / gridDim.x;
+  const int kb0 = blockIdx.x * kbs, kb1 = min(a.KB, kb0 + kbs);
+  const int lo = kb0 * 32, hi = kb0 * 32 + max(kb1 - kb0, 0) * 32;
+  attn_combine_encode(a, lo, hi, kb0, kb1, s_bound, s_mul, s_e, s_x,
+                      reinterpret_cast<uint32_t*>(a.xq));
+  MC_TRACE_END(a.trace_slot);
+}
+
 cudaError_t launch_act_amax(const float* x, int ld, int d, int M, unsigned* amax, cudaStream_t s,
                             bool pdl) {
   if (M < 1 || M > kMaxTokens) return cudaErrorInvalidValue;
@@ -1388,14 +1697,19 @@ cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ctas);
   cfg.blockDim = dim3(kQuantThreads);
-  cfg.dynamicSmemBytes = a.use_stats ? 0 : (size_t)a.M * kbs * 32 * sizeof(float);
-  if (cfg.dynamicSmemBytes > 32 * 1024) return cudaErrorInvalidConfiguration;
+  cfg.dynamicSmemBytes =
+      (a.use_stats && !a.att_o) ? 0 : (size_t)a.M * kbs * 32 * sizeof(float);
+  if (a.att_o && (!a.use_stats || a.att_hdp < 4 || (a.att_hdp & 3) || a.att_chunks > 64 ||
+                  a.att_G < 1 || a.att_qblk < 1))
+    return cudaErrorInvalidValue;
+  if (cfg.dynamicSmemBytes > 40 * 1024) return cudaErrorInvalidConfiguration;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (a.att_o) return cudaLaunchKernelEx(&cfg, k_quant_att, a);
   return a.use_stats ? cudaLaunchKernelEx(&cfg, k_quant<true>, a)
                      : cudaLaunchKernelEx(&cfg, k_quant<false>, a);
 }
@@ -1411,104 +1725,26 @@ cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl) {
 // split).
 constexpr int kAttnThreads = 512;
 
-// Last arriver of one (query block, KV head): combine the pages' partials
-// into the output, one warp per row and lanes over pages for the weights
-// (max_chunks <= 64 = 2 per lane).  Page c contributes
-// e^(m_c - M) * (sum_t e^(s_t - m_c) v_t) to the numerator and
-// e^(m_c - M) * l_c to the denominator; fully masked pages (m_c = -inf)
-// contribute exactly zero.  Then thread -> 4 columns of one row, pages summed
-// in order with eight float4 loads in flight; Rp (>= R) is a multiple of the
-// rows a warp spans, so the row loop and the shuffles stay warp-uniform.
-// wgt: shared [R][n_chunks]; s_l: shared [>= R]; s_mx: shared [>= Mq].
-__device__ __forceinline__ void attn_combine(const AttnArgs& a, int kvh, int cslot, int n_chunks,
-                                             int R, int Rp, int Rs, int G, int mt0, int Mq,
-                                             float* wgt, float* s_l, uint32_t* s_mx) {
-  const int hdp = a.hdp;
-  const int nthr = blockDim.x;
-  const int h4 = hdp >> 2;
-  const int RGc = nthr / h4;
-  const int c4 = threadIdx.x % h4;
-  const int row0 = threadIdx.x / h4;  // this thread's first output row
-  const float4* base =
-      reinterpret_cast<const float4*>(a.part_o) + (size_t)cslot * a.max_chunks * Rs * h4 + c4;
-  const size_t cs4 = (size_t)Rs * h4;
-  {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const float2* ml = reinterpret_cast<const float2*>(a.part_ml) + (size_t)cslot * a.max_chunks * Rs;
-    for (int row = warp; row < R; row += nthr / 32) {
-      float2 v0 = make_float2(-INFINITY, 0.0f), v1 = make_float2(-INFINITY, 0.0f);
-      if (lane < n_chunks) v0 = __ldcg(ml + (size_t)lane * Rs + row);
-      if (lane + 32 < n_chunks) v1 = __ldcg(ml + (size_t)(lane + 32) * Rs + row);
-      float M_ = fmaxf(v0.x, v1.x);
-#pragma unroll
-      for (int o = 16; o; o >>= 1) M_ = fmaxf(M_, __shfl_xor_sync(0xffffffffu, M_, o));
-      const float w0 = (v0.x == -INFINITY) ? 0.0f : expf(v0.x - M_);
-      const float w1 = (v1.x == -INFINITY) ? 0.0f : expf(v1.x - M_);
-      if (lane < n_chunks) wgt[row * n_chunks + lane] = w0;
-      if (lane + 32 < n_chunks) wgt[row * n_chunks + lane + 32] = w1;
-      float l = __fadd_rn(__fmul_rn(w0, v0.y), __fmul_rn(w1, v1.y));
-#pragma unroll
-      for (int o = 16; o; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
-      if (lane == 0) s_l[row] = l;
-    }
-  }
-  for (int i = threadIdx.x; i < Mq; i += nthr) s_mx[i] = 0u;
-  __syncthreads();
-  {
-    const int seg = min(h4, 32);  // lanes of a warp that share a row
-    for (int row = row0; row < Rp; row += RGc) {
-      const bool live = row < R;
-      const int rr = live ? row : R - 1;
-      const float* wr = wgt + rr * n_chunks;
-      const float4* src = base + (size_t)rr * h4;
-      float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      int ch = 0;
-      for (; ch + 8 <= n_chunks; ch += 8) {
-        float4 v[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) v[u] = __ldcg(src + (size_t)(ch + u) * cs4);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const float w = wr[ch + u];
-          acc.x = __fmaf_rn(v[u].x, w, acc.x);
-          acc.y = __fmaf_rn(v[u].y, w, acc.y);
-          acc.z = __fmaf_rn(v[u].z, w, acc.z);
-          acc.w = __fmaf_rn(v[u].w, w, acc.w);
-        }
-      }
-      for (; ch < n_chunks; ++ch) {
-        const float4 v = __ldcg(src + (size_t)ch * cs4);
-        const float w = wr[ch];
-        acc.x = __fmaf_rn(v.x, w, acc.x);
-        acc.y = __fmaf_rn(v.y, w, acc.y);
-        acc.z = __fmaf_rn(v.z, w, acc.z);
-        acc.w = __fmaf_rn(v.w, w, acc.w);
-      }
-      uint32_t bits = 0u;
-      if (live) {
-        const float l = s_l[row];
-        float4 o;
-        o.x = __fdiv_rn(acc.x, l);
-        o.y = __fdiv_rn(acc.y, l);
-        o.z = __fdiv_rn(acc.z, l);
-        o.w = __fdiv_rn(acc.w, l);
-        const int m = row / G, gi = row - m * G;
-        reinterpret_cast<float4*>(a.out + ((size_t)(mt0 + m) * a.H + kvh * G + gi) * hdp)[c4] = o;
-        bits = max(max(__float_as_uint(fabsf(o.x)), __float_as_uint(fabsf(o.y))),
-                   max(__float_as_uint(fabsf(o.z)), __float_as_uint(fabsf(o.w))));
-      }
-      if (a.st_amax) {
-        for (int off = 1; off < seg; off <<= 1)
-          bits = max(bits, __shfl_xor_sync(0xffffffffu, bits, off));
-        if (live && (threadIdx.x % seg) == 0) atomicMax(s_mx + row / G, bits);
-      }
-    }
-  }
-  if (a.st_amax) {
-    __syncthreads();
-    for (int i = threadIdx.x; i < Mq; i += nthr) atomicMax(a.st_amax + mt0 + i, s_mx[i]);
-  }
-  if (threadIdx.x == 0) atomicExch(a.cnt + cslot, 0);
+// The page partials are combined by the O projection's encoder (k_quant
+// reading AttnArgs' partials), which needs each token's max |output| for its
+// exponent before it has the output.  The output of a (token, head) is a
+// convex combination of the pages' normalised partials o_p / l_p (weights
+// e^(m_p - M) l_p / sum), so max over pages and heads of |o_p| / l_p bounds
+// it; a CTA folds its page's share of that bound into st_amax[token].
+// page_bound: this thread's |o_p| value of query row `row`, into s_mx.
+__device__ __forceinline__ void page_bound(uint32_t* s_mx, const float* s_l, int row, int G,
+                                           float abs_o) {
+  const float l = s_l[row];
+  if (!(l > 0.0f)) return;  // no visible position on this page: no share
+  // as float bits (|x| only, so their unsigned order is |x|'s; NaN wins)
+  atomicMax(s_mx + row / G, __float_as_uint(fabsf(__fdiv_rn(abs_o, l))));
+}
+// s_mx (zeroed before the partials) complete: fold it into st_amax.
+__device__ __forceinline__ void publish_bound(const AttnArgs& a, const uint32_t* s_mx, int mt0,
+                                              int Mq) {
+  if (a.st_amax)
+    for (int i = threadIdx.x; i < Mq; i += blockDim.x)
+      if (s_mx[i]) atomicMax(a.st_amax + mt0 + i, s_mx[i]);
 }
 
 // 16-byte global -> shared copy that holds no registers (L2 only, as __ldcg).
@@ -1539,7 +1775,8 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) k_attention(AttnArgs a) {
   MC_TRACE_T0
   extern __shared__ float smem[];
   __shared__ float s_m[128], s_l[128];
-  __shared__ int s_last;
+  __shared__ uint32_t s_mx[64];  // page share of each token's output bound (float bits)
+  if (threadIdx.x < 64) s_mx[threadIdx.x] = 0u;
   if (a.pf && threadIdx.x == 0)
     prefetch_share(a.pf, a.pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
   grid_launch_dependents();
@@ -1691,7 +1928,10 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) k_attention(AttnArgs a) {
       }
 #pragma unroll
       for (int j = 0; j < RB; ++j)
-        if (rq + j * RG < R) a.part_o[(pbase + rq + j * RG) * hdp + c] = acc[j];
+        if (rq + j * RG < R) {
+          a.part_o[(pbase + rq + j * RG) * hdp + c] = acc[j];
+          page_bound(s_mx, s_l, rq + j * RG, G, fabsf(acc[j]));
+        }
     }
   }
   for (int row = threadIdx.x; row < R; row += blockDim.x) {
@@ -1699,24 +1939,8 @@ __global__ void __launch_bounds__(kAttnThreads, MINB) k_attention(AttnArgs a) {
     a.part_ml[(pbase + row) * 2 + 1] = s_l[row];
   }
   __syncthreads();
+  publish_bound(a, s_mx, mt0, Mq);
   MC_TRACE_PHASE(a.trace_slot, 4, mc_tp);
-  // the CTA's partials are ordered before its arrival (one fence per CTA);
-  // the last arriver fences again before reading the others' partials
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const int last = (atomicAdd(a.cnt + cslot, 1) == n_chunks - 1);
-    if (last) __threadfence();
-    s_last = last;
-  }
-  __syncthreads();
-  MC_TRACE_PHASE(a.trace_slot, 5, mc_tp);
-  if (!s_last) {
-    MC_TRACE_END(a.trace_slot);
-    return;
-  }
-  __shared__ uint32_t s_mx[128];  // max |out| per token of the block, float bits
-  attn_combine(a, kvh, cslot, n_chunks, R, Rp, Rs, G, mt0, Mq, ss, s_l, s_mx);
-  MC_TRACE_PHASE(a.trace_slot, 7, mc_tp);
   MC_TRACE_END(a.trace_slot);
 }
 
@@ -1775,8 +1999,8 @@ __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_t
   float* sP = sQl + RM * KS;       // [RM][PS]
   __shared__ float s_red[NW][RM];
   __shared__ float s_m[RM], s_l[RM];
-  __shared__ uint32_t s_mx[64];
-  __shared__ int s_last;
+  __shared__ uint32_t s_mx[64];  // page share of each token's output bound (float bits)
+  if (threadIdx.x < 64) s_mx[threadIdx.x] = 0u;
   if (a.pf && threadIdx.x == 0)
     prefetch_share(a.pf, a.pf_bytes, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
                    gridDim.x * gridDim.y * gridDim.z);
@@ -2007,44 +2231,32 @@ __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_t
   }
   MC_TRACE_PHASE(a.trace_slot, 3, mc_tp);
   const size_t pbase = ((size_t)cslot * a.max_chunks + chunk) * Rs;
+  __syncthreads();  // s_l complete
   if (warp < PV_WARPS)
 #pragma unroll
     for (int mi = 0; mi < MT; ++mi)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int row = 16 * mi + g + 8 * h;
-        if (row < R)
+        if (row < R) {
+          uint32_t mx = 0u;  // max |o| as float bits: NaN and inf win
 #pragma unroll
-          for (int nj = 0; nj < NT_PV; ++nj)
+          for (int nj = 0; nj < NT_PV; ++nj) {
             *reinterpret_cast<float2*>(a.part_o + (pbase + row) * HD + c0 + 8 * nj + 2 * tq) =
                 make_float2(acc[mi][nj][2 * h], acc[mi][nj][2 * h + 1]);
+            mx = max(mx, max(__float_as_uint(fabsf(acc[mi][nj][2 * h])),
+                             __float_as_uint(fabsf(acc[mi][nj][2 * h + 1]))));
+          }
+          page_bound(s_mx, s_l, row, G, __uint_as_float(mx));
+        }
       }
-  __syncthreads();  // s_l complete
   for (int row = threadIdx.x; row < R; row += kAttnTcThreads) {
     a.part_ml[(pbase + row) * 2] = s_m[row];
     a.part_ml[(pbase + row) * 2 + 1] = s_l[row];
   }
   __syncthreads();
+  publish_bound(a, s_mx, mt0, Mq);
   MC_TRACE_PHASE(a.trace_slot, 4, mc_tp);
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const int last = (atomicAdd(a.cnt + cslot, 1) == n_chunks - 1);
-    if (last) __threadfence();
-    s_last = last;
-  }
-  __syncthreads();
-  MC_TRACE_PHASE(a.trace_slot, 5, mc_tp);
-  if (!s_last) {
-    MC_TRACE_END(a.trace_slot);
-    return;
-  }
-  // the page weights [R][n_chunks <= 64] reuse the dead K/V/q/P region
-  // (at least 4096 floats for every instance)
-  const int h4 = HD / 4;
-  const int span = h4 >= 32 ? 1 : 32 / h4;  // rows one warp spans in the column pass
-  const int Rpc = (R + span - 1) / span * span;
-  attn_combine(a, kvh, cslot, n_chunks, R, Rpc, Rs, G, mt0, Mq, asmem, s_l, s_mx);
-  MC_TRACE_PHASE(a.trace_slot, 7, mc_tp);
   MC_TRACE_END(a.trace_slot);
 }
 
@@ -3201,7 +3413,6 @@ constexpr int kTcRows = 128;
 constexpr int kTcMaxStages = 8;
 constexpr int kTcRingBudget = 180 * 1024;  // bytes of ring per CTA (one CTA per SM)
 constexpr int kTcAStep = kTcRows * 32;  // bytes of A per k-step
-constexpr long long kTcSpin = 1ll << 22;  // try_wait rounds before giving up
 constexpr int kTcGroupCols = 48;        // digit columns of one token group
 template <int G>
 struct TcCfg {
@@ -3234,37 +3445,6 @@ struct TcCfg {
                                     ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
 };
 
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(b)), "r"(n) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(b)),
-               "r"(bytes)
-               : "memory");
-}
-// Bounded wait for the completion of the phase with this parity.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
-  uint32_t done = 0;
-  for (long long i = 0; i < kTcSpin && !done; ++i)
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(smem_addr(b)), "r"(parity)
-        : "memory");
-  return done != 0;
-}
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(smem_addr(dst)),
-      "l"(src), "r"(bytes), "r"(smem_addr(b))
-      : "memory");
-}
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
   // start address, LBO 1 (unused by swizzled K-major), SBO 1024 B (16-byte
   // units), descriptor version 1, layout 128-byte swizzle
