@@ -544,10 +544,10 @@ def run_ours(args):
 
 
 def run_profile(args):
-    """Short run for ncu launch lists: prime the 1024-token prompt, then
-    3 verify forwards, one more inside the NVTX range "verify" (select it with
-    ncu --nvtx --nvtx-include verify/), and 2 speculative rounds.  Launch
-    counts before the verify forwards are printed as well."""
+    """Short run for ncu launch lists: prime the 1024-token prompt, 2
+    speculative rounds (their launch count is printed), 3 verify forwards,
+    one more inside the NVTX range "verify" (select it with ncu --nvtx
+    --nvtx-include verify/), and 2 more rounds."""
     import torch
     import modelc_b200 as mb
     torch.cuda.set_device(0)
@@ -555,13 +555,9 @@ def run_profile(args):
     sess = mb.Session(target, draft, gamma=GAMMA,
                       max_context=PROMPT_LEN + NEW_TOKENS + 2 * GAMMA + 8)
     sess.prime(prompt)
+    sess.decode(2)  # captures the round graph
     torch.cuda.synchronize()
-    chunks_t = -(-PROMPT_LEN // 64)  # prefill forwards of up to 64 tokens
-    chunks_d = -(-(PROMPT_LEN - 1) // 64)
-    per_t = (sess.round_launches - 1 - GAMMA * 21)
-    print(json.dumps({"prime_launches": chunks_t * (1 + per_t) + chunks_d * (1 + 21),
-                      "verify_launches": per_t, "round_launches": sess.round_launches}),
-          flush=True)
+    print(json.dumps({"round_launches": sess.round_launches}), flush=True)
     sess.verify_launch(3)
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_push("verify")
@@ -596,19 +592,40 @@ def run_timeline(args):
     sess.decode(8)
     sess.verify_launch(3)
     torch.cuda.synchronize()
+    # with encoding tails (one token group) the norm and SwiGLU-output
+    # encoders run inside the GEMV before them: o, gu and down then include
+    # the encoder of the next projection
+    # (the attention too, when its query rows fit one m-tile and its grid one
+    # wave: then it encodes the O projection's input)
+    M = B * wl.gamma
+    mask = int(os.environ.get("MODELC_CUDA_ENCODER_TAILS", "0"))
+    tails = M <= 16 and bool(mask & 1)
+    c = cfg.resolved()
+    G = c.n_heads // c.n_kv_heads
+    max_ctx = wl.prompt_len + wl.new_tokens + 2 * wl.gamma + 8
+    att_tail = (bool(mask & 2) and G * min(wl.gamma, max(1, 64 // G)) <= 16
+                and c.n_kv_heads * -(-max_ctx // 64) * B <= 2 * 148)
+    att = ["attention+enc"] if att_tail else ["attention", "quant_o"]
     names = ["embed"]
-    for _ in range(cfg.n_layers):
-        names += ["quant_attn", "qkv", "attention", "quant_o", "o", "quant_mlp", "gu", "quant_act",
-                  "down"]
-    names += ["quant_final", "head"]
+    for l in range(cfg.n_layers):
+        if tails:
+            names += (["quant_attn"] if l == 0 else []) + ["qkv"] + att + ["o+enc", "gu+enc",
+                                                                          "down+enc"]
+        else:
+            names += ["quant_attn", "qkv"] + att + ["o", "quant_mlp", "gu", "quant_act", "down"]
+    names += ["head"] if tails else ["quant_final", "head"]
     n = len(names)
     for _ in range(3):  # the last of three repetitions
         L.check(lib.mc_trace_reset())
         sess.verify_launch(1)
         torch.cuda.synchronize()
-        buf = (C.c_ulonglong * (19 * n))()
-        L.check(lib.mc_trace_read(buf, n))
-    raw = np.array(buf, dtype=np.float64)
+        buf = (C.c_ulonglong * (19 * (n + 1)))()
+        L.check(lib.mc_trace_read(buf, n + 1))
+    # the launch list must be the forward's: slot n unused, slot n - 1 used
+    if buf[3 * n] != 2 ** 64 - 1 or buf[3 * (n - 1)] == 2 ** 64 - 1:
+        raise RuntimeError(f"timeline names do not match the forward's {n} launches")
+    raw = np.array(buf, dtype=np.float64)[:19 * (n + 1)]
+    raw = np.r_[raw[:3 * n], raw[3 * (n + 1): 3 * (n + 1) + 16 * n]]
     a = raw[:3 * n].reshape(n, 3)
     ph = raw[3 * n:].reshape(n, 16)
     a = (a - a[0, 0]) / 1e3  # us
@@ -632,7 +649,7 @@ def run_timeline(args):
     quant_ph = ["launch->wait", "producer stats in", "barrier", "encode + stores", "-", "-",
                 "-", "-"]
     for kind in ["qkv", "o", "gu", "down", "head", "attention", "quant_attn", "quant_o",
-                 "quant_mlp", "quant_act"]:
+                 "quant_mlp", "quant_act"]:  # GEMVs with a tail record no phases
         idx = [i for i, nm in enumerate(names) if nm == kind]
         sums, cnts = ph[idx, :8].sum(0), ph[idx, 8:].sum(0)
         if cnts.sum() == 0:

@@ -106,6 +106,7 @@ typedef struct mc_session mc_session;
 typedef struct mc_linear mc_linear;
 typedef struct mc_mlp_drafter mc_mlp_drafter;
 typedef struct mc_ngram_drafter mc_ngram_drafter;
+typedef struct mc_kv_snapshot mc_kv_snapshot;
 
 /* Speculative session configuration (GenerationConfig, generate.rs:65-167,
  * restricted to the fields the speculative step reads). */
@@ -140,7 +141,24 @@ typedef struct mc_spec_cfg {
                            target distribution when 0 < top_p < 1
                            (generate.rs:961-963), as mc_sample_rows states it */
   float min_p;          /* likewise min-p when 0 < min_p < 1 (generate.rs:964-966) */
+  int32_t shift_context;  /* GenerationConfig::max_context (0 = None): after a
+                             round or a fallback step whose context exceeds it,
+                             the context shift of generate.rs:26-63 on the
+                             device (tokens, target KV, draft KV); greedy
+                             sessions only.  Must leave room for a round:
+                             shift_context + gamma + 2 <= max_context. */
+  int32_t anchor_tokens;  /* GenerationConfig::anchor_tokens: tokens kept at the
+                             front by the anchored shift */
+  int32_t kv_mode;        /* target KV variant (make_kv_cache, generate.rs:17-24):
+                             MC_KV_FP32, MC_KV_INT8 (use_int8_kv) or MC_KV_MIXED
+                             (use_mixed_kv, window 64).  Values are held as the
+                             reference's k_all()/v_all() return them (int8 codes
+                             times the token's scale); the storage stays f32. */
 } mc_spec_cfg;
+
+#define MC_KV_FP32 0
+#define MC_KV_INT8 1
+#define MC_KV_MIXED 2
 
 /* Load (quantize-free) weights to the device and repack them for the
  * tensor-core GEMV.  Replaces Runtime::from_raw (runtime/serve.rs:121-132),
@@ -251,6 +269,25 @@ MC_API mc_status mc_spec_prime(mc_session* s, const uint32_t* prompt, int32_t n_
 MC_API mc_status mc_spec_prime_batch(mc_session* s, const uint32_t* prompts,
                               const int32_t* lens, int32_t n_requests);
 MC_API mc_status mc_spec_decode(mc_session* s, int32_t max_tokens, int32_t* n_generated);
+
+/* Prefix cache (prefix_cache.rs:14-110, used by serve/infer.rs:122-175).
+ * mc_kv_snapshot_take copies request z's context tokens and target K/V as
+ * they stand (after mc_spec_prime or decoding: the reference inserts the
+ * prompt plus generated ids with the KvCache speculative_generate returns)
+ * into a device allocation of its own; mc_kv_snapshot_tokens returns its
+ * token count and copies up to cap of them.  mc_spec_prime_cached is
+ * mc_spec_prime for a prompt that starts with the snapshot's tokens
+ * (speculative_generate with a CacheLookup, generate.rs:617-636): the K/V
+ * of the matched tokens are restored and only the rest are forwarded; the
+ * n-gram index still covers the whole prompt, the transformer draft primes
+ * the whole prompt.  Same target model, device and kv_mode; one-request
+ * sessions.  The longest-prefix LRU lookup itself is host logic
+ * (modelc_b200.PrefixCache). */
+MC_API mc_status mc_kv_snapshot_take(mc_session* s, int32_t request, mc_kv_snapshot** out);
+MC_API int32_t mc_kv_snapshot_tokens(const mc_kv_snapshot* snap, uint32_t* out, int32_t cap);
+MC_API mc_status mc_kv_snapshot_destroy(mc_kv_snapshot* snap);
+MC_API mc_status mc_spec_prime_cached(mc_session* s, const mc_kv_snapshot* snap,
+                                      const uint32_t* prompt, int32_t n_prompt);
 /* mc_spec_decode (and mc_speculative_generate) look at the cancel flag of
  * mc_spec_cfg before every batch of at most 64 rounds (generate.rs:639 looks
  * before every round) and return MC_E_CANCELLED with the rounds run so far
@@ -308,7 +345,8 @@ MC_API mc_status mc_spec_verify_launch(mc_session* s, int32_t n);
 /* The session's CUDA stream (a cudaStream_t) for stream-ordered timing. */
 MC_API void* mc_session_stream(mc_session* s);
 /* Kernel launches one speculative round enqueues (draft steps, verify,
- * acceptance). */
+ * acceptance): the kernel nodes of the round's CUDA graph, captured at the
+ * first decode (0 before it). */
 MC_API int32_t mc_session_round_launches(const mc_session* s);
 
 /* Standalone quantized projection y = x . dequant(W)^T (linear_with,

@@ -31,7 +31,8 @@ EXPORTS = [
     "mc_session_tp_open_peers", "mc_speculative_generate_batch", "mc_spec_prime_batch",
     "mc_spec_read_request", "mc_mlp_draft_create", "mc_mlp_draft", "mc_mlp_draft_destroy",
     "mc_ngram_draft_create", "mc_ngram_draft", "mc_ngram_draft_destroy", "mc_sample_rows",
-    "mc_session_set_wait_timeout", "mc_session_create_mlp",
+    "mc_session_set_wait_timeout", "mc_session_create_mlp", "mc_kv_snapshot_take",
+    "mc_kv_snapshot_tokens", "mc_kv_snapshot_destroy", "mc_spec_prime_cached",
 ]
 
 
@@ -58,7 +59,9 @@ class SpecCfg(C.Structure):
     _fields_ = [("gamma", C.c_int32), ("max_context", C.c_int32), ("bonus", C.c_int32),
                 ("temperature", C.c_float), ("seed", C.c_uint64),
                 ("cancel", C.POINTER(C.c_int32)), ("accept_mode", C.c_int32),
-                ("n_requests", C.c_int32), ("top_p", C.c_float), ("min_p", C.c_float)]
+                ("n_requests", C.c_int32), ("top_p", C.c_float), ("min_p", C.c_float),
+                ("shift_context", C.c_int32), ("anchor_tokens", C.c_int32),
+                ("kv_mode", C.c_int32)]
 
 
 _lib = None
@@ -105,6 +108,10 @@ def lib():
         "mc_draft": (i32, [vp, u32p, i32, i32, u32p, i32p]),
         "mc_speculative_generate": (i32, [vp, u32p, i32, i32, u32p, i32, i32p, i32p, i32, i32p]),
         "mc_spec_prime": (i32, [vp, u32p, i32]),
+        "mc_kv_snapshot_take": (i32, [vp, i32, C.POINTER(vp)]),
+        "mc_kv_snapshot_tokens": (i32, [vp, u32p, i32]),
+        "mc_kv_snapshot_destroy": (i32, [vp]),
+        "mc_spec_prime_cached": (i32, [vp, vp, u32p, i32]),
         "mc_spec_decode": (i32, [vp, i32, i32p]),
         "mc_spec_read": (i32, [vp, u32p, i32, i32p, i32p, i32, i32p]),
         "mc_linear_create": (i32, [C.POINTER(TensorDesc), i32, C.POINTER(vp)]),

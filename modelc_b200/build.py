@@ -18,7 +18,7 @@ LIB = os.path.join(HERE, "libmodelc_cuda.so")
 # first-CTA start, release from the dependency wait and last-CTA end
 # (%globaltimer), plus per-phase times of the attention and tcgen05 kernels.
 TRACE_LIB = os.path.join(HERE, "libmodelc_cuda_trace.so")
-SOURCES = ["mc_kernels.cu", "mc_api.cu", "mc_drafters.cu"]
+SOURCES = ["mc_kernels.cu", "mc_api.cu", "mc_drafters.cu", "mc_kvcache.cu"]
 HEADERS = ["mc_internal.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

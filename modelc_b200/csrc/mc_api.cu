@@ -4,6 +4,7 @@
 #include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <dlfcn.h>
@@ -195,7 +196,10 @@ static bool use_tc(const PMat& W, int M) {
 // shared-memory ring, where a deeper stream pays; smaller ones keep register
 // batches, whose first batch before the dependency wait costs the producing
 // encoder less.
-constexpr long long kRingMinBytes = 96ll << 20;
+#ifndef MC_RING_MIN_MB
+#define MC_RING_MIN_MB 96
+#endif
+constexpr long long kRingMinBytes = (long long)MC_RING_MIN_MB << 20;
 static int gemv_wf(const PMat& W) {
   if (W.fmt == WF_I8 && (long long)W.n_stripes * W.KB * kFragBytes >= kRingMinBytes)
     return WF_I8R;
@@ -793,6 +797,11 @@ struct KVSet {
   float* rope_sin = nullptr;
 };
 
+#ifndef MC_DEFAULT_TAILS
+#define MC_DEFAULT_TAILS 0
+#endif
+constexpr int kDefaultTails = MC_DEFAULT_TAILS;  // MODELC_CUDA_ENCODER_TAILS unset
+
 struct mc_session {
   const mc_weights* tw = nullptr;
   const mc_weights* dw = nullptr;
@@ -840,6 +849,14 @@ struct mc_session {
   cudaGraphExec_t verify_exec = nullptr;
   int round_launches = 0;
   int bps[3][6][7] = {};
+  int bps_tail[3][2][7] = {};  // encoding-tail variants of RESID / SWIGLU
+  // encoding tails (GemvArgs::bar, AttnArgs::bar): the grid barrier's
+  // words, and which producers run them -- bit 0 the o / gate-up / down
+  // GEMVs, bit 1 the attention -- from MODELC_CUDA_ENCODER_TAILS at session
+  // creation (a number; 0 keeps every encoder a launch of its own; the
+  // digits are the same either way)
+  unsigned* gbar = nullptr;  // [2]
+  int tails = kDefaultTails;
   // MC_TRACE builds: timeline slots handed to the launches of one capture
   bool trace_on = false;
   int trace_next = 0;
@@ -864,8 +881,9 @@ struct mc_session {
   // caller keeps it alive), or, with neither, the n-gram drafter
   const mc_mlp_drafter* mlp = nullptr;
   float* mlp_hid = nullptr;  // [B][dh]
-  int* ng = nullptr;         // [B][ctx_stride] n-gram index: window starts
-  int* ng_list = nullptr;    // [B][ctx_stride] n-gram scratch
+  uint32_t* ng = nullptr;    // [B][ng_cap][kNgram + 1] n-gram index entries (key, next)
+  int* ng_list = nullptr;    // [B][ng_cap] n-gram scratch
+  int ng_cap = 0;            // index entries per request
 };
 
 // The drafter a session's rounds run (DraftModel, draft.rs:18-21; without a
@@ -879,9 +897,9 @@ static DraftKind draft_kind(const mc_session* s) {
 
 static int trace_slot(mc_session* s) { return s->trace_on ? ++s->trace_next : 0; }
 
-static int bps_of(mc_session* s, int epi, int nt, int wf) {
-  int& b = s->bps[wf][epi][nt];
-  if (!b) b = std::max(1, gemv_blocks_per_sm(epi, nt, wf));
+static int bps_of(mc_session* s, int epi, int nt, int wf, bool tail = false) {
+  int& b = tail ? s->bps_tail[wf][epi == EPI_SWIGLU][nt] : s->bps[wf][epi][nt];
+  if (!b) b = std::max(1, gemv_blocks_per_sm(epi, nt, wf, tail));
   return b;
 }
 
@@ -1003,6 +1021,9 @@ static mc_status session_alloc(mc_session* s) {
   CK(cudaMemcpy(s->wait_ns, &wait_default, sizeof(wait_default), cudaMemcpyHostToDevice));
   CKS(s->al.alloc(&s->st_amax, (size_t)2 * kMaxTokens));
   CK(cudaMemset(s->st_amax, 0, (size_t)2 * kMaxTokens * 4));
+  CKS(s->al.alloc(&s->gbar, 2));
+  CK(cudaMemset(s->gbar, 0, 2 * sizeof(unsigned)));
+  if (const char* e = getenv("MODELC_CUDA_ENCODER_TAILS")) s->tails = atoi(e) & 3;
   s->st_np_cap = std::max(stripes, 1);
   CKS(s->al.alloc(&s->st_pss, (size_t)kMaxTokens * s->st_np_cap));
   if (s->tw->tp_world > 1) {
@@ -1040,14 +1061,20 @@ static mc_status session_alloc(mc_session* s) {
   CK(prepare_tc());
   for (int wf : {(int)WF_I8, (int)WF_Q4, (int)WF_I8R})
     for (int epi = 0; epi < 6; ++epi)
-      for (int nt : {1, 2, 3, 6}) bps_of(s, epi, nt, wf);
+      for (int nt : {1, 2, 3, 6}) {
+        bps_of(s, epi, nt, wf);
+        if (epi == EPI_RESID || epi == EPI_SWIGLU) bps_of(s, epi, nt, wf, true);
+      }
   CKS(s->al.alloc(&s->st, (size_t)s->B));
   CK(cudaMemset(s->st, 0, sizeof(SpecState) * s->B));
   s->ctx_stride = s->cap + 8;
   CKS(s->al.alloc(&s->ctx, (size_t)s->B * s->ctx_stride));
   if (!s->dw) {
-    CKS(s->al.alloc(&s->ng, (size_t)s->B * s->ctx_stride));
-    CKS(s->al.alloc(&s->ng_list, (size_t)s->B * s->ctx_stride));
+    // the prompt's windows plus one per round or step; context shifts let a
+    // request run past its capacity, so room for three more contexts' rounds
+    s->ng_cap = 4 * s->ctx_stride;
+    CKS(s->al.alloc(&s->ng, (size_t)s->B * s->ng_cap * (kNgram + 1)));
+    CKS(s->al.alloc(&s->ng_list, (size_t)s->B * s->ng_cap));
   }
   if (s->mlp) CKS(s->al.alloc(&s->mlp_hid, (size_t)s->B * mlp_hidden(s->mlp)));
   CKS(s->al.alloc(&s->acc_log, (size_t)s->B * s->ctx_stride));
@@ -1101,6 +1128,15 @@ static mc_status session_create(const mc_weights* target, const mc_weights* draf
     return set_err(MC_E_INVALID, "the draft model is replicated: load it with tp_world 1");
   if (target->tp_world > 1 && cfg->temperature > 0.0f)
     return set_err(MC_E_INVALID, "tensor-parallel sessions decode greedily (temperature 0)");
+  if (cfg->kv_mode != KV_FP32 && cfg->kv_mode != KV_INT8)
+    return set_err(MC_E_INVALID, "kv_mode %d is not MC_KV_FP32 or MC_KV_INT8", cfg->kv_mode);
+  if (cfg->shift_context < 0 || cfg->anchor_tokens < 0)
+    return set_err(MC_E_INVALID, "shift_context and anchor_tokens must be >= 0");
+  if (cfg->shift_context > 0 && cfg->temperature > 0.0f)
+    return set_err(MC_E_INVALID, "the context shift runs in greedy sessions (temperature 0)");
+  if (cfg->shift_context > 0 && cfg->shift_context + cfg->gamma + 2 > cfg->max_context)
+    return set_err(MC_E_INVALID, "shift_context %d + gamma + 2 exceeds max_context %d (a round "
+                   "must fit before the shift)", cfg->shift_context, cfg->max_context);
   CK(cudaSetDevice(target->dev));
   mc_session* s = new mc_session();
   s->tw = target;
@@ -1214,10 +1250,10 @@ struct StatIO {
   const PMat* pf = nullptr;  // upcoming GEMV to warm in L2 (idle_prefetch)
 };
 
-static mc_status enq_quant(mc_session* s, const float* h, int ld, int d, int M, const float* w,
-                           float eps, int do_norm, const StatIO* io = nullptr, bool tc = false,
-                           const AttnArgs* att = nullptr) {
-  QuantArgs q{};
+static void fill_quant(mc_session* s, QuantArgs& q, const float* h, int ld, int d, int M,
+                       const float* w, float eps, int do_norm, const StatIO* io, bool tc,
+                       const AttnArgs* att) {
+  q = QuantArgs{};
   if (att) {  // combine the attention's page partials while encoding
     q.att_o = att->part_o;
     q.att_ml = att->part_ml;
@@ -1253,6 +1289,13 @@ static mc_status enq_quant(mc_session* s, const float* h, int ld, int d, int M, 
   q.KB = (d + 31) / 32;
   q.nt = nt_for_tokens(M);
   q.xexp = s->xexp;
+}
+
+static mc_status enq_quant(mc_session* s, const float* h, int ld, int d, int M, const float* w,
+                           float eps, int do_norm, const StatIO* io = nullptr, bool tc = false,
+                           const AttnArgs* att = nullptr) {
+  QuantArgs q;
+  fill_quant(s, q, h, ld, d, M, w, eps, do_norm, io, tc, att);
   q.trace_slot = trace_slot(s);
   CK(launch_quant(q, s->stream, true));
   return MC_OK;
@@ -1276,8 +1319,9 @@ static mc_status enq_gemv(mc_session* s, const PMat& W, int epi, int M, GemvArgs
   a.cnt = s->cnt;
   a.err = s->err;
   a.trace_slot = trace_slot(s);
+  const bool tail = a.bar != nullptr;
   CK(run_projection(W, epi, M, a, s->nsm, s->stream,
-                    [&](int t) { return bps_of(s, epi, t, gemv_wf(W)); }));
+                    [&](int t) { return bps_of(s, epi, t, gemv_wf(W), tail); }));
   return MC_OK;
 }
 
@@ -1307,17 +1351,31 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
   ea.ctx_stride = s->ctx_stride;
   ea.zero_keys = keys;
   ea.n_zero = keys ? M : 0;
-  // Encoders in launch order with the RMSNorm weight each applies (nullptr:
-  // no norm).  Producer j (embedding, attention, or a GEMV epilogue) folds
-  // the statistics of its output into slot j % 2 for encoder j, which zeroes
-  // the other slot for producer j + 1.
-  std::vector<const float*> enc_w;
+  // Encoders in launch order: the rows each reads, the RMSNorm weight it
+  // applies (nullptr: no norm) and the projection that reads its digits.
+  // Producer j (embedding, attention, or a GEMV epilogue) folds the
+  // statistics of its output into slot j % 2 for encoder j, which zeroes the
+  // other slot for producer j + 1.
+  struct EncSpec {
+    const float* h;  // nullptr: the attention's page partials
+    int ld;
+    const float* w;
+    const PMat* cons;
+  };
+  std::vector<EncSpec> encs;
   for (const LayerW& Lw : W->layers) {
-    if (Lw.attn) { enc_w.push_back(Lw.attn_norm); enc_w.push_back(nullptr); }
-    if (Lw.mlp) { enc_w.push_back(Lw.mlp_norm); enc_w.push_back(nullptr); }
+    if (Lw.attn) {
+      encs.push_back({s->h, W->d, Lw.attn_norm, &Lw.qkv});
+      encs.push_back({nullptr, W->H * W->hdp, nullptr, &Lw.o});
+    }
+    if (Lw.mlp) {
+      encs.push_back({s->h, W->d, Lw.mlp_norm, &Lw.gu});
+      encs.push_back({s->act, W->F, nullptr, &Lw.down});
+    }
   }
-  enc_w.push_back(W->final_norm);
+  encs.push_back({s->h, W->d, W->final_norm, &W->head});
   size_t ej = 0;  // next encoder
+  size_t tailed = (size_t)-1;  // encoder run as its producer's tail (GemvArgs::bar)
   auto slot = [&](size_t j) { return s->st_amax + (j & 1) * kMaxTokens; };
   auto io_for = [&](size_t j, int np) {
     return StatIO{s->st_pss, np, slot(j), slot(j + 1), nullptr};
@@ -1325,7 +1383,7 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
   ea.st_pss = s->st_pss;
   ea.st_np = 1;
   ea.st_amax = slot(0);
-  ea.st_w = enc_w[0];
+  ea.st_w = encs[0].w;
   ea.trace_slot = trace_slot(s);
   CK(launch_embed(ea, s->stream, true));
   int prod_np = 1;  // sum-of-squares partials written by the last h producer
@@ -1334,8 +1392,22 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
     g.st_pss = s->st_pss;
     g.st_np = Wm.n_stripes;
     g.st_amax = slot(ej);
-    g.st_w = enc_w[ej];
+    g.st_w = encs[ej].w;
     prod_np = Wm.n_stripes;
+  };
+  // the next encoder as the tail of the single-launch GEMV that produces its
+  // rows (np: that GEMV's sum-of-squares partials; pf: L2 warm-up of upcoming
+  // weights, as the encoder's own launch would issue)
+  auto attach_tail = [&](GemvArgs& g, const PMat& Wm, int np, const PMat* pf) {
+    if (!(s->tails & 1) || M > kGroupTokens || use_tc(Wm, M) || ej >= encs.size() || !encs[ej].h)
+      return;
+    const EncSpec& e = encs[ej];
+    StatIO io = io_for(ej, np);
+    io.pf = pf;
+    fill_quant(s, g.enc, e.h, e.ld, e.ld, M, e.w, W->eps, e.w ? 1 : 0, &io, use_tc(*e.cons, M),
+               nullptr);
+    g.bar = s->gbar;
+    tailed = ej;
   };
   // o / down: h += W x (+ statistics); row-parallel across ranks: partial
   // sums, one all-reduce, then the residual add and the statistics
@@ -1347,6 +1419,7 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
     if (!tp) {
       g.out = s->h;
       resid_stats(g, Wm);
+      attach_tail(g, Wm, Wm.n_stripes, nullptr);
       return enq_gemv(s, Wm, EPI_RESID, M, g, next);
     }
     ResidArgs r{};
@@ -1360,7 +1433,7 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       r.M = M;
       r.pss = s->st_pss;
       r.amax = slot(ej);
-      r.w = enc_w[ej];
+      r.w = encs[ej].w;
       r.trace_slot = trace_slot(s);
       CK(launch_tp_reduce(r, s->tp, s->tp_epoch, s->tp_cnt_red, s->stream, true));
       prod_np = (d + kResidBlock - 1) / kResidBlock;
@@ -1380,7 +1453,7 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
     r.M = M;
     r.pss = s->st_pss;
     r.amax = slot(ej);
-    r.w = enc_w[ej];
+    r.w = encs[ej].w;
     r.trace_slot = trace_slot(s);
     CK(launch_resid_stats(r, s->stream, true));
     prod_np = (d + kResidBlock - 1) / kResidBlock;
@@ -1400,8 +1473,9 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
     const LayerW& Lw = W->layers[l];
     if (Lw.attn) {
       StatIO io = io_for(ej, prod_np);
-      CKS(enq_quant(s, s->h, d, d, M, Lw.attn_norm, W->eps, Lw.attn_norm ? 1 : 0, &io,
-                    use_tc(Lw.qkv, M)));
+      if (tailed != ej)
+        CKS(enq_quant(s, s->h, d, d, M, Lw.attn_norm, W->eps, Lw.attn_norm ? 1 : 0, &io,
+                      use_tc(Lw.qkv, M)));
       ++ej;
       GemvArgs a{};
       a.q_out = s->qb;
@@ -1422,6 +1496,21 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       a.sk = Lw.sk;
       a.kv_prefetch = 1;
       CKS(enq_gemv(s, Lw.qkv, EPI_QKV, M, a, nxt()));
+      if (&kv == &s->tkv && s->cfg.kv_mode == KV_INT8) {  // KvLayer::append of an INT8 layer
+        KvQArgs q{};
+        q.kc = a.kc;
+        q.vc = a.vc;
+        q.page_table = kv.page_table;
+        q.pos_ptr = pos_ptr;
+        q.pos_add = pos_add;
+        q.seq = sm;
+        q.M = M;
+        q.Hkv = W->Hkv;
+        q.hd = W->hdp;  // padding elements are zero: they change neither the scale nor stay nonzero
+        q.hdp = W->hdp;
+        q.page = kPage;
+        CK(launch_kv_qdq(q, s->stream, true));
+      }
       AttnArgs t{};
       t.q = s->qb;
       t.kc = a.kc;
@@ -1444,35 +1533,49 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       t.st_amax = slot(ej);
       // the gate/up projection after O: its weights beyond the O GEMV's prefetch
       idle_prefetch(Lw.mlp ? &Lw.gu : nullptr, kIdlePrefetch, &t.pf, &t.pf_bytes);
+      io = io_for(ej, 0);
+      if (s->tails & 2) {  // the O projection's encoder as the attention's tail
+        fill_quant(s, t.enc, nullptr, W->H * W->hdp, W->H * W->hdp, M, nullptr, 0.0f, 0, &io,
+                   use_tc(Lw.o, M), &t);
+        if (attention_tail_fits(t, s->nsm)) {
+          t.bar = s->gbar;
+          t.err = s->err;
+          tailed = ej;
+        }
+      }
       t.trace_slot = trace_slot(s);
       CK(launch_attention(t, s->stream, true));
-      io = io_for(ej, 0);
-      CKS(enq_quant(s, nullptr, W->H * W->hdp, W->H * W->hdp, M, nullptr, 0.0f, 0, &io,
-                    use_tc(Lw.o, M), &t));
+      if (tailed != ej)
+        CKS(enq_quant(s, nullptr, W->H * W->hdp, W->H * W->hdp, M, nullptr, 0.0f, 0, &io,
+                      use_tc(Lw.o, M), &t));
       ++ej;
       CKS(residual_gemv(Lw.o, nxt()));
     }
     if (Lw.mlp) {
       StatIO io = io_for(ej, prod_np);
-      CKS(enq_quant(s, s->h, d, d, M, Lw.mlp_norm, W->eps, Lw.mlp_norm ? 1 : 0, &io,
-                    use_tc(Lw.gu, M)));
+      if (tailed != ej)
+        CKS(enq_quant(s, s->h, d, d, M, Lw.mlp_norm, W->eps, Lw.mlp_norm ? 1 : 0, &io,
+                      use_tc(Lw.gu, M)));
       ++ej;
       GemvArgs g{};
       g.out = s->act;
       g.ldo = F;
       g.n_out = F;
       g.st_amax = slot(ej);
+      // the down weights beyond the gate/up GEMV's prefetch go with the encoder
+      attach_tail(g, Lw.gu, 0, &Lw.down);
       CKS(enq_gemv(s, Lw.gu, EPI_SWIGLU, M, g, nxt()));
       io = io_for(ej, 0);
-      io.pf = &Lw.down;  // the down weights beyond the gate/up GEMV's prefetch
-      CKS(enq_quant(s, s->act, F, F, M, nullptr, 0.0f, 0, &io, use_tc(Lw.down, M)));
+      io.pf = &Lw.down;
+      if (tailed != ej) CKS(enq_quant(s, s->act, F, F, M, nullptr, 0.0f, 0, &io, use_tc(Lw.down, M)));
       ++ej;
       CKS(residual_gemv(Lw.down, nxt()));
     }
   }
   StatIO io = io_for(ej, prod_np);
-  CKS(enq_quant(s, s->h, d, d, M, W->final_norm, W->eps, W->final_norm ? 1 : 0, &io,
-                use_tc(W->head, M)));
+  if (tailed != ej)
+    CKS(enq_quant(s, s->h, d, d, M, W->final_norm, W->eps, W->final_norm ? 1 : 0, &io,
+                  use_tc(W->head, M)));
   GemvArgs hd{};
   hd.out = logits_dev;
   hd.ldo = W->V;
@@ -1576,11 +1679,6 @@ extern "C" mc_status mc_draft(mc_session* s, const uint32_t* context, int32_t n,
 }
 
 // ------------------------------------------------------------------ speculative loop
-static int forward_launches(const mc_weights* W) {
-  int n = 1 + 2;  // embedding; final norm + LM head
-  for (const LayerW& L : W->layers) n += (L.attn ? 5 : 0) + (L.mlp ? 4 : 0);
-  return n;
-}
 
 // Verify forward of every request: vm positions each (request z's tokens are
 // z * vm .. z * vm + vm - 1), at the request's own target length.
@@ -1623,16 +1721,35 @@ static mc_status capture_verify(mc_session* s) {
 
 // Kernel launches of one round: the drafter's steps, the verify forward,
 // the acceptance (and the stochastic draft samples).
-static int round_launch_count(const mc_session* s) {
-  const int g = s->cfg.gamma;
-  const int dsteps = g + (s->cfg.bonus ? 1 : 0);
-  int draft = 0;
-  switch (draft_kind(s)) {
-    case DRAFT_LLAMA: draft = dsteps * forward_launches(s->dw); break;
-    case DRAFT_MLP: draft = 2 * g; break;
-    case DRAFT_NGRAM: draft = 1; break;
-  }
-  return draft + forward_launches(s->tw) + 1 + (s->cfg.temperature > 0.0f ? g : 0);
+// The session's caches for the context shift: the target KV and, with a
+// transformer draft, the draft KV.
+static KvPlanes kv_planes(const mc_weights* W, const KVSet& kv, int n_pages) {
+  KvPlanes p{};
+  if (!W) return p;
+  p.k = kv.k;
+  p.v = kv.v;
+  p.layer_stride = kv.layer_stride;
+  p.layers = W->L;
+  p.Hkv = W->Hkv;
+  p.hd = W->hdp;  // padding elements are zero
+  p.hdp = W->hdp;
+  p.page = kPage;
+  p.pt = kv.page_table;
+  p.pt_stride = n_pages;
+  return p;
+}
+static ShiftArgs shift_args(mc_session* s) {
+  ShiftArgs a{};
+  a.st = s->st;
+  a.ctx = s->ctx;
+  a.ctx_stride = s->ctx_stride;
+  a.B = s->B;
+  a.shift_context = s->cfg.shift_context;
+  a.anchor = s->cfg.anchor_tokens;
+  a.requant = s->cfg.kv_mode == KV_INT8 && s->cfg.anchor_tokens > 0;
+  a.t = kv_planes(s->tw, s->tkv, s->tkv.n_pages);
+  a.d = kv_planes(s->dw, s->dkv, s->dkv.n_pages);
+  return a;
 }
 
 static mc_status capture_round(mc_session* s) {
@@ -1652,7 +1769,7 @@ static mc_status capture_round(mc_session* s) {
     cudaError_t e = mlp_round(s->mlp, st, s->ctx, s->ctx_stride, s->B, g, s->mlp_hid, s->stream);
     if (e != cudaSuccess) rc = set_err(MC_E_CUDA, "MLP draft: %s", cudaGetErrorString(e));
   } else if (draft_kind(s) == DRAFT_NGRAM) {
-    cudaError_t e = launch_ngram_round(st, s->ctx, s->ng, s->ng_list, s->ctx_stride, s->B,
+    cudaError_t e = launch_ngram_round(st, s->ctx, s->ng, s->ng_list, s->ctx_stride, s->ng_cap, s->B,
                                        s->stream);
     if (e != cudaSuccess) rc = set_err(MC_E_CUDA, "n-gram draft: %s", cudaGetErrorString(e));
   }
@@ -1682,6 +1799,10 @@ static mc_status capture_round(mc_session* s) {
                                                s->ctx_stride, s->stream, true);
     if (e != cudaSuccess) rc = set_err(MC_E_CUDA, "accept launch: %s", cudaGetErrorString(e));
   }
+  if (rc == MC_OK && s->cfg.shift_context > 0) {  // generate.rs:738-748: the context shift
+    cudaError_t e = launch_context_shift(shift_args(s), s->nsm, s->stream, true);
+    if (e != cudaSuccess) rc = set_err(MC_E_CUDA, "context shift: %s", cudaGetErrorString(e));
+  }
   cudaGraph_t graph = nullptr;
   cudaError_t e = cudaStreamEndCapture(s->stream, &graph);
   if (rc != MC_OK) {
@@ -1689,10 +1810,22 @@ static mc_status capture_round(mc_session* s) {
     return rc;
   }
   if (e != cudaSuccess) return set_err(MC_E_CUDA, "capture failed: %s", cudaGetErrorString(e));
+  // the round's kernel launches, as captured
+  size_t n_nodes = 0;
+  int kernels = 0;
+  if (cudaGraphGetNodes(graph, nullptr, &n_nodes) == cudaSuccess) {
+    std::vector<cudaGraphNode_t> nodes(n_nodes);
+    if (cudaGraphGetNodes(graph, nodes.data(), &n_nodes) == cudaSuccess)
+      for (size_t i = 0; i < n_nodes; ++i) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nodes[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel)
+          ++kernels;
+      }
+  }
   e = cudaGraphInstantiate(&s->round_exec, graph, 0);
   cudaGraphDestroy(graph);
   if (e != cudaSuccess) return set_err(MC_E_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
-  s->round_launches = round_launch_count(s);
+  s->round_launches = kernels;
   return MC_OK;
 }
 
@@ -1722,12 +1855,15 @@ static SpecState fresh_state(const mc_session* s, int n_prompt) {
 
 // Prime request z (generate.rs:629-636): its prompt through the target and,
 // all but the last token, through the draft, into its own KV pages.
-static mc_status prime_request(mc_session* s, int z, int n_prompt) {
+// Target forwards over prompt tokens [t0, n_prompt) (t0 > 0: the K/V of the
+// first t0 were restored from a prefix snapshot), draft forwards over all but
+// the last.
+static mc_status prime_request(mc_session* s, int z, int n_prompt, int t0 = 0) {
   uint32_t* ctx = s->ctx + (size_t)z * s->ctx_stride;
   KVSet tkv = s->tkv, dkv = s->dkv;
   tkv.page_table += (size_t)z * tkv.n_pages;
   dkv.page_table += (size_t)z * dkv.n_pages;
-  for (int c0 = 0; c0 < n_prompt; c0 += kChunk) {
+  for (int c0 = t0; c0 < n_prompt; c0 += kChunk) {
     const int M = std::min(kChunk, n_prompt - c0);
     CK(launch_set_int(s->pos, c0, s->stream));
     EmbedArgs ea{};
@@ -1747,8 +1883,28 @@ static mc_status prime_request(mc_session* s, int z, int n_prompt) {
   return MC_OK;
 }
 
+// A prefix-cache entry (prefix_cache.rs:14-24 CachedPrefix): the context
+// tokens of one request and its target K/V -- the pages holding positions
+// [0, len), every layer -- as they stood when it was taken.
+struct mc_kv_snapshot {
+  const mc_weights* W = nullptr;
+  int dev = 0, kv_mode = 0, len = 0, pages = 0;
+  size_t page_floats = 0;  // floats of one KV page (Hkv heads x kPage positions x hdp)
+  float* k = nullptr;      // [L][pages * page_floats]
+  float* v = nullptr;
+  std::vector<uint32_t> tokens;
+};
+
+static mc_status prime_impl(mc_session* s, const uint32_t* prompts, const int32_t* lens,
+                            int32_t n_requests, const mc_kv_snapshot* snap);
+
 extern "C" mc_status mc_spec_prime_batch(mc_session* s, const uint32_t* prompts,
                                          const int32_t* lens, int32_t n_requests) {
+  return prime_impl(s, prompts, lens, n_requests, nullptr);
+}
+
+static mc_status prime_impl(mc_session* s, const uint32_t* prompts, const int32_t* lens,
+                            int32_t n_requests, const mc_kv_snapshot* snap) {
   if (!s || !lens || !prompts) return set_err(MC_E_INVALID, "bad arguments");
   if (n_requests != s->B)
     return set_err(MC_E_INVALID, "%d prompts for a session of %d requests", n_requests, s->B);
@@ -1773,15 +1929,30 @@ extern "C" mc_status mc_spec_prime_batch(mc_session* s, const uint32_t* prompts,
   }
   CK(cudaMemcpyAsync(s->ctx, s->h_ids, (size_t)n_requests * s->ctx_stride * 4,
                      cudaMemcpyHostToDevice, s->stream));
-  if (s->ng) {  // the n-gram index of each prompt: every window start, ascending
-    std::vector<int> starts((size_t)n_requests * s->ctx_stride, 0);
-    for (int z = 0; z < n_requests; ++z)
-      for (int i = 0; i + kNgram < lens[z]; ++i) starts[(size_t)z * s->ctx_stride + i] = i;
-    CK(cudaMemcpyAsync(s->ng, starts.data(), starts.size() * 4, cudaMemcpyHostToDevice,
-                       s->stream));
-    CK(cudaStreamSynchronize(s->stream));  // starts is a host temporary
+  if (s->ng) {  // the n-gram index of each prompt: every window, in order
+    const size_t row = (size_t)s->ng_cap * (kNgram + 1);
+    std::vector<uint32_t> ents((size_t)n_requests * row, 0u);
+    off = 0;
+    for (int z = 0; z < n_requests; ++z) {
+      for (int i = 0; i + kNgram < lens[z]; ++i)
+        memcpy(&ents[z * row + (size_t)i * (kNgram + 1)], prompts + off + i, (kNgram + 1) * 4);
+      off += (size_t)lens[z];
+    }
+    CK(cudaMemcpyAsync(s->ng, ents.data(), ents.size() * 4, cudaMemcpyHostToDevice, s->stream));
+    CK(cudaStreamSynchronize(s->stream));  // ents is a host temporary
   }
-  for (int z = 0; z < n_requests; ++z) CKS(prime_request(s, z, lens[z]));
+  int t0 = 0;
+  if (snap) {  // request 0's first snap->len positions from the snapshot
+    const size_t per_layer = (size_t)snap->pages * snap->page_floats;
+    for (int l = 0; l < s->tw->L; ++l) {
+      CK(cudaMemcpyAsync(s->tkv.k + l * s->tkv.layer_stride, snap->k + l * per_layer,
+                         per_layer * sizeof(float), cudaMemcpyDeviceToDevice, s->stream));
+      CK(cudaMemcpyAsync(s->tkv.v + l * s->tkv.layer_stride, snap->v + l * per_layer,
+                         per_layer * sizeof(float), cudaMemcpyDeviceToDevice, s->stream));
+    }
+    t0 = snap->len;
+  }
+  for (int z = 0; z < n_requests; ++z) CKS(prime_request(s, z, lens[z], z == 0 ? t0 : 0));
   std::vector<SpecState> h(n_requests);
   for (int z = 0; z < n_requests; ++z) h[z] = fresh_state(s, lens[z]);
   CK(cudaMemcpyAsync(s->st, h.data(), sizeof(SpecState) * n_requests, cudaMemcpyHostToDevice,
@@ -1797,6 +1968,86 @@ extern "C" mc_status mc_spec_prime(mc_session* s, const uint32_t* prompt, int32_
   if (!s || (!prompt && n_prompt > 0) || n_prompt < 0) return set_err(MC_E_INVALID, "bad arguments");
   if (s->B != 1) return set_err(MC_E_INVALID, "batched session: use mc_spec_prime_batch");
   return mc_spec_prime_batch(s, prompt, &n_prompt, 1);
+}
+
+extern "C" mc_status mc_kv_snapshot_take(mc_session* s, int32_t request, mc_kv_snapshot** out) {
+  if (!s || !out) return set_err(MC_E_INVALID, "null argument");
+  *out = nullptr;
+  if (request < 0 || request >= s->B)
+    return set_err(MC_E_INVALID, "request %d outside [0, %d)", request, s->B);
+  if (!s->prompt_len) return set_err(MC_E_INVALID, "call mc_spec_prime first");
+  if (s->tw->tp_world > 1) return set_err(MC_E_INVALID, "tensor-parallel sessions take no snapshot");
+  CKS(check_usable(s));
+  CK(cudaSetDevice(s->dev));
+  CK(cudaStreamSynchronize(s->stream));
+  SpecState h{};
+  CK(cudaMemcpy(&h, s->st + request, sizeof(h), cudaMemcpyDeviceToHost));
+  mc_kv_snapshot* snap = new mc_kv_snapshot();
+  snap->W = s->tw;
+  snap->dev = s->dev;
+  snap->kv_mode = s->cfg.kv_mode;
+  snap->len = h.lt;  // equal to the context length after a prime or a round
+  snap->pages = (h.lt + kPage - 1) / kPage;
+  snap->page_floats = (size_t)s->tw->Hkv * kPage * s->tw->hdp;
+  snap->tokens.resize((size_t)h.ctx_len);
+  mc_status st = MC_OK;
+  if (h.ctx_len > 0 &&
+      cudaMemcpy(snap->tokens.data(), s->ctx + (size_t)request * s->ctx_stride, (size_t)h.ctx_len * 4,
+                 cudaMemcpyDeviceToHost) != cudaSuccess)
+    st = set_err(MC_E_CUDA, "snapshot token copy failed");
+  const size_t per_layer = (size_t)snap->pages * snap->page_floats;
+  const size_t total = std::max<size_t>(per_layer * s->tw->L, 1);
+  if (st == MC_OK && (cudaMalloc(&snap->k, total * sizeof(float)) != cudaSuccess ||
+                      cudaMalloc(&snap->v, total * sizeof(float)) != cudaSuccess))
+    st = set_err(MC_E_OOM, "snapshot of %zu bytes", 2 * total * sizeof(float));
+  // request z's pages are [z * n_pages, (z + 1) * n_pages) of every layer
+  const size_t first = (size_t)request * s->tkv.n_pages * snap->page_floats;
+  for (int l = 0; l < s->tw->L && st == MC_OK; ++l)
+    if (cudaMemcpy(snap->k + l * per_layer, s->tkv.k + l * s->tkv.layer_stride + first,
+                   per_layer * sizeof(float), cudaMemcpyDeviceToDevice) != cudaSuccess ||
+        cudaMemcpy(snap->v + l * per_layer, s->tkv.v + l * s->tkv.layer_stride + first,
+                   per_layer * sizeof(float), cudaMemcpyDeviceToDevice) != cudaSuccess)
+      st = set_err(MC_E_CUDA, "snapshot copy failed");
+  if (st != MC_OK) {
+    mc_kv_snapshot_destroy(snap);
+    return st;
+  }
+  *out = snap;
+  return MC_OK;
+}
+
+extern "C" int32_t mc_kv_snapshot_tokens(const mc_kv_snapshot* snap, uint32_t* out, int32_t cap) {
+  if (!snap) return 0;
+  const int n = (int)snap->tokens.size();
+  if (out && cap > 0) memcpy(out, snap->tokens.data(), (size_t)std::min(n, (int)cap) * 4);
+  return n;
+}
+
+extern "C" mc_status mc_kv_snapshot_destroy(mc_kv_snapshot* snap) {
+  if (!snap) return MC_OK;
+  cudaSetDevice(snap->dev);
+  if (snap->k) cudaFree(snap->k);
+  if (snap->v) cudaFree(snap->v);
+  delete snap;
+  return MC_OK;
+}
+
+extern "C" mc_status mc_spec_prime_cached(mc_session* s, const mc_kv_snapshot* snap,
+                                          const uint32_t* prompt, int32_t n_prompt) {
+  if (!s || !snap || !prompt || n_prompt <= 0) return set_err(MC_E_INVALID, "bad arguments");
+  if (s->B != 1) return set_err(MC_E_INVALID, "batched session: prime requests one by one");
+  if (snap->W != s->tw || snap->dev != s->dev)
+    return set_err(MC_E_INVALID, "the snapshot was taken from another target model or device");
+  if (snap->kv_mode != s->cfg.kv_mode)
+    return set_err(MC_E_INVALID, "the snapshot holds another KV variant (%d, session %d)",
+                   snap->kv_mode, s->cfg.kv_mode);
+  const int n = (int)snap->tokens.size();
+  if (n > n_prompt || snap->len != n ||
+      memcmp(snap->tokens.data(), prompt, (size_t)n * 4) != 0)
+    return set_err(MC_E_INVALID, "the snapshot's %d tokens are not a prefix of the prompt", n);
+  if ((size_t)snap->pages * snap->page_floats > s->tkv.layer_stride)
+    return set_err(MC_E_CAPACITY, "the snapshot does not fit this session's KV");
+  return prime_impl(s, prompt, &n_prompt, 1, snap);
 }
 
 // Round loop of every request until each holds >= max_tokens generated ids.
@@ -1817,6 +2068,12 @@ extern "C" mc_status mc_spec_decode(mc_session* s, int32_t max_tokens, int32_t* 
   CK(cudaMemcpy(h.data(), s->st, sizeof(SpecState) * B, cudaMemcpyDeviceToHost));
   for (int z = 0; z < B; ++z)
     CK(cudaMemcpyAsync(&s->st[z].max_tokens, &max_tokens, 4, cudaMemcpyHostToDevice, s->stream));
+  // with the context shift the context stays within shift_context + a round
+  // (checked at session creation), but the generated count can fall when
+  // generated tokens are evicted, as in the reference's loop; a bound on the
+  // rounds ends a decode whose budget the shifts never let it reach
+  const bool shifting = s->cfg.shift_context > 0;
+  long long rounds_left = 8ll * ((long long)max_tokens + s->cap);
   for (;;) {
     if (s->cfg.cancel && *s->cfg.cancel) return set_err(MC_E_CANCELLED, "cancelled");
     int most = 0;
@@ -1824,13 +2081,16 @@ extern "C" mc_status mc_spec_decode(mc_session* s, int32_t max_tokens, int32_t* 
     if (most <= 0) break;
     // at most kRoundsPerBatch rounds between two looks at the cancel flag
     const int R = std::min((most + max_emit - 1) / max_emit, kRoundsPerBatch);
-    for (int z = 0; z < B; ++z) {
+    for (int z = 0; z < B && !shifting; ++z) {
       const int remaining = max_tokens - h[z].generated;
       if (remaining <= 0) continue;
       const int growth = std::min(max_emit * R, remaining + max_emit - 1);
       if (h[z].ctx_len + growth + max_emit + 2 > s->cap)
         return set_err(MC_E_CAPACITY, "generation would exceed KV capacity %d", s->cap);
     }
+    if ((rounds_left -= R) < 0)
+      return set_err(MC_E_CAPACITY, "the context shift keeps the generated count below %d "
+                     "(max_tokens above what a shifted context holds)", max_tokens);
     for (int r = 0; r < R; ++r) CK(cudaGraphLaunch(s->round_exec, s->stream));
     CK(cudaMemcpyAsync(h.data(), s->st, sizeof(SpecState) * B, cudaMemcpyDeviceToHost, s->stream));
     CK(cudaStreamSynchronize(s->stream));
@@ -1878,6 +2138,12 @@ extern "C" mc_status mc_spec_rewind(mc_session* s) {
   if (!s || !s->prompt_len) return set_err(MC_E_INVALID, "call mc_spec_prime first");
   CK(cudaSetDevice(s->dev));
   std::vector<SpecState> h(s->B);
+  if (s->cfg.shift_context > 0) {  // a shifted context no longer holds the prompt
+    CK(cudaMemcpy(h.data(), s->st, sizeof(SpecState) * s->B, cudaMemcpyDeviceToHost));
+    for (int z = 0; z < s->B; ++z)
+      if (h[z].n_shifts > 0)
+        return set_err(MC_E_INVALID, "request %d's context was shifted: prime it again", z);
+  }
   for (int z = 0; z < s->B; ++z) h[z] = fresh_state(s, s->prompt_lens[z]);
   CK(cudaMemcpyAsync(s->st, h.data(), sizeof(SpecState) * s->B, cudaMemcpyHostToDevice, s->stream));
   CK(cudaStreamSynchronize(s->stream));
@@ -2031,7 +2297,7 @@ extern "C" mc_status mc_session_set_wait_timeout(mc_session* s, int32_t ms) {
 }
 
 extern "C" int32_t mc_session_round_launches(const mc_session* s) {
-  return s ? round_launch_count(s) : 0;
+  return s ? s->round_launches : 0;
 }
 
 extern "C" mc_status mc_speculative_generate(mc_session* s, const uint32_t* prompt,

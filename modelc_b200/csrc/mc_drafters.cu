@@ -140,33 +140,32 @@ __global__ void __launch_bounds__(kMlpFc2Threads) k_mlp_fc2(const float* __restr
 // (:832-841), block-wide: among the index entries whose n-token key equals
 // key[0, n) (shared memory), the continuation with the highest count; count
 // ties go to the continuation of the earliest entry (the reference leaves
-// them to HashMap order).  Entry e is the window starting at toks[ent(e)]
-// (key toks[s .. s + n), continuation toks[s + n]); entries ascend.  list:
-// scratch of n_ent ints.  Returns the token, or -1 when no key matches.
-template <class Ent>
-__device__ long long ngram_step(const uint32_t* toks, Ent ent, int n_ent, int n,
-                                const uint32_t* key, int* list, int* s_nm,
-                                unsigned long long* s_best) {
+// them to HashMap order).  Entry e (in insertion order) is row(e): its key
+// row(e)[0 .. n), its continuation row(e)[n].  list: scratch of n_ent ints.
+// Returns the token, or -1 when no key matches.
+template <class Row>
+__device__ long long ngram_step(Row row, int n_ent, int n, const uint32_t* key, int* list,
+                                int* s_nm, unsigned long long* s_best) {
   if (threadIdx.x == 0) *s_nm = 0;
   __syncthreads();
   for (int e = threadIdx.x; e < n_ent; e += blockDim.x) {
-    const int s = ent(e);
+    const uint32_t* r = row(e);
     bool eq = true;
-    for (int q = 0; q < n && eq; ++q) eq = toks[s + q] == key[q];
-    if (eq) list[atomicAdd(s_nm, 1)] = s;
+    for (int q = 0; q < n && eq; ++q) eq = r[q] == key[q];
+    if (eq) list[atomicAdd(s_nm, 1)] = e;
   }
   __syncthreads();
   const int nm = *s_nm;
   if (nm == 0) return -1;  // block-uniform
-  // (count, -first window) of each match's continuation, packed so that the
+  // (count, -first entry) of each match's continuation, packed so that the
   // largest key is the most frequent, earliest-seen continuation
   unsigned long long best = 0ull;
   for (int i = threadIdx.x; i < nm; i += blockDim.x) {
-    const uint32_t c = toks[list[i] + n];
+    const uint32_t c = row(list[i])[n];
     unsigned count = 0;
     int first = 0x7fffffff;
     for (int j = 0; j < nm; ++j)
-      if (toks[list[j] + n] == c) {
+      if (row(list[j])[n] == c) {
         ++count;
         first = min(first, list[j]);
       }
@@ -185,7 +184,7 @@ __device__ long long ngram_step(const uint32_t* toks, Ent ent, int n_ent, int n,
   for (int w = 0; w < (int)(blockDim.x >> 5); ++w) b = s_best[w] > b ? s_best[w] : b;
   const int first = (int)(0x7fffffffu - (unsigned)(b & 0xffffffffull));
   __syncthreads();  // s_best and list may be reused by the next step
-  return (long long)toks[first + n];
+  return (long long)row(first)[n];
 }
 
 // draft_tokens over the index of toks[0, n_tok) (build_ngram_index: every
@@ -204,7 +203,8 @@ __global__ void __launch_bounds__(kNgramThreads) k_ngram_draft(uint32_t* toks, i
     if (clen < n || n < 1 || n > 32) break;  // a short key matches no n-token key (block-uniform)
     if (threadIdx.x < n) s_key[threadIdx.x] = toks[clen - n + threadIdx.x];
     __syncthreads();
-    const long long next = ngram_step(toks, [](int e) { return e; }, max(n_tok - n, 0), n, s_key,
+    // entry e: the window at toks[e] (windows ascend)
+    const long long next = ngram_step([&](int e) { return toks + e; }, max(n_tok - n, 0), n, s_key,
                                       list, &s_nm, s_best);
     if (next < 0) break;  // block-uniform
     if (threadIdx.x == 0) {
@@ -220,25 +220,33 @@ __global__ void __launch_bounds__(kNgramThreads) k_ngram_draft(uint32_t* toks, i
 // The n-gram drafter of a session's round (see launch_ngram_round): one CTA
 // per sequence.  The index is the prompt's windows plus, per earlier round or
 // fallback step, the window ending at the context's last token
-// (update_ngram_index adds only that one).
+// (update_ngram_index adds only that one), each entry a copy of its n + 1
+// tokens (the index keeps them when a context shift drops their tokens, as
+// the reference's HashMap does).  At most ng_cap entries per sequence; the
+// updates past it are dropped.
 __global__ void __launch_bounds__(kNgramThreads) k_ngram_round(mc::SpecState* st_all,
-                                                               const uint32_t* ctx_all, int* ng_all,
-                                                               int* list_all, int ctx_stride) {
+                                                               const uint32_t* ctx_all,
+                                                               uint32_t* ng_all, int* list_all,
+                                                               int ctx_stride, int ng_cap) {
   __shared__ int s_nm, s_len, s_nent, s_stop;
   __shared__ unsigned long long s_best[kNgramThreads / 32];
   __shared__ uint32_t s_tok[32 + mc::kGroupTokens];  // the key window, then the drafts
   const int z = blockIdx.x;
   mc::SpecState* st = st_all + z;
   const uint32_t* ctx = ctx_all + (size_t)z * ctx_stride;
-  int* ng = ng_all + (size_t)z * ctx_stride;
-  int* list = list_all + (size_t)z * ctx_stride;
   const int n = st->ngram, gamma = st->gamma;
+  uint32_t* ng = ng_all + (size_t)z * ng_cap * (n + 1);
+  int* list = list_all + (size_t)z * ng_cap;
   if (threadIdx.x == 0) {
     // a request whose budget is spent takes no more rounds (generate.rs:638)
     s_stop = (st->max_tokens > 0 && st->generated >= st->max_tokens) || n < 1 || n > 32;
     const int len = st->ctx_len;
     if (!s_stop && len > st->ng_last_len) {  // update_ngram_index after the last round
-      if (len >= n + 1) ng[st->ng_len++] = len - (n + 1);
+      if (len >= n + 1 && st->ng_len < ng_cap) {
+        uint32_t* e = ng + (size_t)st->ng_len * (n + 1);
+        for (int q = 0; q <= n; ++q) e[q] = ctx[len - (n + 1) + q];
+        st->ng_len += 1;
+      }
       st->ng_last_len = len;
     }
     s_len = len;
@@ -253,8 +261,8 @@ __global__ void __launch_bounds__(kNgramThreads) k_ngram_round(mc::SpecState* st
   int produced = 0;
   for (int g = 0; g < gamma; ++g) {
     if (len + g < n) break;  // a short key matches no n-token key (block-uniform)
-    const long long next = ngram_step(ctx, [&](int e) { return ng[e]; }, s_nent, n, s_tok + g,
-                                      list, &s_nm, s_best);
+    const long long next = ngram_step([&](int e) { return ng + (size_t)e * (n + 1); }, s_nent, n,
+                                      s_tok + g, list, &s_nm, s_best);
     if (next < 0) break;  // block-uniform
     if (threadIdx.x == 0) s_tok[n + g] = (uint32_t)next;
     ++produced;
@@ -336,9 +344,9 @@ int mlp_device(const mc_mlp_drafter* m) { return m->dev; }
 int mlp_vocab(const mc_mlp_drafter* m) { return m->V; }
 int mlp_hidden(const mc_mlp_drafter* m) { return m->dh; }
 
-cudaError_t launch_ngram_round(SpecState* st, const uint32_t* ctx, int* ng, int* list,
-                               int ctx_stride, int n_seq, cudaStream_t s) {
-  k_ngram_round<<<n_seq, kNgramThreads, 0, s>>>(st, ctx, ng, list, ctx_stride);
+cudaError_t launch_ngram_round(SpecState* st, const uint32_t* ctx, uint32_t* ng, int* list,
+                               int ctx_stride, int ng_cap, int n_seq, cudaStream_t s) {
+  k_ngram_round<<<n_seq, kNgramThreads, 0, s>>>(st, ctx, ng, list, ctx_stride, ng_cap);
   return cudaGetLastError();
 }
 }  // namespace mc

@@ -56,6 +56,17 @@ __host__ __device__ inline int groups_for_tokens(int m) {
 // pos_ptr[z * pos_stride] + pos_add + i, with KV pages
 // page_table[z * pt_stride + ...]; its argmax key goes to
 // keys[z * key_stride + i].
+#ifdef __CUDACC__
+// Programmatic dependent launch: wait for the preceding grid's completion and
+// memory; let the next grid launch.
+__device__ __forceinline__ void grid_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+#endif
+
 struct SeqMap {
   int seq_len;
   int pos_stride;   // ints between the sequences' position counters
@@ -209,11 +220,12 @@ struct GemvArgs {
   int row_offset;        // LMHEAD: global vocabulary index of packed row 0
   const int4* wtc;       // tcgen05 path: weights in the canonical layout (k_gemm_tc)
   TPArgs tp;             // EPI_TP
-  // Fused encoder (bar != nullptr): before the main loop every CTA encodes
-  // its slice of the digits this launch reads (enc, the encoder's statistics
-  // path, k-blocks split over the grid like k_quant's), then the grid meets
-  // at a barrier (bar[0] arrivals, bar[1] generation; bounded wait).  The
-  // grid is at most one wave (occupancy), so all its CTAs are resident.
+  // Encoding tail (bar != nullptr; RESID and SWIGLU): after the epilogues
+  // the grid meets at a barrier (bar[0] arrivals, bar[1] generation; bounded
+  // wait), then every CTA encodes its slice of the next projection's input
+  // as k_quant<true> would with enc (its statistics path, k-blocks split
+  // over the grid).  The grid is at most one wave of the tail variant
+  // (occupancy), so all its CTAs are resident.
   QuantArgs enc;
   unsigned* bar;
   int trace_slot;        // MC_TRACE builds: 1 + timeline slot, 0 = untraced
@@ -243,6 +255,14 @@ struct AttnArgs {
                          // a bound on its max |output| (float bits, atomicMax)
   const void* pf;        // L2 prefetch of upcoming weights while HBM is idle, or nullptr
   long long pf_bytes;
+  // Encoding tail (bar != nullptr; attention_tail_fits): after its partials
+  // and bound are out the grid meets at a bounded barrier (bar[0] arrivals,
+  // bar[1] generation), then every CTA combines and encodes a slice of the O
+  // projection's input as k_quant_att would with enc (its att_* fields
+  // describing these partials), saving that launch.
+  QuantArgs enc;
+  unsigned* bar;
+  int* err;              // raised when the barrier's bounded wait expires
   int trace_slot;        // MC_TRACE builds: 1 + timeline slot, 0 = untraced
 };
 
@@ -332,6 +352,10 @@ struct SpecState {
   int ng_len;
   int ng_last_len;
   int ngram;
+  // the context shift of the last round (generate.rs:26-63): tokens removed
+  // (0: none), where the removed range starts, the target / draft KV
+  // lengths before it, whether it was the anchored form; shifts so far
+  int sh_n, sh_at, sh_lt, sh_ld, sh_anch, n_shifts;
   unsigned long long tkeys[kGroupTokens];
   unsigned long long dkeys[kGroupTokens];
 };
@@ -360,7 +384,7 @@ __host__ __device__ inline uint32_t key_index(unsigned long long k) {
 // data-independent loads (weights) before griddepcontrol.wait.
 cudaError_t launch_gemv(const GemvArgs& a, int epi, int nt, int wf, int grid,
                         cudaStream_t s, bool pdl);
-int gemv_blocks_per_sm(int epi, int nt, int wf);
+int gemv_blocks_per_sm(int epi, int nt, int wf, bool tail = false);
 // tcgen05 GEMM for 9..64 tokens: grid (128-row tiles, ksplit), 48 digit
 // columns per group of 16 tokens; the digits must be encoded with
 // QuantArgs::tc_layout; ksplit > 1 merges through ws/cnt.
@@ -384,10 +408,56 @@ int32_t set_error(int32_t st, const char* msg);
 cudaError_t launch_act_amax(const float* x, int ld, int d, int M, unsigned* amax, cudaStream_t s,
                             bool pdl);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
+// Whether launch_attention runs a with the encoding tail: the tensor-core
+// kernel with one m-tile, a grid of at most one wave of it on nsm SMs, and
+// the combined slice within its shared memory (a.enc.M / KB set).
+bool attention_tail_fits(const AttnArgs& a, int nsm);
 cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t s, bool pdl);
 // One CTA per sequence z of a batch: st + z, ctx + z * ctx_stride,
 // acc_log + z * log_stride.  A sequence whose budget is spent (generated >=
 // max_tokens > 0) is left unchanged.
+// Target KV variants (mc_spec_cfg::kv_mode).
+enum KvMode : int { KV_FP32 = 0, KV_INT8 = 1, KV_MIXED = 2 };
+
+// The new tokens of one forward in one layer's K/V pages: token m =
+// (sequence z, offset i) by seq, at position pos_ptr[z * seq.pos_stride] +
+// pos_add + i, head h column c at ((page * Hkv + h) * page_len + pos % page_len)
+// * hdp + c.
+struct KvQArgs {
+  float* kc;
+  float* vc;
+  const int* page_table;
+  const int* pos_ptr;
+  int pos_add;
+  SeqMap seq;
+  int M, Hkv, hd, hdp, page;
+};
+// KvLayer::append of an INT8 layer on those tokens (mc_kvcache.cu).
+cudaError_t launch_kv_qdq(const KvQArgs& a, cudaStream_t s, bool pdl);
+
+// One KV cache (target or draft) of every request, for the context shift.
+struct KvPlanes {
+  float* k;             // [layers][layer_stride floats]: pages [page][Hkv][page_len][hdp]
+  float* v;
+  size_t layer_stride;
+  int layers, Hkv, hd, hdp, page;
+  const int* pt;        // request z's page-table row at pt + z * pt_stride
+  int pt_stride;
+};
+struct ShiftArgs {
+  SpecState* st;
+  uint32_t* ctx;
+  int ctx_stride;
+  int B;
+  int shift_context;    // GenerationConfig::max_context
+  int anchor;           // GenerationConfig::anchor_tokens
+  int requant;          // INT8 target: re-quantize the kept tokens after an anchored shift
+  KvPlanes t, d;        // target KV; draft KV (d.layers == 0: none)
+};
+// generate.rs:26-63 context_shift after a round, on the device: the plan and
+// token move, the K/V moves, the INT8 re-quantization (three launches).
+cudaError_t launch_context_shift(const ShiftArgs& a, int nsm, cudaStream_t s, bool pdl);
+
 cudaError_t launch_accept_greedy(SpecState* st, uint32_t* ctx, int* acc_log, int vm, int n_seq,
                                  int ctx_stride, int log_stride, cudaStream_t s, bool pdl);
 cudaError_t launch_set_int(int* p, int v, cudaStream_t s);
@@ -397,10 +467,11 @@ cudaError_t launch_set_int(int* p, int v, cudaStream_t s);
 // sequence z: first the window ending at the context's last token joins the
 // index when the context grew since the last update, then up to gamma draft
 // tokens into st->dkeys and their count into st->n_draft.  The index of
-// sequence z is ng + z * ctx_stride: ascending window starts into its
-// context; list: scratch of the same size.
-cudaError_t launch_ngram_round(SpecState* st, const uint32_t* ctx, int* ng, int* list,
-                               int ctx_stride, int n_seq, cudaStream_t s);
+// sequence z is ng + z * ng_cap * (n + 1): up to ng_cap entries of n + 1
+// tokens (key, continuation) in insertion order; list: ng_cap ints per
+// sequence of scratch.
+cudaError_t launch_ngram_round(SpecState* st, const uint32_t* ctx, uint32_t* ng, int* list,
+                               int ctx_stride, int ng_cap, int n_seq, cudaStream_t s);
 }  // namespace mc
 typedef struct mc_mlp_drafter mc_mlp_drafter;
 namespace mc {

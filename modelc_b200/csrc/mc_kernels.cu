@@ -159,12 +159,6 @@ __device__ __forceinline__ uint2 ldg_u2(const void* p) {
                : "l"(p));
   return v;
 }
-__device__ __forceinline__ void grid_wait() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-__device__ __forceinline__ void grid_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
 __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes)
                : "memory");
@@ -467,7 +461,7 @@ __device__ __forceinline__ size_t digit_index(int kb, int c, int kk, int nt, int
   return (size_t)g * KB * 64 * nt + digit_word(kb, c - g * 8 * nt, kk, nt, false);
 }
 
-template <class Src4, class Dst>
+template <int BATCH = kEncBatch, class Src4, class Dst>
 __device__ __forceinline__ void encode_digits(const StatArgs& a, int nt, int KB, int kb0, int kb1,
                                               const float* s_mul, const int* s_e, Src4 src4,
                                               Dst dst, bool tc = false) {
@@ -476,10 +470,10 @@ __device__ __forceinline__ void encode_digits(const StatArgs& a, int nt, int KB,
   const int pad_cols = 8 * nt * groups - 3 * M;
   const int ngroups = (kb1 - kb0) * 8;
   const int tasks = ngroups * (M + pad_cols);
-  for (int t0 = threadIdx.x; t0 < tasks; t0 += blockDim.x * kEncBatch) {
-    float4 v[kEncBatch];
+  for (int t0 = threadIdx.x; t0 < tasks; t0 += blockDim.x * BATCH) {
+    float4 v[BATCH];
 #pragma unroll
-    for (int u = 0; u < kEncBatch; ++u) {
+    for (int u = 0; u < BATCH; ++u) {
       const int task = t0 + u * blockDim.x;
       v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       if (task < tasks) {
@@ -489,7 +483,7 @@ __device__ __forceinline__ void encode_digits(const StatArgs& a, int nt, int KB,
       }
     }
 #pragma unroll
-    for (int u = 0; u < kEncBatch; ++u) {
+    for (int u = 0; u < BATCH; ++u) {
       const int task = t0 + u * blockDim.x;
       if (task >= tasks) continue;
       const int grp = task % ngroups;
@@ -535,7 +529,7 @@ __device__ __forceinline__ void encode_digits(const StatArgs& a, int nt, int KB,
 // statistics, so they are loaded before ready() (which computes s_mul / s_e
 // and ends with a block barrier) and their round trip overlaps it.  The
 // digits are those of encode_digits, bit for bit.
-template <class Src4, class Dst, class Ready>
+template <int BATCH = kEncBatch, class Src4, class Dst, class Ready>
 __device__ __forceinline__ void encode_digits_early(const StatArgs& a, int nt, int KB, int kb0,
                                                     int kb1, const float* s_mul, const int* s_e,
                                                     Src4 src4, Dst dst, bool tc, Ready ready) {
@@ -545,10 +539,10 @@ __device__ __forceinline__ void encode_digits_early(const StatArgs& a, int nt, i
   const int ngroups = (kb1 - kb0) * 8;
   const int tasks = ngroups * (M + pad_cols);
   const bool use_w = a.do_norm && a.w;
-  float4 v[kEncBatch], wv[kEncBatch];
+  float4 v[BATCH], wv[BATCH];
   auto load = [&](int t0) {
 #pragma unroll
-    for (int u = 0; u < kEncBatch; ++u) {
+    for (int u = 0; u < BATCH; ++u) {
       const int task = t0 + u * blockDim.x;
       v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       wv[u] = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
@@ -574,10 +568,10 @@ __device__ __forceinline__ void encode_digits_early(const StatArgs& a, int nt, i
   };
   load(threadIdx.x);
   ready();
-  for (int t0 = threadIdx.x; t0 < tasks; t0 += blockDim.x * kEncBatch) {
+  for (int t0 = threadIdx.x; t0 < tasks; t0 += blockDim.x * BATCH) {
     if (t0 != (int)threadIdx.x) load(t0);
 #pragma unroll
-    for (int u = 0; u < kEncBatch; ++u) {
+    for (int u = 0; u < BATCH; ++u) {
       const int task = t0 + u * blockDim.x;
       if (task >= tasks) continue;
       const int grp = task % ngroups;
@@ -638,21 +632,29 @@ __device__ __forceinline__ float4 load_act4(const float* h, int ld, int d, int m
 // (QuantArgs::att_o): the CTA's slice [lo, hi) of every token is combined
 // into shared memory, then encoded.  Output (token m, head h, columns c..c+3)
 // = sum_p e^(m_p - M) o_p / sum_p e^(m_p - M) l_p over the pages p of its
-// query block, M = max_p m_p.  Two adjacent lanes share an output (pages of
-// even and odd index, at most 16 each in flight), their partial sums added
-// even + odd; so each output is one round trip of loads for up to 32 pages.
-// The exponent comes from the attention's bound (amax), read meanwhile.
+// query block, M = max_p m_p.  kCombLanes adjacent lanes share an output:
+// lane j of the group takes pages j, j + kCombLanes, ..., adding them in
+// order (B of them in flight, which leaves the arithmetic unchanged), and the
+// group's sums meet in an xor-shuffle tree, whose sums are bitwise the same
+// on every lane -- the same result for every B.  The exponent comes from the
+// attention's bound (amax), read meanwhile.  `lead`: this CTA writes the
+// exponents and zeroes the next producer's max slot.  EB: encode_digits'
+// batch.
+constexpr int kCombLanes = 16;
+template <int B, int EB>
 __device__ __forceinline__ void attn_combine_encode(const QuantArgs& a, int lo, int hi, int kb0,
-                                                    int kb1, uint32_t* s_bound, float* s_mul,
-                                                    int* s_e, float* s_slice, uint32_t* xq) {
+                                                    int kb1, bool lead, uint32_t* s_bound,
+                                                    float* s_mul, int* s_e, float* s_slice,
+                                                    uint32_t* xq) {
+  constexpr int LN = kCombLanes;
   if (threadIdx.x < a.M) s_bound[threadIdx.x] = __ldcg(a.amax + threadIdx.x);
   const int hd = a.att_hdp, G = a.att_G, Rs = G * a.att_qblk;
   const int n_qb = (a.att_seq.seq_len + a.att_qblk - 1) / a.att_qblk;
   const int span = hi - lo, q4 = span / 4, n_out = a.M * q4;
   const size_t cs4 = (size_t)Rs * hd / 4;  // float4s between pages
-  constexpr int B = 16;                     // pages per lane in flight
-  for (int base = 0; base < 2 * n_out; base += blockDim.x) {  // block-uniform trip count
-    const int t = base + (int)threadIdx.x, o = t >> 1, half = t & 1;
+  const int sub = (int)threadIdx.x & (LN - 1);
+  for (int base = 0; base < LN * n_out; base += blockDim.x) {  // block-uniform trip count
+    const int t = base + (int)threadIdx.x, o = t / LN;
     const bool live = o < n_out;
     const int m = live ? o / q4 : 0;
     const int k = lo + 4 * (live ? o - m * q4 : 0);
@@ -672,29 +674,32 @@ __device__ __forceinline__ void attn_combine_encode(const QuantArgs& a, int lo, 
       ml = reinterpret_cast<const float2*>(a.att_ml) + row;
       src = reinterpret_cast<const float4*>(a.att_o + row * hd + (k - hh * hd));
     }
-    // M over every page of the row (both lanes' pages): a pre-pass only when
+    // M over every page of the row (all lanes' pages): a pre-pass only when
     // the pages do not fit one batch
     float M_ = -INFINITY;
-    if (nch > 2 * B)
-      for (int p = half; p < nch; p += 2) M_ = fmaxf(M_, __ldcg(&ml[(size_t)p * Rs].x));
+    if (nch > LN * B)
+      for (int p = sub; p < nch; p += LN) M_ = fmaxf(M_, __ldcg(&ml[(size_t)p * Rs].x));
     float l = 0.0f;
     float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    // every lane runs the warp's longest page loop (the shuffle below needs
+    // every lane runs the warp's longest page loop (the shuffles below need
     // all of them; lanes past their own pages load nothing)
-    for (int p0 = 0; __any_sync(0xffffffffu, p0 < nch); p0 += 2 * B) {
+    for (int p0 = 0; __any_sync(0xffffffffu, p0 < nch); p0 += LN * B) {
       float2 mv[B];
       float4 v[B];
 #pragma unroll
       for (int u = 0; u < B; ++u) {
-        const int p = p0 + 2 * u + half;
+        const int p = p0 + LN * u + sub;
         mv[u] = p < nch ? __ldcg(ml + (size_t)p * Rs) : make_float2(-INFINITY, 0.0f);
         v[u] = p < nch ? __ldcg(src + (size_t)p * cs4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       }
-      if (p0 == 0 && nch <= 2 * B) {
+      if (p0 == 0) {
+        if (nch <= LN * B) {
 #pragma unroll
-        for (int u = 0; u < B; ++u) M_ = fmaxf(M_, mv[u].x);
+          for (int u = 0; u < B; ++u) M_ = fmaxf(M_, mv[u].x);
+        }
+#pragma unroll
+        for (int off = LN / 2; off; off >>= 1) M_ = fmaxf(M_, __shfl_xor_sync(0xffffffffu, M_, off));
       }
-      if (p0 == 0) M_ = fmaxf(M_, __shfl_xor_sync(0xffffffffu, M_, 1));
 #pragma unroll
       for (int u = 0; u < B; ++u) {
         const float w = (mv[u].x == -INFINITY) ? 0.0f : expf(mv[u].x - M_);
@@ -705,26 +710,21 @@ __device__ __forceinline__ void attn_combine_encode(const QuantArgs& a, int lo, 
         acc.w = __fmaf_rn(v[u].w, w, acc.w);
       }
     }
-    // even + odd, in that order on both lanes
-    const float lo_l = __shfl_sync(0xffffffffu, l, (threadIdx.x & 31) & ~1);
-    const float hi_l = __shfl_sync(0xffffffffu, l, (threadIdx.x & 31) | 1);
-    float4 e, q;
-    e.x = __shfl_sync(0xffffffffu, acc.x, (threadIdx.x & 31) & ~1);
-    e.y = __shfl_sync(0xffffffffu, acc.y, (threadIdx.x & 31) & ~1);
-    e.z = __shfl_sync(0xffffffffu, acc.z, (threadIdx.x & 31) & ~1);
-    e.w = __shfl_sync(0xffffffffu, acc.w, (threadIdx.x & 31) & ~1);
-    q.x = __shfl_sync(0xffffffffu, acc.x, (threadIdx.x & 31) | 1);
-    q.y = __shfl_sync(0xffffffffu, acc.y, (threadIdx.x & 31) | 1);
-    q.z = __shfl_sync(0xffffffffu, acc.z, (threadIdx.x & 31) | 1);
-    q.w = __shfl_sync(0xffffffffu, acc.w, (threadIdx.x & 31) | 1);
-    if (live && half == 0) {
+#pragma unroll
+    for (int off = LN / 2; off; off >>= 1) {
+      l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, off));
+      acc.x = __fadd_rn(acc.x, __shfl_xor_sync(0xffffffffu, acc.x, off));
+      acc.y = __fadd_rn(acc.y, __shfl_xor_sync(0xffffffffu, acc.y, off));
+      acc.z = __fadd_rn(acc.z, __shfl_xor_sync(0xffffffffu, acc.z, off));
+      acc.w = __fadd_rn(acc.w, __shfl_xor_sync(0xffffffffu, acc.w, off));
+    }
+    if (live && sub == 0) {
       float4 r = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       if (in) {
-        const float den = __fadd_rn(lo_l, hi_l);
-        r.x = __fdiv_rn(__fadd_rn(e.x, q.x), den);
-        r.y = __fdiv_rn(__fadd_rn(e.y, q.y), den);
-        r.z = __fdiv_rn(__fadd_rn(e.z, q.z), den);
-        r.w = __fdiv_rn(__fadd_rn(e.w, q.w), den);
+        r.x = __fdiv_rn(acc.x, l);
+        r.y = __fdiv_rn(acc.y, l);
+        r.z = __fdiv_rn(acc.z, l);
+        r.w = __fdiv_rn(acc.w, l);
       }
       *reinterpret_cast<float4*>(s_slice + (size_t)m * span + (k - lo)) = r;
     }
@@ -744,12 +744,12 @@ __device__ __forceinline__ void attn_combine_encode(const QuantArgs& a, int lo, 
     }
     s_mul[m] = (e != kExpNonFinite) ? ldexpf(1.0f, e) : 0.0f;
     s_e[m] = e;
-    if (blockIdx.x == 0) a.xexp[m] = e;
+    if (lead) a.xexp[m] = e;
   }
-  if (blockIdx.x == 0 && a.amax_next && threadIdx.x < kMaxTokens) a.amax_next[threadIdx.x] = 0u;
+  if (lead && a.amax_next && threadIdx.x < kMaxTokens) a.amax_next[threadIdx.x] = 0u;
   __syncthreads();
   const StatArgs sa{nullptr, 0, a.d, a.M, nullptr, 0, 0.0f, 0};
-  encode_digits(sa, a.nt, a.KB, kb0, kb1, s_mul, s_e,
+  encode_digits<EB>(sa, a.nt, a.KB, kb0, kb1, s_mul, s_e,
                 [&](int m, int k) {
                   const float* p = s_slice + (size_t)m * span + (k - lo);
                   return make_float4(k < a.d ? p[0] : 0.0f, k + 1 < a.d ? p[1] : 0.0f,
@@ -762,7 +762,7 @@ __device__ __forceinline__ void attn_combine_encode(const QuantArgs& a, int lo, 
 // exponents come from the producer's statistics, then the slice is encoded;
 // block 0 also writes the exponents and zeroes the next producer's max slot.
 // s_mul / s_e: kMaxTokens each (shared).  phase(k) marks trace phases 1-3.
-template <class Phase>
+template <int BATCH = kEncBatch, class Phase>
 __device__ __forceinline__ void encode_slice_stats_t(const QuantArgs& a, int kb0, int kb1,
                                                      float* s_mul, int* s_e, Phase phase) {
   uint32_t* xq = reinterpret_cast<uint32_t*>(a.xq);
@@ -813,26 +813,30 @@ __device__ __forceinline__ void encode_slice_stats_t(const QuantArgs& a, int kb0
     phase(2);
     if (blockIdx.x == 0 && threadIdx.x < a.M) a.xexp[threadIdx.x] = s_e[threadIdx.x];
   };
-  encode_digits_early(sa, a.nt, a.KB, kb0, kb1, s_mul, s_e, src4,
+  encode_digits_early<BATCH>(sa, a.nt, a.KB, kb0, kb1, s_mul, s_e, src4,
                       [&](size_t wi, uint32_t v) { xq[wi] = v; }, a.tc_layout != 0, ready);
   phase(3);
 }
 
-// All CTAs of the grid (at most one wave, so all resident) meet here: the
-// last to arrive resets the arrival count and advances the generation; the
-// others wait (acquire) for the generation to change, at most 2 s of
-// %globaltimer, after which the error word is raised and they go on.
-__device__ __forceinline__ void grid_barrier(unsigned* bar, int* err) {
+// All CTAs of the grid (every dimension; at most one wave, so all resident)
+// meet here.  Thread 0 of each CTA arrives with an acquire-release add (the
+// CTA's writes before the block barrier are released with it); the last to
+// arrive resets the count and publishes the next generation (release); the
+// others poll it (acquire), at most 2 s of %globaltimer, after which the
+// error word is raised and they go on.  wait = false: arrive only (a CTA that
+// reads nothing the others wrote).
+__device__ __forceinline__ void grid_barrier(unsigned* bar, int* err, bool wait = true) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    unsigned gen;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(gen) : "l"(bar + 1) : "memory");
-    __threadfence();
-    if (atomicAdd(bar, 1u) == gridDim.x - 1) {
-      bar[0] = 0u;  // every CTA has arrived: nobody reads the count until the next use
-      __threadfence();
+    const unsigned n_cta = gridDim.x * gridDim.y * gridDim.z;
+    unsigned gen, old;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(gen) : "l"(bar + 1) : "memory");
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(bar) : "memory");
+    if (old == n_cta - 1) {
+      // every CTA has arrived: nobody reads the count until the next use
+      asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(bar) : "memory");
       asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(bar + 1), "r"(gen + 1u) : "memory");
-    } else {
+    } else if (wait) {
       unsigned long long t0;
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
       for (long long i = 0;; ++i) {
@@ -1124,6 +1128,14 @@ constexpr int kMaxSplitUnits = 16;  // units per CTA when F > 1 (ns * F <= 14)
 // griddepcontrol.wait, while the producer of its activations still runs.
 // Used by the WF_I8R variant only (large int8 matrices, where the deeper
 // stream pays; the register path is faster for small ones).
+// Ring chunks issued before the dependency wait: one (more competes with the
+// producer -- an encoder on the critical path -- for memory bandwidth, and
+// measured slower).
+#ifndef MC_RING_PREWAIT
+#define MC_RING_PREWAIT 1
+#endif
+constexpr int kRingPreWait = MC_RING_PREWAIT;
+
 template <int NT, int WF>
 struct GemvRing {
   static constexpr bool On = WF == WF_I8R;
@@ -1132,6 +1144,7 @@ struct GemvRing {
   static constexpr int KBS = 0;
   static constexpr int ChunkBytes = U * (KBW + KBS);
   static constexpr int NB = NT <= 2 ? 2 : 3;
+  static constexpr int PreWait = kRingPreWait < NB ? kRingPreWait : NB;
   static constexpr int WarpBytes = On ? NB * ChunkBytes : 0;
   static constexpr size_t Base = ((((size_t)kGemvWarps * 16 * (8 * NT + 1) +
                                     (size_t)(WF == WF_Q4 ? kMaxSplitUnits : kTileSlots) * 16 *
@@ -1144,7 +1157,12 @@ static constexpr size_t gemv_dyn_smem() {
   return GemvRing<NT, WF>::Base + (size_t)kGemvWarps * GemvRing<NT, WF>::WarpBytes;
 }
 
-template <int NT, int EPI, int WF>
+// TAIL (RESID and SWIGLU, one launch per projection): after its epilogues
+// the grid meets at a bounded barrier (the grid is at most one wave, so every
+// CTA is resident), then encodes the next projection's input -- the rows it
+// just wrote, with the statistics its epilogues folded -- exactly as k_quant
+// would (a.enc, k-blocks split over the grid), saving that launch.
+template <int NT, int EPI, int WF, bool TAIL>
 __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   constexpr int U = GemvCfg<NT>::U;
   constexpr int COLS = GemvCfg<NT>::COLS;
@@ -1232,12 +1250,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
     pk += nb;
   };
   if constexpr (RING) {
-    // only the first chunk goes out before the wait: more competes with the
-    // producer (an encoder on the critical path) for memory bandwidth
+    // the first kRingPreWait chunks go out before the wait
     if (lane == 0) {
       for (int b = 0; b < R::NB; ++b) mbar_init(&mbar[b], 1);
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-      issue(0);
+      for (int b = 0; b < R::PreWait; ++b) issue(b);
     }
     __syncwarp();
   } else if (warp < n_units) {
@@ -1289,7 +1306,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   grid_wait();
   MC_TRACE_WAITED(a.trace_slot);
   if (RING && lane == 0)
-    for (int b = 1; b < R::NB; ++b) issue(b);
+    for (int b = R::PreWait; b < R::NB; ++b) issue(b);
   // The token exponents are only needed by the epilogue: issue the load now,
   // consume it there, so its L2 round trip overlaps the first batches.
   const int xe = lane < a.M ? __ldcg(a.xexp + lane) : 0;
@@ -1453,10 +1470,23 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
       atomicMax(a.keys + key_slot(a.seq, a.m0 + threadIdx.x), sm_keys[threadIdx.x]);
   }
   if constexpr (EPI == EPI_TP) tp_publish(a.tp);
+  if constexpr (TAIL) {
+    // HBM is idle while the grid meets: warm L2 with upcoming weights
+    if (a.enc.pf && threadIdx.x == 0)
+      prefetch_share(a.enc.pf, a.enc.pf_bytes, blockIdx.x, gridDim.x);
+    __shared__ float t_mul[kMaxTokens];
+    __shared__ int t_e[kMaxTokens];
+    const int kbs = (a.enc.KB + gridDim.x - 1) / gridDim.x;
+    const int kb0 = blockIdx.x * kbs, kb1 = min(a.enc.KB, kb0 + kbs);
+    // every epilogue's rows and statistics are out; a CTA without k-blocks to
+    // encode only arrives, and leaves its SM to the next kernel
+    grid_barrier(a.bar, a.err, kb0 < kb1);
+    if (kb0 < kb1) encode_slice_stats_t<1>(a.enc, kb0, kb1, t_mul, t_e, [](int) {});
+  }
   MC_TRACE_END(a.trace_slot);
 }
 
-template <int NT, int EPI, int WF>
+template <int NT, int EPI, int WF, bool TAIL = false>
 static cudaError_t launch_gemv_t(const GemvArgs& a, int grid, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -1468,15 +1498,19 @@ static cudaError_t launch_gemv_t(const GemvArgs& a, int grid, cudaStream_t s, bo
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_gemv<NT, EPI, WF>, a);
+  return cudaLaunchKernelEx(&cfg, k_gemv<NT, EPI, WF, TAIL>, a);
 }
 
 template <int NT, int WF>
 static cudaError_t launch_gemv_nt(const GemvArgs& a, int epi, int grid, cudaStream_t s, bool pdl) {
   switch (epi) {
     case EPI_STORE: return launch_gemv_t<NT, EPI_STORE, WF>(a, grid, s, pdl);
-    case EPI_RESID: return launch_gemv_t<NT, EPI_RESID, WF>(a, grid, s, pdl);
-    case EPI_SWIGLU: return launch_gemv_t<NT, EPI_SWIGLU, WF>(a, grid, s, pdl);
+    case EPI_RESID:
+      return a.bar ? launch_gemv_t<NT, EPI_RESID, WF, true>(a, grid, s, pdl)
+                   : launch_gemv_t<NT, EPI_RESID, WF>(a, grid, s, pdl);
+    case EPI_SWIGLU:
+      return a.bar ? launch_gemv_t<NT, EPI_SWIGLU, WF, true>(a, grid, s, pdl)
+                   : launch_gemv_t<NT, EPI_SWIGLU, WF>(a, grid, s, pdl);
     case EPI_QKV: return launch_gemv_t<NT, EPI_QKV, WF>(a, grid, s, pdl);
     case EPI_LMHEAD: return launch_gemv_t<NT, EPI_LMHEAD, WF>(a, grid, s, pdl);
     case EPI_TP: return launch_gemv_t<NT, EPI_TP, WF>(a, grid, s, pdl);
@@ -1502,6 +1536,11 @@ cudaError_t launch_gemv(const GemvArgs& a, int epi, int nt, int wf, int grid, cu
   if (a.M < 1 || a.M > kGroupTokens || 8 * nt < kDigits * a.M || a.m0 < 0 ||
       a.m0 + a.M > kMaxTokens)
     return cudaErrorInvalidValue;
+  // the encoding tail: RESID / SWIGLU only, a grid the caller sized to one
+  // wave of the tail variant (gemv_blocks_per_sm(..., true)), one group
+  if (a.bar && ((epi != EPI_RESID && epi != EPI_SWIGLU) || a.m0 != 0 || a.enc.M != a.M ||
+                a.enc.KB < 1 || !a.enc.use_stats || a.enc.att_o))
+    return cudaErrorInvalidValue;
   if (wf == WF_Q4) {
     if (!a.qscale) return cudaErrorInvalidValue;
     return launch_gemv_wf<WF_Q4>(a, epi, nt, grid, s, pdl);
@@ -1510,25 +1549,27 @@ cudaError_t launch_gemv(const GemvArgs& a, int epi, int nt, int wf, int grid, cu
   return launch_gemv_wf<WF_I8>(a, epi, nt, grid, s, pdl);
 }
 
-template <int NT, int EPI, int WF>
+template <int NT, int EPI, int WF, bool TAIL = false>
 static int bps_t() {
   const size_t sm = gemv_dyn_smem<NT, WF>();
   if (sm > 48 * 1024)
-    cudaFuncSetAttribute(k_gemv<NT, EPI, WF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(k_gemv<NT, EPI, WF, TAIL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)sm);
   int n = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<NT, EPI, WF>, kGemvWarps * 32, sm);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_gemv<NT, EPI, WF, TAIL>, kGemvWarps * 32,
+                                                sm);
   return n;
 }
 
 // Occupancy of a GEMV variant; also raises its dynamic shared-memory limit,
 // so it is called once per variant outside any stream capture.
 template <int NT, int WF>
-static int bps_nt(int epi) {
+static int bps_nt(int epi, bool tail) {
   switch (epi) {
     case EPI_STORE: return bps_t<NT, EPI_STORE, WF>();
-    case EPI_RESID: return bps_t<NT, EPI_RESID, WF>();
-    case EPI_SWIGLU: return bps_t<NT, EPI_SWIGLU, WF>();
+    case EPI_RESID: return tail ? bps_t<NT, EPI_RESID, WF, true>() : bps_t<NT, EPI_RESID, WF>();
+    case EPI_SWIGLU:
+      return tail ? bps_t<NT, EPI_SWIGLU, WF, true>() : bps_t<NT, EPI_SWIGLU, WF>();
     case EPI_QKV: return bps_t<NT, EPI_QKV, WF>();
     case EPI_LMHEAD: return bps_t<NT, EPI_LMHEAD, WF>();
     case EPI_TP: return bps_t<NT, EPI_TP, WF>();
@@ -1537,19 +1578,20 @@ static int bps_nt(int epi) {
 }
 
 template <int WF>
-static int bps_wf(int epi, int nt) {
+static int bps_wf(int epi, int nt, bool tail) {
   switch (nt) {
-    case 1: return bps_nt<1, WF>(epi);
-    case 2: return bps_nt<2, WF>(epi);
-    case 3: return bps_nt<3, WF>(epi);
-    case 6: return bps_nt<6, WF>(epi);
+    case 1: return bps_nt<1, WF>(epi, tail);
+    case 2: return bps_nt<2, WF>(epi, tail);
+    case 3: return bps_nt<3, WF>(epi, tail);
+    case 6: return bps_nt<6, WF>(epi, tail);
   }
   return 0;
 }
 
-int gemv_blocks_per_sm(int epi, int nt, int wf) {
-  return wf == WF_Q4 ? bps_wf<WF_Q4>(epi, nt)
-                     : (wf == WF_I8R ? bps_wf<WF_I8R>(epi, nt) : bps_wf<WF_I8>(epi, nt));
+int gemv_blocks_per_sm(int epi, int nt, int wf, bool tail) {
+  return wf == WF_Q4 ? bps_wf<WF_Q4>(epi, nt, tail)
+                     : (wf == WF_I8R ? bps_wf<WF_I8R>(epi, nt, tail)
+                                     : bps_wf<WF_I8>(epi, nt, tail));
 }
 
 size_t gemv_ws_ints_per_stripe(int nt) { return (size_t)16 * 8 * nt; }
@@ -1660,8 +1702,8 @@ __global__ void __launch_bounds__(kQuantThreads) k_quant_att(QuantArgs a) {
   const int kbs = (a.KB + gridDim.x - 1) / gridDim.x;
   const int kb0 = blockIdx.x * kbs, kb1 = min(a.KB, kb0 + kbs);
   const int lo = kb0 * 32, hi = kb0 * 32 + max(kb1 - kb0, 0) * 32;
-  attn_combine_encode(a, lo, hi, kb0, kb1, s_bound, s_mul, s_e, s_x,
-                      reinterpret_cast<uint32_t*>(a.xq));
+  attn_combine_encode<2, kEncBatch>(a, lo, hi, kb0, kb1, blockIdx.x == 0, s_bound, s_mul, s_e,
+                                    s_x, reinterpret_cast<uint32_t*>(a.xq));
   MC_TRACE_END(a.trace_slot);
 }
 
@@ -1692,6 +1734,13 @@ cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl) {
   if (kbs_fit < 1) return cudaErrorInvalidConfiguration;
   const int need = (a.KB + kbs_fit - 1) / kbs_fit;
   ctas = ctas < need ? need : ctas;
+  if (a.att_o) {
+    // the page combine: kCombLanes lanes per 4 outputs of a token, the CTA's
+    // threads covering its k-blocks in one pass where the grid allows
+    const int lanes_per_kb = kCombLanes * 8 * a.M;
+    const int kb_per_cta = std::max(1, kQuantThreads / lanes_per_kb);
+    ctas = std::max(ctas, std::min((a.KB + kb_per_cta - 1) / kb_per_cta, 4 * kQuantMaxCtas));
+  }
   ctas = ctas > a.KB ? a.KB : ctas;
   const int kbs = (a.KB + ctas - 1) / ctas;
   cudaLaunchConfig_t cfg = {};
@@ -1720,9 +1769,9 @@ cudaError_t launch_quant(const QuantArgs& a, cudaStream_t s, bool pdl) {
 // block / blocks per sequence); its query rows are the G query heads sharing
 // the KV head times those tokens, and token i of the sequence sees positions
 // <= pos_z + i.  Scores are dot / sqrt(head_dim) (transformer.rs:959-966);
-// the softmax subtracts the row max (transformer.rs:985-1000).  Pages are
-// combined by the last CTA of each (query block, KV head) (flash-decoding
-// split).
+// the softmax subtracts the row max (transformer.rs:985-1000).  Each CTA
+// writes its page's partials (flash-decoding split); the O projection's
+// encoder combines them (k_quant_att, or the tensor-core kernel's tail).
 constexpr int kAttnThreads = 512;
 
 // The page partials are combined by the O projection's encoder (k_quant
@@ -1979,8 +2028,27 @@ __device__ __forceinline__ void mma_3xtf32(float* d, const uint32_t* ah, const u
   mma_tf32(d, ah, bh);
 }
 
-// MT: 16-row m-tiles (query rows <= 16 MT); HD: head dim (hdp)
-template <int MT, int HD>
+// The attention's encoding tail (AttnArgs::bar): the grid meets once every
+// CTA's partials and bound are out, then each CTA combines and encodes its
+// slice of the O projection's k-blocks (k-blocks split over the linear
+// block index) in `smem`, as k_quant_att does.
+__device__ __forceinline__ void attn_tail(const AttnArgs& a, float* smem) {
+  __shared__ uint32_t t_bound[kMaxTokens];
+  __shared__ float t_mul[kMaxTokens];
+  __shared__ int t_e[kMaxTokens];
+  grid_barrier(a.bar, a.err);
+  const int nb = gridDim.x * gridDim.y * gridDim.z;
+  const int b = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+  const int kbs = (a.enc.KB + nb - 1) / nb;
+  const int kb0 = b * kbs, kb1 = min(a.enc.KB, kb0 + kbs);
+  if (kb0 < kb1)
+    attn_combine_encode<2, 2>(a.enc, kb0 * 32, kb1 * 32, kb0, kb1, b == 0, t_bound, t_mul, t_e,
+                              smem, reinterpret_cast<uint32_t*>(a.enc.xq));
+}
+
+// MT: 16-row m-tiles (query rows <= 16 MT); HD: head dim (hdp); TAIL: the
+// encoding tail (MT == 1 only)
+template <int MT, int HD, bool TAIL = false>
 __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_tc(AttnArgs a) {
   constexpr int P = 64;
   constexpr int KS = HD + 4;   // K / q row stride: conflict-free fragment loads
@@ -2045,6 +2113,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_t
   const int n_chunks = (L + P - 1) / P;
   const int cslot = zb * a.Hkv + kvh;
   if (chunk >= n_chunks) {
+    if constexpr (TAIL) attn_tail(a, asmem);
     MC_TRACE_END(a.trace_slot);
     return;
   }
@@ -2257,6 +2326,7 @@ __global__ void __launch_bounds__(kAttnTcThreads, MT == 1 ? 2 : 1) k_attention_t
   __syncthreads();
   publish_bound(a, s_mx, mt0, Mq);
   MC_TRACE_PHASE(a.trace_slot, 4, mc_tp);
+  if constexpr (TAIL) attn_tail(a, asmem);
   MC_TRACE_END(a.trace_slot);
 }
 
@@ -2289,7 +2359,7 @@ int attention_qblk(int G, int seq_len) {
 
 static int g_attn_tc_smem = 48 * 1024;  // tensor-core attention dynamic smem limit set so far
 
-template <int MT, int HD>
+template <int MT, int HD, bool TAIL = false>
 static cudaError_t launch_attention_tc(const AttnArgs& a, dim3 grid, cudaStream_t s, bool pdl) {
   const size_t smem = attention_tc_smem_bytes(MT, HD);
   if (smem > (size_t)g_attn_tc_smem) return cudaErrorInvalidConfiguration;
@@ -2303,12 +2373,16 @@ static cudaError_t launch_attention_tc(const AttnArgs& a, dim3 grid, cudaStream_
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k_attention_tc<MT, HD>, a);
+  return cudaLaunchKernelEx(&cfg, k_attention_tc<MT, HD, TAIL>, a);
 }
 
 template <int HD>
 static cudaError_t launch_attention_tc_hd(const AttnArgs& a, int R, dim3 grid, cudaStream_t s,
                                           bool pdl) {
+  if (a.bar) {  // the caller checked attention_tail_fits
+    if (R > 16) return cudaErrorInvalidValue;
+    return launch_attention_tc<1, HD, true>(a, grid, s, pdl);
+  }
   if (R <= 16) return launch_attention_tc<1, HD>(a, grid, s, pdl);
   if (R <= 32) return launch_attention_tc<2, HD>(a, grid, s, pdl);
   return launch_attention_tc<4, HD>(a, grid, s, pdl);
@@ -2320,6 +2394,7 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     return cudaErrorInvalidValue;
   const int n_seq = a.M / a.seq.seq_len;
   const int n_qb = (a.seq.seq_len + a.qblk - 1) / a.qblk;
+  if (a.bar && !attention_tail_fits(a, 0)) return cudaErrorInvalidValue;
   // tensor-core kernel: up to 64 query rows per block, head dims 32 / 64 / 128
   // (the block size depends only on the model, so every forward of a model
   // takes the same kernel)
@@ -2373,14 +2448,46 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
 }
 
 // Raise the dynamic shared-memory limit once, outside any stream capture.
+// CTAs of the tail variant k_attention_tc<1, HD, true> resident per SM
+// (index 0/1/2: HD 32/64/128), settled by prepare_kernels.
+static int g_attn_tail_bps[3] = {0, 0, 0};
+
 template <int HD>
 static cudaError_t prepare_attention_tc_hd() {
-  for (auto f : {k_attention_tc<1, HD>, k_attention_tc<2, HD>, k_attention_tc<4, HD>}) {
+  for (auto f : {k_attention_tc<1, HD>, k_attention_tc<2, HD>, k_attention_tc<4, HD>,
+                 k_attention_tc<1, HD, true>}) {
     cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)attention_tc_smem_bytes(4, 128));
     if (e != cudaSuccess) return e;
   }
+  int n = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+      &n, k_attention_tc<1, HD, true>, kAttnTcThreads, attention_tc_smem_bytes(1, HD));
+  if (e != cudaSuccess) return e;
+  g_attn_tail_bps[HD == 32 ? 0 : (HD == 64 ? 1 : 2)] = n;
   return cudaSuccess;
+}
+
+bool attention_tail_fits(const AttnArgs& a, int nsm) {
+  static int n_sm = 0;
+  if (!n_sm) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+  }
+  if (nsm <= 0) nsm = n_sm;
+  const int G = a.H / std::max(a.Hkv, 1);
+  if (a.page != 64 || a.max_chunks > 64 || G * a.qblk > 16 || a.seq.seq_len < 1 ||
+      a.M % a.seq.seq_len || a.qblk < 1 || !a.enc.att_o || a.enc.KB < 1 || a.enc.M != a.M)
+    return false;
+  if (a.hdp != 32 && a.hdp != 64 && a.hdp != 128) return false;
+  const int bps = g_attn_tail_bps[a.hdp == 32 ? 0 : (a.hdp == 64 ? 1 : 2)];
+  const long long n_qb = (a.seq.seq_len + a.qblk - 1) / a.qblk;
+  const long long grid = (long long)a.Hkv * a.max_chunks * (a.M / a.seq.seq_len) * n_qb;
+  if (bps < 1 || grid > (long long)nsm * bps) return false;
+  const long long kbs = (a.enc.KB + grid - 1) / grid;
+  return (long long)a.M * kbs * 32 * (long long)sizeof(float) <=
+         (long long)attention_tc_smem_bytes(1, a.hdp);
 }
 
 cudaError_t prepare_kernels(size_t quant_smem, size_t attn_smem) {

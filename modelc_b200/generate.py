@@ -27,6 +27,13 @@ class GenerationConfig:
     accept_mode: int = 0  # temperature > 0: 0 = min(1, p/q), 1 = sample == draft
     top_p: float = 0.0    # temperature > 0: applied when in (0, 1) (generate.rs:961-963)
     min_p: float = 0.0    # temperature > 0: applied when in (0, 1) (generate.rs:964-966)
+    max_context: int = 0  # the context shift's threshold (None = 0)
+    anchor_tokens: int = 0
+    use_int8_kv: bool = False
+
+
+# target KV variants (make_kv_cache, generate.rs:17-24)
+KV_FP32, KV_INT8, KV_MIXED = 0, 1, 2
 
 
 def _u32(a) -> np.ndarray:
@@ -41,18 +48,24 @@ class Session:
 
     Mirrors the reference's per-request ``Option<KvCache>`` (generate.rs:
     617-627) plus the draft model's cache; a batched session decodes its
-    requests in lock step, each exactly as it would decode alone."""
+    requests in lock step, each exactly as it would decode alone.
+    ``max_context`` is the KV capacity; ``shift_context`` / ``anchor_tokens``
+    are GenerationConfig::max_context / anchor_tokens (the context shift,
+    generate.rs:26-63); ``kv_mode`` the target cache variant (KV_FP32 or
+    KV_INT8)."""
 
     def __init__(self, target: Weights, draft=None, gamma: int = 4,
                  max_context: int = 2048, bonus: bool = False, temperature: float = 0.0,
                  seed: int = 0, accept_mode: int = 0, n_requests: int = 1,
-                 top_p: float = 0.0, min_p: float = 0.0):
+                 top_p: float = 0.0, min_p: float = 0.0, shift_context: int = 0,
+                 anchor_tokens: int = 0, kv_mode: int = KV_FP32):
         self.target, self.draft = target, draft
         self.gamma = gamma
         self.n_requests = n_requests
         self._cancel = C.c_int32(0)
         cfg = _lib.SpecCfg(gamma, max_context, int(bonus), temperature, seed,
-                           C.pointer(self._cancel), accept_mode, n_requests, top_p, min_p)
+                           C.pointer(self._cancel), accept_mode, n_requests, top_p, min_p,
+                           shift_context, anchor_tokens, kv_mode)
         h = C.c_void_p()
         if isinstance(draft, MlpDraftModel):  # MlpDraftModel drives the rounds
             check(lib().mc_session_create_mlp(target.handle, draft.handle, C.byref(cfg),
@@ -131,6 +144,17 @@ class Session:
     def prime(self, prompt):
         p = _u32(prompt)
         check(lib().mc_spec_prime(self.handle, p.ctypes.data_as(C.POINTER(C.c_uint32)), len(p)))
+
+    def prime_cached(self, snapshot: "KvSnapshot", prompt):
+        """prime() for a prompt that starts with the snapshot's tokens: their
+        K/V are restored, the rest forwarded (generate.rs:617-636)."""
+        p = _u32(prompt)
+        check(lib().mc_spec_prime_cached(self.handle, snapshot.handle,
+                                         p.ctypes.data_as(C.POINTER(C.c_uint32)), len(p)))
+
+    def snapshot(self, request: int = 0) -> "KvSnapshot":
+        """The request's context tokens and target K/V as they stand."""
+        return KvSnapshot(self, request)
 
     def prime_batch(self, prompts):
         """Prime one prompt per request (n_requests of them)."""
@@ -304,13 +328,91 @@ class NgramDraftModel:
             pass
 
 
+class KvSnapshot:
+    """A device copy of one request's context tokens and target K/V
+    (CachedPrefix, prefix_cache.rs:14-24; last_logits are not kept)."""
+
+    def __init__(self, session: Session, request: int = 0):
+        h = C.c_void_p()
+        check(lib().mc_kv_snapshot_take(session.handle, request, C.byref(h)))
+        self.handle = h
+        n = lib().mc_kv_snapshot_tokens(h, None, 0)
+        out = np.zeros(max(n, 1), np.uint32)
+        lib().mc_kv_snapshot_tokens(h, out.ctypes.data_as(C.POINTER(C.c_uint32)), n)
+        self.tokens = out[:n].tolist()
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().mc_kv_snapshot_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+@dataclass
+class CacheLookup:
+    """prefix_cache.rs:26-37: tokens covered by the match and the entry."""
+    matched_len: int
+    kv: object
+
+
+class PrefixCache:
+    """Bounded LRU cache of prompt-prefix K/V snapshots (prefix_cache.rs:
+    39-110): ``lookup`` returns the longest cached sequence that is a prefix
+    of the query (ties: the most recently used entry), ``insert`` puts an
+    entry first (replacing an equal key) and evicts from the tail beyond
+    ``max_entries`` (at least 1).  Values are any objects -- KvSnapshot in a
+    serving loop -- and are closed when evicted if they have ``close``."""
+
+    def __init__(self, max_entries: int):
+        self.entries: list[tuple[tuple[int, ...], object]] = []
+        self.max_entries = max(max_entries, 1)
+
+    def lookup(self, tokens) -> CacheLookup | None:
+        t = tuple(int(x) for x in tokens)
+        best = None
+        for seq, kv in self.entries:  # most recently used first
+            if t[:len(seq)] == seq and (best is None or len(seq) > len(best[0])):
+                best = (seq, kv)
+        return None if best is None else CacheLookup(len(best[0]), best[1])
+
+    def insert(self, tokens, kv):
+        key = tuple(int(x) for x in tokens)
+        for i, (seq, old) in enumerate(self.entries):
+            if seq == key:
+                del self.entries[i]
+                if old is not kv and hasattr(old, "close"):
+                    old.close()
+                break
+        self.entries.insert(0, (key, kv))
+        while len(self.entries) > self.max_entries:
+            _, old = self.entries.pop()
+            if hasattr(old, "close"):
+                old.close()
+
+    def __len__(self):
+        return len(self.entries)
+
+    def is_empty(self) -> bool:
+        return not self.entries
+
+    def capacity(self) -> int:
+        return self.max_entries
+
+
 def speculative_generate(target: Weights, draft: Weights, prompt, config: GenerationConfig,
                          max_context: int | None = None):
     """generate.rs:598-767 with a transformer draft; returns (ids, accepted)."""
     cap = max_context or (len(prompt) + config.max_tokens + config.gamma + 8)
     s = Session(target, draft, gamma=config.gamma, max_context=cap, bonus=config.bonus,
                 temperature=config.temperature, seed=config.seed,
-                accept_mode=config.accept_mode, top_p=config.top_p, min_p=config.min_p)
+                accept_mode=config.accept_mode, top_p=config.top_p, min_p=config.min_p,
+                shift_context=config.max_context, anchor_tokens=config.anchor_tokens,
+                kv_mode=KV_INT8 if config.use_int8_kv else KV_FP32)
     try:
         return s.speculative_generate(prompt, config.max_tokens)
     finally:

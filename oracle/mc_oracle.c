@@ -533,7 +533,123 @@ void oracle_kv_free(oracle_kv* kv) {
  * only front eviction (transformer.rs:424-583); its sequential verify never
  * forwards a rejected draft, and truncation reproduces exactly that state. */
 void oracle_kv_truncate(oracle_kv* kv, int len) {
-  if (len < kv->len) kv->len = len < 0 ? 0 : len;
+  if (len < kv->len) {
+    if (len < 0) len = 0;
+    if (kv->mode == ORACLE_KV_MIXED) {
+      kv->hot -= kv->len - len;
+      if (kv->hot < 0) kv->hot = 0;
+    }
+    kv->len = len;
+  }
+}
+
+/* make_kv_cache (generate.rs:17-24): the KvLayer variant of every layer;
+ * MIXED keeps `window` tokens in f32 (the reference passes 64). */
+void oracle_kv_set_mode(oracle_kv* kv, int mode, int window) {
+  kv->mode = mode;
+  kv->window = window;
+  kv->hot = 0;
+}
+
+/* transformer.rs:196-206 quantize_scale + quantize, then the dequantization
+ * k_all()/v_all() apply (q as f32 * scale, :287-297): x becomes the values
+ * an int8 layer returns for it.  scale = max|x| / 127 (1 when the max is 0);
+ * q = round(x / scale) (halves away from zero) clamped to +-127, and a NaN
+ * quotient casts to 0 (Rust's saturating `as i8`).  f32::max ignores NaN, as
+ * fmaxf does. */
+void oracle_kv_qdq(float* x, int n) {
+  float mx = 0.0f;
+  for (int i = 0; i < n; ++i) mx = fmaxf(mx, fabsf(x[i]));
+  const float scale = mx > 0.0f ? mx / 127.0f : 1.0f;
+  for (int i = 0; i < n; ++i) {
+    const float r = roundf(x[i] / scale);
+    const float q = isnan(r) ? 0.0f : (r < -127.0f ? -127.0f : (r > 127.0f ? 127.0f : r));
+    x[i] = q * scale;
+  }
+}
+
+/* One position's K and V in every layer through oracle_kv_qdq. */
+static void kv_qdq_pos(oracle_kv* kv, int pos) {
+  for (int l = 0; l < kv->n_layers; ++l) {
+    const size_t off = ((size_t)l * kv->cap + (size_t)pos) * kv->kv_dim;
+    oracle_kv_qdq(kv->k + off, kv->kv_dim);
+    oracle_kv_qdq(kv->v + off, kv->kv_dim);
+  }
+}
+
+/* Positions [from + n, len) move to [from, len - n) in every layer. */
+static void kv_remove(oracle_kv* kv, int from, int n) {
+  const size_t row = (size_t)kv->kv_dim;
+  const int tail = kv->len - from - n;
+  for (int l = 0; l < kv->n_layers; ++l) {
+    float* k = kv->k + (size_t)l * kv->cap * row;
+    float* v = kv->v + (size_t)l * kv->cap * row;
+    if (tail > 0) {
+      memmove(k + (size_t)from * row, k + (size_t)(from + n) * row, sizeof(float) * (size_t)tail * row);
+      memmove(v + (size_t)from * row, v + (size_t)(from + n) * row, sizeof(float) * (size_t)tail * row);
+    }
+  }
+  kv->len -= n;
+}
+
+/* KvCache::shift_anchored -> KvLayer::shift_anchored (transformer.rs:495-583),
+ * which falls back to KvLayer::shift (:427-493) when anchor is 0, n is 0,
+ * n >= len or len - n <= anchor.  shift drops the oldest min(n, len) tokens
+ * (a MIXED layer from its cold tokens first).  The anchored form keeps the
+ * first `anchor` tokens, drops the next n and re-appends the kept ones to a
+ * cleared layer: an INT8 layer re-quantizes every kept token from its
+ * dequantized values, a MIXED layer re-quantizes all but the last `window`
+ * (they reach the cold part again), an FP32 layer is unchanged. */
+void oracle_kv_shift(oracle_kv* kv, int n, int anchor) {
+  const int len = kv->len;
+  if (anchor == 0 || n == 0 || n >= len || len - n <= anchor) {
+    const int remove = n < len ? n : len;
+    if (kv->mode == ORACLE_KV_MIXED) {
+      const int cold = len - kv->hot;
+      if (remove > cold) kv->hot -= remove - cold;
+    }
+    kv_remove(kv, 0, remove);
+    return;
+  }
+  const int keep = len - n;
+  kv_remove(kv, anchor, n);
+  if (kv->mode == ORACLE_KV_INT8) {
+    for (int p = 0; p < keep; ++p) kv_qdq_pos(kv, p);
+  } else if (kv->mode == ORACLE_KV_MIXED) {
+    for (int p = 0; p + kv->window < keep; ++p) kv_qdq_pos(kv, p);
+    kv->hot = keep < kv->window ? keep : kv->window;
+  }
+}
+
+/* generate.rs:26-63 context_shift: with overflow = len - max_ctx + max_ctx/4,
+ * either the anchored eviction (anchor > 0 and len > anchor + overflow: the
+ * tokens [anchor, anchor + overflow) leave the list and the cache) or the
+ * oldest `overflow` tokens leave.  prompt_len shrinks by the prompt tokens
+ * removed.  *removed_at: where the removed range started.  Returns overflow. */
+int oracle_context_shift(uint32_t* tok, int* len, int* prompt_len, oracle_kv* kv, int max_ctx,
+                         int anchor, int* removed_at) {
+  const int L = *len;
+  const int overflow = L - max_ctx + max_ctx / 4;
+  if (anchor > 0 && overflow > 0 && L > anchor + overflow) {
+    if (kv) oracle_kv_shift(kv, overflow, anchor);
+    const int suffix_start = anchor + overflow, suffix_len = L - suffix_start;
+    memmove(tok + anchor, tok + suffix_start, sizeof(uint32_t) * (size_t)suffix_len);
+    *len = anchor + suffix_len;
+    if (*prompt_len > anchor) {
+      const int non_anchor = *prompt_len - anchor;
+      const int removed = overflow < non_anchor ? overflow : non_anchor;
+      *prompt_len = anchor + non_anchor - removed;
+    }
+    if (removed_at) *removed_at = anchor;
+  } else {
+    if (kv) oracle_kv_shift(kv, overflow, 0);
+    const int new_len = L - overflow;
+    memmove(tok, tok + overflow, sizeof(uint32_t) * (size_t)new_len);
+    *len = new_len;
+    *prompt_len = *prompt_len > overflow ? *prompt_len - overflow : 0;
+    if (removed_at) *removed_at = 0;
+  }
+  return overflow;
 }
 
 int oracle_kv_len(const oracle_kv* kv) { return kv ? kv->len : 0; }
@@ -573,6 +689,12 @@ int oracle_forward(const oracle_model* m, const float* input, oracle_kv* kv,
   float* u = (float*)malloc(sizeof(float) * (size_t)(f > 0 ? f : 1));
   memcpy(h, input, sizeof(float) * (size_t)d);
   int pos = kv ? kv->len : 0;
+  /* KvLayer::append (transformer.rs:348-420): an INT8 layer quantizes the
+   * new token; a MIXED layer whose hot part would exceed its window moves
+   * the oldest hot token to the cold part (quantized) */
+  const int stored = kv && pos < kv->cap;
+  const int cold = (stored && kv->mode == ORACLE_KV_MIXED && kv->hot + 1 > kv->window)
+                       ? pos - kv->window : -1;
 
   for (int l = 0; l < m->n_layers; ++l) {
     const oracle_layer* L = &m->layers[l];
@@ -593,6 +715,13 @@ int oracle_forward(const oracle_model* m, const float* input, oracle_kv* kv,
         float* vl = kv->v + ((size_t)l * kv->cap) * kvd;
         memcpy(kl + (size_t)pos * kvd, k, sizeof(float) * (size_t)kvd);
         memcpy(vl + (size_t)pos * kvd, v, sizeof(float) * (size_t)kvd);
+        if (kv->mode == ORACLE_KV_INT8) {
+          oracle_kv_qdq(kl + (size_t)pos * kvd, kvd);
+          oracle_kv_qdq(vl + (size_t)pos * kvd, kvd);
+        } else if (cold >= 0) {
+          oracle_kv_qdq(kl + (size_t)cold * kvd, kvd);
+          oracle_kv_qdq(vl + (size_t)cold * kvd, kvd);
+        }
         k_all = kl;
         v_all = vl;
         seq = pos + 1;
@@ -615,7 +744,10 @@ int oracle_forward(const oracle_model* m, const float* input, oracle_kv* kv,
       oracle_add(h, d, tmp, d, h);
     }
   }
-  if (kv && pos < kv->cap) kv->len = pos + 1;
+  if (stored) {
+    kv->len = pos + 1;
+    if (kv->mode == ORACLE_KV_MIXED && kv->hot < kv->window) kv->hot++;
+  }
 
   if (m->final_norm) oracle_rms_norm(h, d, m->final_norm, d, m->eps, h);
   int have = 0;
@@ -702,6 +834,18 @@ int oracle_llama_draft_run(oracle_llama_draft* d, const uint32_t* ctx, int n,
     if (j + 1 < gamma) draft_step(d, out[j]);
   }
   return gamma;
+}
+
+/* The transformer draft's side of a context shift (the reference has no
+ * transformer drafter; this is the definition the device follows): the
+ * positions [at, at + n) leave its cache and its token list, so both keep
+ * matching the shifted context. */
+void oracle_llama_draft_shift(oracle_llama_draft* d, int at, int n) {
+  const int len = d->kv->len;
+  if (len <= at || n <= 0) return;
+  const int rm = len - at < n ? len - at : n;
+  kv_remove(d->kv, at, rm);
+  memmove(d->cached + at, d->cached + at + rm, sizeof(uint32_t) * (size_t)(len - at - rm));
 }
 
 /* draft.rs:91-147 MlpDraftModel::{forward, draft}: embed -> FC1+ReLU -> FC2
@@ -830,6 +974,9 @@ int oracle_ngram_draft(const uint32_t* tokens, int n_tokens,
 
 /* ======================= generation ======================= */
 
+/* generate.rs:19: KvCache::new_mixed(n_layers, hidden, 64) */
+static const int kMixedWindow = 64;
+
 static int is_cancelled(const oracle_gen_cfg* cfg) {
   return cfg->cancel && *cfg->cancel;
 }
@@ -883,14 +1030,43 @@ int oracle_speculative_generate(const oracle_model* m, int draft_kind,
                                 int n_prompt, const oracle_gen_cfg* cfg,
                                 uint32_t* out, int cap, int* accepted,
                                 int* n_rounds, int rounds_cap) {
+  return oracle_speculative_generate_kv(m, draft_kind, drafter, prompt, n_prompt, cfg, out, cap,
+                                        accepted, n_rounds, rounds_cap, NULL, 0);
+}
+
+/* speculative_generate with a CacheLookup (generate.rs:617-636): kv_io
+ * (when not NULL) holds the K/V of the first matched_len prompt tokens and
+ * receives the cache the run ends with (the KvCache speculative_generate
+ * returns); only prompt tokens [matched_len, n_prompt) are primed. */
+int oracle_speculative_generate_kv(const oracle_model* m, int draft_kind,
+                                   void* drafter, const uint32_t* prompt,
+                                   int n_prompt, const oracle_gen_cfg* cfg,
+                                   uint32_t* out, int cap, int* accepted,
+                                   int* n_rounds, int rounds_cap, oracle_kv* kv_io,
+                                   int matched_len) {
   if (n_rounds) *n_rounds = 0;
   if (n_prompt <= 0) return 0;
   int gamma = cfg->gamma;
-  int tcap = n_prompt + cfg->max_tokens + gamma + 2;
+  int tcap = (n_prompt > cfg->max_context ? n_prompt : cfg->max_context) + cfg->max_tokens +
+             gamma + 2;
   uint32_t* tok = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)tcap);
   memcpy(tok, prompt, sizeof(uint32_t) * (size_t)n_prompt);
   int len = n_prompt, prompt_len = n_prompt;
-  oracle_kv* kv = oracle_kv_new(m->n_layers, m->n_kv_heads * m->head_dim, tcap + 1);
+  oracle_kv* kv = kv_io;
+  if (!kv) {
+    kv = oracle_kv_new(m->n_layers, m->n_kv_heads * m->head_dim, tcap + 1);
+    oracle_kv_set_mode(kv, cfg->kv_mode, kMixedWindow);
+    matched_len = 0;
+  }
+  /* generate.rs:671-681, :738-748: the context shift after a step or a round */
+  #define SHIFT_CONTEXT()                                                                  \
+    if (cfg->max_context > 0 && len > cfg->max_context) {                                 \
+      int at_ = 0;                                                                         \
+      const int ov_ = oracle_context_shift(tok, &len, &prompt_len, kv, cfg->max_context,   \
+                                           cfg->anchor_tokens, &at_);                      \
+      if (draft_kind == ORACLE_DRAFT_LLAMA)                                                \
+        oracle_llama_draft_shift((oracle_llama_draft*)drafter, at_, ov_);                  \
+    }
   float* logits = (float*)malloc(sizeof(float) * (size_t)m->vocab);
   float* e = (float*)malloc(sizeof(float) * (size_t)m->hidden);
   uint32_t* draft = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)(gamma + 1));
@@ -898,7 +1074,7 @@ int oracle_speculative_generate(const oracle_model* m, int draft_kind,
   ix.n = 3;
   ngram_build(&ix, tok, len);
 
-  for (int i = 0; i < n_prompt; ++i) {
+  for (int i = matched_len; i < n_prompt; ++i) {
     oracle_token_embedding(m, prompt[i], e);
     oracle_forward(m, e, kv, logits);
   }
@@ -921,6 +1097,7 @@ int oracle_speculative_generate(const oracle_model* m, int draft_kind,
                                     (uint64_t)(len - prompt_len), cfg->seed);
       tok[len++] = next;
       ngram_update(&ix, tok, len);
+      SHIFT_CONTEXT()
       if (cfg->tok_vocab > 0 && (int)next >= cfg->tok_vocab) break;
       continue;
     }
@@ -954,6 +1131,7 @@ int oracle_speculative_generate(const oracle_model* m, int draft_kind,
     if (accepted && rounds < rounds_cap) accepted[rounds] = acc;
     rounds++;
     ngram_update(&ix, tok, len);
+    SHIFT_CONTEXT()
     if (len - prompt_len >= cfg->max_tokens) break;
     if (acc < nd && cfg->tok_vocab > 0 && (int)tok[len - 1] >= cfg->tok_vocab)
       break;
@@ -962,10 +1140,11 @@ int oracle_speculative_generate(const oracle_model* m, int draft_kind,
   int ncopy = gen < cap ? gen : cap;
   memcpy(out, tok + prompt_len, sizeof(uint32_t) * (size_t)ncopy);
   if (n_rounds) *n_rounds = rounds;
-  oracle_kv_free(kv);
+  if (kv != kv_io) oracle_kv_free(kv);
   free(logits); free(e); free(draft); free(tok);
   free(ix.keys); free(ix.next);
   return ncopy;
+  #undef SHIFT_CONTEXT
 }
 
 /* ---------------- stochastic speculative sampling ----------------

@@ -102,10 +102,20 @@ typedef struct {
   int n_threads;           /* 1 = reference-faithful sequential linear */
 } oracle_model;
 
+/* KvLayer variants (transformer.rs:167-193).  The cache holds f32 values
+ * as k_all()/v_all() return them: INT8 tokens and MIXED cold tokens hold
+ * their dequantized int8 codes (q * scale). */
+#define ORACLE_KV_FP32 0
+#define ORACLE_KV_INT8 1
+#define ORACLE_KV_MIXED 2
+
 typedef struct {
   int n_layers, kv_dim, len, cap;
   float* k; /* [n_layers][cap][kv_dim] */
   float* v;
+  int mode;   /* ORACLE_KV_* */
+  int window; /* MIXED: f32 ("hot") tokens kept */
+  int hot;    /* MIXED: tokens now in the hot window (the last `hot` positions) */
 } oracle_kv;
 
 int oracle_model_resolve(oracle_model* m);
@@ -113,6 +123,11 @@ oracle_kv* oracle_kv_new(int n_layers, int kv_dim, int cap);
 void oracle_kv_free(oracle_kv* kv);
 void oracle_kv_truncate(oracle_kv* kv, int len);
 int oracle_kv_len(const oracle_kv* kv);
+void oracle_kv_set_mode(oracle_kv* kv, int mode, int window);
+void oracle_kv_qdq(float* x, int n);
+void oracle_kv_shift(oracle_kv* kv, int n, int anchor);
+int oracle_context_shift(uint32_t* tok, int* len, int* prompt_len, oracle_kv* kv, int max_ctx,
+                         int anchor, int* removed_at);
 
 void oracle_token_embedding(const oracle_model* m, uint32_t id, float* out);
 int oracle_forward(const oracle_model* m, const float* input, oracle_kv* kv,
@@ -137,6 +152,7 @@ oracle_llama_draft* oracle_llama_draft_new(const oracle_model* m, int cap);
 void oracle_llama_draft_free(oracle_llama_draft* d);
 int oracle_llama_draft_run(oracle_llama_draft* d, const uint32_t* ctx, int n,
                        int gamma, uint32_t* out);
+void oracle_llama_draft_shift(oracle_llama_draft* d, int at, int n);
 int oracle_mlp_draft_run(const oracle_mlp_draft* d, const uint32_t* ctx, int n,
                          int gamma, uint32_t* out);
 int oracle_ngram_draft(const uint32_t* tokens, int n_tokens,
@@ -152,6 +168,9 @@ typedef struct {
   int tok_vocab;   /* tokenizer vocab for the OOV stop; 0 disables */
   int bonus;       /* 0: reference verify (k forwards, no bonus); 1: k+1 */
   volatile int* cancel;
+  int max_context;   /* GenerationConfig::max_context (0 = None) */
+  int anchor_tokens; /* GenerationConfig::anchor_tokens */
+  int kv_mode;       /* ORACLE_KV_*: use_int8_kv / use_mixed_kv (window 64) */
 } oracle_gen_cfg;
 
 int oracle_generate_core(const oracle_model* m, const uint32_t* prompt,
@@ -162,6 +181,12 @@ int oracle_speculative_generate(const oracle_model* m, int draft_kind,
                                 int n_prompt, const oracle_gen_cfg* cfg,
                                 uint32_t* out, int cap, int* accepted,
                                 int* n_rounds, int rounds_cap);
+int oracle_speculative_generate_kv(const oracle_model* m, int draft_kind,
+                                   void* drafter, const uint32_t* prompt,
+                                   int n_prompt, const oracle_gen_cfg* cfg,
+                                   uint32_t* out, int cap, int* accepted,
+                                   int* n_rounds, int rounds_cap, oracle_kv* kv_io,
+                                   int matched_len);
 
 /* ---------------- stochastic speculative sampling (not in the reference) */
 void oracle_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]);

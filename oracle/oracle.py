@@ -42,7 +42,11 @@ class Model(C.Structure):
 
 class KV(C.Structure):
     _fields_ = [("n_layers", C.c_int), ("kv_dim", C.c_int), ("len", C.c_int),
-                ("cap", C.c_int), ("k", _fp), ("v", _fp)]
+                ("cap", C.c_int), ("k", _fp), ("v", _fp), ("mode", C.c_int),
+                ("window", C.c_int), ("hot", C.c_int)]
+
+
+KV_FP32, KV_INT8, KV_MIXED = 0, 1, 2  # KvLayer variants (transformer.rs:167-193)
 
 
 class MlpDraft(C.Structure):
@@ -56,7 +60,8 @@ class GenCfg(C.Structure):
     _fields_ = [("max_tokens", C.c_int), ("temperature", C.c_float),
                 ("top_p", C.c_float), ("min_p", C.c_float), ("gamma", C.c_int),
                 ("seed", C.c_uint64), ("tok_vocab", C.c_int),
-                ("bonus", C.c_int), ("cancel", C.POINTER(C.c_int))]
+                ("bonus", C.c_int), ("cancel", C.POINTER(C.c_int)),
+                ("max_context", C.c_int), ("anchor_tokens", C.c_int), ("kv_mode", C.c_int)]
 
 
 def build() -> str:
@@ -93,6 +98,13 @@ def lib():
         L.oracle_kv_free.argtypes = [C.POINTER(KV)]
         L.oracle_kv_truncate.argtypes = [C.POINTER(KV), C.c_int]
         L.oracle_kv_len.argtypes = [C.POINTER(KV)]
+        L.oracle_kv_set_mode.argtypes = [C.POINTER(KV), C.c_int, C.c_int]
+        L.oracle_kv_qdq.argtypes = [_fp, C.c_int]
+        L.oracle_kv_shift.argtypes = [C.POINTER(KV), C.c_int, C.c_int]
+        L.oracle_context_shift.restype = C.c_int
+        L.oracle_context_shift.argtypes = [_u32p, C.POINTER(C.c_int), C.POINTER(C.c_int),
+                                           C.POINTER(KV), C.c_int, C.c_int,
+                                           C.POINTER(C.c_int)]
         L.oracle_model_resolve.argtypes = [C.POINTER(Model)]
         L.oracle_forward.argtypes = [C.POINTER(Model), _fp, C.POINTER(KV), _fp]
         L.oracle_forward_ids.argtypes = [C.POINTER(Model), _u32p, C.c_int,
@@ -111,6 +123,10 @@ def lib():
             C.POINTER(Model), C.c_int, C.c_void_p, _u32p, C.c_int,
             C.POINTER(GenCfg), _u32p, C.c_int, C.POINTER(C.c_int),
             C.POINTER(C.c_int), C.c_int]
+        L.oracle_speculative_generate_kv.argtypes = [
+            C.POINTER(Model), C.c_int, C.c_void_p, _u32p, C.c_int,
+            C.POINTER(GenCfg), _u32p, C.c_int, C.POINTER(C.c_int),
+            C.POINTER(C.c_int), C.c_int, C.POINTER(KV), C.c_int]
         L.oracle_philox4x32_10.argtypes = [_u32p, _u32p, _u32p]
         L.oracle_philox_uniform.restype = C.c_float
         L.oracle_philox_uniform.argtypes = [C.c_uint64, C.c_uint32, C.c_uint32]
@@ -358,9 +374,10 @@ class OracleModel:
                                     kv.ptr if kv is not None else None, fptr(out))
         return out if have else None
 
-    def _cfg(self, max_tokens, temperature, gamma, seed, top_p, min_p, tok_vocab, bonus):
+    def _cfg(self, max_tokens, temperature, gamma, seed, top_p, min_p, tok_vocab, bonus,
+             max_context=0, anchor_tokens=0, kv_mode=KV_FP32):
         return GenCfg(max_tokens, temperature, top_p, min_p, gamma, seed, tok_vocab,
-                      bonus, None)
+                      bonus, None, max_context, anchor_tokens, kv_mode)
 
     def generate_core(self, prompt, max_tokens, temperature=0.0, seed=0,
                       top_p=0.0, min_p=0.0, tok_vocab=0):
@@ -373,23 +390,31 @@ class OracleModel:
 
     def speculative_generate(self, prompt, max_tokens, gamma, draft=None,
                              temperature=0.0, seed=0, top_p=0.0, min_p=0.0,
-                             tok_vocab=0, bonus=False):
-        """Returns (tokens, accepted-per-round)."""
+                             tok_vocab=0, bonus=False, max_context=0, anchor_tokens=0,
+                             kv_mode=KV_FP32, rounds_cap=None, kv=None, matched_len=0):
+        """Returns (tokens, accepted-per-round).  max_context / anchor_tokens:
+        the context shift (0: none); kv_mode: KV_FP32, KV_INT8 or KV_MIXED.
+        kv (an OracleKV, its mode set): the cache holding the first
+        matched_len prompt tokens' K/V (a prefix-cache hit), which ends the
+        run holding the final cache."""
         prompt = np.ascontiguousarray(np.asarray(prompt, np.uint32))
         cfg = self._cfg(max_tokens, temperature, gamma, seed, top_p, min_p,
-                        tok_vocab, int(bonus))
+                        tok_vocab, int(bonus), max_context, anchor_tokens, kv_mode)
         cap = max_tokens + gamma + 2
         out = np.zeros(cap, np.uint32)
-        acc = (C.c_int * (cap + 1))()
+        rounds_cap = rounds_cap or cap + 1
+        acc = (C.c_int * rounds_cap)()
         nr = C.c_int()
         if draft is None:
             kind, ptr = DRAFT_NGRAM, None
         else:
             kind, ptr = draft.kind, draft.handle
-        n = lib().oracle_speculative_generate(C.byref(self.m), kind, ptr, u32ptr(prompt),
-                                              len(prompt), C.byref(cfg), u32ptr(out), cap,
-                                              acc, C.byref(nr), cap + 1)
-        return out[:n].tolist(), [acc[i] for i in range(min(nr.value, cap + 1))]
+        n = lib().oracle_speculative_generate_kv(C.byref(self.m), kind, ptr, u32ptr(prompt),
+                                                 len(prompt), C.byref(cfg), u32ptr(out), cap,
+                                                 acc, C.byref(nr), rounds_cap,
+                                                 kv.ptr if kv is not None else None,
+                                                 matched_len)
+        return out[:n].tolist(), [acc[i] for i in range(min(nr.value, rounds_cap))]
 
 
     def speculative_sample(self, prompt, max_tokens, gamma, draft, temperature, seed,
@@ -433,6 +458,25 @@ def filtered_weights(logits, temperature, top_p=0.0, min_p=0.0):
     return w, float(s)
 
 
+def kv_qdq(x):
+    """A token's K or V as an int8 KvLayer returns it (quantize_scale, quantize,
+    then q * scale)."""
+    x = np.array(f32(x), copy=True)
+    lib().oracle_kv_qdq(fptr(x), len(x))
+    return x
+
+
+def context_shift(tokens, prompt_len, max_ctx, anchor, kv=None):
+    """generate.rs:26-63 on a token list (and optionally an OracleKV):
+    returns (tokens, prompt_len, overflow, removed_at)."""
+    t = np.ascontiguousarray(np.asarray(tokens, np.uint32)).copy()
+    n, pl, at = C.c_int(len(t)), C.c_int(prompt_len), C.c_int(0)
+    ov = lib().oracle_context_shift(u32ptr(t), C.byref(n), C.byref(pl),
+                                    kv.ptr if kv is not None else None, max_ctx, anchor,
+                                    C.byref(at))
+    return t[:n.value].tolist(), pl.value, ov, at.value
+
+
 def sample_philox(logits, temperature, seed, rnd, slot, top_p=0.0, min_p=0.0):
     """One token of logits after the filters, with the Philox uniform of
     (seed, rnd, slot); greedy at temperature <= 0."""
@@ -442,8 +486,9 @@ def sample_philox(logits, temperature, seed, rnd, slot, top_p=0.0, min_p=0.0):
 
 
 class OracleKV:
-    def __init__(self, model: OracleModel, cap: int):
-        self.ptr = lib().oracle_kv_new(model.m.n_layers, model.kv_dim, cap)
+    def __init__(self, model: OracleModel | None, cap: int, n_layers=None, kv_dim=None):
+        self.ptr = lib().oracle_kv_new(model.m.n_layers if model else n_layers,
+                                       model.kv_dim if model else kv_dim, cap)
         self._model = model
 
     def __len__(self):
@@ -451,6 +496,40 @@ class OracleKV:
 
     def truncate(self, n):
         lib().oracle_kv_truncate(self.ptr, n)
+
+    def set_mode(self, mode, window=64):
+        """The KvLayer variant of every layer (KV_FP32 / KV_INT8 / KV_MIXED)."""
+        lib().oracle_kv_set_mode(self.ptr, mode, window)
+
+    def append(self, k, v):
+        """KvLayer::append of one token's k and v (kv_dim values each) to every
+        layer: the slot is written, then quantized as the variant does."""
+        kv = self.ptr.contents
+        assert kv.len < kv.cap
+        ka = np.ctypeslib.as_array(kv.k, shape=(kv.n_layers * kv.cap * kv.kv_dim,))
+        va = np.ctypeslib.as_array(kv.v, shape=(kv.n_layers * kv.cap * kv.kv_dim,))
+        pos = kv.len
+        # the token an INT8 layer quantizes now, or the one a MIXED layer moves cold
+        quantized = []
+        if kv.mode == KV_INT8:
+            quantized = [pos]
+        elif kv.mode == KV_MIXED and kv.hot + 1 > kv.window:
+            quantized = [pos - kv.window]
+        for layer in range(kv.n_layers):
+            base = (layer * kv.cap + pos) * kv.kv_dim
+            ka[base: base + kv.kv_dim] = f32(k)
+            va[base: base + kv.kv_dim] = f32(v)
+            for p in quantized:
+                o = (layer * kv.cap + p) * kv.kv_dim
+                for a in (ka, va):
+                    a[o: o + kv.kv_dim] = kv_qdq(a[o: o + kv.kv_dim])
+        kv.len = pos + 1
+        if kv.mode == KV_MIXED and kv.hot < kv.window:
+            kv.hot += 1
+
+    def shift(self, n, anchor=0):
+        """KvCache::shift (anchor 0) / shift_anchored."""
+        lib().oracle_kv_shift(self.ptr, n, anchor)
 
     def layer_k(self, layer):
         kv = self.ptr.contents
