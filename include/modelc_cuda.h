@@ -153,7 +153,10 @@ typedef struct mc_spec_cfg {
                              MC_KV_FP32, MC_KV_INT8 (use_int8_kv) or MC_KV_MIXED
                              (use_mixed_kv, window 64).  Values are held as the
                              reference's k_all()/v_all() return them (int8 codes
-                             times the token's scale); the storage stays f32. */
+                             times the token's scale); the storage stays f32.
+                             INT8 and MIXED: one-rank sessions.  MIXED: greedy;
+                             its forwards (prime and verify) append one token at
+                             a time, as the cache ages token by token. */
 } mc_spec_cfg;
 
 #define MC_KV_FP32 0

@@ -857,6 +857,12 @@ struct mc_session {
   // digits are the same either way)
   unsigned* gbar = nullptr;  // [2]
   int tails = kDefaultTails;
+  // MIXED target cache: the originals of the tokens verify steps quantize
+  // ([B][vm][L][2][Hkv * hdp]); each request's window count after its prime;
+  // the window count of the plain forward API's cache
+  float* mx_bak = nullptr;
+  std::vector<int> mx_hot0;
+  int plain_hot = 0;
   // MC_TRACE builds: timeline slots handed to the launches of one capture
   bool trace_on = false;
   int trace_next = 0;
@@ -1023,6 +1029,11 @@ static mc_status session_alloc(mc_session* s) {
   CK(cudaMemset(s->st_amax, 0, (size_t)2 * kMaxTokens * 4));
   CKS(s->al.alloc(&s->gbar, 2));
   CK(cudaMemset(s->gbar, 0, 2 * sizeof(unsigned)));
+  if (s->cfg.kv_mode == KV_MIXED) {
+    const int vm = s->cfg.gamma + (s->cfg.bonus ? 1 : 0);
+    CKS(s->al.alloc(&s->mx_bak, (size_t)s->B * std::max(vm, 1) * std::max(s->tw->L, 1) * 2 *
+                                     s->tw->Hkv * s->tw->hdp));
+  }
   if (const char* e = getenv("MODELC_CUDA_ENCODER_TAILS")) s->tails = atoi(e) & 3;
   s->st_np_cap = std::max(stripes, 1);
   CKS(s->al.alloc(&s->st_pss, (size_t)kMaxTokens * s->st_np_cap));
@@ -1128,8 +1139,14 @@ static mc_status session_create(const mc_weights* target, const mc_weights* draf
     return set_err(MC_E_INVALID, "the draft model is replicated: load it with tp_world 1");
   if (target->tp_world > 1 && cfg->temperature > 0.0f)
     return set_err(MC_E_INVALID, "tensor-parallel sessions decode greedily (temperature 0)");
-  if (cfg->kv_mode != KV_FP32 && cfg->kv_mode != KV_INT8)
-    return set_err(MC_E_INVALID, "kv_mode %d is not MC_KV_FP32 or MC_KV_INT8", cfg->kv_mode);
+  if (cfg->kv_mode != KV_FP32 && cfg->kv_mode != KV_INT8 && cfg->kv_mode != KV_MIXED)
+    return set_err(MC_E_INVALID, "kv_mode %d is not MC_KV_FP32, MC_KV_INT8 or MC_KV_MIXED",
+                   cfg->kv_mode);
+  if (cfg->kv_mode != KV_FP32 && target->tp_world > 1)
+    return set_err(MC_E_INVALID, "int8 and mixed KV caches quantize each token over all KV "
+                   "heads: tensor-parallel sessions keep an f32 cache");
+  if (cfg->kv_mode == KV_MIXED && cfg->temperature > 0.0f)
+    return set_err(MC_E_INVALID, "mixed KV caches run in greedy sessions (temperature 0)");
   if (cfg->shift_context < 0 || cfg->anchor_tokens < 0)
     return set_err(MC_E_INVALID, "shift_context and anchor_tokens must be >= 0");
   if (cfg->shift_context > 0 && cfg->temperature > 0.0f)
@@ -1329,9 +1346,25 @@ static mc_status enq_gemv(mc_session* s, const PMat& W, int epi, int M, GemvArgs
 // transformer.rs:64-96, for M positions at once): sm.seq_len tokens of each
 // of M / sm.seq_len sequences, whose positions, KV page-table rows and key
 // slots sm maps (one sequence: sm.seq_len = M).
+// A MIXED target forward's place in the cache's append sequence (KvMixArgs):
+// the window count before it (hot_ptr[z * hot_stride], or hot_const), the
+// appends before it (step), and for a verify step the originals' buffer and
+// the round's first position.
+struct MixStep {
+  const int* hot_ptr = nullptr;
+  int hot_stride = 0;
+  int hot_const = 0;
+  int step = 0;
+  float* bak = nullptr;
+  int bak_steps = 0;
+  int* base_out = nullptr;
+  int base_stride = 0;
+};
+
 static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv, int M,
                              SeqMap sm, EmbedArgs ea, const int* pos_ptr, int pos_add,
-                             unsigned long long* keys, float* logits_dev, bool kv_pre = false) {
+                             unsigned long long* keys, float* logits_dev, bool kv_pre = false,
+                             const MixStep* mix = nullptr) {
   if (M < 1 || M > kMaxTokens || sm.seq_len < 1 || M % sm.seq_len)
     return set_err(MC_E_INVALID, "forward of %d tokens in sequences of %d", M, sm.seq_len);
   if (!W->has_head) return set_err(MC_E_NO_HEAD, "model has no lm_head and no embedding");
@@ -1496,7 +1529,7 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
       a.sk = Lw.sk;
       a.kv_prefetch = 1;
       CKS(enq_gemv(s, Lw.qkv, EPI_QKV, M, a, nxt()));
-      if (&kv == &s->tkv && s->cfg.kv_mode == KV_INT8) {  // KvLayer::append of an INT8 layer
+      if (kv.k == s->tkv.k && s->cfg.kv_mode == KV_INT8) {  // KvLayer::append of an INT8 layer
         KvQArgs q{};
         q.kc = a.kc;
         q.vc = a.vc;
@@ -1510,6 +1543,33 @@ static mc_status enq_forward(mc_session* s, const mc_weights* W, const KVSet& kv
         q.hdp = W->hdp;
         q.page = kPage;
         CK(launch_kv_qdq(q, s->stream, true));
+      }
+      if (kv.k == s->tkv.k && s->cfg.kv_mode == KV_MIXED) {  // KvLayer::append of a MIXED layer
+        if (!mix || sm.seq_len != 1)
+          return set_err(MC_E_INVALID, "mixed KV forwards append one token per request");
+        KvMixArgs x{};
+        x.kc = a.kc;
+        x.vc = a.vc;
+        x.page_table = kv.page_table;
+        x.pos_ptr = pos_ptr;
+        x.pos_add = pos_add;
+        x.seq = sm;
+        x.B = M;
+        x.Hkv = W->Hkv;
+        x.hdp = W->hdp;
+        x.page = kPage;
+        x.window = kMixedWindow;
+        x.hot_ptr = mix->hot_ptr;
+        x.hot_stride = mix->hot_stride;
+        x.hot_const = mix->hot_const;
+        x.step = mix->step;
+        x.bak = mix->bak;
+        x.bak_steps = mix->bak_steps;
+        x.layer = l;
+        x.layers = W->L;
+        x.base_out = mix->base_out;
+        x.base_stride = mix->base_stride;
+        CK(launch_kv_mixed_age(x, s->stream, true));
       }
       AttnArgs t{};
       t.q = s->qb;
@@ -1608,16 +1668,22 @@ static mc_status forward_api(mc_session* s, int which, const uint32_t* ids, int 
   if (len + n > s->cap - 1) return set_err(MC_E_CAPACITY, "KV capacity %d exceeded", s->cap);
   CKS(check_usable(s));
   CK(cudaSetDevice(s->dev));
-  for (int c0 = 0; c0 < n; c0 += kChunk) {
-    const int M = std::min(kChunk, n - c0);
+  // a MIXED target cache appends token by token (plain_hot: its window count)
+  const bool mixed = !which && s->cfg.kv_mode == KV_MIXED;
+  const int chunk = mixed ? 1 : kChunk;
+  for (int c0 = 0; c0 < n; c0 += chunk) {
+    const int M = std::min(chunk, n - c0);
     memcpy(s->h_ids, ids + c0, (size_t)M * 4);
     CK(cudaMemcpyAsync(s->ids, s->h_ids, (size_t)M * 4, cudaMemcpyHostToDevice, s->stream));
     CK(launch_set_int(s->pos + which, len, s->stream));
     EmbedArgs ea{};
     ea.src = SRC_IDS;
     ea.ids = s->ids;
+    MixStep mx;
+    mx.hot_const = s->plain_hot;
     CKS(enq_forward(s, W, kv, M, SeqMap{M, 0, 0, 0}, ea, s->pos + which, 0, s->fkeys,
-                    logits ? s->logits : nullptr));
+                    logits ? s->logits : nullptr, false, mixed ? &mx : nullptr));
+    if (mixed) s->plain_hot = std::min(s->plain_hot + 1, kMixedWindow);
     if (logits)
       CK(cudaMemcpyAsync(logits + (size_t)c0 * W->V, s->logits, (size_t)M * W->V * 4,
                          cudaMemcpyDeviceToHost, s->stream));
@@ -1644,7 +1710,10 @@ extern "C" int32_t mc_kv_len(const mc_session* s) { return s ? s->lt : 0; }
 
 extern "C" mc_status mc_kv_truncate(mc_session* s, int32_t len) {
   if (!s || len < 0) return set_err(MC_E_INVALID, "bad arguments");
-  if (len < s->lt) s->lt = len;
+  if (len < s->lt) {
+    s->plain_hot = std::max(0, s->plain_hot - (s->lt - len));
+    s->lt = len;
+  }
   return MC_OK;
 }
 
@@ -1684,6 +1753,35 @@ extern "C" mc_status mc_draft(mc_session* s, const uint32_t* context, int32_t n,
 // z * vm .. z * vm + vm - 1), at the request's own target length.
 static mc_status enq_verify(mc_session* s, float* logits = nullptr) {
   const int vm = s->cfg.gamma + (s->cfg.bonus ? 1 : 0);
+  if (s->cfg.kv_mode == KV_MIXED) {
+    // a MIXED cache appends and ages token by token (each step's attention
+    // sees the window as the reference's sequential verify leaves it): vm
+    // forwards of one token per request -- the context's last token, then
+    // the drafts -- their originals kept for the acceptance's roll-back
+    const SeqMap sm{1, kStateInts, s->tkv.n_pages, kStateKeys};
+    for (int i = 0; i < vm; ++i) {
+      EmbedArgs ea{};
+      if (i == 0) {
+        ea.src = SRC_CTX_AT;
+        ea.ctx = s->ctx;
+        ea.off = &s->st->ld;
+      } else {
+        ea.src = SRC_KEYS;
+        ea.keys = &s->st->dkeys[i - 1];
+      }
+      MixStep mx;
+      mx.hot_ptr = &s->st->kv_hot;
+      mx.hot_stride = kStateInts;
+      mx.step = i;
+      mx.bak = s->mx_bak;
+      mx.bak_steps = vm;
+      mx.base_out = &s->st->mx_base;
+      mx.base_stride = kStateInts;
+      CKS(enq_forward(s, s->tw, s->tkv, s->B, sm, ea, &s->st->lt, i, &s->st->tkeys[i],
+                      logits ? logits + (size_t)i * s->tw->V : nullptr, false, &mx));
+    }
+    return MC_OK;
+  }
   EmbedArgs ea{};
   ea.src = SRC_VERIFY;
   ea.ctx = s->ctx;
@@ -1746,7 +1844,8 @@ static ShiftArgs shift_args(mc_session* s) {
   a.B = s->B;
   a.shift_context = s->cfg.shift_context;
   a.anchor = s->cfg.anchor_tokens;
-  a.requant = s->cfg.kv_mode == KV_INT8 && s->cfg.anchor_tokens > 0;
+  a.requant = s->cfg.kv_mode != KV_FP32 && s->cfg.anchor_tokens > 0;
+  a.window = s->cfg.kv_mode == KV_MIXED ? kMixedWindow : 0;
   a.t = kv_planes(s->tw, s->tkv, s->tkv.n_pages);
   a.d = kv_planes(s->dw, s->dkv, s->dkv.n_pages);
   return a;
@@ -1798,6 +1897,11 @@ static mc_status capture_round(mc_session* s) {
                         : launch_accept_greedy(st, s->ctx, s->acc_log, vm, s->B, s->ctx_stride,
                                                s->ctx_stride, s->stream, true);
     if (e != cudaSuccess) rc = set_err(MC_E_CUDA, "accept launch: %s", cudaGetErrorString(e));
+  }
+  if (rc == MC_OK && s->cfg.kv_mode == KV_MIXED) {  // roll back dropped steps' window moves
+    cudaError_t e = launch_kv_mixed_commit(s->st, kv_planes(s->tw, s->tkv, s->tkv.n_pages),
+                                           s->mx_bak, s->B, vm, kMixedWindow, s->stream, true);
+    if (e != cudaSuccess) rc = set_err(MC_E_CUDA, "mixed KV commit: %s", cudaGetErrorString(e));
   }
   if (rc == MC_OK && s->cfg.shift_context > 0) {  // generate.rs:738-748: the context shift
     cudaError_t e = launch_context_shift(shift_args(s), s->nsm, s->stream, true);
@@ -1852,25 +1956,38 @@ static SpecState fresh_state(const mc_session* s, int n_prompt) {
   h.ng_last_len = n_prompt;
   return h;
 }
+static SpecState fresh_state(const mc_session* s, int z, int n_prompt) {
+  SpecState h = fresh_state(s, n_prompt);
+  if (s->cfg.kv_mode == KV_MIXED && z < (int)s->mx_hot0.size()) h.kv_hot = s->mx_hot0[z];
+  return h;
+}
 
 // Prime request z (generate.rs:629-636): its prompt through the target and,
 // all but the last token, through the draft, into its own KV pages.
 // Target forwards over prompt tokens [t0, n_prompt) (t0 > 0: the K/V of the
 // first t0 were restored from a prefix snapshot), draft forwards over all but
 // the last.
-static mc_status prime_request(mc_session* s, int z, int n_prompt, int t0 = 0) {
+static mc_status prime_request(mc_session* s, int z, int n_prompt, int t0 = 0, int hot0 = 0) {
   uint32_t* ctx = s->ctx + (size_t)z * s->ctx_stride;
   KVSet tkv = s->tkv, dkv = s->dkv;
   tkv.page_table += (size_t)z * tkv.n_pages;
   dkv.page_table += (size_t)z * dkv.n_pages;
-  for (int c0 = t0; c0 < n_prompt; c0 += kChunk) {
-    const int M = std::min(kChunk, n_prompt - c0);
+  // a MIXED cache appends token by token (hot0: its window count at t0)
+  const bool mixed = s->cfg.kv_mode == KV_MIXED;
+  const int chunk = mixed ? 1 : kChunk;
+  for (int c0 = t0; c0 < n_prompt; c0 += chunk) {
+    const int M = std::min(chunk, n_prompt - c0);
     CK(launch_set_int(s->pos, c0, s->stream));
     EmbedArgs ea{};
     ea.src = SRC_IDS;
     ea.ids = ctx + c0;
-    CKS(enq_forward(s, s->tw, tkv, M, SeqMap{M, 0, 0, 0}, ea, s->pos, 0, s->fkeys, nullptr));
+    MixStep mx;
+    mx.hot_const = hot0;
+    mx.step = c0 - t0;
+    CKS(enq_forward(s, s->tw, tkv, M, SeqMap{M, 0, 0, 0}, ea, s->pos, 0, s->fkeys, nullptr,
+                    false, mixed ? &mx : nullptr));
   }
+  if (mixed) s->mx_hot0[z] = std::min(hot0 + n_prompt - t0, kMixedWindow);
   // the draft gets all but the last prompt token (the first round forwards it)
   for (int c0 = 0; c0 < n_prompt - 1 && s->dw; c0 += kChunk) {
     const int M = std::min(kChunk, n_prompt - 1 - c0);
@@ -1889,6 +2006,7 @@ static mc_status prime_request(mc_session* s, int z, int n_prompt, int t0 = 0) {
 struct mc_kv_snapshot {
   const mc_weights* W = nullptr;
   int dev = 0, kv_mode = 0, len = 0, pages = 0;
+  int hot = 0;             // MIXED: tokens in the f32 window
   size_t page_floats = 0;  // floats of one KV page (Hkv heads x kPage positions x hdp)
   float* k = nullptr;      // [L][pages * page_floats]
   float* v = nullptr;
@@ -1941,7 +2059,8 @@ static mc_status prime_impl(mc_session* s, const uint32_t* prompts, const int32_
     CK(cudaMemcpyAsync(s->ng, ents.data(), ents.size() * 4, cudaMemcpyHostToDevice, s->stream));
     CK(cudaStreamSynchronize(s->stream));  // ents is a host temporary
   }
-  int t0 = 0;
+  int t0 = 0, hot0 = 0;
+  s->mx_hot0.assign(n_requests, 0);
   if (snap) {  // request 0's first snap->len positions from the snapshot
     const size_t per_layer = (size_t)snap->pages * snap->page_floats;
     for (int l = 0; l < s->tw->L; ++l) {
@@ -1951,10 +2070,12 @@ static mc_status prime_impl(mc_session* s, const uint32_t* prompts, const int32_
                          per_layer * sizeof(float), cudaMemcpyDeviceToDevice, s->stream));
     }
     t0 = snap->len;
+    hot0 = snap->hot;
   }
-  for (int z = 0; z < n_requests; ++z) CKS(prime_request(s, z, lens[z], z == 0 ? t0 : 0));
+  for (int z = 0; z < n_requests; ++z)
+    CKS(prime_request(s, z, lens[z], z == 0 ? t0 : 0, z == 0 ? hot0 : 0));
   std::vector<SpecState> h(n_requests);
-  for (int z = 0; z < n_requests; ++z) h[z] = fresh_state(s, lens[z]);
+  for (int z = 0; z < n_requests; ++z) h[z] = fresh_state(s, z, lens[z]);
   CK(cudaMemcpyAsync(s->st, h.data(), sizeof(SpecState) * n_requests, cudaMemcpyHostToDevice,
                      s->stream));
   CK(cudaStreamSynchronize(s->stream));
@@ -1987,6 +2108,7 @@ extern "C" mc_status mc_kv_snapshot_take(mc_session* s, int32_t request, mc_kv_s
   snap->dev = s->dev;
   snap->kv_mode = s->cfg.kv_mode;
   snap->len = h.lt;  // equal to the context length after a prime or a round
+  snap->hot = h.kv_hot;
   snap->pages = (h.lt + kPage - 1) / kPage;
   snap->page_floats = (size_t)s->tw->Hkv * kPage * s->tw->hdp;
   snap->tokens.resize((size_t)h.ctx_len);
@@ -2144,7 +2266,7 @@ extern "C" mc_status mc_spec_rewind(mc_session* s) {
       if (h[z].n_shifts > 0)
         return set_err(MC_E_INVALID, "request %d's context was shifted: prime it again", z);
   }
-  for (int z = 0; z < s->B; ++z) h[z] = fresh_state(s, s->prompt_lens[z]);
+  for (int z = 0; z < s->B; ++z) h[z] = fresh_state(s, z, s->prompt_lens[z]);
   CK(cudaMemcpyAsync(s->st, h.data(), sizeof(SpecState) * s->B, cudaMemcpyHostToDevice, s->stream));
   CK(cudaStreamSynchronize(s->stream));
   s->lt = h[0].lt;

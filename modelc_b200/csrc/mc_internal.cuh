@@ -356,6 +356,9 @@ struct SpecState {
   // (0: none), where the removed range starts, the target / draft KV
   // lengths before it, whether it was the anchored form; shifts so far
   int sh_n, sh_at, sh_lt, sh_ld, sh_anch, n_shifts;
+  // MIXED target cache: tokens in its f32 window (the last kv_hot
+  // positions), and the round's first verify position
+  int kv_hot, mx_base;
   unsigned long long tkeys[kGroupTokens];
   unsigned long long dkeys[kGroupTokens];
 };
@@ -435,6 +438,35 @@ struct KvQArgs {
 // KvLayer::append of an INT8 layer on those tokens (mc_kvcache.cu).
 cudaError_t launch_kv_qdq(const KvQArgs& a, cudaStream_t s, bool pdl);
 
+// The window of a MIXED layer (make_kv_cache, generate.rs:19).
+constexpr int kMixedWindow = 64;
+
+// KvLayer::append of a MIXED layer (transformer.rs:389-419) for one token
+// per request at position pos_ptr[z * seq.pos_stride] + pos_add in one
+// layer: when the f32 window already holds `window` tokens -- min(hot +
+// step, window) with hot = hot_ptr[z * hot_stride] (or hot_const) before the
+// first of `step` earlier appends -- the token `window` positions back is
+// quantized (its originals saved to bak first when bak is set: a verify
+// step, which the acceptance may roll back).
+struct KvMixArgs {
+  float* kc;
+  float* vc;
+  const int* page_table;
+  const int* pos_ptr;
+  int pos_add;
+  SeqMap seq;            // seq_len 1: one token per request
+  int B, Hkv, hdp, page, window;
+  const int* hot_ptr;
+  int hot_stride;
+  int hot_const;
+  int step;
+  float* bak;            // [B][bak_steps][layers][2][Hkv * hdp] or nullptr
+  int bak_steps, layer, layers;
+  int* base_out;         // step 0, layer 0: the position into base_out[z * base_stride]
+  int base_stride;
+};
+cudaError_t launch_kv_mixed_age(const KvMixArgs& a, cudaStream_t s, bool pdl);
+
 // One KV cache (target or draft) of every request, for the context shift.
 struct KvPlanes {
   float* k;             // [layers][layer_stride floats]: pages [page][Hkv][page_len][hdp]
@@ -451,12 +483,19 @@ struct ShiftArgs {
   int B;
   int shift_context;    // GenerationConfig::max_context
   int anchor;           // GenerationConfig::anchor_tokens
-  int requant;          // INT8 target: re-quantize the kept tokens after an anchored shift
+  int requant;          // re-quantize kept tokens after an anchored shift (INT8, MIXED)
+  int window;           // MIXED target: its window (kept f32 tokens); 0 otherwise
   KvPlanes t, d;        // target KV; draft KV (d.layers == 0: none)
 };
 // generate.rs:26-63 context_shift after a round, on the device: the plan and
-// token move, the K/V moves, the INT8 re-quantization (three launches).
+// token move, the K/V moves, the re-quantization (three launches).
 cudaError_t launch_context_shift(const ShiftArgs& a, int nsm, cudaStream_t s, bool pdl);
+
+// After a MIXED session's acceptance: the window quantizations of verify
+// steps the acceptance dropped (steps >= lt - mx_base) are undone from bak,
+// then kv_hot advances by the steps kept (two launches).
+cudaError_t launch_kv_mixed_commit(SpecState* st, const KvPlanes& t, const float* bak, int B,
+                                   int steps, int window, cudaStream_t s, bool pdl);
 
 cudaError_t launch_accept_greedy(SpecState* st, uint32_t* ctx, int* acc_log, int vm, int n_seq,
                                  int ctx_stride, int log_stride, cudaStream_t s, bool pdl);

@@ -70,6 +70,35 @@ __global__ void __launch_bounds__(kKvqThreads) k_kv_qdq(KvQArgs a) {
   qdq_token_warp(base, a.Hkv * a.hd, a.hd, (size_t)a.page * a.hdp, lane);
 }
 
+// KvLayer::append of a MIXED layer (transformer.rs:389-419): one warp per
+// (request, K or V).  The hot part holds the last min(hot + step, window)
+// tokens before this append; when that is the window, the append pushes the
+// oldest hot token -- `window` positions back -- into the cold part.
+__global__ void __launch_bounds__(kKvqThreads) k_kv_mixed_age(KvMixArgs a) {
+  grid_launch_dependents();
+  grid_wait();
+  const int warp = (int)(blockIdx.x * (kKvqThreads / 32) + (threadIdx.x >> 5));
+  const int lane = threadIdx.x & 31;
+  if (warp >= 2 * a.B) return;
+  const int z = warp >> 1, sel = warp & 1;
+  const int pos = a.pos_ptr[z * a.seq.pos_stride] + a.pos_add;
+  if (a.base_out && a.step == 0 && a.layer == 0 && sel == 0 && lane == 0)
+    a.base_out[z * a.base_stride] = pos;
+  const int hot = a.hot_ptr ? a.hot_ptr[z * a.hot_stride] : a.hot_const;
+  if (min(hot + a.step, a.window) < a.window) return;  // warp-uniform
+  const int c = pos - a.window;
+  const int pg = a.page_table[z * a.seq.pt_stride + c / a.page];
+  float* base = (sel ? a.vc : a.kc) + ((size_t)pg * a.Hkv * a.page + (size_t)(c % a.page)) * a.hdp;
+  const int n = a.Hkv * a.hdp;
+  const size_t head_stride = (size_t)a.page * a.hdp;
+  if (a.bak) {
+    float* b = a.bak + ((((size_t)z * a.bak_steps + a.step) * a.layers + a.layer) * 2 + sel) * n;
+    for (int i = lane; i < n; i += 32) b[i] = base[(size_t)(i / a.hdp) * head_stride + i % a.hdp];
+    __syncwarp();
+  }
+  qdq_token_warp(base, n, a.hdp, head_stride, lane);
+}
+
 // Position p of head h in one layer of request z's KV (K or V base).
 __device__ __forceinline__ float* kv_at(const KvPlanes& P, float* layer_base, int z, int h,
                                         int p) {
@@ -112,6 +141,14 @@ __global__ void __launch_bounds__(kKvqThreads) k_shift_plan(ShiftArgs a) {
         }
       } else {
         st->prompt_len = max(st->prompt_len - n, 0);
+      }
+      if (a.window > 0) {  // MIXED: shift drops cold tokens first; shift_anchored re-appends
+        if (anch) {
+          st->kv_hot = min(L - n, a.window);
+        } else {
+          const int cold = st->lt - st->kv_hot;
+          if (n > cold) st->kv_hot -= n - cold;
+        }
       }
       st->ctx_len = L - n;
       st->lt = st->lt - min(n, max(st->lt - at, 0));
@@ -175,9 +212,10 @@ __global__ void __launch_bounds__(kKvqThreads) k_shift_kv(ShiftArgs a) {
   }
 }
 
-// After an anchored shift of an INT8 target: the kept tokens [0, len)
-// re-appended (transformer.rs:577-582), each re-quantized from its current
-// values; one warp per (request, layer, position, K or V).
+// After an anchored shift of an INT8 or MIXED target: the kept tokens
+// re-appended (transformer.rs:577-582), each one that reaches the int8 part
+// re-quantized from its current values; one warp per (request, layer,
+// position, K or V).
 __global__ void __launch_bounds__(kKvqThreads) k_shift_requant(ShiftArgs a) {
   grid_launch_dependents();
   grid_wait();
@@ -193,11 +231,51 @@ __global__ void __launch_bounds__(kKvqThreads) k_shift_requant(ShiftArgs a) {
     const int layer = (int)(r / ((long long)a.ctx_stride * 2));
     r -= (long long)layer * a.ctx_stride * 2;
     const int p = (int)(r >> 1);
-    if (p >= st->lt) continue;
+    // re-appended tokens land in the cold part: all of them in an INT8
+    // layer, all but the last `window` in a MIXED one
+    if (p >= st->lt - a.window) continue;
     float* lb = ((r & 1) ? a.t.v : a.t.k) + (size_t)layer * a.t.layer_stride;
     qdq_token_warp(kv_at(a.t, lb, z, 0, p), a.t.Hkv * a.t.hd, a.t.hd,
                    (size_t)a.t.page * a.t.hdp, lane);
   }
+}
+
+// The verify steps a MIXED round's acceptance dropped: each one that moved a
+// token to the cold part gets it back from bak.  One warp per (request,
+// step, layer, K or V).
+__global__ void __launch_bounds__(kKvqThreads) k_kv_mixed_restore(SpecState* st, KvPlanes t,
+                                                                  const float* bak, int B,
+                                                                  int steps, int window) {
+  grid_launch_dependents();
+  grid_wait();
+  const int lane = threadIdx.x & 31;
+  const long long w = (long long)blockIdx.x * (kKvqThreads / 32) + (threadIdx.x >> 5);
+  if (w >= (long long)B * steps * t.layers * 2) return;
+  const int sel = (int)(w & 1);
+  long long r = w >> 1;
+  const int layer = (int)(r % t.layers);
+  r /= t.layers;
+  const int i = (int)(r % steps), z = (int)(r / steps);
+  const SpecState* q = st + z;
+  const int kept = q->lt - q->mx_base;
+  if (i < kept || min(q->kv_hot + i, window) < window) return;
+  const int c = q->mx_base + i - window;
+  const int n = t.Hkv * t.hdp;
+  const float* b = bak + ((((size_t)z * steps + i) * t.layers + layer) * 2 + sel) * n;
+  float* lb = (sel ? t.v : t.k) + (size_t)layer * t.layer_stride;
+  for (int e = lane; e < n; e += 32) {
+    const int h = e / t.hdp;
+    kv_at(t, lb, z, h, c)[e - h * t.hdp] = b[e];
+  }
+}
+
+__global__ void k_kv_mixed_hot(SpecState* st, int B, int window) {
+  grid_launch_dependents();
+  grid_wait();
+  const int z = blockIdx.x * blockDim.x + threadIdx.x;
+  if (z >= B) return;
+  SpecState* q = st + z;
+  q->kv_hot = min(q->kv_hot + (q->lt - q->mx_base), window);
 }
 
 cudaError_t launch_pdl(const void* f, dim3 grid, dim3 block, void** args, cudaStream_t s,
@@ -223,6 +301,34 @@ cudaError_t launch_kv_qdq(const KvQArgs& a, cudaStream_t s, bool pdl) {
   const int warps = 2 * a.M, per = kKvqThreads / 32;
   return launch_pdl((const void*)k_kv_qdq, dim3((warps + per - 1) / per), dim3(kKvqThreads), args,
                     s, pdl);
+}
+
+cudaError_t launch_kv_mixed_age(const KvMixArgs& a, cudaStream_t s, bool pdl) {
+  if (a.B < 1 || a.Hkv < 1 || a.hdp < 1 || a.page < 1 || a.window < 1 || a.step < 0 ||
+      (a.bak && (a.step >= a.bak_steps || a.layer >= a.layers)))
+    return cudaErrorInvalidValue;
+  KvMixArgs x = a;
+  void* args[] = {&x};
+  const int warps = 2 * a.B, per = kKvqThreads / 32;
+  return launch_pdl((const void*)k_kv_mixed_age, dim3((warps + per - 1) / per), dim3(kKvqThreads),
+                    args, s, pdl);
+}
+
+cudaError_t launch_kv_mixed_commit(SpecState* st, const KvPlanes& t, const float* bak, int B,
+                                   int steps, int window, cudaStream_t s, bool pdl) {
+  if (B < 1 || steps < 1 || window < 1 || t.layers < 1) return cudaErrorInvalidValue;
+  SpecState* st_ = st;
+  KvPlanes t_ = t;
+  const float* bak_ = bak;
+  int B_ = B, steps_ = steps, window_ = window;
+  void* args[] = {&st_, &t_, &bak_, &B_, &steps_, &window_};
+  const long long warps = (long long)B * steps * t.layers * 2;
+  const int per = kKvqThreads / 32;
+  cudaError_t e = launch_pdl((const void*)k_kv_mixed_restore, dim3((unsigned)((warps + per - 1) / per)),
+                             dim3(kKvqThreads), args, s, pdl);
+  if (e != cudaSuccess) return e;
+  void* args2[] = {&st_, &B_, &window_};
+  return launch_pdl((const void*)k_kv_mixed_hot, dim3((B + 127) / 128), dim3(128), args2, s, pdl);
 }
 
 cudaError_t launch_context_shift(const ShiftArgs& a, int nsm, cudaStream_t s, bool pdl) {

@@ -30,6 +30,7 @@ class GenerationConfig:
     max_context: int = 0  # the context shift's threshold (None = 0)
     anchor_tokens: int = 0
     use_int8_kv: bool = False
+    use_mixed_kv: bool = False
 
 
 # target KV variants (make_kv_cache, generate.rs:17-24)
@@ -51,8 +52,8 @@ class Session:
     requests in lock step, each exactly as it would decode alone.
     ``max_context`` is the KV capacity; ``shift_context`` / ``anchor_tokens``
     are GenerationConfig::max_context / anchor_tokens (the context shift,
-    generate.rs:26-63); ``kv_mode`` the target cache variant (KV_FP32 or
-    KV_INT8)."""
+    generate.rs:26-63); ``kv_mode`` the target cache variant (KV_FP32,
+    KV_INT8 or KV_MIXED)."""
 
     def __init__(self, target: Weights, draft=None, gamma: int = 4,
                  max_context: int = 2048, bonus: bool = False, temperature: float = 0.0,
@@ -412,7 +413,8 @@ def speculative_generate(target: Weights, draft: Weights, prompt, config: Genera
                 temperature=config.temperature, seed=config.seed,
                 accept_mode=config.accept_mode, top_p=config.top_p, min_p=config.min_p,
                 shift_context=config.max_context, anchor_tokens=config.anchor_tokens,
-                kv_mode=KV_INT8 if config.use_int8_kv else KV_FP32)
+                kv_mode=(KV_MIXED if config.use_mixed_kv else
+                         KV_INT8 if config.use_int8_kv else KV_FP32))
     try:
         return s.speculative_generate(prompt, config.max_tokens)
     finally:

@@ -77,6 +77,13 @@ def _mirror_mlp(tw, scale=0.05):
     return tw, t, ref
 
 
+def _prefix_draft(tw):
+    """The target's embedding, norms, first layer and head: a one-layer draft
+    that agrees with the target on some rounds."""
+    return {k: v for k, v in tw.items()
+            if not k.startswith("model.layers.") or k.startswith("model.layers.0.")}
+
+
 def _close_enough(got, ref, rtol=1e-3):
     for i in range(ref.shape[0]):
         scale = np.abs(ref[i]).max()
@@ -105,7 +112,7 @@ def test_int8_kv_forward_matches_oracle(cfg):
 def test_int8_kv_spec_decode_matches_oracle(drafter):
     cfg = SMALL_GQA
     tw = _weak_layers(mb.synth_weights(cfg, seed=0), 0.25)
-    dw = mb.synth_weights(cfg.with_layers(1), seed=1)
+    dw = _prefix_draft(tw)
     ot, od = _oracle(tw, cfg), _oracle(dw, cfg.with_layers(1))
     prompt = _prompt(cfg)
     D = mb.Weights(dw, cfg.with_layers(1)) if drafter == "llama" else None
@@ -136,7 +143,7 @@ def test_context_shift_matches_oracle(drafter, anchor, kv_mode):
         tw, t, odraft = _mirror_mlp(tw)
         D = mb.MlpDraftModel(t)
     elif drafter == "llama":
-        dw = mb.synth_weights(cfg.with_layers(1), seed=3)
+        dw = _prefix_draft(tw)
         odraft = o.OracleLlamaDraft(_oracle(dw, cfg.with_layers(1)), 256)
         D = mb.Weights(dw, cfg.with_layers(1))
     ot = _oracle(tw, cfg)
@@ -218,3 +225,96 @@ def test_prefix_cache_restore_matches_oracle(drafter, kv_mode):
     with pytest.raises(mb.McError):
         s.prime_cached(hit.kv, [1, 2, 3] + p2)
     s.close()
+
+
+# ---------------------------------------------------------------- MIXED KV
+# use_mixed_kv (KvLayer::Mixed, transformer.rs:180-193, :389-419): the last 64
+# tokens in f32, older ones int8.  The device appends and ages a MIXED cache
+# token by token, verify steps included; the acceptance rolls back the window
+# moves of the steps it drops.  Contexts past 64 tokens exercise the cold part.
+def _long_prompt(cfg, n, seed):
+    rng = np.random.default_rng(seed)
+    motif = rng.integers(0, cfg.vocab, 6).tolist()
+    out = []
+    while len(out) < n:
+        out += motif + rng.integers(0, cfg.vocab, 3).tolist()
+    return out[:n]
+
+
+@pytest.mark.parametrize("cfg", [SMALL_REF, SMALL_GQA], ids=lambda c: c.name)
+def test_mixed_kv_forward_matches_oracle(cfg):
+    ws = mb.synth_weights(cfg, seed=0)
+    ids = np.random.default_rng(9).integers(0, cfg.vocab, 90).tolist()
+    om = _oracle(ws, cfg)
+    kv = om.new_kv(128)
+    kv.set_mode(o.KV_MIXED, 64)
+    ref = np.concatenate([om.forward_ids(ids[:50], kv), om.forward_ids(ids[50:], kv)])
+    s = mb.Session(mb.Weights(ws, cfg), None, gamma=1, max_context=128, kv_mode=mb.KV_MIXED)
+    got = np.concatenate([s.forward(ids[:50]), s.forward(ids[50:])])
+    s.close()
+    _close_enough(got, ref)
+
+
+@pytest.mark.parametrize("drafter", ["llama", "ngram"])
+def test_mixed_kv_spec_decode_matches_oracle(drafter):
+    cfg = SMALL_GQA
+    tw = _weak_layers(mb.synth_weights(cfg, seed=0), 0.25)
+    dw = _prefix_draft(tw)
+    ot, od = _oracle(tw, cfg), _oracle(dw, cfg.with_layers(1))
+    prompt = _long_prompt(cfg, 70, seed=3)
+    D = mb.Weights(dw, cfg.with_layers(1)) if drafter == "llama" else None
+    odraft = o.OracleLlamaDraft(od, 256) if drafter == "llama" else None
+    ref, racc = ot.speculative_generate(prompt, 30, 3, odraft, kv_mode=o.KV_MIXED)
+    s = mb.Session(mb.Weights(tw, cfg), D, gamma=3, max_context=160, kv_mode=mb.KV_MIXED)
+    got, gacc = s.speculative_generate(prompt, 30)
+    s.close()
+    assert got == ref
+    assert gacc == racc
+    print(f"mixed {drafter}: {len(ref)} ids, {len(racc)} rounds, {sum(racc)} drafts accepted")
+
+
+@pytest.mark.parametrize("anchor", [0, 4])
+def test_mixed_kv_context_shift_matches_oracle(anchor):
+    cfg = SMALL_GQA
+    tw = _weak_layers(mb.synth_weights(cfg, seed=2), 0.25)
+    ot = _oracle(tw, cfg)
+    prompt = _long_prompt(cfg, 80, seed=4)
+    shift, n_new = 90, 40
+    ref, racc = ot.speculative_generate(prompt, n_new, 3, None, max_context=shift,
+                                        anchor_tokens=anchor, kv_mode=o.KV_MIXED, rounds_cap=512)
+    s = mb.Session(mb.Weights(tw, cfg), None, gamma=3, max_context=128, shift_context=shift,
+                   anchor_tokens=anchor, kv_mode=mb.KV_MIXED)
+    s.prime(prompt)
+    s.decode(n_new)
+    got, gacc = s.read(cap=256)
+    s.close()
+    assert got == ref
+    assert gacc == racc
+
+
+def test_mixed_kv_prefix_cache_matches_oracle():
+    cfg = SMALL_GQA
+    tw = _weak_layers(mb.synth_weights(cfg, seed=6), 0.25)
+    ot = _oracle(tw, cfg)
+    W = mb.Weights(tw, cfg)
+    p1 = _long_prompt(cfg, 66, seed=8)
+    s = mb.Session(W, None, gamma=3, max_context=160, kv_mode=mb.KV_MIXED)
+    s.prime(p1)
+    s.decode(10)
+    g1, _ = s.read()
+    snap = s.snapshot()
+    s.close()
+    okv = ot.new_kv(200)
+    okv.set_mode(o.KV_MIXED, 64)
+    r1, _ = ot.speculative_generate(p1, 10, 3, None, kv_mode=o.KV_MIXED, kv=okv)
+    assert r1 == g1
+    p2 = p1 + g1 + [3, 1, 4, 1, 5]
+    s = mb.Session(W, None, gamma=3, max_context=160, kv_mode=mb.KV_MIXED)
+    s.prime_cached(snap, p2)
+    s.decode(14)
+    got, gacc = s.read()
+    s.close()
+    ref, racc = ot.speculative_generate(p2, 14, 3, None, kv_mode=o.KV_MIXED, kv=okv,
+                                        matched_len=len(p1) + len(g1))
+    assert got == ref
+    assert gacc == racc
