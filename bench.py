@@ -19,10 +19,13 @@ the GPU.  Inputs (7.5 GB of weights) exceed the 126 MB L2 on every step.
 
 ``--impl reference`` times the reference's CPU algorithm (the oracle's
 bit-identical row-parallel linear on all host cores) on the same workload.
-Multi-GPU (torchrun, N ranks): one request with the target tensor-parallel
-over the N GPUs (NCCL all-reduce after each row-parallel projection; strong
-scaling), value = that request's tokens / max-over-ranks time.  --replicas
-instead runs N independent requests (weak scaling).
+Multi-GPU (torchrun, N ranks): N independent requests, one per GPU, each
+with its own replica of the models -- requests are independent units, so
+nothing crosses NVLink on the data path (weak scaling); value = all ranks'
+tokens / max-over-ranks time.  --tp instead runs one request with the target
+tensor-parallel over the N GPUs (the fused NVLink reduction after each
+row-parallel projection, or NCCL with --tp-nccl; strong scaling), value =
+that request's tokens / max-over-ranks time.
 """
 from __future__ import annotations
 
@@ -382,9 +385,9 @@ def run_ours(args):
     PROMPT_LEN, NEW_TOKENS, GAMMA = wl.prompt_len, wl.new_tokens, wl.gamma
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
-    # N > 1: one request, target tensor-parallel over the N GPUs (strong
-    # scaling); --replicas: N independent requests (weak scaling)
-    tp = world > 1 and not args.replicas
+    # N > 1: N independent requests (weak scaling); --tp: one request, target
+    # tensor-parallel over the N GPUs (strong scaling)
+    tp = world > 1 and (args.tp or args.tp_nccl)
     if world > 1:
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
@@ -574,7 +577,9 @@ def run_timeline(args):
     per launch the first CTA's start, its release from griddepcontrol.wait and
     the last CTA's end (%globaltimer), summed per kernel kind; plus per-phase
     times (thread 0 of each CTA) of the attention and the tcgen05 GEMMs.
-    Single GPU; --config selects the workload (batch included)."""
+    --config selects the workload (batch included).  Under torchrun with N
+    ranks: the target tensor-parallel over them with the fused NVLink
+    reduction, rank 0's timeline printed."""
     import ctypes as C
     import torch
     import modelc_b200 as mb
@@ -582,12 +587,25 @@ def run_timeline(args):
     L.use_trace_library()
     lib = L.lib()
     wl = workloads()[args.config]
-    torch.cuda.set_device(0)
-    cfg, target, draft, prompt = build_models(0, wl=wl)
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    cfg, target, draft, prompt = build_models(local, wl=wl, tp=(rank, world))
     B = wl.batch
     prompts = prompt if B > 1 else [prompt]
     sess = mb.Session(target, draft, gamma=wl.gamma,
                       max_context=wl.prompt_len + wl.new_tokens + 2 * wl.gamma + 8, n_requests=B)
+    if world > 1:
+        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(mb.tp_unique_id()), dtype=torch.uint8))
+        torch.distributed.broadcast(uid, 0)
+        sess.tp_init(bytes(uid.cpu().numpy().tobytes()), rank, world)
+        handles = [None] * world
+        torch.distributed.all_gather_object(handles, sess.tp_ipc_handle())
+        sess.tp_open_peers(handles)
     sess.prime_batch(prompts)
     sess.decode(8)
     sess.verify_launch(3)
@@ -608,15 +626,22 @@ def run_timeline(args):
     att = ["attention+enc"] if att_tail else ["attention", "quant_o"]
     names = ["embed"]
     for l in range(cfg.n_layers):
-        if tails:
+        if world > 1:  # row-parallel GEMVs store partial rows; a reduce follows each
+            names += ["quant_attn", "qkv"] + att + ["o", "o_reduce", "quant_mlp", "gu",
+                                                    "quant_act", "down", "down_reduce"]
+        elif tails:
             names += (["quant_attn"] if l == 0 else []) + ["qkv"] + att + ["o+enc", "gu+enc",
                                                                           "down+enc"]
         else:
             names += ["quant_attn", "qkv"] + att + ["o", "quant_mlp", "gu", "quant_act", "down"]
-    names += ["head"] if tails else ["quant_final", "head"]
+    names += ["head"] if tails and world == 1 else ["quant_final", "head"]
     n = len(names)
     for _ in range(3):  # the last of three repetitions
+        if world > 1:
+            torch.distributed.barrier()
         L.check(lib.mc_trace_reset())
+        if world > 1:
+            torch.distributed.barrier()
         sess.verify_launch(1)
         torch.cuda.synchronize()
         buf = (C.c_ulonglong * (19 * (n + 1)))()
@@ -626,6 +651,13 @@ def run_timeline(args):
         raise RuntimeError(f"timeline names do not match the forward's {n} launches")
     raw = np.array(buf, dtype=np.float64)[:19 * (n + 1)]
     raw = np.r_[raw[:3 * n], raw[3 * (n + 1): 3 * (n + 1) + 16 * n]]
+    if world > 1:  # the peers still read this rank's exchange buffers until all are done
+        torch.distributed.barrier()
+        if rank != 0:
+            sess.close()
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+            return
     a = raw[:3 * n].reshape(n, 3)
     ph = raw[3 * n:].reshape(n, 16)
     a = (a - a[0, 0]) / 1e3  # us
@@ -662,6 +694,9 @@ def run_timeline(args):
                 print(f"  {k} {labels[k]:22s} {sums[k] / cnts[k] / 1e3:7.2f}   "
                       f"{cnts[k] / len(idx):7.1f}")
     sess.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
 
 
 def run_sweep(args):
@@ -800,10 +835,10 @@ def main():
     ap.add_argument("--config", default="llama3-8b",
                     choices=["llama3-8b", "llama3-8b-bs8", "tinyllama", "llama2-70b"],
                     help="workload (default: the headline 8B int8 batch-1 configuration)")
+    ap.add_argument("--tp", action="store_true",
+                    help="N > 1: one request, target tensor-parallel over the N GPUs")
     ap.add_argument("--tp-nccl", action="store_true",
-                    help="tensor parallelism: NCCL all-reduces instead of the fused NVLink reduction")
-    ap.add_argument("--replicas", action="store_true",
-                    help="N > 1: independent requests per GPU instead of tensor parallelism")
+                    help="with --tp: NCCL all-reduces instead of the fused NVLink reduction")
     ap.add_argument("--timeline", action="store_true",
                     help="in-situ per-kernel timeline of one verify forward (MC_TRACE build)")
     ap.add_argument("--sweep", action="store_true",
