@@ -353,7 +353,7 @@ def cpu_baseline_full(wl, cfg, device_index, rounds, tokens, accepted):
 
 # ---------------------------------------------------------------------- GPU
 def build_models(device_index: int, layers: int | None = None, wl: Workload | None = None,
-                 tp: tuple = (0, 1)):
+                 tp: tuple = (0, 1), draft_layers: int | None = None):
     """Random-init weights N(0, 0.02) generated on the GPU (target seed 0,
     draft seed 1) and a uniform prompt (seed 2).  tp = (rank, world) keeps
     this rank's tensor-parallel shard of the target; the draft is replicated."""
@@ -362,7 +362,7 @@ def build_models(device_index: int, layers: int | None = None, wl: Workload | No
     wl = wl or workloads()["llama3-8b"]
     dev = torch.device("cuda", device_index)
     cfg = wl.target if not layers else wl.target.with_layers(layers)
-    dcfg = wl.draft
+    dcfg = wl.draft if not draft_layers else wl.draft.with_layers(draft_layers)
     tt = mb.synth_weights_torch(cfg, seed=0, device=dev, fmt=wl.fmt)
     target = mb.Weights(tt, cfg, device=device_index, tp_rank=tp[0], tp_world=tp[1])
     del tt
@@ -554,9 +554,12 @@ def run_profile(args):
     import torch
     import modelc_b200 as mb
     torch.cuda.set_device(0)
-    cfg, target, draft, prompt = build_models(0, args.layers)
-    sess = mb.Session(target, draft, gamma=GAMMA,
-                      max_context=PROMPT_LEN + NEW_TOKENS + 2 * GAMMA + 8)
+    wl = workloads()[args.config]
+    cfg, target, draft, prompt = build_models(0, args.layers, wl=wl,
+                                              draft_layers=args.draft_layers)
+    sess = mb.Session(target, draft, gamma=wl.gamma,
+                      max_context=wl.prompt_len + wl.new_tokens + 2 * wl.gamma + 8,
+                      temperature=wl.temperature, seed=wl.seed, accept_mode=wl.accept_mode)
     sess.prime(prompt)
     sess.decode(2)  # captures the round graph
     torch.cuda.synchronize()
@@ -832,6 +835,8 @@ def main():
     ap.add_argument("--profile", action="store_true", help="short run for ncu launch lists")
     ap.add_argument("--layers", type=int, default=None,
                     help="--profile only: target layers (fewer = smaller device footprint)")
+    ap.add_argument("--draft-layers", type=int, default=None,
+                    help="--profile only: draft layers")
     ap.add_argument("--config", default="llama3-8b",
                     choices=["llama3-8b", "llama3-8b-bs8", "tinyllama", "llama2-70b"],
                     help="workload (default: the headline 8B int8 batch-1 configuration)")

@@ -8,7 +8,9 @@ import ctypes as C
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libmodelc_cuda.so")
+# MODELC_CUDA_LIB: another build of the library (a variant built with other
+# compile-time settings); the in-tree build otherwise
+LIB_PATH = os.environ.get("MODELC_CUDA_LIB") or os.path.join(HERE, "libmodelc_cuda.so")
 
 MC_OK = 0
 STATUS = {0: "MC_OK", -1: "MC_E_INVALID", -2: "MC_E_SHAPE", -3: "MC_E_DTYPE", -4: "MC_E_OOM",
