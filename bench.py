@@ -19,13 +19,14 @@ the GPU.  Inputs (7.5 GB of weights) exceed the 126 MB L2 on every step.
 
 ``--impl reference`` times the reference's CPU algorithm (the oracle's
 bit-identical row-parallel linear on all host cores) on the same workload.
-Multi-GPU (torchrun, N ranks): N independent requests, one per GPU, each
-with its own replica of the models -- requests are independent units, so
-nothing crosses NVLink on the data path (weak scaling); value = all ranks'
-tokens / max-over-ranks time.  --tp instead runs one request with the target
-tensor-parallel over the N GPUs (the fused NVLink reduction after each
-row-parallel projection, or NCCL with --tp-nccl; strong scaling), value =
-that request's tokens / max-over-ranks time.
+Multi-GPU (torchrun, N ranks): the workload's requests with the target
+Megatron tensor-parallel over the N GPUs (column-parallel QKV and gate/up,
+row-parallel O and down followed by the fused NVLink reduction, or NCCL
+all-reduces with --tp-nccl; vocab-parallel LM head; the draft replicated);
+strong scaling, value = the requests' tokens / max-over-ranks time.
+--replicas instead runs N independent copies of the workload, one per GPU,
+with nothing crossing NVLink (weak scaling); value = all ranks' tokens /
+max-over-ranks time.
 """
 from __future__ import annotations
 
@@ -64,6 +65,11 @@ def workloads():
     from dataclasses import replace
     import modelc_b200 as mb
     return {
+        "tiny": Workload(
+            "tiny", "spec-decode tokens/s, tiny 4-layer d256 int8 bs1 (L2-resident, latency-bound)",
+            "tiny-4l-d256 int8-row target (reference-exact: heads = d/64, eps 1e-6, theta 1e4) + "
+            "1-layer draft, bs1, prompt 32, gamma 4, greedy, 128 new",
+            mb.TINY, mb.TINY.with_layers(1), "i8_row", "i8_row", 32, 128, 4),
         "llama3-8b": Workload("llama3-8b", METRIC, WORKLOAD, mb.LLAMA3_8B,
                               mb.LLAMA3_8B.with_layers(2), "i8_row", "i8_row", PROMPT_LEN,
                               NEW_TOKENS, GAMMA),
@@ -385,9 +391,9 @@ def run_ours(args):
     PROMPT_LEN, NEW_TOKENS, GAMMA = wl.prompt_len, wl.new_tokens, wl.gamma
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
-    # N > 1: N independent requests (weak scaling); --tp: one request, target
-    # tensor-parallel over the N GPUs (strong scaling)
-    tp = world > 1 and (args.tp or args.tp_nccl)
+    # N > 1: the target tensor-parallel over the N GPUs (strong scaling);
+    # --replicas: N independent copies of the workload (weak scaling)
+    tp = world > 1 and not args.replicas
     if world > 1:
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
@@ -427,9 +433,15 @@ def run_ours(args):
     rounds = 0
     accepted = []
     ev = []
+    # weights smaller than L2: flush it (write 512 MB) before every timed step
+    l2_flush = (torch.empty(512 << 20, dtype=torch.uint8, device="cuda")
+                if target.streamed_bytes < (256 << 20) else None)
     with ClockSampler(local) as clk:
         for _ in range(args.steps):
             sess.rewind()
+            if l2_flush is not None:
+                l2_flush.fill_(1)
+                torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             sess.decode(NEW_TOKENS)
@@ -526,7 +538,12 @@ def run_ours(args):
                        "prompt_len": PROMPT_LEN, "new_tokens": NEW_TOKENS, "gamma": GAMMA,
                        "temperature": wl.temperature, "batch": B,
                        "parallelism": parallelism,
-                       "l2": f"inputs larger than L2 ({wbytes / 1e9:.2f} GB of weights per verify)"},
+                       "l2": (f"inputs larger than L2 ({wbytes / 1e9:.2f} GB of weights per verify)"
+                              if l2_flush is None else
+                              f"L2 flushed (512 MB write) before each timed step; "
+                              f"{wbytes / 1e6:.2f} MB of weights per verify stay L2-resident "
+                              f"within a step")},
+            "us_per_round": round(t_total * 1e6 / max(rounds, 1), 2),
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
@@ -838,12 +855,13 @@ def main():
     ap.add_argument("--draft-layers", type=int, default=None,
                     help="--profile only: draft layers")
     ap.add_argument("--config", default="llama3-8b",
-                    choices=["llama3-8b", "llama3-8b-bs8", "tinyllama", "llama2-70b"],
+                    choices=["tiny", "llama3-8b", "llama3-8b-bs8", "tinyllama", "llama2-70b"],
                     help="workload (default: the headline 8B int8 batch-1 configuration)")
-    ap.add_argument("--tp", action="store_true",
-                    help="N > 1: one request, target tensor-parallel over the N GPUs")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1: N independent copies of the workload, one per GPU, instead "
+                         "of the target tensor-parallel over the N GPUs")
     ap.add_argument("--tp-nccl", action="store_true",
-                    help="with --tp: NCCL all-reduces instead of the fused NVLink reduction")
+                    help="N > 1: NCCL all-reduces instead of the fused NVLink reduction")
     ap.add_argument("--timeline", action="store_true",
                     help="in-situ per-kernel timeline of one verify forward (MC_TRACE build)")
     ap.add_argument("--sweep", action="store_true",

@@ -1607,7 +1607,16 @@ size_t gemv_ws_ints_per_stripe(int nt) { return (size_t)16 * 8 * nt; }
 // margin (digits tolerate |X| < 2^21).
 constexpr int kQuantThreads = 512;
 constexpr int kQuantMaxCtas = 64;
-static int g_attn_smem = 48 * 1024;  // attention dynamic smem limit set so far
+// Function attributes (the dynamic shared-memory limits) belong to one
+// device's context, so what has been set is kept per device.
+constexpr int kMaxDevices = 64;
+static int cur_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return (d >= 0 && d < kMaxDevices) ? d : 0;
+}
+static int g_attn_smem[kMaxDevices];  // attention dynamic smem limit set beyond 48 KB, per device
+static int attn_smem_limit() { return std::max(g_attn_smem[cur_device()], 48 * 1024); }
 
 // STATS: the producer supplied the statistics (use_stats); otherwise the
 // kernel reduces them itself (two instances keep the forward's one lean).
@@ -2357,12 +2366,14 @@ int attention_qblk(int G, int seq_len) {
   return std::max(1, std::min(seq_len, cap));
 }
 
-static int g_attn_tc_smem = 48 * 1024;  // tensor-core attention dynamic smem limit set so far
+// tensor-core attention dynamic smem limit set beyond 48 KB, per device
+static int g_attn_tc_smem[kMaxDevices];
+static int attn_tc_smem_limit() { return std::max(g_attn_tc_smem[cur_device()], 48 * 1024); }
 
 template <int MT, int HD, bool TAIL = false>
 static cudaError_t launch_attention_tc(const AttnArgs& a, dim3 grid, cudaStream_t s, bool pdl) {
   const size_t smem = attention_tc_smem_bytes(MT, HD);
-  if (smem > (size_t)g_attn_tc_smem) return cudaErrorInvalidConfiguration;
+  if (smem > (size_t)attn_tc_smem_limit()) return cudaErrorInvalidConfiguration;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kAttnTcThreads);
@@ -2418,7 +2429,7 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
   const int rb = attention_rb(Rp, a.hdp, a.page);
   if (rb == 0) return cudaErrorInvalidValue;
   const size_t smem = attention_smem_bytes(G, a.qblk, a.hdp, a.page);
-  if (smem > (size_t)g_attn_smem) return cudaErrorInvalidConfiguration;
+  if (smem > (size_t)attn_smem_limit()) return cudaErrorInvalidConfiguration;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.Hkv, a.max_chunks, n_seq * n_qb);
   cfg.blockDim = dim3(kAttnThreads);
@@ -2449,8 +2460,8 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
 
 // Raise the dynamic shared-memory limit once, outside any stream capture.
 // CTAs of the tail variant k_attention_tc<1, HD, true> resident per SM
-// (index 0/1/2: HD 32/64/128), settled by prepare_kernels.
-static int g_attn_tail_bps[3] = {0, 0, 0};
+// (index 0/1/2: HD 32/64/128) on each device, settled by prepare_kernels.
+static int g_attn_tail_bps[kMaxDevices][3];
 
 template <int HD>
 static cudaError_t prepare_attention_tc_hd() {
@@ -2464,7 +2475,7 @@ static cudaError_t prepare_attention_tc_hd() {
   cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
       &n, k_attention_tc<1, HD, true>, kAttnTcThreads, attention_tc_smem_bytes(1, HD));
   if (e != cudaSuccess) return e;
-  g_attn_tail_bps[HD == 32 ? 0 : (HD == 64 ? 1 : 2)] = n;
+  g_attn_tail_bps[cur_device()][HD == 32 ? 0 : (HD == 64 ? 1 : 2)] = n;
   return cudaSuccess;
 }
 
@@ -2481,7 +2492,7 @@ bool attention_tail_fits(const AttnArgs& a, int nsm) {
       a.M % a.seq.seq_len || a.qblk < 1 || !a.enc.att_o || a.enc.KB < 1 || a.enc.M != a.M)
     return false;
   if (a.hdp != 32 && a.hdp != 64 && a.hdp != 128) return false;
-  const int bps = g_attn_tail_bps[a.hdp == 32 ? 0 : (a.hdp == 64 ? 1 : 2)];
+  const int bps = g_attn_tail_bps[cur_device()][a.hdp == 32 ? 0 : (a.hdp == 64 ? 1 : 2)];
   const long long n_qb = (a.seq.seq_len + a.qblk - 1) / a.qblk;
   const long long grid = (long long)a.Hkv * a.max_chunks * (a.M / a.seq.seq_len) * n_qb;
   if (bps < 1 || grid > (long long)nsm * bps) return false;
@@ -2492,22 +2503,23 @@ bool attention_tail_fits(const AttnArgs& a, int nsm) {
 
 cudaError_t prepare_kernels(size_t quant_smem, size_t attn_smem) {
   (void)quant_smem;
-  if (g_attn_tc_smem < (int)attention_tc_smem_bytes(4, 128)) {
+  const int dev = cur_device();
+  if (g_attn_tc_smem[dev] < (int)attention_tc_smem_bytes(4, 128)) {
     cudaError_t e = prepare_attention_tc_hd<32>();
     if (e == cudaSuccess) e = prepare_attention_tc_hd<64>();
     if (e == cudaSuccess) e = prepare_attention_tc_hd<128>();
     if (e != cudaSuccess) return e;
-    g_attn_tc_smem = (int)attention_tc_smem_bytes(4, 128);
+    g_attn_tc_smem[dev] = (int)attention_tc_smem_bytes(4, 128);
   }
 
-  if (attn_smem > (size_t)g_attn_smem) {
+  if (attn_smem > (size_t)attn_smem_limit()) {
     for (auto f : {k_attention<8, 1>, k_attention<4, 1>, k_attention<2, 1>, k_attention<1, 1>,
                    k_attention<2, 2>, k_attention<1, 2>}) {
       cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)attn_smem);
       if (e != cudaSuccess) return e;
     }
-    g_attn_smem = (int)attn_smem;
+    g_attn_smem[dev] = (int)attn_smem;
   }
   return cudaSuccess;
 }
