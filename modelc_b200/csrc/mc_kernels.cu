@@ -241,20 +241,26 @@ __device__ __forceinline__ void imma(int* c, const int4& a, uint32_t b0, uint32_
       : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
 }
 
+// This lane's B fragments of one k-block (base: the k-block's 256 * NT
+// bytes; layout as digit_word).  Each load instruction of the warp covers a
+// contiguous span: 8 * NT bytes per lane, or for three tiles 16 bytes per
+// lane (tiles 0-1) and then 8 (tile 2).
 template <int NT>
-__device__ __forceinline__ void load_x(uint32_t* xv, const uint8_t* p) {
+__device__ __forceinline__ void load_x(uint32_t* xv, const uint8_t* base, int lane) {
+  if constexpr (NT == 3) {
+    uint4 v = ldg_u4(base + lane * 16);
+    xv[0] = v.x; xv[1] = v.y; xv[2] = v.z; xv[3] = v.w;
+    uint2 w = ldg_u2(base + 512 + lane * 8);
+    xv[4] = w.x; xv[5] = w.y;
+    return;
+  }
+  const uint8_t* p = base + lane * 8 * NT;
   if constexpr (NT == 1) {
     uint2 v = ldg_u2(p);
     xv[0] = v.x; xv[1] = v.y;
   } else if constexpr (NT == 2) {
     uint4 v = ldg_u4(p);
     xv[0] = v.x; xv[1] = v.y; xv[2] = v.z; xv[3] = v.w;
-  } else if constexpr (NT == 3) {
-#pragma unroll
-    for (int i = 0; i < 3; ++i) {
-      uint2 v = ldg_u2(p + 8 * i);
-      xv[2 * i] = v.x; xv[2 * i + 1] = v.y;
-    }
   } else {
 #pragma unroll
     for (int i = 0; i < NT / 2; ++i) {
@@ -440,7 +446,10 @@ constexpr int kEncBatch = 8;
 
 // Word index of the 4 digit bytes of column c, k-block kb, k = kk..kk+3
 // (kk % 4 == 0).  mma.sync layout: [kb][lane][tile][reg], lane = (c%8)*4 +
-// (kk%16)/4, the B fragment of m16n8k32.  tcgen05 layout (tc): K-major with
+// (kk%16)/4, the B fragment of m16n8k32; with three tiles a k-block holds
+// [lane][tiles 0-1][reg] and then [lane][reg] of tile 2, so that each of the
+// GEMV's two loads per lane reads a contiguous span (24-byte lane strides
+// cost three times the L1 wavefronts).  tcgen05 layout (tc): K-major with
 // the 128-byte swizzle, [kb/4][column][128 bytes] with the row's 16-byte
 // chunk q = (kb%4)*2 + kk/16 stored at q ^ (column % 8).
 __device__ __forceinline__ size_t digit_word(int kb, int c, int kk, int nt, bool tc) {
@@ -448,7 +457,9 @@ __device__ __forceinline__ size_t digit_word(int kb, int c, int kk, int nt, bool
     const int q = ((kb & 3) << 1) | (kk >> 4);
     return ((size_t)(kb >> 2) * (8 * nt) + c) * 32 + (size_t)(((q ^ (c & 7)) << 2) + ((kk & 15) >> 2));
   }
-  return (((size_t)kb * 32 + (c & 7) * 4 + ((kk & 15) >> 2)) * nt + (c >> 3)) * 2 + (kk >> 4);
+  const int lane = (c & 7) * 4 + ((kk & 15) >> 2), t = c >> 3, r = kk >> 4;
+  if (nt == 3) return (size_t)kb * 192 + (t < 2 ? lane * 4 + t * 2 + r : 128 + lane * 2 + r);
+  return (((size_t)kb * 32 + lane) * nt + t) * 2 + r;
 }
 // Word index of column c of a forward of `groups` token groups: the tcgen05
 // layout spans all groups (nt * groups tiles); the mma.sync layout keeps each
@@ -869,7 +880,9 @@ __device__ __forceinline__ void grid_barrier(unsigned* bar, int* err, bool wait 
 // workspace (int32 sums, so the reduction order never changes the result).
 template <int NT>
 struct GemvCfg {
-  static constexpr int U = (NT <= 2) ? 8 : 4;  // k-blocks per load batch
+  // k-blocks per load batch: its weight fragments and activation words stay
+  // in registers, 8 up to three tiles (24 columns, 8 tokens), 4 beyond
+  static constexpr int U = (NT <= 3) ? 8 : 4;
   static constexpr int COLS = 8 * NT;
 };
 
@@ -1143,7 +1156,7 @@ struct GemvRing {
   static constexpr int KBW = 512;
   static constexpr int KBS = 0;
   static constexpr int ChunkBytes = U * (KBW + KBS);
-  static constexpr int NB = NT <= 2 ? 2 : 3;
+  static constexpr int NB = NT <= 3 ? 2 : 3;  // two 4 KB chunks, or three 2 KB ones
   static constexpr int PreWait = kRingPreWait < NB ? kRingPreWait : NB;
   static constexpr int WarpBytes = On ? NB * ChunkBytes : 0;
   static constexpr size_t Base = ((((size_t)kGemvWarps * 16 * (8 * NT + 1) +
@@ -1339,7 +1352,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
     Acc acc[NT][4];
 #pragma unroll
     for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0;
-    const uint8_t* xp = a.x + ((size_t)k0 * 32 + lane) * COLS;
+    const uint8_t* xp = a.x + (size_t)k0 * 32 * COLS;
     for (int i = 0; i < n; i += U, ++c) {
       const int nb = min(U, n - i);
       if (!RING && !pre) load_batch(stripe, k0 + i, nb);
@@ -1347,7 +1360,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
       uint32_t xv[U][2 * NT];
 #pragma unroll
       for (int j = 0; j < U; ++j)
-        if (j < nb) load_x<NT>(xv[j], xp + (size_t)(i + j) * 32 * COLS);
+        if (j < nb) load_x<NT>(xv[j], xp + (size_t)(i + j) * 32 * COLS, lane);
       const int b = RING ? c % R::NB : 0;
       if constexpr (RING) ring_ok &= mbar_wait(&mbar[b], (uint32_t)((c / R::NB) & 1));
       const uint8_t* cb = wring + (size_t)b * R::ChunkBytes;
