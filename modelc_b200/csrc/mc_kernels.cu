@@ -242,31 +242,18 @@ __device__ __forceinline__ void imma(int* c, const int4& a, uint32_t b0, uint32_
 }
 
 // This lane's B fragments of one k-block (base: the k-block's 256 * NT
-// bytes; layout as digit_word).  Each load instruction of the warp covers a
-// contiguous span: 8 * NT bytes per lane, or for three tiles 16 bytes per
-// lane (tiles 0-1) and then 8 (tile 2).
+// bytes; layout as digit_word): one 16-byte load per pair of tiles and an
+// 8-byte one for an odd last tile, each contiguous across the warp.
 template <int NT>
 __device__ __forceinline__ void load_x(uint32_t* xv, const uint8_t* base, int lane) {
-  if constexpr (NT == 3) {
-    uint4 v = ldg_u4(base + lane * 16);
-    xv[0] = v.x; xv[1] = v.y; xv[2] = v.z; xv[3] = v.w;
-    uint2 w = ldg_u2(base + 512 + lane * 8);
-    xv[4] = w.x; xv[5] = w.y;
-    return;
-  }
-  const uint8_t* p = base + lane * 8 * NT;
-  if constexpr (NT == 1) {
-    uint2 v = ldg_u2(p);
-    xv[0] = v.x; xv[1] = v.y;
-  } else if constexpr (NT == 2) {
-    uint4 v = ldg_u4(p);
-    xv[0] = v.x; xv[1] = v.y; xv[2] = v.z; xv[3] = v.w;
-  } else {
 #pragma unroll
-    for (int i = 0; i < NT / 2; ++i) {
-      uint4 v = ldg_u4(p + 16 * i);
-      xv[4 * i] = v.x; xv[4 * i + 1] = v.y; xv[4 * i + 2] = v.z; xv[4 * i + 3] = v.w;
-    }
+  for (int i = 0; i < NT / 2; ++i) {
+    uint4 v = ldg_u4(base + i * 512 + lane * 16);
+    xv[4 * i] = v.x; xv[4 * i + 1] = v.y; xv[4 * i + 2] = v.z; xv[4 * i + 3] = v.w;
+  }
+  if constexpr (NT & 1) {
+    uint2 w = ldg_u2(base + (NT / 2) * 512 + lane * 8);
+    xv[NT * 2 - 2] = w.x; xv[NT * 2 - 1] = w.y;
   }
 }
 
@@ -446,10 +433,11 @@ constexpr int kEncBatch = 8;
 
 // Word index of the 4 digit bytes of column c, k-block kb, k = kk..kk+3
 // (kk % 4 == 0).  mma.sync layout: [kb][lane][tile][reg], lane = (c%8)*4 +
-// (kk%16)/4, the B fragment of m16n8k32; with three tiles a k-block holds
-// [lane][tiles 0-1][reg] and then [lane][reg] of tile 2, so that each of the
-// GEMV's two loads per lane reads a contiguous span (24-byte lane strides
-// cost three times the L1 wavefronts).  tcgen05 layout (tc): K-major with
+// (kk%16)/4, the B fragment of m16n8k32, in planes of two tiles:
+// [kb][tile/2][lane][tile%2][reg], an odd last tile as its own plane
+// [lane][reg].  Each of the GEMV's loads then reads a contiguous span across
+// the warp (a 24- or 48-byte lane stride costs three times the L1
+// wavefronts).  tcgen05 layout (tc): K-major with
 // the 128-byte swizzle, [kb/4][column][128 bytes] with the row's 16-byte
 // chunk q = (kb%4)*2 + kk/16 stored at q ^ (column % 8).
 __device__ __forceinline__ size_t digit_word(int kb, int c, int kk, int nt, bool tc) {
@@ -458,8 +446,8 @@ __device__ __forceinline__ size_t digit_word(int kb, int c, int kk, int nt, bool
     return ((size_t)(kb >> 2) * (8 * nt) + c) * 32 + (size_t)(((q ^ (c & 7)) << 2) + ((kk & 15) >> 2));
   }
   const int lane = (c & 7) * 4 + ((kk & 15) >> 2), t = c >> 3, r = kk >> 4;
-  if (nt == 3) return (size_t)kb * 192 + (t < 2 ? lane * 4 + t * 2 + r : 128 + lane * 2 + r);
-  return (((size_t)kb * 32 + lane) * nt + t) * 2 + r;
+  const size_t plane = (size_t)kb * 64 * nt + (t >> 1) * 128;
+  return plane + ((nt & 1) && t == nt - 1 ? lane * 2 + r : lane * 4 + (t & 1) * 2 + r);
 }
 // Word index of column c of a forward of `groups` token groups: the tcgen05
 // layout spans all groups (nt * groups tiles); the mma.sync layout keeps each
