@@ -86,7 +86,7 @@ def workloads():
             mb.TINYLLAMA, mb.TINYLLAMA.with_layers(2), "q4_0", "q4_0", 512, 256, 5,
             temperature=0.8, seed=7),
         "llama2-70b": Workload(
-            "llama2-70b", "spec-decode tokens/s, 70B-shape q4_0 bs1 (1 GPU)",
+            "llama2-70b", "spec-decode tokens/s, 70B-shape q4_0 bs1",
             "llama2-70b-shape q4_0 target + llama3-8b-shape int8 draft (vocab 32000), bs1, "
             "prompt 2048, gamma 4, greedy, 256 new",
             mb.LLAMA2_70B, replace(mb.LLAMA3_8B, vocab=32000), "q4_0", "i8_row", 2048, 256, 4),
