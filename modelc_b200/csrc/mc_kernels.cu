@@ -1203,8 +1203,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
   auto unit_range = [&](int u, int& stripe, int& kb0, int& kb1) {
     stripe = s0 + u / F;
     const int part = u - (u / F) * F;
-    kb0 = (int)((long long)a.KB * part / F);
-    kb1 = (int)((long long)a.KB * (part + 1) / F);
+    kb0 = a.KB * part / F;  // KB * F < 2^31
+    kb1 = a.KB * (part + 1) / F;
   };
   // Weights never depend on the producer grid: start streaming them before
   // the wait.  Register path: the first batch of this warp's first unit.
@@ -1429,13 +1429,16 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) k_gemv(GemvArgs a) {
         __threadfence_block();
         if constexpr (Q4) {
           // add the stripe's non-empty partial tiles in k order into this
-          // warp's staging (empty k-ranges wrote no tile)
+          // warp's staging (empty k-ranges wrote no tile); which parts are
+          // non-empty is settled once, not per element
+          unsigned live = 0;
+          for (int p = 0; p < F; ++p)
+            if (a.KB * (p + 1) / F > a.KB * p / F) live |= 1u << p;
           const Acc* parts = sm_tile[slot * F];
           for (int i = lane; i < 16 * COLS; i += 32) {
             float v = 0.0f;
             for (int p = 0; p < F; ++p)
-              if ((long long)a.KB * (p + 1) / F > (long long)a.KB * p / F)
-                v = __fadd_rn(v, parts[p * 16 * COLS + i]);
+              if ((live >> p) & 1u) v = __fadd_rn(v, parts[p * 16 * COLS + i]);
             sm_epi[warp][i / COLS][i % COLS] = v;
           }
           __syncwarp();
